@@ -1,0 +1,348 @@
+// Python bindings of the astrai_b200 CUDA kernels.
+//
+// The .cu files are torch-free (raw pointers + cudaStream_t); this file owns
+// every tensor check (device, dtype, contiguity of the innermost dimension,
+// 16-byte alignment required by TMA and vector loads) and passes the current
+// PyTorch stream, so all kernels order correctly with the rest of autograd.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <cuda_runtime.h>
+
+namespace astrai_host {
+int num_sms(int device);
+int read_and_clear_error();
+void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int N, int K, int batch, int a_mn,
+               long long lda, long long strideA, int b_mn, long long ldb, long long strideB, long long ldd,
+               long long strideD, int out_f32, long long ldc, long long strideC, float alpha, float beta,
+               int force_bn, cudaStream_t stream);
+void rmsnorm_fwd(const void* x, long long ldx, const void* w, void* y, long long ldy, float* rstd, int rows, int D,
+                 float eps, cudaStream_t s);
+long long rmsnorm_bwd_scratch(int rows, int D, int* nblocks_out);
+void rmsnorm_bwd(const void* dy, long long lddy, const void* x, long long ldx, const void* w, const float* rstd,
+                 void* dx, long long lddx, void* dw_bf16, float* dw_f32, float* scratch, int rows, int D,
+                 cudaStream_t s);
+void rope_apply(void* x, long long ld, int rows, int col0, int n_heads, int head_dim, const int* pos, int seq_len,
+                const void* cs, int inverse, int rot_dim, int rot_off, cudaStream_t s);
+void swiglu_fwd(const void* h, long long ldh, void* out, long long ldo, int rows, int F, cudaStream_t s);
+void swiglu_bwd(const void* dy, long long lddy, const void* h, long long ldh, void* dh, long long lddh, int rows, int F,
+                cudaStream_t s);
+void embedding_fwd(const long long* ids, const void* w, void* out, int n_tok, int d, int vocab, cudaStream_t s);
+void embedding_bwd(const long long* ids, const void* g, float* gw, int n_tok, int d, int vocab, cudaStream_t s);
+void f32_to_bf16(const float* in, void* out, long long n, int accumulate, cudaStream_t s);
+void transpose_bf16(const void* in, void* out, int batch, int R, int C, cudaStream_t s);
+void ce_fwd(const void* logits, long long ld, const long long* target, int rows, int V, float smoothing,
+            long long ignore_index, int mode, float* lse, float* out, cudaStream_t s);
+void ce_bwd(const void* logits, long long ld, const long long* target, int rows, int V, float smoothing,
+            long long ignore_index, int mode, const float* lse, const float* gscale, const float* grow,
+            void* dlogits, long long ldd, cudaStream_t s);
+void grad_sumsq(const void* chunks, int n_chunks, const long long* gptr, const int* group, float* acc, cudaStream_t s);
+void clip_coef(const float* acc, int n, float max_norm, float* coef, float* norm_out, cudaStream_t s);
+void adamw_step(const void* chunks, int n_chunks, const long long* pptr, const long long* gptr, const long long* mptr,
+                const long long* vptr, const float* wd, int fp32_params, float lr, float b1, float b2, float eps,
+                float bc1, float bc2, const float* coef, cudaStream_t s);
+void muon_momentum(const long long* gptr, const long long* bufptr, int buf_fp32, void* U, int batch, long long numel,
+                   float mu, int nesterov, const float* coef, float* sumsq, cudaStream_t s);
+void muon_normalize(const void* U, void* X, int batch, int R, int C, int transpose, const float* sumsq, float eps,
+                    cudaStream_t s);
+void muon_apply(const long long* pptr, int fp32_params, const void* X, int batch, int R, int C, int transpose,
+                float decay, float adj_lr, cudaStream_t s);
+}  // namespace astrai_host
+
+namespace {
+
+#define I64(t) reinterpret_cast<const long long*>((t).data_ptr<int64_t>())
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check_cuda(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+void check_bf16(const at::Tensor& t, const char* name) {
+  check_cuda(t, name);
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bfloat16");
+}
+void check_rows(const at::Tensor& t, const char* name) {
+  // 2-D view with unit inner stride and 16-byte aligned row stride / base
+  TORCH_CHECK(t.dim() == 2, name, " must be 2-D");
+  TORCH_CHECK(t.stride(1) == 1, name, " must have a contiguous inner dimension");
+  TORCH_CHECK((t.stride(0) * t.element_size()) % 16 == 0, name, ": row stride must be a multiple of 16 bytes");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, " must be 16-byte aligned");
+}
+
+// ----------------------------------------------------------------- GEMM
+// D = alpha * op(A) op(B)^T + beta * C over 2-D or batched 3-D operands.
+//   a: [.., M, K] when a_mn == 0, [.., K, M] when a_mn == 1
+//   b: [.., N, K] when b_mn == 0, [.., K, N] when b_mn == 1
+void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& d, const c10::optional<at::Tensor>& c, int64_t a_mn,
+          int64_t b_mn, double alpha, double beta, int64_t force_bn) {
+  check_bf16(a, "a");
+  check_bf16(b, "b");
+  check_cuda(d, "d");
+  TORCH_CHECK(d.scalar_type() == at::kBFloat16 || d.scalar_type() == at::kFloat, "d must be bf16 or fp32");
+  TORCH_CHECK(a.dim() == b.dim() && a.dim() == d.dim() && (a.dim() == 2 || a.dim() == 3), "rank mismatch");
+  const bool batched = a.dim() == 3;
+  const int batch = batched ? (int)a.size(0) : 1;
+  const int ar = batched ? 1 : 0;
+  const long long M = a_mn ? a.size(ar + 1) : a.size(ar);
+  const long long K = a_mn ? a.size(ar) : a.size(ar + 1);
+  const long long N = b_mn ? b.size(ar + 1) : b.size(ar);
+  const long long Kb = b_mn ? b.size(ar) : b.size(ar + 1);
+  TORCH_CHECK(K == Kb, "gemm: K mismatch ", K, " vs ", Kb);
+  TORCH_CHECK(d.size(ar) == M && d.size(ar + 1) == N, "gemm: output shape mismatch");
+  TORCH_CHECK(a.stride(ar + 1) == 1 && b.stride(ar + 1) == 1 && d.stride(ar + 1) == 1,
+              "gemm: operands need a contiguous inner dimension");
+  TORCH_CHECK((a.stride(ar) * 2) % 16 == 0 && (b.stride(ar) * 2) % 16 == 0, "gemm: row strides must be 16B multiples");
+  if (batched) TORCH_CHECK(b.size(0) == batch && d.size(0) == batch, "gemm: batch mismatch");
+  const void* cptr = nullptr;
+  long long ldc = 0, sc = 0;
+  if (c.has_value() && c->defined()) {
+    TORCH_CHECK(c->scalar_type() == d.scalar_type(), "gemm: c must match d dtype");
+    TORCH_CHECK(c->sizes() == d.sizes() && c->stride(ar + 1) == 1, "gemm: c shape mismatch");
+    cptr = c->data_ptr();
+    ldc = c->stride(ar);
+    sc = batched ? c->stride(0) : 0;
+  }
+  c10::cuda::CUDAGuard g(a.device());
+  astrai_host::gemm_bf16(a.data_ptr(), b.data_ptr(), d.data_ptr(), cptr, (int)M, (int)N, (int)K, batch, (int)a_mn,
+                         a.stride(ar), batched ? a.stride(0) : 0, (int)b_mn, b.stride(ar), batched ? b.stride(0) : 0,
+                         d.stride(ar), batched ? d.stride(0) : 0, d.scalar_type() == at::kFloat ? 1 : 0, ldc, sc,
+                         (float)alpha, (float)beta, (int)force_bn, stream());
+}
+
+// ----------------------------------------------------------------- RMSNorm
+void rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, c10::optional<at::Tensor> rstd, double eps) {
+  check_bf16(x, "x");
+  check_bf16(w, "w");
+  check_bf16(y, "y");
+  check_rows(x, "x");
+  check_rows(y, "y");
+  const int D = (int)x.size(1);
+  TORCH_CHECK(w.numel() == D && w.is_contiguous(), "w shape");
+  TORCH_CHECK(D % 8 == 0 && (D <= 256 ? D % 32 == 0 : true), "rmsnorm: unsupported width ", D);
+  float* r = nullptr;
+  if (rstd.has_value() && rstd->defined()) {
+    TORCH_CHECK(rstd->scalar_type() == at::kFloat && rstd->numel() == x.size(0), "rstd");
+    r = rstd->data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard g(x.device());
+  astrai_host::rmsnorm_fwd(x.data_ptr(), x.stride(0), w.data_ptr(), y.data_ptr(), y.stride(0), r, (int)x.size(0), D,
+                           (float)eps, stream());
+}
+
+int64_t rmsnorm_bwd_scratch(int64_t rows, int64_t D) { return astrai_host::rmsnorm_bwd_scratch((int)rows, (int)D, nullptr); }
+
+void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w, const at::Tensor& rstd, at::Tensor& dx,
+                 at::Tensor& dw, at::Tensor& scratch) {
+  check_bf16(dy, "dy");
+  check_bf16(x, "x");
+  check_bf16(dx, "dx");
+  check_rows(dy, "dy");
+  check_rows(x, "x");
+  check_rows(dx, "dx");
+  const int D = (int)x.size(1);
+  TORCH_CHECK(scratch.scalar_type() == at::kFloat && scratch.numel() >= rmsnorm_bwd_scratch(x.size(0), D), "scratch");
+  c10::cuda::CUDAGuard g(x.device());
+  astrai_host::rmsnorm_bwd(dy.data_ptr(), dy.stride(0), x.data_ptr(), x.stride(0), w.data_ptr(),
+                           rstd.data_ptr<float>(), dx.data_ptr(), dx.stride(0),
+                           dw.scalar_type() == at::kBFloat16 ? dw.data_ptr() : nullptr,
+                           dw.scalar_type() == at::kFloat ? dw.data_ptr<float>() : nullptr, scratch.data_ptr<float>(),
+                           (int)x.size(0), D, stream());
+}
+
+// ----------------------------------------------------------------- RoPE / SwiGLU / embedding
+void rope_(at::Tensor& x, int64_t col0, int64_t n_heads, int64_t head_dim, const c10::optional<at::Tensor>& pos,
+           int64_t seq_len, const at::Tensor& cs, bool inverse, int64_t rot_dim, int64_t rot_off) {
+  check_bf16(x, "x");
+  check_rows(x, "x");
+  TORCH_CHECK(cs.scalar_type() == at::kFloat && cs.is_contiguous() && cs.is_cuda(), "cos/sin table");
+  TORCH_CHECK(rot_dim % 8 == 0 && (col0 + rot_off) % 8 == 0 && head_dim % 8 == 0, "rope: alignment");
+  const int* p = nullptr;
+  if (pos.has_value() && pos->defined()) {
+    TORCH_CHECK(pos->scalar_type() == at::kInt && pos->is_contiguous() && pos->numel() == x.size(0), "positions");
+    p = pos->data_ptr<int>();
+  }
+  c10::cuda::CUDAGuard g(x.device());
+  astrai_host::rope_apply(x.data_ptr(), x.stride(0), (int)x.size(0), (int)col0, (int)n_heads, (int)head_dim, p,
+                          (int)seq_len, cs.data_ptr(), inverse ? 1 : 0, (int)rot_dim, (int)rot_off, stream());
+}
+
+void swiglu_fwd(const at::Tensor& h, at::Tensor& out) {
+  check_bf16(h, "h");
+  check_bf16(out, "out");
+  check_rows(h, "h");
+  check_rows(out, "out");
+  const int F = (int)out.size(1);
+  TORCH_CHECK(h.size(1) == 2 * F && F % 8 == 0, "swiglu: h must be [rows, 2F] with F % 8 == 0");
+  c10::cuda::CUDAGuard g(h.device());
+  astrai_host::swiglu_fwd(h.data_ptr(), h.stride(0), out.data_ptr(), out.stride(0), (int)h.size(0), F, stream());
+}
+
+void swiglu_bwd(const at::Tensor& dy, const at::Tensor& h, at::Tensor& dh) {
+  check_bf16(dy, "dy");
+  check_bf16(h, "h");
+  check_bf16(dh, "dh");
+  check_rows(dy, "dy");
+  check_rows(h, "h");
+  check_rows(dh, "dh");
+  const int F = (int)dy.size(1);
+  c10::cuda::CUDAGuard g(h.device());
+  astrai_host::swiglu_bwd(dy.data_ptr(), dy.stride(0), h.data_ptr(), h.stride(0), dh.data_ptr(), dh.stride(0),
+                          (int)h.size(0), F, stream());
+}
+
+void embedding_fwd(const at::Tensor& ids, const at::Tensor& w, at::Tensor& out) {
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous() && ids.is_cuda(), "ids");
+  check_bf16(w, "w");
+  check_bf16(out, "out");
+  TORCH_CHECK(w.is_contiguous() && out.is_contiguous() && w.size(1) % 8 == 0, "embedding layout");
+  c10::cuda::CUDAGuard g(w.device());
+  astrai_host::embedding_fwd(I64(ids), w.data_ptr(), out.data_ptr(), (int)ids.numel(), (int)w.size(1),
+                             (int)w.size(0), stream());
+}
+
+void embedding_bwd(const at::Tensor& ids, const at::Tensor& grad, at::Tensor& gw_f32) {
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous(), "ids");
+  check_bf16(grad, "grad");
+  TORCH_CHECK(gw_f32.scalar_type() == at::kFloat && gw_f32.is_contiguous() && grad.is_contiguous(), "layout");
+  c10::cuda::CUDAGuard g(grad.device());
+  astrai_host::embedding_bwd(I64(ids), grad.data_ptr(), gw_f32.data_ptr<float>(), (int)ids.numel(),
+                             (int)gw_f32.size(1), (int)gw_f32.size(0), stream());
+}
+
+void f32_to_bf16(const at::Tensor& in, at::Tensor& out, bool accumulate) {
+  TORCH_CHECK(in.scalar_type() == at::kFloat && in.is_contiguous() && out.is_contiguous(), "layout");
+  check_bf16(out, "out");
+  TORCH_CHECK(in.numel() == out.numel(), "numel");
+  c10::cuda::CUDAGuard g(in.device());
+  astrai_host::f32_to_bf16(in.data_ptr<float>(), out.data_ptr(), in.numel(), accumulate ? 1 : 0, stream());
+}
+
+void transpose_bf16(const at::Tensor& in, at::Tensor& out) {
+  check_bf16(in, "in");
+  check_bf16(out, "out");
+  TORCH_CHECK(in.is_contiguous() && out.is_contiguous() && in.dim() == 3, "transpose: contiguous [B,R,C]");
+  c10::cuda::CUDAGuard g(in.device());
+  astrai_host::transpose_bf16(in.data_ptr(), out.data_ptr(), (int)in.size(0), (int)in.size(1), (int)in.size(2),
+                              stream());
+}
+
+// ----------------------------------------------------------------- cross entropy
+void ce_fwd(const at::Tensor& logits, const at::Tensor& target, double smoothing, int64_t ignore_index, int64_t mode,
+            at::Tensor& lse, at::Tensor& out) {
+  check_bf16(logits, "logits");
+  check_rows(logits, "logits");
+  TORCH_CHECK(target.scalar_type() == at::kLong && target.is_contiguous() && target.numel() == logits.size(0), "target");
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && out.scalar_type() == at::kFloat, "lse/out must be fp32");
+  c10::cuda::CUDAGuard g(logits.device());
+  astrai_host::ce_fwd(logits.data_ptr(), logits.stride(0), I64(target), (int)logits.size(0),
+                      (int)logits.size(1), (float)smoothing, ignore_index, (int)mode, lse.data_ptr<float>(),
+                      out.data_ptr<float>(), stream());
+}
+
+void ce_bwd(const at::Tensor& logits, const at::Tensor& target, double smoothing, int64_t ignore_index, int64_t mode,
+            const at::Tensor& lse, const c10::optional<at::Tensor>& gscale, const c10::optional<at::Tensor>& grow,
+            at::Tensor& dlogits) {
+  check_bf16(logits, "logits");
+  check_bf16(dlogits, "dlogits");
+  check_rows(logits, "logits");
+  check_rows(dlogits, "dlogits");
+  const float* gs = (gscale.has_value() && gscale->defined()) ? gscale->data_ptr<float>() : nullptr;
+  const float* gr = (grow.has_value() && grow->defined()) ? grow->data_ptr<float>() : nullptr;
+  TORCH_CHECK(mode == 0 ? gs != nullptr : gr != nullptr, "ce_bwd: missing gradient input");
+  c10::cuda::CUDAGuard g(logits.device());
+  astrai_host::ce_bwd(logits.data_ptr(), logits.stride(0), I64(target), (int)logits.size(0),
+                      (int)logits.size(1), (float)smoothing, ignore_index, (int)mode, lse.data_ptr<float>(), gs, gr,
+                      dlogits.data_ptr(), dlogits.stride(0), stream());
+}
+
+// ----------------------------------------------------------------- optimizer
+void grad_sumsq(const at::Tensor& chunks, const at::Tensor& gptr, const c10::optional<at::Tensor>& group,
+                at::Tensor& acc) {
+  const int n = (int)(chunks.numel() * chunks.element_size() / 16);
+  c10::cuda::CUDAGuard g(acc.device());
+  astrai_host::grad_sumsq(chunks.data_ptr(), n, I64(gptr),
+                          (group.has_value() && group->defined()) ? group->data_ptr<int>() : nullptr,
+                          acc.data_ptr<float>(), stream());
+}
+
+void clip_coef(const at::Tensor& acc, double max_norm, at::Tensor& coef, at::Tensor& norm_out) {
+  c10::cuda::CUDAGuard g(acc.device());
+  astrai_host::clip_coef(acc.data_ptr<float>(), (int)acc.numel(), (float)max_norm, coef.data_ptr<float>(),
+                         norm_out.data_ptr<float>(), stream());
+}
+
+void adamw_step(const at::Tensor& chunks, const at::Tensor& pptr, const at::Tensor& gptr, const at::Tensor& mptr,
+                const at::Tensor& vptr, const at::Tensor& wd, bool fp32_params, double lr, double b1, double b2,
+                double eps, double bc1, double bc2, const c10::optional<at::Tensor>& coef) {
+  const int n = (int)(chunks.numel() * chunks.element_size() / 16);
+  c10::cuda::CUDAGuard g(pptr.device());
+  astrai_host::adamw_step(chunks.data_ptr(), n, I64(pptr), I64(gptr),
+                          I64(mptr), I64(vptr), wd.data_ptr<float>(), fp32_params ? 1 : 0,
+                          (float)lr, (float)b1, (float)b2, (float)eps, (float)bc1, (float)bc2,
+                          (coef.has_value() && coef->defined()) ? coef->data_ptr<float>() : nullptr, stream());
+}
+
+void muon_momentum(const at::Tensor& gptr, const at::Tensor& bufptr, bool buf_fp32, at::Tensor& U, double mu,
+                   bool nesterov, const c10::optional<at::Tensor>& coef, at::Tensor& sumsq) {
+  check_bf16(U, "U");
+  TORCH_CHECK(U.dim() == 3 && U.is_contiguous(), "U must be contiguous [B, R, C]");
+  c10::cuda::CUDAGuard g(U.device());
+  astrai_host::muon_momentum(I64(gptr), I64(bufptr), buf_fp32 ? 1 : 0, U.data_ptr(),
+                             (int)U.size(0), U.size(1) * U.size(2), (float)mu, nesterov ? 1 : 0,
+                             (coef.has_value() && coef->defined()) ? coef->data_ptr<float>() : nullptr,
+                             sumsq.data_ptr<float>(), stream());
+}
+
+void muon_normalize(const at::Tensor& U, at::Tensor& X, bool transpose, const at::Tensor& sumsq, double eps) {
+  c10::cuda::CUDAGuard g(U.device());
+  astrai_host::muon_normalize(U.data_ptr(), X.data_ptr(), (int)U.size(0), (int)U.size(1), (int)U.size(2),
+                              transpose ? 1 : 0, sumsq.data_ptr<float>(), (float)eps, stream());
+}
+
+void muon_apply(const at::Tensor& pptr, bool fp32_params, const at::Tensor& X, int64_t R, int64_t C, bool transpose,
+                double decay, double adj_lr) {
+  c10::cuda::CUDAGuard g(X.device());
+  astrai_host::muon_apply(I64(pptr), fp32_params ? 1 : 0, X.data_ptr(), (int)X.size(0), (int)R, (int)C,
+                          transpose ? 1 : 0, (float)decay, (float)adj_lr, stream());
+}
+
+int64_t num_sms(int64_t device) { return astrai_host::num_sms((int)device); }
+int64_t read_error() { return astrai_host::read_and_clear_error(); }
+
+}  // namespace
+
+void register_attention(pybind11::module& m);
+void register_inference(pybind11::module& m);
+void register_comm(pybind11::module& m);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "astrai_b200 sm_100a kernels";
+  m.def("gemm", &gemm, "bf16 tcgen05 GEMM", py::arg("a"), py::arg("b"), py::arg("d"), py::arg("c") = py::none(),
+        py::arg("a_mn") = 0, py::arg("b_mn") = 0, py::arg("alpha") = 1.0, py::arg("beta") = 0.0,
+        py::arg("force_bn") = 0);
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd_scratch", &rmsnorm_bwd_scratch);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("rope_", &rope_);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("embedding_fwd", &embedding_fwd);
+  m.def("embedding_bwd", &embedding_bwd);
+  m.def("f32_to_bf16", &f32_to_bf16);
+  m.def("transpose_bf16", &transpose_bf16);
+  m.def("ce_fwd", &ce_fwd);
+  m.def("ce_bwd", &ce_bwd);
+  m.def("grad_sumsq", &grad_sumsq);
+  m.def("clip_coef", &clip_coef);
+  m.def("adamw_step", &adamw_step);
+  m.def("muon_momentum", &muon_momentum);
+  m.def("muon_normalize", &muon_normalize);
+  m.def("muon_apply", &muon_apply);
+  m.def("num_sms", &num_sms);
+  m.def("read_error", &read_error);
+  register_attention(m);
+  register_inference(m);
+  register_comm(m);
+}

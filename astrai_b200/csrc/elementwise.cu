@@ -1,0 +1,217 @@
+// Bandwidth-bound elementwise kernels (sm_100a): interleaved RoPE, SwiGLU,
+// embedding gather / scatter-add, batched bf16 transpose.
+//
+// RoPE parity: astrai/model/components/rope.py:26-33 rotates interleaved
+// pairs (x[2i], x[2i+1]) by angle pos * theta_i with theta_i = base^(-2i/d),
+// in fp32. Here the angle table is precomputed on the host as fp32
+// (cos, sin) pairs [max_pos, d/2] and applied in place on the q / k columns
+// of the fused QKV projection output (any row stride), so no copy of q or k
+// is ever made. Backward is the same kernel with the rotation negated.
+// SwiGLU parity: astrai/model/components/mlp.py:22-25 (up * silu(gate)).
+#include "common.cuh"
+
+namespace astrai {
+
+// x: [rows, ld] bf16; heads occupy columns [col0, col0 + n_heads*head_dim).
+// pos: per-row position (nullable -> row % seq_len). cs: float2 [max_pos][head_dim/2].
+__global__ void rope_kernel(__nv_bfloat16* __restrict__ x, long long ld, int rows, int col0, int n_heads, int head_dim,
+                            const int* __restrict__ pos, int seq_len, const float2* __restrict__ cs, float sign,
+                            int rot_dim, int rot_off) {
+  // each thread handles 8 consecutive elements (4 pairs) of one head
+  const int per_head = rot_dim / 8;
+  const long long total = (long long)rows * n_heads * per_head;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int chunk = idx % per_head;
+    const long long t = idx / per_head;
+    const int h = t % n_heads;
+    const int row = t / n_heads;
+    const int p = pos ? pos[row] : row % seq_len;
+    __nv_bfloat16* ptr = x + (long long)row * ld + col0 + h * head_dim + rot_off + chunk * 8;
+    uint4 u = *reinterpret_cast<uint4*>(ptr);
+    uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    const float2* c = cs + (long long)p * (rot_dim / 2) + chunk * 4;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 v = unpack_bf16(w[j]);
+      float2 r = c[j];
+      const float sn = sign * r.y;
+      w[j] = pack_bf16(v.x * r.x - v.y * sn, v.x * sn + v.y * r.x);
+    }
+    *reinterpret_cast<uint4*>(ptr) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.f + __expf(-g)); }
+
+// h: [rows, ldh] with up = h[:, 0:F], gate = h[:, F:2F];  out: [rows, ldo]
+__global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ h, long long ldh, __nv_bfloat16* __restrict__ out,
+                                  long long ldo, int rows, int F) {
+  const int per_row = F / 8;
+  const long long total = (long long)rows * per_row;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int row = idx / per_row;
+    const int c = (idx % per_row) * 8;
+    const uint4 uu = *reinterpret_cast<const uint4*>(h + (long long)row * ldh + c);
+    const uint4 gg = *reinterpret_cast<const uint4*>(h + (long long)row * ldh + F + c);
+    uint32_t u[4] = {uu.x, uu.y, uu.z, uu.w}, g[4] = {gg.x, gg.y, gg.z, gg.w}, o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 a = unpack_bf16(u[j]), b = unpack_bf16(g[j]);
+      o[j] = pack_bf16(a.x * silu_f(b.x), a.y * silu_f(b.y));
+    }
+    *reinterpret_cast<uint4*>(out + (long long)row * ldo + c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// dh[:, :F] = dy * silu(g);  dh[:, F:] = dy * up * silu'(g)
+__global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dy, long long lddy,
+                                  const __nv_bfloat16* __restrict__ h, long long ldh, __nv_bfloat16* __restrict__ dh,
+                                  long long lddh, int rows, int F) {
+  const int per_row = F / 8;
+  const long long total = (long long)rows * per_row;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int row = idx / per_row;
+    const int c = (idx % per_row) * 8;
+    const uint4 uu = *reinterpret_cast<const uint4*>(h + (long long)row * ldh + c);
+    const uint4 gg = *reinterpret_cast<const uint4*>(h + (long long)row * ldh + F + c);
+    const uint4 dd = *reinterpret_cast<const uint4*>(dy + (long long)row * lddy + c);
+    uint32_t u[4] = {uu.x, uu.y, uu.z, uu.w}, g[4] = {gg.x, gg.y, gg.z, gg.w}, d[4] = {dd.x, dd.y, dd.z, dd.w};
+    uint32_t du[4], dg[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 a = unpack_bf16(u[j]), b = unpack_bf16(g[j]), e = unpack_bf16(d[j]);
+      const float s0 = 1.f / (1.f + __expf(-b.x)), s1 = 1.f / (1.f + __expf(-b.y));
+      du[j] = pack_bf16(e.x * b.x * s0, e.y * b.y * s1);
+      dg[j] = pack_bf16(e.x * a.x * s0 * (1.f + b.x * (1.f - s0)), e.y * a.y * s1 * (1.f + b.y * (1.f - s1)));
+    }
+    *reinterpret_cast<uint4*>(dh + (long long)row * lddh + c) = make_uint4(du[0], du[1], du[2], du[3]);
+    *reinterpret_cast<uint4*>(dh + (long long)row * lddh + F + c) = make_uint4(dg[0], dg[1], dg[2], dg[3]);
+  }
+}
+
+// out[t, :] = w[ids[t], :]   (d multiple of 8)
+__global__ void embedding_fwd_kernel(const long long* __restrict__ ids, const __nv_bfloat16* __restrict__ w,
+                                     __nv_bfloat16* __restrict__ out, int n_tok, int d, int vocab, int* err) {
+  const int per = d / 8;
+  const long long total = (long long)n_tok * per;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int t = idx / per, c = (idx % per) * 8;
+    long long id = ids[t];
+    if (id < 0 || id >= vocab) {
+      set_error(err, kErrBadArg);
+      id = 0;
+    }
+    *reinterpret_cast<uint4*>(out + (long long)t * d + c) = *reinterpret_cast<const uint4*>(w + id * d + c);
+  }
+}
+
+// gw_f32[ids[t], :] += g[t, :]
+__global__ void embedding_bwd_kernel(const long long* __restrict__ ids, const __nv_bfloat16* __restrict__ g,
+                                     float* __restrict__ gw, int n_tok, int d, int vocab) {
+  const int per = d / 8;
+  const long long total = (long long)n_tok * per;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int t = idx / per, c = (idx % per) * 8;
+    const long long id = ids[t];
+    if (id < 0 || id >= vocab) continue;
+    const uint4 u = *reinterpret_cast<const uint4*>(g + (long long)t * d + c);
+    uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    float* dst = gw + id * d + c;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 f = unpack_bf16(w[j]);
+      atomicAdd(dst + 2 * j, f.x);
+      atomicAdd(dst + 2 * j + 1, f.y);
+    }
+  }
+}
+
+// out (bf16 or accumulate into bf16) from fp32 buffer
+__global__ void f32_to_bf16_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out, long long n,
+                                   int accumulate) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    float v = in[i];
+    if (accumulate) v += __bfloat162float(out[i]);
+    out[i] = __float2bfloat16_rn(v);
+  }
+}
+
+// Batched transpose of bf16 matrices: out[b][c][r] = in[b][r][c]; 32x32 tiles via smem.
+__global__ void transpose_bf16_kernel(const __nv_bfloat16* __restrict__ in, __nv_bfloat16* __restrict__ out, int R,
+                                      int C, long long in_bstride, long long out_bstride) {
+  __shared__ __nv_bfloat16 tile[32][33];
+  const int b = blockIdx.z;
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  const __nv_bfloat16* src = in + b * in_bstride;
+  __nv_bfloat16* dst = out + b * out_bstride;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int r = r0 + i, c = c0 + threadIdx.x;
+    if (r < R && c < C) tile[i][threadIdx.x] = src[(long long)r * C + c];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int c = c0 + i, r = r0 + threadIdx.x;
+    if (r < R && c < C) dst[(long long)c * R + r] = tile[threadIdx.x][i];
+  }
+}
+
+}  // namespace astrai
+
+namespace astrai_host {
+using namespace astrai;
+
+static inline int ew_grid(long long work) {
+  long long g = (work + 255) / 256;
+  if (g > 148 * 16) g = 148 * 16;
+  return (int)(g < 1 ? 1 : g);
+}
+
+void rope_apply(void* x, long long ld, int rows, int col0, int n_heads, int head_dim, const int* pos, int seq_len,
+                const void* cs, int inverse, int rot_dim, int rot_off, cudaStream_t s) {
+  const long long work = (long long)rows * n_heads * (rot_dim / 8);
+  rope_kernel<<<ew_grid(work), 256, 0, s>>>(static_cast<__nv_bfloat16*>(x), ld, rows, col0, n_heads, head_dim, pos,
+                                            seq_len, static_cast<const float2*>(cs), inverse ? -1.f : 1.f, rot_dim,
+                                            rot_off);
+}
+
+void swiglu_fwd(const void* h, long long ldh, void* out, long long ldo, int rows, int F, cudaStream_t s) {
+  swiglu_fwd_kernel<<<ew_grid((long long)rows * F / 8), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(h), ldh,
+                                                                      static_cast<__nv_bfloat16*>(out), ldo, rows, F);
+}
+
+void swiglu_bwd(const void* dy, long long lddy, const void* h, long long ldh, void* dh, long long lddh, int rows, int F,
+                cudaStream_t s) {
+  swiglu_bwd_kernel<<<ew_grid((long long)rows * F / 8), 256, 0, s>>>(
+      static_cast<const __nv_bfloat16*>(dy), lddy, static_cast<const __nv_bfloat16*>(h), ldh,
+      static_cast<__nv_bfloat16*>(dh), lddh, rows, F);
+}
+
+void embedding_fwd(const long long* ids, const void* w, void* out, int n_tok, int d, int vocab, cudaStream_t s) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  embedding_fwd_kernel<<<ew_grid((long long)n_tok * d / 8), 256, 0, s>>>(
+      ids, static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(out), n_tok, d, vocab, error_word(dev));
+}
+
+void embedding_bwd(const long long* ids, const void* g, float* gw, int n_tok, int d, int vocab, cudaStream_t s) {
+  embedding_bwd_kernel<<<ew_grid((long long)n_tok * d / 8), 256, 0, s>>>(ids, static_cast<const __nv_bfloat16*>(g),
+                                                                          gw, n_tok, d, vocab);
+}
+
+void f32_to_bf16(const float* in, void* out, long long n, int accumulate, cudaStream_t s) {
+  f32_to_bf16_kernel<<<ew_grid(n), 256, 0, s>>>(in, static_cast<__nv_bfloat16*>(out), n, accumulate);
+}
+
+void transpose_bf16(const void* in, void* out, int batch, int R, int C, cudaStream_t s) {
+  dim3 grid((C + 31) / 32, (R + 31) / 32, batch);
+  transpose_bf16_kernel<<<grid, dim3(32, 8), 0, s>>>(static_cast<const __nv_bfloat16*>(in),
+                                                     static_cast<__nv_bfloat16*>(out), R, C, (long long)R * C,
+                                                     (long long)R * C);
+}
+
+}  // namespace astrai_host

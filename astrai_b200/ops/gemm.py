@@ -1,0 +1,97 @@
+"""Linear layers on the tcgen05 GEMM.
+
+``linear(x, w, residual=None)`` computes ``x @ w.T (+ residual)`` with
+``w`` stored ``[out, in]`` like the reference Linear
+(astrai/model/components/linear.py:7-24). Forward, data-grad and weight-grad
+all run on the same persistent sm_100a kernel; the three products only differ
+in which operand is K-major and which is MN-major, so no transposed copies of
+activations or weights are made. A residual passed in is added in the GEMM
+epilogue (used for the o_proj / down projections of a pre-norm block).
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from astrai_b200.ops._ext import native
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *, a_mn: bool = False,
+         b_mn: bool = False, c: Optional[torch.Tensor] = None, alpha: float = 1.0, beta: float = 0.0,
+         out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """D = alpha * op(a) @ op(b)^T + beta * c on CUDA (bf16 inputs).
+
+    a: [M, K] (a_mn False) or [K, M] (a_mn True); b: [N, K] or [K, N];
+    3-D inputs are batched over dim 0.
+    """
+    batched = a.dim() == 3
+    M = a.shape[-1] if a_mn else a.shape[-2]
+    N = b.shape[-1] if b_mn else b.shape[-2]
+    if out is None:
+        shape = (a.shape[0], M, N) if batched else (M, N)
+        out = torch.empty(shape, device=a.device, dtype=out_dtype)
+    native().gemm(a, b, out, c, int(a_mn), int(b_mn), float(alpha), float(beta), 0)
+    return out
+
+
+def gemm_reference(a, b, *, a_mn=False, b_mn=False, c=None, alpha=1.0, beta=0.0):
+    """fp32 oracle of :func:`gemm` (any device)."""
+    A = a.float().transpose(-1, -2) if a_mn else a.float()
+    B = b.float().transpose(-1, -2) if b_mn else b.float()
+    d = alpha * (A @ B.transpose(-1, -2))
+    if c is not None:
+        d = d + beta * c.float()
+    return d
+
+
+def _as_rows(t: torch.Tensor) -> torch.Tensor:
+    t2 = t.reshape(-1, t.shape[-1])
+    if t2.stride(-1) != 1 or (t2.stride(0) * t2.element_size()) % 16:
+        t2 = t2.contiguous()
+    return t2
+
+
+class _LinearFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, residual):
+        x2 = _as_rows(x)
+        M, N = x2.shape[0], w.shape[0]
+        out = torch.empty((M, N), device=x.device, dtype=torch.bfloat16)
+        r2 = _as_rows(residual) if residual is not None else None
+        native().gemm(x2, w, out, r2, 0, 0, 1.0, 1.0 if r2 is not None else 0.0, 0)
+        ctx.save_for_backward(x2, w)
+        ctx.has_res = residual is not None
+        ctx.x_shape = x.shape
+        return out.view(*x.shape[:-1], N)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w = ctx.saved_tensors
+        dy2 = _as_rows(dy)
+        dx = dw = None
+        C = native()
+        if ctx.needs_input_grad[0]:
+            dx = torch.empty_like(x2)
+            C.gemm(dy2, w, dx, None, 0, 1, 1.0, 0.0, 0)
+            dx = dx.view(ctx.x_shape)
+        if ctx.needs_input_grad[1]:
+            dw = torch.empty_like(w)
+            C.gemm(dy2, x2, dw, None, 1, 1, 1.0, 0.0, 0)
+        dres = dy if ctx.has_res else None
+        return dx, dw, dres
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None,
+           bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y = x @ w.T (+ bias) (+ residual)."""
+    if (not x.is_cuda) or bias is not None or x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 \
+            or (x.shape[-1] * 2) % 16 or (w.shape[0] * 2) % 16:
+        # CPU oracle path (and odd dtypes / shapes that TMA cannot address)
+        if x.is_cuda and x.dtype == torch.bfloat16 and bias is None:
+            raise ValueError(f"linear: dims {tuple(x.shape)} x {tuple(w.shape)} need 16-byte aligned rows")
+        y = F.linear(x, w, bias)
+        return y + residual if residual is not None else y
+    return _LinearFn.apply(x, w, residual)

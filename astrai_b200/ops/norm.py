@@ -1,0 +1,44 @@
+"""RMSNorm (parity: astrai/model/components/norm.py:7-15, ``F.rms_norm``)."""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from astrai_b200.ops._ext import native
+
+
+class _RMSNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, eps):
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1])
+        if x2.stride(-1) != 1 or (x2.stride(0) * 2) % 16:
+            x2 = x2.contiguous()
+        y = torch.empty((x2.shape[0], shape[-1]), device=x.device, dtype=x.dtype)
+        rstd = torch.empty(x2.shape[0], device=x.device, dtype=torch.float32)
+        native().rmsnorm_fwd(x2, w, y, rstd, float(eps))
+        ctx.save_for_backward(x2, w, rstd)
+        ctx.shape = shape
+        return y.view(shape)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w, rstd = ctx.saved_tensors
+        C = native()
+        dy2 = dy.reshape(-1, x2.shape[1])
+        if dy2.stride(-1) != 1 or (dy2.stride(0) * 2) % 16:
+            dy2 = dy2.contiguous()
+        dx = torch.empty_like(x2)
+        dw = torch.empty_like(w)
+        scratch = torch.empty(C.rmsnorm_bwd_scratch(x2.shape[0], x2.shape[1]), device=x2.device, dtype=torch.float32)
+        C.rmsnorm_bwd(dy2, x2, w, rstd, dx, dw, scratch)
+        return dx.view(ctx.shape), dw, None
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    D = x.shape[-1]
+    if x.is_cuda and x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and D % 8 == 0 \
+            and (D > 256 or D % 32 == 0):
+        return _RMSNormFn.apply(x, weight, eps)
+    return F.rms_norm(x, (D,), weight, eps)

@@ -1,0 +1,92 @@
+"""Device-timed micro-benchmarks of the framework's kernels.
+
+    python -m astrai_b200.utils.kernel_bench [gemm|norm|ce|attn|all]
+
+Each case is timed with CUDA events on the launching stream after warm-up,
+with a synchronize on both sides; inputs larger than L2 are used where the
+op is bandwidth-bound. Prints one JSON line per case with the achieved rate
+and its fraction of the measured peaks (MEASURED_PEAKS.json when present,
+else the pool's fallback figures).
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import sys
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as fh:
+            d = json.load(fh)
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def time_fn(fn, warmup=5, iters=20):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def bench_gemm():
+    from astrai_b200.ops._ext import native
+
+    hbm, tf, src = peaks()
+    C = native()
+    cases = [
+        # name, M, N, K, a_mn, b_mn  (1.1B dense config, 4 x 2048 tokens)
+        ("qkv_fwd", 8192, 3072, 2048, 0, 0),
+        ("o_fwd", 8192, 2048, 2048, 0, 0),
+        ("upgate_fwd", 8192, 11264, 2048, 0, 0),
+        ("down_fwd", 8192, 2048, 5632, 0, 0),
+        ("lm_head_fwd", 8192, 32000, 2048, 0, 0),
+        ("down_dgrad", 8192, 5632, 2048, 0, 1),
+        ("upgate_wgrad", 11264, 2048, 8192, 1, 1),
+        ("o_wgrad", 2048, 2048, 8192, 1, 1),
+        ("square_8192", 8192, 8192, 8192, 0, 0),
+    ]
+    for name, M, N, K, amn, bmn in cases:
+        a = torch.randn((K, M) if amn else (M, K), device="cuda", dtype=torch.bfloat16)
+        b = torch.randn((K, N) if bmn else (N, K), device="cuda", dtype=torch.bfloat16)
+        d = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        ms = time_fn(lambda: C.gemm(a, b, d, None, amn, bmn, 1.0, 0.0, 0))
+        A = a.t() if amn else a
+        B = b if bmn else b.t()
+        ms_ref = time_fn(lambda: torch.matmul(A, B))
+        fl = 2.0 * M * N * K
+        print(json.dumps({"kernel": "gemm", "case": name, "M": M, "N": N, "K": K, "ms": round(ms, 4),
+                          "tflops": round(fl / ms / 1e9, 1), "frac_of_peak": round(fl / ms / 1e9 / tf, 3),
+                          "peak_src": src, "cublas_ms": round(ms_ref, 4),
+                          "cublas_tflops": round(fl / ms_ref / 1e9, 1)}))
+
+
+def main(argv=None):
+    which = (argv or sys.argv[1:] or ["all"])[0]
+    torch.manual_seed(0)
+    if which in ("gemm", "all"):
+        bench_gemm()
+    if which in ("attn", "all"):
+        try:
+            from astrai_b200.ops.attention import bench_attention
+
+            bench_attention(time_fn, peaks)
+        except ImportError:
+            pass
+
+
+if __name__ == "__main__":
+    main()

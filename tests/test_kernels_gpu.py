@@ -1,0 +1,248 @@
+"""Numerics of every sm_100a kernel against a plain fp32 PyTorch reference.
+
+Small shapes, one launch each; every test also checks the device error word
+that the kernels' bounded waits write, so a stalled pipeline shows up as a
+failure instead of a hang.
+"""
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _clean_error_word():
+    from astrai_b200.ops._ext import native
+
+    native().read_error()
+    yield
+    torch.cuda.synchronize()
+    assert native().read_error() == 0, "a kernel's bounded wait expired"
+
+
+def rel_err(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / b.norm().clamp_min(1e-12)).item()
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 192), (300, 200, 136), (1024, 768, 1024)])
+def test_gemm_majors(a_mn, b_mn, M, N, K):
+    from astrai_b200.ops.gemm import gemm, gemm_reference
+
+    torch.manual_seed(0)
+    a = torch.randn((K, M) if a_mn else (M, K), device="cuda", dtype=torch.bfloat16)
+    b = torch.randn((K, N) if b_mn else (N, K), device="cuda", dtype=torch.bfloat16)
+    if (a.shape[-1] * 2) % 16 or (b.shape[-1] * 2) % 16:
+        pytest.skip("TMA needs 16-byte row strides")
+    d = gemm(a, b, a_mn=bool(a_mn), b_mn=bool(b_mn))
+    ref = gemm_reference(a, b, a_mn=bool(a_mn), b_mn=bool(b_mn))
+    assert rel_err(d, ref) < 1e-2
+
+
+@pytest.mark.parametrize("force_bn", [128, 256])
+def test_gemm_tiles_and_epilogue(force_bn):
+    from astrai_b200.ops._ext import native
+    from astrai_b200.ops.gemm import gemm_reference
+
+    torch.manual_seed(1)
+    M, N, K = 640, 1280, 512
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+    c = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
+    d = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    native().gemm(a, b, d, c, 0, 0, 0.5, -2.0, force_bn)
+    ref = gemm_reference(a, b, c=c, alpha=0.5, beta=-2.0)
+    assert rel_err(d, ref) < 1e-2
+    d32 = torch.empty(M, N, device="cuda", dtype=torch.float32)
+    native().gemm(a, b, d32, None, 0, 0, 1.0, 0.0, force_bn)
+    assert rel_err(d32, gemm_reference(a, b)) < 5e-3
+
+
+def test_gemm_batched():
+    from astrai_b200.ops.gemm import gemm, gemm_reference
+
+    torch.manual_seed(2)
+    x = torch.randn(3, 256, 384, device="cuda", dtype=torch.bfloat16)
+    # X X^T and (A) X with MN-major B, as in Newton-Schulz
+    a = gemm(x, x)
+    assert rel_err(a, gemm_reference(x, x)) < 1e-2
+    y = gemm(a, x, b_mn=True)
+    assert rel_err(y, gemm_reference(a, x, b_mn=True)) < 1e-2
+
+
+def test_linear_autograd():
+    from astrai_b200.ops.gemm import linear
+
+    torch.manual_seed(3)
+    x = torch.randn(4, 96, 512, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = (torch.randn(768, 512, device="cuda") * 0.05).to(torch.bfloat16).requires_grad_()
+    r = torch.randn(4, 96, 768, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    y = linear(x, w, residual=r)
+    g = torch.randn_like(y)
+    y.backward(g)
+    xf, wf, rf = x.detach().float().requires_grad_(), w.detach().float().requires_grad_(), r.detach().float().requires_grad_()
+    yf = xf @ wf.t() + rf
+    yf.backward(g.float())
+    assert rel_err(y, yf) < 1e-2
+    assert rel_err(x.grad, xf.grad) < 1e-2
+    assert rel_err(w.grad, wf.grad) < 1e-2
+    assert rel_err(r.grad, rf.grad) < 1e-3
+
+
+@pytest.mark.parametrize("D", [128, 1024, 2048, 4096])
+def test_rmsnorm(D):
+    from astrai_b200.ops.norm import rms_norm
+
+    torch.manual_seed(4)
+    x = torch.randn(333, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = (1 + 0.1 * torch.randn(D, device="cuda")).to(torch.bfloat16).requires_grad_()
+    y = rms_norm(x, w, 1e-5)
+    g = torch.randn_like(y)
+    y.backward(g)
+    xf, wf = x.detach().float().requires_grad_(), w.detach().float().requires_grad_()
+    yf = F.rms_norm(xf, (D,), wf, 1e-5)
+    yf.backward(g.float())
+    assert rel_err(y, yf) < 1e-2
+    assert rel_err(x.grad, xf.grad) < 1e-2
+    assert rel_err(w.grad, wf.grad) < 1e-2
+
+
+def test_rope_inplace_roundtrip():
+    from astrai_b200.ops.rope import apply_rope_reference, rope_inplace, rope_table
+
+    torch.manual_seed(5)
+    B, S, H, Hkv, D = 2, 64, 4, 2, 128
+    qkv = torch.randn(B * S, (H + 2 * Hkv) * D, device="cuda", dtype=torch.bfloat16)
+    tab = rope_table(D, 256, 10000.0, device="cuda")
+    ref_q = apply_rope_reference(qkv[:, : H * D].view(B, S, H, D), tab[:S].unsqueeze(0).expand(B, -1, -1, -1))
+    buf = qkv.clone()
+    rope_inplace(buf, 0, H + Hkv, D, tab, None, S)
+    assert rel_err(buf[:, : H * D].view(B, S, H, D), ref_q) < 1e-2
+    assert torch.equal(buf[:, (H + Hkv) * D :], qkv[:, (H + Hkv) * D :])
+    rope_inplace(buf, 0, H + Hkv, D, tab, None, S, inverse=True)
+    assert rel_err(buf, qkv) < 1e-2
+
+
+def test_swiglu():
+    from astrai_b200.ops.activation import swiglu
+
+    torch.manual_seed(6)
+    h = torch.randn(257, 2 * 688, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    y = swiglu(h)
+    g = torch.randn_like(y)
+    y.backward(g)
+    hf = h.detach().float().requires_grad_()
+    yf = hf[:, :688] * F.silu(hf[:, 688:])
+    yf.backward(g.float())
+    assert rel_err(y, yf) < 1e-2
+    assert rel_err(h.grad, hf.grad) < 1e-2
+
+
+@pytest.mark.parametrize("V", [1000, 32000])
+def test_cross_entropy_and_logprobs(V):
+    from astrai_b200.ops.loss import cross_entropy, token_logprobs
+
+    torch.manual_seed(7)
+    x = (3 * torch.randn(130, V, device="cuda")).to(torch.bfloat16).requires_grad_()
+    t = torch.randint(0, V, (130,), device="cuda")
+    t[::7] = -100
+    loss = cross_entropy(x, t, label_smoothing=0.05)
+    loss.backward()
+    xf = x.detach().float().requires_grad_()
+    lf = F.cross_entropy(xf, t, label_smoothing=0.05, ignore_index=-100)
+    lf.backward()
+    assert abs(loss.item() - lf.item()) < 2e-3 * max(1.0, abs(lf.item()))
+    assert rel_err(x.grad, xf.grad) < 2e-2
+    x.grad = None
+    t2 = t.clamp_min(0)
+    lp = token_logprobs(x, t2)
+    g = torch.randn_like(lp)
+    lp.backward(g)
+    xf2 = x.detach().float().requires_grad_()
+    lpf = torch.log_softmax(xf2, -1).gather(-1, t2[:, None]).squeeze(-1)
+    lpf.backward(g)
+    assert rel_err(lp, lpf) < 1e-3
+    assert rel_err(x.grad, xf2.grad) < 2e-2
+
+
+def test_embedding():
+    from astrai_b200.ops.embedding import embedding
+
+    torch.manual_seed(8)
+    w = torch.randn(1000, 256, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    ids = torch.randint(0, 1000, (4, 77), device="cuda")
+    y = embedding(ids, w)
+    g = torch.randn_like(y)
+    y.backward(g)
+    wf = w.detach().float().requires_grad_()
+    yf = F.embedding(ids, wf)
+    yf.backward(g.float())
+    assert torch.equal(y.float(), yf)
+    assert rel_err(w.grad, wf.grad) < 1e-2
+
+
+@pytest.mark.parametrize("B,S,Hq,Hkv,causal", [(1, 128, 2, 1, True), (2, 256, 4, 2, True), (1, 200, 4, 4, True),
+                                                (2, 384, 8, 2, False), (1, 300, 2, 2, False)])
+def test_flash_attention(B, S, Hq, Hkv, causal):
+    from astrai_b200.ops.attention import attention, attention_reference
+
+    torch.manual_seed(9)
+    D = 128
+    q = torch.randn(B, S, Hq, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn(B, S, Hkv, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    v = torch.randn(B, S, Hkv, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    o = attention(q, k, v, causal=causal)
+    g = torch.randn_like(o)
+    o.backward(g)
+    qf, kf, vf = (t.detach().float().requires_grad_() for t in (q, k, v))
+    of = attention_reference(qf, kf, vf, causal=causal)
+    of.backward(g.float())
+    assert rel_err(o, of) < 2e-2
+    assert rel_err(q.grad, qf.grad) < 3e-2
+    assert rel_err(k.grad, kf.grad) < 3e-2
+    assert rel_err(v.grad, vf.grad) < 3e-2
+
+
+def test_flash_attention_segments():
+    from astrai_b200.ops.attention import attention, attention_reference
+
+    torch.manual_seed(10)
+    B, S, Hq, Hkv, D = 2, 256, 2, 1, 128
+    seg = torch.zeros(B, S, dtype=torch.int32, device="cuda")
+    seg[0, 100:] = 1
+    seg[1, 37:180] = 1
+    seg[1, 180:] = 2
+    q = torch.randn(B, S, Hq, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn(B, S, Hkv, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    v = torch.randn(B, S, Hkv, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    o = attention(q, k, v, causal=True, seg=seg)
+    g = torch.randn_like(o)
+    o.backward(g)
+    qf, kf, vf = (t.detach().float().requires_grad_() for t in (q, k, v))
+    of = attention_reference(qf, kf, vf, causal=True, seg=seg)
+    of.backward(g.float())
+    assert rel_err(o, of) < 2e-2
+    assert rel_err(q.grad, qf.grad) < 3e-2
+    assert rel_err(k.grad, kf.grad) < 3e-2
+
+
+def test_attention_qkv_fused_rope():
+    from astrai_b200.ops.attention import attention_qkv
+    from astrai_b200.ops.rope import rope_table
+
+    torch.manual_seed(11)
+    B, S, Hq, Hkv, D = 2, 256, 4, 2, 128
+    tab = rope_table(D, 512, 1e6, device="cuda")
+    qkv = torch.randn(B * S, (Hq + 2 * Hkv) * D, device="cuda", dtype=torch.bfloat16)
+    x1 = qkv.clone().requires_grad_()
+    o = attention_qkv(x1.clone(), B, S, Hq, Hkv, tab)
+    g = torch.randn_like(o)
+    o.backward(g)
+    x2 = qkv.cpu().float().requires_grad_()
+    o2 = attention_qkv(x2, B, S, Hq, Hkv, tab.cpu())
+    o2.backward(g.cpu().float())
+    assert rel_err(o.cpu(), o2) < 2e-2
+    assert rel_err(x1.grad.cpu(), x2.grad) < 3e-2
