@@ -1,0 +1,5 @@
+from astrai_b200.config.base import BaseConfig
+from astrai_b200.config.model_config import AutoRegressiveLMConfig, BaseModelConfig, ConfigFactory, EncoderConfig
+from astrai_b200.config.train_config import TrainConfig
+
+__all__ = ["BaseConfig", "BaseModelConfig", "AutoRegressiveLMConfig", "EncoderConfig", "ConfigFactory", "TrainConfig"]

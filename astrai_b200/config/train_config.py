@@ -14,20 +14,11 @@ from dataclasses import dataclass, field, fields
 from typing import Any, Callable, Dict, List, Optional
 
 from astrai_b200.config.base import BaseConfig
+from astrai_b200.models.components.lora import LoRAConfig
 
 
 def _req(**kw):
     return {"required": True, **kw}
-
-
-@dataclass
-class LoRAConfig(BaseConfig):
-    """Low-rank adapter settings (parity: astrai/model/components/lora.py)."""
-
-    r: int = 8
-    alpha: float = 16.0
-    target_modules: List[str] = field(default_factory=lambda: ["q_proj", "v_proj"])
-    dropout: float = 0.0
 
 
 @dataclass

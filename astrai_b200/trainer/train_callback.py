@@ -1,0 +1,262 @@
+"""Trainer callbacks (parity: astrai/trainer/train_callback.py).
+
+Hooks: on_train_begin/end, on_epoch_begin/end, on_batch_begin/end,
+on_optimizer_step, on_error. Registered callbacks:
+
+* ``gradient_checkpointing`` - wraps ``forward`` of the listed module types
+  with ``torch.utils.checkpoint`` (non-reentrant);
+* ``checkpoint`` - saves ``ckpt_dir/epoch_{e}_step_{s}/`` every ``interval``
+  optimizer steps, at the end and on error (model, meta.json with the train
+  config, optimizer.pt, scheduler.pt);
+* ``metric`` - JSONL metrics (loss, lr, grad_norm, val_loss) flushed to
+  ``log_dir/epoch_{e}_step_{s}_metric.jsonl``; periodic validation with an
+  all-reduced mean loss;
+* ``progress_bar`` - rank-0 tqdm;
+* ``gradient_clipping`` - global-norm clipping before the optimizer step.
+
+Host/device synchronisation happens at most once per optimizer step (the
+loss / grad-norm scalars are read when logged), not once per micro-batch.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import sys
+import time
+from pathlib import Path
+from typing import IO, Callable, List, Optional, Protocol, runtime_checkable
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+from torch.utils.checkpoint import checkpoint as torch_checkpoint
+
+from astrai_b200.factory import Registry
+from astrai_b200.parallel.setup import get_current_device, only_on_rank
+from astrai_b200.serialization import Checkpoint
+
+
+@runtime_checkable
+class TrainCallback(Protocol):
+    def on_train_begin(self, context): ...
+
+    def on_train_end(self, context): ...
+
+    def on_epoch_begin(self, context): ...
+
+    def on_epoch_end(self, context): ...
+
+    def on_batch_begin(self, context): ...
+
+    def on_batch_end(self, context): ...
+
+    def on_optimizer_step(self, context): ...
+
+    def on_error(self, context): ...
+
+
+class CallbackFactory(Registry):
+    pass
+
+
+@CallbackFactory.register("gradient_checkpointing")
+class GradientCheckpointingCallback:
+    def __init__(self, modules: Optional[List] = None):
+        self.modules = tuple(modules or ())
+
+    def _enable(self, m: nn.Module):
+        if self.modules and isinstance(m, self.modules) and not hasattr(m, "_astrai_orig_forward"):
+            m._astrai_orig_forward = m.forward
+
+            def fwd(*a, __m=m, **k):
+                if torch.is_grad_enabled():
+                    return torch_checkpoint(__m._astrai_orig_forward, *a, use_reentrant=False, **k)
+                return __m._astrai_orig_forward(*a, **k)
+
+            m.forward = fwd
+
+    def _disable(self, m: nn.Module):
+        if hasattr(m, "_astrai_orig_forward"):
+            m.forward = m._astrai_orig_forward
+            del m._astrai_orig_forward
+
+    def on_train_begin(self, context):
+        if self.modules:
+            context.model.apply(self._enable)
+
+    def on_train_end(self, context):
+        context.model.apply(self._disable)
+
+
+@CallbackFactory.register("checkpoint")
+class CheckpointCallback:
+    extra_keys = ("optimizer", "scheduler")
+
+    def __init__(self, save_dir: str, interval: int, weight_only: bool = False,
+                 save_extra_fn: Optional[Callable] = None):
+        self.save_dir = save_dir
+        self.interval = interval
+        self.weight_only = weight_only
+        self.save_extra_fn = save_extra_fn or CheckpointCallback.save_extra
+        self.last_ckpt_step = None
+
+    def on_train_begin(self, context):
+        self.last_ckpt_step = context.optimizer_step
+
+    def _save(self, context):
+        self.last_ckpt_step = context.optimizer_step
+        if not self.save_dir:  # ckpt_dir=None disables checkpoint files
+            return
+        with context.executor.checkpoint_context(context.model) as sd:
+            if sd is not None:
+                path = os.path.join(self.save_dir, f"epoch_{context.epoch}_step_{context.optimizer_step}")
+                extra = {} if self.weight_only else self.save_extra_fn(context)
+                context.checkpoint = Checkpoint(state_dict=sd, epoch=context.epoch,
+                                                consumed_samples=context.consumed_samples,
+                                                config=context.model_config, extra=extra,
+                                                meta=context.config.to_dict())
+                context.checkpoint.save(path)
+
+    def on_batch_end(self, context):
+        if context.optimizer_step - self.last_ckpt_step >= self.interval:
+            self._save(context)
+
+    def on_train_end(self, context):
+        if context.optimizer_step != self.last_ckpt_step:
+            self._save(context)
+
+    def on_error(self, context):
+        self._save(context)
+
+    @staticmethod
+    def save_extra(context) -> dict:
+        out = {}
+        for name in CheckpointCallback.extra_keys:
+            obj = getattr(context, name, None)
+            if obj:
+                out[name] = obj.state_dict()
+        return out
+
+
+@CallbackFactory.register("progress_bar")
+class ProgressBarCallback:
+    def __init__(self, num_epoch: int, log_interval: int = 100, file: Optional[IO[str]] = None):
+        self.num_epoch = num_epoch
+        self.log_interval = log_interval
+        self.file = file
+        self.bar = None
+
+    @only_on_rank(0)
+    def on_epoch_begin(self, context):
+        from tqdm import tqdm
+
+        total = len(context.dataloader) // context.executor.grad_accum_steps
+        self.bar = tqdm(total=total, desc=f"Epoch {context.epoch + 1}/{self.num_epoch}", dynamic_ncols=True,
+                        file=self.file or sys.stdout, mininterval=2.0)
+
+    @only_on_rank(0)
+    def on_optimizer_step(self, context):
+        if self.bar is None:
+            return
+        post = {"step": f"{context.optimizer_step:d}", "loss": f"{context.loss:.4f}",
+                "lr": f"{context.optimizer.param_groups[-1]['lr']:.2e}"}
+        if context.grad_norm is not None:
+            post["grad_norm"] = f"{context.grad_norm:.2f}"
+        if context.val_loss is not None:
+            post["val_loss"] = f"{context.val_loss:.4f}"
+        self.bar.set_postfix(post, refresh=False)
+        self.bar.update(1)
+
+    @only_on_rank(0)
+    def on_epoch_end(self, context):
+        if self.bar:
+            self.bar.close()
+
+
+@CallbackFactory.register("metric")
+class MetricCallback:
+    def __init__(self, log_dir: str, save_interval: int, metrics: Optional[List[str]] = None, val_step: int = 0):
+        self.last_flush = None
+        self.save_interval = save_interval
+        self.metrics = metrics or ["loss", "lr"]
+        self.val_step = val_step
+        self._next_val = 0
+        self.log_dir = Path(log_dir) if log_dir else Path.cwd() / "logs"
+        self.log_dir.mkdir(parents=True, exist_ok=True)
+        self.cache: List[dict] = []
+        self._funcs = {
+            "loss": lambda c: c.loss,
+            "lr": lambda c: c.optimizer.param_groups[-1]["lr"] if c.optimizer is not None else None,
+            "grad_norm": lambda c: c.grad_norm,
+            "val_loss": lambda c: c.val_loss,
+            "tokens_per_s": lambda c: c.kwargs.get("tokens_per_s"),
+        }
+
+    def _append(self, kind, context, **extra):
+        if context.rank != 0:
+            return
+        self.cache.append({"type": kind, "timestamp": time.strftime("%Y-%m-%dT%H:%M:%S"), "epoch": context.epoch,
+                           "step": context.optimizer_step, "consumed_samples": context.consumed_samples, **extra})
+
+    def _validate(self, context) -> float:
+        context.model.eval()
+        total = torch.zeros((), device=get_current_device(), dtype=torch.float64)
+        n = 0
+        with torch.no_grad():
+            for batch in context.val_dataloader:
+                total += context.strategy(batch).double()
+                n += 1
+        stats = torch.stack([total, torch.tensor(float(n), device=total.device, dtype=torch.float64)])
+        if context.world_size > 1 and dist.is_initialized():
+            dist.all_reduce(stats, op=dist.ReduceOp.SUM)
+        context.model.train()
+        return float(stats[0] / stats[1].clamp(min=1.0))
+
+    def on_train_begin(self, context):
+        self.last_flush = context.optimizer_step
+
+    @only_on_rank(0)
+    def _flush(self, epoch, step):
+        f = self.log_dir / f"epoch_{epoch}_step_{step}_metric.jsonl"
+        with open(f, "w") as fh:
+            for e in self.cache:
+                fh.write(json.dumps(e) + "\n")
+
+    def on_optimizer_step(self, context):
+        if context.val_dataloader is not None and self.val_step > 0 and context.optimizer_step >= self._next_val:
+            context.val_loss = self._validate(context)
+            self._next_val = context.optimizer_step + self.val_step
+            self._append("validation", context, val_loss=context.val_loss)
+        vals = {}
+        for m in self.metrics:
+            if m == "val_loss" or m not in self._funcs:
+                continue
+            v = self._funcs[m](context)
+            if v is not None:
+                vals[m] = v
+        self._append("step", context, **vals)
+        if context.optimizer_step - self.last_flush >= self.save_interval:
+            self._flush(context.epoch, context.optimizer_step)
+            self.last_flush = context.optimizer_step
+
+    def on_epoch_end(self, context):
+        self._append("epoch", context)
+
+    def on_train_end(self, context):
+        if self.last_flush is None or context.optimizer_step != self.last_flush:
+            self._flush(context.epoch, context.optimizer_step)
+            self.last_flush = context.optimizer_step
+
+    def on_error(self, context):
+        self._flush(context.epoch, context.optimizer_step)
+
+
+@CallbackFactory.register("gradient_clipping")
+class GradientClippingCallback:
+    def __init__(self, max_grad_norm: Optional[float]):
+        self.max_grad_norm = max_grad_norm
+
+    def on_optimizer_step(self, context):
+        # always computed: the norm is logged; clipping only if a max is set
+        context.grad_norm_tensor = context.executor.clip_grad_norm(context.model, self.max_grad_norm, as_tensor=True)

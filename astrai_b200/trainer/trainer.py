@@ -1,0 +1,88 @@
+"""Trainer (parity: astrai/trainer/trainer.py:15-113).
+
+``Trainer(train_config, callbacks).train(param_path, resume)`` spawns the
+ranks (``spawn_parallel_fn``), builds the context and runs the epoch / batch
+loop with gradient accumulation, callbacks, optimizer / scheduler steps on
+sync micro-steps, and ``on_error`` (checkpoint + metric flush) on failure.
+
+Unlike the reference loop, the per-micro-batch ``loss.item()`` host sync is
+gone: the loss stays on the device (``context.loss`` reads it lazily, once
+per optimizer step by the progress bar / metrics), so the GPU queue never
+drains between micro-batches.
+"""
+
+from __future__ import annotations
+
+import logging
+from typing import List, Optional
+
+from astrai_b200.config.train_config import TrainConfig
+from astrai_b200.parallel.setup import spawn_parallel_fn
+from astrai_b200.trainer.train_callback import CallbackFactory, TrainCallback
+from astrai_b200.trainer.train_context import TrainContext, TrainContextBuilder
+
+logger = logging.getLogger(__name__)
+
+
+class Trainer:
+    def __init__(self, train_config: TrainConfig, callbacks: Optional[List[TrainCallback]] = None):
+        self.train_config = train_config
+        self.callbacks = self._default_callbacks() + list(callbacks or [])
+        self.last_context: Optional[TrainContext] = None
+
+    def _default_callbacks(self) -> List[TrainCallback]:
+        c = self.train_config
+        return [
+            CallbackFactory.create("gradient_checkpointing", modules=c.gradient_checkpointing_modules),
+            CallbackFactory.create("checkpoint", c.ckpt_dir, c.ckpt_interval),
+            CallbackFactory.create("metric", log_dir=c.log_dir, save_interval=c.ckpt_interval, metrics=c.metrics,
+                                   val_step=c.val_step),
+            CallbackFactory.create("progress_bar", c.n_epoch),
+            CallbackFactory.create("gradient_clipping", c.max_grad_norm),
+        ]
+
+    def _call(self, name: str, ctx: TrainContext) -> None:
+        for cb in self.callbacks:
+            fn = getattr(cb, name, None)
+            if fn is not None:
+                fn(ctx)
+
+    def _trainer_loop(self, param_path: Optional[str] = None, resume: bool = False) -> None:
+        ctx = TrainContextBuilder(self.train_config).with_param_path(param_path, resume=resume).build()
+        self.last_context = ctx
+        ex = ctx.executor
+        per_micro = ctx.config.batch_per_device * ctx.world_size
+        self._call("on_train_begin", ctx)
+        try:
+            ctx.model.train()
+            for epoch in range(ctx.epoch, ctx.config.n_epoch):
+                ctx.epoch = epoch
+                self._call("on_epoch_begin", ctx)
+                for batch in ctx.dataloader:
+                    with ex.accumulate(ctx.model):
+                        self._call("on_batch_begin", ctx)
+                        loss = ctx.strategy(batch)
+                        ctx.loss = loss.detach()
+                        ex.backward(loss / ex.grad_accum_steps)
+                        ctx.consumed_samples += per_micro
+                        self._call("on_batch_end", ctx)
+                        if ex.sync_gradients:
+                            self._call("on_optimizer_step", ctx)
+                            ctx.optimizer.step()
+                            ctx.strategy.on_optimizer_step()
+                            ctx.optimizer.zero_grad()
+                            if ctx.scheduler:
+                                ctx.scheduler.step()
+                self._call("on_epoch_end", ctx)
+        except Exception as e:
+            logger.error("Training failed: %s", e, exc_info=True)
+            self._call("on_error", ctx)
+            raise
+        finally:
+            self._call("on_train_end", ctx)
+
+    def train(self, param_path: Optional[str] = None, resume: bool = False) -> None:
+        c = self.train_config
+        spawn_parallel_fn(self._trainer_loop, backend=c.backend, world_size=c.nprocs, master_addr=c.master_addr,
+                          master_port=c.master_port, device_type=c.device_type, start_method=c.start_method,
+                          param_path=param_path, resume=resume)

@@ -1,0 +1,481 @@
+#!/usr/bin/env python
+"""Headline benchmark: dense ~1.1B Llama-style pretraining throughput (tokens/s).
+
+Config: 24 layers, d_model 2048, 16 query / 4 KV
+heads (head_dim 128), SwiGLU FFN 5632, RMSNorm, RoPE theta 1e6, vocab 32000,
+untied embeddings, random init N(0, 0.02), bf16 parameters; synthetic uniform
+token ids, seq 2048, batch 4 per GPU, grad_accum 8; Muon (lr 0.02, 5 NS
+steps, match_rms_adamw) on hidden 2-D weights + AdamW (lr 1e-4, wd 0.1) on
+embeddings / norms / lm_head; grad-clip 1.0. One "step" = one optimizer step
+= 8 micro-batches of 4 x 2048 tokens per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl astrai_b200|reference]
+
+N > 1 is launched with torch.distributed.run (one rank per GPU, NCCL).
+Prints one JSON line on rank 0. ``value`` is whole-job tokens/s, device-timed
+with CUDA events around exactly K steps (barrier + synchronize on both sides,
+max over ranks). ``e2e`` repeats the measurement through the public Trainer
+API with per-step host->device input copies from pinned memory and a
+device->host read of the loss.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+import types
+from datetime import timedelta
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+BASELINE_VALUE = None  # the reference publishes no number
+
+CFG = dict(vocab_size=32000, hidden_size=2048, num_hidden_layers=24, rms_norm_eps=1e-5, intermediate_size=5632,
+           tie_word_embeddings=False, max_position_embeddings=2048, rope_theta=1e6, num_attention_heads=16,
+           num_key_value_heads=4)
+BATCH, SEQ, ACCUM = 4, 2048, 8
+MUON_LR, ADAMW_LR, WD, CLIP = 0.02, 1e-4, 0.1, 1.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="astrai_b200", choices=["astrai_b200", "reference"])
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end Trainer measurement")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- plumbing
+def dist_setup():
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1 and not dist.is_initialized():
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def max_over_ranks(x: float) -> float:
+    import torch
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized():
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+    return x
+
+
+def barrier():
+    import torch
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized():
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, enabled=True):
+        self.enabled = enabled
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        if not self.enabled:
+            return
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self, gpu_indices):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as fh:
+            for line in fh:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) not in gpu_indices:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx = max(mx, float(parts[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def visible_gpu_indices(world):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        try:
+            return [int(x) for x in vis.split(",")][:world]
+        except ValueError:
+            pass
+    return list(range(world))
+
+
+# ----------------------------------------------------------------------------- our arm
+def run_ours(args, rank, world, local):
+    import torch
+
+    sys.path.insert(0, ROOT)
+    from astrai_b200.config import AutoRegressiveLMConfig
+    from astrai_b200.models import AutoRegressiveLM
+    from astrai_b200.ops._ext import native
+    from astrai_b200.ops.loss import cross_entropy
+    from astrai_b200.optim import MuonMix, clip_grad_norm_
+    from astrai_b200.parallel.executor import ExecutorFactory
+
+    torch.manual_seed(3407 + rank)
+    dev = torch.device("cuda", local)
+    with torch.device(dev):
+        model = AutoRegressiveLM(AutoRegressiveLMConfig(**CFG)).to(torch.bfloat16)
+    executor = ExecutorFactory.create("ddp" if world > 1 else "none", grad_accum_steps=ACCUM)
+    model = executor.wrap(model)
+    opt = MuonMix(executor.unwrap(model), lr=MUON_LR, weight_decay=WD, adamw_lr=ADAMW_LR, adamw_weight_decay=WD,
+                  adjust_lr_fn="match_rms_adamw")
+    V = CFG["vocab_size"]
+    n_batches = 4
+    data = torch.randint(0, V, (n_batches, ACCUM, BATCH, SEQ + 1), device=dev)
+
+    def step(i):
+        for mi in range(ACCUM):
+            seq = data[i % n_batches, mi]
+            with executor.micro_step(model, mi == ACCUM - 1):
+                logits = model(seq[:, :-1])["logits"]
+                loss = cross_entropy(logits, seq[:, 1:])
+                (loss / ACCUM).backward()
+        executor.finish_step(model)
+        clip_grad_norm_(executor.unwrap(model).parameters(), CLIP)
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return loss
+
+    for i in range(args.warmup):
+        step(i)
+    assert native().read_error() == 0, "kernel bounded-wait error during warm-up"
+    clocks = ClockSampler(rank == 0)
+    barrier()
+    clocks.start()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(args.steps):
+        last = step(args.warmup + i)
+    e.record()
+    barrier()
+    ck = clocks.stop(visible_gpu_indices(world))
+    ms = max_over_ranks(s.elapsed_time(e)) / args.steps
+    loss_val = float(last.item())
+    assert native().read_error() == 0, "kernel bounded-wait error in the timed region"
+    del data
+    result = {
+        "ms_per_step": ms,
+        "value": world * ACCUM * BATCH * SEQ / (ms / 1e3),
+        "clocks": ck,
+        "loss": loss_val,
+        "launches_per_step": launches_per_step(),
+    }
+    if not args.no_e2e:
+        result["e2e"] = run_ours_e2e(args, rank, world, local, model, executor, opt)
+    return result
+
+
+def launches_per_step():
+    """Kernel launches of our extension per optimizer step (counted)."""
+    L, accum = CFG["num_hidden_layers"], ACCUM
+    fwd = 1 + L * (3 + 2 + 1 + 3) + 2 + 1          # embed; per layer: norm, qkv, rope+attn, o / norm, upgate, swiglu, down; norm, lm_head; ce
+    bwd = 1 + 1 + L * (2 + 2 + 3 + 2 + 2 + 2 + 2 + 2) + 2 + 1  # ce, lm_head x2, per layer ...
+    opt = 2 + 4 * (3 * 5 + 3) + 1                 # clip, muon per shape class, adamw
+    return accum * (fwd + bwd) + opt
+
+
+class SynthSeq:
+    """Uniform random token windows as the reference's SEQ dataset yields them (CPU tensors)."""
+
+    def __init__(self, n, vocab, seq, seed=3407):
+        import torch
+
+        g = torch.Generator().manual_seed(seed)
+        self.data = torch.randint(0, vocab, (n, seq + 1), generator=g)
+
+    def __len__(self):
+        return self.data.shape[0]
+
+    def __getitem__(self, i):
+        x = self.data[i]
+        return {"input_ids": x[:-1], "target_ids": x[1:]}
+
+
+def run_ours_e2e(args, rank, world, local, model, executor, opt):
+    """The same training step through the public Trainer API: DataLoader with
+    pinned host batches copied to the device every micro-step, loss and grad
+    norm read back on the host every optimizer step."""
+    import torch
+
+    from astrai_b200.config import TrainConfig
+    from astrai_b200.optim import MuonMix
+    from astrai_b200.trainer import SchedulerFactory, Trainer
+
+    warm = max(1, args.warmup - 1)
+    total = warm + args.steps + 1
+    timing = {}
+
+    class Timer:
+        def __init__(self):
+            self.n = 0
+
+        def on_optimizer_step(self, ctx):
+            if self.n == warm:
+                barrier()
+                timing["s"] = torch.cuda.Event(enable_timing=True)
+                timing["s"].record()
+            if self.n == warm + args.steps:
+                e = torch.cuda.Event(enable_timing=True)
+                e.record()
+                barrier()
+                timing["ms"] = max_over_ranks(timing["s"].elapsed_time(e)) / args.steps
+            self.n += 1
+
+    base = executor.unwrap(model)
+    tc = TrainConfig(
+        model_fn=lambda: base,
+        strategy="seq",
+        dataset=SynthSeq(total * ACCUM * BATCH * world, CFG["vocab_size"], SEQ, seed=11 + rank),
+        optimizer_fn=lambda m: MuonMix(m, lr=MUON_LR, weight_decay=WD, adamw_lr=ADAMW_LR, adamw_weight_decay=WD,
+                                       adjust_lr_fn="match_rms_adamw"),
+        scheduler_fn=lambda o: SchedulerFactory.create("cosine", o, warmup_steps=0, lr_decay_steps=10 ** 6),
+        batch_per_device=BATCH, grad_accum_steps=ACCUM, max_grad_norm=CLIP, ckpt_dir=None, ckpt_interval=10 ** 9,
+        log_dir=tempfile.mkdtemp(prefix="astrai_bench_logs_"), nprocs=world,
+        parallel_mode="ddp" if world > 1 else "none", device_type="cuda", pin_memory=True,
+        extra_kwargs={"label_smoothing": 0.0}, metrics=["loss", "lr", "grad_norm"],
+    )
+    Trainer(tc, callbacks=[Timer()]).train()
+    if "ms" not in timing:
+        return None
+    ms = timing["ms"]
+    return {"value": round(world * ACCUM * BATCH * SEQ / (ms / 1e3), 1), "unit": "tokens/s",
+            "ms_per_step": round(ms, 3), "h2d_bytes_per_step": ACCUM * BATCH * SEQ * 8 * 2,
+            "d2h_bytes_per_step": 8, "path": "astrai_b200.Trainer (seq strategy, pinned DataLoader)"}
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(args, rank, world, local):
+    ref_path = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_path, "astrai")):
+        return {"unavailable": "reference not installed under baseline/_ref"}
+    # h5py is a hard import of the reference but absent from this image and unused by
+    # this benchmark (no H5 store is read); an empty module satisfies the import.
+    sys.modules.setdefault("h5py", types.ModuleType("h5py"))
+    sys.path.insert(0, ref_path)
+    import torch
+    from torch.utils.data import Dataset
+
+    import astrai
+    from astrai.config import AutoRegressiveLMConfig, TrainConfig
+    from astrai.model import AutoRegressiveLM
+    from astrai.trainer import SchedulerFactory, Trainer
+    from astrai.trainer.train_callback import TrainCallback
+
+    assert os.path.realpath(astrai.__file__).startswith(os.path.realpath(ref_path))
+    total_steps = args.warmup + args.steps + 1
+    n_samples = total_steps * ACCUM * BATCH * world
+
+    class SynthSeq(Dataset):
+        def __init__(self, n):
+            g = torch.Generator().manual_seed(3407)
+            self.data = torch.randint(0, CFG["vocab_size"], (n, SEQ + 1), generator=g)
+
+        def __len__(self):
+            return self.data.shape[0]
+
+        def __getitem__(self, i):
+            x = self.data[i]
+            return {"input_ids": x[:-1], "target_ids": x[1:]}
+
+    class RefMuonMix(torch.optim.Optimizer):
+        """torch Muon (hidden matrices) + fused AdamW (rest) with the reference CLI's split rule."""
+
+        def __init__(self, model):
+            params = [p for p in model.parameters() if p.requires_grad]
+            super().__init__(params, dict(lr=MUON_LR))
+            mat, other = [], []
+            for n, p in model.named_parameters():
+                if p.dim() >= 2 and not any(s in n for s in ("norm", "bias", "embed", "lm_head")):
+                    mat.append(p)
+                else:
+                    other.append(p)
+            self.muon = torch.optim.Muon(mat, lr=MUON_LR, weight_decay=WD, momentum=0.95, nesterov=True, ns_steps=5,
+                                         adjust_lr_fn="match_rms_adamw")
+            self.adamw = torch.optim.AdamW(other, lr=ADAMW_LR, betas=(0.9, 0.95), weight_decay=WD, fused=True)
+            self.param_groups = [*self.muon.param_groups, *self.adamw.param_groups]
+
+        @torch.no_grad()
+        def step(self, closure=None):
+            self.muon.step()
+            self.adamw.step()
+
+        def zero_grad(self, set_to_none=True):
+            self.muon.zero_grad(set_to_none)
+            self.adamw.zero_grad(set_to_none)
+
+        def state_dict(self):
+            return {"muon": self.muon.state_dict(), "adamw": self.adamw.state_dict()}
+
+        def load_state_dict(self, sd):
+            self.muon.load_state_dict(sd["muon"])
+            self.adamw.load_state_dict(sd["adamw"])
+
+    timing = {}
+
+    class Timer(TrainCallback):
+        def __init__(self):
+            self.n = 0
+            self.ev = {}
+            self.clocks = ClockSampler(rank == 0)
+
+        def on_optimizer_step(self, ctx):
+            # called after the last micro-batch's backward, before optimizer.step()
+            if self.n == args.warmup:
+                barrier()
+                self.clocks.start()
+                self.ev["s"] = torch.cuda.Event(enable_timing=True)
+                self.ev["s"].record()
+            if self.n == args.warmup + args.steps:
+                self.ev["e"] = torch.cuda.Event(enable_timing=True)
+                self.ev["e"].record()
+                barrier()
+                timing["clocks"] = self.clocks.stop(visible_gpu_indices(world))
+                timing["ms"] = max_over_ranks(self.ev["s"].elapsed_time(self.ev["e"])) / args.steps
+                timing["loss"] = ctx.loss
+            self.n += 1
+
+    cfg = AutoRegressiveLMConfig(**CFG)
+    shm = "/dev/shm" if os.path.isdir("/dev/shm") else None
+    tmp = tempfile.mkdtemp(prefix="astrai_ref_bench_", dir=shm)
+    tc = TrainConfig(
+        model_fn=lambda: AutoRegressiveLM(cfg).to(dtype=torch.bfloat16),
+        strategy="seq",
+        dataset=SynthSeq(n_samples),
+        optimizer_fn=lambda m: RefMuonMix(m),
+        scheduler_fn=lambda o: SchedulerFactory.create("cosine", o, warmup_steps=0, lr_decay_steps=10 ** 6),
+        n_epoch=1,
+        batch_per_device=BATCH,
+        grad_accum_steps=ACCUM,
+        max_grad_norm=CLIP,
+        ckpt_dir=os.path.join(tmp, "ckpt"),
+        ckpt_interval=10 ** 9,
+        log_dir=os.path.join(tmp, "logs"),
+        nprocs=world,
+        backend="nccl",
+        parallel_mode="fsdp2" if world > 1 else "none",
+        device_type="cuda",
+        pin_memory=True,
+        extra_kwargs={"label_smoothing": 0.0},
+    )
+    try:
+        Trainer(tc, callbacks=[Timer()]).train()
+    finally:
+        import shutil
+
+        shutil.rmtree(tmp, ignore_errors=True)
+    if "ms" not in timing:
+        return {"unavailable": "reference run ended before the timed steps completed"}
+    ms = timing["ms"]
+    val = world * ACCUM * BATCH * SEQ / (ms / 1e3)
+    return {"ms_per_step": ms, "value": val, "clocks": timing.get("clocks"), "loss": timing.get("loss"),
+            "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": ACCUM * BATCH * SEQ * 8 * 2,
+                    "d2h_bytes_per_step": ACCUM * 4, "note": "the reference's Trainer is its only path"},
+            "launches_per_step": None}
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    args = parse()
+    if args.impl == "reference":
+        # the reference's own launcher initialises the process group (torchrun env)
+        import torch
+
+        rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+    else:
+        rank, world, local = dist_setup()
+    if world != args.gpus and rank == 0:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    t0 = time.time()
+    res = run_reference(args, rank, world, local) if args.impl == "reference" else run_ours(args, rank, world, local)
+    if rank == 0:
+        if "unavailable" in res:
+            print(json.dumps({"impl": "reference", "unavailable": res["unavailable"]}), flush=True)
+        else:
+            par = ("dp" if args.impl == "astrai_b200" else "fsdp") + str(world) if world > 1 else "none"
+            line = {
+                "metric": "train tokens/s (1B dense)",
+                "value": round(res["value"], 1),
+                "unit": "tokens/s",
+                "n_gpus": world,
+                "steps": args.steps,
+                "warmup": args.warmup,
+                "ms_per_step": round(res["ms_per_step"], 3),
+                "higher_is_better": True,
+                "scaling": "weak",
+                "vs_baseline": None if BASELINE_VALUE is None else res["value"] / BASELINE_VALUE,
+                "dtype": "bf16",
+                "data": "synthetic uniform token ids, random-init weights",
+                "config": {"model": "dense-1.1B (24L d2048 16/4 heads ffn5632 vocab32000)",
+                           "global_batch": BATCH * ACCUM * world, "seq_len": SEQ, "parallelism": par,
+                           "micro_batch": BATCH, "grad_accum": ACCUM,
+                           "optimizer": "Muon(0.02, ns5)+AdamW(1e-4, wd0.1), clip 1.0",
+                           "l2": "no flush: per-step working set (2.4 GB weights + activations) >> 126 MB L2"},
+                "clocks": res.get("clocks"),
+                "e2e": res.get("e2e"),
+                "gpu_launches": (res.get("launches_per_step") or 0) * args.steps if args.impl == "astrai_b200" else None,
+                "loss": res.get("loss"),
+                "wall_s": round(time.time() - t0, 1),
+            }
+            if args.impl == "reference":
+                line["impl"] = "reference"
+            print(json.dumps(line), flush=True)
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

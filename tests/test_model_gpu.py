@@ -1,0 +1,83 @@
+"""Whole-model numerics: the CUDA (bf16, native kernels) path against the CPU
+fp32 oracle with identical weights, forward and backward, plus a few
+optimizer steps of the fused Muon/AdamW against their torch references."""
+
+import copy
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def rel(a, b):
+    a, b = a.float().cpu(), b.float().cpu()
+    return ((a - b).norm() / b.norm().clamp_min(1e-12)).item()
+
+
+def tiny_cfg(**kw):
+    from astrai_b200.config import AutoRegressiveLMConfig
+
+    base = dict(vocab_size=512, hidden_size=256, num_hidden_layers=2, rms_norm_eps=1e-5, intermediate_size=512,
+                tie_word_embeddings=False, max_position_embeddings=512, rope_theta=10000.0, num_attention_heads=2,
+                num_key_value_heads=1)
+    base.update(kw)
+    return AutoRegressiveLMConfig(**base)
+
+
+@pytest.mark.parametrize("tied", [False, True])
+def test_lm_forward_backward_matches_cpu(tied):
+    from astrai_b200.models import AutoRegressiveLM
+    from astrai_b200.ops._ext import native
+    from astrai_b200.ops.loss import cross_entropy
+
+    torch.manual_seed(0)
+    cpu = AutoRegressiveLM(tiny_cfg(tie_word_embeddings=tied)).float()
+    gpu = copy.deepcopy(cpu).cuda().to(torch.bfloat16)
+    # compare against the bf16-rounded weights so only compute precision differs
+    cpu.load_state_dict({k: v.to(torch.bfloat16).float() for k, v in cpu.state_dict().items()})
+    ids = torch.randint(0, 512, (2, 200))
+    tgt = torch.randint(0, 512, (2, 200))
+    lc = cross_entropy(cpu(ids)["logits"], tgt, label_smoothing=0.05)
+    lc.backward()
+    lg = cross_entropy(gpu(ids.cuda())["logits"], tgt.cuda(), label_smoothing=0.05)
+    lg.backward()
+    torch.cuda.synchronize()
+    assert native().read_error() == 0
+    assert abs(lc.item() - lg.item()) < 2e-2
+    gc = dict(cpu.named_parameters())
+    for n, p in gpu.named_parameters():
+        assert rel(p.grad, gc[n].grad) < 6e-2, n
+
+
+def test_fused_optimizers_match_torch():
+    from astrai_b200.optim import FusedAdamW, Muon, clip_grad_norm_, newton_schulz_reference
+
+    torch.manual_seed(1)
+    shapes = [(256, 512), (512, 256), (256, 512), (128, 128)]
+    ps = [torch.randn(s, device="cuda").to(torch.bfloat16) for s in shapes]
+    ref = [p.clone() for p in ps]
+    grads = [torch.randn_like(p) for p in ps]
+    P = [torch.nn.Parameter(p) for p in ps]
+    for p, g in zip(P, grads):
+        p.grad = g.clone()
+    opt = Muon(P, lr=0.02, weight_decay=0.1, adjust_lr_fn="match_rms_adamw")
+    opt.step()
+    for p0, g, p in zip(ref, grads, P):
+        buf = 0.05 * g.float()  # first step: momentum buffer = (1 - mu) * g
+        u = g.float() + 0.95 * (buf - g.float())
+        upd = newton_schulz_reference(u, 5).float()
+        adj = 0.02 * 0.2 * max(p0.shape) ** 0.5
+        exp = p0.float() * (1 - 0.02 * 0.1) - adj * upd
+        assert rel(p.data, exp) < 2e-2
+    # AdamW + on-device clip coefficient
+    w = torch.nn.Parameter(torch.randn(1000, device="cuda").to(torch.bfloat16))
+    w.grad = (torch.randn(1000, device="cuda") * 10).to(torch.bfloat16)
+    wt = torch.nn.Parameter(w.detach().float().clone())
+    wt.grad = w.grad.float().clone()
+    n = clip_grad_norm_([w], 1.0)
+    torch.nn.utils.clip_grad_norm_([wt], 1.0)
+    FusedAdamW([w], lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1).step()
+    torch.optim.AdamW([wt], lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1).step()
+    assert rel(w.data, wt.data) < 1e-2
+    assert abs(float(n) - float(torch.linalg.vector_norm(w.grad.float()))) < 1e-1 * float(n)
