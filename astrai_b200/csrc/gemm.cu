@@ -38,16 +38,29 @@ struct GemmParams {
   int* err;
 };
 
-template <int BN>
+// Tile shapes: BM x BN per CTA, BK = 64 (one 128-byte swizzle atom of bf16).
+//   BM = 128: one 128 x BN UMMA per k-step, accumulator double-buffered in
+//             TMEM so the epilogue of tile t overlaps the MMAs of tile t+1.
+//   BM = 256: two 128 x 256 UMMAs per k-step share the B tile (half the
+//             L2->SM bytes per FLOP of BM = 128); both accumulators fill TMEM,
+//             8 epilogue warps drain them.
+template <int BM_, int BN_>
 struct GemmCfg {
-  static constexpr int BM = 128;
+  static constexpr int BM = BM_;
+  static constexpr int BN = BN_;
   static constexpr int BK = 64;
-  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int MH = BM / 128;                 // 128-row MMA halves
+  static constexpr int NACC = (BM == 128) ? 2 : 1;    // accumulator buffers
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int STAGES_FIT = (225 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
+  static constexpr int TMEM_COLS = NACC * MH * BN;
+  static constexpr int EPI_WARPS = 4 * MH;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  static_assert(TMEM_COLS <= 512, "accumulators exceed tensor memory");
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& b, int& mb, int& nb) {
@@ -64,11 +77,11 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
   nb = r / gsize;
 }
 
-template <int BN, int A_MN, int B_MN, int OUT_F32>
-__global__ void __launch_bounds__(192, 1)
+template <int BM, int BN, int A_MN, int B_MN, int OUT_F32>
+__global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
-  using Cfg = GemmCfg<BN>;
-  constexpr int BM = Cfg::BM, BK = Cfg::BK, STAGES = Cfg::STAGES;
+  using Cfg = GemmCfg<BM, BN>;
+  constexpr int BK = Cfg::BK, STAGES = Cfg::STAGES, MH = Cfg::MH, NACC = Cfg::NACC;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -89,13 +102,13 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 4);
+      mbar_init(&acc_empty[a], Cfg::EPI_WARPS);
     }
     fence_mbar_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
   }
-  if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+  if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS < 32 ? 32 : Cfg::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -126,7 +139,8 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
             for (int c = 0; c < BM / 64; ++c) tma_load_3d(a_dst + c * 8192, &tmA, &full[stage], m0 + c * 64, k0, b);
           } else {
-            tma_load_3d(a_dst, &tmA, &full[stage], k0, m0, b);
+#pragma unroll
+            for (int h = 0; h < MH; ++h) tma_load_3d(a_dst + h * 16384, &tmA, &full[stage], k0, m0 + h * 128, b);
           }
           if (B_MN) {
 #pragma unroll
@@ -144,7 +158,7 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------------------------------------------------- MMA issuer
-      constexpr uint32_t idesc = idesc_bf16(BM, BN, A_MN, B_MN);
+      constexpr uint32_t idesc = idesc_bf16(128, BN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -153,7 +167,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err, kErrWaitAccEmpty)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
+        const uint32_t d_tmem = tmem_base + acc * MH * BN;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.err, kErrWaitFull)) {
             ok = false;
@@ -164,9 +178,13 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t b_base = smem_u32(sB + stage * Cfg::B_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t ad = A_MN ? sdesc_sw128(a_base + k * 2048, 8192, 1024) : sdesc_sw128(a_base + k * 32, 16, 1024);
             const uint64_t bd = B_MN ? sdesc_sw128(b_base + k * 2048, 8192, 1024) : sdesc_sw128(b_base + k * 32, 16, 1024);
-            umma_bf16(d_tmem, ad, bd, idesc, (kb | k) != 0);
+#pragma unroll
+            for (int h = 0; h < MH; ++h) {
+              const uint64_t ad = A_MN ? sdesc_sw128(a_base + h * 16384 + k * 2048, 8192, 1024)
+                                       : sdesc_sw128(a_base + h * 16384 + k * 32, 16, 1024);
+              umma_bf16(d_tmem + h * BN, ad, bd, idesc, (kb | k) != 0);
+            }
           }
           umma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -175,7 +193,7 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
         umma_commit(&acc_full[acc]);
-        if (++acc == 2) {
+        if (++acc == NACC) {
           acc = 0;
           acc_phase ^= 1;
         }
@@ -183,7 +201,8 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int q = warp & 3;          // TMEM lane quadrant this warp may access
+    const int half = (warp - 2) >> 2;  // which 128-row MMA half (BM = 256)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -191,80 +210,89 @@ __global__ void __launch_bounds__(192, 1)
       tile_coords(tile, p.tiles_m, p.tiles_n, b, mb, nb);
       if (!mbar_wait(&acc_full[acc], acc_phase, p.err, kErrWaitAccFull)) break;
       tc_fence_after();
-      const int row = mb * BM + q * 32 + lane;
+      const int row = mb * BM + half * 128 + q * 32 + lane;
       const int n0 = nb * BN;
       const bool row_ok = row < p.M;
       using OutT = typename std::conditional<OUT_F32, float, __nv_bfloat16>::type;
       OutT* drow = reinterpret_cast<OutT*>(p.D) + (long long)b * p.strideD + (long long)row * p.ldd;
       const OutT* crow = p.C ? reinterpret_cast<const OutT*>(p.C) + (long long)b * p.strideC + (long long)row * p.ldc
                              : nullptr;
+      const uint32_t t_acc = tmem_base + ((uint32_t)(q * 32) << 16) + (acc * MH + half) * BN;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + c, r);
+      for (int c = 0; c < BN; c += 64) {
+        uint32_t r2[64];
+        tmem_ld32(t_acc + c, *reinterpret_cast<uint32_t(*)[32]>(&r2[0]));
+        tmem_ld32(t_acc + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&r2[32]));
         tmem_wait_ld();
-        const int col = n0 + c;
-        if (!row_ok || col >= p.N) continue;
-        float v[32];
+        if (c + 64 >= BN) {
+          // last chunk read: release the accumulator before the global stores
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        }
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
-        const bool full_chunk = (col + 32 <= p.N) && p.vec_ok;
-        if (full_chunk) {
-          if (crow && p.beta != 0.f) {
-            if (OUT_F32) {
-              const float4* src = reinterpret_cast<const float4*>(crow + col);
+        for (int sub = 0; sub < 2; ++sub) {
+          const uint32_t* r = &r2[sub * 32];
+          const int col = n0 + c + sub * 32;
+          if (!row_ok || col >= p.N) continue;
+          float v[32];
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                float4 t = src[i];
-                v[4 * i] += p.beta * t.x;
-                v[4 * i + 1] += p.beta * t.y;
-                v[4 * i + 2] += p.beta * t.z;
-                v[4 * i + 3] += p.beta * t.w;
-              }
-            } else {
-              const uint4* src = reinterpret_cast<const uint4*>(crow + col);
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
+          const bool full_chunk = (col + 32 <= p.N) && p.vec_ok;
+          if (full_chunk) {
+            if (crow && p.beta != 0.f) {
+              if (OUT_F32) {
+                const float4* src = reinterpret_cast<const float4*>(crow + col);
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                uint4 t = src[i];
-                uint32_t w[4] = {t.x, t.y, t.z, t.w};
+                for (int i = 0; i < 8; ++i) {
+                  float4 t = src[i];
+                  v[4 * i] += p.beta * t.x;
+                  v[4 * i + 1] += p.beta * t.y;
+                  v[4 * i + 2] += p.beta * t.z;
+                  v[4 * i + 3] += p.beta * t.w;
+                }
+              } else {
+                const uint4* src = reinterpret_cast<const uint4*>(crow + col);
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  float2 f = unpack_bf16(w[j]);
-                  v[8 * i + 2 * j] += p.beta * f.x;
-                  v[8 * i + 2 * j + 1] += p.beta * f.y;
+                for (int i = 0; i < 4; ++i) {
+                  uint4 t = src[i];
+                  uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) {
+                    float2 f = unpack_bf16(w[j]);
+                    v[8 * i + 2 * j] += p.beta * f.x;
+                    v[8 * i + 2 * j + 1] += p.beta * f.y;
+                  }
                 }
               }
             }
-          }
-          if (OUT_F32) {
-            float4* dst = reinterpret_cast<float4*>(drow + col);
+            if (OUT_F32) {
+              float4* dst = reinterpret_cast<float4*>(drow + col);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+              for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            } else {
+              uint4* dst = reinterpret_cast<uint4*>(drow + col);
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                dst[i] = make_uint4(pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
+                                    pack_bf16(v[8 * i + 4], v[8 * i + 5]), pack_bf16(v[8 * i + 6], v[8 * i + 7]));
+            }
           } else {
-            uint4* dst = reinterpret_cast<uint4*>(drow + col);
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              dst[i] = make_uint4(pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
-                                  pack_bf16(v[8 * i + 4], v[8 * i + 5]), pack_bf16(v[8 * i + 6], v[8 * i + 7]));
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            if (col + i < p.N) {
-              float x = v[i];
-              if (crow && p.beta != 0.f) x += p.beta * to_f(crow[col + i]);
-              if (OUT_F32)
-                reinterpret_cast<float*>(drow)[col + i] = x;
-              else
-                reinterpret_cast<__nv_bfloat16*>(drow)[col + i] = __float2bfloat16_rn(x);
+            for (int i = 0; i < 32; ++i) {
+              if (col + i < p.N) {
+                float x = v[i];
+                if (crow && p.beta != 0.f) x += p.beta * to_f(crow[col + i]);
+                if (OUT_F32)
+                  reinterpret_cast<float*>(drow)[col + i] = x;
+                else
+                  reinterpret_cast<__nv_bfloat16*>(drow)[col + i] = __float2bfloat16_rn(x);
+              }
             }
           }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[acc]);
-      if (++acc == 2) {
+      if (++acc == NACC) {
         acc = 0;
         acc_phase ^= 1;
       }
@@ -273,7 +301,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS < 32 ? 32 : Cfg::TMEM_COLS);
   }
 }
 
@@ -284,25 +312,25 @@ namespace astrai_host {
 using astrai::GemmCfg;
 using astrai::GemmParams;
 
-template <int BN, int A_MN, int B_MN, int OUT_F32>
+template <int BM, int BN, int A_MN, int B_MN, int OUT_F32>
 static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
                         cudaStream_t stream) {
-  auto kern = astrai::gemm_kernel<BN, A_MN, B_MN, OUT_F32>;
+  auto kern = astrai::gemm_kernel<BM, BN, A_MN, B_MN, OUT_F32>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::SMEM);
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BM, BN>::SMEM);
     attr_set[dev & 63] = true;
   }
-  kern<<<grid, 192, GemmCfg<BN>::SMEM, stream>>>(ta, tb, p);
+  kern<<<grid, GemmCfg<BM, BN>::THREADS, GemmCfg<BM, BN>::SMEM, stream>>>(ta, tb, p);
 }
 
-template <int BN>
+template <int BM, int BN>
 static void dispatch_majors(int a_mn, int b_mn, int out_f32, const CUtensorMap& ta, const CUtensorMap& tb,
                             const GemmParams& p, int grid, cudaStream_t s) {
 #define ASTRAI_GEMM_CASE(AM, BMJ, OF) \
-  if (a_mn == AM && b_mn == BMJ && out_f32 == OF) return launch_gemm<BN, AM, BMJ, OF>(ta, tb, p, grid, s);
+  if (a_mn == AM && b_mn == BMJ && out_f32 == OF) return launch_gemm<BM, BN, AM, BMJ, OF>(ta, tb, p, grid, s);
   ASTRAI_GEMM_CASE(0, 0, 0)
   ASTRAI_GEMM_CASE(0, 1, 0)
   ASTRAI_GEMM_CASE(1, 0, 0)
@@ -314,20 +342,36 @@ static void dispatch_majors(int a_mn, int b_mn, int out_f32, const CUtensorMap& 
 #undef ASTRAI_GEMM_CASE
 }
 
-static int pick_bn(int M, int N, int batch, int sms) {
-  if (N <= 128) return 128;
-  auto eff = [&](int bn) {
-    long long tiles = (long long)((M + 127) / 128) * ((N + bn - 1) / bn) * batch;
-    long long waves = (tiles + sms - 1) / sms;
-    return (double)tiles / (double)(waves * sms);
-  };
-  // 256-wide tiles halve A re-reads; only drop to 128 when it fixes a bad tail.
-  return eff(128) > eff(256) + 0.12 ? 128 : 256;
+// Pick the tile shape minimising (waves x per-tile cost); per-tile costs are
+// relative throughputs of the three variants (256x256 moves the fewest bytes
+// per FLOP, 128x128 the most).
+static void pick_tile(int M, int N, int batch, int sms, int& bm, int& bn) {
+  // Measured on B200 (relative per-tile throughput at large K): 256x256 1.0,
+  // 128x256 0.93; 128x128 is slower on every training shape and only used
+  // when N <= 128.
+  struct Opt { int bm, bn; double rel_speed; };
+  const Opt opts[2] = {{256, 256, 1.0}, {128, 256, 0.93}};
+  double best = 1e30;
+  bm = 128;
+  bn = N <= 128 ? 128 : 256;
+  if (N <= 128) return;
+  for (const Opt& o : opts) {
+    if (o.bm == 256 && M <= 128) continue;
+    const long long tiles = (long long)((M + o.bm - 1) / o.bm) * ((N + o.bn - 1) / o.bn) * batch;
+    const long long waves = (tiles + sms - 1) / sms;
+    const double t = (double)waves * o.bm * o.bn / o.rel_speed;
+    if (t < best * 0.999) {
+      best = t;
+      bm = o.bm;
+      bn = o.bn;
+    }
+  }
 }
 
 // Row strides (lda, ldb, ldd, ldc) and batch strides are in elements.
 // a_mn == 0: A stored [batch][M][lda] (K contiguous); a_mn == 1: [batch][K][lda] (M contiguous).
 // b_mn == 0: B stored [batch][N][ldb];                b_mn == 1: [batch][K][ldb].
+// force_bn: 0 = automatic; 128 / 256 = BM 128 with that BN; 512 = 256 x 256 tiles.
 void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int N, int K, int batch, int a_mn,
                long long lda, long long strideA, int b_mn, long long ldb, long long strideB, long long ldd,
                long long strideD, int out_f32, long long ldc, long long strideC, float alpha, float beta,
@@ -336,7 +380,14 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
   int dev = 0;
   cudaGetDevice(&dev);
   const int sms = num_sms(dev);
-  const int BN = force_bn ? force_bn : pick_bn(M, N, batch, sms);
+  int BM = 128, BN = 256;
+  if (force_bn == 128 || force_bn == 256) {
+    BN = force_bn;
+  } else if (force_bn == 512) {
+    BM = 256;
+  } else {
+    pick_tile(M, N, batch, sms, BM, BN);
+  }
 
   CUtensorMap ta, tb;
   {
@@ -362,7 +413,7 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
   p.N = N;
   p.K = K;
   p.batch = batch;
-  p.tiles_m = (M + 127) / 128;
+  p.tiles_m = (M + BM - 1) / BM;
   p.tiles_n = (N + BN - 1) / BN;
   p.k_blocks = (K + 63) / 64;
   p.D = D;
@@ -381,10 +432,12 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
   p.err = error_word(dev);
   const int tiles = batch * p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, sms);
-  if (BN == 256)
-    dispatch_majors<256>(a_mn, b_mn, out_f32, ta, tb, p, grid, stream);
+  if (BM == 256)
+    dispatch_majors<256, 256>(a_mn, b_mn, out_f32, ta, tb, p, grid, stream);
+  else if (BN == 256)
+    dispatch_majors<128, 256>(a_mn, b_mn, out_f32, ta, tb, p, grid, stream);
   else
-    dispatch_majors<128>(a_mn, b_mn, out_f32, ta, tb, p, grid, stream);
+    dispatch_majors<128, 128>(a_mn, b_mn, out_f32, ta, tb, p, grid, stream);
 }
 
 }  // namespace astrai_host

@@ -120,9 +120,9 @@ class GQA(nn.Module):
         Linear layers), else per-module calls (LoRA-wrapped or biased)."""
         mods = (self.q_proj, self.k_proj, self.v_proj)
         if all(type(m) is Linear and m.bias is None for m in mods):
-            from astrai_b200.ops.gemm import linear
+            from astrai_b200.ops.gemm import packed_linear
 
-            return linear(x, self.qkv_weight())
+            return packed_linear(x, [m.weight for m in mods])
         return torch.cat([m(x) for m in mods], dim=-1)
 
 

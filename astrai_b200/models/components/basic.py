@@ -18,6 +18,7 @@ import torch.nn as nn
 
 from astrai_b200.ops.embedding import embedding as _embedding
 from astrai_b200.ops.gemm import linear as _linear
+from astrai_b200.ops.gemm import packed_linear as _packed_linear
 from astrai_b200.ops.norm import rms_norm as _rms_norm
 from astrai_b200.ops.rope import ntk_base, rope_table
 
@@ -44,6 +45,8 @@ class Linear(nn.Module):
             nn.init.uniform_(self.bias, -bound, bound)
 
     def forward(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if self.bias is None:
+            return _packed_linear(x, [self.weight], residual=residual)
         return _linear(x, self.weight, residual=residual, bias=self.bias)
 
 

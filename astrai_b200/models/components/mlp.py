@@ -25,7 +25,7 @@ import torch.nn as nn
 from astrai_b200.factory import Registry
 from astrai_b200.models.components.basic import Linear
 from astrai_b200.ops.activation import swiglu
-from astrai_b200.ops.gemm import linear
+from astrai_b200.ops.gemm import linear, packed_linear
 
 
 class FFNFactory(Registry[nn.Module]):
@@ -42,7 +42,7 @@ class MLP(nn.Module):
 
     def forward(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None, ctx=None) -> torch.Tensor:
         if type(self.up) is Linear and type(self.gate) is Linear and self.up.bias is None and self.gate.bias is None:
-            h = linear(x, torch.cat([self.up.weight, self.gate.weight], 0))
+            h = packed_linear(x, [self.up.weight, self.gate.weight])
         else:
             h = torch.cat([self.up(x), self.gate(x)], dim=-1)
         return self.down(swiglu(h), residual=residual)

@@ -84,6 +84,124 @@ class _LinearFn(torch.autograd.Function):
         return dx, dw, dres
 
 
+def pack_params(params) -> torch.Tensor:
+    """Make the 2-D parameters ``params`` (same in-dim) views of ONE contiguous
+    buffer, in order, and return the buffer. Parameter objects are kept (only
+    ``.data`` is re-pointed), so optimizers and state dicts are unaffected."""
+    params = list(params)
+    base = params[0]
+    if len(params) > 1 and _packed(params):
+        return _packed_view(params)
+    rows = sum(p.shape[0] for p in params)
+    buf = torch.empty((rows, base.shape[1]), device=base.device, dtype=base.dtype)
+    r = 0
+    with torch.no_grad():
+        for p in params:
+            n = p.shape[0]
+            buf[r:r + n].copy_(p.data)
+            p.data = buf[r:r + n]
+            r += n
+    return buf
+
+
+def _packed(params) -> bool:
+    p0 = params[0]
+    if not p0.is_contiguous():
+        return False
+    ptr = p0.data_ptr()
+    for p in params:
+        if p.data_ptr() != ptr or not p.is_contiguous() or p.dtype != p0.dtype or p.shape[1] != p0.shape[1] \
+                or p.untyped_storage().data_ptr() != p0.untyped_storage().data_ptr():
+            return False
+        ptr += p.numel() * p.element_size()
+    return True
+
+
+def _packed_view(params) -> torch.Tensor:
+    p0 = params[0]
+    rows = sum(p.shape[0] for p in params)
+    return p0.data.as_strided((rows, p0.shape[1]), (p0.shape[1], 1))
+
+
+class _PackedLinearFn(torch.autograd.Function):
+    """y = x @ W^T (+ residual) with W = rows of the packed parameters.
+
+    The weight gradient is written by the GEMM straight into a packed
+    gradient buffer whose row slices are the parameters' ``.grad`` tensors:
+    the first micro-batch after ``zero_grad`` overwrites (beta = 0), later
+    ones accumulate in the GEMM epilogue (beta = 1). No autograd
+    accumulation kernels, no split copies."""
+
+    @staticmethod
+    def forward(ctx, x, w, residual, *params):
+        x2 = _as_rows(x)
+        M, N = x2.shape[0], w.shape[0]
+        out = torch.empty((M, N), device=x.device, dtype=torch.bfloat16)
+        r2 = _as_rows(residual) if residual is not None else None
+        native().gemm(x2, w, out, r2, 0, 0, 1.0, 1.0 if r2 is not None else 0.0, 0)
+        ctx.save_for_backward(x2, w)
+        ctx.params = params
+        ctx.has_res = residual is not None
+        ctx.x_shape = x.shape
+        return out.view(*x.shape[:-1], N)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w = ctx.saved_tensors
+        dy2 = _as_rows(dy)
+        C = native()
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = torch.empty_like(x2)
+            C.gemm(dy2, w, dx, None, 0, 1, 1.0, 0.0, 0)
+            dx = dx.view(ctx.x_shape)
+        params = [p for p in ctx.params if p.requires_grad]
+        if params:
+            g0 = params[0].grad
+            if g0 is None:
+                buf = torch.empty_like(w)
+                C.gemm(dy2, x2, buf, None, 1, 1, 1.0, 0.0, 0)
+                r = 0
+                for p in ctx.params:
+                    n = p.shape[0]
+                    if p.requires_grad:
+                        p.grad = buf[r:r + n]
+                    r += n
+            else:
+                grads = [p.grad for p in ctx.params]
+                if all(g is not None for g in grads) and _packed(grads):
+                    buf = _packed_view(grads)
+                    C.gemm(dy2, x2, buf, buf, 1, 1, 1.0, 1.0, 0)
+                else:  # foreign gradient layout: compute and add
+                    tmp = torch.empty_like(w)
+                    C.gemm(dy2, x2, tmp, None, 1, 1, 1.0, 0.0, 0)
+                    r = 0
+                    for p in ctx.params:
+                        n = p.shape[0]
+                        if p.requires_grad:
+                            p.grad = tmp[r:r + n].clone() if p.grad is None else p.grad.add_(tmp[r:r + n])
+                        r += n
+        dres = dy if ctx.has_res else None
+        return (dx, None, dres) + (None,) * len(ctx.params)
+
+
+def packed_linear(x: torch.Tensor, params, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``x @ cat(params)^T (+ residual)`` for bias-free 2-D bf16 parameters.
+
+    On CUDA the parameters are packed once into one contiguous weight (views),
+    so no concatenation happens per call, and weight gradients accumulate in
+    the GEMM epilogue. Parameters held as DTensors (FSDP) or on the CPU take
+    the autograd path of :func:`linear`."""
+    params = list(params)
+    cuda_ok = x.is_cuda and x.dtype == torch.bfloat16 and all(
+        p.is_cuda and p.dtype == torch.bfloat16 and type(p.data) is torch.Tensor for p in params)
+    if not cuda_ok or (x.shape[-1] * 2) % 16:
+        w = params[0] if len(params) == 1 else torch.cat(list(params), 0)
+        return linear(x, w, residual=residual)
+    w = pack_params(params) if len(params) > 1 else params[0]
+    return _PackedLinearFn.apply(x, w.detach(), residual, *params)
+
+
 def linear(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None,
            bias: Optional[torch.Tensor] = None) -> torch.Tensor:
     """y = x @ w.T (+ bias) (+ residual)."""

@@ -42,7 +42,7 @@ def test_gemm_majors(a_mn, b_mn, M, N, K):
     assert rel_err(d, ref) < 1e-2
 
 
-@pytest.mark.parametrize("force_bn", [128, 256])
+@pytest.mark.parametrize("force_bn", [128, 256, 512])
 def test_gemm_tiles_and_epilogue(force_bn):
     from astrai_b200.ops._ext import native
     from astrai_b200.ops.gemm import gemm_reference
