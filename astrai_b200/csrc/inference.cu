@@ -1,0 +1,601 @@
+// Inference kernels (sm_100a): paged KV-cache write / gather, paged split-KV
+// decode attention, split combine, and the fused token sampler.
+//
+// Paged KV layout (per layer):  cache[page][kv_head][slot][128]  (bf16)
+// so the keys of one head inside a page are contiguous and a decode warp
+// streams them with fully coalesced 256-byte rows.
+//
+// Decode (replaces gather + repeat_kv + SDPA over the gathered cache of the
+// reference, astrai/inference/core/cache.py:256-276 + attention.py:89-101):
+// grid (split, kv_head, batch); a CTA reads each K/V row of its key range
+// ONCE and applies it to all Hq/Hkv query heads of the group; lanes split
+// the head dimension, warps split the keys, online softmax in fp32. Split
+// partials (m, l, acc) are merged by a second kernel (flash-decoding).
+// Decode is bound by HBM bandwidth (one pass over the live KV), so CUDA-core
+// math is enough; the kernel reads the page table itself - nothing is
+// gathered.
+//
+// Sampling (replaces astrai/inference/sample.py:18-375): one CTA per row
+// applies temperature, top-k (k-th largest logit found by a binary search on
+// the float bit pattern), top-p (nucleus threshold by a binary search on
+// probability: keep token i iff the mass of strictly more likely tokens is
+// <= top_p), the frequency penalty (count of each token in the row's history
+// window) and draws from the final distribution with a block-wide prefix
+// scan; it also returns log p(token) under that distribution. Greedy rows
+// (temperature 0) take the argmax of the raw logits. No host
+// synchronisation, no sort.
+#include <cfloat>
+#include <stdexcept>
+#include <string>
+
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace astrai {
+
+constexpr int DEC_D = 128;
+constexpr int DEC_MAXG = 16;
+
+// ------------------------------------------------------------------ KV write / gather
+// src k/v: [T, Hkv, D] rows with row stride ld (elements); slot[t] = page * page_size + offset
+__global__ void paged_kv_write_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
+                                      long long ld_src, const int* __restrict__ slot, int T, int Hkv, int page_size,
+                                      __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc) {
+  const int per = DEC_D / 8;  // 16-byte chunks per head row
+  const long long total = (long long)T * Hkv * per;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int c = i % per;
+    const long long th = i / per;
+    const int h = th % Hkv;
+    const int t = th / Hkv;
+    const int s = slot[t];
+    if (s < 0) continue;
+    const int page = s / page_size, off = s % page_size;
+    const long long dst = (((long long)page * Hkv + h) * page_size + off) * DEC_D + c * 8;
+    const long long src = (long long)t * ld_src + h * DEC_D + c * 8;
+    *reinterpret_cast<uint4*>(kc + dst) = *reinterpret_cast<const uint4*>(k + src);
+    *reinterpret_cast<uint4*>(vc + dst) = *reinterpret_cast<const uint4*>(v + src);
+  }
+}
+
+// out k/v: [B, S_out, Hkv, D] contiguous; positions >= len[b] are zero-filled
+__global__ void paged_kv_gather_kernel(const __nv_bfloat16* __restrict__ kc, const __nv_bfloat16* __restrict__ vc,
+                                       const int* __restrict__ table, int max_pages, const int* __restrict__ lens,
+                                       int B, int S_out, int Hkv, int page_size, __nv_bfloat16* __restrict__ ko,
+                                       __nv_bfloat16* __restrict__ vo) {
+  const int per = DEC_D / 8;
+  const long long total = (long long)B * S_out * Hkv * per;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int c = i % per;
+    long long r = i / per;
+    const int h = r % Hkv;
+    r /= Hkv;
+    const int pos = r % S_out;
+    const int b = r / S_out;
+    uint4 kk = make_uint4(0, 0, 0, 0), vv = kk;
+    if (pos < lens[b]) {
+      const int page = table[(long long)b * max_pages + pos / page_size];
+      if (page >= 0) {
+        const long long src = (((long long)page * Hkv + h) * page_size + pos % page_size) * DEC_D + c * 8;
+        kk = *reinterpret_cast<const uint4*>(kc + src);
+        vv = *reinterpret_cast<const uint4*>(vc + src);
+      }
+    }
+    const long long dst = (((long long)b * S_out + pos) * Hkv + h) * DEC_D + c * 8;
+    *reinterpret_cast<uint4*>(ko + dst) = kk;
+    *reinterpret_cast<uint4*>(vo + dst) = vv;
+  }
+}
+
+// ------------------------------------------------------------------ decode attention
+struct DecodeParams {
+  const __nv_bfloat16* q;  // [B, Hq, D] (row stride ldq per batch row, head stride D)
+  long long ldq;
+  const __nv_bfloat16* kc;
+  const __nv_bfloat16* vc;
+  const int* table;  // [B, max_pages]
+  int max_pages;
+  const int* lens;   // [B] number of cached keys (including the current token)
+  int B, Hq, Hkv, page_size, splits;
+  float scale_log2;
+  float* part_acc;   // [B, Hkv, splits, G, D]
+  float* part_ml;    // [B, Hkv, splits, G, 2]
+  __nv_bfloat16* out;  // [B, Hq, D] (row stride ldo)
+  long long ldo;
+};
+
+__device__ __forceinline__ float ex2f_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int G>
+__global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams p) {
+  const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int len = p.lens[b];
+  // this row's keys are divided evenly over the splits (multiples of 16 keys)
+  const int kps = ((len + p.splits - 1) / p.splits + 15) & ~15;
+  const int k0 = split * kps;
+  const int k1 = min(len, k0 + kps);
+  // q for the G heads of this group: lane owns dims [4*lane, 4*lane+4)
+  float q[G][4];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const __nv_bfloat16* qp = p.q + (long long)b * p.ldq + (hk * G + g) * DEC_D + lane * 4;
+    const uint2 u = *reinterpret_cast<const uint2*>(qp);
+    const float2 a = unpack_bf16(u.x), c = unpack_bf16(u.y);
+    q[g][0] = a.x * p.scale_log2;
+    q[g][1] = a.y * p.scale_log2;
+    q[g][2] = c.x * p.scale_log2;
+    q[g][3] = c.y * p.scale_log2;
+  }
+  float m[G], l[G], acc[G][4];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+    acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.f;
+  }
+  const int* trow = p.table + (long long)b * p.max_pages;
+  // each warp takes 4 consecutive keys per iteration: 8 independent 8-byte
+  // loads per lane in flight before any math
+  constexpr int KU = 4;
+  for (int kb = k0 + warp * KU; kb < k1; kb += 4 * KU) {
+    uint2 ku[KU], vu[KU];
+    bool ok[KU];
+#pragma unroll
+    for (int u = 0; u < KU; ++u) {
+      const int k = kb + u;
+      const int page = k < k1 ? trow[k / p.page_size] : -1;
+      ok[u] = page >= 0;
+      if (ok[u]) {
+        const long long row = (((long long)page * p.Hkv + hk) * p.page_size + k % p.page_size) * DEC_D + lane * 4;
+        ku[u] = *reinterpret_cast<const uint2*>(p.kc + row);
+        vu[u] = *reinterpret_cast<const uint2*>(p.vc + row);
+      } else {
+        ku[u] = vu[u] = make_uint2(0, 0);
+      }
+    }
+    float s[KU][G];
+#pragma unroll
+    for (int u = 0; u < KU; ++u) {
+      const float2 k01 = unpack_bf16(ku[u].x), k23 = unpack_bf16(ku[u].y);
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+        s[u][g] = q[g][0] * k01.x + q[g][1] * k01.y + q[g][2] * k23.x + q[g][3] * k23.y;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+      for (int u = 0; u < KU; ++u)
+#pragma unroll
+        for (int g = 0; g < G; ++g) s[u][g] += __shfl_xor_sync(0xffffffff, s[u][g], o);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float mx = m[g];
+#pragma unroll
+      for (int u = 0; u < KU; ++u)
+        if (ok[u]) mx = fmaxf(mx, s[u][g]);
+      if (mx == -INFINITY) continue;
+      const float corr = ex2f_fast(m[g] - mx);
+      m[g] = mx;
+      l[g] *= corr;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[g][i] *= corr;
+#pragma unroll
+      for (int u = 0; u < KU; ++u) {
+        if (!ok[u]) continue;
+        const float e = ex2f_fast(s[u][g] - mx);
+        const float2 v01 = unpack_bf16(vu[u].x), v23 = unpack_bf16(vu[u].y);
+        l[g] += e;
+        acc[g][0] += e * v01.x;
+        acc[g][1] += e * v01.y;
+        acc[g][2] += e * v23.x;
+        acc[g][3] += e * v23.y;
+      }
+    }
+  }
+  // merge the 4 warps through shared memory
+  __shared__ float sm_ml[4][G][2];
+  __shared__ float sm_acc[4][G][DEC_D];
+  if (lane == 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      sm_ml[warp][g][0] = m[g];
+      sm_ml[warp][g][1] = l[g];
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sm_acc[warp][g][lane * 4 + i] = acc[g][i];
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < G * DEC_D; idx += 128) {
+    const int g = idx / DEC_D, d = idx % DEC_D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_ml[w][g][0]);
+    float L = 0.f, A = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float c = ex2f_fast(sm_ml[w][g][0] - M);
+        L += sm_ml[w][g][1] * c;
+        A += sm_acc[w][g][d] * c;
+      }
+    }
+    if (p.splits == 1) {
+      p.out[(long long)b * p.ldo + (hk * G + g) * DEC_D + d] = __float2bfloat16_rn(L > 0.f ? A / L : 0.f);
+    } else {
+      const long long base = (((long long)b * p.Hkv + hk) * p.splits + split) * G + g;
+      p.part_acc[base * DEC_D + d] = A;
+      if (d == 0) {
+        p.part_ml[base * 2] = M;
+        p.part_ml[base * 2 + 1] = L;
+      }
+    }
+  }
+}
+
+// merge split partials: one block per (b, q head), D threads
+__global__ void decode_combine_kernel(const float* __restrict__ part_acc, const float* __restrict__ part_ml, int B,
+                                      int Hq, int Hkv, int splits, __nv_bfloat16* __restrict__ out, long long ldo) {
+  const int bh = blockIdx.x;
+  const int b = bh / Hq, h = bh % Hq;
+  const int G = Hq / Hkv, hk = h / G, g = h % G;
+  const int d = threadIdx.x;
+  float M = -INFINITY;
+  for (int s = 0; s < splits; ++s)
+    M = fmaxf(M, part_ml[((((long long)b * Hkv + hk) * splits + s) * G + g) * 2]);
+  float L = 0.f, A = 0.f;
+  if (M != -INFINITY) {
+    for (int s = 0; s < splits; ++s) {
+      const long long base = (((long long)b * Hkv + hk) * splits + s) * G + g;
+      const float c = ex2f_fast(part_ml[base * 2] - M);
+      L += part_ml[base * 2 + 1] * c;
+      A += part_acc[base * DEC_D + d] * c;
+    }
+  }
+  out[(long long)b * ldo + h * DEC_D + d] = __float2bfloat16_rn(L > 0.f ? A / L : 0.f);
+}
+
+// ------------------------------------------------------------------ sampling
+// One thread-block cluster per row: CTA r of the cluster holds vocabulary
+// chunk [r * 16384, (r + 1) * 16384) in registers (1024 threads x 16 values),
+// so a row is read from HBM exactly once. Row-wide sums / maxima are block
+// reductions merged across the cluster through distributed shared memory.
+constexpr int SMP_THREADS = 1024;
+constexpr int SMP_PER = 16;
+constexpr int SMP_CHUNK = SMP_THREADS * SMP_PER;  // 16384 tokens per CTA
+constexpr int SMP_MAX_CLUSTER = 16;               // non-portable cluster size -> V <= 262144
+
+// SplitMix64 finaliser (public-domain construction): uniform in [0, 1)
+__device__ __forceinline__ float uniform_from(unsigned long long seed, unsigned long long a, unsigned long long b) {
+  unsigned long long z = seed + 0x9E3779B97F4A7C15ull * (a * 0x100000001B3ull + b + 1);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  return (float)(z >> 40) * (1.0f / 16777216.0f);
+}
+
+// order-preserving map of floats to uint32 (greater float -> greater key)
+__device__ __forceinline__ uint32_t fkey(float x) {
+  const uint32_t u = __float_as_uint(x);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+enum RedOp { RED_SUM = 0, RED_MAX = 1 };
+
+__device__ __forceinline__ float red2(float a, float b, int op) { return op == RED_MAX ? fmaxf(a, b) : a + b; }
+
+// Row-wide reduction: block reduction, then (cluster > 1) a merge of the
+// per-CTA results read from every CTA's shared memory.
+__device__ __forceinline__ float row_reduce(float v, int op, float* sh, int csize) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = red2(v, __shfl_xor_sync(0xffffffff, v, o), op);
+  if (lane == 0) sh[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = sh[lane];  // SMP_THREADS / 32 == 32 partials
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = red2(v, __shfl_xor_sync(0xffffffff, v, o), op);
+    if (lane == 0) sh[32] = v;
+  }
+  if (csize == 1) {
+    __syncthreads();
+    v = sh[32];
+    __syncthreads();  // sh reusable by the next reduction
+    return v;
+  }
+  cg::cluster_group cl = cg::this_cluster();
+  cl.sync();
+  float r = op == RED_MAX ? -INFINITY : 0.f;
+  for (int c = 0; c < csize; ++c) r = red2(r, *cl.map_shared_rank(sh + 32, c), op);
+  cl.sync();
+  return r;
+}
+
+// Exclusive prefix of a per-CTA value over cluster ranks (rank order)
+__device__ __forceinline__ float cluster_exclusive(float v, float* slot, int csize, int rank) {
+  if (csize == 1) return 0.f;
+  cg::cluster_group cl = cg::this_cluster();
+  if (threadIdx.x == 0) *slot = v;
+  cl.sync();
+  float r = 0.f;
+  for (int c = 0; c < rank; ++c) r += *cl.map_shared_rank(slot, c);
+  cl.sync();
+  return r;
+}
+
+__global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(
+    const void* __restrict__ logits, int logits_f32, long long ld, int V, const float* __restrict__ temperature,
+    const int* __restrict__ top_k, const float* __restrict__ top_p, const float* __restrict__ penalty,
+    const long long* __restrict__ hist, int hist_len, long long ld_hist,
+    const unsigned long long* __restrict__ rng, long long* __restrict__ out_tok, float* __restrict__ out_lp) {
+  __shared__ float sh[33];
+  __shared__ float sh_scan[SMP_THREADS / 32];
+  __shared__ float sh_slot;
+  const int cs = (int)cg::this_cluster().num_blocks();
+  const int rank = cs > 1 ? (int)cg::this_cluster().block_rank() : 0;
+  const int row = blockIdx.x / cs;
+  const int t = threadIdx.x;
+  const int base = rank * SMP_CHUNK;
+  float x[SMP_PER];
+  float raw_max = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < SMP_PER; ++j) {
+    const int i = base + t + j * SMP_THREADS;
+    float v = -INFINITY;
+    if (i < V) {
+      v = logits_f32 ? reinterpret_cast<const float*>(logits)[(long long)row * ld + i]
+                     : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(logits)[(long long)row * ld + i]);
+      if (v != v) v = -INFINITY;  // NaN never wins
+    }
+    x[j] = v;
+    raw_max = fmaxf(raw_max, v);
+  }
+  const float temp = temperature ? temperature[row] : 1.f;
+  const float gmax = row_reduce(raw_max, RED_MAX, sh, cs);
+  if (temp == 0.f) {
+    // greedy: first index of the maximum; logprob under softmax(raw logits)
+    float sum = 0.f;
+    int best = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < SMP_PER; ++j) {
+      sum += (x[j] == -INFINITY) ? 0.f : __expf(x[j] - gmax);
+      if (x[j] == gmax && best == 0x7fffffff && base + t + j * SMP_THREADS < V) best = base + t + j * SMP_THREADS;
+    }
+    const float Z = row_reduce(sum, RED_SUM, sh, cs);
+    const float bi = row_reduce(best == 0x7fffffff ? -3.0e38f : -(float)best, RED_MAX, sh, cs);
+    if (t == 0 && rank == 0) {
+      out_tok[row] = bi < -1.0e38f ? 0 : (long long)(-bi);
+      if (out_lp) out_lp[row] = gmax == -INFINITY ? -INFINITY : -__logf(Z);
+    }
+    return;
+  }
+  const float inv_t = 1.f / fmaxf(temp, 1e-8f);
+#pragma unroll
+  for (int j = 0; j < SMP_PER; ++j) x[j] *= inv_t;
+  const float mx = gmax * inv_t;  // scaling by a positive factor keeps the argmax
+  // ---- top-k: the largest key threshold `lo` with count(key >= lo) >= k
+  const int k = top_k ? top_k[row] : 0;
+  if (k > 0 && k < V) {
+    uint32_t lo = 0, hi = fkey(mx);
+    while (lo < hi) {
+      const uint32_t mid = lo + (hi - lo + 1) / 2;
+      float c = 0.f;
+#pragma unroll
+      for (int j = 0; j < SMP_PER; ++j) c += (x[j] != -INFINITY && fkey(x[j]) >= mid) ? 1.f : 0.f;
+      const float tot = row_reduce(c, RED_SUM, sh, cs);
+      if (tot >= (float)k) {
+        lo = mid;
+        if (tot == (float)k) break;  // exactly the k largest: done
+      } else {
+        hi = mid - 1;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < SMP_PER; ++j)
+      if (x[j] != -INFINITY && fkey(x[j]) < lo) x[j] = -INFINITY;
+  }
+  // ---- top-p: keep token i iff the mass of strictly larger tokens <= top_p
+  const float pp = top_p ? top_p[row] : 1.f;
+  if (pp < 1.f) {
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < SMP_PER; ++j) s += (x[j] == -INFINITY) ? 0.f : __expf(x[j] - mx);
+    const float Z = row_reduce(s, RED_SUM, sh, cs);
+    // smallest key `lo` whose strictly-greater mass is <= pp * Z (the max is always kept)
+    uint32_t lo = 0, hi = fkey(mx);
+    while (lo < hi) {
+      const uint32_t mid = lo + (hi - lo) / 2;
+      float c = 0.f;
+#pragma unroll
+      for (int j = 0; j < SMP_PER; ++j) c += (x[j] != -INFINITY && fkey(x[j]) > mid) ? __expf(x[j] - mx) : 0.f;
+      const float above = row_reduce(c, RED_SUM, sh, cs);
+      if (above <= pp * Z) hi = mid; else lo = mid + 1;
+    }
+#pragma unroll
+    for (int j = 0; j < SMP_PER; ++j)
+      if (x[j] != -INFINITY && fkey(x[j]) < lo) x[j] = -INFINITY;
+  }
+  // ---- frequency penalty: subtract penalty * count(token in the history window)
+  const float pen = penalty ? penalty[row] : 0.f;
+  if (pen != 0.f && hist) {
+    for (int h = 0; h < hist_len; ++h) {
+      const long long id = hist[(long long)row * ld_hist + h];
+      if (id < base || id >= base + SMP_CHUNK || id >= V) continue;
+      const int local = (int)(id - base);
+      if ((local % SMP_THREADS) != t) continue;
+      const int j = local / SMP_THREADS;
+#pragma unroll
+      for (int jj = 0; jj < SMP_PER; ++jj)
+        if (jj == j && x[jj] != -INFINITY) x[jj] -= pen;
+    }
+  }
+  // ---- draw from softmax(x) by inverse CDF over a fixed token order
+  float m2 = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < SMP_PER; ++j) m2 = fmaxf(m2, x[j]);
+  m2 = row_reduce(m2, RED_MAX, sh, cs);
+  float tsum = 0.f;
+#pragma unroll
+  for (int j = 0; j < SMP_PER; ++j) tsum += (x[j] == -INFINITY) ? 0.f : __expf(x[j] - m2);
+  const int lane = t & 31, w = t >> 5;
+  float incl = tsum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffff, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) sh_scan[w] = incl;
+  __syncthreads();
+  if (w == 0) {
+    float v = sh_scan[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffff, v, o);
+      if (lane >= o) v += y;
+    }
+    sh_scan[lane] = v;  // inclusive warp totals
+  }
+  __syncthreads();
+  const float cta_total = sh_scan[SMP_THREADS / 32 - 1];
+  const float cta_before = cluster_exclusive(cta_total, &sh_slot, cs, rank);
+  const float Z = row_reduce(t == 0 ? cta_total : 0.f, RED_SUM, sh, cs);
+  // the last thread (in token order) holding any mass takes rounding leftovers
+  const float last_owner = row_reduce(tsum > 0.f ? (float)(rank * SMP_THREADS + t) : -1.f, RED_MAX, sh, cs);
+  const float before = cta_before + (incl - tsum) + (w > 0 ? sh_scan[w - 1] : 0.f);
+  const float u = uniform_from(rng[0], rng[1], (unsigned long long)row) * Z;
+  const bool is_last = (float)(rank * SMP_THREADS + t) == last_owner;
+  if (tsum > 0.f && u >= before && (u < before + tsum || is_last)) {
+    float c = before;
+    int pick = -1, last_nz = -1;
+#pragma unroll
+    for (int j = 0; j < SMP_PER; ++j) {
+      const float e = (x[j] == -INFINITY) ? 0.f : __expf(x[j] - m2);
+      if (e > 0.f) last_nz = j;
+      if (pick < 0 && e > 0.f && u < c + e) pick = j;
+      c += e;
+    }
+    if (pick < 0) pick = last_nz;
+    float xv = -INFINITY;
+#pragma unroll
+    for (int jj = 0; jj < SMP_PER; ++jj)
+      if (jj == pick) xv = x[jj];
+    out_tok[row] = base + t + pick * SMP_THREADS;
+    if (out_lp) out_lp[row] = (xv - m2) - __logf(Z);
+  } else if (last_owner < 0.f && t == 0 && rank == 0) {
+    out_tok[row] = 0;  // every logit was -inf / NaN
+    if (out_lp) out_lp[row] = -INFINITY;
+  }
+}
+
+}  // namespace astrai
+
+namespace astrai_host {
+using namespace astrai;
+
+void paged_kv_write(const void* k, const void* v, long long ld_src, const int* slot, int T, int Hkv, int page_size,
+                    void* kc, void* vc, cudaStream_t s) {
+  const long long work = (long long)T * Hkv * (DEC_D / 8);
+  int blocks = (int)std::min<long long>((work + 255) / 256, 148 * 8);
+  if (blocks < 1) blocks = 1;
+  paged_kv_write_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(k),
+                                               static_cast<const __nv_bfloat16*>(v), ld_src, slot, T, Hkv, page_size,
+                                               static_cast<__nv_bfloat16*>(kc), static_cast<__nv_bfloat16*>(vc));
+}
+
+void paged_kv_gather(const void* kc, const void* vc, const int* table, int max_pages, const int* lens, int B, int S_out,
+                     int Hkv, int page_size, void* ko, void* vo, cudaStream_t s) {
+  const long long work = (long long)B * S_out * Hkv * (DEC_D / 8);
+  int blocks = (int)std::min<long long>((work + 255) / 256, 148 * 16);
+  if (blocks < 1) blocks = 1;
+  paged_kv_gather_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(kc),
+                                                static_cast<const __nv_bfloat16*>(vc), table, max_pages, lens, B, S_out,
+                                                Hkv, page_size, static_cast<__nv_bfloat16*>(ko),
+                                                static_cast<__nv_bfloat16*>(vo));
+}
+
+// splits > 1 writes partials to part_acc [B*Hq*splits*128] / part_ml [B*Hq*splits*2]
+void paged_decode_launch(const void* q, long long ldq, const void* kc, const void* vc, const int* table, int max_pages,
+                         const int* lens, int B, int Hq, int Hkv, int page_size, int splits, float scale_log2,
+                         float* part_acc, float* part_ml, void* out, long long ldo, cudaStream_t s) {
+  DecodeParams p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.ldq = ldq;
+  p.kc = static_cast<const __nv_bfloat16*>(kc);
+  p.vc = static_cast<const __nv_bfloat16*>(vc);
+  p.table = table;
+  p.max_pages = max_pages;
+  p.lens = lens;
+  p.B = B;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.page_size = page_size;
+  p.splits = splits;
+  p.scale_log2 = scale_log2;
+  p.part_acc = part_acc;
+  p.part_ml = part_ml;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  dim3 grid(splits, Hkv, B);
+  switch (Hq / Hkv) {
+    case 1: paged_decode_kernel<1><<<grid, 128, 0, s>>>(p); break;
+    case 2: paged_decode_kernel<2><<<grid, 128, 0, s>>>(p); break;
+    case 4: paged_decode_kernel<4><<<grid, 128, 0, s>>>(p); break;
+    case 8: paged_decode_kernel<8><<<grid, 128, 0, s>>>(p); break;
+    default: throw std::runtime_error("paged_decode: n_heads / n_kv_heads must be 1, 2, 4 or 8");
+  }
+  if (splits > 1)
+    decode_combine_kernel<<<B * Hq, DEC_D, 0, s>>>(part_acc, part_ml, B, Hq, Hkv, splits, static_cast<__nv_bfloat16*>(out), ldo);
+}
+
+// Splits per (batch row, kv head): enough CTAs for two waves of the SMs,
+// at most one split per 64 keys of capacity, at most 32.
+int decode_splits(int B, int Hkv, int max_len, int sms) {
+  const int ctas = B * Hkv;
+  int splits = (2 * sms + ctas - 1) / ctas;
+  const int max_splits = std::max(1, (max_len + 63) / 64);
+  return std::max(1, std::min(splits, std::min(max_splits, 32)));
+}
+
+void sample_tokens(const void* logits, int f32, long long ld, int rows, int V, const float* temperature,
+                   const int* top_k, const float* top_p, const float* penalty, const long long* hist, int hist_len,
+                   long long ld_hist, const unsigned long long* rng, long long* out_tok, float* out_lp,
+                   cudaStream_t s) {
+  const int cs = (V + SMP_CHUNK - 1) / SMP_CHUNK;
+  if (cs > SMP_MAX_CLUSTER) throw std::runtime_error("sample: vocabulary larger than 262144 is not supported");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(rows * cs);
+  cfg.blockDim = dim3(SMP_THREADS);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cs > 8) {
+    static bool nonportable_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!nonportable_set[dev & 63]) {
+      cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      nonportable_set[dev & 63] = true;
+    }
+  }
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, sample_kernel, logits, f32, ld, V, temperature, top_k, top_p, penalty,
+                                           hist, hist_len, ld_hist, rng, out_tok, out_lp);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("sample: launch failed: ") + cudaGetErrorString(e));
+}
+
+}  // namespace astrai_host

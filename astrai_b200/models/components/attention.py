@@ -92,10 +92,15 @@ class GQA(nn.Module):
     def forward(self, x: torch.Tensor, ctx: AttnContext, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
         B, S, _ = x.shape
         Hq, Hkv, D = self.n_heads, self.n_kv_heads, self.head_dim
-        fused = not self.use_qk_norm and ctx.cache is None and ctx.dense_mask is None
+        fused = not self.use_qk_norm and ctx.dense_mask is None
+        if fused and ctx.cache is not None:  # inference: the cache view runs RoPE + KV write + attention
+            fused = getattr(ctx.cache, "supports_qkv", False) and x.is_cuda and x.dtype == torch.bfloat16
         if fused:
             qkv = self.qkv_proj(x).reshape(B * S, (Hq + 2 * Hkv) * D)
-            o = attention_qkv(qkv, B, S, Hq, Hkv, ctx.table, ctx.positions, ctx.causal, ctx.seg)
+            if ctx.cache is not None:
+                o = ctx.cache.attend_qkv(self.layer_id, qkv, B, S, Hq, Hkv, ctx.table)
+            else:
+                o = attention_qkv(qkv, B, S, Hq, Hkv, ctx.table, ctx.positions, ctx.causal, ctx.seg)
             o = o.view(B, S, Hq * D)
         else:
             qkv = self.qkv_proj(x)

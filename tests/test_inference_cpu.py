@@ -1,0 +1,232 @@
+"""CPU tests: KV-cache bookkeeping, sampling semantics, scheduler / engine
+generation against a full forward pass, streaming, tool parsing, stop
+sequences and the HTTP server (FastAPI test client)."""
+
+import json
+
+import pytest
+import torch
+
+from tests.conftest import TINY_CFG
+
+
+def _model(seed=0):
+    from astrai_b200.config import AutoRegressiveLMConfig
+    from astrai_b200.models import AutoRegressiveLM
+
+    torch.manual_seed(seed)
+    m = AutoRegressiveLM(AutoRegressiveLMConfig(**TINY_CFG)).eval()
+    with torch.no_grad():
+        m.lm_head.weight.mul_(20.0)
+    return m
+
+
+def test_allocator_refcount_and_lru_eviction():
+    from astrai_b200.inference import Allocator
+
+    a = Allocator(3)
+    evicted = []
+    a.on_evict = evicted.append
+    assert [a.alloc() for _ in range(3)] == [0, 1, 2]
+    assert a.alloc() == -1
+    a.free(1, keep_cached=True)
+    a.inc_ref(0)
+    a.free(0)
+    assert a.ref_count(0) == 1
+    a.free(0, keep_cached=True)
+    a.touch(1)  # 1 becomes most recent: 0 is evicted first
+    assert a.alloc() == 0 and evicted == [0]
+    assert a.alloc() == 1 and evicted == [0, 1]
+
+
+def test_prefix_hash_chains_pages():
+    from astrai_b200.inference import PrefixCache, page_hash
+
+    pc = PrefixCache(4)
+    a = [1, 2, 3, 4, 9, 9, 9, 9]
+    b = [5, 6, 7, 8, 9, 9, 9, 9]  # same second page content, different prefix
+    assert page_hash(a, 1, 4) != page_hash(b, 1, 4)
+    pc.record(10, a, 0)
+    pc.record(11, a, 1)
+    assert pc.lookup(a) == [10, 11]
+    assert pc.lookup(b) == []
+    assert pc.lookup(a + [1, 2]) == [10, 11]
+
+
+def test_page_cache_sharing_and_extend():
+    from astrai_b200.inference import PageCache
+
+    c = PageCache(1, 8, 4, 1, 8, "cpu", torch.float32)
+    prompt = list(range(10))  # 2 full pages + 2 tokens
+    assert c.task_alloc("a", prompt)
+    assert len(c._table.get("a")) == 3 and c.task_cached("a") == 0
+    c.task_record_hashes("a", prompt)
+    assert c.task_alloc("b", prompt)
+    assert c.task_cached("b") == 8 and c._table.get("b")[:2] == c._table.get("a")[:2]
+    exact = list(range(8))  # a full-page prompt never hits its last page
+    assert c.task_alloc("c", exact) and c.task_cached("c") == 4
+    assert c.task_extend("b", 12) and len(c._table.get("b")) == 4
+    c.task_free("a")
+    c.task_free("b")
+    c.task_free("c")
+    assert c.pool.allocator.num_free == 8
+
+
+def test_strategies_match_reference_semantics():
+    from astrai_b200.inference import FrequencyPenaltyStrategy, TopKStrategy, TopPStrategy
+
+    x = torch.tensor([[3.0, 1.0, 2.0, 0.0]])
+    assert torch.isinf(TopKStrategy(2).apply(x.clone())).tolist() == [[False, True, False, True]]
+    p = torch.softmax(x, -1)[0]
+    # keep while the mass of more likely tokens <= top_p
+    kept = ~torch.isinf(TopPStrategy(float(p[0]) + 1e-3).apply(x.clone()))
+    assert kept.tolist() == [[True, False, True, False]]
+    y = FrequencyPenaltyStrategy(0.5).apply(x.clone(), input_ids=torch.tensor([[0, 0, 3, 7]]),
+                                            input_mask=torch.tensor([[True, True, True, False]]))
+    assert y.tolist() == [[2.0, 1.0, 2.0, -0.5]]
+
+
+def test_sample_cpu_greedy_and_logprobs():
+    from astrai_b200.inference import sample
+
+    x = torch.randn(5, 50)
+    tok, lp = sample(x, temperature=0.0, return_logprobs=True)
+    assert torch.equal(tok, x.argmax(-1))
+    torch.testing.assert_close(lp, torch.log_softmax(x, -1).gather(1, tok[:, None]).squeeze(1))
+    tok = sample(x, temperature=1.0, top_k=1)
+    assert torch.equal(tok, x.argmax(-1))
+
+
+class _Tok:
+    """Whitespace tokenizer over integers (stop id 1)."""
+
+    stop_ids = [1]
+
+    def encode(self, s):
+        return [int(t) for t in s.split()] if isinstance(s, str) else [self.encode(x) for x in s]
+
+    def decode(self, ids, skip_special_tokens=True):
+        return "".join(f" {i}" for i in ids)
+
+    def apply_chat_template(self, messages, tokenize=False, **kw):
+        return " ".join(m["content"] for m in messages)
+
+
+@pytest.mark.parametrize("paged", [False, True])
+def test_run_batch_matches_full_forward(paged):
+    from astrai_b200.inference import InferenceScheduler, PageCache
+
+    m = _model()
+    cache = PageCache(TINY_CFG["num_hidden_layers"], 32, 4, 2, 16, "cpu", torch.float32) if paged else None
+    sch = InferenceScheduler(m, _Tok(), max_batch_size=2, max_seq_len=64, cache=cache)
+    prompts = [[5, 6, 7, 8, 9, 10], [11, 12], [13, 14, 15, 16, 17]]  # 3 prompts: two waves
+    out = sch.run_batch(prompts, max_tokens=5, temperature=0.0, return_logprobs=True)
+    with torch.no_grad():
+        for p, (toks, lps) in zip(prompts, out):
+            seq = list(p)
+            for _ in range(len(toks)):
+                seq.append(int(m(torch.tensor([seq]))["logits"][0, -1].argmax()))
+            assert seq[len(p):] == toks
+            full = torch.log_softmax(m(torch.tensor([seq]))["logits"][0], -1)
+            ref = [float(full[len(p) - 1 + i, t]) for i, t in enumerate(toks)]
+            assert max(abs(a - b) for a, b in zip(ref, lps)) < 1e-4
+    if paged:  # second pass reuses the recorded prompt pages and must produce the same tokens
+        again = sch.run_batch(prompts, max_tokens=5, temperature=0.0)
+        assert again == [o[0] for o in out]
+
+
+def test_engine_streaming_batch_and_stats():
+    from astrai_b200.inference import GenerationRequest, InferenceEngine
+
+    with InferenceEngine(_model(), _Tok(), max_batch_size=2, max_seq_len=48) as eng:
+        stream = list(eng.generate("5 6 7", stream=True, max_tokens=4, temperature=0.0))
+        text = eng.generate("5 6 7", max_tokens=4, temperature=0.0)
+        assert "".join(stream) == text and len(text.split()) <= 4
+        outs = eng.generate(["5 6 7", "8 9", "10"], max_tokens=3, temperature=0.0)
+        assert outs[0] == " ".join(text.split()[:3]).join(["", ""]) or outs[0].split() == text.split()[:3]
+        pairs = list(eng.generate(["5 6 7", "8 9"], stream=True, max_tokens=2, temperature=0.0))
+        assert {i for i, _ in pairs} <= {0, 1}
+        assert eng.get_stats()["total_tasks"] == 7
+        req = GenerationRequest([{"role": "user", "content": "5 6"}], max_tokens=2, temperature=0.0)
+        assert isinstance(eng.generate_with_request(req), str)
+    with pytest.raises(ValueError):
+        GenerationRequest([], top_p=1.5)
+
+
+def test_stream_decoder_holds_partial_utf8():
+    from astrai_b200.inference import StreamDecoder
+
+    class ByteTok:
+        def decode(self, ids, skip_special_tokens=True):
+            return bytes(ids).decode("utf-8", errors="replace")
+
+    d = StreamDecoder(ByteTok())
+    dash = "—".encode()
+    assert d.push(ord("a")) == "a"
+    assert d.push(dash[0]) == "" and d.push(dash[1]) == ""
+    assert d.push(dash[2]) == "—"
+
+
+def test_stop_checker_holds_back_prefixes():
+    from astrai_b200.inference import StopChecker
+
+    c = StopChecker(["</s>", "STOP"])
+    assert c.cut("hello </") == (None, "hello ")
+    assert c.cut("hello </s> more") == ("</s>", "hello ")
+    assert c.cut("abc") == (None, "abc")
+    assert StopChecker([]).cut("x</") == (None, "x</")
+
+
+def test_tool_parser_streaming_equals_complete():
+    from astrai_b200.inference import ToolParserFactory
+
+    text = 'Let me check. {"name": "weather", "arguments": {"city": "Paris", "d": {"x": [1, 2]}}} ok'
+    p = ToolParserFactory.create("simple_json", tools=[{"type": "function"}])
+    deltas = []
+    for i in range(1, len(text) + 1):
+        deltas += p.feed(text[:i])
+    content = "".join(d["content"] for d in deltas if "content" in d)
+    args = "".join(tc["function"].get("arguments", "") for d in deltas for tc in d.get("tool_calls", []))
+    assert content.startswith("Let me check. ") and "{" not in content
+    assert json.loads(args) == {"city": "Paris", "d": {"x": [1, 2]}}
+    full = p.parse_complete(text)
+    assert full["content"] == "Let me check." and json.loads(full["tool_calls"][0]["function"]["arguments"]) == \
+        {"city": "Paris", "d": {"x": [1, 2]}}
+    assert p.has_tool_calls
+
+
+def test_http_server_openai_and_anthropic():
+    from fastapi.testclient import TestClient
+
+    from astrai_b200.inference import InferenceEngine, get_app
+
+    eng = InferenceEngine(_model(), _Tok(), max_batch_size=2, max_seq_len=48)
+    app = get_app()
+    app.state.engine = eng
+    try:
+        with TestClient(app) as client:
+            assert client.get("/health").json() == {"status": "ok", "model_loaded": True}
+            r = client.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "5 6 7"}],
+                                                          "max_tokens": 4, "temperature": 0.0}).json()
+            text = r["choices"][0]["message"]["content"]
+            assert r["object"] == "chat.completion" and r["usage"]["completion_tokens"] == len(text.split())
+            stop_at = text.split()[1]
+            r2 = client.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "5 6 7"}],
+                                                           "max_tokens": 4, "temperature": 0.0,
+                                                           "stop": f" {stop_at}"}).json()
+            assert r2["choices"][0]["message"]["content"] == text[: text.find(f" {stop_at}")]
+            with client.stream("POST", "/v1/chat/completions",
+                               json={"messages": [{"role": "user", "content": "5 6 7"}], "max_tokens": 4,
+                                     "temperature": 0.0, "stream": True}) as s:
+                lines = [ln for ln in s.iter_lines() if ln.startswith("data: ")]
+            assert lines[-1] == "data: [DONE]"
+            chunks = [json.loads(ln[6:]) for ln in lines[:-1]]
+            streamed = "".join(c["choices"][0]["delta"].get("content", "") for c in chunks)
+            assert streamed == text and chunks[-1]["choices"][0]["finish_reason"] in ("stop", "length")
+            a = client.post("/v1/messages", json={"messages": [{"role": "user", "content": "5 6 7"}],
+                                                  "max_tokens": 4, "temperature": 0.0}).json()
+            assert a["type"] == "message" and a["content"][0]["text"] == text
+            assert client.get("/stats").json()["total_tasks"] >= 4
+    finally:
+        app.state.engine = None
+        eng.shutdown()
