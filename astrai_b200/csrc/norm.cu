@@ -308,3 +308,90 @@ void rmsnorm_bwd(const void* dy, long long lddy, const void* x, long long ldx, c
 }
 
 }  // namespace astrai_host
+
+// ---------------------------------------------------------------------------
+// Allocation-free RMSNorm backward (declared and documented in astrai_c_api.h;
+// no counterpart in the reference project). Same kernels as rmsnorm_bwd above,
+// with the dw partials in a fixed device array instead of caller scratch.
+#include <cstdio>
+#include <mutex>
+
+#include "astrai_c_api.h"
+
+namespace {
+
+static __device__ __align__(256) float g_rmsnorm_bwd_scratch[ASTRAI_RMSNORM_BWD_SCRATCH_FLOATS];
+
+constexpr int kMaxDevices = 64;
+float* g_scratch_ptr[kMaxDevices] = {};
+cudaError_t g_setup_err[kMaxDevices] = {};
+std::once_flag g_setup_once[kMaxDevices];
+
+// Once per device, with that device current: the array's address and the
+// kernels' dynamic shared-memory limits. Allocates nothing.
+void static_scratch_setup(int dev) {
+  float* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_rmsnorm_bwd_scratch);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(astrai::rmsnorm_bwd_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 1024 * 4);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(astrai::rmsnorm_bwd_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 2048 * 4);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(astrai::rmsnorm_bwd_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 4096 * 4);
+  g_setup_err[dev] = e;
+  g_scratch_ptr[dev] = e == cudaSuccess ? p : nullptr;
+}
+
+}  // namespace
+
+extern "C" int astrai_rmsnorm_bwd_static_scratch(const void* dy, long long lddy, const void* x, long long ldx,
+                                                 const void* w, const float* rstd, void* dx, long long lddx,
+                                                 void* dw_bf16, float* dw_f32, int rows, int D, void* stream) {
+  using namespace astrai;
+  if (rows <= 0 || D <= 0 || D % 8 != 0 || D > 4096) {
+    std::fprintf(stderr, "astrai_rmsnorm_bwd_static_scratch: unsupported shape rows=%d D=%d "
+                         "(need rows > 0, D a multiple of 8, D <= 4096)\n", rows, D);
+    return -1;
+  }
+  const int rpb = 64;
+  const long long nb = (static_cast<long long>(rows) + rpb - 1) / rpb;
+  const long long need = nb * D;
+  if (need > ASTRAI_RMSNORM_BWD_SCRATCH_FLOATS) {
+    std::fprintf(stderr, "astrai_rmsnorm_bwd_static_scratch: rows=%d D=%d needs %lld floats of scratch, "
+                         "more than the %lld in the static array\n", rows, D, need,
+                 static_cast<long long>(ASTRAI_RMSNORM_BWD_SCRATCH_FLOATS));
+    return -1;
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (dev < 0 || dev >= kMaxDevices) {
+    std::fprintf(stderr, "astrai_rmsnorm_bwd_static_scratch: device %d is beyond the supported %d\n", dev,
+                 kMaxDevices);
+    return -1;
+  }
+  std::call_once(g_setup_once[dev], static_scratch_setup, dev);
+  if (g_setup_err[dev] != cudaSuccess) return static_cast<int>(g_setup_err[dev]);
+  float* scratch = g_scratch_ptr[dev];
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto DY = static_cast<const __nv_bfloat16*>(dy);
+  auto X = static_cast<const __nv_bfloat16*>(x);
+  auto W = static_cast<const __nv_bfloat16*>(w);
+  auto DX = static_cast<__nv_bfloat16*>(dx);
+  const int blocks = static_cast<int>(nb);
+  const size_t sm = static_cast<size_t>(8) * D * sizeof(float);
+  if (D <= 256 && D % 32 == 0) {
+    rmsnorm_bwd_small_kernel<<<blocks, 256, 0, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb);
+  } else if (D <= 1024) {
+    rmsnorm_bwd_kernel<4><<<blocks, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb);
+  } else if (D <= 2048) {
+    rmsnorm_bwd_kernel<8><<<blocks, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb);
+  } else {
+    rmsnorm_bwd_kernel<16><<<blocks, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return static_cast<int>(e);
+  reduce_cols_kernel<<<(D + 255) / 256, 256, 0, s>>>(scratch, blocks, D, static_cast<__nv_bfloat16*>(dw_bf16),
+                                                     dw_f32);
+  return static_cast<int>(cudaGetLastError());
+}
