@@ -142,6 +142,7 @@ void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
   check_rows(x, "x");
   check_rows(dx, "dx");
   const int D = (int)x.size(1);
+  TORCH_CHECK(D % 8 == 0 && D <= 4096, "rmsnorm_bwd: D must be a multiple of 8 and at most 4096");
   TORCH_CHECK(scratch.scalar_type() == at::kFloat && scratch.numel() >= rmsnorm_bwd_scratch(x.size(0), D), "scratch");
   c10::cuda::CUDAGuard g(x.device());
   astrai_host::rmsnorm_bwd(dy.data_ptr(), dy.stride(0), x.data_ptr(), x.stride(0), w.data_ptr(),

@@ -39,6 +39,6 @@ class _RMSNormFn(torch.autograd.Function):
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     D = x.shape[-1]
     if x.is_cuda and x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and D % 8 == 0 \
-            and (D > 256 or D % 32 == 0):
+            and (D > 256 or D % 32 == 0) and D <= 4096:  # the warp-per-row kernels hold a row in registers
         return _RMSNormFn.apply(x, weight, eps)
     return F.rms_norm(x, (D,), weight, eps)
