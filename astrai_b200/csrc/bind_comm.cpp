@@ -1,4 +1,81 @@
-// Python bindings for the comm kernels (filled in as the kernels land).
+// Python bindings of the NVLink peer-memory collectives.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
-void register_comm(pybind11::module& m) { (void)m; }
+#include <cuda_runtime.h>
+
+namespace astrai_host {
+int* error_word(int device);
+void* symm_alloc(long long bytes, void* handle_out);
+void* symm_open(const void* handle);
+void symm_close(void* p);
+void symm_free(void* p);
+void fused_allreduce(const long long* seg_ptr, const long long* seg_off, int n_seg, long long N, int rank, int world,
+                     long long R, const long long* peer_base, long long off_flag_a, long long off_flag_b,
+                     long long off_sumsq, long long off_recv, long long off_gather, unsigned epoch0, int ctas,
+                     float* sumsq_out, float* clip_coef, float max_norm, unsigned* done, int* err,
+                     unsigned long long wait_ns, cudaStream_t s);
+}  // namespace astrai_host
+
+namespace {
+
+pybind11::tuple symm_alloc(int64_t bytes) {
+  char h[64];
+  void* p = astrai_host::symm_alloc(bytes, h);
+  return pybind11::make_tuple(reinterpret_cast<int64_t>(p), pybind11::bytes(h, 64));
+}
+
+int64_t symm_open(const std::string& handle) {
+  TORCH_CHECK(handle.size() == 64, "symm_open: an IPC handle has 64 bytes");
+  return reinterpret_cast<int64_t>(astrai_host::symm_open(handle.data()));
+}
+
+void i64_check(const at::Tensor& t, const char* n) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kLong && t.is_contiguous(), n, " must be a CUDA int64 tensor");
+}
+
+void fused_allreduce(const at::Tensor& seg_ptr, const at::Tensor& seg_off, int64_t N, int64_t rank, int64_t world,
+                     int64_t R, const at::Tensor& peer_base, int64_t off_flag_a, int64_t off_flag_b, int64_t off_sumsq,
+                     int64_t off_recv, int64_t off_gather, int64_t epoch0, int64_t ctas, at::Tensor& sumsq_out,
+                     const c10::optional<at::Tensor>& clip_coef, double max_norm, at::Tensor& done, double wait_s) {
+  i64_check(seg_ptr, "seg_ptr");
+  i64_check(seg_off, "seg_off");
+  i64_check(peer_base, "peer_base");
+  TORCH_CHECK(seg_off.numel() == seg_ptr.numel() + 1, "seg_off needs n_seg + 1 entries");
+  TORCH_CHECK(peer_base.numel() == world && rank >= 0 && rank < world, "peer_base / rank mismatch");
+  TORCH_CHECK(N % 8 == 0 && R % (8 * world) == 0, "sizes must be multiples of 8 elements per rank");
+  TORCH_CHECK(sumsq_out.is_cuda() && sumsq_out.scalar_type() == at::kFloat, "sumsq_out must be CUDA fp32");
+  TORCH_CHECK(done.is_cuda() && done.scalar_type() == at::kInt, "done must be CUDA int32");
+  float* cc = nullptr;
+  if (clip_coef.has_value()) {
+    TORCH_CHECK(clip_coef->is_cuda() && clip_coef->scalar_type() == at::kFloat, "clip_coef must be CUDA fp32");
+    cc = clip_coef->data_ptr<float>();
+  }
+  if (N == 0) return;
+  const c10::cuda::CUDAGuard g(sumsq_out.device());
+  astrai_host::fused_allreduce(reinterpret_cast<const long long*>(seg_ptr.data_ptr<int64_t>()),
+                               reinterpret_cast<const long long*>(seg_off.data_ptr<int64_t>()),
+                               static_cast<int>(seg_ptr.numel()), N, static_cast<int>(rank), static_cast<int>(world), R,
+                               reinterpret_cast<const long long*>(peer_base.data_ptr<int64_t>()), off_flag_a,
+                               off_flag_b, off_sumsq, off_recv, off_gather, static_cast<unsigned>(epoch0),
+                               static_cast<int>(ctas), sumsq_out.data_ptr<float>(), cc, static_cast<float>(max_norm),
+                               reinterpret_cast<unsigned*>(done.data_ptr<int>()),
+                               astrai_host::error_word(sumsq_out.device().index()),
+                               static_cast<unsigned long long>(wait_s * 1e9), at::cuda::getCurrentCUDAStream().stream());
+}
+
+}  // namespace
+
+void register_comm(pybind11::module& m) {
+  m.def("symm_alloc", &symm_alloc, "cudaMalloc + IPC handle -> (address, 64-byte handle)");
+  m.def("symm_open", &symm_open, "map a peer's IPC handle -> address");
+  m.def("symm_close", [](int64_t p) { astrai_host::symm_close(reinterpret_cast<void*>(p)); });
+  m.def("symm_free", [](int64_t p) { astrai_host::symm_free(reinterpret_cast<void*>(p)); });
+  m.def("fused_allreduce", &fused_allreduce, pybind11::arg("seg_ptr"), pybind11::arg("seg_off"), pybind11::arg("N"),
+        pybind11::arg("rank"), pybind11::arg("world"), pybind11::arg("R"), pybind11::arg("peer_base"),
+        pybind11::arg("off_flag_a"), pybind11::arg("off_flag_b"), pybind11::arg("off_sumsq"),
+        pybind11::arg("off_recv"), pybind11::arg("off_gather"), pybind11::arg("epoch0"), pybind11::arg("ctas"),
+        pybind11::arg("sumsq_out"), pybind11::arg("clip_coef"), pybind11::arg("max_norm"), pybind11::arg("done"),
+        pybind11::arg("wait_s") = 20.0);
+}

@@ -34,6 +34,7 @@ class GradReducer:
         self.group = group
         self.bucket_cap = bucket_cap_mb << 20
         self._fused = None
+        self.last_sumsq: Optional[torch.Tensor] = None  # set by the fused backend, consumed by clipping
 
     def _grads(self) -> List[torch.Tensor]:
         out = []
@@ -52,7 +53,8 @@ class GradReducer:
                 from astrai_b200.parallel.symm import FusedAllReduce
 
                 self._fused = FusedAllReduce(self.group)
-            return self._fused.all_reduce_mean(grads)
+            self.last_sumsq = self._fused.all_reduce_mean(grads)
+            return self.last_sumsq
         works = [dist.all_reduce(g, op=dist.ReduceOp.AVG, group=self.group, async_op=True)
                  if g.is_cuda else dist.all_reduce(g, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
                  for g in grads]

@@ -236,6 +236,21 @@ class DDPExecutor(BaseExecutor):
             self._reducer = GradReducer(m, backend=self.comm_backend, bucket_cap_mb=self.bucket_cap_mb)
         self._reducer.reduce()
 
+    def clip_grad_norm(self, model: nn.Module, max_norm: Optional[float], as_tensor: bool = False):
+        r = self._reducer
+        if r is None or r.last_sumsq is None:
+            return super().clip_grad_norm(model, max_norm, as_tensor)
+        # the fused all-reduce already produced the global squared norm
+        from astrai_b200.ops._ext import native
+        from astrai_b200.optim.fused import clip_state
+
+        st = clip_state(r.last_sumsq.device)
+        native().clip_coef(r.last_sumsq, float(max_norm) if max_norm is not None else -1.0, st.coef, st.norm)
+        r.last_sumsq = None
+        norm = st.norm[0]
+        self.last_grad_norm = norm
+        return norm if as_tensor else float(norm)
+
 
 @ExecutorFactory.register("fsdp2")
 class FSDP2Executor(BaseExecutor):

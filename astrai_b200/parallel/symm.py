@@ -1,0 +1,184 @@
+"""Symmetric peer memory over NVLink and the fused gradient all-reduce.
+
+:class:`SymmetricBuffer` gives every rank of a process group a buffer of the
+same size and maps every peer's buffer into this process (cudaMalloc + CUDA
+IPC handles exchanged over the group), so a kernel can load from and store
+to any rank's buffer through NVLink / NVSwitch. :class:`FusedAllReduce` runs
+the data-parallel gradient all-reduce as one kernel over such a buffer
+(push-based two-shot: scatter slices to their owners, reduce + scale + push
+to every peer, gather), fused with the bf16 cast, the 1/world scaling and
+the global squared gradient norm (bitwise identical on every rank), so
+gradient clipping needs no extra pass over the gradients.
+
+Parity: replaces DDP's bucketed NCCL all-reduce (astrai/parallel/executor.py
+:178-236) and the separate ``clip_grad_norm_`` pass (executor.py:162-166).
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+_ALIGN = 256
+
+
+def _align(x: int) -> int:
+    return (x + _ALIGN - 1) // _ALIGN * _ALIGN
+
+
+class SymmetricBuffer:
+    """``nbytes`` of device memory on every rank, each mapped into every rank."""
+
+    def __init__(self, nbytes: int, group=None, device: Optional[torch.device] = None):
+        from astrai_b200.ops._ext import native
+
+        self.C = native()
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.nbytes = int(nbytes)
+        with torch.cuda.device(self.device):
+            self.local_ptr, handle = self.C.symm_alloc(self.nbytes)
+            handles: List[bytes] = [b""] * self.world
+            dist.all_gather_object(handles, handle, group=group)
+            self.ptrs = [self.local_ptr if q == self.rank else self.C.symm_open(handles[q]) for q in range(self.world)]
+        self.peer_base = torch.tensor(self.ptrs, dtype=torch.int64, device=self.device)
+
+    def close(self) -> None:
+        if getattr(self, "ptrs", None) is None:
+            return
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize()
+            for q, p in enumerate(self.ptrs):
+                if q != self.rank:
+                    self.C.symm_close(p)
+            self.C.symm_free(self.local_ptr)
+        self.ptrs = None
+
+
+class AllReducePlan:
+    """Byte layout of the all-reduce buffer and the round / slice / chunk split.
+
+    Shared by the CUDA path and :func:`emulate_fused_allreduce` (which restates
+    the kernel's index arithmetic on the host).
+    """
+
+    THREADS, UNROLL = 512, 4
+    CHUNK = THREADS * UNROLL * 8  # elements a CTA moves per chunk
+
+    def __init__(self, world: int, round_elems: int, ctas: int):
+        self.world, self.ctas = world, ctas
+        q = 8 * world
+        self.R = max(q, round_elems // q * q)
+        self.S = self.R // world
+        flags = world * ctas * 4
+        self.off_flag_a = 0
+        self.off_flag_b = _align(flags)
+        self.off_sumsq = self.off_flag_b + _align(flags)
+        self.off_recv = self.off_sumsq + _align(world * ctas * 4)
+        self.off_gather = self.off_recv + _align(2 * self.R * 2)
+        self.nbytes = self.off_gather + _align(2 * self.R * 2)
+
+    def rounds(self, N: int) -> int:
+        return (N + self.R - 1) // self.R
+
+    def chunks(self, N: int, rd: int, s: int, b: int):
+        """Element ranges of slice ``s`` of round ``rd`` handled by CTA ``b``."""
+        s0 = rd * self.R + s * self.S
+        s1 = min(s0 + self.S, N)
+        c0 = s0 + b * self.CHUNK
+        while c0 < s1:
+            yield c0, min(c0 + self.CHUNK, s1)
+            c0 += self.ctas * self.CHUNK
+
+
+def emulate_fused_allreduce(flats: Sequence[torch.Tensor], plan: AllReducePlan) -> Tuple[List[torch.Tensor], float]:
+    """Host restatement of the kernel on per-rank flat bf16 arrays: returns the
+    per-rank results and the squared norm (summed in the kernel's order)."""
+    W, G = plan.world, plan.ctas
+    N = flats[0].numel()
+    out = [f.clone() for f in flats]
+    slots = [[0.0] * G for _ in range(W)]
+    for rd in range(plan.rounds(N)):
+        for s in range(W):  # owner s reduces its slice
+            for b in range(G):
+                part = 0.0
+                for c0, c1 in plan.chunks(N, rd, s, b):
+                    acc = sum(f[c0:c1].float() for f in flats)
+                    red = (acc * (1.0 / W)).to(torch.bfloat16)
+                    part += float((red.float() ** 2).sum())
+                    for o in out:
+                        o[c0:c1] = red
+                slots[s][b] += part
+    total = 0.0
+    for q in range(W):
+        total += sum(slots[q])
+    return out, total
+
+
+class FusedAllReduce:
+    """Mean all-reduce of bf16 gradients in place + global squared norm."""
+
+    def __init__(self, group=None, round_elems: int = 16 << 20, ctas: Optional[int] = None, wait_s: float = 20.0):
+        from astrai_b200.ops._ext import native
+
+        self.C = native()
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        n_sm = torch.cuda.get_device_properties(self.device).multi_processor_count
+        self.plan = AllReducePlan(self.world, round_elems, ctas or min(32, n_sm))
+        self.buf = SymmetricBuffer(self.plan.nbytes, group, self.device)
+        self.epoch = 1
+        self.wait_s = float(wait_s)  # bound of every peer wait inside the kernel
+        self.sumsq = torch.zeros(1, device=self.device, dtype=torch.float32)
+        self.done = torch.zeros(1, device=self.device, dtype=torch.int32)
+        self._tables: Dict[tuple, Tuple[torch.Tensor, torch.Tensor, int]] = {}
+
+    @staticmethod
+    def eligible(t: torch.Tensor) -> bool:
+        return (t.is_cuda and t.dtype == torch.bfloat16 and t.is_contiguous() and t.numel() % 8 == 0
+                and t.data_ptr() % 16 == 0)
+
+    def _table(self, grads: List[torch.Tensor]):
+        key = tuple((g.data_ptr(), g.numel()) for g in grads)
+        t = self._tables.get(key)
+        if t is None:
+            offs = [0]
+            for g in grads:
+                offs.append(offs[-1] + g.numel())
+            t = (torch.tensor([g.data_ptr() for g in grads], dtype=torch.int64, device=self.device),
+                 torch.tensor(offs, dtype=torch.int64, device=self.device), offs[-1])
+            self._tables = {key: t}  # one live layout (grads are reused step to step)
+        return t
+
+    def all_reduce_mean(self, grads: List[torch.Tensor]) -> torch.Tensor:
+        """In-place mean over ranks; returns the device fp32 squared norm.
+
+        Every rank must pass gradients of the same sizes in the same order.
+        Gradients that are not 16-byte-aligned contiguous bf16 with a size
+        divisible by 8 go through NCCL instead (and add their own squares).
+        """
+        fused = [g for g in grads if self.eligible(g)]
+        rest = [g for g in grads if not self.eligible(g)]
+        if fused:
+            seg_ptr, seg_off, N = self._table(fused)
+            p = self.plan
+            self.C.fused_allreduce(seg_ptr, seg_off, N, self.rank, self.world, p.R, self.buf.peer_base, p.off_flag_a,
+                                   p.off_flag_b, p.off_sumsq, p.off_recv, p.off_gather, self.epoch, p.ctas,
+                                   self.sumsq, None, 0.0, self.done, self.wait_s)
+            self.epoch += p.rounds(N)
+        else:
+            self.sumsq.zero_()
+        for g in rest:
+            dist.all_reduce(g, op=dist.ReduceOp.AVG, group=self.group)
+            self.sumsq += g.float().pow(2).sum()
+        return self.sumsq
+
+    def close(self) -> None:
+        self.buf.close()

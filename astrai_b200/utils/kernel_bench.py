@@ -1,6 +1,7 @@
 """Device-timed micro-benchmarks of the framework's kernels.
 
-    python -m astrai_b200.utils.kernel_bench [gemm|norm|ce|attn|all]
+    python -m astrai_b200.utils.kernel_bench [gemm|attn|decode|sample|all]
+    torchrun --nproc-per-node N -m astrai_b200.utils.kernel_bench allreduce
 
 Each case is timed with CUDA events on the launching stream after warm-up,
 with a synchronize on both sides; inputs larger than L2 are used where the
@@ -74,9 +75,53 @@ def bench_gemm():
                           "cublas_tflops": round(fl / ms_ref / 1e9, 1)}))
 
 
+def bench_allreduce():
+    """Fused NVLink gradient all-reduce vs NCCL (AVG) on 1 GiB of bf16
+    gradients in 26 tensors; device time, max over ranks."""
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from astrai_b200.parallel.symm import FusedAllReduce
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    W = dist.get_world_size()
+    sizes = [2048 * 2048 * 2] * 16 + [32000 * 2048] * 2 + [2048 * 5632 * 3] * 8
+    n = sum(sizes)
+    grads = [torch.randn(k, device="cuda").to(torch.bfloat16) for k in sizes[:26]]
+    n = sum(g.numel() for g in grads)
+    ar = FusedAllReduce()
+
+    def t_max(fn, iters=10):
+        ms = time_fn(fn, warmup=3, iters=iters)
+        v = torch.tensor([ms], device="cuda")
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+        return float(v)
+
+    fused = t_max(lambda: ar.all_reduce_mean(grads))
+
+    def nccl():
+        for g in grads:
+            dist.all_reduce(g, op=dist.ReduceOp.AVG)
+    ref = t_max(nccl)
+    if dist.get_rank() == 0:
+        bytes_ = n * 2
+        bus = lambda ms: bytes_ * 2 * (W - 1) / W / (ms / 1e3) / 1e9  # noqa: E731
+        print(json.dumps({"kernel": "fused_allreduce", "world": W, "bytes": bytes_, "fused_ms": round(fused, 3),
+                          "fused_busbw_gbs": round(bus(fused), 1), "nccl_ms": round(ref, 3),
+                          "nccl_busbw_gbs": round(bus(ref), 1), "link_ref_gbs": 770.0}))
+    ar.close()
+    dist.destroy_process_group()
+
+
 def main(argv=None):
     which = (argv or sys.argv[1:] or ["all"])[0]
     torch.manual_seed(0)
+    if which == "allreduce":
+        bench_allreduce()
+        return
     if which in ("gemm", "all"):
         bench_gemm()
     if which in ("attn", "all"):

@@ -164,7 +164,8 @@ def run_ours(args, rank, world, local):
     dev = torch.device("cuda", local)
     with torch.device(dev):
         model = AutoRegressiveLM(AutoRegressiveLMConfig(**CFG)).to(torch.bfloat16)
-    executor = ExecutorFactory.create("ddp" if world > 1 else "none", grad_accum_steps=ACCUM)
+    # world > 1: gradient all-reduce + grad-norm^2 in one NVLink peer-memory kernel
+    executor = ExecutorFactory.create("ddp" if world > 1 else "none", grad_accum_steps=ACCUM, comm_backend="fused")
     model = executor.wrap(model)
     opt = MuonMix(executor.unwrap(model), lr=MUON_LR, weight_decay=WD, adamw_lr=ADAMW_LR, adamw_weight_decay=WD,
                   adjust_lr_fn="match_rms_adamw")
@@ -180,7 +181,7 @@ def run_ours(args, rank, world, local):
                 loss = cross_entropy(logits, seq[:, 1:])
                 (loss / ACCUM).backward()
         executor.finish_step(model)
-        clip_grad_norm_(executor.unwrap(model).parameters(), CLIP)
+        executor.clip_grad_norm(model, CLIP, as_tensor=True)
         opt.step()
         opt.zero_grad(set_to_none=True)
         return loss
@@ -281,6 +282,7 @@ def run_ours_e2e(args, rank, world, local, model, executor, opt):
         batch_per_device=BATCH, grad_accum_steps=ACCUM, max_grad_norm=CLIP, ckpt_dir=None, ckpt_interval=10 ** 9,
         log_dir=tempfile.mkdtemp(prefix="astrai_bench_logs_"), nprocs=world,
         parallel_mode="ddp" if world > 1 else "none", device_type="cuda", pin_memory=True,
+        executor_kwargs={"comm_backend": "fused"},
         extra_kwargs={"label_smoothing": 0.0}, metrics=["loss", "lr", "grad_norm"],
     )
     Trainer(tc, callbacks=[Timer()]).train()
