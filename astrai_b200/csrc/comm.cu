@@ -140,8 +140,11 @@ __device__ __forceinline__ void add8(float* a, uint4 u) {
   }
 }
 
+template <int W>
 __global__ void __launch_bounds__(AR_THREADS) fused_allreduce_kernel(ARParams p) {
-  const int b = blockIdx.x, G = gridDim.x, W = p.world, r = p.rank;
+  // phase B keeps UB chunks x W vectors in flight per thread (8 loads)
+  constexpr int UB = W >= 8 ? 1 : 8 / W;
+  const int b = blockIdx.x, G = gridDim.x, r = p.rank;
   const long long S = p.R / W;  // slice elements
   const int n_rounds = (int)((p.N + p.R - 1) / p.R);
   SegCursor cur;
@@ -152,6 +155,7 @@ __global__ void __launch_bounds__(AR_THREADS) fused_allreduce_kernel(ARParams p)
     const int par = rd & 1;
     const long long base = (long long)rd * p.R;
     // ---------------- A: scatter slices s != r to their owners
+#pragma unroll 1
     for (int s = 0; s < W; ++s) {
       if (s == r) continue;
       const long long s0 = base + s * S;
@@ -180,28 +184,44 @@ __global__ void __launch_bounds__(AR_THREADS) fused_allreduce_kernel(ARParams p)
       const long long s1 = min(s0 + S, p.N);
       const __nv_bfloat16* recv = reinterpret_cast<const __nv_bfloat16*>(region(p, r, p.off_recv)) + (long long)par * W * S;
       for (long long c0 = s0 + (long long)b * AR_CHUNK; c0 < s1; c0 += (long long)G * AR_CHUNK) {
+#pragma unroll 1
+        for (int u0 = 0; u0 < AR_UNROLL; u0 += UB) {
+          uint4 in[UB][W];
+          __nv_bfloat16* gp[UB];
 #pragma unroll
-        for (int u = 0; u < AR_UNROLL; ++u) {
-          const long long i = c0 + ((long long)u * AR_THREADS + threadIdx.x) * 8;
-          if (i >= s1) continue;
-          __nv_bfloat16* g = cur.at(p, i);
-          float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-          add8(acc, *reinterpret_cast<const uint4*>(g));
-          for (int q = 0; q < W; ++q)
-            if (q != r) add8(acc, *reinterpret_cast<const uint4*>(recv + (long long)q * S + (i - s0)));
-          uint32_t o[4];
+          for (int u = 0; u < UB; ++u) {
+            const long long i = c0 + ((long long)(u0 + u) * AR_THREADS + threadIdx.x) * 8;
+            gp[u] = nullptr;
+            if (i < s1) {
+              gp[u] = cur.at(p, i);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            o[j] = pack_bf16(acc[2 * j] * p.scale, acc[2 * j + 1] * p.scale);
-            const float2 f = unpack_bf16(o[j]);
-            local_sq += f.x * f.x + f.y * f.y;
+              for (int q = 0; q < W; ++q)
+                in[u][q] = q == r ? *reinterpret_cast<const uint4*>(gp[u])
+                                  : *reinterpret_cast<const uint4*>(recv + (long long)q * S + (i - s0));
+            }
           }
-          const uint4 ov = make_uint4(o[0], o[1], o[2], o[3]);
-          *reinterpret_cast<uint4*>(g) = ov;
-          for (int q = 0; q < W; ++q) {
-            if (q == r) continue;
-            __nv_bfloat16* gq = reinterpret_cast<__nv_bfloat16*>(region(p, q, p.off_gather)) + ((long long)par * W + r) * S;
-            *reinterpret_cast<uint4*>(gq + (i - s0)) = ov;
+#pragma unroll
+          for (int u = 0; u < UB; ++u) {
+            if (gp[u] == nullptr) continue;
+            const long long i = c0 + ((long long)(u0 + u) * AR_THREADS + threadIdx.x) * 8;
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int q = 0; q < W; ++q) add8(acc, in[u][q]);
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              o[j] = pack_bf16(acc[2 * j] * p.scale, acc[2 * j + 1] * p.scale);
+              const float2 f = unpack_bf16(o[j]);
+              local_sq += f.x * f.x + f.y * f.y;
+            }
+            const uint4 ov = make_uint4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<uint4*>(gp[u]) = ov;
+#pragma unroll
+            for (int q = 0; q < W; ++q) {
+              if (q == r) continue;
+              __nv_bfloat16* gq = reinterpret_cast<__nv_bfloat16*>(region(p, q, p.off_gather)) + ((long long)par * W + r) * S;
+              *reinterpret_cast<uint4*>(gq + (i - s0)) = ov;
+            }
           }
         }
       }
@@ -327,7 +347,12 @@ void fused_allreduce(const long long* seg_ptr, const long long* seg_off, int n_s
   p.done = done;
   p.err = err;
   p.wait_ns = wait_ns;
-  fused_allreduce_kernel<<<ctas, AR_THREADS, 0, s>>>(p);
+  switch (world) {
+    case 2: fused_allreduce_kernel<2><<<ctas, AR_THREADS, 0, s>>>(p); break;
+    case 4: fused_allreduce_kernel<4><<<ctas, AR_THREADS, 0, s>>>(p); break;
+    case 8: fused_allreduce_kernel<8><<<ctas, AR_THREADS, 0, s>>>(p); break;
+    default: throw std::runtime_error("fused_allreduce: world size must be 2, 4 or 8");
+  }
 }
 
 }  // namespace astrai_host

