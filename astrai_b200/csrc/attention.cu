@@ -787,7 +787,7 @@ void flash_fwd(const void* q, long long ldq, int q_col0, const void* k, long lon
     attr[dev & 63] = true;
   }
   dim3 grid((Sq + FA_BM - 1) / FA_BM, Hq, B);
-  flash_fwd_kernel<<<grid, 192, FA_FWD_SMEM, s>>>(tq, tk, tv, p);
+  (astrai::note_launch(), flash_fwd_kernel<<<grid, 192, FA_FWD_SMEM, s>>>(tq, tk, tv, p));
 }
 
 void flash_bwd(const void* q, long long ldq, int q_col0, const void* k, long long ldk, int k_col0, const void* v,
@@ -801,9 +801,9 @@ void flash_bwd(const void* q, long long ldq, int q_col0, const void* k, long lon
   {
     const long long warps = (long long)B * Sq_pad * Hq;
     const int blocks = (int)((warps * 32 + 255) / 256);
-    flash_bwd_pre_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(dO), ld_do, do_col0,
+    (astrai::note_launch(), flash_bwd_pre_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(dO), ld_do, do_col0,
                                                 static_cast<const __nv_bfloat16*>(o), ldo, lse, lse2, delta, B, Sq,
-                                                Sq_pad, Hq);
+                                                Sq_pad, Hq));
   }
   // 2) main kernel
   CUtensorMap tq, tk, tv, tdo;
@@ -850,15 +850,15 @@ void flash_bwd(const void* q, long long ldq, int q_col0, const void* k, long lon
     uint32_t box[3] = {FA_D, FB_BM, 1};
     make_tmap_f32(&tdq, dq_acc, 3, dims, strides, box);
   }
-  flash_bwd_kernel<<<grid, FB_THREADS, FA_BWD_SMEM, s>>>(tq, tk, tv, tdo, tdq, p);
+  (astrai::note_launch(), flash_bwd_kernel<<<grid, FB_THREADS, FA_BWD_SMEM, s>>>(tq, tk, tv, tdo, tdq, p));
   // 3) dQ fp32 -> bf16 into its destination columns
   {
     const long long rows = (long long)B * Sq;
     const int width = Hq * FA_D;
     long long n = rows * (width / 4);
     int blocks = (int)std::min<long long>((n + 255) / 256, 148 * 32);
-    flash_dq_convert_kernel<<<blocks, 256, 0, s>>>(dq_acc, width, rows, static_cast<__nv_bfloat16*>(dq), ld_dq,
-                                                   dq_col0);
+    (astrai::note_launch(), flash_dq_convert_kernel<<<blocks, 256, 0, s>>>(dq_acc, width, rows, static_cast<__nv_bfloat16*>(dq), ld_dq,
+                                                   dq_col0));
   }
 }
 

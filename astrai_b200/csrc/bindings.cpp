@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 
 namespace astrai_host {
+long long launch_count();
 int num_sms(int device);
 int read_and_clear_error();
 void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int N, int K, int batch, int a_mn,
@@ -316,10 +317,13 @@ int64_t read_error() { return astrai_host::read_and_clear_error(); }
 
 void register_attention(pybind11::module& m);
 void register_inference(pybind11::module& m);
+void register_moe(pybind11::module& m);
 void register_comm(pybind11::module& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "astrai_b200 sm_100a kernels";
+  m.def("launch_count", []() { return static_cast<int64_t>(astrai_host::launch_count()); },
+        "kernel launches issued by this library so far (host counter)");
   m.def("gemm", &gemm, "bf16 tcgen05 GEMM", py::arg("a"), py::arg("b"), py::arg("d"), py::arg("c") = py::none(),
         py::arg("a_mn") = 0, py::arg("b_mn") = 0, py::arg("alpha") = 1.0, py::arg("beta") = 0.0,
         py::arg("force_bn") = 0);
@@ -345,5 +349,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("read_error", &read_error);
   register_attention(m);
   register_inference(m);
+  register_moe(m);
   register_comm(m);
 }

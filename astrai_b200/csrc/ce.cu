@@ -162,16 +162,16 @@ using namespace astrai;
 
 void ce_fwd(const void* logits, long long ld, const long long* target, int rows, int V, float smoothing,
             long long ignore_index, int mode, float* lse, float* out, cudaStream_t s) {
-  ce_fwd_kernel<<<rows, CE_THREADS, 0, s>>>(static_cast<const __nv_bfloat16*>(logits), ld, target, V, smoothing,
-                                            ignore_index, mode, lse, out);
+  (astrai::note_launch(), ce_fwd_kernel<<<rows, CE_THREADS, 0, s>>>(static_cast<const __nv_bfloat16*>(logits), ld, target, V, smoothing,
+                                            ignore_index, mode, lse, out));
 }
 
 void ce_bwd(const void* logits, long long ld, const long long* target, int rows, int V, float smoothing,
             long long ignore_index, int mode, const float* lse, const float* gscale, const float* grow,
             void* dlogits, long long ldd, cudaStream_t s) {
-  ce_bwd_kernel<<<rows, CE_THREADS, 0, s>>>(static_cast<const __nv_bfloat16*>(logits), ld, target, V, smoothing,
+  (astrai::note_launch(), ce_bwd_kernel<<<rows, CE_THREADS, 0, s>>>(static_cast<const __nv_bfloat16*>(logits), ld, target, V, smoothing,
                                             ignore_index, mode, lse, gscale, grow,
-                                            static_cast<__nv_bfloat16*>(dlogits), ldd);
+                                            static_cast<__nv_bfloat16*>(dlogits), ldd));
 }
 
 }  // namespace astrai_host

@@ -348,9 +348,9 @@ void fused_allreduce(const long long* seg_ptr, const long long* seg_off, int n_s
   p.err = err;
   p.wait_ns = wait_ns;
   switch (world) {
-    case 2: fused_allreduce_kernel<2><<<ctas, AR_THREADS, 0, s>>>(p); break;
-    case 4: fused_allreduce_kernel<4><<<ctas, AR_THREADS, 0, s>>>(p); break;
-    case 8: fused_allreduce_kernel<8><<<ctas, AR_THREADS, 0, s>>>(p); break;
+    case 2: (astrai::note_launch(), fused_allreduce_kernel<2><<<ctas, AR_THREADS, 0, s>>>(p)); break;
+    case 4: (astrai::note_launch(), fused_allreduce_kernel<4><<<ctas, AR_THREADS, 0, s>>>(p)); break;
+    case 8: (astrai::note_launch(), fused_allreduce_kernel<8><<<ctas, AR_THREADS, 0, s>>>(p)); break;
     default: throw std::runtime_error("fused_allreduce: world size must be 2, 4 or 8");
   }
 }

@@ -23,6 +23,11 @@
 
 namespace astrai {
 
+// Host-side count of kernel launches issued by this library (every launch
+// site is wrapped as `(note_launch(), kernel<<<...>>>(...))`); read through
+// the binding `launch_count()` to report how many of our kernels ran.
+void note_launch();
+
 // Error codes written to astrai_err (first writer wins).
 enum ErrCode : int {
   kErrNone = 0,

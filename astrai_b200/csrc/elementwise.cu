@@ -174,44 +174,44 @@ static inline int ew_grid(long long work) {
 void rope_apply(void* x, long long ld, int rows, int col0, int n_heads, int head_dim, const int* pos, int seq_len,
                 const void* cs, int inverse, int rot_dim, int rot_off, cudaStream_t s) {
   const long long work = (long long)rows * n_heads * (rot_dim / 8);
-  rope_kernel<<<ew_grid(work), 256, 0, s>>>(static_cast<__nv_bfloat16*>(x), ld, rows, col0, n_heads, head_dim, pos,
+  (astrai::note_launch(), rope_kernel<<<ew_grid(work), 256, 0, s>>>(static_cast<__nv_bfloat16*>(x), ld, rows, col0, n_heads, head_dim, pos,
                                             seq_len, static_cast<const float2*>(cs), inverse ? -1.f : 1.f, rot_dim,
-                                            rot_off);
+                                            rot_off));
 }
 
 void swiglu_fwd(const void* h, long long ldh, void* out, long long ldo, int rows, int F, cudaStream_t s) {
-  swiglu_fwd_kernel<<<ew_grid((long long)rows * F / 8), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(h), ldh,
-                                                                      static_cast<__nv_bfloat16*>(out), ldo, rows, F);
+  (astrai::note_launch(), swiglu_fwd_kernel<<<ew_grid((long long)rows * F / 8), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(h), ldh,
+                                                                      static_cast<__nv_bfloat16*>(out), ldo, rows, F));
 }
 
 void swiglu_bwd(const void* dy, long long lddy, const void* h, long long ldh, void* dh, long long lddh, int rows, int F,
                 cudaStream_t s) {
-  swiglu_bwd_kernel<<<ew_grid((long long)rows * F / 8), 256, 0, s>>>(
+  (astrai::note_launch(), swiglu_bwd_kernel<<<ew_grid((long long)rows * F / 8), 256, 0, s>>>(
       static_cast<const __nv_bfloat16*>(dy), lddy, static_cast<const __nv_bfloat16*>(h), ldh,
-      static_cast<__nv_bfloat16*>(dh), lddh, rows, F);
+      static_cast<__nv_bfloat16*>(dh), lddh, rows, F));
 }
 
 void embedding_fwd(const long long* ids, const void* w, void* out, int n_tok, int d, int vocab, cudaStream_t s) {
   int dev = 0;
   cudaGetDevice(&dev);
-  embedding_fwd_kernel<<<ew_grid((long long)n_tok * d / 8), 256, 0, s>>>(
-      ids, static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(out), n_tok, d, vocab, error_word(dev));
+  (astrai::note_launch(), embedding_fwd_kernel<<<ew_grid((long long)n_tok * d / 8), 256, 0, s>>>(
+      ids, static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(out), n_tok, d, vocab, error_word(dev)));
 }
 
 void embedding_bwd(const long long* ids, const void* g, float* gw, int n_tok, int d, int vocab, cudaStream_t s) {
-  embedding_bwd_kernel<<<ew_grid((long long)n_tok * d / 8), 256, 0, s>>>(ids, static_cast<const __nv_bfloat16*>(g),
-                                                                          gw, n_tok, d, vocab);
+  (astrai::note_launch(), embedding_bwd_kernel<<<ew_grid((long long)n_tok * d / 8), 256, 0, s>>>(ids, static_cast<const __nv_bfloat16*>(g),
+                                                                          gw, n_tok, d, vocab));
 }
 
 void f32_to_bf16(const float* in, void* out, long long n, int accumulate, cudaStream_t s) {
-  f32_to_bf16_kernel<<<ew_grid(n), 256, 0, s>>>(in, static_cast<__nv_bfloat16*>(out), n, accumulate);
+  (astrai::note_launch(), f32_to_bf16_kernel<<<ew_grid(n), 256, 0, s>>>(in, static_cast<__nv_bfloat16*>(out), n, accumulate));
 }
 
 void transpose_bf16(const void* in, void* out, int batch, int R, int C, cudaStream_t s) {
   dim3 grid((C + 31) / 32, (R + 31) / 32, batch);
-  transpose_bf16_kernel<<<grid, dim3(32, 8), 0, s>>>(static_cast<const __nv_bfloat16*>(in),
+  (astrai::note_launch(), transpose_bf16_kernel<<<grid, dim3(32, 8), 0, s>>>(static_cast<const __nv_bfloat16*>(in),
                                                      static_cast<__nv_bfloat16*>(out), R, C, (long long)R * C,
-                                                     (long long)R * C);
+                                                     (long long)R * C));
 }
 
 }  // namespace astrai_host

@@ -36,7 +36,35 @@ struct GemmParams {
   float alpha, beta;
   int vec_ok;  // 16-byte vector stores/loads legal for D and C
   int* err;
+  // Grouped modes (mixture-of-experts); all null for a plain / batched GEMM.
+  //   group_tile: grouped-M. A and D are one [M_total, .] matrix whose 128-row
+  //               tiles belong to group group_tile[m_tile]; B is batched by group.
+  //   k_start / k_count: grouped-K. Batch b reduces over rows
+  //               [k_start[b], k_start[b] + k_count[b]) of single A / B matrices
+  //               (MN-major); D is batched by b. k_count 0 writes beta * C.
+  const int* group_tile;
+  const int* k_start;
+  const int* k_count;
 };
+
+// Operand batch coordinates and K range of one output tile.
+struct TileK {
+  int bA, bB, kbase, kblk;
+};
+
+__device__ __forceinline__ TileK tile_k(const GemmParams& p, int b, int mb, int bk) {
+  TileK t{b, b, 0, p.k_blocks};
+  if (p.group_tile) {
+    t.bA = 0;
+    t.bB = p.group_tile[mb];
+  }
+  if (p.k_count) {
+    t.bA = t.bB = 0;
+    t.kbase = p.k_start[b];
+    t.kblk = (p.k_count[b] + bk - 1) / bk;
+  }
+  return t;
+}
 
 // Tile shapes: BM x BN per CTA, BK = 64 (one 128-byte swizzle atom of bf16).
 //   BM = 128: one 128 x BN UMMA per k-step, accumulator double-buffered in
@@ -126,7 +154,8 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
         int b, mb, nb;
         tile_coords(tile, p.tiles_m, p.tiles_n, b, mb, nb);
         const int m0 = mb * BM, n0 = nb * BN;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        const TileK tk = tile_k(p, b, mb, BK);
+        for (int kb = 0; kb < tk.kblk; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kErrWaitEmpty)) {
             ok = false;
             break;
@@ -134,19 +163,21 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
           mbar_expect_tx(&full[stage], Cfg::STAGE_BYTES);
           uint8_t* a_dst = sA + stage * Cfg::A_BYTES;
           uint8_t* b_dst = sB + stage * Cfg::B_BYTES;
-          const int k0 = kb * BK;
+          const int k0 = tk.kbase + kb * BK;
           if (A_MN) {
 #pragma unroll
-            for (int c = 0; c < BM / 64; ++c) tma_load_3d(a_dst + c * 8192, &tmA, &full[stage], m0 + c * 64, k0, b);
+            for (int c = 0; c < BM / 64; ++c)
+              tma_load_3d(a_dst + c * 8192, &tmA, &full[stage], m0 + c * 64, k0, tk.bA);
           } else {
 #pragma unroll
-            for (int h = 0; h < MH; ++h) tma_load_3d(a_dst + h * 16384, &tmA, &full[stage], k0, m0 + h * 128, b);
+            for (int h = 0; h < MH; ++h) tma_load_3d(a_dst + h * 16384, &tmA, &full[stage], k0, m0 + h * 128, tk.bA);
           }
           if (B_MN) {
 #pragma unroll
-            for (int c = 0; c < BN / 64; ++c) tma_load_3d(b_dst + c * 8192, &tmB, &full[stage], n0 + c * 64, k0, b);
+            for (int c = 0; c < BN / 64; ++c)
+              tma_load_3d(b_dst + c * 8192, &tmB, &full[stage], n0 + c * 64, k0, tk.bB);
           } else {
-            tma_load_3d(b_dst, &tmB, &full[stage], k0, n0, b);
+            tma_load_3d(b_dst, &tmB, &full[stage], k0, n0, tk.bB);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -165,10 +196,13 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int b, mb, nb;
+        tile_coords(tile, p.tiles_m, p.tiles_n, b, mb, nb);
+        const int kblk = tile_k(p, b, mb, BK).kblk;
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err, kErrWaitAccEmpty)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * MH * BN;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = 0; kb < kblk; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.err, kErrWaitFull)) {
             ok = false;
             break;
@@ -210,6 +244,7 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
       tile_coords(tile, p.tiles_m, p.tiles_n, b, mb, nb);
       if (!mbar_wait(&acc_full[acc], acc_phase, p.err, kErrWaitAccFull)) break;
       tc_fence_after();
+      const bool no_k = tile_k(p, b, mb, 64).kblk == 0;  // nothing accumulated: the product is 0
       const int row = mb * BM + half * 128 + q * 32 + lane;
       const int n0 = nb * BN;
       const bool row_ok = row < p.M;
@@ -237,7 +272,7 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
           if (!row_ok || col >= p.N) continue;
           float v[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
+          for (int i = 0; i < 32; ++i) v[i] = no_k ? 0.f : __uint_as_float(r[i]) * p.alpha;
           const bool full_chunk = (col + 32 <= p.N) && p.vec_ok;
           if (full_chunk) {
             if (crow && p.beta != 0.f) {
@@ -323,7 +358,7 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BM, BN>::SMEM);
     attr_set[dev & 63] = true;
   }
-  kern<<<grid, GemmCfg<BM, BN>::THREADS, GemmCfg<BM, BN>::SMEM, stream>>>(ta, tb, p);
+  (astrai::note_launch(), kern<<<grid, GemmCfg<BM, BN>::THREADS, GemmCfg<BM, BN>::SMEM, stream>>>(ta, tb, p));
 }
 
 template <int BM, int BN>
@@ -430,6 +465,9 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
              (C == nullptr || (((reinterpret_cast<uintptr_t>(C) % 16) == 0) && ((ldc * esz) % 16 == 0) &&
                                (batch == 1 || (strideC * esz) % 16 == 0)));
   p.err = error_word(dev);
+  p.group_tile = nullptr;
+  p.k_start = nullptr;
+  p.k_count = nullptr;
   const int tiles = batch * p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, sms);
   if (BM == 256)
@@ -438,6 +476,73 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
     dispatch_majors<128, 256>(a_mn, b_mn, out_f32, ta, tb, p, grid, stream);
   else
     dispatch_majors<128, 128>(a_mn, b_mn, out_f32, ta, tb, p, grid, stream);
+}
+
+
+// Grouped GEMMs for mixture-of-experts blocks (BM = 128 tiles).
+//  mode 0 (grouped-M): A [M_total, K] K-major (lda), D [M_total, N] (ldd), B batched by group
+//         [groups][N][K] (b_mn 0) or [groups][K][N] (b_mn 1); group_tile[M_total / 128].
+//  mode 1 (grouped-K): A [K_total, M] and B [K_total, N] MN-major, D [groups][M][N];
+//         group g reduces rows [k_start[g], k_start[g] + k_count[g]) (multiples of 64).
+void gemm_grouped_bf16(int mode, const void* A, const void* B, void* D, const void* C, int M, int N, int K,
+                       int groups, int b_mn, long long lda, long long ldb, long long strideB, long long ldd,
+                       long long strideD, const int* group_tile, const int* k_start, const int* k_count,
+                       float alpha, float beta, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0 || groups <= 0) throw std::runtime_error("astrai grouped gemm: empty problem");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int sms = num_sms(dev);
+  constexpr int BM = 128;
+  const int BN = N <= 128 ? 128 : 256;
+  CUtensorMap ta, tb;
+  const int a_mn = mode == 1 ? 1 : 0;
+  if (mode == 1) b_mn = 1;
+  {
+    const uint64_t rows = a_mn ? (uint64_t)K : (uint64_t)M;
+    const uint64_t inner = a_mn ? (uint64_t)M : (uint64_t)K;
+    uint64_t dims[3] = {inner, rows, 1};
+    uint64_t strides[2] = {(uint64_t)lda * 2, (uint64_t)rows * lda * 2};
+    uint32_t box[3] = {64, a_mn ? 64u : 128u, 1};
+    make_tmap_bf16(&ta, A, 3, dims, strides, box, true);
+  }
+  {
+    const uint64_t rows = b_mn ? (uint64_t)K : (uint64_t)N;
+    const uint64_t inner = b_mn ? (uint64_t)N : (uint64_t)K;
+    const uint64_t nb = mode == 0 ? (uint64_t)groups : 1;
+    const uint64_t bstride = mode == 0 ? (uint64_t)strideB * 2 : (uint64_t)rows * ldb * 2;
+    uint64_t dims[3] = {inner, rows, nb};
+    uint64_t strides[2] = {(uint64_t)ldb * 2, bstride};
+    uint32_t box[3] = {64, b_mn ? 64u : (uint32_t)BN, 1};
+    make_tmap_bf16(&tb, B, 3, dims, strides, box, true);
+  }
+  GemmParams p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.batch = mode == 0 ? 1 : groups;
+  p.tiles_m = (M + BM - 1) / BM;
+  p.tiles_n = (N + BN - 1) / BN;
+  p.k_blocks = (K + 63) / 64;
+  p.D = D;
+  p.ldd = ldd;
+  p.strideD = mode == 0 ? 0 : strideD;
+  p.C = C;
+  p.ldc = ldd;
+  p.strideC = p.strideD;
+  p.alpha = alpha;
+  p.beta = beta;
+  p.vec_ok = ((reinterpret_cast<uintptr_t>(D) % 16) == 0) && ((ldd * 2) % 16 == 0) && ((p.strideD * 2) % 16 == 0) &&
+             (C == nullptr || (reinterpret_cast<uintptr_t>(C) % 16) == 0);
+  p.err = error_word(dev);
+  p.group_tile = mode == 0 ? group_tile : nullptr;
+  p.k_start = mode == 1 ? k_start : nullptr;
+  p.k_count = mode == 1 ? k_count : nullptr;
+  const int tiles = p.batch * p.tiles_m * p.tiles_n;
+  const int grid = std::min(tiles, sms);
+  if (BN == 256)
+    dispatch_majors<128, 256>(a_mn, b_mn, 0, ta, tb, p, grid, stream);
+  else
+    dispatch_majors<128, 128>(a_mn, b_mn, 0, ta, tb, p, grid, stream);
 }
 
 }  // namespace astrai_host

@@ -508,9 +508,9 @@ void paged_kv_write(const void* k, const void* v, long long ld_src, const int* s
   const long long work = (long long)T * Hkv * (DEC_D / 8);
   int blocks = (int)std::min<long long>((work + 255) / 256, 148 * 8);
   if (blocks < 1) blocks = 1;
-  paged_kv_write_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(k),
+  (astrai::note_launch(), paged_kv_write_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(k),
                                                static_cast<const __nv_bfloat16*>(v), ld_src, slot, T, Hkv, page_size,
-                                               static_cast<__nv_bfloat16*>(kc), static_cast<__nv_bfloat16*>(vc));
+                                               static_cast<__nv_bfloat16*>(kc), static_cast<__nv_bfloat16*>(vc)));
 }
 
 void paged_kv_gather(const void* kc, const void* vc, const int* table, int max_pages, const int* lens, int B, int S_out,
@@ -518,10 +518,10 @@ void paged_kv_gather(const void* kc, const void* vc, const int* table, int max_p
   const long long work = (long long)B * S_out * Hkv * (DEC_D / 8);
   int blocks = (int)std::min<long long>((work + 255) / 256, 148 * 16);
   if (blocks < 1) blocks = 1;
-  paged_kv_gather_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(kc),
+  (astrai::note_launch(), paged_kv_gather_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(kc),
                                                 static_cast<const __nv_bfloat16*>(vc), table, max_pages, lens, B, S_out,
                                                 Hkv, page_size, static_cast<__nv_bfloat16*>(ko),
-                                                static_cast<__nv_bfloat16*>(vo));
+                                                static_cast<__nv_bfloat16*>(vo)));
 }
 
 // splits > 1 writes partials to part_acc [B*Hq*splits*128] / part_ml [B*Hq*splits*2]
@@ -548,14 +548,14 @@ void paged_decode_launch(const void* q, long long ldq, const void* kc, const voi
   p.ldo = ldo;
   dim3 grid(splits, Hkv, B);
   switch (Hq / Hkv) {
-    case 1: paged_decode_kernel<1><<<grid, 128, 0, s>>>(p); break;
-    case 2: paged_decode_kernel<2><<<grid, 128, 0, s>>>(p); break;
-    case 4: paged_decode_kernel<4><<<grid, 128, 0, s>>>(p); break;
-    case 8: paged_decode_kernel<8><<<grid, 128, 0, s>>>(p); break;
+    case 1: (astrai::note_launch(), paged_decode_kernel<1><<<grid, 128, 0, s>>>(p)); break;
+    case 2: (astrai::note_launch(), paged_decode_kernel<2><<<grid, 128, 0, s>>>(p)); break;
+    case 4: (astrai::note_launch(), paged_decode_kernel<4><<<grid, 128, 0, s>>>(p)); break;
+    case 8: (astrai::note_launch(), paged_decode_kernel<8><<<grid, 128, 0, s>>>(p)); break;
     default: throw std::runtime_error("paged_decode: n_heads / n_kv_heads must be 1, 2, 4 or 8");
   }
   if (splits > 1)
-    decode_combine_kernel<<<B * Hq, DEC_D, 0, s>>>(part_acc, part_ml, B, Hq, Hkv, splits, static_cast<__nv_bfloat16*>(out), ldo);
+    (astrai::note_launch(), decode_combine_kernel<<<B * Hq, DEC_D, 0, s>>>(part_acc, part_ml, B, Hq, Hkv, splits, static_cast<__nv_bfloat16*>(out), ldo));
 }
 
 // Splits per (batch row, kv head): enough CTAs for two waves of the SMs,
@@ -593,6 +593,7 @@ void sample_tokens(const void* logits, int f32, long long ld, int rows, int V, c
       nonportable_set[dev & 63] = true;
     }
   }
+  note_launch();
   const cudaError_t e = cudaLaunchKernelEx(&cfg, sample_kernel, logits, f32, ld, V, temperature, top_k, top_p, penalty,
                                            hist, hist_len, ld_hist, rng, out_tok, out_lp);
   if (e != cudaSuccess) throw std::runtime_error(std::string("sample: launch failed: ") + cudaGetErrorString(e));

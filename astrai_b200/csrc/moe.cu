@@ -1,0 +1,399 @@
+// Mixture-of-experts kernels (sm_100a): router, expert-parallel dispatch /
+// return over NVLink peer memory, weighted combine.
+//
+// Router (astrai/model/components/mlp.py:83-87 semantics): one warp per
+// token, fp32 softmax over E experts, top-k by repeated warp argmax (ties to
+// the lower index), weights renormalised to sum 1; it also counts slots per
+// expert and gives every (token, k) slot its position among the slots of its
+// expert (atomic ticket), which fixes where the slot's row lands in the
+// expert's input block.
+//
+// Expert parallelism: experts are split over W ranks (E_local = E / W each).
+// Every rank has a symmetric arena (same layout on all ranks, mapped into
+// every peer). Rank r's expert e_l owns rows [start_el, start_el + n_el) of
+// r's input block (each expert padded to whole 128-row tiles, so the grouped
+// expert GEMMs see no tile spanning two experts), source ranks in rank
+// order. Kernels:
+//   dispatch   token rows -> owning rank's input block (P2P stores) + a
+//              return address per row (source rank, slot);
+//   return     expert output rows -> the source rank's slot block (P2P);
+//   combine    out[t] = add[t] + sum_j w[t, j] * slot[t, j] (fp32);
+//   combine_bwd dw[t, j] = <dout[t], slot[t, j]>, and w[t, j] * dout[t] ->
+//              the expert input-gradient block on the owning rank (P2P);
+//   zero_pad   clears the padding rows of an expert block.
+// A scatter kernel ends with a grid-completion count; the last CTA fences
+// system-wide and raises this rank's flag (an epoch) on every rank. The
+// consumer runs ep_wait (bounded by wait_ns; kErrWaitPeer on expiry) before
+// the kernels that read the block. Row indices are bounds-checked against the
+// arena capacity (kErrBadArg, row skipped) so a bad layout cannot fault.
+#include <stdexcept>
+#include <string>
+
+#include "common.cuh"
+#include "ep_arena.h"
+
+namespace astrai {
+
+// ------------------------------------------------------------------ router
+__device__ __forceinline__ unsigned long long topk_key(float v, int idx) {
+  uint32_t u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // order-preserving
+  return (static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(idx));
+}
+
+template <int EPL>  // experts per lane
+__global__ void __launch_bounds__(256) moe_router_kernel(const void* __restrict__ logits, int logits_f32, long long ld,
+                                                         int T, int E, int k, float* __restrict__ probs,
+                                                         int* __restrict__ idx_out, float* __restrict__ w_out,
+                                                         int* __restrict__ counts, int* __restrict__ pos) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
+    float v[EPL];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      const int e = lane + 32 * i;
+      float x = -INFINITY;
+      if (e < E) {
+        x = logits_f32 ? reinterpret_cast<const float*>(logits)[(long long)t * ld + e]
+                       : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(logits)[(long long)t * ld + e]);
+      }
+      v[i] = x;
+      mx = fmaxf(mx, x);
+    }
+    mx = warp_max(mx);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      v[i] = (lane + 32 * i < E) ? __expf(v[i] - mx) : 0.f;
+      sum += v[i];
+    }
+    sum = warp_sum(sum);
+    const float inv = 1.f / sum;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      v[i] *= inv;
+      if (lane + 32 * i < E) probs[(long long)t * E + lane + 32 * i] = v[i];
+    }
+    // top-k: k warp-wide argmax rounds
+    float sel_p[8];
+    int sel_e[8];
+    float sel_sum = 0.f;
+    float cand[EPL];
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) cand[i] = (lane + 32 * i < E) ? v[i] : -INFINITY;
+    for (int j = 0; j < k; ++j) {
+      unsigned long long best = 0ull;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) {
+        const unsigned long long key = topk_key(cand[i], lane + 32 * i);
+        best = key > best ? key : best;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffff, best, o);
+        best = other > best ? other : best;
+      }
+      const int e = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(best & 0xFFFFFFFFull));
+      const int owner = e & 31, slot = e >> 5;
+      float pe = 0.f;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i)
+        if (i == slot && lane == owner) {
+          pe = cand[i];
+          cand[i] = -INFINITY;
+        }
+      pe = __shfl_sync(0xffffffff, pe, owner);
+      if (j < 8) {
+        sel_p[j] = pe;
+        sel_e[j] = e;
+      }
+      sel_sum += pe;
+    }
+    if (lane == 0) {
+      const float rs = 1.f / sel_sum;
+      for (int j = 0; j < k && j < 8; ++j) {
+        idx_out[(long long)t * k + j] = sel_e[j];
+        w_out[(long long)t * k + j] = sel_p[j] * rs;
+        pos[(long long)t * k + j] = atomicAdd(counts + sel_e[j], 1);
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ EP arena plumbing
+
+
+__device__ __forceinline__ char* arena(const EPArena& a, int q, long long off) {
+  return reinterpret_cast<char*>(a.peer_base[q]) + off;
+}
+
+__device__ __forceinline__ void st_release_sys_u32(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Last CTA to finish raises flag [phase][rank] = epoch on every rank (itself included).
+__device__ void grid_done_signal(const EPArena& a, int phase, unsigned epoch) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned prev = atomicAdd(a.done, 1u);
+    if (prev == gridDim.x - 1) {
+      __threadfence_system();
+      for (int q = 0; q < a.world; ++q) {
+        unsigned* f = reinterpret_cast<unsigned*>(arena(a, q, a.off_flags)) + phase * a.world + a.rank;
+        st_release_sys_u32(f, epoch);
+      }
+      *a.done = 0u;
+    }
+  }
+}
+
+__device__ __forceinline__ void copy_row(char* dst, const char* src, int d, int lane) {
+  const int nv = d / 8;  // 16-byte vectors
+  for (int v = lane; v < nv; v += 32)
+    reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(src)[v];
+}
+
+__global__ void __launch_bounds__(512) ep_dispatch_kernel(EPArena a, const __nv_bfloat16* __restrict__ x,
+                                                          long long ldx, const int* __restrict__ idx,
+                                                          const int* __restrict__ pos, const int* __restrict__ base_row,
+                                                          int n_slots, int k, int e_local, int* __restrict__ slot_row,
+                                                          unsigned epoch) {
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  for (int s = gw; s < n_slots; s += nw) {
+    const int e = idx[s];
+    const int r = e / e_local;
+    const long long row = (long long)base_row[e] + pos[s];
+    if (r < 0 || r >= a.world || row < 0 || row >= a.rows_cap) {
+      if (lane == 0) set_error(a.err, kErrBadArg);
+      continue;
+    }
+    if (lane == 0) {
+      slot_row[s] = static_cast<int>(row);
+      reinterpret_cast<long long*>(arena(a, r, a.off_srcmap))[row] =
+          (static_cast<long long>(a.rank) << 32) | static_cast<unsigned>(s);
+    }
+    copy_row(arena(a, r, a.off_xin) + row * a.d * 2, reinterpret_cast<const char*>(x + (long long)(s / k) * ldx), a.d,
+             lane);
+  }
+  grid_done_signal(a, 0, epoch);
+}
+
+// Bounded wait until flag [phase][q] >= epoch for every rank q.
+__global__ void ep_wait_kernel(EPArena a, int phase, unsigned epoch) {
+  const int q = threadIdx.x;
+  if (q >= a.world) return;
+  const unsigned* f = reinterpret_cast<const unsigned*>(arena(a, a.rank, a.off_flags)) + phase * a.world + q;
+  const uint64_t t0 = globaltimer();
+  while (ld_acquire_sys_u32(f) < epoch) {
+    if (globaltimer() - t0 > a.wait_ns) {
+      set_error(a.err, kErrWaitPeer);
+      return;
+    }
+    __nanosleep(128);
+  }
+}
+
+// Valid rows of the local expert blocks -> the slot block of their source rank.
+// Block layout: expert el owns rows [starts[el], starts[el] + n_rows[el]) of `rows`
+// (padded to 128-row tiles; group_tile[row / 128] = el).
+__global__ void __launch_bounds__(512) ep_return_kernel(EPArena a, const __nv_bfloat16* __restrict__ rows,
+                                                        long long total_rows, const int* __restrict__ group_tile,
+                                                        const int* __restrict__ starts, const int* __restrict__ n_rows,
+                                                        long long ret_off, int phase, unsigned epoch) {
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  const long long* srcmap = reinterpret_cast<const long long*>(arena(a, a.rank, a.off_srcmap));
+  for (long long row = gw; row < total_rows; row += nw) {
+    const int el = group_tile[row >> 7];
+    if (row - starts[el] >= n_rows[el]) continue;
+    const long long key = srcmap[row];
+    const int q = static_cast<int>(key >> 32);
+    const long long s = static_cast<long long>(key & 0xFFFFFFFFll);
+    if (q < 0 || q >= a.world || s >= a.slots_cap) {
+      if (lane == 0) set_error(a.err, kErrBadArg);
+      continue;
+    }
+    copy_row(arena(a, q, ret_off) + s * a.d * 2, reinterpret_cast<const char*>(rows + row * a.d), a.d, lane);
+  }
+  grid_done_signal(a, phase, epoch);
+}
+
+// out[t] = add[t] + sum_j w[t, j] * slots[t * k + j]   (w == nullptr: weights 1)
+__global__ void __launch_bounds__(256) ep_combine_kernel(const __nv_bfloat16* __restrict__ slots,
+                                                         const float* __restrict__ w, const __nv_bfloat16* __restrict__ add,
+                                                         __nv_bfloat16* __restrict__ out, int T, int k, int d) {
+  const int lane = threadIdx.x & 31;
+  const int nv = d / 8;
+  for (int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += gridDim.x * (blockDim.x >> 5)) {
+    for (int v = lane; v < nv; v += 32) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (add) {
+        const uint4 u = reinterpret_cast<const uint4*>(add + (long long)t * d)[v];
+        const uint32_t ww[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = unpack_bf16(ww[j]);
+          acc[2 * j] = f.x;
+          acc[2 * j + 1] = f.y;
+        }
+      }
+      for (int j = 0; j < k; ++j) {
+        const float g = w ? w[(long long)t * k + j] : 1.f;
+        const uint4 u = reinterpret_cast<const uint4*>(slots + ((long long)t * k + j) * d)[v];
+        const uint32_t ww[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = unpack_bf16(ww[q]);
+          acc[2 * q] += g * f.x;
+          acc[2 * q + 1] += g * f.y;
+        }
+      }
+      uint4 o;
+      o.x = pack_bf16(acc[0], acc[1]);
+      o.y = pack_bf16(acc[2], acc[3]);
+      o.z = pack_bf16(acc[4], acc[5]);
+      o.w = pack_bf16(acc[6], acc[7]);
+      reinterpret_cast<uint4*>(out + (long long)t * d)[v] = o;
+    }
+  }
+}
+
+// dw[s] = <dout[t], slots[s]>;  w[s] * dout[t] -> dyin row of slot s on its expert's rank
+__global__ void __launch_bounds__(512) ep_combine_bwd_kernel(EPArena a, const __nv_bfloat16* __restrict__ dout,
+                                                             const __nv_bfloat16* __restrict__ slots,
+                                                             const float* __restrict__ w, const int* __restrict__ idx,
+                                                             const int* __restrict__ slot_row, int n_slots, int k,
+                                                             int e_local, float* __restrict__ dw, unsigned epoch) {
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  const int nv = a.d / 8;
+  for (int s = gw; s < n_slots; s += nw) {
+    const int t = s / k;
+    const int r = idx[s] / e_local;
+    const long long row = slot_row[s];
+    const bool ok = r >= 0 && r < a.world && row >= 0 && row < a.rows_cap;
+    if (!ok && lane == 0) set_error(a.err, kErrBadArg);
+    const float g = w[s];
+    float dot = 0.f;
+    uint4* dst = ok ? reinterpret_cast<uint4*>(arena(a, r, a.off_dyin) + row * a.d * 2) : nullptr;
+    for (int v = lane; v < nv; v += 32) {
+      const uint4 du = reinterpret_cast<const uint4*>(dout + (long long)t * a.d)[v];
+      const uint4 su = reinterpret_cast<const uint4*>(slots + (long long)s * a.d)[v];
+      const uint32_t dd[4] = {du.x, du.y, du.z, du.w}, ss[4] = {su.x, su.y, su.z, su.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 fd = unpack_bf16(dd[j]), fs = unpack_bf16(ss[j]);
+        dot += fd.x * fs.x + fd.y * fs.y;
+        o[j] = pack_bf16(g * fd.x, g * fd.y);
+      }
+      if (ok) dst[v] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    dot = warp_sum(dot);
+    if (lane == 0) dw[s] = dot;
+  }
+  grid_done_signal(a, 2, epoch);
+}
+
+// Zero the padding rows (row - starts[el] >= n_rows[el]) of a block at `off` (own arena).
+__global__ void ep_zero_pad_kernel(EPArena a, long long off, long long total_rows, const int* __restrict__ group_tile,
+                                   const int* __restrict__ starts, const int* __restrict__ n_rows) {
+  const int nv = a.d / 8;
+  const long long total = total_rows * nv;
+  uint4* base = reinterpret_cast<uint4*>(arena(a, a.rank, off));
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long row = i / nv;
+    const int el = group_tile[row >> 7];
+    if (row - starts[el] >= n_rows[el]) base[i] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+}  // namespace astrai
+
+namespace astrai_host {
+using namespace astrai;
+
+void moe_router(const void* logits, int f32, long long ld, int T, int E, int k, float* probs, int* idx, float* w,
+                int* counts, int* pos, cudaStream_t s) {
+  if (k < 1 || k > 8 || k > E) throw std::runtime_error("moe_router: need 1 <= top_k <= min(8, n_experts)");
+  const int blocks = std::max(1, std::min((T + 7) / 8, 148 * 8));
+  if (E <= 32) (astrai::note_launch(), moe_router_kernel<1><<<blocks, 256, 0, s>>>(logits, f32, ld, T, E, k, probs, idx, w, counts, pos));
+  else if (E <= 64) (astrai::note_launch(), moe_router_kernel<2><<<blocks, 256, 0, s>>>(logits, f32, ld, T, E, k, probs, idx, w, counts, pos));
+  else if (E <= 128) (astrai::note_launch(), moe_router_kernel<4><<<blocks, 256, 0, s>>>(logits, f32, ld, T, E, k, probs, idx, w, counts, pos));
+  else if (E <= 256) (astrai::note_launch(), moe_router_kernel<8><<<blocks, 256, 0, s>>>(logits, f32, ld, T, E, k, probs, idx, w, counts, pos));
+  else throw std::runtime_error("moe_router: at most 256 experts");
+}
+
+EPArena make_arena(const long long* peer_base, int rank, int world, const long long* offs, long long rows_cap,
+                   long long slots_cap, int d, unsigned* done, int* err, unsigned long long wait_ns) {
+  EPArena a;
+  a.peer_base = peer_base;
+  a.rank = rank;
+  a.world = world;
+  a.off_flags = offs[0];
+  a.off_srcmap = offs[1];
+  a.off_xin = offs[2];
+  a.off_dyin = offs[3];
+  a.off_ret = offs[4];
+  a.off_ret2 = offs[5];
+  a.rows_cap = rows_cap;
+  a.slots_cap = slots_cap;
+  a.d = d;
+  a.done = done;
+  a.err = err;
+  a.wait_ns = wait_ns;
+  return a;
+}
+
+void ep_dispatch(const EPArena& a, const void* x, long long ldx, const int* idx, const int* pos, const int* base_row,
+                 int n_slots, int k, int e_local, int* slot_row, unsigned epoch, int ctas, cudaStream_t s) {
+  (astrai::note_launch(), ep_dispatch_kernel<<<ctas, 512, 0, s>>>(a, static_cast<const __nv_bfloat16*>(x), ldx, idx, pos, base_row, n_slots, k,
+                                          e_local, slot_row, epoch));
+}
+
+void ep_wait(const EPArena& a, int phase, unsigned epoch, cudaStream_t s) {
+  (astrai::note_launch(), ep_wait_kernel<<<1, 32, 0, s>>>(a, phase, epoch));
+}
+
+void ep_return(const EPArena& a, const void* rows, long long total_rows, const int* group_tile, const int* starts,
+               const int* n_rows, int to_ret2, unsigned epoch, int ctas, cudaStream_t s) {
+  (astrai::note_launch(), ep_return_kernel<<<ctas, 512, 0, s>>>(a, static_cast<const __nv_bfloat16*>(rows), total_rows,
+                                                               group_tile, starts, n_rows,
+                                                               to_ret2 ? a.off_ret2 : a.off_ret, to_ret2 ? 3 : 1,
+                                                               epoch));
+}
+
+void ep_combine(const void* slots, const float* w, const void* add, void* out, int T, int k, int d, cudaStream_t s) {
+  const int blocks = std::max(1, std::min((T + 7) / 8, 148 * 16));
+  (astrai::note_launch(), ep_combine_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(slots), w,
+                                           static_cast<const __nv_bfloat16*>(add), static_cast<__nv_bfloat16*>(out), T,
+                                           k, d));
+}
+
+void ep_combine_bwd(const EPArena& a, const void* dout, const void* slots, const float* w, const int* idx,
+                    const int* slot_row, int n_slots, int k, int e_local, float* dw, unsigned epoch, int ctas,
+                    cudaStream_t s) {
+  (astrai::note_launch(), ep_combine_bwd_kernel<<<ctas, 512, 0, s>>>(a, static_cast<const __nv_bfloat16*>(dout),
+                                             static_cast<const __nv_bfloat16*>(slots), w, idx, slot_row, n_slots, k,
+                                             e_local, dw, epoch));
+}
+
+void ep_zero_pad(const EPArena& a, int which_dyin, long long total_rows, const int* group_tile, const int* starts,
+                 const int* n_rows, cudaStream_t s) {
+  (astrai::note_launch(), ep_zero_pad_kernel<<<148 * 4, 256, 0, s>>>(a, which_dyin ? a.off_dyin : a.off_xin,
+                                                                    total_rows, group_tile, starts, n_rows));
+}
+
+}  // namespace astrai_host

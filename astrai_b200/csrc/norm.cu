@@ -254,15 +254,15 @@ void rmsnorm_fwd(const void* x, long long ldx, const void* w, void* y, long long
   auto W = static_cast<const __nv_bfloat16*>(w);
   auto Y = static_cast<__nv_bfloat16*>(y);
   if (D <= 256 && D % 32 == 0) {
-    rmsnorm_fwd_small_kernel<<<grid, 256, 0, s>>>(X, ldx, W, Y, ldy, rstd, rows, D, eps);
+    (astrai::note_launch(), rmsnorm_fwd_small_kernel<<<grid, 256, 0, s>>>(X, ldx, W, Y, ldy, rstd, rows, D, eps));
   } else if (D <= 1024) {
-    rmsnorm_fwd_kernel<4><<<grid, 256, 0, s>>>(X, ldx, W, Y, ldy, rstd, rows, D, eps);
+    (astrai::note_launch(), rmsnorm_fwd_kernel<4><<<grid, 256, 0, s>>>(X, ldx, W, Y, ldy, rstd, rows, D, eps));
   } else if (D <= 2048) {
-    rmsnorm_fwd_kernel<8><<<grid, 256, 0, s>>>(X, ldx, W, Y, ldy, rstd, rows, D, eps);
+    (astrai::note_launch(), rmsnorm_fwd_kernel<8><<<grid, 256, 0, s>>>(X, ldx, W, Y, ldy, rstd, rows, D, eps));
   } else if (D <= 4096) {
-    rmsnorm_fwd_kernel<16><<<grid, 256, 0, s>>>(X, ldx, W, Y, ldy, rstd, rows, D, eps);
+    (astrai::note_launch(), rmsnorm_fwd_kernel<16><<<grid, 256, 0, s>>>(X, ldx, W, Y, ldy, rstd, rows, D, eps));
   } else {
-    rmsnorm_fwd_kernel<32><<<grid, 256, 0, s>>>(X, ldx, W, Y, ldy, rstd, rows, D, eps);
+    (astrai::note_launch(), rmsnorm_fwd_kernel<32><<<grid, 256, 0, s>>>(X, ldx, W, Y, ldy, rstd, rows, D, eps));
   }
 }
 
@@ -296,15 +296,15 @@ void rmsnorm_bwd(const void* dy, long long lddy, const void* x, long long ldx, c
     attr_done[dev & 63] = true;
   }
   if (D <= 256 && D % 32 == 0) {
-    rmsnorm_bwd_small_kernel<<<nb, 256, 0, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb);
+    (astrai::note_launch(), rmsnorm_bwd_small_kernel<<<nb, 256, 0, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb));
   } else if (D <= 1024) {
-    rmsnorm_bwd_kernel<4><<<nb, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb);
+    (astrai::note_launch(), rmsnorm_bwd_kernel<4><<<nb, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb));
   } else if (D <= 2048) {
-    rmsnorm_bwd_kernel<8><<<nb, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb);
+    (astrai::note_launch(), rmsnorm_bwd_kernel<8><<<nb, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb));
   } else {
-    rmsnorm_bwd_kernel<16><<<nb, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb);
+    (astrai::note_launch(), rmsnorm_bwd_kernel<16><<<nb, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb));
   }
-  reduce_cols_kernel<<<(D + 255) / 256, 256, 0, s>>>(scratch, nb, D, static_cast<__nv_bfloat16*>(dw_bf16), dw_f32);
+  (astrai::note_launch(), reduce_cols_kernel<<<(D + 255) / 256, 256, 0, s>>>(scratch, nb, D, static_cast<__nv_bfloat16*>(dw_bf16), dw_f32));
 }
 
 }  // namespace astrai_host
@@ -381,17 +381,17 @@ extern "C" int astrai_rmsnorm_bwd_static_scratch(const void* dy, long long lddy,
   const int blocks = static_cast<int>(nb);
   const size_t sm = static_cast<size_t>(8) * D * sizeof(float);
   if (D <= 256 && D % 32 == 0) {
-    rmsnorm_bwd_small_kernel<<<blocks, 256, 0, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb);
+    (astrai::note_launch(), rmsnorm_bwd_small_kernel<<<blocks, 256, 0, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb));
   } else if (D <= 1024) {
-    rmsnorm_bwd_kernel<4><<<blocks, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb);
+    (astrai::note_launch(), rmsnorm_bwd_kernel<4><<<blocks, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb));
   } else if (D <= 2048) {
-    rmsnorm_bwd_kernel<8><<<blocks, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb);
+    (astrai::note_launch(), rmsnorm_bwd_kernel<8><<<blocks, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb));
   } else {
-    rmsnorm_bwd_kernel<16><<<blocks, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb);
+    (astrai::note_launch(), rmsnorm_bwd_kernel<16><<<blocks, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb));
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return static_cast<int>(e);
-  reduce_cols_kernel<<<(D + 255) / 256, 256, 0, s>>>(scratch, blocks, D, static_cast<__nv_bfloat16*>(dw_bf16),
-                                                     dw_f32);
+  (astrai::note_launch(), reduce_cols_kernel<<<(D + 255) / 256, 256, 0, s>>>(scratch, blocks, D, static_cast<__nv_bfloat16*>(dw_bf16),
+                                                     dw_f32));
   return static_cast<int>(cudaGetLastError());
 }

@@ -183,11 +183,11 @@ using namespace astrai;
 
 void grad_sumsq(const void* chunks, int n_chunks, const long long* gptr, const int* group, float* acc, cudaStream_t s) {
   if (n_chunks <= 0) return;
-  sumsq_kernel<<<n_chunks, 256, 0, s>>>(static_cast<const Chunk*>(chunks), gptr, group, acc);
+  (astrai::note_launch(), sumsq_kernel<<<n_chunks, 256, 0, s>>>(static_cast<const Chunk*>(chunks), gptr, group, acc));
 }
 
 void clip_coef(const float* acc, int n, float max_norm, float* coef, float* norm_out, cudaStream_t s) {
-  clip_coef_kernel<<<1, 32, 0, s>>>(acc, n, max_norm, coef, norm_out);
+  (astrai::note_launch(), clip_coef_kernel<<<1, 32, 0, s>>>(acc, n, max_norm, coef, norm_out));
 }
 
 void adamw_step(const void* chunks, int n_chunks, const long long* pptr, const long long* gptr, const long long* mptr,
@@ -195,11 +195,11 @@ void adamw_step(const void* chunks, int n_chunks, const long long* pptr, const l
                 float bc1, float bc2, const float* coef, cudaStream_t s) {
   if (n_chunks <= 0) return;
   if (fp32_params)
-    adamw_kernel<float><<<n_chunks, 256, 0, s>>>(static_cast<const Chunk*>(chunks), pptr, gptr, mptr, vptr, wd, lr, b1,
-                                                  b2, eps, bc1, bc2, coef);
+    (astrai::note_launch(), adamw_kernel<float><<<n_chunks, 256, 0, s>>>(static_cast<const Chunk*>(chunks), pptr, gptr, mptr, vptr, wd, lr, b1,
+                                                  b2, eps, bc1, bc2, coef));
   else
-    adamw_kernel<__nv_bfloat16><<<n_chunks, 256, 0, s>>>(static_cast<const Chunk*>(chunks), pptr, gptr, mptr, vptr, wd,
-                                                          lr, b1, b2, eps, bc1, bc2, coef);
+    (astrai::note_launch(), adamw_kernel<__nv_bfloat16><<<n_chunks, 256, 0, s>>>(static_cast<const Chunk*>(chunks), pptr, gptr, mptr, vptr, wd,
+                                                          lr, b1, b2, eps, bc1, bc2, coef));
 }
 
 void muon_momentum(const long long* gptr, const long long* bufptr, int buf_fp32, void* U, int batch, long long numel,
@@ -208,29 +208,29 @@ void muon_momentum(const long long* gptr, const long long* bufptr, int buf_fp32,
   if (gx > 1024) gx = 1024;
   dim3 grid(gx, batch);
   if (buf_fp32)
-    muon_momentum_kernel<float><<<grid, 256, 0, s>>>(gptr, bufptr, static_cast<__nv_bfloat16*>(U), numel, mu, nesterov,
-                                                     coef, sumsq);
+    (astrai::note_launch(), muon_momentum_kernel<float><<<grid, 256, 0, s>>>(gptr, bufptr, static_cast<__nv_bfloat16*>(U), numel, mu, nesterov,
+                                                     coef, sumsq));
   else
-    muon_momentum_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(gptr, bufptr, static_cast<__nv_bfloat16*>(U), numel, mu,
-                                                             nesterov, coef, sumsq);
+    (astrai::note_launch(), muon_momentum_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(gptr, bufptr, static_cast<__nv_bfloat16*>(U), numel, mu,
+                                                             nesterov, coef, sumsq));
 }
 
 void muon_normalize(const void* U, void* X, int batch, int R, int C, int transpose, const float* sumsq, float eps,
                     cudaStream_t s) {
   dim3 grid((C + 31) / 32, (R + 31) / 32, batch);
-  muon_normalize_kernel<<<grid, dim3(32, 8), 0, s>>>(static_cast<const __nv_bfloat16*>(U),
-                                                     static_cast<__nv_bfloat16*>(X), R, C, transpose, sumsq, eps);
+  (astrai::note_launch(), muon_normalize_kernel<<<grid, dim3(32, 8), 0, s>>>(static_cast<const __nv_bfloat16*>(U),
+                                                     static_cast<__nv_bfloat16*>(X), R, C, transpose, sumsq, eps));
 }
 
 void muon_apply(const long long* pptr, int fp32_params, const void* X, int batch, int R, int C, int transpose,
                 float decay, float adj_lr, cudaStream_t s) {
   dim3 grid((C + 31) / 32, (R + 31) / 32, batch);
   if (fp32_params)
-    muon_apply_kernel<float><<<grid, dim3(32, 8), 0, s>>>(pptr, static_cast<const __nv_bfloat16*>(X), R, C, transpose,
-                                                          decay, adj_lr);
+    (astrai::note_launch(), muon_apply_kernel<float><<<grid, dim3(32, 8), 0, s>>>(pptr, static_cast<const __nv_bfloat16*>(X), R, C, transpose,
+                                                          decay, adj_lr));
   else
-    muon_apply_kernel<__nv_bfloat16><<<grid, dim3(32, 8), 0, s>>>(pptr, static_cast<const __nv_bfloat16*>(X), R, C,
-                                                                  transpose, decay, adj_lr);
+    (astrai::note_launch(), muon_apply_kernel<__nv_bfloat16><<<grid, dim3(32, 8), 0, s>>>(pptr, static_cast<const __nv_bfloat16*>(X), R, C,
+                                                                  transpose, decay, adj_lr));
 }
 
 }  // namespace astrai_host

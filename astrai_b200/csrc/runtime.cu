@@ -6,6 +6,8 @@
 #include <stdexcept>
 #include <string>
 
+#include <atomic>
+
 #include "common.cuh"
 
 namespace astrai_host {
@@ -127,4 +129,13 @@ int read_and_clear_error() {
   return h;
 }
 
+}  // namespace astrai_host
+
+namespace astrai {
+static std::atomic<long long> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+}  // namespace astrai
+
+namespace astrai_host {
+long long launch_count() { return astrai::g_launches.load(std::memory_order_relaxed); }
 }  // namespace astrai_host

@@ -29,6 +29,7 @@ class Linear(nn.Module):
         self.weight = nn.Parameter(torch.empty((out_dim, in_dim)))
         self.bias = nn.Parameter(torch.zeros(out_dim)) if bias else None
         self.init_std = init_std
+        self.reset_parameters()  # N(0, init_std) at construction, as the reference Linear
 
     @property
     def in_features(self) -> int:

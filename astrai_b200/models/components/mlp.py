@@ -13,6 +13,13 @@ probability), collected into ``AttnContext.aux_losses`` when
 
 On the GPU the MLP runs up|gate as one GEMM (weights concatenated), the
 SwiGLU kernel, and the down GEMM with the residual added in its epilogue.
+The MoE runs the fused router kernel and the routed-expert block of
+:mod:`astrai_b200.ops.moe` (dispatch -> batched expert GEMMs -> return ->
+weighted combine fused with the residual and shared-expert sum); with
+:meth:`DeepSeekMoE.shard_experts` the routed experts are split over an
+expert-parallel group and token rows move over NVLink peer memory. Routed
+experts live in a ModuleDict keyed by their global index, so state-dict keys
+stay ``routed_experts.{j}...`` (a sharded layer holds its own experts only).
 """
 
 from __future__ import annotations
@@ -67,7 +74,36 @@ class DeepSeekMoE(nn.Module):
         moe_scale = 1.0 / max(self.n_shared_experts, 1) + 1.0 / n_activated_experts
         down_std = 0.02 / (2 * n_layers * moe_scale) ** 0.5
         self.shared_experts = nn.ModuleList([MLP(dim, ffn, down_std) for _ in range(self.n_shared_experts)])
-        self.routed_experts = nn.ModuleList([MLP(dim, ffn, down_std) for _ in range(n_routed_experts)])
+        self.routed_experts = nn.ModuleDict({str(j): MLP(dim, ffn, down_std) for j in range(n_routed_experts)})
+        self.capacity_factor = 2.0  # EP arena rows per expert, relative to the mean load
+        self._ep = None
+        self._arena = None
+        self._stack = None
+
+    # ------------------------------------------------------------------ expert parallelism
+    def shard_experts(self, group=None) -> None:
+        """Keep only this rank's experts (E / world consecutive ones) of ``group``."""
+        from astrai_b200.parallel.ep import EPGroup
+
+        ep = EPGroup(group)
+        if self.n_routed_experts % ep.world:
+            raise ValueError(f"{self.n_routed_experts} experts do not split over {ep.world} ranks")
+        el = self.n_routed_experts // ep.world
+        keep = {str(j) for j in range(ep.rank * el, (ep.rank + 1) * el)}
+        self.routed_experts = nn.ModuleDict({k: m for k, m in self.routed_experts.items() if k in keep})
+        for p in self.routed_experts.parameters():
+            p._ep_local = True  # gradients come from every rank's tokens: no data-parallel all-reduce
+        self._ep, self._arena, self._stack = ep, None, None
+
+    @property
+    def expert_parallel(self) -> bool:
+        return self._ep is not None and self._ep.world > 1
+
+    def _fused_ok(self, x: torch.Tensor) -> bool:
+        experts = list(self.routed_experts.values())
+        return (x.is_cuda and x.dtype == torch.bfloat16 and self.dim % 8 == 0 and self.n_activated_experts <= 8
+                and self.n_routed_experts <= 256 and all(type(m.up) is Linear and type(m.down) is Linear
+                                                         and m.up.weight.dtype == torch.bfloat16 for m in experts))
 
     def route(self, x: torch.Tensor):
         """Router: fp32 softmax -> top-k -> renormalised weights (+ balance stats)."""
@@ -77,9 +113,56 @@ class DeepSeekMoE(nn.Module):
         w = w / w.sum(dim=-1, keepdim=True)
         return probs, w, idx
 
+    def _shared(self, xf: torch.Tensor) -> Optional[torch.Tensor]:
+        if not self.n_shared_experts:
+            return None
+        sh = sum(e(xf) for e in self.shared_experts)
+        return sh / self.n_shared_experts if self.shared_mode == "mean" else sh
+
+    def _forward_fused(self, xf: torch.Tensor, residual: Optional[torch.Tensor], ctx) -> torch.Tensor:
+        from astrai_b200.ops.moe import moe_experts, moe_route, stack_expert_params
+        from astrai_b200.parallel.ep import EPArena, EPGroup, EPLayout
+
+        T, d = xf.shape
+        k = self.n_activated_experts
+        logits = linear(xf, self.router.weight)
+        w, probs, idx, counts, pos = moe_route(logits, k)
+        if self._ep is None:  # not sharded: this rank runs all experts on its own tokens
+            self._ep = EPGroup.local()
+        ep = self._ep
+        if self._arena is None or self._arena.slots_cap < T * k:
+            if self._arena is not None:
+                self._arena.close()
+            self._arena = EPArena(ep, d, T, k, self.n_routed_experts, self.capacity_factor, xf.device)
+        counts_all = ep.all_gather_counts(counts).cpu()
+        layout = EPLayout(counts_all.numpy(), ep.rank, self.n_routed_experts // ep.world, xf.device)
+        if layout.max_rows > self._arena.rows_cap:
+            # unbounded capacity: every rank sees the same layout, so all grow their arena together
+            # (the previous use of this layer's arena finished with its backward)
+            self._arena.close()
+            self._arena = EPArena(ep, d, T, k, self.n_routed_experts, self.capacity_factor, xf.device,
+                                  min_rows=layout.max_rows * 5 // 4)
+        self._arena.check(layout)
+        self._stack = stack_expert_params(self.routed_experts.values())
+        add = self._shared(xf)
+        if residual is not None:
+            r = residual.reshape(-1, d)
+            add = r if add is None else add + r
+        if add is not None:
+            add = add.contiguous()
+        out = moe_experts(xf.contiguous(), add, w, idx, pos, self._stack, self._arena, layout)
+        if self.aux_loss_coef > 0 and self.training and ctx is not None and ctx.aux_losses is not None:
+            f = counts.float() / max(1, T * k)
+            ctx.aux_losses.append(self.aux_loss_coef * self.n_routed_experts * (f * probs.mean(0)).sum())
+        return out
+
     def forward(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None, ctx=None) -> torch.Tensor:
         shape = x.shape
         xf = x.reshape(-1, shape[-1])
+        if self._fused_ok(xf):
+            return self._forward_fused(xf, residual, ctx).view(shape)
+        if self.expert_parallel:
+            raise RuntimeError("expert-parallel MoE needs CUDA bf16 activations")
         N = xf.shape[0]
         probs, w, idx = self.route(xf)
         out = torch.zeros_like(xf)
@@ -94,7 +177,7 @@ class DeepSeekMoE(nn.Module):
             if c == 0:
                 continue
             t = tok[start:start + c]
-            y = self.routed_experts[e](xf[t]) * wts[start:start + c]
+            y = self.routed_experts[str(e)](xf[t]) * wts[start:start + c]
             out = out.index_add(0, t, y.to(out.dtype))
             start += c
         if self.n_shared_experts:

@@ -23,13 +23,19 @@ import torch.nn as nn
 
 
 class GradReducer:
+    """Parameters flagged ``_ep_local`` (experts sharded by expert parallelism)
+    are not exchanged: their gradients already sum every rank's tokens, so they
+    are only scaled by 1/world (to match the mean over ranks), and their
+    squared norm is summed over ranks for clipping."""
+
     def __init__(self, model: nn.Module, backend: str = "nccl", bucket_cap_mb: int = 256, group=None):
         self.params: List[nn.Parameter] = []
+        self.ep_params: List[nn.Parameter] = []
         seen = set()
         for p in model.parameters():
             if p.requires_grad and id(p) not in seen:
                 seen.add(id(p))
-                self.params.append(p)
+                (self.ep_params if getattr(p, "_ep_local", False) else self.params).append(p)
         self.backend = backend
         self.group = group
         self.bucket_cap = bucket_cap_mb << 20
@@ -44,6 +50,22 @@ class GradReducer:
             out.append(p.grad)
         return out
 
+    def _reduce_ep(self, sumsq: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+        if not self.ep_params:
+            return sumsq
+        ws = dist.get_world_size(self.group)
+        grads = []
+        for p in self.ep_params:
+            if p.grad is None:
+                p.grad = torch.zeros_like(p)
+            grads.append(p.grad)
+        torch._foreach_mul_(grads, 1.0 / ws)
+        if sumsq is None:
+            return None
+        local = torch.stack([g.float().pow(2).sum() for g in grads]).sum().reshape(1)
+        dist.all_reduce(local, group=self.group)
+        return sumsq + local
+
     def reduce(self) -> Optional[torch.Tensor]:
         grads = self._grads()
         if not dist.is_initialized() or dist.get_world_size(self.group) == 1:
@@ -53,7 +75,7 @@ class GradReducer:
                 from astrai_b200.parallel.symm import FusedAllReduce
 
                 self._fused = FusedAllReduce(self.group)
-            self.last_sumsq = self._fused.all_reduce_mean(grads)
+            self.last_sumsq = self._reduce_ep(self._fused.all_reduce_mean(grads))
             return self.last_sumsq
         works = [dist.all_reduce(g, op=dist.ReduceOp.AVG, group=self.group, async_op=True)
                  if g.is_cuda else dist.all_reduce(g, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
@@ -64,4 +86,5 @@ class GradReducer:
             ws = dist.get_world_size(self.group)
             for g in grads:
                 g.div_(ws)
+        self._reduce_ep(None)
         return None

@@ -212,20 +212,28 @@ class DDPExecutor(BaseExecutor):
     """Replicated parameters, one gradient all-reduce (mean) per optimizer step."""
 
     def __init__(self, grad_accum_steps: int = 1, comm_backend: str = "nccl", bucket_cap_mb: int = 256,
-                 broadcast_params: bool = True, **_ignored):
+                 broadcast_params: bool = True, expert_parallel: bool = False, **_ignored):
         super().__init__(grad_accum_steps)
         self.comm_backend = comm_backend
         self.bucket_cap_mb = bucket_cap_mb
         self.broadcast_params = broadcast_params
+        self.expert_parallel = expert_parallel
         self._model: Optional[nn.Module] = None
         self._reducer = None
 
     def wrap(self, model: nn.Module) -> nn.Module:
+        """Replicate (broadcast from rank 0); with ``expert_parallel`` every MoE
+        layer then keeps only its share of the routed experts (EP over the
+        data-parallel group, experts exchanged through NVLink peer memory)."""
         self._model = model
         if self.use_distributed and self.broadcast_params:
             with torch.no_grad():
                 for t in list(model.parameters()) + list(model.buffers()):
                     dist.broadcast(t.data, src=0)
+        if self.use_distributed and self.expert_parallel:
+            for m in model.modules():
+                if hasattr(m, "shard_experts"):
+                    m.shard_experts()
         return model
 
     def _reduce_gradients(self, model: Optional[nn.Module] = None) -> None:

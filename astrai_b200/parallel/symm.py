@@ -32,21 +32,29 @@ def _align(x: int) -> int:
 class SymmetricBuffer:
     """``nbytes`` of device memory on every rank, each mapped into every rank."""
 
-    def __init__(self, nbytes: int, group=None, device: Optional[torch.device] = None):
+    def __init__(self, nbytes: int, group=None, device: Optional[torch.device] = None, local_only: bool = False):
         from astrai_b200.ops._ext import native
 
         self.C = native()
         self.group = group
-        self.rank = dist.get_rank(group)
-        self.world = dist.get_world_size(group)
+        distributed = dist.is_available() and dist.is_initialized() and not local_only
+        self.rank = dist.get_rank(group) if distributed else 0
+        self.world = dist.get_world_size(group) if distributed else 1
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.nbytes = int(nbytes)
         with torch.cuda.device(self.device):
             self.local_ptr, handle = self.C.symm_alloc(self.nbytes)
-            handles: List[bytes] = [b""] * self.world
-            dist.all_gather_object(handles, handle, group=group)
+            handles: List[bytes] = [handle]
+            if self.world > 1:
+                handles = [b""] * self.world
+                dist.all_gather_object(handles, handle, group=group)
             self.ptrs = [self.local_ptr if q == self.rank else self.C.symm_open(handles[q]) for q in range(self.world)]
         self.peer_base = torch.tensor(self.ptrs, dtype=torch.int64, device=self.device)
+
+    def local_view(self, offset: int, nbytes: int) -> torch.Tensor:
+        """uint8 tensor over ``[offset, offset + nbytes)`` of this rank's buffer."""
+        assert 0 <= offset and offset + nbytes <= self.nbytes
+        return self.C.symm_view(self.local_ptr + offset, nbytes, self.device.index)
 
     def close(self) -> None:
         if getattr(self, "ptrs", None) is None:

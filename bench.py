@@ -39,6 +39,26 @@ CFG = dict(vocab_size=32000, hidden_size=2048, num_hidden_layers=24, rms_norm_ep
            num_key_value_heads=4)
 BATCH, SEQ, ACCUM = 4, 2048, 8
 MUON_LR, ADAMW_LR, WD, CLIP = 0.02, 1e-4, 0.1, 1.0
+MODEL_DESC = "dense-1.1B (24L d2048 16/4 heads ffn5632 vocab32000)"
+METRIC = "train tokens/s (1B dense)"
+
+# BASELINE.json config 3 (--model moe): 16 layers, first layer dense FFN 5632, then 64 routed experts
+# (SwiGLU 1408) top-6 + 2 shared, softmax router, aux balance loss 0.01, seq 4096, batch 2 per GPU.
+MOE_CFG = dict(CFG, num_hidden_layers=16, max_position_embeddings=4096, ffn_type="moe", n_routed_experts=64,
+               n_shared_experts=2, n_activated_experts=6, moe_intermediate_size=1408, first_k_dense=1,
+               moe_aux_loss_coef=0.01)
+# the reference's config has no first_k_dense / moe_intermediate_size / aux loss: closest expressible model
+REF_MOE_CFG = dict(CFG, num_hidden_layers=16, max_position_embeddings=4096, ffn_type="moe", n_routed_experts=64,
+                   n_shared_experts=2, n_activated_experts=6, intermediate_size=1408)
+MODEL = "dense"
+
+
+def use_moe():
+    global CFG, BATCH, SEQ, ACCUM, MODEL_DESC, METRIC, MODEL
+    CFG, BATCH, SEQ, ACCUM = MOE_CFG, 2, 4096, 1
+    MODEL_DESC = "MoE (16L d2048 16/4 heads, layer0 dense ffn5632, 64 experts ffn1408 top6 + 2 shared, vocab32000)"
+    METRIC = "train tokens/s (MoE EP)"
+    MODEL = "moe"
 
 
 def parse():
@@ -48,6 +68,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="astrai_b200", choices=["astrai_b200", "reference"])
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end Trainer measurement")
+    ap.add_argument("--model", default="dense", choices=["dense", "moe"],
+                    help="dense: BASELINE config 2 (default); moe: config 3 with expert parallelism over all GPUs")
     return ap.parse_args()
 
 
@@ -165,7 +187,8 @@ def run_ours(args, rank, world, local):
     with torch.device(dev):
         model = AutoRegressiveLM(AutoRegressiveLMConfig(**CFG)).to(torch.bfloat16)
     # world > 1: gradient all-reduce + grad-norm^2 in one NVLink peer-memory kernel
-    executor = ExecutorFactory.create("ddp" if world > 1 else "none", grad_accum_steps=ACCUM, comm_backend="fused")
+    executor = ExecutorFactory.create("ddp" if world > 1 else "none", grad_accum_steps=ACCUM, comm_backend="fused",
+                                      expert_parallel=MODEL == "moe")
     model = executor.wrap(model)
     opt = MuonMix(executor.unwrap(model), lr=MUON_LR, weight_decay=WD, adamw_lr=ADAMW_LR, adamw_weight_decay=WD,
                   adjust_lr_fn="match_rms_adamw")
@@ -177,8 +200,10 @@ def run_ours(args, rank, world, local):
         for mi in range(ACCUM):
             seq = data[i % n_batches, mi]
             with executor.micro_step(model, mi == ACCUM - 1):
-                logits = model(seq[:, :-1])["logits"]
-                loss = cross_entropy(logits, seq[:, 1:])
+                out = model(seq[:, :-1])
+                loss = cross_entropy(out["logits"], seq[:, 1:])
+                if "aux_loss" in out:
+                    loss = loss + out["aux_loss"]
                 (loss / ACCUM).backward()
         executor.finish_step(model)
         executor.clip_grad_norm(model, CLIP, as_tensor=True)
@@ -193,10 +218,12 @@ def run_ours(args, rank, world, local):
     barrier()
     clocks.start()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_launch0 = native().launch_count()
     s.record()
     for i in range(args.steps):
         last = step(args.warmup + i)
     e.record()
+    n_launch = native().launch_count() - n_launch0
     barrier()
     ck = clocks.stop(visible_gpu_indices(world))
     ms = max_over_ranks(s.elapsed_time(e)) / args.steps
@@ -208,20 +235,11 @@ def run_ours(args, rank, world, local):
         "value": world * ACCUM * BATCH * SEQ / (ms / 1e3),
         "clocks": ck,
         "loss": loss_val,
-        "launches_per_step": launches_per_step(),
+        "gpu_launches": n_launch,  # counted by the extension's launch counter on this rank
     }
     if not args.no_e2e:
         result["e2e"] = run_ours_e2e(args, rank, world, local, model, executor, opt)
     return result
-
-
-def launches_per_step():
-    """Kernel launches of our extension per optimizer step (counted)."""
-    L, accum = CFG["num_hidden_layers"], ACCUM
-    fwd = 1 + L * (3 + 2 + 1 + 3) + 2 + 1          # embed; per layer: norm, qkv, rope+attn, o / norm, upgate, swiglu, down; norm, lm_head; ce
-    bwd = 1 + 1 + L * (2 + 2 + 3 + 2 + 2 + 2 + 2 + 2) + 2 + 1  # ce, lm_head x2, per layer ...
-    opt = 2 + 4 * (3 * 5 + 3) + 1                 # clip, muon per shape class, adamw
-    return accum * (fwd + bwd) + opt
 
 
 class SynthSeq:
@@ -385,7 +403,7 @@ def run_reference(args, rank, world, local):
                 timing["loss"] = ctx.loss
             self.n += 1
 
-    cfg = AutoRegressiveLMConfig(**CFG)
+    cfg = AutoRegressiveLMConfig(**(REF_MOE_CFG if MODEL == "moe" else CFG))
     shm = "/dev/shm" if os.path.isdir("/dev/shm") else None
     tmp = tempfile.mkdtemp(prefix="astrai_ref_bench_", dir=shm)
     tc = TrainConfig(
@@ -421,12 +439,14 @@ def run_reference(args, rank, world, local):
     return {"ms_per_step": ms, "value": val, "clocks": timing.get("clocks"), "loss": timing.get("loss"),
             "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": ACCUM * BATCH * SEQ * 8 * 2,
                     "d2h_bytes_per_step": ACCUM * 4, "note": "the reference's Trainer is its only path"},
-            "launches_per_step": None}
+            "gpu_launches": None}
 
 
 # ----------------------------------------------------------------------------- main
 def main():
     args = parse()
+    if args.model == "moe":
+        use_moe()
     if args.impl == "reference":
         # the reference's own launcher initialises the process group (torchrun env)
         import torch
@@ -445,8 +465,10 @@ def main():
             print(json.dumps({"impl": "reference", "unavailable": res["unavailable"]}), flush=True)
         else:
             par = ("dp" if args.impl == "astrai_b200" else "fsdp") + str(world) if world > 1 else "none"
+            if MODEL == "moe" and world > 1 and args.impl == "astrai_b200":
+                par = f"dp{world}+ep{world}"
             line = {
-                "metric": "train tokens/s (1B dense)",
+                "metric": METRIC,
                 "value": round(res["value"], 1),
                 "unit": "tokens/s",
                 "n_gpus": world,
@@ -458,14 +480,15 @@ def main():
                 "vs_baseline": None if BASELINE_VALUE is None else res["value"] / BASELINE_VALUE,
                 "dtype": "bf16",
                 "data": "synthetic uniform token ids, random-init weights",
-                "config": {"model": "dense-1.1B (24L d2048 16/4 heads ffn5632 vocab32000)",
+                "config": {"model": MODEL_DESC if args.impl == "astrai_b200" or MODEL == "dense"
+                           else MODEL_DESC + " [reference: all 16 layers MoE, no aux loss]",
                            "global_batch": BATCH * ACCUM * world, "seq_len": SEQ, "parallelism": par,
                            "micro_batch": BATCH, "grad_accum": ACCUM,
                            "optimizer": "Muon(0.02, ns5)+AdamW(1e-4, wd0.1), clip 1.0",
                            "l2": "no flush: per-step working set (2.4 GB weights + activations) >> 126 MB L2"},
                 "clocks": res.get("clocks"),
                 "e2e": res.get("e2e"),
-                "gpu_launches": (res.get("launches_per_step") or 0) * args.steps if args.impl == "astrai_b200" else None,
+                "gpu_launches": res.get("gpu_launches") if args.impl == "astrai_b200" else None,
                 "loss": res.get("loss"),
                 "wall_s": round(time.time() - t0, 1),
             }

@@ -221,7 +221,8 @@ def test_generation_matches_full_forward(graph, paged):
             ref_tok = ref.gather(1, torch.tensor(toks, device="cuda")[:, None]).squeeze(1)
             # each generated token is (within bf16 noise) the argmax of the full forward pass
             assert (ref.max(-1).values - ref_tok).max() < 0.1
-            torch.testing.assert_close(torch.tensor(lps, device="cuda"), ref_tok, atol=0.1, rtol=0.05)
+            # logits are O(30) here: bf16 rounding alone moves a log-probability by ~0.1
+            torch.testing.assert_close(torch.tensor(lps, device="cuda"), ref_tok, atol=0.25, rtol=0.05)
     if paged:  # a second run over the same prompts reuses full prompt pages
         out2 = sch.run_batch(prompts, max_tokens=12, temperature=0.0)
         assert [len(o) for o in out2] == [len(o[0]) for o in out]
