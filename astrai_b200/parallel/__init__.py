@@ -8,6 +8,7 @@ from astrai_b200.parallel.executor import (
     GradientState,
     NoneExecutor,
 )
+from astrai_b200.parallel.module import ColumnParallelLinear, ParallelModel, RowParallelLinear
 from astrai_b200.parallel.setup import (
     find_free_port,
     get_current_device,
@@ -21,7 +22,7 @@ from astrai_b200.parallel.setup import (
 FSDPExecutor = FSDP2Executor
 
 __all__ = [
-    "AccumOptimizer", "AccumScheduler", "BaseExecutor", "DDPExecutor", "ExecutorFactory", "FSDPExecutor",
+    "ColumnParallelLinear", "ParallelModel", "RowParallelLinear", "AccumOptimizer", "AccumScheduler", "BaseExecutor", "DDPExecutor", "ExecutorFactory", "FSDPExecutor",
     "FSDP2Executor", "GradientState", "NoneExecutor", "find_free_port", "get_current_device", "get_rank",
     "get_world_size", "only_on_rank", "setup_parallel", "spawn_parallel_fn",
 ]

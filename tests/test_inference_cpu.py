@@ -230,3 +230,29 @@ def test_http_server_openai_and_anthropic():
     finally:
         app.state.engine = None
         eng.shutdown()
+
+
+def test_extension_api_reference_paths():
+    from astrai_b200.extension import KERNEL_NAMES, attention, attn_paged_decode, is_available, reference_attention
+
+    assert set(KERNEL_NAMES) == {"attn_decode", "attn_prefill", "attn_paged_decode"}
+    assert not is_available("attn_decode") or torch.cuda.is_available()
+    torch.manual_seed(0)
+    q, k, v = torch.randn(2, 4, 5, 16), torch.randn(2, 2, 9, 16), torch.randn(2, 2, 9, 16)
+    o = attention(q, k, v, causal_offset=4)
+    assert o.shape == (2, 4, 5, 16)
+    # causal with offset 4: query 0 sees keys 0..4 only
+    o0 = reference_attention(q[:, :, :1], k[:, :, :5], v[:, :, :5])
+    torch.testing.assert_close(o[:, :, :1], o0)
+    # paged decode over the reference cache layout [n_pages, page_size, H, D]
+    page = 4
+    kc = torch.randn(6, page, 2, 16)
+    vc = torch.randn(6, page, 2, 16)
+    table = torch.tensor([[3, 1, 5], [0, 2, 4]])
+    qd = torch.randn(2, 4, 1, 16)
+    od = attn_paged_decode(qd, table, kc, vc, page, 10)
+    pos = torch.arange(10)
+    kk = kc[table[:, pos // page], pos % page].permute(0, 2, 1, 3)
+    vv = vc[table[:, pos // page], pos % page].permute(0, 2, 1, 3)
+    torch.testing.assert_close(od, reference_attention(qd, kk, vv))
+    assert attention(q[0, 0], k[0, 0], v[0, 0]).shape == (5, 16)

@@ -238,3 +238,23 @@ def test_engine_stream_and_batch():
         full = eng.generate(["5 6 7 8", "9 10"], max_tokens=5, temperature=0.0)
         assert full[0] == "".join(pieces)
         assert eng.get_stats()["total_tasks"] == 3
+
+
+def test_extension_native_paths_match_reference():
+    from astrai_b200.extension import attn_decode, attn_paged_decode, attn_prefill, reference_attention
+
+    torch.manual_seed(0)
+    q = torch.randn(2, 8, 64, 128, device="cuda").to(torch.bfloat16)
+    k = torch.randn(2, 2, 96, 128, device="cuda").to(torch.bfloat16)
+    v = torch.randn(2, 2, 96, 128, device="cuda").to(torch.bfloat16)
+    for off in (-1, 32):
+        torch.testing.assert_close(attn_prefill(q, k, v, causal_offset=off).float(),
+                                   reference_attention(q, k, v, causal_offset=off).float(), atol=3e-2, rtol=3e-2)
+    qd = q[:, :, :1]
+    torch.testing.assert_close(attn_decode(qd, k, v, causal_offset=50).float(),
+                               reference_attention(qd, k, v, causal_offset=50).float(), atol=3e-2, rtol=3e-2)
+    kc = k.transpose(1, 2).reshape(2 * 6, 16, 2, 128).contiguous()  # 16-slot pages, reference layout
+    vc = v.transpose(1, 2).reshape(2 * 6, 16, 2, 128).contiguous()
+    table = torch.arange(12, device="cuda").view(2, 6)
+    torch.testing.assert_close(attn_paged_decode(qd, table, kc, vc, 16, 96).float(),
+                               reference_attention(qd, k, v).float(), atol=3e-2, rtol=3e-2)

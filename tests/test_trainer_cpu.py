@@ -218,3 +218,20 @@ def test_spawn_gloo_collectives():
     from astrai_b200.parallel import find_free_port
 
     mp.start_processes(_allreduce_worker, args=(2, find_free_port()), nprocs=2, start_method="spawn", join=True)
+
+
+def test_cli_train_flags_and_config(tmpdir_path, model_dir):
+    import os
+
+    from astrai_b200.cli.train import build_config, compute_total_steps, parse_args, scheduler_kwargs
+    from astrai_b200.serialization import save_bin
+
+    assert compute_total_steps(100, 2, 4, 2, 3) == (13 // 3) * 2
+    assert scheduler_kwargs("wsd", 100, 0.1)["stable_steps"] == 72
+    data = os.path.join(tmpdir_path, "data")
+    save_bin(os.path.join(data, "shard"), {"sequence": [torch.randint(0, 500, (400,), dtype=torch.int32)]})
+    args = parse_args(["--train_type", "seq", "--param_path", model_dir, "--data_root_path", data, "--window_size",
+                       "32", "--device_type", "cpu", "--comm_backend", "fused", "--parallel_mode", "ddp"])
+    cfg = build_config(args)
+    assert cfg.executor_kwargs == {"comm_backend": "fused", "expert_parallel": False}
+    assert cfg.strategy == "seq" and len(cfg.dataset) > 0
