@@ -112,7 +112,8 @@ def run_engine_decode(model, cfg, kind: str, batch: int, prompt: int, gen: int) 
 
     dev = next(model.parameters()).device
     dtype = next(model.parameters()).dtype
-    max_seq = prompt + gen + 1
+    warm = 3
+    max_seq = prompt + 1 + warm + gen  # prefill token + warm-up steps + timed steps
     cache = _make_cache(cfg, kind, batch, max_seq, dev, dtype)
     ex = Executor(model, None, cache, dev, dtype, use_cuda_graph=True, max_batch_size=batch, max_seq_len=max_seq,
                   seed=0)
@@ -123,7 +124,7 @@ def run_engine_decode(model, cfg, kind: str, batch: int, prompt: int, gen: int) 
         cache.task_alloc(t.task_id, t.prompt_ids)
         cache.task_extend(t.task_id, max_seq - 1)
     ex.execute_prefill(tasks, prompt, 0)
-    for _ in range(3):  # capture + warm the graph
+    for _ in range(warm):  # capture + warm the graph
         ex.execute_decode(tasks)
     t = _timed(lambda: [ex.execute_decode(tasks) for _ in range(gen)])
     n = batch * gen

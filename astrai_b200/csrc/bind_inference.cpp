@@ -9,11 +9,11 @@
 namespace astrai_host {
 int num_sms(int device);
 void paged_kv_write(const void* k, const void* v, long long ld_src, const int* slot, int T, int Hkv, int page_size,
-                    void* kc, void* vc, cudaStream_t s);
+                    int n_pages, void* kc, void* vc, cudaStream_t s);
 void paged_kv_gather(const void* kc, const void* vc, const int* table, int max_pages, const int* lens, int B, int S_out,
-                     int Hkv, int page_size, void* ko, void* vo, cudaStream_t s);
+                     int Hkv, int page_size, int n_pages, void* ko, void* vo, cudaStream_t s);
 void paged_decode_launch(const void* q, long long ldq, const void* kc, const void* vc, const int* table, int max_pages,
-                         const int* lens, int B, int Hq, int Hkv, int page_size, int splits, float scale_log2,
+                         int n_pages, const int* lens, int B, int Hq, int Hkv, int page_size, int splits, float scale_log2,
                          float* part_acc, float* part_ml, void* out, long long ldo, cudaStream_t s);
 int decode_splits(int B, int Hkv, int max_len, int sms);
 void sample_tokens(const void* logits, int f32, long long ld, int rows, int V, const float* temperature,
@@ -60,7 +60,8 @@ void paged_kv_write(const at::Tensor& k, const at::Tensor& v, const at::Tensor& 
   if (T == 0) return;
   const c10::cuda::CUDAGuard g(k.device());
   astrai_host::paged_kv_write(k.data_ptr(), v.data_ptr(), k.stride(0), slot.data_ptr<int>(), T, Hkv,
-                              static_cast<int>(kc.size(2)), kc.data_ptr(), vc.data_ptr(), cur_stream());
+                              static_cast<int>(kc.size(2)), static_cast<int>(kc.size(0)), kc.data_ptr(), vc.data_ptr(),
+                              cur_stream());
 }
 
 // -> (k, v) [B, S_out, Hkv, 128]; rows past lens[b] are zero
@@ -79,7 +80,7 @@ std::vector<at::Tensor> paged_kv_gather(const at::Tensor& kc, const at::Tensor& 
   const c10::cuda::CUDAGuard g(kc.device());
   astrai_host::paged_kv_gather(kc.data_ptr(), vc.data_ptr(), table.data_ptr<int>(), static_cast<int>(table.size(1)),
                                lens.data_ptr<int>(), B, static_cast<int>(S_out), Hkv, static_cast<int>(kc.size(2)),
-                               ko.data_ptr(), vo.data_ptr(), cur_stream());
+                               static_cast<int>(kc.size(0)), ko.data_ptr(), vo.data_ptr(), cur_stream());
   return {ko, vo};
 }
 
@@ -121,7 +122,8 @@ void paged_decode(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& v
   }
   const c10::cuda::CUDAGuard g(q.device());
   astrai_host::paged_decode_launch(q.data_ptr(), q.stride(0), kc.data_ptr(), vc.data_ptr(), table.data_ptr<int>(),
-                                   static_cast<int>(table.size(1)), lens.data_ptr<int>(), B, static_cast<int>(Hq), Hkv,
+                                   static_cast<int>(table.size(1)), static_cast<int>(kc.size(0)), lens.data_ptr<int>(),
+                                   B, static_cast<int>(Hq), Hkv,
                                    static_cast<int>(kc.size(2)), static_cast<int>(splits),
                                    static_cast<float>(scale * 1.4426950408889634), part_acc, part_ml, out.data_ptr(),
                                    out.stride(0), cur_stream());

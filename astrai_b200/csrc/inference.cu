@@ -43,7 +43,7 @@ constexpr int DEC_MAXG = 16;
 // src k/v: [T, Hkv, D] rows with row stride ld (elements); slot[t] = page * page_size + offset
 __global__ void paged_kv_write_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
                                       long long ld_src, const int* __restrict__ slot, int T, int Hkv, int page_size,
-                                      __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc) {
+                                      int n_pages, __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc) {
   const int per = DEC_D / 8;  // 16-byte chunks per head row
   const long long total = (long long)T * Hkv * per;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
@@ -52,7 +52,7 @@ __global__ void paged_kv_write_kernel(const __nv_bfloat16* __restrict__ k, const
     const int h = th % Hkv;
     const int t = th / Hkv;
     const int s = slot[t];
-    if (s < 0) continue;
+    if (s < 0 || s >= n_pages * page_size) continue;  // -1 = skip; never write outside the cache
     const int page = s / page_size, off = s % page_size;
     const long long dst = (((long long)page * Hkv + h) * page_size + off) * DEC_D + c * 8;
     const long long src = (long long)t * ld_src + h * DEC_D + c * 8;
@@ -64,7 +64,7 @@ __global__ void paged_kv_write_kernel(const __nv_bfloat16* __restrict__ k, const
 // out k/v: [B, S_out, Hkv, D] contiguous; positions >= len[b] are zero-filled
 __global__ void paged_kv_gather_kernel(const __nv_bfloat16* __restrict__ kc, const __nv_bfloat16* __restrict__ vc,
                                        const int* __restrict__ table, int max_pages, const int* __restrict__ lens,
-                                       int B, int S_out, int Hkv, int page_size, __nv_bfloat16* __restrict__ ko,
+                                       int B, int S_out, int Hkv, int page_size, int n_pages, __nv_bfloat16* __restrict__ ko,
                                        __nv_bfloat16* __restrict__ vo) {
   const int per = DEC_D / 8;
   const long long total = (long long)B * S_out * Hkv * per;
@@ -76,9 +76,9 @@ __global__ void paged_kv_gather_kernel(const __nv_bfloat16* __restrict__ kc, con
     const int pos = r % S_out;
     const int b = r / S_out;
     uint4 kk = make_uint4(0, 0, 0, 0), vv = kk;
-    if (pos < lens[b]) {
+    if (pos < lens[b] && pos / page_size < max_pages) {
       const int page = table[(long long)b * max_pages + pos / page_size];
-      if (page >= 0) {
+      if (page >= 0 && page < n_pages) {
         const long long src = (((long long)page * Hkv + h) * page_size + pos % page_size) * DEC_D + c * 8;
         kk = *reinterpret_cast<const uint4*>(kc + src);
         vv = *reinterpret_cast<const uint4*>(vc + src);
@@ -98,6 +98,7 @@ struct DecodeParams {
   const __nv_bfloat16* vc;
   const int* table;  // [B, max_pages]
   int max_pages;
+  int n_pages;       // pages in the cache: table entries outside [0, n_pages) are skipped
   const int* lens;   // [B] number of cached keys (including the current token)
   int B, Hq, Hkv, page_size, splits;
   float scale_log2;
@@ -151,8 +152,9 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams p) {
 #pragma unroll
     for (int u = 0; u < KU; ++u) {
       const int k = kb + u;
-      const int page = k < k1 ? trow[k / p.page_size] : -1;
-      ok[u] = page >= 0;
+      const int pidx = k / p.page_size;
+      const int page = (k < k1 && pidx < p.max_pages) ? trow[pidx] : -1;
+      ok[u] = page >= 0 && page < p.n_pages;
       if (ok[u]) {
         const long long row = (((long long)page * p.Hkv + hk) * p.page_size + k % p.page_size) * DEC_D + lane * 4;
         ku[u] = *reinterpret_cast<const uint2*>(p.kc + row);
@@ -504,29 +506,29 @@ namespace astrai_host {
 using namespace astrai;
 
 void paged_kv_write(const void* k, const void* v, long long ld_src, const int* slot, int T, int Hkv, int page_size,
-                    void* kc, void* vc, cudaStream_t s) {
+                    int n_pages, void* kc, void* vc, cudaStream_t s) {
   const long long work = (long long)T * Hkv * (DEC_D / 8);
   int blocks = (int)std::min<long long>((work + 255) / 256, 148 * 8);
   if (blocks < 1) blocks = 1;
   (astrai::note_launch(), paged_kv_write_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(k),
-                                               static_cast<const __nv_bfloat16*>(v), ld_src, slot, T, Hkv, page_size,
+                                               static_cast<const __nv_bfloat16*>(v), ld_src, slot, T, Hkv, page_size, n_pages,
                                                static_cast<__nv_bfloat16*>(kc), static_cast<__nv_bfloat16*>(vc)));
 }
 
 void paged_kv_gather(const void* kc, const void* vc, const int* table, int max_pages, const int* lens, int B, int S_out,
-                     int Hkv, int page_size, void* ko, void* vo, cudaStream_t s) {
+                     int Hkv, int page_size, int n_pages, void* ko, void* vo, cudaStream_t s) {
   const long long work = (long long)B * S_out * Hkv * (DEC_D / 8);
   int blocks = (int)std::min<long long>((work + 255) / 256, 148 * 16);
   if (blocks < 1) blocks = 1;
   (astrai::note_launch(), paged_kv_gather_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(kc),
                                                 static_cast<const __nv_bfloat16*>(vc), table, max_pages, lens, B, S_out,
-                                                Hkv, page_size, static_cast<__nv_bfloat16*>(ko),
+                                                Hkv, page_size, n_pages, static_cast<__nv_bfloat16*>(ko),
                                                 static_cast<__nv_bfloat16*>(vo)));
 }
 
 // splits > 1 writes partials to part_acc [B*Hq*splits*128] / part_ml [B*Hq*splits*2]
 void paged_decode_launch(const void* q, long long ldq, const void* kc, const void* vc, const int* table, int max_pages,
-                         const int* lens, int B, int Hq, int Hkv, int page_size, int splits, float scale_log2,
+                         int n_pages, const int* lens, int B, int Hq, int Hkv, int page_size, int splits, float scale_log2,
                          float* part_acc, float* part_ml, void* out, long long ldo, cudaStream_t s) {
   DecodeParams p;
   p.q = static_cast<const __nv_bfloat16*>(q);
@@ -535,6 +537,7 @@ void paged_decode_launch(const void* q, long long ldq, const void* kc, const voi
   p.vc = static_cast<const __nv_bfloat16*>(vc);
   p.table = table;
   p.max_pages = max_pages;
+  p.n_pages = n_pages;
   p.lens = lens;
   p.B = B;
   p.Hq = Hq;

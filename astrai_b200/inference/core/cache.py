@@ -286,9 +286,10 @@ class Storage:
             return k, v
         B = table.shape[0]
         pos = torch.arange(total, device=table.device)
-        pidx = (pos // self.page_size).clamp(max=max(table.shape[1] - 1, 0))
+        raw = pos // self.page_size
+        pidx = raw.clamp(max=max(table.shape[1] - 1, 0))
         pages = table.long()[:, pidx] if table.shape[1] else torch.full((B, total), -1, device=table.device)
-        valid = (pages >= 0) & (pos[None, :] < lens.long()[:, None])
+        valid = (pages >= 0) & (pos[None, :] < lens.long()[:, None]) & (raw < table.shape[1])[None, :]
         p = pages.clamp(min=0)
         off = (pos % self.page_size)[None, :].expand(B, -1)
         k = self.k_cache[layer_id][p, :, off]  # [B, total, H, D]
@@ -398,9 +399,10 @@ class PageCacheView(CacheView):
         if S not in self._slots:
             pos = self.positions(S).view(self.B, S).long()
             ps = self._storage.page_size
-            pidx = (pos // ps).clamp(max=max(self.table.shape[1] - 1, 0))
+            raw = pos // ps
+            pidx = raw.clamp(min=0, max=max(self.table.shape[1] - 1, 0))
             pages = self.table.long().gather(1, pidx) if self.table.shape[1] else torch.full_like(pos, -1)
-            ok = (pages >= 0) & (pos >= 0)
+            ok = (pages >= 0) & (pos >= 0) & (raw < self.table.shape[1])  # past the table: not written
             self._slots[S] = torch.where(ok, pages * ps + pos % ps, -1).reshape(-1).to(torch.int32).contiguous()
         return self._slots[S]
 

@@ -258,3 +258,22 @@ def test_extension_native_paths_match_reference():
     table = torch.arange(12, device="cuda").view(2, 6)
     torch.testing.assert_close(attn_paged_decode(qd, table, kc, vc, 16, 96).float(),
                                reference_attention(qd, k, v).float(), atol=3e-2, rtol=3e-2)
+
+
+def test_paged_decode_ignores_keys_beyond_the_table():
+    """Lengths past the page table's capacity read no table entry past the row
+    and no page outside the cache: those keys are skipped."""
+    from astrai_b200.ops._ext import native
+
+    C = native()
+    kc, vc = _rand_cache(3, 2, 16, seed=5)
+    table = torch.tensor([[2], [0]], dtype=torch.int32, device="cuda")  # one 16-slot page per row
+    lens = torch.tensor([40, 16], dtype=torch.int32, device="cuda")     # row 0 claims 40 keys
+    q = torch.randn(2, 4 * 128, device="cuda").to(torch.bfloat16)
+    out = torch.empty_like(q)
+    ws = torch.empty(2 * 4 * 3 * 130, device="cuda", dtype=torch.float32)
+    C.paged_decode(q, kc, vc, table, lens, out, 4, 1 / math.sqrt(128), 3, ws)
+    ref = torch.empty_like(q)
+    C.paged_decode(q, kc, vc, table, torch.tensor([16, 16], dtype=torch.int32, device="cuda"), ref, 4,
+                   1 / math.sqrt(128), 3, ws)
+    torch.testing.assert_close(out.float(), ref.float(), atol=1e-2, rtol=1e-2)
