@@ -12,6 +12,8 @@
 
 namespace astrai_host {
 long long launch_count();
+void skinny_gemm(const void* X, long long ldx, const void* W, long long ldw, const void* residual, long long ldr,
+                 void* Y, long long ldy, int M, int N, int K, int sms, cudaStream_t s);
 int num_sms(int device);
 int read_and_clear_error();
 void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int N, int K, int batch, int a_mn,
@@ -70,6 +72,31 @@ void check_rows(const at::Tensor& t, const char* name) {
   TORCH_CHECK(t.stride(1) == 1, name, " must have a contiguous inner dimension");
   TORCH_CHECK((t.stride(0) * t.element_size()) % 16 == 0, name, ": row stride must be a multiple of 16 bytes");
   TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, " must be 16-byte aligned");
+}
+
+// ----------------------------------------------------------------- skinny GEMM (decode)
+// y [M, N] = x [M, K] @ w [N, K]^T (+ residual), 1 <= M <= 16.
+void skinny_gemm(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::optional<at::Tensor>& residual) {
+  check_bf16(x, "x");
+  check_bf16(w, "w");
+  check_bf16(y, "y");
+  check_rows(x, "x");
+  check_rows(w, "w");
+  TORCH_CHECK(y.dim() == 2 && y.stride(1) == 1, "y must be 2-D rows");  // scalar stores: any row stride
+  const int M = (int)x.size(0), K = (int)x.size(1), N = (int)w.size(0);
+  TORCH_CHECK(w.size(1) == K && y.size(0) == M && y.size(1) == N, "skinny_gemm: shape mismatch");
+  const void* r = nullptr;
+  long long ldr = 0;
+  if (residual.has_value() && residual->defined()) {
+    check_bf16(*residual, "residual");
+    TORCH_CHECK(residual->dim() == 2 && residual->size(0) == M && residual->size(1) == N &&
+                    residual->stride(1) == 1, "residual must be [M, N] rows");
+    r = residual->data_ptr();
+    ldr = residual->stride(0);
+  }
+  c10::cuda::CUDAGuard g(x.device());
+  astrai_host::skinny_gemm(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), r, ldr, y.data_ptr(), y.stride(0), M, N,
+                           K, astrai_host::num_sms(x.device().index()), stream());
 }
 
 // ----------------------------------------------------------------- GEMM
@@ -324,6 +351,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "astrai_b200 sm_100a kernels";
   m.def("launch_count", []() { return static_cast<int64_t>(astrai_host::launch_count()); },
         "kernel launches issued by this library so far (host counter)");
+  m.def("skinny_gemm", &skinny_gemm, py::arg("x"), py::arg("w"), py::arg("y"), py::arg("residual") = py::none());
   m.def("gemm", &gemm, "bf16 tcgen05 GEMM", py::arg("a"), py::arg("b"), py::arg("d"), py::arg("c") = py::none(),
         py::arg("a_mn") = 0, py::arg("b_mn") = 0, py::arg("alpha") = 1.0, py::arg("beta") = 0.0,
         py::arg("force_bn") = 0);

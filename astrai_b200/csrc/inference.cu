@@ -336,6 +336,79 @@ __device__ __forceinline__ float cluster_exclusive(float v, float* slot, int csi
   return r;
 }
 
+constexpr int SMP_CAND = 1024;  // survivors of top-k handled in shared memory
+
+// Sum / min over this CTA only (all CTAs of a row hold the same candidate list).
+__device__ __forceinline__ float block_sum_local(float v, float* scratch) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) scratch[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = warp_sum(scratch[lane]);
+    if (lane == 0) scratch[32] = v;
+  }
+  __syncthreads();
+  return scratch[32];
+}
+
+__device__ __forceinline__ float block_min_local(float v, float* scratch) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffff, v, o));
+  __syncthreads();
+  if (lane == 0) scratch[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = scratch[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffff, v, o));
+    if (lane == 0) scratch[32] = v;
+  }
+  __syncthreads();
+  return scratch[32];
+}
+
+// Row-wide sums of NV values at once (block, then cluster through DSMEM):
+// one synchronisation round for all of them.
+template <int NV>
+__device__ __forceinline__ void row_reduce_vec(float (&v)[NV], float* scratch /* [32 * NV + NV] */, int csize) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v[i] += __shfl_xor_sync(0xffffffff, v[i], o);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) scratch[w * NV + i] = v[i];
+  }
+  __syncthreads();
+  float* tot = scratch + 32 * NV;
+  if (threadIdx.x < NV) {
+    float acc = 0.f;
+    for (int ww = 0; ww < SMP_THREADS / 32; ++ww) acc += scratch[ww * NV + threadIdx.x];
+    tot[threadIdx.x] = acc;
+  }
+  if (csize == 1) {
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < NV; ++i) v[i] = tot[i];
+    __syncthreads();
+    return;
+  }
+  cg::cluster_group cl = cg::this_cluster();
+  cl.sync();
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    float acc = 0.f;
+    for (int c = 0; c < csize; ++c) acc += *cl.map_shared_rank(tot + i, c);
+    v[i] = acc;
+  }
+  cl.sync();
+}
+
 __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(
     const void* __restrict__ logits, int logits_f32, long long ld, int V, const float* __restrict__ temperature,
     const int* __restrict__ top_k, const float* __restrict__ top_p, const float* __restrict__ penalty,
@@ -386,47 +459,172 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(
 #pragma unroll
   for (int j = 0; j < SMP_PER; ++j) x[j] *= inv_t;
   const float mx = gmax * inv_t;  // scaling by a positive factor keeps the argmax
-  // ---- top-k: the largest key threshold `lo` with count(key >= lo) >= k
+  // ---- top-k: the largest key L with count(key >= L) >= k; keep key >= L.
+  // 8-ary search over the 32-bit key space: 7 thresholds per round, one
+  // fused row reduction each, about 11 rounds.
+  constexpr int NT = 7;
+  __shared__ float red_scratch[33 * NT];
   const int k = top_k ? top_k[row] : 0;
   if (k > 0 && k < V) {
-    uint32_t lo = 0, hi = fkey(mx);
+    unsigned long long lo = 0, hi = fkey(mx);  // invariant: count(>= lo) >= k, answer <= hi
     while (lo < hi) {
-      const uint32_t mid = lo + (hi - lo + 1) / 2;
-      float c = 0.f;
+      uint32_t th[NT];
+      float c[NT];
 #pragma unroll
-      for (int j = 0; j < SMP_PER; ++j) c += (x[j] != -INFINITY && fkey(x[j]) >= mid) ? 1.f : 0.f;
-      const float tot = row_reduce(c, RED_SUM, sh, cs);
-      if (tot >= (float)k) {
-        lo = mid;
-        if (tot == (float)k) break;  // exactly the k largest: done
-      } else {
-        hi = mid - 1;
+      for (int i = 0; i < NT; ++i) {
+        th[i] = (uint32_t)(lo + ((hi - lo) * (unsigned long long)(i + 1) + NT) / (NT + 1));
+        c[i] = 0.f;
       }
+#pragma unroll
+      for (int j = 0; j < SMP_PER; ++j) {
+        if (x[j] == -INFINITY) continue;
+        const uint32_t key = fkey(x[j]);
+#pragma unroll
+        for (int i = 0; i < NT; ++i) c[i] += key >= th[i] ? 1.f : 0.f;
+      }
+      row_reduce_vec<NT>(c, red_scratch, cs);
+      int best = -1;
+#pragma unroll
+      for (int i = 0; i < NT; ++i)
+        if (c[i] >= (float)k) best = i;  // counts fall as thresholds rise
+      if (best >= 0 && c[best] == (float)k) {  // exactly the k largest
+        lo = hi = th[best];
+        break;
+      }
+      const unsigned long long nlo = best >= 0 ? (unsigned long long)th[best] : lo;
+      const unsigned long long nhi = best + 1 < NT ? (unsigned long long)th[best + 1] - 1 : hi;
+      if (nlo == lo && nhi == hi) break;  // range too small to split further: lo is exact
+      lo = nlo;
+      hi = nhi < nlo ? nlo : nhi;
     }
 #pragma unroll
     for (int j = 0; j < SMP_PER; ++j)
-      if (x[j] != -INFINITY && fkey(x[j]) < lo) x[j] = -INFINITY;
+      if (x[j] != -INFINITY && fkey(x[j]) < (uint32_t)lo) x[j] = -INFINITY;
   }
-  // ---- top-p: keep token i iff the mass of strictly larger tokens <= top_p
+  // ---- top-p: keep token i iff the mass of strictly larger tokens <= top_p.
   const float pp = top_p ? top_p[row] : 1.f;
-  if (pp < 1.f) {
-    float s = 0.f;
+  bool topp_done = false;
+  if (pp < 1.f && k > 0 && k <= SMP_CAND) {
+    // after top-k at most k values (plus ties) survive: gather them (cluster-wide,
+    // rank order, so every CTA holds the same list) and decide on the list
+    __shared__ float cand_local[SMP_CAND], cand[SMP_CAND];
+    __shared__ int sh_cnt[SMP_THREADS / 32 + 1];
+    __shared__ int sh_n;
+    __shared__ float sh_thr;
+    int mine = 0;
 #pragma unroll
-    for (int j = 0; j < SMP_PER; ++j) s += (x[j] == -INFINITY) ? 0.f : __expf(x[j] - mx);
-    const float Z = row_reduce(s, RED_SUM, sh, cs);
-    // smallest key `lo` whose strictly-greater mass is <= pp * Z (the max is always kept)
-    uint32_t lo = 0, hi = fkey(mx);
+    for (int j = 0; j < SMP_PER; ++j) mine += x[j] != -INFINITY;
+    const int lane = t & 31, w = t >> 5;
+    int incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffff, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) sh_cnt[w] = incl;
+    __syncthreads();
+    if (w == 0) {
+      int v = sh_cnt[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffff, v, o);
+        if (lane >= o) v += y;
+      }
+      sh_cnt[lane] = v;  // inclusive warp totals
+    }
+    __syncthreads();
+    const int cta_n = sh_cnt[SMP_THREADS / 32 - 1];
+    int off = incl - mine + (w > 0 ? sh_cnt[w - 1] : 0);
+#pragma unroll
+    for (int j = 0; j < SMP_PER; ++j)
+      if (x[j] != -INFINITY && off < SMP_CAND) cand_local[off++] = x[j];
+    if (t == 0) sh_n = cta_n;
+    int n = 0;
+    if (cs > 1) {
+      cg::cluster_group cl = cg::this_cluster();
+      cl.sync();
+      for (int c = 0; c < cs; ++c) {
+        const int nc = *cl.map_shared_rank(&sh_n, c);
+        const float* src = cl.map_shared_rank(cand_local, c);
+        for (int i = t; i < nc && n + i < SMP_CAND; i += SMP_THREADS) cand[n + i] = src[i];
+        n += nc;
+      }
+      cl.sync();
+    } else {
+      __syncthreads();
+      n = cta_n;
+      for (int i = t; i < n && i < SMP_CAND; i += SMP_THREADS) cand[i] = cand_local[i];
+    }
+    if (n <= SMP_CAND) {  // (more survivors than fit only with massive ties: use the search below)
+      __syncthreads();
+      float e1[1] = {0.f};
+      if (t < n) e1[0] = __expf(cand[t] - mx);
+      const float ct = t < n ? cand[t] : 0.f;
+      float zsum = e1[0];
+      zsum = block_sum_local(zsum, red_scratch);
+      float greater = 0.f;
+      if (t < n)
+        for (int j = 0; j < n; ++j)
+          if (cand[j] > ct) greater += __expf(cand[j] - mx);
+      const bool keep = t < n && greater <= pp * zsum;
+      float kept_min = keep ? ct : INFINITY;
+      kept_min = block_min_local(kept_min, red_scratch);
+      if (t == 0) sh_thr = kept_min;
+      __syncthreads();
+      const float thr = sh_thr;
+#pragma unroll
+      for (int j = 0; j < SMP_PER; ++j)
+        if (x[j] < thr) x[j] = -INFINITY;
+      topp_done = true;
+    }
+  }
+  if (pp < 1.f && !topp_done) {
+    // the smallest key L with mass(key > L) <= top_p * Z (8-ary search as above)
+    float s1[1] = {0.f};
+#pragma unroll
+    for (int j = 0; j < SMP_PER; ++j) s1[0] += (x[j] == -INFINITY) ? 0.f : __expf(x[j] - mx);
+    row_reduce_vec<1>(s1, red_scratch, cs);
+    const float target = pp * s1[0];
+    unsigned long long lo = 0, hi = fkey(mx);  // invariant: mass(> hi) <= target; answer >= lo
     while (lo < hi) {
-      const uint32_t mid = lo + (hi - lo) / 2;
-      float c = 0.f;
+      uint32_t th[NT];
+      float m[NT];
 #pragma unroll
-      for (int j = 0; j < SMP_PER; ++j) c += (x[j] != -INFINITY && fkey(x[j]) > mid) ? __expf(x[j] - mx) : 0.f;
-      const float above = row_reduce(c, RED_SUM, sh, cs);
-      if (above <= pp * Z) hi = mid; else lo = mid + 1;
+      for (int i = 0; i < NT; ++i) {
+        th[i] = (uint32_t)(lo + ((hi - lo) * (unsigned long long)(i + 1)) / (NT + 1));
+        m[i] = 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < SMP_PER; ++j) {
+        if (x[j] == -INFINITY) continue;
+        const uint32_t key = fkey(x[j]);
+        const float e = __expf(x[j] - mx);
+#pragma unroll
+        for (int i = 0; i < NT; ++i) m[i] += key > th[i] ? e : 0.f;
+      }
+      row_reduce_vec<NT>(m, red_scratch, cs);
+      int first = NT;
+#pragma unroll
+      for (int i = NT - 1; i >= 0; --i)
+        if (m[i] <= target) first = i;  // masses fall as thresholds rise
+      const unsigned long long nhi = first < NT ? (unsigned long long)th[first] : hi;
+      const unsigned long long nlo = first > 0 ? (unsigned long long)th[first - 1] + 1 : lo;
+      if (nlo == lo && nhi == hi) {  // thresholds collapsed onto the range: finish bisecting
+        const unsigned long long mid = lo + (hi - lo) / 2;
+        float mm[1] = {0.f};
+#pragma unroll
+        for (int j = 0; j < SMP_PER; ++j)
+          if (x[j] != -INFINITY && (unsigned long long)fkey(x[j]) > mid) mm[0] += __expf(x[j] - mx);
+        row_reduce_vec<1>(mm, red_scratch, cs);
+        if (mm[0] <= target) hi = mid; else lo = mid + 1;
+        continue;
+      }
+      lo = nlo;
+      hi = nhi < nlo ? nlo : nhi;
     }
 #pragma unroll
     for (int j = 0; j < SMP_PER; ++j)
-      if (x[j] != -INFINITY && fkey(x[j]) < lo) x[j] = -INFINITY;
+      if (x[j] != -INFINITY && fkey(x[j]) < (uint32_t)lo) x[j] = -INFINITY;
   }
   // ---- frequency penalty: subtract penalty * count(token in the history window)
   const float pen = penalty ? penalty[row] : 0.f;

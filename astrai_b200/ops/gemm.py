@@ -54,6 +54,24 @@ def _as_rows(t: torch.Tensor) -> torch.Tensor:
     return t2
 
 
+SKINNY_MAX_ROWS = 16
+
+
+def _skinny(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+    """Decode-shaped products (<= 16 rows, no autograd): the skinny kernel that
+    streams the weight once over the whole GPU. None when not applicable."""
+    if torch.is_grad_enabled():
+        return None
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.shape[0] > SKINNY_MAX_ROWS or x2.shape[0] == 0:
+        return None
+    x2 = _as_rows(x2)
+    out = torch.empty((x2.shape[0], w.shape[0]), device=x.device, dtype=torch.bfloat16)
+    r2 = _as_rows(residual) if residual is not None else None
+    native().skinny_gemm(x2, w, out, r2)
+    return out.view(*x.shape[:-1], w.shape[0])
+
+
 class _LinearFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, residual):
@@ -199,6 +217,9 @@ def packed_linear(x: torch.Tensor, params, residual: Optional[torch.Tensor] = No
         w = params[0] if len(params) == 1 else torch.cat(list(params), 0)
         return linear(x, w, residual=residual)
     w = pack_params(params) if len(params) > 1 else params[0]
+    y = _skinny(x, w.detach(), residual)
+    if y is not None:
+        return y
     return _PackedLinearFn.apply(x, w.detach(), residual, *params)
 
 
@@ -212,4 +233,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = 
             raise ValueError(f"linear: dims {tuple(x.shape)} x {tuple(w.shape)} need 16-byte aligned rows")
         y = F.linear(x, w, bias)
         return y + residual if residual is not None else y
+    y = _skinny(x, w, residual)
+    if y is not None:
+        return y
     return _LinearFn.apply(x, w, residual)

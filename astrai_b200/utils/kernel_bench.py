@@ -121,12 +121,53 @@ def bench_allreduce():
     dist.destroy_process_group()
 
 
+def bench_skinny():
+    """Decode GEMMs (M token rows x weight [N, K]): device time and weight-read bandwidth."""
+    from astrai_b200.ops._ext import native
+
+    hbm, tf, src = peaks()
+    C = native()
+    for M in (1, 4, 16):
+        for name, N, K in (("qkv", 3072, 2048), ("o", 2048, 2048), ("upgate", 11264, 2048), ("down", 2048, 5632),
+                           ("lm_head", 32000, 2048)):
+            x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+            # weights > L2 in total: rotate through 8 copies so every call streams from HBM
+            ws = [torch.randn(N, K, device="cuda", dtype=torch.bfloat16) for _ in range(8)]
+            y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+            it = [0]
+
+            def run():
+                C.skinny_gemm(x, ws[it[0] % 8], y, None)
+                it[0] += 1
+            ms = time_fn(run, warmup=8, iters=40)
+            gbs = N * K * 2 / (ms / 1e3) / 1e9
+            print(json.dumps({"kernel": "skinny_gemm", "case": name, "M": M, "N": N, "K": K, "us": round(ms * 1e3, 2),
+                              "weight_gbs": round(gbs, 1), "frac_of_hbm": round(gbs / hbm, 3), "peak_src": src}))
+
+
+def bench_sample():
+    """Fused sampler on [rows, 32000] logits: greedy, top-k, top-p, both."""
+    from astrai_b200.inference.sample import sample
+
+    for rows in (1, 4, 32):
+        x = torch.randn(rows, 32000, device="cuda") * 3
+        for name, kw in (("greedy", dict(temperature=0.0)), ("topk50", dict(temperature=0.8, top_k=50)),
+                         ("topp0.95", dict(temperature=0.8, top_p=0.95)),
+                         ("topk50_topp0.95", dict(temperature=0.8, top_k=50, top_p=0.95))):
+            ms = time_fn(lambda: sample(x, **kw), warmup=5, iters=20)
+            print(json.dumps({"kernel": "sample", "rows": rows, "case": name, "us": round(ms * 1e3, 2)}))
+
+
 def main(argv=None):
     which = (argv or sys.argv[1:] or ["all"])[0]
     torch.manual_seed(0)
     if which == "allreduce":
         bench_allreduce()
         return
+    if which in ("skinny", "all"):
+        bench_skinny()
+    if which in ("sample", "all"):
+        bench_sample()
     if which in ("gemm", "all"):
         bench_gemm()
     if which in ("attn", "all"):

@@ -246,3 +246,18 @@ def test_attention_qkv_fused_rope():
     o2.backward(g.cpu().float())
     assert rel_err(o.cpu(), o2) < 2e-2
     assert rel_err(x1.grad.cpu(), x2.grad) < 3e-2
+
+
+@pytest.mark.parametrize("M", [1, 3, 4, 8, 16])
+@pytest.mark.parametrize("N,K", [(2048, 2048), (11264, 2048), (2048, 5632), (32000, 2048), (130, 264)])
+def test_skinny_gemm(M, N, K):
+    from astrai_b200.ops._ext import native
+
+    torch.manual_seed(M)
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda") * 0.05).to(torch.bfloat16)
+    r = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
+    y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    native().skinny_gemm(x, w, y, r)
+    ref = x.float() @ w.float().t() + r.float()
+    assert rel_err(y, ref) < 1e-2
