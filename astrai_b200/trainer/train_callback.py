@@ -24,6 +24,7 @@ import json
 import os
 import sys
 import time
+from contextlib import contextmanager
 from pathlib import Path
 from typing import IO, Callable, List, Optional, Protocol, runtime_checkable
 
@@ -33,7 +34,7 @@ import torch.nn as nn
 from torch.utils.checkpoint import checkpoint as torch_checkpoint
 
 from astrai_b200.factory import Registry
-from astrai_b200.parallel.setup import get_current_device, only_on_rank
+from astrai_b200.parallel.setup import get_current_device, get_rank, only_on_rank
 from astrai_b200.serialization import Checkpoint
 
 
@@ -260,3 +261,53 @@ class GradientClippingCallback:
     def on_optimizer_step(self, context):
         # always computed: the norm is logged; clipping only if a max is set
         context.grad_norm_tensor = context.executor.clip_grad_norm(context.model, self.max_grad_norm, as_tensor=True)
+
+
+@contextmanager
+def nvtx_range(name: str):
+    """NVTX range on CUDA (visible in Nsight / torch.profiler traces); no-op on CPU."""
+    if torch.cuda.is_available():
+        torch.cuda.nvtx.range_push(name)
+        try:
+            yield
+        finally:
+            torch.cuda.nvtx.range_pop()
+    else:
+        yield
+
+
+@CallbackFactory.register("profiler")
+class ProfilerCallback:
+    """torch.profiler over a window of optimizer steps (skip ``wait``, warm ``warmup``,
+    record ``active``); rank 0 writes a Chrome trace + a kernel table to ``profile_dir``."""
+
+    def __init__(self, profile_dir: str, wait: int = 2, warmup: int = 1, active: int = 2):
+        self.profile_dir, self.wait, self.warmup, self.active = profile_dir, wait, warmup, active
+        self._prof = None
+
+    def on_train_begin(self, context) -> None:
+        from torch.profiler import ProfilerActivity, profile, schedule
+
+        if get_rank() != 0:
+            return
+        os.makedirs(self.profile_dir, exist_ok=True)
+        acts = [ProfilerActivity.CPU] + ([ProfilerActivity.CUDA] if torch.cuda.is_available() else [])
+
+        def done(p):
+            p.export_chrome_trace(os.path.join(self.profile_dir, f"trace_step{p.step_num}.json"))
+            sort = "cuda_time_total" if torch.cuda.is_available() else "cpu_time_total"
+            with open(os.path.join(self.profile_dir, "kernels.txt"), "w") as fh:
+                fh.write(p.key_averages().table(sort_by=sort, row_limit=40))
+
+        self._prof = profile(activities=acts, schedule=schedule(wait=self.wait, warmup=self.warmup,
+                                                                active=self.active, repeat=1), on_trace_ready=done)
+        self._prof.__enter__()
+
+    def on_optimizer_step(self, context) -> None:
+        if self._prof is not None:
+            self._prof.step()
+
+    def on_train_end(self, context) -> None:
+        if self._prof is not None:
+            self._prof.__exit__(None, None, None)
+            self._prof = None

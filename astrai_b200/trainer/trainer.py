@@ -18,7 +18,7 @@ from typing import List, Optional
 
 from astrai_b200.config.train_config import TrainConfig
 from astrai_b200.parallel.setup import spawn_parallel_fn
-from astrai_b200.trainer.train_callback import CallbackFactory, TrainCallback
+from astrai_b200.trainer.train_callback import CallbackFactory, TrainCallback, nvtx_range
 from astrai_b200.trainer.train_context import TrainContext, TrainContextBuilder
 
 logger = logging.getLogger(__name__)
@@ -32,7 +32,7 @@ class Trainer:
 
     def _default_callbacks(self) -> List[TrainCallback]:
         c = self.train_config
-        return [
+        cbs = [
             CallbackFactory.create("gradient_checkpointing", modules=c.gradient_checkpointing_modules),
             CallbackFactory.create("checkpoint", c.ckpt_dir, c.ckpt_interval),
             CallbackFactory.create("metric", log_dir=c.log_dir, save_interval=c.ckpt_interval, metrics=c.metrics,
@@ -40,6 +40,9 @@ class Trainer:
             CallbackFactory.create("progress_bar", c.n_epoch),
             CallbackFactory.create("gradient_clipping", c.max_grad_norm),
         ]
+        if c.profile_dir:
+            cbs.append(CallbackFactory.create("profiler", profile_dir=c.profile_dir))
+        return cbs
 
     def _call(self, name: str, ctx: TrainContext) -> None:
         for cb in self.callbacks:
@@ -61,14 +64,17 @@ class Trainer:
                 for batch in ctx.dataloader:
                     with ex.accumulate(ctx.model):
                         self._call("on_batch_begin", ctx)
-                        loss = ctx.strategy(batch)
+                        with nvtx_range("forward"):
+                            loss = ctx.strategy(batch)
                         ctx.loss = loss.detach()
-                        ex.backward(loss / ex.grad_accum_steps)
+                        with nvtx_range("backward"):
+                            ex.backward(loss / ex.grad_accum_steps)
                         ctx.consumed_samples += per_micro
                         self._call("on_batch_end", ctx)
                         if ex.sync_gradients:
                             self._call("on_optimizer_step", ctx)
-                            ctx.optimizer.step()
+                            with nvtx_range("optimizer"):
+                                ctx.optimizer.step()
                             ctx.strategy.on_optimizer_step()
                             ctx.optimizer.zero_grad()
                             if ctx.scheduler:

@@ -235,3 +235,17 @@ def test_cli_train_flags_and_config(tmpdir_path, model_dir):
     cfg = build_config(args)
     assert cfg.executor_kwargs == {"comm_backend": "fused", "expert_parallel": False}
     assert cfg.strategy == "seq" and len(cfg.dataset) > 0
+
+
+def test_profiler_callback_writes_trace(tmp_path):
+    from astrai_b200.trainer.train_callback import CallbackFactory, nvtx_range
+
+    cb = CallbackFactory.create("profiler", profile_dir=str(tmp_path), wait=0, warmup=1, active=1)
+    cb.on_train_begin(None)
+    for _ in range(3):
+        with nvtx_range("forward"):
+            torch.randn(32, 32) @ torch.randn(32, 32)
+        cb.on_optimizer_step(None)
+    cb.on_train_end(None)
+    names = os.listdir(tmp_path)
+    assert "kernels.txt" in names and any(n.startswith("trace_step") for n in names)
