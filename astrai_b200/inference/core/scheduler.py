@@ -45,6 +45,7 @@ class InferenceScheduler:
             if max_seq_len is None:
                 raise ValueError("max_seq_len must be given or set as config.max_position_embeddings")
         self.max_seq_len = int(max_seq_len)
+        self.max_batch_size = int(max_batch_size)
         p = next(model.parameters())
         self.model = model
         self.device = torch.device(device) if device is not None else p.device

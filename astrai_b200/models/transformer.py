@@ -94,11 +94,17 @@ class AutoRegressiveLM(AutoModel):
 
     def forward(self, input_ids: torch.Tensor, input_mask: Optional[torch.Tensor] = None, paged_cache=None,
                 position_ids: Optional[torch.Tensor] = None, seg_ids: Optional[torch.Tensor] = None,
-                logits_to_keep: Optional[int] = None) -> Dict[str, torch.Tensor]:
+                logits_to_keep=None) -> Dict[str, torch.Tensor]:
+        """``logits_to_keep``: None (all positions), an int n (the last n positions), or a bool
+        ``[B, S]`` tensor selecting positions, in which case ``logits`` is ``[N, V]`` in row-major
+        order of the selected positions (scoring packed documents without full-vocab logits)."""
         assert input_ids.ndim == 2
         ctx = self.make_context(input_ids, input_mask, paged_cache, position_ids, seg_ids)
         hidden = self.backbone(input_ids, ctx)
-        h = hidden if logits_to_keep is None else hidden[:, -logits_to_keep:]
+        if isinstance(logits_to_keep, torch.Tensor):
+            h = hidden[logits_to_keep]  # bool [B, S]: logits [N, V] for the selected positions only
+        else:
+            h = hidden if logits_to_keep is None else hidden[:, -logits_to_keep:]
         out = {"logits": self.lm_head(h), "hidden_states": hidden}
         if ctx.aux_losses:
             out["aux_loss"] = torch.stack(ctx.aux_losses).sum()

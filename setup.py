@@ -10,7 +10,7 @@ import os
 
 os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0a")
 
-from setuptools import setup  # noqa: E402
+from setuptools import find_packages, setup  # noqa: E402
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -27,10 +27,9 @@ NVCC_FLAGS = [
     "-DNDEBUG",
 ]
 
+# name, version and dependencies live in pyproject.toml
 setup(
-    name="astrai_b200",
-    version="0.1.0",
-    packages=[],
+    packages=find_packages(include=["astrai_b200*"]),
     ext_modules=[
         CUDAExtension(
             name="astrai_b200._C",
