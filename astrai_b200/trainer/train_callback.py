@@ -191,8 +191,30 @@ class MetricCallback:
             "lr": lambda c: c.optimizer.param_groups[-1]["lr"] if c.optimizer is not None else None,
             "grad_norm": lambda c: c.grad_norm,
             "val_loss": lambda c: c.val_loss,
-            "tokens_per_s": lambda c: c.kwargs.get("tokens_per_s"),
+            "tokens_per_s": lambda c: self._rate(c)[0],
+            "mfu": lambda c: self._rate(c)[1],
         }
+        self._t_last = None
+        self._tok_last = 0
+        self._rate_cache = (None, None, -1)
+
+    # B200 dense bf16 tensor peak per GPU (nominal), the denominator of the logged MFU
+    PEAK_FLOPS = 2.25e15
+
+    def _rate(self, c):
+        """(whole-job tokens/s since the previous optimizer step, model FLOPs utilisation per GPU)."""
+        if self._rate_cache[2] == c.optimizer_step:
+            return self._rate_cache[:2]
+        now, tok = time.perf_counter(), c.kwargs.get("tokens", 0)
+        tps = mfu = None
+        if self._t_last is not None and now > self._t_last and tok > self._tok_last:
+            tps = (tok - self._tok_last) / (now - self._t_last)
+            model = getattr(c.model, "module", c.model)
+            n_params = sum(p.numel() for p in model.parameters())
+            mfu = 6.0 * n_params * tps / max(1, c.world_size) / self.PEAK_FLOPS
+        self._t_last, self._tok_last = now, tok
+        self._rate_cache = (tps, mfu, c.optimizer_step)
+        return tps, mfu
 
     def _append(self, kind, context, **extra):
         if context.rank != 0:
@@ -216,6 +238,7 @@ class MetricCallback:
 
     def on_train_begin(self, context):
         self.last_flush = context.optimizer_step
+        self._t_last, self._tok_last = time.perf_counter(), context.kwargs.get("tokens", 0)
 
     @only_on_rank(0)
     def _flush(self, epoch, step):
@@ -311,3 +334,40 @@ class ProfilerCallback:
         if self._prof is not None:
             self._prof.__exit__(None, None, None)
             self._prof = None
+
+
+@CallbackFactory.register("health")
+class HealthCallback:
+    """Peer failure detection for multi-rank training (no-op on one rank).
+
+    Starts a store heartbeat when training begins, checks the peers before each
+    batch (at most once per ``check_every`` seconds, a few store reads), records
+    this rank's failure from ``on_error`` so the other ranks raise
+    :class:`astrai_b200.parallel.health.PeerFailure` with the cause before their
+    next collective instead of waiting for the process-group timeout."""
+
+    def __init__(self, interval: float = 1.0, timeout: float = 30.0, check_every: float = 2.0):
+        self.interval, self.timeout, self.check_every = interval, timeout, check_every
+        self.hb = None
+        self._last = 0.0
+
+    def on_train_begin(self, context) -> None:
+        if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+            from astrai_b200.parallel.health import Heartbeat
+
+            self.hb = Heartbeat(interval=self.interval, timeout=self.timeout).start()
+
+    def on_batch_begin(self, context) -> None:
+        if self.hb is not None and time.monotonic() - self._last >= self.check_every:
+            self._last = time.monotonic()
+            self.hb.check()
+
+    def on_error(self, context) -> None:
+        if self.hb is not None:
+            err = sys.exc_info()[1]
+            self.hb.mark_failed(repr(err) if err is not None else "error")
+
+    def on_train_end(self, context) -> None:
+        if self.hb is not None:
+            self.hb.stop()
+            self.hb = None

@@ -24,6 +24,14 @@ from astrai_b200.trainer.train_context import TrainContext, TrainContextBuilder
 logger = logging.getLogger(__name__)
 
 
+def _batch_tokens(batch) -> int:
+    """Token positions processed by one micro-batch on this rank (the largest id tensor of the batch dict)."""
+    if not isinstance(batch, dict):
+        return 0
+    n = [v.numel() for v in batch.values() if hasattr(v, "dtype") and not v.is_floating_point() and v.dim() >= 2]
+    return max(n, default=0)
+
+
 class Trainer:
     def __init__(self, train_config: TrainConfig, callbacks: Optional[List[TrainCallback]] = None):
         self.train_config = train_config
@@ -42,6 +50,8 @@ class Trainer:
         ]
         if c.profile_dir:
             cbs.append(CallbackFactory.create("profiler", profile_dir=c.profile_dir))
+        if c.nprocs > 1:
+            cbs.append(CallbackFactory.create("health"))
         return cbs
 
     def _call(self, name: str, ctx: TrainContext) -> None:
@@ -70,6 +80,7 @@ class Trainer:
                         with nvtx_range("backward"):
                             ex.backward(loss / ex.grad_accum_steps)
                         ctx.consumed_samples += per_micro
+                        ctx.kwargs["tokens"] = ctx.kwargs.get("tokens", 0) + _batch_tokens(batch) * ctx.world_size
                         self._call("on_batch_end", ctx)
                         if ex.sync_gradients:
                             self._call("on_optimizer_step", ctx)

@@ -55,7 +55,7 @@ def make_cfg(ds, d, **kw):
 def test_trainer_steps_checkpoints_metrics(tmpdir_path):
     from astrai_b200.trainer import Trainer
 
-    t = Trainer(make_cfg(RandSeq(16), tmpdir_path))
+    t = Trainer(make_cfg(RandSeq(16), tmpdir_path, metrics=["loss", "grad_norm", "tokens_per_s", "mfu"]))
     t.train()
     ctx = t.last_context
     assert ctx.optimizer_step == 4 and ctx.consumed_samples == 16
@@ -66,6 +66,8 @@ def test_trainer_steps_checkpoints_metrics(tmpdir_path):
     logs = os.listdir(os.path.join(tmpdir_path, "logs"))
     rows = [json.loads(x) for x in open(os.path.join(tmpdir_path, "logs", sorted(logs)[-1]))]
     assert any(r["type"] == "step" and "grad_norm" in r for r in rows)
+    assert all(r["tokens_per_s"] > 0 and 0 < r["mfu"] < 1 for r in rows if r["type"] == "step")
+    assert ctx.kwargs["tokens"] == 16 * (RandSeq(1).x.shape[1] - 1)
 
 
 def test_failure_checkpoint_and_resume(tmpdir_path):
