@@ -8,7 +8,9 @@ steps and warmup from the dataset length; scheduler kwargs per schedule
 type; DecoderBlock checkpointing with --gradient_checkpointing). Added
 flags: ``--comm_backend fused`` (NVLink peer-memory gradient all-reduce for
 ddp), ``--expert_parallel`` (shard MoE experts over the ranks),
-``--profile_dir``.
+``--profile_dir``, ``--shard_muon`` (owner-sharded Muon: each rank runs
+Newton-Schulz on 1/world of the matrices and writes the updated weights into
+every replica over NVLink).
 """
 
 from __future__ import annotations
@@ -81,6 +83,8 @@ def parse_args(argv: Optional[List[str]] = None) -> argparse.Namespace:
     a("--comm_backend", type=str, default="nccl", choices=["nccl", "fused"],
       help="ddp gradient exchange: NCCL, or the NVLink peer-memory all-reduce fused with the grad norm.")
     a("--expert_parallel", action="store_true", help="Split MoE experts over the ranks (ddp).")
+    a("--shard_muon", action="store_true",
+      help="ddp: each rank orthogonalises 1/world of the Muon matrices and writes the update into every replica.")
     a("--profile_dir", type=str, default=None)
     return p.parse_args(argv)
 
@@ -140,7 +144,7 @@ def build_config(args: argparse.Namespace):
         strategy=args.train_type, dataset=dataset,
         optimizer_fn=partial(MuonMix, lr=args.max_lr, weight_decay=args.weight_decay, momentum=args.muon_momentum,
                              nesterov=args.muon_nesterov, ns_steps=args.muon_ns_steps,
-                             adjust_lr_fn=args.muon_adjust_lr),
+                             adjust_lr_fn=args.muon_adjust_lr, shard_muon=args.shard_muon),
         scheduler_fn=lambda o: SchedulerFactory.create(args.schedule_type, o, **skw),
         ckpt_dir=args.ckpt_dir, n_epoch=args.n_epoch, batch_per_device=args.batch_per_device,
         start_epoch=args.start_epoch, start_samples=args.start_samples, ckpt_interval=args.ckpt_interval,

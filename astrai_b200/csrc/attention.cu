@@ -91,6 +91,26 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// 2^x for x <= 0 on the FMA pipe instead of the MUFU unit, so both pipes share
+// the softmax's exponentials. Split x = n + f with n = floor(x) (a round-down
+// add of 1.5 * 2^23 leaves n in the low mantissa bits), approximate 2^f on
+// [0, 1) by 1 + c1 f + c2 f^2 + c3 f^3 (coefficients from a relative-error
+// least-squares fit with Lawson reweighting, max relative error 8.6e-5, well
+// under bf16 resolution), and put n into the exponent field (exponent-field
+// construction as in Schraudolph, 1999). x < -127 gives 0.
+__device__ __forceinline__ float exp2_fma(float x) {
+  const float xc = fmaxf(x, -127.f);
+  const float t = __fadd_rd(xc, 12582912.f);
+  const float n = t - 12582912.f;
+  const float f = xc - n;
+  const float p = fmaf(fmaf(fmaf(0.07706134f, f, 0.22765121f), f, 0.69511539f), f, 1.f);
+  const int ni = __float_as_int(t) - 0x4B400000;
+  const float y = __int_as_float(__float_as_int(p) + (ni << 23));
+  return x < -127.f ? 0.f : y;
+}
+// of every 16 exponential pairs in the forward softmax, this many go to exp2_fma
+constexpr int FA_EMU_PAIRS = 7;
+
 __global__ void __launch_bounds__(192, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, FlashFwdParams p) {
@@ -113,8 +133,12 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = warp_id(), lane = lane_id();
   const int n_mblocks = (p.Sq + FA_BM - 1) / FA_BM;
-  const int mb = n_mblocks - 1 - blockIdx.x;  // heavy (late) causal blocks first
-  const int h = blockIdx.y, b = blockIdx.z;
+  // 1-D grid in longest-first order: CTAs start in index order, so every causal
+  // query block of the last position (the most key blocks) of all heads and
+  // batches is issued before any lighter one and the light blocks fill the tail
+  const int hb = p.Hq * p.B;
+  const int mb = n_mblocks - 1 - (int)(blockIdx.x / hb);
+  const int h = (int)(blockIdx.x % hb) % p.Hq, b = (int)(blockIdx.x % hb) / p.Hq;
   const int hk = h / (p.Hq / p.Hkv);
   const int m0 = mb * FA_BM;
   const int off = p.Sk - p.Sq;  // causal offset (queries are the last Sq positions)
@@ -306,8 +330,11 @@ __global__ void __launch_bounds__(192, 1)
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float e0 = ex2(fmaf(__uint_as_float(v[c * 32 + 2 * i]), sl2, -msafe));
-          const float e1 = ex2(fmaf(__uint_as_float(v[c * 32 + 2 * i + 1]), sl2, -msafe));
+          const float x0 = fmaf(__uint_as_float(v[c * 32 + 2 * i]), sl2, -msafe);
+          const float x1 = fmaf(__uint_as_float(v[c * 32 + 2 * i + 1]), sl2, -msafe);
+          const bool emu = i < FA_EMU_PAIRS;  // compile-time after unrolling
+          const float e0 = emu ? exp2_fma(x0) : ex2(x0);
+          const float e1 = emu ? exp2_fma(x1) : ex2(x1);
           l0 += e0;
           l1 += e1;
           pk[i] = pack_bf16(e0, e1);
@@ -408,18 +435,26 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
   float* sDelta = sLse + 128;                                  // [2][64]
   float* sdQ = sDelta + 128;                                   // [64][128] fp32 staging
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sdQ) + FB_DQ_BYTES);
+  // TMEM: two score buffers of 128 columns (S^T in the first 64, dP^T in the
+  // next 64), dV at 256, dK at 384. Iteration `it` uses buffer it & 1; its dQ^T
+  // (64 columns) is written over its own S^T once the softmax has read it, and
+  // the buffer is free again when the dQ warps have drained dQ^T. So the S/dP
+  // MMAs of the next query tile run while this tile's softmax works.
   uint64_t* kv_full = bars;          // K, V loaded
   uint64_t* qd_full = bars + 1;      // [2] Q/dO slot loaded (+ stats written)
   uint64_t* qd_empty = bars + 3;     // [2] dV/dK MMAs done with the slot
-  uint64_t* sd_full = bars + 5;      // S^T and dP^T in TMEM
-  uint64_t* ps_ready = bars + 6;     // P^T/dS^T in smem, S/dP TMEM free (4 warps)
-  uint64_t* dq_full = bars + 7;      // [2] dQ^T in TMEM; all MMAs of the iteration done
-  uint64_t* dq_free = bars + 9;      // dQ^T read out (4 warps)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* sd_full = bars + 5;      // [2] S^T and dP^T of buffer i in TMEM
+  uint64_t* ps_ready = bars + 7;     // [2] P^T/dS^T in smem slot i, buffer i read (4 warps)
+  uint64_t* dq_full = bars + 9;      // [2] dQ^T in buffer i; all MMAs of the iteration done
+  uint64_t* dq_free = bars + 11;     // [2] dQ^T of buffer i read out (4 warps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
 
   const int warp = warp_id(), lane = lane_id();
-  const int nb = blockIdx.x;
-  const int hk = blockIdx.y, b = blockIdx.z;
+  // 1-D grid in longest-first order: with a causal mask key block 0 sees every
+  // query tile, the last one the fewest, so block nb = rank of the work size
+  const int hb = p.Hkv * p.B;
+  const int nb = (int)(blockIdx.x / hb);
+  const int hk = (int)(blockIdx.x % hb) % p.Hkv, b = (int)(blockIdx.x % hb) / p.Hkv;
   const int G = p.Hq / p.Hkv;
   const int n0 = nb * FA_BN;
   const int off = p.Sk - p.Sq;
@@ -435,10 +470,10 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
       mbar_init(&qd_full[i], 1);
       mbar_init(&qd_empty[i], 1);
       mbar_init(&dq_full[i], 1);
+      mbar_init(&sd_full[i], 1);
+      mbar_init(&ps_ready[i], 4);
+      mbar_init(&dq_free[i], 4);
     }
-    mbar_init(sd_full, 1);
-    mbar_init(ps_ready, 4);
-    mbar_init(dq_free, 4);
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
@@ -446,7 +481,8 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tdP = tmem + 64, tdQ = tmem + 128, tdV = tmem + 256, tdK = tmem + 384;
+  const uint32_t tdV = tmem + 256, tdK = tmem + 384;
+  // buffer i: S^T at tmem + 128 i (also dQ^T), dP^T at tmem + 128 i + 64
 
   if (warp == 0) {
     // ---------------------------------------------------------- loads
@@ -499,24 +535,24 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
                     (it | k) != 0);
         }
         umma_commit(&qd_empty[slot]);
-        // dQ^T = K^T dS^T  (M = d, N = 64 queries, K = 128 keys); TMEM dQ^T must be drained
-        if (it >= 1 && !mbar_wait(dq_free, (it - 1) & 1, p.err, kErrWaitAccEmpty)) return false;
-        tc_fence_after();
+        // dQ^T = K^T dS^T  (M = d, N = 64 queries, K = 128 keys) over this iteration's S^T,
+        // which the softmax has read (ps_ready waited by the caller)
 #pragma unroll
         for (int k = 0; k < FA_BN / 16; ++k)
-          umma_bf16(tdQ, sdesc_sw128(k_base + k * 2048, FA_TILE, 1024), sdesc_sw128(ds_base + k * 2048, 2 * FA_TILE, 1024),
-                    idDQ, k > 0);
+          umma_bf16(tmem + slot * 128, sdesc_sw128(k_base + k * 2048, FA_TILE, 1024),
+                    sdesc_sw128(ds_base + k * 2048, 2 * FA_TILE, 1024), idDQ, k > 0);
         umma_commit(&dq_full[slot]);
         return true;
       };
       for (int it = 0; it < iters && ok; ++it) {
         const int slot = it & 1;
         ok = mbar_wait(&qd_full[slot], (it >> 1) & 1, p.err, kErrWaitFull);
-        // S^T / dP^T TMEM is free once the softmax of it-1 arrived on ps_ready
-        if (ok && it >= 1) ok = mbar_wait(ps_ready, (it - 1) & 1, p.err, kErrWaitAccEmpty);
+        // buffer `slot` is free once the dQ^T of it-2 (written over its S^T) was drained
+        if (ok && it >= 2) ok = mbar_wait(&dq_free[slot], ((it - 2) >> 1) & 1, p.err, kErrWaitAccEmpty);
         if (!ok) break;
         tc_fence_after();
         const uint32_t q_base = smem_u32(sQ + slot * 2 * FB_QT), do_base = smem_u32(sdO + slot * 2 * FB_QT);
+        const uint32_t tS = tmem + slot * 128, tdP = tS + 64;
         // S^T = K Q^T ; dP^T = V dO^T   (M = 128 keys, N = 64 queries, K = d)
 #pragma unroll
         for (int k = 0; k < FA_D / 16; ++k) {
@@ -525,10 +561,17 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
           umma_bf16(tS, sdesc_sw128(k_base + o, 16, 1024), sdesc_sw128(q_base + oq, 16, 1024), idSP, k > 0);
           umma_bf16(tdP, sdesc_sw128(v_base + o, 16, 1024), sdesc_sw128(do_base + oq, 16, 1024), idSP, k > 0);
         }
-        umma_commit(sd_full);
-        if (it >= 1) ok = issue_grads(it - 1);
+        umma_commit(&sd_full[slot]);
+        // gradients of it-1 once its softmax is done; they overlap the softmax of it
+        if (it >= 1) {
+          ok = mbar_wait(&ps_ready[slot ^ 1], ((it - 1) >> 1) & 1, p.err, kErrWaitAccEmpty);
+          if (ok) {
+            tc_fence_after();
+            ok = issue_grads(it - 1);
+          }
+        }
       }
-      if (ok && mbar_wait(ps_ready, (iters - 1) & 1, p.err, kErrWaitAccEmpty)) {
+      if (ok && mbar_wait(&ps_ready[(iters - 1) & 1], ((iters - 1) >> 1) & 1, p.err, kErrWaitAccEmpty)) {
         tc_fence_after();
         issue_grads(iters - 1);
       }
@@ -544,7 +587,7 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
     for (int it = 0; it < iters; ++it) {
       const int slot = it & 1;
       const int m0 = (mb_first + it % per_head) * FB_BM;
-      ok = mbar_wait(sd_full, it & 1, p.err, kErrWaitAccFull) &&
+      ok = mbar_wait(&sd_full[slot], (it >> 1) & 1, p.err, kErrWaitAccFull) &&
            mbar_wait(&qd_full[slot], (it >> 1) & 1, p.err, kErrWaitAccFull);
       // the P^T/dS^T slot was last read by the MMAs of it-2
       if (ok && it >= 2) ok = mbar_wait(&dq_full[slot], ((it - 2) >> 1) & 1, p.err, kErrWaitAccFull);
@@ -567,6 +610,7 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
       const uint32_t lse_a = smem_u32(sLse + slot * 64), dlt_a = smem_u32(sDelta + slot * 64);
       const uint32_t pc = smem_u32(sP + slot * FA_TILE), dc = smem_u32(sdS + slot * FA_TILE);
       uint32_t sv[64], dpv[64];
+      const uint32_t tS = tmem + slot * 128, tdP = tS + 64;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         tmem_ld32(tS + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]));
@@ -607,7 +651,7 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
       fence_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(ps_ready);
+      if (lane == 0) mbar_arrive(&ps_ready[slot]);
     }
     // final dK / dV: TMEM rows -> bf16 global (after the last iteration's MMAs)
     if (ok && iters > 0 && mbar_wait(&dq_full[(iters - 1) & 1], ((iters - 1) >> 1) & 1, p.err, kErrWaitAccFull)) {
@@ -659,14 +703,15 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
       const int m0 = (mb_first + it % per_head) * FB_BM;
       if (!mbar_wait(&dq_full[it & 1], (it >> 1) & 1, p.err, kErrWaitAccFull)) break;
       tc_fence_after();
+      const uint32_t tdQ = tmem + (it & 1) * 128;
       uint32_t v[64];
       tmem_ld32(tdQ + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
       tmem_ld32(tdQ + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
       tmem_wait_ld();
-      // dQ^T is drained from TMEM: let the next dQ MMA start before the atomics
+      // dQ^T is drained from TMEM: the buffer can take the next S^T / dP^T
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(dq_free);
+      if (lane == 0) mbar_arrive(&dq_free[it & 1]);
       // staging buffer must be free: the previous bulk reduce finished reading it
       if (it > 0) {
         if (warp == 6 && lane == 0) bulk_wait_read0();
@@ -786,7 +831,7 @@ void flash_fwd(const void* q, long long ldq, int q_col0, const void* k, long lon
     cudaFuncSetAttribute(flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_FWD_SMEM);
     attr[dev & 63] = true;
   }
-  dim3 grid((Sq + FA_BM - 1) / FA_BM, Hq, B);
+  const unsigned grid = (unsigned)((Sq + FA_BM - 1) / FA_BM) * Hq * B;
   (astrai::note_launch(), flash_fwd_kernel<<<grid, 192, FA_FWD_SMEM, s>>>(tq, tk, tv, p));
 }
 
@@ -842,7 +887,7 @@ void flash_bwd(const void* q, long long ldq, int q_col0, const void* k, long lon
     cudaFuncSetAttribute(flash_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_BWD_SMEM);
     attr[dev & 63] = true;
   }
-  dim3 grid((Sk + FA_BN - 1) / FA_BN, Hkv, B);
+  const unsigned grid = (unsigned)((Sk + FA_BN - 1) / FA_BN) * Hkv * B;
   CUtensorMap tdq;
   {
     uint64_t dims[3] = {(uint64_t)Hq * FA_D, (uint64_t)Sq, (uint64_t)B};

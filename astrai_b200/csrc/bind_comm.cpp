@@ -16,6 +16,11 @@ void fused_allreduce(const long long* seg_ptr, const long long* seg_off, int n_s
                      long long off_sumsq, long long off_recv, long long off_gather, unsigned epoch0, int ctas,
                      float* sumsq_out, float* clip_coef, float max_norm, unsigned* done, int* err,
                      unsigned long long wait_ns, cudaStream_t s);
+void muon_apply_peers(const long long* pptr, const long long* poff, const long long* peer_base, const void* X,
+                      int batch, int R, int C, int transpose, float decay, float adj_lr, int rank, int world,
+                      long long flag_off, int slot, unsigned epoch, unsigned* done, cudaStream_t s);
+void peer_flags_wait(const unsigned* flags, int rank, int world, int rows, unsigned epoch, double wait_s,
+                     cudaStream_t s);
 }  // namespace astrai_host
 
 namespace {
@@ -65,9 +70,54 @@ void fused_allreduce(const at::Tensor& seg_ptr, const at::Tensor& seg_off, int64
                                static_cast<unsigned long long>(wait_s * 1e9), at::cuda::getCurrentCUDAStream().stream());
 }
 
+// Owner-sharded Muon: apply the orthogonalised update X (bf16 [batch][R][C], or [batch][C][R] when
+// transpose) to the parameters at pptr and store the result into every rank's copy (peer_base[q] + poff).
+void muon_apply_peers(const at::Tensor& pptr, const at::Tensor& poff, const at::Tensor& peer_base,
+                      const c10::optional<at::Tensor>& X, int64_t batch, int64_t R, int64_t C, bool transpose,
+                      double decay, double adj_lr, int64_t rank, int64_t world, int64_t flag_off, int64_t slot,
+                      int64_t epoch, at::Tensor& done) {
+  i64_check(peer_base, "peer_base");
+  TORCH_CHECK(peer_base.numel() == world && rank >= 0 && rank < world, "peer_base / rank mismatch");
+  TORCH_CHECK(done.is_cuda() && done.scalar_type() == at::kInt && done.numel() >= 1, "done must be CUDA int32");
+  TORCH_CHECK(flag_off % 4 == 0 && slot >= 0, "bad flag offset / slot");
+  const void* xp = nullptr;
+  const long long* pp = nullptr;
+  const long long* po = nullptr;
+  if (batch > 0) {
+    i64_check(pptr, "pptr");
+    i64_check(poff, "poff");
+    TORCH_CHECK(pptr.numel() == batch && poff.numel() == batch, "pptr / poff need one entry per matrix");
+    TORCH_CHECK(X.has_value() && X->is_cuda() && X->scalar_type() == at::kBFloat16 && X->is_contiguous() &&
+                    X->numel() == batch * R * C,
+                "X must be a contiguous CUDA bf16 [batch, R, C] (or [batch, C, R]) tensor");
+    xp = X->data_ptr();
+    pp = reinterpret_cast<const long long*>(pptr.data_ptr<int64_t>());
+    po = reinterpret_cast<const long long*>(poff.data_ptr<int64_t>());
+  }
+  const c10::cuda::CUDAGuard g(done.device());
+  astrai_host::muon_apply_peers(pp, po, reinterpret_cast<const long long*>(peer_base.data_ptr<int64_t>()), xp,
+                                static_cast<int>(batch), static_cast<int>(R), static_cast<int>(C), transpose ? 1 : 0,
+                                static_cast<float>(decay), static_cast<float>(adj_lr), static_cast<int>(rank),
+                                static_cast<int>(world), flag_off, static_cast<int>(slot),
+                                static_cast<unsigned>(epoch), reinterpret_cast<unsigned*>(done.data_ptr<int>()),
+                                at::cuda::getCurrentCUDAStream().stream());
+}
+
+// Wait (bounded) until every peer raised flag rows [0, rows) of `flags` (u32 [rows][world], this rank's copy).
+void peer_flags_wait(int64_t flags_addr, int64_t device, int64_t rank, int64_t world, int64_t rows, int64_t epoch,
+                     double wait_s) {
+  TORCH_CHECK(flags_addr % 4 == 0 && rank >= 0 && rank < world && rows >= 0, "bad peer_flags_wait arguments");
+  const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  astrai_host::peer_flags_wait(reinterpret_cast<const unsigned*>(flags_addr), static_cast<int>(rank),
+                               static_cast<int>(world), static_cast<int>(rows), static_cast<unsigned>(epoch), wait_s,
+                               at::cuda::getCurrentCUDAStream().stream());
+}
+
 }  // namespace
 
 void register_comm(pybind11::module& m) {
+  m.def("muon_apply_peers", &muon_apply_peers);
+  m.def("peer_flags_wait", &peer_flags_wait);
   m.def("symm_alloc", &symm_alloc, "cudaMalloc + IPC handle -> (address, 64-byte handle)");
   m.def("symm_open", &symm_open, "map a peer's IPC handle -> address");
   m.def("symm_close", [](int64_t p) { astrai_host::symm_close(reinterpret_cast<void*>(p)); });

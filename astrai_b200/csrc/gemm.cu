@@ -85,7 +85,10 @@ struct GemmCfg {
   static constexpr int STAGES_FIT = (225 * 1024) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
   static constexpr int TMEM_COLS = NACC * MH * BN;
-  static constexpr int EPI_WARPS = 4 * MH;
+  // BM = 256: 16 epilogue warps, each pair of warps on one TMEM lane quadrant
+  // splits the columns, so a thread holds half a row (fits the early release)
+  static constexpr int CSPLIT = MH;
+  static constexpr int EPI_WARPS = 4 * MH * CSPLIT;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
   static_assert(TMEM_COLS <= 512, "accumulators exceed tensor memory");
@@ -235,8 +238,10 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;          // TMEM lane quadrant this warp may access
-    const int half = (warp - 2) >> 2;  // which 128-row MMA half (BM = 256)
+    const int q = warp & 3;                     // TMEM lane quadrant this warp may access
+    const int half = ((warp - 2) >> 2) % MH;    // which 128-row MMA half (BM = 256)
+    const int cpart = (warp - 2) >> (2 + (MH - 1));  // which column part (BM = 256)
+    constexpr int BNP = BN / Cfg::CSPLIT;       // columns drained by one thread
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -246,27 +251,76 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
       tc_fence_after();
       const bool no_k = tile_k(p, b, mb, 64).kblk == 0;  // nothing accumulated: the product is 0
       const int row = mb * BM + half * 128 + q * 32 + lane;
-      const int n0 = nb * BN;
+      const int n0 = nb * BN + cpart * BNP;
       const bool row_ok = row < p.M;
       using OutT = typename std::conditional<OUT_F32, float, __nv_bfloat16>::type;
       OutT* drow = reinterpret_cast<OutT*>(p.D) + (long long)b * p.strideD + (long long)row * p.ldd;
       const OutT* crow = p.C ? reinterpret_cast<const OutT*>(p.C) + (long long)b * p.strideC + (long long)row * p.ldc
                              : nullptr;
-      const uint32_t t_acc = tmem_base + ((uint32_t)(q * 32) << 16) + (acc * MH + half) * BN;
+      const uint32_t t_acc = tmem_base + ((uint32_t)(q * 32) << 16) + (acc * MH + half) * BN + cpart * BNP;
+      if (MH == 2 && !OUT_F32 && (crow == nullptr || p.beta == 0.f)) {
+        // BM = 256 (one accumulator buffer) without a C operand: drain the whole
+        // accumulator row slice into packed bf16 registers, release TMEM, then
+        // store, so the next tile's MMAs wait only for the TMEM reads.
+        uint32_t pk[MH == 2 ? BNP / 2 : 1];
+#pragma unroll
+        for (int c = 0; c < BNP; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(t_acc + c, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            pk[c / 2 + i] = no_k ? 0u
+                                 : pack_bf16(__uint_as_float(r[2 * i]) * p.alpha,
+                                             __uint_as_float(r[2 * i + 1]) * p.alpha);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        if (row_ok) {
+          __nv_bfloat16* dr = reinterpret_cast<__nv_bfloat16*>(drow);
+#pragma unroll
+          for (int c = 0; c < BNP; c += 8) {
+            const int col = n0 + c;
+            if (col + 8 <= p.N && p.vec_ok) {
+              *reinterpret_cast<uint4*>(dr + col) =
+                  make_uint4(pk[c / 2], pk[c / 2 + 1], pk[c / 2 + 2], pk[c / 2 + 3]);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                if (col + i < p.N) {
+                  const uint32_t w = pk[(c + i) / 2];
+                  const unsigned short h = (i & 1) ? (unsigned short)(w >> 16) : (unsigned short)(w & 0xffffu);
+                  dr[col + i] = __ushort_as_bfloat16(h);
+                }
+              }
+            }
+          }
+        }
+        if (++acc == NACC) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+        continue;
+      }
+      // chunks of SUBS x 32 columns (one sub-chunk when the register budget is
+      // that of the 576-thread BM = 256 kernel)
+      constexpr int SUBS = MH == 2 ? 1 : 2;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 64) {
-        uint32_t r2[64];
-        tmem_ld32(t_acc + c, *reinterpret_cast<uint32_t(*)[32]>(&r2[0]));
-        tmem_ld32(t_acc + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&r2[32]));
+      for (int c = 0; c < BNP; c += 32 * SUBS) {
+        uint32_t r2[32 * SUBS];
+#pragma unroll
+        for (int sub = 0; sub < SUBS; ++sub)
+          tmem_ld32(t_acc + c + sub * 32, *reinterpret_cast<uint32_t(*)[32]>(&r2[sub * 32]));
         tmem_wait_ld();
-        if (c + 64 >= BN) {
+        if (c + 32 * SUBS >= BNP) {
           // last chunk read: release the accumulator before the global stores
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[acc]);
         }
 #pragma unroll
-        for (int sub = 0; sub < 2; ++sub) {
+        for (int sub = 0; sub < SUBS; ++sub) {
           const uint32_t* r = &r2[sub * 32];
           const int col = n0 + c + sub * 32;
           if (!row_ok || col >= p.N) continue;

@@ -237,9 +237,16 @@ def newton_schulz_batched(X: torch.Tensor, steps: int = 5, coeffs=NS_COEFFS, wor
 
 
 class Muon(Optimizer):
+    """``shard=True`` (data parallelism with replicated parameters and all-reduced gradients):
+    matrix i of every same-shape group is owned by rank ``i % world``; only the owner keeps its
+    momentum and runs Newton-Schulz, and one kernel applies the update to every rank's copy over
+    NVLink peer memory (the parameters are moved into a symmetric buffer on the first step).
+    Parameters marked ``_ep_local`` (expert-parallel shards, different on every rank) stay local."""
+
     def __init__(self, params, lr: float = 1e-3, weight_decay: float = 0.1, momentum: float = 0.95,
                  nesterov: bool = True, ns_coefficients=NS_COEFFS, eps: float = 1e-7, ns_steps: int = 5,
-                 adjust_lr_fn: Optional[str] = None, use_clip_coef: bool = True):
+                 adjust_lr_fn: Optional[str] = None, use_clip_coef: bool = True, shard: bool = False,
+                 process_group=None, wait_s: float = 60.0):
         super().__init__(params, dict(lr=lr, weight_decay=weight_decay, momentum=momentum, nesterov=nesterov,
                                       ns_coefficients=tuple(ns_coefficients), eps=eps, ns_steps=ns_steps,
                                       adjust_lr_fn=adjust_lr_fn))
@@ -250,6 +257,16 @@ class Muon(Optimizer):
         self.use_clip_coef = use_clip_coef
         self._reset_clip = True
         self._work: Dict[tuple, dict] = {}
+        self.shard, self.process_group, self.wait_s = shard, process_group, wait_s
+        self._arena = None
+        self._epoch = 0
+
+    @property
+    def sharded(self) -> bool:
+        import torch.distributed as dist
+
+        return bool(self.shard and dist.is_available() and dist.is_initialized()
+                    and dist.get_world_size(self.process_group) > 1)
 
     def _buf(self, p):
         st = self.state[p]
@@ -260,6 +277,9 @@ class Muon(Optimizer):
     @torch.no_grad()
     def step(self, closure=None):
         loss = closure() if closure is not None else None
+        if self.sharded:
+            self._step_sharded()
+            return loss
         for gi, group in enumerate(self.param_groups):
             params = [p for p in group["params"] if p.grad is not None]
             if not params:
@@ -276,18 +296,79 @@ class Muon(Optimizer):
                 clip_state(params[0].device).coef.fill_(1.0)
         return loss
 
-    def _step_batched(self, gi, shape, ps, group):
+    # ------------------------------------------------------------------ owner-sharded step
+    def _shared_groups(self):
+        """[(gi, shape, params)] of the replicated matrices, in the same order on every rank."""
+        out = []
+        for gi, group in enumerate(self.param_groups):
+            by_shape: Dict[tuple, List[torch.Tensor]] = {}
+            for p in group["params"]:
+                if not getattr(p, "_ep_local", False):
+                    by_shape.setdefault(tuple(p.shape), []).append(p)
+            out += [(gi, shape, ps) for shape, ps in by_shape.items()]
+        return out
+
+    def _step_sharded(self):
+        import torch.distributed as dist
+
+        from astrai_b200.parallel.symm import ParamArena
+
+        groups = self._shared_groups()
+        shared = [p for _, _, ps in groups for p in ps]
+        if shared and (self._arena is None or not all(self._arena.holds(p) for p in shared)):
+            if self._arena is not None:  # parameters were re-packed elsewhere: rebuild on every rank
+                dist.barrier(group=self.process_group)
+            self._arena = ParamArena(shared, self.process_group)
+            self._work = {k: v for k, v in self._work.items() if k[0] != "own"}
+        if len(groups) > ParamArena.FLAG_ROWS:
+            raise RuntimeError(f"sharded Muon supports at most {ParamArena.FLAG_ROWS} shape groups")
+        C = native()
+        a = self._arena
+        W, r = (a.world, a.rank) if a is not None else (1, 0)
+        self._epoch += 1
+        dev = None
+        for slot, (gi, shape, ps) in enumerate(groups):
+            group = self.param_groups[gi]
+            own = [p for i, p in enumerate(ps) if i % W == r]
+            if any(p.grad is None for p in own):
+                raise RuntimeError("sharded Muon: an owned parameter has no gradient")
+            R, Cc = shape
+            lr = float(group["lr"])
+            adj = _adjust_lr(lr, group["adjust_lr_fn"], shape)
+            dev = ps[0].device
+            if own:
+                w, out, tall = self._orthogonalize(("own", gi, shape), own, group)
+                C.muon_apply_peers(w["pptr"], w["poff"], a.buf.peer_base, out, len(own), R, Cc, tall,
+                                   1.0 - lr * group["weight_decay"], adj, r, W, a.flag_off, slot, self._epoch, a.done)
+            else:  # nothing owned in this group: only raise its flag on the peers
+                C.muon_apply_peers(None, None, a.buf.peer_base, None, 0, R, Cc, False, 1.0, 0.0, r, W, a.flag_off,
+                                   slot, self._epoch, a.done)
+        # expert-parallel shards: every rank updates its own
+        for gi, group in enumerate(self.param_groups):
+            local = [p for p in group["params"] if getattr(p, "_ep_local", False) and p.grad is not None]
+            by_shape: Dict[tuple, List[torch.Tensor]] = {}
+            for p in local:
+                by_shape.setdefault(tuple(p.shape), []).append(p)
+            for shape, ps in by_shape.items():
+                self._step_batched(gi, shape, ps, group)
+        if groups:
+            C.peer_flags_wait(a.flags_addr, dev.index, r, W, len(groups), self._epoch, self.wait_s)
+        if self._reset_clip and self.use_clip_coef and dev is not None:
+            clip_state(dev).coef.fill_(1.0)
+
+    def _orthogonalize(self, key, ps, group):
+        """Momentum + Frobenius normalisation + Newton-Schulz of the same-shape matrices ``ps``."""
         C = native()
         dev = ps[0].device
-        R, Cc = shape
+        R, Cc = ps[0].shape
         tall = R > Cc
         m, n = (Cc, R) if tall else (R, Cc)
         Bn = len(ps)
-        key = (gi, shape, tuple(p.data_ptr() for p in ps))
-        w = self._work.get((gi, shape))
-        if w is None or w["key"] != key:
+        ident = tuple(p.data_ptr() for p in ps)
+        w = self._work.get(key)
+        if w is None or w["ident"] != ident:
             w = {
-                "key": key,
+                "ident": ident,
                 "U": torch.empty(Bn, R, Cc, device=dev, dtype=torch.bfloat16),
                 "X": torch.empty(Bn, m, n, device=dev, dtype=torch.bfloat16),
                 "Y": torch.empty(Bn, m, n, device=dev, dtype=torch.bfloat16),
@@ -297,16 +378,23 @@ class Muon(Optimizer):
                 "pptr": _i64([p.data_ptr() for p in ps], dev),
                 "bptr": _i64([self._buf(p).data_ptr() for p in ps], dev),
             }
-            self._work[(gi, shape)] = w
+            if self._arena is not None and all(self._arena.holds(p) for p in ps):
+                w["poff"] = _i64([self._arena.offset[id(p)] for p in ps], dev)
+            self._work[key] = w
         gptr = _i64([p.grad.data_ptr() for p in ps], dev)
         w["sumsq"].zero_()
         coef = clip_state(dev).coef if self.use_clip_coef else None
         C.muon_momentum(gptr, w["bptr"], True, w["U"], group["momentum"], group["nesterov"], coef, w["sumsq"])
         C.muon_normalize(w["U"], w["X"], tall, w["sumsq"], group["eps"])
         out = newton_schulz_batched(w["X"], group["ns_steps"], group["ns_coefficients"], (w["Y"], w["A"], w["Bm"]))
+        return w, out, tall
+
+    def _step_batched(self, gi, shape, ps, group):
+        w, out, tall = self._orthogonalize((gi, shape), ps, group)
+        R, Cc = shape
         lr = float(group["lr"])
         adj = _adjust_lr(lr, group["adjust_lr_fn"], shape)
-        C.muon_apply(w["pptr"], False, out, R, Cc, tall, 1.0 - lr * group["weight_decay"], adj)
+        native().muon_apply(w["pptr"], False, out, R, Cc, tall, 1.0 - lr * group["weight_decay"], adj)
 
     def _step_reference(self, params, group):
         mu = group["momentum"]
@@ -334,7 +422,7 @@ class MuonMix(Optimizer):
     def __init__(self, model: torch.nn.Module, lr: float = 3e-4, weight_decay: float = 0.1, momentum: float = 0.95,
                  nesterov: bool = True, ns_steps: int = 5, adjust_lr_fn: Optional[str] = "match_rms_adamw",
                  adamw_lr: Optional[float] = None, adamw_weight_decay: float = 0.0,
-                 adamw_betas: Tuple[float, float] = (0.9, 0.95)):
+                 adamw_betas: Tuple[float, float] = (0.9, 0.95), shard_muon: bool = False, process_group=None):
         params = [p for p in model.parameters() if p.requires_grad]
         super().__init__(params, dict(lr=lr))
         seen = set()
@@ -345,7 +433,8 @@ class MuonMix(Optimizer):
             seen.add(id(p))
             (mat if is_muon_param(name, p) else other).append(p)
         self.muon = Muon(mat, lr=lr, weight_decay=weight_decay, momentum=momentum, nesterov=nesterov,
-                         ns_steps=ns_steps, adjust_lr_fn=adjust_lr_fn) if mat else None
+                         ns_steps=ns_steps, adjust_lr_fn=adjust_lr_fn, shard=shard_muon,
+                         process_group=process_group) if mat else None
         self.adamw = FusedAdamW([{"params": other, "weight_decay": adamw_weight_decay}],
                                 lr=adamw_lr if adamw_lr is not None else lr, betas=adamw_betas) if other else None
         self.param_groups = [*(self.muon.param_groups if self.muon else []),
@@ -369,6 +458,11 @@ class MuonMix(Optimizer):
             self.muon.zero_grad(set_to_none)
         if self.adamw:
             self.adamw.zero_grad(set_to_none)
+
+    @property
+    def sharded(self) -> bool:
+        """True when every rank holds different optimizer state (save one file per rank)."""
+        return bool(self.muon is not None and self.muon.sharded)
 
     def state_dict(self):
         return {"muon": self.muon.state_dict() if self.muon else {},

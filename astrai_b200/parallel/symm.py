@@ -68,6 +68,77 @@ class SymmetricBuffer:
         self.ptrs = None
 
 
+class ParamArena:
+    """Parameters moved into one symmetric buffer, at the same offset on every rank.
+
+    A kernel can then write any rank's copy of a parameter at
+    ``peer_base[q] + offset(p)``. Parameters that share a storage (packed
+    q/k/v or up/gate views) are moved as one region, so they stay adjacent
+    views of one tensor. Only ``.data`` is re-pointed: parameter objects,
+    optimizer state keys and module references are unchanged. A block of u32
+    flags (``FLAG_ROWS`` x world, zeroed) follows the parameters.
+    """
+
+    FLAG_ROWS = 32
+
+    def __init__(self, params: Sequence[torch.Tensor], group=None):
+        params = list(params)
+        if not params:
+            raise ValueError("ParamArena needs at least one parameter")
+        dev = params[0].device
+        regions: Dict[int, List[int]] = {}
+        owner: Dict[int, torch.Tensor] = {}
+        for p in params:
+            if not p.is_contiguous():
+                raise ValueError("ParamArena parameters must be contiguous")
+            st = p.untyped_storage().data_ptr()
+            lo, hi = p.data_ptr(), p.data_ptr() + p.numel() * p.element_size()
+            r = regions.setdefault(st, [lo, hi])
+            r[0], r[1] = min(r[0], lo), max(r[1], hi)
+            owner.setdefault(st, p)
+        region_off: Dict[int, int] = {}
+        off = 0
+        for st, (lo, hi) in regions.items():
+            region_off[st] = off
+            off = _align(off + hi - lo)
+        self.flag_off = off
+        self.buf = SymmetricBuffer(off + _align(self.FLAG_ROWS * 4 * max(1, self._world(group))), group, dev)
+        self.world, self.rank = self.buf.world, self.buf.rank
+        self.buf.local_view(self.flag_off, self.FLAG_ROWS * 4 * self.world).zero_()
+        base = self.buf.local_view(0, off)
+        with torch.no_grad():
+            for st, (lo, hi) in regions.items():
+                old = torch.empty(0, dtype=torch.uint8, device=dev).set_(owner[st].untyped_storage())
+                o0 = lo - st
+                base[region_off[st]:region_off[st] + hi - lo].copy_(old[o0:o0 + hi - lo])
+            self.offset: Dict[int, int] = {}
+            for p in params:
+                st = p.untyped_storage().data_ptr()
+                o = region_off[st] + p.data_ptr() - regions[st][0]
+                n = p.numel() * p.element_size()
+                self.offset[id(p)] = o
+                p.data = base[o:o + n].view(p.dtype).view(p.shape)
+        torch.cuda.synchronize(dev)
+        if self.world > 1:
+            dist.barrier(group=group)
+        self.lo, self.hi = self.buf.local_ptr, self.buf.local_ptr + off
+        self.done = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    @staticmethod
+    def _world(group) -> int:
+        return dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+
+    def holds(self, p: torch.Tensor) -> bool:
+        return id(p) in self.offset and self.lo <= p.data_ptr() < self.hi
+
+    @property
+    def flags_addr(self) -> int:
+        return self.buf.local_ptr + self.flag_off
+
+    def close(self) -> None:
+        self.buf.close()
+
+
 class AllReducePlan:
     """Byte layout of the all-reduce buffer and the round / slice / chunk split.
 

@@ -118,6 +118,14 @@ class CheckpointCallback:
                                                 config=context.model_config, extra=extra,
                                                 meta=context.config.to_dict())
                 context.checkpoint.save(path)
+        opt = getattr(context, "optimizer", None)
+        if not self.weight_only and opt is not None and getattr(opt, "sharded", False):
+            # every rank holds a different optimizer shard: one file per rank next to optimizer.pt
+            path = os.path.join(self.save_dir, f"epoch_{context.epoch}_step_{context.optimizer_step}")
+            os.makedirs(path, exist_ok=True)
+            torch.save(opt.state_dict(), os.path.join(path, f"optimizer.rank{context.rank}.pt"))
+            if dist.is_available() and dist.is_initialized():
+                dist.barrier()
 
     def on_batch_end(self, context):
         if context.optimizer_step - self.last_ckpt_step >= self.interval:

@@ -14,6 +14,8 @@ the hot loop never synchronises with the host per micro-batch.
 
 from __future__ import annotations
 
+import os
+
 from dataclasses import dataclass, field
 from pathlib import Path
 from typing import Any, Dict, Optional
@@ -156,6 +158,11 @@ class TrainContextBuilder:
                 obj = getattr(ctx, name, None)
                 if obj is not None and name in ctx.checkpoint.extra:
                     obj.load_state_dict(ctx.checkpoint.extra[name])
+        shard_file = os.path.join(str(self._param_path), f"optimizer.rank{ctx.rank}.pt") \
+            if self._param_path and self._resume else None
+        if ctx.optimizer is not None and getattr(ctx.optimizer, "sharded", False) and shard_file \
+                and os.path.exists(shard_file):
+            ctx.optimizer.load_state_dict(torch.load(shard_file, map_location="cpu", weights_only=False))
 
         skw = dict(cfg.extra_kwargs)
         if cfg.strategy in ("dpo", "grpo", "online_grpo", "online_dpo"):

@@ -1,7 +1,7 @@
 """Device-timed micro-benchmarks of the framework's kernels.
 
     python -m astrai_b200.utils.kernel_bench [gemm|attn|decode|sample|all]
-    torchrun --nproc-per-node N -m astrai_b200.utils.kernel_bench allreduce
+    torchrun --nproc-per-node N -m astrai_b200.utils.kernel_bench allreduce|ep
 
 Each case is timed with CUDA events on the launching stream after warm-up,
 with a synchronize on both sides; inputs larger than L2 are used where the
@@ -121,6 +121,103 @@ def bench_allreduce():
     dist.destroy_process_group()
 
 
+def bench_ep(tokens: int = 8192, d: int = 2048, n_experts: int = 64, k: int = 6):
+    """Expert-parallel dispatch and combine of one MoE layer's forward (the BASELINE MoE shape:
+    seq 4096 x batch 2 tokens per rank, d 2048, 64 experts top-6), our P2P kernels vs an NCCL
+    all_to_all_single pipeline moving the same rows; device time, max over ranks.
+
+    dispatch = ep_dispatch + ep_wait (token rows stored into the owning ranks' expert blocks);
+    combine = ep_return + ep_wait + ep_combine (expert outputs stored back into the source ranks'
+    slot blocks, then the gate-weighted sum). NCCL arm: gather rows by destination rank,
+    all_to_all_single, and back with all_to_all_single + a gate-weighted index_add."""
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from astrai_b200.ops._ext import native
+    from astrai_b200.ops.moe import moe_route
+    from astrai_b200.parallel.ep import PH_DISPATCH, PH_RETURN, EPArena, EPGroup, EPLayout
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    C = native()
+    ep = EPGroup()
+    W, rank = ep.world, ep.rank
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    x = torch.randn(tokens, d, device=dev, generator=g).to(torch.bfloat16)
+    logits = torch.randn(tokens, n_experts, device=dev, generator=g).to(torch.bfloat16)
+    w, _, idx, counts, pos = moe_route(logits, k)
+    layout = EPLayout(ep.all_gather_counts(counts).cpu().numpy(), rank, n_experts // W, dev)
+    arena = EPArena(ep, d, tokens, k, n_experts, 2.0, dev, min_rows=layout.max_rows)
+    El, R = layout.e_local, layout.total
+    slot_row = torch.empty(tokens * k, device=dev, dtype=torch.int32)
+    y = torch.randn(max(R, 1), d, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty(tokens, d, device=dev, dtype=torch.bfloat16)
+
+    def dispatch():
+        e = arena.next_epoch(PH_DISPATCH)
+        C.ep_dispatch(*arena.args(), x, idx.view(-1), pos, layout.base_row, El, slot_row, e)
+        C.ep_wait(*arena.args(), PH_DISPATCH, e)
+
+    def combine():
+        e = arena.next_epoch(PH_RETURN)
+        C.ep_return(*arena.args(), y[:R], layout.group_tile, layout.starts, layout.n_rows, 0, e)
+        C.ep_wait(*arena.args(), PH_RETURN, e)
+        C.ep_combine(arena.block("ret", tokens * k), w, None, out, k)
+
+    # NCCL arm: rows ordered by destination rank (experts are contiguous per rank)
+    dest = (idx.view(-1) // El).to(torch.int64)
+    order = torch.argsort(dest, stable=True)
+    send_counts = torch.bincount(dest, minlength=W)
+    recv_counts = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv_counts, send_counts)
+    sc, rc = send_counts.tolist(), recv_counts.tolist()
+    tok_of = order // k
+    wts = w.reshape(-1)[order].unsqueeze(-1)
+    recv = torch.empty(sum(rc), d, device=dev, dtype=torch.bfloat16)
+    back = torch.empty(tokens * k, d, device=dev, dtype=torch.bfloat16)
+
+    def nccl_dispatch():
+        dist.all_to_all_single(recv, x.index_select(0, tok_of), rc, sc)
+
+    def nccl_combine():
+        dist.all_to_all_single(back, recv, sc, rc)
+        torch.zeros(tokens, d, device=dev, dtype=torch.float32).index_add_(0, tok_of, back.float() * wts)
+
+    def t_max(fn, iters=20):
+        ms = time_fn(fn, warmup=5, iters=iters)
+        v = torch.tensor([ms], device=dev)
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+        return float(v) * 1e3  # us
+
+    res = {"dispatch_us": t_max(dispatch), "combine_us": t_max(combine),
+           "dispatch_combine_us": t_max(lambda: (dispatch(), combine())),
+           "nccl_dispatch_us": t_max(nccl_dispatch), "nccl_combine_us": t_max(nccl_combine),
+           "nccl_dispatch_combine_us": t_max(lambda: (nccl_dispatch(), nccl_combine()))}
+    from astrai_b200.ops._ext import check_error
+
+    err = check_error()
+    # rows that cross NVLink from this rank (slots whose expert lives elsewhere), max over ranks
+    remote = torch.tensor([float((dest != rank).sum())], device=dev)
+    dist.all_reduce(remote, op=dist.ReduceOp.MAX)
+    nbytes = float(remote) * d * 2
+    arena.close()
+    if rank == 0:
+        link = 770.0  # GB/s per direction, measured peer copy on this pool
+        floor_us = nbytes / (link * 1e3)
+        print(json.dumps({"kernel": "ep_dispatch_combine", "world": W, "tokens_per_rank": tokens, "d": d,
+                          "experts": n_experts, "top_k": k, "remote_bytes_per_rank_each_way": int(nbytes),
+                          **{k2: round(v, 1) for k2, v in res.items()},
+                          "nvlink_floor_us_each_way": round(floor_us, 1),
+                          "dispatch_frac_of_link": round(floor_us / res["dispatch_us"], 3),
+                          "combine_frac_of_link": round(floor_us / res["combine_us"], 3),
+                          "speedup_vs_nccl": round(res["nccl_dispatch_combine_us"] / res["dispatch_combine_us"], 2),
+                          "device_error_word": err}))
+    dist.destroy_process_group()
+
+
 def bench_skinny():
     """Decode GEMMs (M token rows x weight [N, K]): device time and weight-read bandwidth."""
     from astrai_b200.ops._ext import native
@@ -163,6 +260,9 @@ def main(argv=None):
     torch.manual_seed(0)
     if which == "allreduce":
         bench_allreduce()
+        return
+    if which == "ep":
+        bench_ep()
         return
     if which in ("skinny", "all"):
         bench_skinny()

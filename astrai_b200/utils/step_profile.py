@@ -86,7 +86,7 @@ def main(argv=None) -> None:
     per = defaultdict(lambda: [0.0, 0])
     for ev in prof.events():
         if ev.device_type == torch.autograd.DeviceType.CUDA:
-            per[ev.name][0] += ev.device_time_total / 1e3 if hasattr(ev, "device_time_total") else ev.cuda_time / 1e3
+            per[ev.name][0] += ev.time_range.elapsed_us() / 1e3  # kernel records: start/end on the device
             per[ev.name][1] += 1
     total = sum(v[0] for v in per.values()) or 1.0
     cats = defaultdict(float)

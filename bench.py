@@ -68,8 +68,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="astrai_b200", choices=["astrai_b200", "reference"])
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end Trainer measurement")
-    ap.add_argument("--model", default="dense", choices=["dense", "moe"],
-                    help="dense: BASELINE config 2 (default); moe: config 3 with expert parallelism over all GPUs")
+    ap.add_argument("--model", default="dense", choices=["dense", "moe", "dpo", "grpo"],
+                    help="dense: BASELINE config 2 (default); moe: config 3 with expert parallelism over all GPUs; "
+                         "dpo / grpo: configs 4 / 5 (post-training on the dense model)")
     return ap.parse_args()
 
 
@@ -190,8 +191,10 @@ def run_ours(args, rank, world, local):
     executor = ExecutorFactory.create("ddp" if world > 1 else "none", grad_accum_steps=ACCUM, comm_backend="fused",
                                       expert_parallel=MODEL == "moe")
     model = executor.wrap(model)
+    # world > 1: each rank orthogonalises 1/world of the hidden matrices and writes the updated
+    # weights into every rank's copy over NVLink (owner-sharded Muon)
     opt = MuonMix(executor.unwrap(model), lr=MUON_LR, weight_decay=WD, adamw_lr=ADAMW_LR, adamw_weight_decay=WD,
-                  adjust_lr_fn="match_rms_adamw")
+                  adjust_lr_fn="match_rms_adamw", shard_muon=world > 1)
     V = CFG["vocab_size"]
     n_batches = 4
     data = torch.randint(0, V, (n_batches, ACCUM, BATCH, SEQ + 1), device=dev)
@@ -295,7 +298,7 @@ def run_ours_e2e(args, rank, world, local, model, executor, opt):
         strategy="seq",
         dataset=SynthSeq(total * ACCUM * BATCH * world, CFG["vocab_size"], SEQ, seed=11 + rank),
         optimizer_fn=lambda m: MuonMix(m, lr=MUON_LR, weight_decay=WD, adamw_lr=ADAMW_LR, adamw_weight_decay=WD,
-                                       adjust_lr_fn="match_rms_adamw"),
+                                       adjust_lr_fn="match_rms_adamw", shard_muon=world > 1),
         scheduler_fn=lambda o: SchedulerFactory.create("cosine", o, warmup_steps=0, lr_decay_steps=10 ** 6),
         batch_per_device=BATCH, grad_accum_steps=ACCUM, max_grad_norm=CLIP, ckpt_dir=None, ckpt_interval=10 ** 9,
         log_dir=tempfile.mkdtemp(prefix="astrai_bench_logs_"), nprocs=world,
@@ -442,11 +445,210 @@ def run_reference(args, rank, world, local):
             "gpu_launches": None}
 
 
+# ----------------------------------------------------------------------------- post-training configs
+# DPO on the 1.1B model, 8 pairs per GPU of a 512-token prompt + 512-token
+# chosen / rejected responses (uniform ids), loss on response tokens, beta 0.1, AdamW lr 5e-7.
+DPO_PAIRS, DPO_PROMPT, DPO_RESP, DPO_BETA, DPO_LR = 8, 512, 512, 0.1, 5e-7
+# config 5: GRPO, 64 prompts of 256 tokens per 8 GPUs (8 per GPU), group 8, up to 512 new tokens at
+# T 0.8 / top_p 0.95 / top_k 50, hash reward in [0, 1], KL 0.04, one PPO-clip(0.2) update.
+GRPO_PROMPTS_PER_GPU, GRPO_PROMPT, GRPO_G, GRPO_NEW = 8, 256, 8, 512
+GRPO_T, GRPO_TOP_P, GRPO_TOP_K, GRPO_KL, GRPO_CLIP, GRPO_LR = 0.8, 0.95, 50, 0.04, 0.2, 5e-7
+
+
+def _post_train_models(rank, world, local, n_copies):
+    """Policy (wrapped by the DDP executor for world > 1) and frozen copies sharing its init."""
+    import copy
+
+    import torch
+
+    sys.path.insert(0, ROOT)
+    from astrai_b200.config import AutoRegressiveLMConfig
+    from astrai_b200.models import AutoRegressiveLM
+    from astrai_b200.parallel.executor import ExecutorFactory
+
+    torch.manual_seed(3407)  # every rank: same init, as a loaded checkpoint would be
+    dev = torch.device("cuda", local)
+    with torch.device(dev):
+        model = AutoRegressiveLM(AutoRegressiveLMConfig(**CFG)).to(torch.bfloat16)
+    frozen = []
+    for _ in range(n_copies):
+        m = copy.deepcopy(model).eval()
+        m.requires_grad_(False)
+        frozen.append(m)
+    executor = ExecutorFactory.create("ddp" if world > 1 else "none", grad_accum_steps=1, comm_backend="fused")
+    return executor.wrap(model), frozen, executor, dev
+
+
+def run_ours_dpo(args, rank, world, local):
+    import torch
+
+    from astrai_b200.ops._ext import native
+    from astrai_b200.optim import FusedAdamW
+    from astrai_b200.trainer.strategy import DPOStrategy
+
+    model, (ref,), executor, dev = _post_train_models(rank, world, local, 1)
+    opt = FusedAdamW(executor.unwrap(model).parameters(), lr=DPO_LR, weight_decay=0.0)
+    strat = DPOStrategy(model, dev, ref_model=ref, beta=DPO_BETA)
+    L = DPO_PROMPT + DPO_RESP
+    g = torch.Generator(device=dev).manual_seed(11 + rank)
+    V = CFG["vocab_size"]
+    mask = torch.zeros(DPO_PAIRS, L, device=dev)
+    mask[:, DPO_PROMPT:] = 1.0
+    batches = [{"chosen": torch.randint(1, V, (DPO_PAIRS, L), device=dev, generator=g),
+                "rejected": torch.randint(1, V, (DPO_PAIRS, L), device=dev, generator=g),
+                "chosen_mask": mask, "rejected_mask": mask} for _ in range(2)]
+
+    def step(i):
+        with executor.micro_step(model, True):
+            loss = strat.compute_loss(batches[i % 2])
+            loss.backward()
+        executor.finish_step(model)
+        executor.clip_grad_norm(model, CLIP, as_tensor=True)
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return loss
+
+    for i in range(args.warmup):
+        step(i)
+    clocks = ClockSampler(rank == 0)
+    barrier()
+    clocks.start()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = native().launch_count()
+    s.record()
+    for i in range(args.steps):
+        last = step(i)
+    e.record()
+    n_launch = native().launch_count() - n0
+    barrier()
+    ck = clocks.stop(visible_gpu_indices(world))
+    ms = max_over_ranks(s.elapsed_time(e)) / args.steps
+    assert native().read_error() == 0
+    tokens = 2 * DPO_PAIRS * L  # policy sequences per GPU per step (the frozen reference re-reads them)
+    return {"ms_per_step": ms, "value": world * tokens / (ms / 1e3), "clocks": ck, "loss": float(last.item()),
+            "gpu_launches": n_launch}
+
+
+class _IdTokenizer:
+    """Rollouts on token ids only: no stop tokens (uniform random prompts), no text."""
+
+    stop_ids: list = []
+
+    def decode(self, ids, skip_special_tokens=True):
+        return ""
+
+
+def run_ours_grpo(args, rank, world, local):
+    import torch
+
+    from astrai_b200.inference.core.scheduler import InferenceScheduler
+    from astrai_b200.ops._ext import native
+    from astrai_b200.optim import FusedAdamW
+    from astrai_b200.trainer.rollout import RolloutGenerator
+    from astrai_b200.trainer.strategy import GRPOStrategy
+
+    model, (old, ref), executor, dev = _post_train_models(rank, world, local, 2)
+    base = executor.unwrap(model)
+    opt = FusedAdamW(base.parameters(), lr=GRPO_LR, weight_decay=0.0)
+    n_seq = GRPO_PROMPTS_PER_GPU * GRPO_G
+    sched = InferenceScheduler(base, _IdTokenizer(), max_batch_size=n_seq, max_seq_len=GRPO_PROMPT + GRPO_NEW + 1,
+                               max_prompt_len=GRPO_PROMPT, use_cuda_graph=True, seed=rank)
+    gen = RolloutGenerator(sched, None, max_tokens=GRPO_NEW, group_size=GRPO_G, temperature=GRPO_T,
+                           top_k=GRPO_TOP_K, top_p=GRPO_TOP_P)
+    strat = GRPOStrategy(model, dev, old_model=old, ref_model=ref, clip_eps=GRPO_CLIP, kl_coef=GRPO_KL,
+                         group_size=GRPO_G, executor=None)
+    g = torch.Generator().manual_seed(101 + rank)
+    V = CFG["vocab_size"]
+
+    def reward(resp, rmask):
+        # deterministic hash of the response ids -> [0, 1)
+        pos = torch.arange(resp.shape[-1], device=resp.device)
+        h = ((resp * 1000003 + pos * 7919) * rmask).sum(-1) % 65521
+        return h.float() / 65521.0
+
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+
+    def step(i):
+        prompts = torch.randint(1, V, (GRPO_PROMPTS_PER_GPU, GRPO_PROMPT), generator=g).tolist()
+        t0, t1, t2 = ev(), ev(), ev()
+        t0.record()
+        base.eval()
+        with torch.no_grad():
+            raw = gen.generate_from_ids(prompts)
+        base.train()
+        t1.record()
+        batch = {"prompts": raw.prompts, "prompt_mask": raw.prompt_mask, "responses": raw.responses,
+                 "masks": raw.response_mask, "rewards": reward(raw.responses, raw.response_mask.long())}
+        old.load_state_dict(base.state_dict())  # the rollout policy is the PPO "old" policy
+        with executor.micro_step(model, True):
+            loss = strat.compute_loss(batch)
+            loss.backward()
+        executor.finish_step(model)
+        executor.clip_grad_norm(model, CLIP, as_tensor=True)
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        t2.record()
+        new_tokens = int(raw.response_mask.sum().item())
+        train_tokens = int(raw.response_mask.shape[0] * raw.response_mask.shape[1]
+                           * (raw.prompts.shape[1] + raw.responses.shape[-1]))
+        return (t0, t1, t2), new_tokens, train_tokens, loss
+
+    for i in range(args.warmup):
+        step(i)
+    clocks = ClockSampler(rank == 0)
+    barrier()
+    clocks.start()
+    n0 = native().launch_count()
+    dec_ms = tr_ms = 0.0
+    dec_tok = tr_tok = 0
+    s, e = ev(), ev()
+    s.record()
+    for i in range(args.steps):
+        (t0, t1, t2), nt, tt, last = step(args.warmup + i)
+        torch.cuda.synchronize()
+        dec_ms += t0.elapsed_time(t1)
+        tr_ms += t1.elapsed_time(t2)
+        dec_tok += nt
+        tr_tok += tt
+    e.record()
+    n_launch = native().launch_count() - n0
+    barrier()
+    ck = clocks.stop(visible_gpu_indices(world))
+    ms = max_over_ranks(s.elapsed_time(e)) / args.steps
+    dec_ms, tr_ms = max_over_ranks(dec_ms), max_over_ranks(tr_ms)
+    assert native().read_error() == 0
+    sched.stop()
+    return {"ms_per_step": ms, "value": world * dec_tok / (dec_ms / 1e3), "clocks": ck, "loss": float(last.item()),
+            "gpu_launches": n_launch,
+            "grpo": {"decode_tokens_per_s": round(world * dec_tok / (dec_ms / 1e3), 1),
+                     "train_tokens_per_s": round(world * tr_tok / (tr_ms / 1e3), 1),
+                     "decode_ms_per_step": round(dec_ms / args.steps, 1),
+                     "train_ms_per_step": round(tr_ms / args.steps, 1),
+                     "new_tokens_per_gpu_step": dec_tok // args.steps,
+                     "rollout": f"{GRPO_PROMPTS_PER_GPU} prompts x G{GRPO_G} per GPU, paged KV + CUDA-graph decode"}}
+
+
 # ----------------------------------------------------------------------------- main
+def use_post_train(kind):
+    global MODEL_DESC, METRIC, MODEL, BATCH, SEQ, ACCUM
+    MODEL = kind
+    if kind == "dpo":
+        METRIC = "DPO train tokens/s (1B dense)"
+        BATCH, SEQ, ACCUM = 2 * DPO_PAIRS, DPO_PROMPT + DPO_RESP, 1
+        MODEL_DESC += f", DPO {DPO_PAIRS} pairs/GPU, prompt {DPO_PROMPT} + chosen/rejected {DPO_RESP}, beta 0.1"
+    else:
+        METRIC = "GRPO rollout decode tokens/s (1B dense)"
+        BATCH, SEQ, ACCUM = GRPO_PROMPTS_PER_GPU * GRPO_G, GRPO_PROMPT + GRPO_NEW, 1
+        MODEL_DESC += (f", GRPO {GRPO_PROMPTS_PER_GPU} prompts/GPU x G{GRPO_G}, prompt {GRPO_PROMPT}, "
+                       f"<= {GRPO_NEW} new tokens, T0.8 top_p0.95 top_k50, KL 0.04, clip 0.2")
+
+
 def main():
     args = parse()
     if args.model == "moe":
         use_moe()
+    elif args.model in ("dpo", "grpo"):
+        use_post_train(args.model)
     if args.impl == "reference":
         # the reference's own launcher initialises the process group (torchrun env)
         import torch
@@ -459,7 +661,15 @@ def main():
     if world != args.gpus and rank == 0:
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
     t0 = time.time()
-    res = run_reference(args, rank, world, local) if args.impl == "reference" else run_ours(args, rank, world, local)
+    if args.impl == "reference":
+        res = run_reference(args, rank, world, local) if MODEL in ("dense", "moe") else \
+            {"unavailable": f"reference arm for --model {MODEL} is not wired in this bench"}
+    elif MODEL == "dpo":
+        res = run_ours_dpo(args, rank, world, local)
+    elif MODEL == "grpo":
+        res = run_ours_grpo(args, rank, world, local)
+    else:
+        res = run_ours(args, rank, world, local)
     if rank == 0:
         if "unavailable" in res:
             print(json.dumps({"impl": "reference", "unavailable": res["unavailable"]}), flush=True)
@@ -484,7 +694,8 @@ def main():
                            else MODEL_DESC + " [reference: all 16 layers MoE, no aux loss]",
                            "global_batch": BATCH * ACCUM * world, "seq_len": SEQ, "parallelism": par,
                            "micro_batch": BATCH, "grad_accum": ACCUM,
-                           "optimizer": "Muon(0.02, ns5)+AdamW(1e-4, wd0.1), clip 1.0",
+                           "optimizer": "Muon(0.02, ns5)+AdamW(1e-4, wd0.1), clip 1.0"
+                           + (", Muon owner-sharded over ranks" if world > 1 and args.impl == "astrai_b200" else ""),
                            "l2": "no flush: per-step working set (2.4 GB weights + activations) >> 126 MB L2"},
                 "clocks": res.get("clocks"),
                 "e2e": res.get("e2e"),
@@ -492,6 +703,12 @@ def main():
                 "loss": res.get("loss"),
                 "wall_s": round(time.time() - t0, 1),
             }
+            if MODEL in ("dpo", "grpo"):
+                line["config"]["optimizer"] = "AdamW(5e-7), clip 1.0"
+                line["config"]["grad_accum"] = 1
+                line["e2e"] = None
+            if "grpo" in res:
+                line["grpo"] = res["grpo"]
             if args.impl == "reference":
                 line["impl"] = "reference"
             print(json.dumps(line), flush=True)

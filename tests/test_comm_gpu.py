@@ -114,6 +114,50 @@ def _timeout_worker(rank, world, port):
         dist.destroy_process_group()
 
 
+def _sharded_muon_worker(rank, world, port, out_path):
+    """Owner-sharded Muon (update applied to every rank's copy over NVLink) against the plain
+    replicated Muon run on the same gradients: equal parameters, identical on every rank."""
+    dist = _init(rank, world, port)
+    try:
+        from astrai_b200.ops._ext import native
+        from astrai_b200.optim import Muon
+
+        native().read_error()
+        shapes = [(256, 512)] * 3 + [(512, 256)] * 2 + [(128, 128)] + [(64, 192)]
+        torch.manual_seed(0)  # same initial weights and gradient stream on every rank
+        init = [torch.randn(s, device="cuda").to(torch.bfloat16) * 0.05 for s in shapes]
+        packed = torch.cat([init[0], init[1]])  # two packed views of one storage, as q/k/v are
+        a = [torch.nn.Parameter(packed[:256]), torch.nn.Parameter(packed[256:])] + \
+            [torch.nn.Parameter(t.clone()) for t in init[2:]]
+        b = [torch.nn.Parameter(t.clone()) for t in init]
+        kw = dict(lr=0.02, weight_decay=0.1, adjust_lr_fn="match_rms_adamw")
+        opt_a = Muon(a, shard=True, **kw)
+        opt_b = Muon(b, **kw)
+        for step in range(3):
+            for pa, pb in zip(a, b):
+                g = torch.randn(pa.shape, device="cuda").to(torch.bfloat16)
+                pa.grad, pb.grad = g.clone(), g.clone()
+            opt_a.step()
+            opt_b.step()
+        torch.cuda.synchronize()
+        assert native().read_error() == 0
+        assert opt_a._arena is not None and all(opt_a._arena.holds(p) for p in a)
+        assert a[1].data_ptr() == a[0].data_ptr() + a[0].numel() * 2, "packed views no longer adjacent"
+        for pa, pb in zip(a, b):
+            torch.testing.assert_close(pa.float(), pb.float(), atol=2e-3, rtol=2e-2)
+        flat = torch.cat([p.detach().reshape(-1) for p in a])
+        allv = [torch.empty_like(flat) for _ in range(world)]
+        dist.all_gather(allv, flat)
+        assert all(torch.equal(allv[0], v) for v in allv), "replicas differ across ranks"
+        owned = sum(1 for p in a if len(opt_a.state.get(p, {})) > 0)
+        counts = [torch.zeros(1, device="cuda") for _ in range(world)]
+        dist.all_gather(counts, torch.tensor([float(owned)], device="cuda"))
+        if rank == 0:
+            torch.save({"owned": [int(c) for c in counts]}, out_path)
+    finally:
+        dist.destroy_process_group()
+
+
 def _spawn(fn, world, *args):
     import torch.multiprocessing as mp
 
@@ -142,3 +186,10 @@ def test_ddp_fused_backend_matches_nccl(tmp_path):
 @need2
 def test_fused_allreduce_bounded_wait_reports_missing_peer():
     _spawn(_timeout_worker, 2)
+
+
+@need2
+def test_sharded_muon_matches_replicated(tmp_path):
+    _spawn(_sharded_muon_worker, 2, str(tmp_path / "owned.pt"))
+    owned = torch.load(tmp_path / "owned.pt")["owned"]
+    assert sum(owned) == 7 and all(n > 0 for n in owned)  # each matrix has exactly one owner

@@ -61,6 +61,30 @@ def test_gemm_tiles_and_epilogue(force_bn):
     assert rel_err(d32, gemm_reference(a, b)) < 5e-3
 
 
+@pytest.mark.parametrize("force_bn", [0, 128, 256, 512])
+@pytest.mark.parametrize("out_f32,with_c", [(False, False), (False, True), (True, False)])
+def test_gemm_canary_padding_untouched(force_bn, out_f32, with_c):
+    """Output written through a strided view of a larger canary-filled buffer: the kernel
+    must write exactly the M x N window (ragged M and N, every tile shape and epilogue)."""
+    from astrai_b200.ops._ext import native
+    from astrai_b200.ops.gemm import gemm_reference
+
+    torch.manual_seed(3)
+    M, N, K = 300, 200, 128
+    dt = torch.float32 if out_f32 else torch.bfloat16
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+    canary = 1234.5
+    big = torch.full((M + 7, N + 24), canary, device="cuda", dtype=dt)
+    d = big[:M, :N]
+    c = torch.randn(M, N, device="cuda", dtype=dt) if with_c else None
+    native().gemm(a, b, d, c, 0, 0, 1.0, 1.0 if with_c else 0.0, force_bn)
+    torch.cuda.synchronize()
+    assert (big[M:] == canary).all() and (big[:, N:] == canary).all(), "write outside the output window"
+    ref = gemm_reference(a, b, c=c.to(torch.bfloat16) if with_c else None, alpha=1.0, beta=1.0 if with_c else 0.0)
+    assert rel_err(d, ref) < 1e-2
+
+
 def test_gemm_batched():
     from astrai_b200.ops.gemm import gemm, gemm_reference
 
@@ -185,7 +209,8 @@ def test_embedding():
 
 
 @pytest.mark.parametrize("B,S,Hq,Hkv,causal", [(1, 128, 2, 1, True), (2, 256, 4, 2, True), (1, 200, 4, 4, True),
-                                                (2, 384, 8, 2, False), (1, 300, 2, 2, False)])
+                                                (2, 384, 8, 2, False), (1, 300, 2, 2, False),
+                                                (1, 1024, 8, 2, True)])
 def test_flash_attention(B, S, Hq, Hkv, causal):
     from astrai_b200.ops.attention import attention, attention_reference
 
