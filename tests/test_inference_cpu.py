@@ -256,3 +256,32 @@ def test_extension_api_reference_paths():
     vv = vc[table[:, pos // page], pos % page].permute(0, 2, 1, 3)
     torch.testing.assert_close(od, reference_attention(qd, kk, vv))
     assert attention(q[0, 0], k[0, 0], v[0, 0]).shape == (5, 16)
+
+
+def test_engine_concurrent_clients_match_sequential():
+    """Many threads submitting at once (continuous batching, more requests than batch slots):
+    every greedy result equals the single-request result, and the scheduler ends empty."""
+    import threading
+
+    from astrai_b200.inference import InferenceEngine
+
+    prompts = [f"{a} {a + 1} {a + 2}" for a in range(5, 17)]
+    with InferenceEngine(_model(), _Tok(), max_batch_size=3, max_seq_len=48) as eng:
+        solo = {p: eng.generate(p, max_tokens=4, temperature=0.0) for p in prompts}
+        got, errors = {}, []
+
+        def client(p):
+            try:
+                got[p] = eng.generate(p, max_tokens=4, temperature=0.0)
+            except Exception as e:  # pragma: no cover - reported below
+                errors.append(repr(e))
+
+        threads = [threading.Thread(target=client, args=(p,)) for p in prompts * 2]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join(timeout=120)
+        assert not errors and all(not t.is_alive() for t in threads)
+        assert got == solo
+        stats = eng.get_stats()
+        assert stats["active_tasks"] == 0 and stats["waiting_queue"] == 0
