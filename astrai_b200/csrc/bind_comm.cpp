@@ -72,7 +72,8 @@ void fused_allreduce(const at::Tensor& seg_ptr, const at::Tensor& seg_off, int64
 
 // Owner-sharded Muon: apply the orthogonalised update X (bf16 [batch][R][C], or [batch][C][R] when
 // transpose) to the parameters at pptr and store the result into every rank's copy (peer_base[q] + poff).
-void muon_apply_peers(const at::Tensor& pptr, const at::Tensor& poff, const at::Tensor& peer_base,
+void muon_apply_peers(const c10::optional<at::Tensor>& pptr, const c10::optional<at::Tensor>& poff,
+                      const at::Tensor& peer_base,
                       const c10::optional<at::Tensor>& X, int64_t batch, int64_t R, int64_t C, bool transpose,
                       double decay, double adj_lr, int64_t rank, int64_t world, int64_t flag_off, int64_t slot,
                       int64_t epoch, at::Tensor& done) {
@@ -84,15 +85,16 @@ void muon_apply_peers(const at::Tensor& pptr, const at::Tensor& poff, const at::
   const long long* pp = nullptr;
   const long long* po = nullptr;
   if (batch > 0) {
-    i64_check(pptr, "pptr");
-    i64_check(poff, "poff");
-    TORCH_CHECK(pptr.numel() == batch && poff.numel() == batch, "pptr / poff need one entry per matrix");
+    TORCH_CHECK(pptr.has_value() && poff.has_value(), "pptr / poff are required when batch > 0");
+    i64_check(*pptr, "pptr");
+    i64_check(*poff, "poff");
+    TORCH_CHECK(pptr->numel() == batch && poff->numel() == batch, "pptr / poff need one entry per matrix");
     TORCH_CHECK(X.has_value() && X->is_cuda() && X->scalar_type() == at::kBFloat16 && X->is_contiguous() &&
                     X->numel() == batch * R * C,
                 "X must be a contiguous CUDA bf16 [batch, R, C] (or [batch, C, R]) tensor");
     xp = X->data_ptr();
-    pp = reinterpret_cast<const long long*>(pptr.data_ptr<int64_t>());
-    po = reinterpret_cast<const long long*>(poff.data_ptr<int64_t>());
+    pp = reinterpret_cast<const long long*>(pptr->data_ptr<int64_t>());
+    po = reinterpret_cast<const long long*>(poff->data_ptr<int64_t>());
   }
   const c10::cuda::CUDAGuard g(done.device());
   astrai_host::muon_apply_peers(pp, po, reinterpret_cast<const long long*>(peer_base.data_ptr<int64_t>()), xp,
