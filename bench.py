@@ -51,6 +51,8 @@ MOE_CFG = dict(CFG, num_hidden_layers=16, max_position_embeddings=4096, ffn_type
 REF_MOE_CFG = dict(CFG, num_hidden_layers=16, max_position_embeddings=4096, ffn_type="moe", n_routed_experts=64,
                    n_shared_experts=2, n_activated_experts=6, intermediate_size=1408)
 MODEL = "dense"
+# owner-sharded Muon for N > 1 (each rank orthogonalises 1/N of the matrices, NVLink broadcast)
+SHARD_MUON = os.environ.get("ASTRAI_SHARD_MUON", "0") == "1"
 
 
 def use_moe():
@@ -194,7 +196,7 @@ def run_ours(args, rank, world, local):
     # world > 1: each rank orthogonalises 1/world of the hidden matrices and writes the updated
     # weights into every rank's copy over NVLink (owner-sharded Muon)
     opt = MuonMix(executor.unwrap(model), lr=MUON_LR, weight_decay=WD, adamw_lr=ADAMW_LR, adamw_weight_decay=WD,
-                  adjust_lr_fn="match_rms_adamw", shard_muon=world > 1)
+                  adjust_lr_fn="match_rms_adamw", shard_muon=SHARD_MUON and world > 1)
     V = CFG["vocab_size"]
     n_batches = 4
     data = torch.randint(0, V, (n_batches, ACCUM, BATCH, SEQ + 1), device=dev)
@@ -298,7 +300,7 @@ def run_ours_e2e(args, rank, world, local, model, executor, opt):
         strategy="seq",
         dataset=SynthSeq(total * ACCUM * BATCH * world, CFG["vocab_size"], SEQ, seed=11 + rank),
         optimizer_fn=lambda m: MuonMix(m, lr=MUON_LR, weight_decay=WD, adamw_lr=ADAMW_LR, adamw_weight_decay=WD,
-                                       adjust_lr_fn="match_rms_adamw", shard_muon=world > 1),
+                                       adjust_lr_fn="match_rms_adamw", shard_muon=SHARD_MUON and world > 1),
         scheduler_fn=lambda o: SchedulerFactory.create("cosine", o, warmup_steps=0, lr_decay_steps=10 ** 6),
         batch_per_device=BATCH, grad_accum_steps=ACCUM, max_grad_norm=CLIP, ckpt_dir=None, ckpt_interval=10 ** 9,
         log_dir=tempfile.mkdtemp(prefix="astrai_bench_logs_"), nprocs=world,
@@ -695,7 +697,8 @@ def main():
                            "global_batch": BATCH * ACCUM * world, "seq_len": SEQ, "parallelism": par,
                            "micro_batch": BATCH, "grad_accum": ACCUM,
                            "optimizer": "Muon(0.02, ns5)+AdamW(1e-4, wd0.1), clip 1.0"
-                           + (", Muon owner-sharded over ranks" if world > 1 and args.impl == "astrai_b200" else ""),
+                           + (", Muon owner-sharded over ranks"
+                              if SHARD_MUON and world > 1 and args.impl == "astrai_b200" else ""),
                            "l2": "no flush: per-step working set (2.4 GB weights + activations) >> 126 MB L2"},
                 "clocks": res.get("clocks"),
                 "e2e": res.get("e2e"),
