@@ -56,3 +56,39 @@ def test_reference_checkpoint_loads_and_matches(name, tmp_path):
     back = rmodel_mod.AutoModel.from_pretrained(str(tmp_path / "ours")).float().eval()
     with torch.no_grad():
         torch.testing.assert_close(back(ids)["logits"].float(), a, atol=1e-4, rtol=1e-4)
+
+
+def test_training_trajectory_matches_reference(tmp_path):
+    """BASELINE config 1 in one process: the same init, batches, AdamW(1e-4, wd 0.1), clip 1.0 and label
+    smoothing 0.05 give the reference's loss trajectory (fp32 CPU)."""
+    import torch.nn.functional as F
+
+    from astrai_b200.models import AutoModel
+    from astrai_b200.ops.loss import cross_entropy
+    from astrai_b200.optim import FusedAdamW
+
+    rcfg_mod, rmodel_mod = _ref()
+    kw = dict(vocab_size=1024, hidden_size=256, num_attention_heads=8, num_key_value_heads=2, intermediate_size=688,
+              max_position_embeddings=128, num_hidden_layers=4, rms_norm_eps=1e-5, rope_theta=10000.0,
+              tie_word_embeddings=True)
+    torch.manual_seed(3407)
+    ref = rmodel_mod.AutoRegressiveLM(rcfg_mod.AutoRegressiveLMConfig(**kw)).float().train()
+    ref.save_pretrained(str(tmp_path / "init"))
+    ours = AutoModel.from_pretrained(str(tmp_path / "init")).float().train()
+    opt_r = torch.optim.AdamW(ref.parameters(), lr=1e-4, weight_decay=0.1)
+    opt_o = FusedAdamW(ours.parameters(), lr=1e-4, weight_decay=0.1)
+    g = torch.Generator().manual_seed(3407)
+    lr_, lo_ = [], []
+    for _ in range(6):
+        x = torch.randint(0, 1024, (2, 129), generator=g)
+        lr = F.cross_entropy(ref(x[:, :-1])["logits"].reshape(-1, 1024).float(), x[:, 1:].reshape(-1),
+                             label_smoothing=0.05)
+        lo = cross_entropy(ours(x[:, :-1])["logits"], x[:, 1:], label_smoothing=0.05)
+        for m, loss, opt in ((ref, lr, opt_r), (ours, lo, opt_o)):
+            opt.zero_grad()
+            loss.backward()
+            torch.nn.utils.clip_grad_norm_(m.parameters(), 1.0)
+            opt.step()
+        lr_.append(lr.item())
+        lo_.append(lo.item())
+    assert max(abs(a - b) for a, b in zip(lr_, lo_)) < 1e-4, (lr_, lo_)
