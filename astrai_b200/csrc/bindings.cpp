@@ -27,7 +27,7 @@ void rmsnorm_bwd(const void* dy, long long lddy, const void* x, long long ldx, c
                  void* dx, long long lddx, void* dw_bf16, float* dw_f32, float* scratch, int rows, int D,
                  cudaStream_t s);
 void rope_apply(void* x, long long ld, int rows, int col0, int n_heads, int head_dim, const int* pos, int seq_len,
-                const void* cs, int inverse, int rot_dim, int rot_off, cudaStream_t s);
+                const void* cs, int inverse, int rot_dim, int rot_off, int max_pos, cudaStream_t s);
 void swiglu_fwd(const void* h, long long ldh, void* out, long long ldo, int rows, int F, cudaStream_t s);
 void swiglu_bwd(const void* dy, long long lddy, const void* h, long long ldh, void* dh, long long lddh, int rows, int F,
                 cudaStream_t s);
@@ -192,9 +192,12 @@ void rope_(at::Tensor& x, int64_t col0, int64_t n_heads, int64_t head_dim, const
     TORCH_CHECK(pos->scalar_type() == at::kInt && pos->is_contiguous() && pos->numel() == x.size(0), "positions");
     p = pos->data_ptr<int>();
   }
+  const int64_t max_pos = cs.numel() / rot_dim;  // [max_pos][rot_dim / 2] (cos, sin) pairs
+  TORCH_CHECK(p != nullptr || seq_len <= max_pos, "rope: sequence longer than the position table");
   c10::cuda::CUDAGuard g(x.device());
   astrai_host::rope_apply(x.data_ptr(), x.stride(0), (int)x.size(0), (int)col0, (int)n_heads, (int)head_dim, p,
-                          (int)seq_len, cs.data_ptr(), inverse ? 1 : 0, (int)rot_dim, (int)rot_off, stream());
+                          (int)seq_len, cs.data_ptr(), inverse ? 1 : 0, (int)rot_dim, (int)rot_off, (int)max_pos,
+                          stream());
 }
 
 void swiglu_fwd(const at::Tensor& h, at::Tensor& out) {

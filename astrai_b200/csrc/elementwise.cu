@@ -14,9 +14,10 @@ namespace astrai {
 
 // x: [rows, ld] bf16; heads occupy columns [col0, col0 + n_heads*head_dim).
 // pos: per-row position (nullable -> row % seq_len). cs: float2 [max_pos][head_dim/2].
+// A position outside [0, max_pos) records kErrBadArg and leaves the chunk unrotated (no table read).
 __global__ void rope_kernel(__nv_bfloat16* __restrict__ x, long long ld, int rows, int col0, int n_heads, int head_dim,
                             const int* __restrict__ pos, int seq_len, const float2* __restrict__ cs, float sign,
-                            int rot_dim, int rot_off) {
+                            int rot_dim, int rot_off, int max_pos, int* err) {
   // each thread handles 8 consecutive elements (4 pairs) of one head
   const int per_head = rot_dim / 8;
   const long long total = (long long)rows * n_heads * per_head;
@@ -27,6 +28,10 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ x, long long ld, int row
     const int h = t % n_heads;
     const int row = t / n_heads;
     const int p = pos ? pos[row] : row % seq_len;
+    if (p < 0 || p >= max_pos) {
+      set_error(err, kErrBadArg);
+      continue;
+    }
     __nv_bfloat16* ptr = x + (long long)row * ld + col0 + h * head_dim + rot_off + chunk * 8;
     uint4 u = *reinterpret_cast<uint4*>(ptr);
     uint32_t w[4] = {u.x, u.y, u.z, u.w};
@@ -172,11 +177,13 @@ static inline int ew_grid(long long work) {
 }
 
 void rope_apply(void* x, long long ld, int rows, int col0, int n_heads, int head_dim, const int* pos, int seq_len,
-                const void* cs, int inverse, int rot_dim, int rot_off, cudaStream_t s) {
+                const void* cs, int inverse, int rot_dim, int rot_off, int max_pos, cudaStream_t s) {
   const long long work = (long long)rows * n_heads * (rot_dim / 8);
+  int dev = 0;
+  cudaGetDevice(&dev);
   (astrai::note_launch(), rope_kernel<<<ew_grid(work), 256, 0, s>>>(static_cast<__nv_bfloat16*>(x), ld, rows, col0, n_heads, head_dim, pos,
                                             seq_len, static_cast<const float2*>(cs), inverse ? -1.f : 1.f, rot_dim,
-                                            rot_off));
+                                            rot_off, max_pos, error_word(dev)));
 }
 
 void swiglu_fwd(const void* h, long long ldh, void* out, long long ldo, int rows, int F, cudaStream_t s) {
