@@ -337,6 +337,9 @@ def run_reference(args, rank, world, local):
 
     assert os.path.realpath(astrai.__file__).startswith(os.path.realpath(ref_path))
     total_steps = args.warmup + args.steps + 1
+    if MODEL == "dpo":
+        return _run_reference_dpo(args, rank, world, total_steps, Dataset, AutoRegressiveLMConfig, TrainConfig,
+                                  AutoRegressiveLM, SchedulerFactory, Trainer, TrainCallback)
     n_samples = total_steps * ACCUM * BATCH * world
 
     class SynthSeq(Dataset):
@@ -630,6 +633,76 @@ def run_ours_grpo(args, rank, world, local):
                      "rollout": f"{GRPO_PROMPTS_PER_GPU} prompts x G{GRPO_G} per GPU, paged KV + CUDA-graph decode"}}
 
 
+def _run_reference_dpo(args, rank, world, total_steps, Dataset, AutoRegressiveLMConfig, TrainConfig,
+                       AutoRegressiveLM, SchedulerFactory, Trainer, TrainCallback):
+    """BASELINE config 4 through the reference's own Trainer and DPO strategy (its dense masks,
+    its frozen reference copy); torch fused AdamW(5e-7), FSDP2 for N > 1."""
+    import torch
+
+    L = DPO_PROMPT + DPO_RESP
+
+    class SynthDPO(Dataset):
+        def __init__(self, n):
+            g = torch.Generator().manual_seed(11)
+            V = CFG["vocab_size"]
+            self.c = torch.randint(1, V, (n, L), generator=g)
+            self.r = torch.randint(1, V, (n, L), generator=g)
+            self.m = torch.zeros(L, dtype=torch.bool)
+            self.m[DPO_PROMPT:] = True
+
+        def __len__(self):
+            return self.c.shape[0]
+
+        def __getitem__(self, i):
+            return {"chosen": self.c[i], "rejected": self.r[i], "chosen_mask": self.m, "rejected_mask": self.m}
+
+    timing = {}
+
+    class Timer(TrainCallback):
+        def __init__(self):
+            self.n = 0
+            self.ev = {}
+            self.clocks = ClockSampler(rank == 0)
+
+        def on_optimizer_step(self, ctx):
+            if self.n == args.warmup:
+                barrier()
+                self.clocks.start()
+                self.ev["s"] = torch.cuda.Event(enable_timing=True)
+                self.ev["s"].record()
+            if self.n == args.warmup + args.steps:
+                self.ev["e"] = torch.cuda.Event(enable_timing=True)
+                self.ev["e"].record()
+                barrier()
+                timing["clocks"] = self.clocks.stop(visible_gpu_indices(world))
+                timing["ms"] = max_over_ranks(self.ev["s"].elapsed_time(self.ev["e"])) / args.steps
+            self.n += 1
+
+    cfg = AutoRegressiveLMConfig(**CFG)
+    shm = "/dev/shm" if os.path.isdir("/dev/shm") else None
+    tmp = tempfile.mkdtemp(prefix="astrai_ref_dpo_", dir=shm)
+    tc = TrainConfig(
+        model_fn=lambda: AutoRegressiveLM(cfg).to(dtype=torch.bfloat16), strategy="dpo",
+        dataset=SynthDPO(total_steps * DPO_PAIRS * world),
+        optimizer_fn=lambda m: torch.optim.AdamW(m.parameters(), lr=DPO_LR, weight_decay=0.0, fused=True),
+        scheduler_fn=lambda o: SchedulerFactory.create("cosine", o, warmup_steps=0, lr_decay_steps=10 ** 6),
+        n_epoch=1, batch_per_device=DPO_PAIRS, grad_accum_steps=1, max_grad_norm=CLIP,
+        ckpt_dir=os.path.join(tmp, "ckpt"), ckpt_interval=10 ** 9, log_dir=os.path.join(tmp, "logs"), nprocs=world,
+        backend="nccl", parallel_mode="fsdp2" if world > 1 else "none", device_type="cuda", pin_memory=True,
+        extra_kwargs={"beta": DPO_BETA})
+    try:
+        Trainer(tc, callbacks=[Timer()]).train()
+    finally:
+        import shutil
+
+        shutil.rmtree(tmp, ignore_errors=True)
+    if "ms" not in timing:
+        return {"unavailable": "reference DPO run ended before the timed steps completed"}
+    ms = timing["ms"]
+    return {"ms_per_step": ms, "value": world * 2 * DPO_PAIRS * L / (ms / 1e3), "clocks": timing.get("clocks"),
+            "gpu_launches": None}
+
+
 # ----------------------------------------------------------------------------- main
 def use_post_train(kind):
     global MODEL_DESC, METRIC, MODEL, BATCH, SEQ, ACCUM
@@ -664,7 +737,7 @@ def main():
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
     t0 = time.time()
     if args.impl == "reference":
-        res = run_reference(args, rank, world, local) if MODEL in ("dense", "moe") else \
+        res = run_reference(args, rank, world, local) if MODEL in ("dense", "moe", "dpo") else \
             {"unavailable": f"reference arm for --model {MODEL} is not wired in this bench"}
     elif MODEL == "dpo":
         res = run_ours_dpo(args, rank, world, local)
