@@ -109,7 +109,8 @@ __device__ __forceinline__ float exp2_fma(float x) {
   return x < -127.f ? 0.f : y;
 }
 // of every 16 exponential pairs in the forward softmax, this many go to exp2_fma
-constexpr int FA_EMU_PAIRS = 7;
+// (7 of 16 measured no faster than MUFU only at B4 S2048 H16/4: the softmax is not MUFU-bound)
+constexpr int FA_EMU_PAIRS = 0;
 
 __global__ void __launch_bounds__(192, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -414,9 +415,16 @@ struct FlashBwdParams {
 // Query tile of the backward pass (keys per CTA stay 128).
 constexpr int FB_BM = 64;
 constexpr int FB_QT = 64 * 64 * 2;  // one 64-row x 64-col swizzled chunk (8 KB)
-// smem: K(2 chunks) V(2) | Q ring 2 x 2 chunks(8K) | dO ring 2 x 2 | P^T 2 x [128x64] | dS^T 2 x [128x64]
+// smem: K(2 chunks) V(2) | Q ring FB_QD x 2 chunks(8K) | dO ring FB_QD x 2 | P^T [128x64] | dS^T [128x64]
+// | lse / delta ring | dQ staging. The Q/dO ring is 3 deep so the loads of a query tile are issued one
+// tile earlier than a 2-deep ring allows (a slot frees only when the gradient MMAs of its tile finish,
+// which follow that tile's softmax); P^T / dS^T have one slot, which the softmax of tile t fills only
+// after the MMAs of tile t-1 read it (its own math overlaps those MMAs). Total: exactly 227 KB.
+constexpr int FB_QD = 3;
 constexpr int FB_DQ_BYTES = 64 * 128 * 4;  // fp32 dQ staging tile [64 q][128 d]
-constexpr int FA_BWD_SMEM = 4 * FA_TILE + 8 * FB_QT + 4 * FA_TILE + 2 * 2 * 64 * 4 + FB_DQ_BYTES + 1024 + 512;
+constexpr int FA_BWD_SMEM =
+    4 * FA_TILE + 2 * FB_QD * 2 * FB_QT + 2 * FA_TILE + 2 * FB_QD * 64 * 4 + FB_DQ_BYTES + 1024 + 512;
+static_assert(FA_BWD_SMEM <= 227 * 1024, "flash backward exceeds the shared memory of one CTA");
 constexpr int FB_THREADS = 320;
 
 __global__ void __launch_bounds__(FB_THREADS, 1)
@@ -427,27 +435,27 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;                   // 2 chunks [128 keys][64 d]
   uint8_t* sV = sK + 2 * FA_TILE;       // 2 chunks
-  uint8_t* sQ = sV + 2 * FA_TILE;       // [2 slots][2 chunks][64 q][64 d]
-  uint8_t* sdO = sQ + 4 * FB_QT;        // same
-  uint8_t* sP = sdO + 4 * FB_QT;        // [2 slots][128 keys][64 q]
-  uint8_t* sdS = sP + 2 * FA_TILE;      // [2 slots][128 keys][64 q]
-  float* sLse = reinterpret_cast<float*>(sdS + 2 * FA_TILE);  // [2][64] log2 units
-  float* sDelta = sLse + 128;                                  // [2][64]
-  float* sdQ = sDelta + 128;                                   // [64][128] fp32 staging
+  uint8_t* sQ = sV + 2 * FA_TILE;              // [FB_QD slots][2 chunks][64 q][64 d]
+  uint8_t* sdO = sQ + FB_QD * 2 * FB_QT;       // same
+  uint8_t* sP = sdO + FB_QD * 2 * FB_QT;       // [128 keys][64 q]
+  uint8_t* sdS = sP + FA_TILE;                 // [128 keys][64 q]
+  float* sLse = reinterpret_cast<float*>(sdS + FA_TILE);  // [FB_QD][64] log2 units
+  float* sDelta = sLse + FB_QD * 64;                       // [FB_QD][64]
+  float* sdQ = sDelta + FB_QD * 64;                        // [64][128] fp32 staging
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sdQ) + FB_DQ_BYTES);
   // TMEM: two score buffers of 128 columns (S^T in the first 64, dP^T in the
   // next 64), dV at 256, dK at 384. Iteration `it` uses buffer it & 1; its dQ^T
   // (64 columns) is written over its own S^T once the softmax has read it, and
   // the buffer is free again when the dQ warps have drained dQ^T. So the S/dP
   // MMAs of the next query tile run while this tile's softmax works.
-  uint64_t* kv_full = bars;          // K, V loaded
-  uint64_t* qd_full = bars + 1;      // [2] Q/dO slot loaded (+ stats written)
-  uint64_t* qd_empty = bars + 3;     // [2] dV/dK MMAs done with the slot
-  uint64_t* sd_full = bars + 5;      // [2] S^T and dP^T of buffer i in TMEM
-  uint64_t* ps_ready = bars + 7;     // [2] P^T/dS^T in smem slot i, buffer i read (4 warps)
-  uint64_t* dq_full = bars + 9;      // [2] dQ^T in buffer i; all MMAs of the iteration done
-  uint64_t* dq_free = bars + 11;     // [2] dQ^T of buffer i read out (4 warps)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* kv_full = bars;                   // K, V loaded
+  uint64_t* qd_full = bars + 1;               // [FB_QD] Q/dO slot loaded (+ stats written)
+  uint64_t* qd_empty = qd_full + FB_QD;       // [FB_QD] dV/dK MMAs done with the slot
+  uint64_t* sd_full = qd_empty + FB_QD;       // [2] S^T and dP^T of buffer i in TMEM
+  uint64_t* ps_ready = sd_full + 2;           // [2] P^T/dS^T of tile t in smem, buffer t & 1 read (4 warps)
+  uint64_t* dq_full = ps_ready + 2;           // [2] dQ^T in buffer i; all MMAs of the tile done
+  uint64_t* dq_free = dq_full + 2;            // [2] dQ^T of buffer i read out (4 warps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dq_free + 2);
 
   const int warp = warp_id(), lane = lane_id();
   // 1-D grid in longest-first order: with a causal mask key block 0 sees every
@@ -466,9 +474,11 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < FB_QD; ++i) {
       mbar_init(&qd_full[i], 1);
       mbar_init(&qd_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&dq_full[i], 1);
       mbar_init(&sd_full[i], 1);
       mbar_init(&ps_ready[i], 4);
@@ -494,12 +504,14 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
       tma_load_3d(sV + FA_TILE, &tmV, kv_full, p.v_col0 + hk * FA_D + 64, n0, b);
     }
     for (int it = 0; it < iters; ++it) {
-      const int slot = it & 1;
+      const int slot = it % FB_QD;
       const int h = hk * G + it / per_head;
       const int m0 = (mb_first + it % per_head) * FB_BM;
-      // slot reuse: qd_empty(it-2) follows the dV/dK MMAs of it-2, which were
-      // issued after the softmax of it-2 (the stats reader) arrived on ps_ready
-      if (lane == 0 && it >= 2 && !mbar_wait(&qd_empty[slot], ((it - 2) >> 1) & 1, p.err, kErrWaitEmpty)) break;
+      // slot reuse: qd_empty(it - FB_QD) follows the dV/dK MMAs of that tile, which were
+      // issued after its softmax (the stats reader) arrived on ps_ready
+      if (lane == 0 && it >= FB_QD &&
+          !mbar_wait(&qd_empty[slot], ((it / FB_QD) - 1) & 1, p.err, kErrWaitEmpty))
+        break;
       if (lane == 0) {
         mbar_expect_tx(&qd_full[slot], 4 * FB_QT + 2 * 64 * 4);
         const long long so = ((long long)b * p.Hq + h) * p.Sq_pad + m0;
@@ -524,9 +536,9 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
       const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV);
       auto issue_grads = [&](int it) -> bool {
         // dV += P^T dO ; dK += dS^T Q   (M = keys, N = d, K = 64 queries)
-        const int slot = it & 1;
-        const uint32_t q_base = smem_u32(sQ + slot * 2 * FB_QT), do_base = smem_u32(sdO + slot * 2 * FB_QT);
-        const uint32_t p_base = smem_u32(sP + slot * FA_TILE), ds_base = smem_u32(sdS + slot * FA_TILE);
+        const int slot = it & 1, qs = it % FB_QD;
+        const uint32_t q_base = smem_u32(sQ + qs * 2 * FB_QT), do_base = smem_u32(sdO + qs * 2 * FB_QT);
+        const uint32_t p_base = smem_u32(sP), ds_base = smem_u32(sdS);
 #pragma unroll
         for (int k = 0; k < FB_BM / 16; ++k) {
           umma_bf16(tdV, sdesc_sw128(p_base + k * 32, 16, 1024), sdesc_sw128(do_base + k * 2048, FB_QT, 1024), idGR,
@@ -534,7 +546,7 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
           umma_bf16(tdK, sdesc_sw128(ds_base + k * 32, 16, 1024), sdesc_sw128(q_base + k * 2048, FB_QT, 1024), idGR,
                     (it | k) != 0);
         }
-        umma_commit(&qd_empty[slot]);
+        umma_commit(&qd_empty[qs]);
         // dQ^T = K^T dS^T  (M = d, N = 64 queries, K = 128 keys) over this iteration's S^T,
         // which the softmax has read (ps_ready waited by the caller)
 #pragma unroll
@@ -545,13 +557,13 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
         return true;
       };
       for (int it = 0; it < iters && ok; ++it) {
-        const int slot = it & 1;
-        ok = mbar_wait(&qd_full[slot], (it >> 1) & 1, p.err, kErrWaitFull);
+        const int slot = it & 1, qs = it % FB_QD;
+        ok = mbar_wait(&qd_full[qs], (it / FB_QD) & 1, p.err, kErrWaitFull);
         // buffer `slot` is free once the dQ^T of it-2 (written over its S^T) was drained
         if (ok && it >= 2) ok = mbar_wait(&dq_free[slot], ((it - 2) >> 1) & 1, p.err, kErrWaitAccEmpty);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t q_base = smem_u32(sQ + slot * 2 * FB_QT), do_base = smem_u32(sdO + slot * 2 * FB_QT);
+        const uint32_t q_base = smem_u32(sQ + qs * 2 * FB_QT), do_base = smem_u32(sdO + qs * 2 * FB_QT);
         const uint32_t tS = tmem + slot * 128, tdP = tS + 64;
         // S^T = K Q^T ; dP^T = V dO^T   (M = 128 keys, N = 64 queries, K = d)
 #pragma unroll
@@ -585,12 +597,10 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
     const int seg_k = (p.seg && ki < p.Sk) ? p.seg[(long long)b * p.Sk + ki] : 0;
     bool ok = true;
     for (int it = 0; it < iters; ++it) {
-      const int slot = it & 1;
+      const int slot = it & 1, qs = it % FB_QD;
       const int m0 = (mb_first + it % per_head) * FB_BM;
       ok = mbar_wait(&sd_full[slot], (it >> 1) & 1, p.err, kErrWaitAccFull) &&
-           mbar_wait(&qd_full[slot], (it >> 1) & 1, p.err, kErrWaitAccFull);
-      // the P^T/dS^T slot was last read by the MMAs of it-2
-      if (ok && it >= 2) ok = mbar_wait(&dq_full[slot], ((it - 2) >> 1) & 1, p.err, kErrWaitAccFull);
+           mbar_wait(&qd_full[qs], (it / FB_QD) & 1, p.err, kErrWaitAccFull);
       if (!ok) break;
       tc_fence_after();
       // visible query columns of this key row, as a 64-bit mask
@@ -607,8 +617,8 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
           }
         }
       }
-      const uint32_t lse_a = smem_u32(sLse + slot * 64), dlt_a = smem_u32(sDelta + slot * 64);
-      const uint32_t pc = smem_u32(sP + slot * FA_TILE), dc = smem_u32(sdS + slot * FA_TILE);
+      const uint32_t lse_a = smem_u32(sLse + qs * 64), dlt_a = smem_u32(sDelta + qs * 64);
+      const uint32_t pc = smem_u32(sP), dc = smem_u32(sdS);
       uint32_t sv[64], dpv[64];
       const uint32_t tS = tmem + slot * 128, tdP = tS + 64;
 #pragma unroll
@@ -617,6 +627,7 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
         tmem_ld32(tdP + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&dpv[c * 32]));
       }
       tmem_wait_ld();
+      uint32_t pk[2][16], dk[2][16];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const uint32_t* s = &sv[c * 32];
@@ -627,7 +638,6 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
           ld_shared_v4f(lse_a + (c * 32 + 4 * j) * 4, lse2[4 * j], lse2[4 * j + 1], lse2[4 * j + 2], lse2[4 * j + 3]);
           ld_shared_v4f(dlt_a + (c * 32 + 4 * j) * 4, dlt[4 * j], dlt[4 * j + 1], dlt[4 * j + 2], dlt[4 * j + 3]);
         }
-        uint32_t pk[16], dk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           float pv[2], dsv[2];
@@ -639,13 +649,22 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
             pv[e] = pr;
             dsv[e] = pr * (__uint_as_float(dp[2 * i + e]) - dlt[2 * i + e]) * p.scale;
           }
-          pk[i] = pack_bf16(pv[0], pv[1]);
-          dk[i] = pack_bf16(dsv[0], dsv[1]);
+          pk[c][i] = pack_bf16(pv[0], pv[1]);
+          dk[c][i] = pack_bf16(dsv[0], dsv[1]);
         }
+      }
+      // the single P^T/dS^T slot was last read by the MMAs of it-1 (issued when its softmax
+      // arrived on ps_ready): wait only now, so this tile's math overlapped those MMAs
+      if (it >= 1 && !mbar_wait(&dq_full[(it - 1) & 1], ((it - 1) >> 1) & 1, p.err, kErrWaitAccFull)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
-          st_shared_v4(swz(pc, r, c * 4 + g), pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
-          st_shared_v4(swz(dc, r, c * 4 + g), dk[4 * g], dk[4 * g + 1], dk[4 * g + 2], dk[4 * g + 3]);
+          st_shared_v4(swz(pc, r, c * 4 + g), pk[c][4 * g], pk[c][4 * g + 1], pk[c][4 * g + 2], pk[c][4 * g + 3]);
+          st_shared_v4(swz(dc, r, c * 4 + g), dk[c][4 * g], dk[c][4 * g + 1], dk[c][4 * g + 2], dk[c][4 * g + 3]);
         }
       }
       fence_async_smem();
