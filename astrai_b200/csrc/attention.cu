@@ -23,6 +23,7 @@
 //   dQ_part = dS K -> fp32 atomics into a dQ accumulator.
 // All waits are time-bounded (common.cuh).
 #include <cfloat>
+#include <stdexcept>
 
 #include "common.cuh"
 
@@ -755,41 +756,49 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
   }
 }
 
-// Backward preprocessing, one warp per (row, head):
+// Backward preprocessing, one warp per query row (all heads of the row):
 //   delta[b, h, s] = sum_d dO[b*S+s, h*D+d] * O[b*S+s, h*D+d]
 //   lse2[b, h, s]  = lse * log2(e)  (+inf for empty rows)
 // Both arrays are padded to Sq_pad (lse2 = +inf, delta = 0 in the padding) so
-// the main kernel fetches whole 64-query tiles with bulk copies.
+// the main kernel fetches whole 64-query tiles with bulk copies. Each lane
+// loads 16-byte vectors; 16 lanes cover one 128-wide head, so a warp reduces
+// two heads per step with 4 shuffles.
 __global__ void flash_bwd_pre_kernel(const __nv_bfloat16* __restrict__ dO, long long ld_do, int do_col0,
                                      const __nv_bfloat16* __restrict__ O, long long ldo,
                                      const float* __restrict__ lse, float* __restrict__ lse2,
                                      float* __restrict__ delta, int B, int S, int S_pad, int H) {
   const long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (w >= (long long)B * S_pad * H) return;
-  const int h = w % H;
-  const long long t = w / H;
-  const int b = t / S_pad, si = t % S_pad;
-  const long long out = ((long long)b * H + h) * S_pad + si;
-  if (si >= S) {
-    if (lane == 0) {
-      delta[out] = 0.f;
-      lse2[out] = INFINITY;
+  if (w >= (long long)B * S_pad) return;
+  const int b = (int)(w / S_pad), si = (int)(w % S_pad);
+  const int half = lane >> 4, sub = lane & 15;
+  for (int h0 = 0; h0 < H; h0 += 2) {
+    const int h = h0 + half;
+    float sum = 0.f;
+    if (si < S && h < H) {
+      const long long row = (long long)b * S + si;
+      const uint4 ua = *reinterpret_cast<const uint4*>(dO + row * ld_do + do_col0 + h * FA_D + sub * 8);
+      const uint4 uo = *reinterpret_cast<const uint4*>(O + row * ldo + h * FA_D + sub * 8);
+      const uint32_t a4[4] = {ua.x, ua.y, ua.z, ua.w}, o4[4] = {uo.x, uo.y, uo.z, uo.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 a = unpack_bf16(a4[j]), o = unpack_bf16(o4[j]);
+        sum = fmaf(a.x, o.x, fmaf(a.y, o.y, sum));
+      }
     }
-    return;
-  }
-  const long long row = (long long)b * S + si;
-  const __nv_bfloat16* a = dO + row * ld_do + do_col0 + h * FA_D + lane * 4;
-  const __nv_bfloat16* o = O + row * ldo + h * FA_D + lane * 4;
-  const uint2 ua = *reinterpret_cast<const uint2*>(a);
-  const uint2 uo = *reinterpret_cast<const uint2*>(o);
-  const float2 a0 = unpack_bf16(ua.x), a1 = unpack_bf16(ua.y), o0 = unpack_bf16(uo.x), o1 = unpack_bf16(uo.y);
-  float sum = a0.x * o0.x + a0.y * o0.y + a1.x * o1.x + a1.y * o1.y;
-  sum = warp_sum(sum);
-  if (lane == 0) {
-    delta[out] = sum;
-    const float ls = lse[((long long)b * H + h) * S + si];
-    lse2[out] = (ls == -INFINITY) ? INFINITY : ls * 1.4426950408889634f;
+#pragma unroll
+    for (int off = 8; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffff, sum, off);
+    if (sub == 0 && h < H) {
+      const long long out = ((long long)b * H + h) * S_pad + si;
+      if (si >= S) {
+        delta[out] = 0.f;
+        lse2[out] = INFINITY;
+      } else {
+        delta[out] = sum;
+        const float ls = lse[((long long)b * H + h) * S + si];
+        lse2[out] = (ls == -INFINITY) ? INFINITY : ls * 1.4426950408889634f;
+      }
+    }
   }
 }
 
@@ -860,10 +869,13 @@ void flash_bwd(const void* q, long long ldq, int q_col0, const void* k, long lon
                void* dv, long long ld_dkv, int dk_col0, int dv_col0, int B, int Sq, int Sk, int Hq, int Hkv,
                float scale, int causal, const int* seg, cudaStream_t s) {
   // 1) delta = rowsum(dO * O), lse2 = lse * log2(e); both padded to 64-query tiles
+  if (ld_do % 8 || do_col0 % 8 || ldo % 8 || reinterpret_cast<uintptr_t>(dO) % 16 ||
+      reinterpret_cast<uintptr_t>(o) % 16)
+    throw std::runtime_error("flash_bwd: dO / O need 16-byte aligned rows");
   const int Sq_pad = (Sq + FB_BM - 1) / FB_BM * FB_BM;
   float* lse2 = delta + (long long)B * Hq * Sq_pad;
   {
-    const long long warps = (long long)B * Sq_pad * Hq;
+    const long long warps = (long long)B * Sq_pad;  // one warp per query row
     const int blocks = (int)((warps * 32 + 255) / 256);
     (astrai::note_launch(), flash_bwd_pre_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(dO), ld_do, do_col0,
                                                 static_cast<const __nv_bfloat16*>(o), ldo, lse, lse2, delta, B, Sq,

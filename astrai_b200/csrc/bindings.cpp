@@ -25,7 +25,7 @@ void rmsnorm_fwd(const void* x, long long ldx, const void* w, void* y, long long
 long long rmsnorm_bwd_scratch(int rows, int D, int* nblocks_out);
 void rmsnorm_bwd(const void* dy, long long lddy, const void* x, long long ldx, const void* w, const float* rstd,
                  void* dx, long long lddx, void* dw_bf16, float* dw_f32, float* scratch, int rows, int D,
-                 cudaStream_t s);
+                 cudaStream_t s, const void* dres = nullptr, long long ldres = 0);
 void rope_apply(void* x, long long ld, int rows, int col0, int n_heads, int head_dim, const int* pos, int seq_len,
                 const void* cs, int inverse, int rot_dim, int rot_off, int max_pos, cudaStream_t s);
 void swiglu_fwd(const void* h, long long ldh, void* out, long long ldo, int rows, int F, cudaStream_t s);
@@ -161,8 +161,9 @@ void rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, c10::o
 
 int64_t rmsnorm_bwd_scratch(int64_t rows, int64_t D) { return astrai_host::rmsnorm_bwd_scratch((int)rows, (int)D, nullptr); }
 
+// dres (optional): gradient of a second use of x (the residual branch), added into dx by the kernel.
 void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w, const at::Tensor& rstd, at::Tensor& dx,
-                 at::Tensor& dw, at::Tensor& scratch) {
+                 at::Tensor& dw, at::Tensor& scratch, const c10::optional<at::Tensor>& dres) {
   check_bf16(dy, "dy");
   check_bf16(x, "x");
   check_bf16(dx, "dx");
@@ -172,12 +173,21 @@ void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
   const int D = (int)x.size(1);
   TORCH_CHECK(D % 8 == 0 && D <= 4096, "rmsnorm_bwd: D must be a multiple of 8 and at most 4096");
   TORCH_CHECK(scratch.scalar_type() == at::kFloat && scratch.numel() >= rmsnorm_bwd_scratch(x.size(0), D), "scratch");
+  const void* dr = nullptr;
+  long long ldr = 0;
+  if (dres.has_value() && dres->defined()) {
+    check_bf16(*dres, "dres");
+    check_rows(*dres, "dres");
+    TORCH_CHECK(dres->sizes() == x.sizes(), "rmsnorm_bwd: dres must have the shape of x");
+    dr = dres->data_ptr();
+    ldr = dres->stride(0);
+  }
   c10::cuda::CUDAGuard g(x.device());
   astrai_host::rmsnorm_bwd(dy.data_ptr(), dy.stride(0), x.data_ptr(), x.stride(0), w.data_ptr(),
                            rstd.data_ptr<float>(), dx.data_ptr(), dx.stride(0),
                            dw.scalar_type() == at::kBFloat16 ? dw.data_ptr() : nullptr,
                            dw.scalar_type() == at::kFloat ? dw.data_ptr<float>() : nullptr, scratch.data_ptr<float>(),
-                           (int)x.size(0), D, stream());
+                           (int)x.size(0), D, stream(), dr, ldr);
 }
 
 // ----------------------------------------------------------------- RoPE / SwiGLU / embedding
@@ -360,7 +370,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("force_bn") = 0);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd_scratch", &rmsnorm_bwd_scratch);
-  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"), py::arg("dx"),
+        py::arg("dw"), py::arg("scratch"), py::arg("dres") = py::none());
   m.def("rope_", &rope_);
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("swiglu_bwd", &swiglu_bwd);

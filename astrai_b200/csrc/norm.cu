@@ -95,6 +95,7 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const __nv_bfloat16* _
                                                           const __nv_bfloat16* __restrict__ w,
                                                           const float* __restrict__ rstd,
                                                           __nv_bfloat16* __restrict__ dx, long long lddx,
+                                                          const __nv_bfloat16* __restrict__ dres, long long ldres,
                                                           float* __restrict__ dw_part, int rows, int D,
                                                           int rows_per_block) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -156,11 +157,22 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const __nv_bfloat16* _
     for (int c = 0; c < CHUNKS; ++c) {
       const int col = (c * 32 + lane) * 8;
       if (col < D) {
+        float add[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (dres) {  // gradient of the residual branch that also reads x
+          const uint4 ru = *reinterpret_cast<const uint4*>(dres + (long long)row * ldres + col);
+          const uint32_t rr[4] = {ru.x, ru.y, ru.z, ru.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = unpack_bf16(rr[j]);
+            add[2 * j] = f.x;
+            add[2 * j + 1] = f.y;
+          }
+        }
         uint32_t o[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          o[j] = pack_bf16(r * wv[c][2 * j] * gv[c][2 * j] - xv[c][2 * j] * k,
-                           r * wv[c][2 * j + 1] * gv[c][2 * j + 1] - xv[c][2 * j + 1] * k);
+          o[j] = pack_bf16(r * wv[c][2 * j] * gv[c][2 * j] - xv[c][2 * j] * k + add[2 * j],
+                           r * wv[c][2 * j + 1] * gv[c][2 * j + 1] - xv[c][2 * j + 1] * k + add[2 * j + 1]);
         *reinterpret_cast<uint4*>(dx + (long long)row * lddx + col) = make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
@@ -190,8 +202,9 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_small_kernel(const __nv_bfloa
                                                                 const __nv_bfloat16* __restrict__ w,
                                                                 const float* __restrict__ rstd,
                                                                 __nv_bfloat16* __restrict__ dx, long long lddx,
-                                                                float* __restrict__ dw_part, int rows, int D,
-                                                                int rows_per_block) {
+                                                                const __nv_bfloat16* __restrict__ dres,
+                                                                long long ldres, float* __restrict__ dw_part, int rows,
+                                                                int D, int rows_per_block) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int per = D / 32;
   float wv[8], acc[8];
@@ -216,7 +229,10 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_small_kernel(const __nv_bfloa
     const float k = dot * r * r * r / (float)D;
 #pragma unroll
     for (int j = 0; j < 8; ++j)
-      if (j < per) dx[(long long)row * lddx + lane * per + j] = __float2bfloat16_rn(r * wv[j] * gv[j] - xv[j] * k);
+      if (j < per)
+        dx[(long long)row * lddx + lane * per + j] = __float2bfloat16_rn(
+            r * wv[j] * gv[j] - xv[j] * k +
+            (dres ? __bfloat162float(dres[(long long)row * ldres + lane * per + j]) : 0.f));
   }
   __shared__ float red[8][256];
 #pragma unroll
@@ -276,7 +292,7 @@ long long rmsnorm_bwd_scratch(int rows, int D, int* nblocks_out) {
 
 void rmsnorm_bwd(const void* dy, long long lddy, const void* x, long long ldx, const void* w, const float* rstd,
                  void* dx, long long lddx, void* dw_bf16, float* dw_f32, float* scratch, int rows, int D,
-                 cudaStream_t s) {
+                 cudaStream_t s, const void* dres, long long ldres) {
   using namespace astrai;
   int nb = 0;
   rmsnorm_bwd_scratch(rows, D, &nb);
@@ -285,6 +301,7 @@ void rmsnorm_bwd(const void* dy, long long lddy, const void* x, long long ldx, c
   auto X = static_cast<const __nv_bfloat16*>(x);
   auto W = static_cast<const __nv_bfloat16*>(w);
   auto DX = static_cast<__nv_bfloat16*>(dx);
+  auto DR = static_cast<const __nv_bfloat16*>(dres);
   const size_t sm = (size_t)8 * D * sizeof(float);
   static bool attr_done[64] = {false};
   int dev = 0;
@@ -296,13 +313,13 @@ void rmsnorm_bwd(const void* dy, long long lddy, const void* x, long long ldx, c
     attr_done[dev & 63] = true;
   }
   if (D <= 256 && D % 32 == 0) {
-    (astrai::note_launch(), rmsnorm_bwd_small_kernel<<<nb, 256, 0, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb));
+    (astrai::note_launch(), rmsnorm_bwd_small_kernel<<<nb, 256, 0, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, DR, ldres, scratch, rows, D, rpb));
   } else if (D <= 1024) {
-    (astrai::note_launch(), rmsnorm_bwd_kernel<4><<<nb, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb));
+    (astrai::note_launch(), rmsnorm_bwd_kernel<4><<<nb, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, DR, ldres, scratch, rows, D, rpb));
   } else if (D <= 2048) {
-    (astrai::note_launch(), rmsnorm_bwd_kernel<8><<<nb, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb));
+    (astrai::note_launch(), rmsnorm_bwd_kernel<8><<<nb, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, DR, ldres, scratch, rows, D, rpb));
   } else {
-    (astrai::note_launch(), rmsnorm_bwd_kernel<16><<<nb, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb));
+    (astrai::note_launch(), rmsnorm_bwd_kernel<16><<<nb, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, DR, ldres, scratch, rows, D, rpb));
   }
   (astrai::note_launch(), reduce_cols_kernel<<<(D + 255) / 256, 256, 0, s>>>(scratch, nb, D, static_cast<__nv_bfloat16*>(dw_bf16), dw_f32));
 }
@@ -381,13 +398,13 @@ extern "C" int astrai_rmsnorm_bwd_static_scratch(const void* dy, long long lddy,
   const int blocks = static_cast<int>(nb);
   const size_t sm = static_cast<size_t>(8) * D * sizeof(float);
   if (D <= 256 && D % 32 == 0) {
-    (astrai::note_launch(), rmsnorm_bwd_small_kernel<<<blocks, 256, 0, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb));
+    (astrai::note_launch(), rmsnorm_bwd_small_kernel<<<blocks, 256, 0, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, nullptr, 0, scratch, rows, D, rpb));
   } else if (D <= 1024) {
-    (astrai::note_launch(), rmsnorm_bwd_kernel<4><<<blocks, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb));
+    (astrai::note_launch(), rmsnorm_bwd_kernel<4><<<blocks, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, nullptr, 0, scratch, rows, D, rpb));
   } else if (D <= 2048) {
-    (astrai::note_launch(), rmsnorm_bwd_kernel<8><<<blocks, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb));
+    (astrai::note_launch(), rmsnorm_bwd_kernel<8><<<blocks, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, nullptr, 0, scratch, rows, D, rpb));
   } else {
-    (astrai::note_launch(), rmsnorm_bwd_kernel<16><<<blocks, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, scratch, rows, D, rpb));
+    (astrai::note_launch(), rmsnorm_bwd_kernel<16><<<blocks, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, nullptr, 0, scratch, rows, D, rpb));
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return static_cast<int>(e);

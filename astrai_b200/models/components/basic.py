@@ -64,6 +64,12 @@ class RMSNorm(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return _rms_norm(x, self.weight, self.norm_eps)
 
+    def forward_fork(self, x: torch.Tensor):
+        """``(self(x), x)`` where the gradient of the second output is added inside the norm backward."""
+        from astrai_b200.ops.norm import rms_norm_fork
+
+        return rms_norm_fork(x, self.weight, self.norm_eps)
+
 
 class Embedding(nn.Module):
     def __init__(self, vocab_size: int, embedding_dim: int, neftune_alpha: float = 0.0):

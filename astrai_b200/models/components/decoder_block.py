@@ -43,5 +43,8 @@ class DecoderBlock(nn.Module):
         self.mlp = FFNFactory.create(ffn_type, **cfg)
 
     def forward(self, x: torch.Tensor, ctx: AttnContext) -> torch.Tensor:
-        h = self.attention(self.input_norm(x), ctx, residual=x)
-        return self.mlp(self.post_attention_norm(h), residual=h, ctx=ctx)
+        # forward_fork: the residual branch's gradient is summed inside the norm backward kernel
+        xn, xr = self.input_norm.forward_fork(x)
+        h = self.attention(xn, ctx, residual=xr)
+        hn, hr = self.post_attention_norm.forward_fork(h)
+        return self.mlp(hn, residual=hr, ctx=ctx)

@@ -36,9 +36,53 @@ class _RMSNormFn(torch.autograd.Function):
         return dx.view(ctx.shape), dw, None
 
 
-def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+class _RMSNormForkFn(torch.autograd.Function):
+    """``(rms_norm(x), x)`` for a pre-norm block that also feeds x to its residual add: the gradient
+    arriving through the second output is added to dx inside the norm backward kernel, instead of
+    autograd summing the two branches with a separate elementwise kernel."""
+
+    @staticmethod
+    def forward(ctx, x, w, eps):
+        y = _RMSNormFn.forward(ctx, x, w, eps)
+        return y, x
+
+    @staticmethod
+    def backward(ctx, dy, dres):
+        x2, w, rstd = ctx.saved_tensors
+        C = native()
+        D = x2.shape[1]
+        if dy is None:
+            return dres, None, None
+        dy2 = dy.reshape(-1, D)
+        if dy2.stride(-1) != 1 or (dy2.stride(0) * 2) % 16:
+            dy2 = dy2.contiguous()
+        r2 = None
+        if dres is not None:
+            r2 = dres.reshape(-1, D)
+            if r2.stride(-1) != 1 or (r2.stride(0) * 2) % 16:
+                r2 = r2.contiguous()
+        dx = torch.empty_like(x2)
+        dw = torch.empty_like(w)
+        scratch = torch.empty(C.rmsnorm_bwd_scratch(x2.shape[0], D), device=x2.device, dtype=torch.float32)
+        C.rmsnorm_bwd(dy2, x2, w, rstd, dx, dw, scratch, r2)
+        return dx.view(ctx.shape), dw, None
+
+
+def _fast(x: torch.Tensor, weight: torch.Tensor) -> bool:
     D = x.shape[-1]
-    if x.is_cuda and x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and D % 8 == 0 \
-            and (D > 256 or D % 32 == 0) and D <= 4096:  # the warp-per-row kernels hold a row in registers
+    # the warp-per-row kernels hold a row in registers
+    return x.is_cuda and x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and D % 8 == 0 \
+        and (D > 256 or D % 32 == 0) and D <= 4096
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    if _fast(x, weight):
         return _RMSNormFn.apply(x, weight, eps)
-    return F.rms_norm(x, (D,), weight, eps)
+    return F.rms_norm(x, (x.shape[-1],), weight, eps)
+
+
+def rms_norm_fork(x: torch.Tensor, weight: torch.Tensor, eps: float):
+    """``(rms_norm(x), x)``; on the kernel path the two gradients of x are summed in the norm backward."""
+    if _fast(x, weight) and torch.is_grad_enabled() and x.requires_grad:
+        return _RMSNormForkFn.apply(x, weight, eps)
+    return rms_norm(x, weight, eps), x

@@ -134,6 +134,26 @@ def test_rmsnorm(D):
     assert rel_err(w.grad, wf.grad) < 1e-2
 
 
+@pytest.mark.parametrize("D", [128, 2048])
+def test_rmsnorm_fork_adds_residual_gradient(D):
+    """(rms_norm(x), x) used by a norm branch and a residual branch: the kernel's dx equals the fp32
+    sum of both branches' gradients."""
+    from astrai_b200.ops.norm import rms_norm_fork
+
+    torch.manual_seed(5)
+    x = torch.randn(257, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = (1 + 0.1 * torch.randn(D, device="cuda")).to(torch.bfloat16).requires_grad_()
+    y, xr = rms_norm_fork(x, w, 1e-5)
+    g1, g2 = torch.randn_like(y), torch.randn_like(y)
+    ((y * g1).sum() + (xr * g2).sum()).backward()
+    xf, wf = x.detach().float().requires_grad_(), w.detach().float().requires_grad_()
+    yf = F.rms_norm(xf, (D,), wf, 1e-5)
+    ((yf * g1.float()).sum() + (xf * g2.float()).sum()).backward()
+    assert rel_err(y, yf) < 1e-2
+    assert rel_err(x.grad, xf.grad) < 1e-2
+    assert rel_err(w.grad, wf.grad) < 1e-2
+
+
 def test_rope_inplace_roundtrip():
     from astrai_b200.ops.rope import apply_rope_reference, rope_inplace, rope_table
 
