@@ -20,6 +20,9 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
                long long lda, long long strideA, int b_mn, long long ldb, long long strideB, long long ldd,
                long long strideD, int out_f32, long long ldc, long long strideC, float alpha, float beta,
                int force_bn, cudaStream_t stream);
+void gemm_swiglu_bf16(int mode, const void* A, long long lda, const void* B, long long ldb, int b_mn, void* D,
+                      long long ldd, void* aux, long long ldaux, const void* h, long long ldh, int M, int F, int K,
+                      cudaStream_t stream);
 void rmsnorm_fwd(const void* x, long long ldx, const void* w, void* y, long long ldy, float* rstd, int rows, int D,
                  float eps, cudaStream_t s);
 long long rmsnorm_bwd_scratch(int rows, int D, int* nblocks_out);
@@ -101,6 +104,42 @@ void skinny_gemm(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const 
 
 // ----------------------------------------------------------------- GEMM
 // D = alpha * op(A) op(B)^T + beta * C over 2-D or batched 3-D operands.
+// SwiGLU GEMMs (2-D, bf16):
+//   mode 1: x [M, K] @ w_ug [2F, K]^T -> h [M, 2F] and a = silu(g) * u [M, F] (out);  h_saved unused
+//   mode 2: dy [M, K] @ W_down^T (w: [K, F] = W_down's storage [out=K][in=F], read MN-major) with the
+//           saved h [M, 2F] -> dh [M, 2F] (out); the product da is never stored
+void gemm_swiglu(int64_t mode, const at::Tensor& a, const at::Tensor& w, const c10::optional<at::Tensor>& h_out,
+                 at::Tensor& out, const c10::optional<at::Tensor>& h_saved) {
+  check_bf16(a, "a");
+  check_bf16(w, "w");
+  check_bf16(out, "out");
+  TORCH_CHECK(a.dim() == 2 && w.dim() == 2 && out.dim() == 2, "gemm_swiglu: 2-D operands");
+  TORCH_CHECK(a.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "gemm_swiglu: contiguous rows");
+  TORCH_CHECK((a.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0, "gemm_swiglu: 16-byte row strides");
+  const int M = (int)a.size(0), K = (int)a.size(1);
+  c10::cuda::CUDAGuard g(a.device());
+  if (mode == 1) {
+    TORCH_CHECK(h_out.has_value() && h_out->defined(), "gemm_swiglu mode 1 needs h_out");
+    check_bf16(*h_out, "h_out");
+    const int F = (int)w.size(0) / 2;
+    TORCH_CHECK(w.size(0) == 2 * F && w.size(1) == K && h_out->size(0) == M && h_out->size(1) == 2 * F &&
+                    out.size(0) == M && out.size(1) == F && h_out->stride(1) == 1,
+                "gemm_swiglu mode 1: shapes x [M, K], w [2F, K], h [M, 2F], a [M, F]");
+    astrai_host::gemm_swiglu_bf16(1, a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), 0, h_out->data_ptr(),
+                                  h_out->stride(0), out.data_ptr(), out.stride(0), nullptr, 0, M, F, K, stream());
+  } else {
+    TORCH_CHECK(mode == 2 && h_saved.has_value() && h_saved->defined(), "gemm_swiglu mode 2 needs h_saved");
+    check_bf16(*h_saved, "h_saved");
+    const int F = (int)w.size(1);
+    TORCH_CHECK(w.size(0) == K && h_saved->size(0) == M && h_saved->size(1) == 2 * F && out.size(0) == M &&
+                    out.size(1) == 2 * F && h_saved->stride(1) == 1,
+                "gemm_swiglu mode 2: shapes dy [M, K], w [K, F], h [M, 2F], dh [M, 2F]");
+    astrai_host::gemm_swiglu_bf16(2, a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), 1, nullptr, 0,
+                                  out.data_ptr(), out.stride(0), h_saved->data_ptr(), h_saved->stride(0), M, F, K,
+                                  stream());
+  }
+}
+
 //   a: [.., M, K] when a_mn == 0, [.., K, M] when a_mn == 1
 //   b: [.., N, K] when b_mn == 0, [.., K, N] when b_mn == 1
 void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& d, const c10::optional<at::Tensor>& c, int64_t a_mn,
@@ -368,6 +407,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "bf16 tcgen05 GEMM", py::arg("a"), py::arg("b"), py::arg("d"), py::arg("c") = py::none(),
         py::arg("a_mn") = 0, py::arg("b_mn") = 0, py::arg("alpha") = 1.0, py::arg("beta") = 0.0,
         py::arg("force_bn") = 0);
+  m.def("gemm_swiglu", &gemm_swiglu, "GEMM with a fused SwiGLU epilogue (mode 1 forward, mode 2 backward)",
+        py::arg("mode"), py::arg("a"), py::arg("w"), py::arg("h_out"), py::arg("out"), py::arg("h_saved"));
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd_scratch", &rmsnorm_bwd_scratch);
   m.def("rmsnorm_bwd", &rmsnorm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"), py::arg("dx"),

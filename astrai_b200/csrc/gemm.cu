@@ -45,7 +45,22 @@ struct GemmParams {
   const int* group_tile;
   const int* k_start;
   const int* k_count;
+  // Fused SwiGLU epilogues (epi 0: plain GEMM).
+  //   epi 1 (forward, B K-major = the packed [up; gate] weight [2F, K]): tile n covers output
+  //         columns j in [n * BN/2, (n+1) * BN/2) of F; its B tile is up rows j.. and gate rows
+  //         F + j.., so the accumulator holds u and g of the same columns. Writes h = (u, g) to D
+  //         ([M, 2F], ldd) and a = silu(g) * u to aux ([M, F], ldaux).
+  //   epi 2 (backward, D = dY W_down would be da [M, F]): da stays in TMEM; with the saved
+  //         h ([M, 2F], ldh) the epilogue writes dh = (da * silu(g), da * u * silu'(g)) to aux.
+  int epi;
+  int F;
+  __nv_bfloat16* aux;
+  long long ldaux;
+  const __nv_bfloat16* h;
+  long long ldh;
 };
+
+__device__ __forceinline__ float sigmoid_f(float g) { return 1.f / (1.f + __expf(-g)); }
 
 // Operand batch coordinates and K range of one output tile.
 struct TileK {
@@ -179,6 +194,10 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
 #pragma unroll
             for (int c = 0; c < BN / 64; ++c)
               tma_load_3d(b_dst + c * 8192, &tmB, &full[stage], n0 + c * 64, k0, tk.bB);
+          } else if (p.epi == 1) {
+            // up rows then gate rows of the same BN/2 output columns (box = BN/2 rows)
+            tma_load_3d(b_dst, &tmB, &full[stage], k0, nb * (BN / 2), tk.bB);
+            tma_load_3d(b_dst + (BN / 2) * 128, &tmB, &full[stage], k0, p.F + nb * (BN / 2), tk.bB);
           } else {
             tma_load_3d(b_dst, &tmB, &full[stage], k0, n0, tk.bB);
           }
@@ -258,6 +277,127 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
       const OutT* crow = p.C ? reinterpret_cast<const OutT*>(p.C) + (long long)b * p.strideC + (long long)row * p.ldc
                              : nullptr;
       const uint32_t t_acc = tmem_base + ((uint32_t)(q * 32) << 16) + (acc * MH + half) * BN + cpart * BNP;
+      if (!OUT_F32 && p.epi == 1) {
+        constexpr int HALF = BN / 2, PER = HALF / Cfg::CSPLIT;  // (u, g) pairs per thread
+        const int j0 = nb * HALF + cpart * PER;
+        const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (acc * MH + half) * BN + cpart * PER;
+        __nv_bfloat16* hrow = reinterpret_cast<__nv_bfloat16*>(p.D) + (long long)row * p.ldd;
+        __nv_bfloat16* arow = p.aux + (long long)row * p.ldaux;
+#pragma unroll 1
+        for (int c = 0; c < PER; c += 32) {
+          uint32_t ru[32], rg[32];
+          tmem_ld32(tb + c, ru);
+          tmem_ld32(tb + HALF + c, rg);
+          tmem_wait_ld();
+          if (c + 32 >= PER) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[acc]);
+          }
+          if (!row_ok) continue;
+#pragma unroll
+          for (int g8 = 0; g8 < 32; g8 += 8) {
+            const int j = j0 + c + g8;
+            if (j >= p.F) break;
+            uint32_t hu[4], hg[4], ha[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float u0 = __uint_as_float(ru[g8 + 2 * e]) * p.alpha, u1 = __uint_as_float(ru[g8 + 2 * e + 1]) * p.alpha;
+              const float v0 = __uint_as_float(rg[g8 + 2 * e]) * p.alpha, v1 = __uint_as_float(rg[g8 + 2 * e + 1]) * p.alpha;
+              hu[e] = pack_bf16(u0, u1);
+              hg[e] = pack_bf16(v0, v1);
+              // a from the bf16-rounded h, exactly what the separate SwiGLU kernel would compute
+              const float2 ub = unpack_bf16(hu[e]), gb = unpack_bf16(hg[e]);
+              ha[e] = pack_bf16(ub.x * gb.x * sigmoid_f(gb.x), ub.y * gb.y * sigmoid_f(gb.y));
+            }
+            if (j + 8 <= p.F && p.vec_ok) {
+              *reinterpret_cast<uint4*>(hrow + j) = make_uint4(hu[0], hu[1], hu[2], hu[3]);
+              *reinterpret_cast<uint4*>(hrow + p.F + j) = make_uint4(hg[0], hg[1], hg[2], hg[3]);
+              *reinterpret_cast<uint4*>(arow + j) = make_uint4(ha[0], ha[1], ha[2], ha[3]);
+            } else {
+              for (int e = 0; e < 8 && j + e < p.F; ++e) {
+                const int sh = (e & 1) * 16;
+                hrow[j + e] = __ushort_as_bfloat16((unsigned short)(hu[e >> 1] >> sh));
+                hrow[p.F + j + e] = __ushort_as_bfloat16((unsigned short)(hg[e >> 1] >> sh));
+                arow[j + e] = __ushort_as_bfloat16((unsigned short)(ha[e >> 1] >> sh));
+              }
+            }
+          }
+        }
+        if (++acc == NACC) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+        continue;
+      }
+      if (!OUT_F32 && p.epi == 2) {
+        const __nv_bfloat16* hr = p.h + (long long)row * p.ldh;
+        __nv_bfloat16* dh = p.aux + (long long)row * p.ldaux;
+#pragma unroll 1
+        for (int c = 0; c < BNP; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(t_acc + c, r);
+          tmem_wait_ld();
+          if (c + 32 >= BNP) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[acc]);
+          }
+          if (!row_ok) continue;
+#pragma unroll
+          for (int g8 = 0; g8 < 32; g8 += 8) {
+            const int j = n0 + c + g8;
+            if (j >= p.N) break;
+            float u[8], gt[8], da[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) da[e] = no_k ? 0.f : __uint_as_float(r[g8 + e]) * p.alpha;
+            if (j + 8 <= p.N && p.vec_ok) {
+              const uint4 uu = *reinterpret_cast<const uint4*>(hr + j);
+              const uint4 gg = *reinterpret_cast<const uint4*>(hr + p.F + j);
+              const uint32_t uw[4] = {uu.x, uu.y, uu.z, uu.w}, gw[4] = {gg.x, gg.y, gg.z, gg.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 a2 = unpack_bf16(uw[e]), b2 = unpack_bf16(gw[e]);
+                u[2 * e] = a2.x;
+                u[2 * e + 1] = a2.y;
+                gt[2 * e] = b2.x;
+                gt[2 * e + 1] = b2.y;
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                u[e] = j + e < p.N ? __bfloat162float(hr[j + e]) : 0.f;
+                gt[e] = j + e < p.N ? __bfloat162float(hr[p.F + j + e]) : 0.f;
+              }
+            }
+            // da rounded to bf16 first, as the separate SwiGLU backward kernel reads it
+            uint32_t du[4], dg[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 d2 = unpack_bf16(pack_bf16(da[2 * e], da[2 * e + 1]));
+              const float s0 = sigmoid_f(gt[2 * e]), s1 = sigmoid_f(gt[2 * e + 1]);
+              du[e] = pack_bf16(d2.x * gt[2 * e] * s0, d2.y * gt[2 * e + 1] * s1);
+              dg[e] = pack_bf16(d2.x * u[2 * e] * s0 * (1.f + gt[2 * e] * (1.f - s0)),
+                                d2.y * u[2 * e + 1] * s1 * (1.f + gt[2 * e + 1] * (1.f - s1)));
+            }
+            if (j + 8 <= p.N && p.vec_ok) {
+              *reinterpret_cast<uint4*>(dh + j) = make_uint4(du[0], du[1], du[2], du[3]);
+              *reinterpret_cast<uint4*>(dh + p.F + j) = make_uint4(dg[0], dg[1], dg[2], dg[3]);
+            } else {
+              for (int e = 0; e < 8 && j + e < p.N; ++e) {
+                const int sh = (e & 1) * 16;
+                dh[j + e] = __ushort_as_bfloat16((unsigned short)(du[e >> 1] >> sh));
+                dh[p.F + j + e] = __ushort_as_bfloat16((unsigned short)(dg[e >> 1] >> sh));
+              }
+            }
+          }
+        }
+        if (++acc == NACC) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+        continue;
+      }
       if (MH == 2 && !OUT_F32 && (crow == nullptr || p.beta == 0.f)) {
         // BM = 256 (one accumulator buffer) without a C operand: drain the whole
         // accumulator row slice into packed bf16 registers, release TMEM, then
@@ -522,6 +662,12 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
   p.group_tile = nullptr;
   p.k_start = nullptr;
   p.k_count = nullptr;
+  p.epi = 0;
+  p.F = 0;
+  p.aux = nullptr;
+  p.ldaux = 0;
+  p.h = nullptr;
+  p.ldh = 0;
   const int tiles = batch * p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, sms);
   if (BM == 256)
@@ -591,12 +737,93 @@ void gemm_grouped_bf16(int mode, const void* A, const void* B, void* D, const vo
   p.group_tile = mode == 0 ? group_tile : nullptr;
   p.k_start = mode == 1 ? k_start : nullptr;
   p.k_count = mode == 1 ? k_count : nullptr;
+  p.epi = 0;
+  p.F = 0;
+  p.aux = nullptr;
+  p.ldaux = 0;
+  p.h = nullptr;
+  p.ldh = 0;
   const int tiles = p.batch * p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, sms);
   if (BN == 256)
     dispatch_majors<128, 256>(a_mn, b_mn, 0, ta, tb, p, grid, stream);
   else
     dispatch_majors<128, 128>(a_mn, b_mn, 0, ta, tb, p, grid, stream);
+}
+
+
+// GEMMs with a fused SwiGLU epilogue (see GemmParams::epi). A is K-major [M, K] (lda).
+//  mode 1: B = packed [up; gate] weight [2F, K] K-major (ldb); writes h [M, 2F] (ldd) and
+//          a = silu(g) * u [M, F] (ldaux). Needs F % 128 == 0 (tiles pair 128 up and 128 gate rows).
+//  mode 2: B = W_down stored [K][F] (b_mn 1) or [F][K] (b_mn 0); with the saved h [M, 2F] (ldh)
+//          writes dh [M, 2F] (ldaux); da = A @ B^T itself is never stored.
+void gemm_swiglu_bf16(int mode, const void* A, long long lda, const void* B, long long ldb, int b_mn, void* D,
+                      long long ldd, void* aux, long long ldaux, const void* h, long long ldh, int M, int F, int K,
+                      cudaStream_t stream) {
+  if (M <= 0 || F <= 0 || K <= 0) throw std::runtime_error("astrai gemm_swiglu: empty problem");
+  if (mode == 1 && (F % 128 || b_mn)) throw std::runtime_error("gemm_swiglu mode 1: F % 128 == 0, K-major B");
+  if (mode != 1 && mode != 2) throw std::runtime_error("gemm_swiglu: mode 1 or 2");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int sms = num_sms(dev);
+  const int BN = 256;
+  int BM = 128, bn_unused = 256;
+  if (mode == 1)
+    BM = M > 128 ? 256 : 128;
+  else
+    pick_tile(M, F, 1, sms, BM, bn_unused);
+  if (mode == 2 && F <= 128) throw std::runtime_error("gemm_swiglu mode 2: F > 128");
+  CUtensorMap ta, tb;
+  {
+    uint64_t dims[3] = {(uint64_t)K, (uint64_t)M, 1};
+    uint64_t strides[2] = {(uint64_t)lda * 2, (uint64_t)M * lda * 2};
+    uint32_t box[3] = {64, 128u, 1};
+    make_tmap_bf16(&ta, A, 3, dims, strides, box, true);
+  }
+  {
+    const uint64_t rows = mode == 1 ? (uint64_t)2 * F : (b_mn ? (uint64_t)K : (uint64_t)F);
+    const uint64_t inner = mode == 1 ? (uint64_t)K : (b_mn ? (uint64_t)F : (uint64_t)K);
+    uint64_t dims[3] = {inner, rows, 1};
+    uint64_t strides[2] = {(uint64_t)ldb * 2, rows * ldb * 2};
+    const uint32_t box_rows = mode == 1 ? (uint32_t)(BN / 2) : (b_mn ? 64u : (uint32_t)BN);
+    uint32_t box[3] = {64, box_rows, 1};
+    make_tmap_bf16(&tb, B, 3, dims, strides, box, true);
+  }
+  GemmParams p;
+  p.M = M;
+  p.N = mode == 1 ? 2 * F : F;
+  p.K = K;
+  p.batch = 1;
+  p.tiles_m = (M + BM - 1) / BM;
+  p.tiles_n = mode == 1 ? F / (BN / 2) : (F + BN - 1) / BN;
+  p.k_blocks = (K + 63) / 64;
+  p.D = mode == 1 ? D : aux;
+  p.ldd = mode == 1 ? ldd : ldaux;
+  p.strideD = 0;
+  p.C = nullptr;
+  p.ldc = 0;
+  p.strideC = 0;
+  p.alpha = 1.f;
+  p.beta = 0.f;
+  const auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) % 16) == 0; };
+  p.vec_ok = al16(aux) && (ldaux * 2) % 16 == 0 && (mode == 1 ? (al16(D) && (ldd * 2) % 16 == 0)
+                                                              : (al16(h) && (ldh * 2) % 16 == 0)) && F % 8 == 0;
+  p.err = error_word(dev);
+  p.group_tile = nullptr;
+  p.k_start = nullptr;
+  p.k_count = nullptr;
+  p.epi = mode;
+  p.F = F;
+  p.aux = static_cast<__nv_bfloat16*>(aux);
+  p.ldaux = ldaux;
+  p.h = static_cast<const __nv_bfloat16*>(h);
+  p.ldh = ldh;
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int grid = std::min(tiles, sms);
+  if (BM == 256)
+    dispatch_majors<256, 256>(0, mode == 1 ? 0 : b_mn, 0, ta, tb, p, grid, stream);
+  else
+    dispatch_majors<128, 256>(0, mode == 1 ? 0 : b_mn, 0, ta, tb, p, grid, stream);
 }
 
 }  // namespace astrai_host

@@ -32,7 +32,7 @@ import torch.nn as nn
 from astrai_b200.factory import Registry
 from astrai_b200.models.components.basic import Linear
 from astrai_b200.ops.activation import swiglu
-from astrai_b200.ops.gemm import linear, packed_linear
+from astrai_b200.ops.gemm import linear, packed_linear, swiglu_mlp
 
 
 class FFNFactory(Registry[nn.Module]):
@@ -48,6 +48,11 @@ class MLP(nn.Module):
         self.down = Linear(dim_ffn, dim, init_std=down_init_std)
 
     def forward(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None, ctx=None) -> torch.Tensor:
+        plain = all(type(m) is Linear and m.bias is None for m in (self.up, self.gate, self.down))
+        if plain:
+            y = swiglu_mlp(x, self.up.weight, self.gate.weight, self.down.weight, residual)
+            if y is not None:
+                return y
         if type(self.up) is Linear and type(self.gate) is Linear and self.up.bias is None and self.gate.bias is None:
             h = packed_linear(x, [self.up.weight, self.gate.weight])
         else:

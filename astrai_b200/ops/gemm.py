@@ -173,34 +173,104 @@ class _PackedLinearFn(torch.autograd.Function):
             dx = torch.empty_like(x2)
             C.gemm(dy2, w, dx, None, 0, 1, 1.0, 0.0, 0)
             dx = dx.view(ctx.x_shape)
-        params = [p for p in ctx.params if p.requires_grad]
-        if params:
-            g0 = params[0].grad
-            if g0 is None:
-                buf = torch.empty_like(w)
-                C.gemm(dy2, x2, buf, None, 1, 1, 1.0, 0.0, 0)
-                r = 0
-                for p in ctx.params:
-                    n = p.shape[0]
-                    if p.requires_grad:
-                        p.grad = buf[r:r + n]
-                    r += n
-            else:
-                grads = [p.grad for p in ctx.params]
-                if all(g is not None for g in grads) and _packed(grads):
-                    buf = _packed_view(grads)
-                    C.gemm(dy2, x2, buf, buf, 1, 1, 1.0, 1.0, 0)
-                else:  # foreign gradient layout: compute and add
-                    tmp = torch.empty_like(w)
-                    C.gemm(dy2, x2, tmp, None, 1, 1, 1.0, 0.0, 0)
-                    r = 0
-                    for p in ctx.params:
-                        n = p.shape[0]
-                        if p.requires_grad:
-                            p.grad = tmp[r:r + n].clone() if p.grad is None else p.grad.add_(tmp[r:r + n])
-                        r += n
+        accumulate_weight_grad(dy2, x2, w, ctx.params)
         dres = dy if ctx.has_res else None
         return (dx, None, dres) + (None,) * len(ctx.params)
+
+
+def accumulate_weight_grad(dy2: torch.Tensor, x2: torch.Tensor, w: torch.Tensor, params) -> None:
+    """``params[i].grad += rows of dy2^T x2`` (the weight gradient of ``x2 @ cat(params)^T``).
+
+    The first micro-batch after ``zero_grad`` writes one packed gradient buffer whose row slices
+    become the ``.grad`` tensors (beta 0); later micro-batches accumulate in the GEMM epilogue
+    (beta 1), so gradient accumulation costs no extra kernel."""
+    C = native()
+    live = [p for p in params if p.requires_grad]
+    if not live:
+        return
+    if live[0].grad is None:
+        buf = torch.empty_like(w)
+        C.gemm(dy2, x2, buf, None, 1, 1, 1.0, 0.0, 0)
+        r = 0
+        for p in params:
+            n = p.shape[0]
+            if p.requires_grad:
+                p.grad = buf[r:r + n]
+            r += n
+        return
+    grads = [p.grad for p in params]
+    if all(g is not None for g in grads) and _packed(grads):
+        buf = _packed_view(grads)
+        C.gemm(dy2, x2, buf, buf, 1, 1, 1.0, 1.0, 0)
+        return
+    tmp = torch.empty_like(w)  # foreign gradient layout: compute and add
+    C.gemm(dy2, x2, tmp, None, 1, 1, 1.0, 0.0, 0)
+    r = 0
+    for p in params:
+        n = p.shape[0]
+        if p.requires_grad:
+            p.grad = tmp[r:r + n].clone() if p.grad is None else p.grad.add_(tmp[r:r + n])
+        r += n
+
+
+class _SwiGLUMLPFn(torch.autograd.Function):
+    """``down(up(x) * silu(gate(x))) + residual`` with the SwiGLU in GEMM epilogues.
+
+    Forward: one GEMM whose tiles pair 128 up rows with the matching 128 gate rows of the packed
+    weight writes h = (u, g) and a = silu(g) * u; a second GEMM applies down (+ residual).
+    Backward: the down data-gradient GEMM turns da into dh = (da * silu(g), da * u * silu'(g)) in
+    its epilogue (da is never stored), then dx = dh W_ug and the three weight gradients."""
+
+    @staticmethod
+    def forward(ctx, x, w_ug, w_down, residual, n_ug, *params):
+        C = native()
+        x2 = _as_rows(x)
+        M, F_ = x2.shape[0], w_ug.shape[0] // 2
+        h = torch.empty((M, 2 * F_), device=x.device, dtype=torch.bfloat16)
+        a = torch.empty((M, F_), device=x.device, dtype=torch.bfloat16)
+        C.gemm_swiglu(1, x2, w_ug, h, a, None)
+        D = w_down.shape[0]
+        out = torch.empty((M, D), device=x.device, dtype=torch.bfloat16)
+        r2 = _as_rows(residual) if residual is not None else None
+        C.gemm(a, w_down, out, r2, 0, 0, 1.0, 1.0 if r2 is not None else 0.0, 0)
+        ctx.save_for_backward(x2, w_ug, w_down, h, a)
+        ctx.n_ug, ctx.params, ctx.has_res, ctx.x_shape = n_ug, params, residual is not None, x.shape
+        return out.view(*x.shape[:-1], D)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w_ug, w_down, h, a = ctx.saved_tensors
+        C = native()
+        dy2 = _as_rows(dy)
+        ug, dn = ctx.params[:ctx.n_ug], ctx.params[ctx.n_ug:]
+        accumulate_weight_grad(dy2, a, w_down, dn)
+        dh = torch.empty_like(h)
+        C.gemm_swiglu(2, dy2, w_down, None, dh, h)
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = torch.empty_like(x2)
+            C.gemm(dh, w_ug, dx, None, 0, 1, 1.0, 0.0, 0)
+            dx = dx.view(ctx.x_shape)
+        accumulate_weight_grad(dh, x2, w_ug, ug)
+        dres = dy if ctx.has_res else None
+        return (dx, None, None, dres, None) + (None,) * len(ctx.params)
+
+
+def swiglu_mlp(x: torch.Tensor, up: torch.Tensor, gate: torch.Tensor, down: torch.Tensor,
+               residual: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+    """Fused SwiGLU MLP on the kernel path, or None when it does not apply (then compose
+    :func:`packed_linear`, :func:`astrai_b200.ops.activation.swiglu` and :func:`linear`)."""
+    params = (up, gate, down)
+    if not (x.is_cuda and x.dtype == torch.bfloat16 and all(
+            p.is_cuda and p.dtype == torch.bfloat16 and type(p.data) is torch.Tensor for p in params)):
+        return None
+    F_, d = up.shape
+    if F_ % 128 or (d * 2) % 16 or down.shape != (d, F_) or x.shape[-1] != d:
+        return None
+    if not torch.is_grad_enabled() and x.reshape(-1, d).shape[0] <= SKINNY_MAX_ROWS:
+        return None  # decode rows: the skinny kernels stream each weight once
+    w_ug = pack_params([up, gate])
+    return _SwiGLUMLPFn.apply(x, w_ug.detach(), down.detach(), residual, 2, up, gate, down)
 
 
 def packed_linear(x: torch.Tensor, params, residual: Optional[torch.Tensor] = None) -> torch.Tensor:

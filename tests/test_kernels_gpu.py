@@ -306,3 +306,37 @@ def test_skinny_gemm(M, N, K):
     native().skinny_gemm(x, w, y, r)
     ref = x.float() @ w.float().t() + r.float()
     assert rel_err(y, ref) < 1e-2
+
+
+@pytest.mark.parametrize("M,d,F", [(512, 256, 384), (300, 512, 1408), (2048, 2048, 5632)])
+def test_swiglu_mlp_fused_epilogues(M, d, F):
+    """Fused SwiGLU MLP (paired up/gate tiles writing h and a; dh from the down data-gradient
+    epilogue) against an fp32 reference, with weight gradients accumulated over two calls."""
+    from astrai_b200.ops.gemm import swiglu_mlp
+
+    torch.manual_seed(M)
+    up, gate = (torch.nn.Parameter((torch.randn(F, d, device="cuda") * d ** -0.5).to(torch.bfloat16))
+                for _ in range(2))
+    down = torch.nn.Parameter((torch.randn(d, F, device="cuda") * F ** -0.5).to(torch.bfloat16))
+    xs = [torch.randn(M, d, device="cuda", dtype=torch.bfloat16, requires_grad=True) for _ in range(2)]
+    res = torch.randn(M, d, device="cuda", dtype=torch.bfloat16)
+    gs = [torch.randn(M, d, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+    for x, g in zip(xs, gs):
+        y = swiglu_mlp(x, up, gate, down, res)
+        assert y is not None
+        y.backward(g)
+    ref = {n: torch.zeros(t.shape, device="cuda") for n, t in (("up", up), ("gate", gate), ("down", down))}
+    for x, g in zip(xs, gs):
+        xf = x.detach().float().requires_grad_()
+        uf, gf, df = (t.detach().float().requires_grad_() for t in (up, gate, down))
+        yf = (xf @ uf.T * F.silu(xf @ gf.T)) @ df.T + res.float()
+        yf.backward(g.float())
+        for n, t in (("up", uf), ("gate", gf), ("down", df)):
+            ref[n] += t.grad
+        assert rel_err(x.grad, xf.grad) < 2e-2
+    y = swiglu_mlp(xs[0].detach(), up, gate, down, res)
+    xf = xs[0].detach().float()
+    yf = (xf @ up.float().T * F.silu(xf @ gate.float().T)) @ down.float().T + res.float()
+    assert rel_err(y, yf) < 1e-2
+    for n, t in (("up", up), ("gate", gate), ("down", down)):
+        assert rel_err(t.grad, ref[n]) < 2e-2, n
