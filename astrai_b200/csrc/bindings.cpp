@@ -20,6 +20,7 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
                long long lda, long long strideA, int b_mn, long long ldb, long long strideB, long long ldd,
                long long strideD, int out_f32, long long ldc, long long strideC, float alpha, float beta,
                int force_bn, cudaStream_t stream);
+void gemm_profile_set(unsigned long long* counters);
 void gemm_swiglu_bf16(int mode, const void* A, long long lda, const void* B, long long ldb, int b_mn, void* D,
                       long long ldd, void* aux, long long ldaux, const void* h, long long ldh, int M, int F, int K,
                       cudaStream_t stream);
@@ -407,6 +408,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "bf16 tcgen05 GEMM", py::arg("a"), py::arg("b"), py::arg("d"), py::arg("c") = py::none(),
         py::arg("a_mn") = 0, py::arg("b_mn") = 0, py::arg("alpha") = 1.0, py::arg("beta") = 0.0,
         py::arg("force_bn") = 0);
+  m.def("gemm_profile_set", [](const c10::optional<at::Tensor>& counters) {
+    // int64 [4] CUDA tensor that later GEMM launches add their wait cycles to, or None (off)
+    if (counters.has_value() && counters->defined()) {
+      TORCH_CHECK(counters->is_cuda() && counters->scalar_type() == at::kLong && counters->numel() >= 4,
+                  "counters: CUDA int64 [4]");
+      astrai_host::gemm_profile_set(reinterpret_cast<unsigned long long*>(counters->data_ptr<int64_t>()));
+    } else {
+      astrai_host::gemm_profile_set(nullptr);
+    }
+  });
   m.def("gemm_swiglu", &gemm_swiglu, "GEMM with a fused SwiGLU epilogue (mode 1 forward, mode 2 backward)",
         py::arg("mode"), py::arg("a"), py::arg("w"), py::arg("h_out"), py::arg("out"), py::arg("h_saved"));
   m.def("rmsnorm_fwd", &rmsnorm_fwd);

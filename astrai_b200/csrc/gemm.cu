@@ -52,6 +52,9 @@ struct GemmParams {
   //         ([M, 2F], ldd) and a = silu(g) * u to aux ([M, F], ldaux).
   //   epi 2 (backward, D = dY W_down would be da [M, F]): da stays in TMEM; with the saved
   //         h ([M, 2F], ldh) the epilogue writes dh = (da * silu(g), da * u * silu'(g)) to aux.
+  // optional wait-cycle counters (nullptr: off): [0] producer on empty, [1] MMA on full,
+  // [2] MMA on acc_empty, [3] epilogue on acc_full (summed over the waiting threads' CTAs)
+  unsigned long long* prof;
   int epi;
   int F;
   __nv_bfloat16* aux;
@@ -174,7 +177,10 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
         const int m0 = mb * BM, n0 = nb * BN;
         const TileK tk = tile_k(p, b, mb, BK);
         for (int kb = 0; kb < tk.kblk; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kErrWaitEmpty)) {
+          const long long tw0 = p.prof ? clock64() : 0;
+          const bool got = mbar_wait(&empty[stage], phase ^ 1, p.err, kErrWaitEmpty);
+          if (p.prof) atomicAdd(p.prof + 0, (unsigned long long)(clock64() - tw0));
+          if (!got) {
             ok = false;
             break;
           }
@@ -221,11 +227,17 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
         int b, mb, nb;
         tile_coords(tile, p.tiles_m, p.tiles_n, b, mb, nb);
         const int kblk = tile_k(p, b, mb, BK).kblk;
-        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err, kErrWaitAccEmpty)) break;
+        const long long ta0 = p.prof ? clock64() : 0;
+        const bool got_acc = mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err, kErrWaitAccEmpty);
+        if (p.prof) atomicAdd(p.prof + 2, (unsigned long long)(clock64() - ta0));
+        if (!got_acc) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * MH * BN;
         for (int kb = 0; kb < kblk; ++kb) {
-          if (!mbar_wait(&full[stage], phase, p.err, kErrWaitFull)) {
+          const long long tf0 = p.prof ? clock64() : 0;
+          const bool got = mbar_wait(&full[stage], phase, p.err, kErrWaitFull);
+          if (p.prof) atomicAdd(p.prof + 1, (unsigned long long)(clock64() - tf0));
+          if (!got) {
             ok = false;
             break;
           }
@@ -266,7 +278,10 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       int b, mb, nb;
       tile_coords(tile, p.tiles_m, p.tiles_n, b, mb, nb);
-      if (!mbar_wait(&acc_full[acc], acc_phase, p.err, kErrWaitAccFull)) break;
+      const long long te0 = (p.prof && lane == 0) ? clock64() : 0;
+      const bool got_full = mbar_wait(&acc_full[acc], acc_phase, p.err, kErrWaitAccFull);
+      if (p.prof && lane == 0 && warp == 2) atomicAdd(p.prof + 3, (unsigned long long)(clock64() - te0));
+      if (!got_full) break;
       tc_fence_after();
       const bool no_k = tile_k(p, b, mb, 64).kblk == 0;  // nothing accumulated: the product is 0
       const int row = mb * BM + half * 128 + q * 32 + lane;
@@ -541,6 +556,10 @@ namespace astrai_host {
 using astrai::GemmCfg;
 using astrai::GemmParams;
 
+// When set (gemm_profile_set), every GEMM launch adds its wait cycles to these 4 counters.
+static unsigned long long* g_gemm_prof = nullptr;
+void gemm_profile_set(unsigned long long* counters) { g_gemm_prof = counters; }
+
 template <int BM, int BN, int A_MN, int B_MN, int OUT_F32>
 static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
                         cudaStream_t stream) {
@@ -662,6 +681,7 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
   p.group_tile = nullptr;
   p.k_start = nullptr;
   p.k_count = nullptr;
+  p.prof = g_gemm_prof;
   p.epi = 0;
   p.F = 0;
   p.aux = nullptr;
@@ -737,6 +757,7 @@ void gemm_grouped_bf16(int mode, const void* A, const void* B, void* D, const vo
   p.group_tile = mode == 0 ? group_tile : nullptr;
   p.k_start = mode == 1 ? k_start : nullptr;
   p.k_count = mode == 1 ? k_count : nullptr;
+  p.prof = g_gemm_prof;
   p.epi = 0;
   p.F = 0;
   p.aux = nullptr;
@@ -812,6 +833,7 @@ void gemm_swiglu_bf16(int mode, const void* A, long long lda, const void* B, lon
   p.group_tile = nullptr;
   p.k_start = nullptr;
   p.k_count = nullptr;
+  p.prof = g_gemm_prof;
   p.epi = mode;
   p.F = F;
   p.aux = static_cast<__nv_bfloat16*>(aux);

@@ -69,10 +69,22 @@ def bench_gemm():
         B = b if bmn else b.t()
         ms_ref = time_fn(lambda: torch.matmul(A, B))
         fl = 2.0 * M * N * K
+        # one extra launch with the wait-cycle counters on: where the pipeline stalls
+        cnt = torch.zeros(4, device="cuda", dtype=torch.int64)
+        C.gemm_profile_set(cnt)
+        C.gemm(a, b, d, None, amn, bmn, 1.0, 0.0, 0)
+        torch.cuda.synchronize()
+        C.gemm_profile_set(None)
+        w = [int(v) for v in cnt.tolist()]
+        sms = torch.cuda.get_device_properties(0).multi_processor_count
+        cyc = ms * 1e-3 * 1.9e9  # cycles of one CTA at ~1.9 GHz
         print(json.dumps({"kernel": "gemm", "case": name, "M": M, "N": N, "K": K, "ms": round(ms, 4),
                           "tflops": round(fl / ms / 1e9, 1), "frac_of_peak": round(fl / ms / 1e9 / tf, 3),
                           "peak_src": src, "cublas_ms": round(ms_ref, 4),
-                          "cublas_tflops": round(fl / ms_ref / 1e9, 1)}))
+                          "cublas_tflops": round(fl / ms_ref / 1e9, 1),
+                          "wait_frac_per_cta": {k: round(v / sms / cyc, 3) for k, v in
+                                                zip(("producer_empty", "mma_full", "mma_acc_empty", "epi_acc_full"),
+                                                    w)}}))
 
 
 def bench_allreduce():
