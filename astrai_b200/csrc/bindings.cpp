@@ -21,6 +21,9 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
                long long strideD, int out_f32, long long ldc, long long strideC, float alpha, float beta,
                int force_bn, cudaStream_t stream);
 void gemm_profile_set(unsigned long long* counters);
+void gemm_rope_bf16(const void* A, long long lda, const void* B, long long ldb, void* D, long long ldd, int M, int N,
+                    int K, const void* cs, const int* pos, int seq, int rope_cols, int head_dim, int max_pos,
+                    cudaStream_t stream);
 void gemm_swiglu_bf16(int mode, const void* A, long long lda, const void* B, long long ldb, int b_mn, void* D,
                       long long ldd, void* aux, long long ldaux, const void* h, long long ldh, int M, int F, int K,
                       cudaStream_t stream);
@@ -139,6 +142,31 @@ void gemm_swiglu(int64_t mode, const at::Tensor& a, const at::Tensor& w, const c
                                   out.data_ptr(), out.stride(0), h_saved->data_ptr(), h_saved->stride(0), M, F, K,
                                   stream());
   }
+}
+
+// out [M, N] = x [M, K] @ w [N, K]^T with RoPE on columns [0, rope_cols) (heads of head_dim columns):
+// the row's position is positions[row] (int32) or row % seq_len; table is fp32 [max_pos, head_dim/2, 2].
+void gemm_rope(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const at::Tensor& table,
+               const c10::optional<at::Tensor>& positions, int64_t seq_len, int64_t rope_cols, int64_t head_dim) {
+  check_bf16(x, "x");
+  check_bf16(w, "w");
+  check_bf16(out, "out");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && out.dim() == 2 && x.stride(1) == 1 && w.stride(1) == 1 &&
+                  out.stride(1) == 1, "gemm_rope: 2-D operands with contiguous rows");
+  TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0, "gemm_rope: 16-byte row strides");
+  TORCH_CHECK(w.size(1) == x.size(1) && out.size(0) == x.size(0) && out.size(1) == w.size(0), "gemm_rope: shapes");
+  TORCH_CHECK(table.is_cuda() && table.scalar_type() == at::kFloat && table.is_contiguous(), "rope table");
+  const int* pos = nullptr;
+  if (positions.has_value() && positions->defined()) {
+    TORCH_CHECK(positions->scalar_type() == at::kInt && positions->is_contiguous() &&
+                    positions->numel() == x.size(0), "positions: int32, one per row");
+    pos = positions->data_ptr<int>();
+  }
+  const int64_t max_pos = table.numel() / head_dim;
+  c10::cuda::CUDAGuard g(x.device());
+  astrai_host::gemm_rope_bf16(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(), out.stride(0),
+                              (int)x.size(0), (int)w.size(0), (int)x.size(1), table.data_ptr(), pos, (int)seq_len,
+                              (int)rope_cols, (int)head_dim, (int)max_pos, stream());
 }
 
 //   a: [.., M, K] when a_mn == 0, [.., K, M] when a_mn == 1
@@ -418,6 +446,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       astrai_host::gemm_profile_set(nullptr);
     }
   });
+  m.def("gemm_rope", &gemm_rope, "GEMM with RoPE applied in the epilogue", py::arg("x"), py::arg("w"),
+        py::arg("out"), py::arg("table"), py::arg("positions"), py::arg("seq_len"), py::arg("rope_cols"),
+        py::arg("head_dim"));
   m.def("gemm_swiglu", &gemm_swiglu, "GEMM with a fused SwiGLU epilogue (mode 1 forward, mode 2 backward)",
         py::arg("mode"), py::arg("a"), py::arg("w"), py::arg("h_out"), py::arg("out"), py::arg("h_saved"));
   m.def("rmsnorm_fwd", &rmsnorm_fwd);

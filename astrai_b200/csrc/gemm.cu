@@ -61,6 +61,12 @@ struct GemmParams {
   long long ldaux;
   const __nv_bfloat16* h;
   long long ldh;
+  // epi 3 (RoPE): rotate interleaved pairs of output columns [0, rope_cols) (heads of rope_hd
+  // columns) by the angles of the row's position (rope_pos[row], or row % rope_seq) from the
+  // fp32 (cos, sin) table [rope_max][rope_hd / 2], before rounding to bf16.
+  const float2* rope_cs;
+  const int* rope_pos;
+  int rope_seq, rope_cols, rope_hd, rope_max;
 };
 
 __device__ __forceinline__ float sigmoid_f(float g) { return 1.f / (1.f + __expf(-g)); }
@@ -330,13 +336,62 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
               *reinterpret_cast<uint4*>(hrow + p.F + j) = make_uint4(hg[0], hg[1], hg[2], hg[3]);
               *reinterpret_cast<uint4*>(arow + j) = make_uint4(ha[0], ha[1], ha[2], ha[3]);
             } else {
-              for (int e = 0; e < 8 && j + e < p.F; ++e) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                if (j + e >= p.F) continue;
                 const int sh = (e & 1) * 16;
                 hrow[j + e] = __ushort_as_bfloat16((unsigned short)(hu[e >> 1] >> sh));
                 hrow[p.F + j + e] = __ushort_as_bfloat16((unsigned short)(hg[e >> 1] >> sh));
                 arow[j + e] = __ushort_as_bfloat16((unsigned short)(ha[e >> 1] >> sh));
               }
             }
+          }
+        }
+        if (++acc == NACC) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+        continue;
+      }
+      if (!OUT_F32 && p.epi == 3) {
+        int pos = p.rope_pos ? p.rope_pos[min(row, p.M - 1)] : row % p.rope_seq;
+        const bool pos_ok = pos >= 0 && pos < p.rope_max;
+        if (row_ok && !pos_ok && lane == 0) set_error(p.err, kErrBadArg);
+        __nv_bfloat16* dr = reinterpret_cast<__nv_bfloat16*>(p.D) + (long long)row * p.ldd;
+#pragma unroll 1
+        for (int c = 0; c < BNP; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(t_acc + c, r);
+          tmem_wait_ld();
+          if (c + 32 >= BNP) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[acc]);
+          }
+          if (!row_ok) continue;
+          const int j0 = n0 + c;
+          uint32_t o[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            float x0 = no_k ? 0.f : __uint_as_float(r[2 * e]) * p.alpha;
+            float x1 = no_k ? 0.f : __uint_as_float(r[2 * e + 1]) * p.alpha;
+            const int j = j0 + 2 * e;
+            if (pos_ok && j < p.rope_cols) {
+              const float2 cs = p.rope_cs[(long long)pos * (p.rope_hd / 2) + (j % p.rope_hd) / 2];
+              const float y0 = x0 * cs.x - x1 * cs.y, y1 = x0 * cs.y + x1 * cs.x;
+              x0 = y0;
+              x1 = y1;
+            }
+            o[e] = pack_bf16(x0, x1);
+          }
+          if (j0 + 32 <= p.N && p.vec_ok) {
+            uint4* dst = reinterpret_cast<uint4*>(dr + j0);
+#pragma unroll
+            for (int v4 = 0; v4 < 4; ++v4) dst[v4] = make_uint4(o[4 * v4], o[4 * v4 + 1], o[4 * v4 + 2], o[4 * v4 + 3]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (j0 + e < p.N) dr[j0 + e] = __ushort_as_bfloat16((unsigned short)(o[e >> 1] >> ((e & 1) * 16)));
           }
         }
         if (++acc == NACC) {
@@ -399,7 +454,9 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
               *reinterpret_cast<uint4*>(dh + j) = make_uint4(du[0], du[1], du[2], du[3]);
               *reinterpret_cast<uint4*>(dh + p.F + j) = make_uint4(dg[0], dg[1], dg[2], dg[3]);
             } else {
-              for (int e = 0; e < 8 && j + e < p.N; ++e) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                if (j + e >= p.N) continue;
                 const int sh = (e & 1) * 16;
                 dh[j + e] = __ushort_as_bfloat16((unsigned short)(du[e >> 1] >> sh));
                 dh[p.F + j + e] = __ushort_as_bfloat16((unsigned short)(dg[e >> 1] >> sh));
@@ -688,6 +745,12 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
   p.ldaux = 0;
   p.h = nullptr;
   p.ldh = 0;
+  p.rope_cs = nullptr;
+  p.rope_pos = nullptr;
+  p.rope_seq = 1;
+  p.rope_cols = 0;
+  p.rope_hd = 2;
+  p.rope_max = 0;
   const int tiles = batch * p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, sms);
   if (BM == 256)
@@ -764,6 +827,12 @@ void gemm_grouped_bf16(int mode, const void* A, const void* B, void* D, const vo
   p.ldaux = 0;
   p.h = nullptr;
   p.ldh = 0;
+  p.rope_cs = nullptr;
+  p.rope_pos = nullptr;
+  p.rope_seq = 1;
+  p.rope_cols = 0;
+  p.rope_hd = 2;
+  p.rope_max = 0;
   const int tiles = p.batch * p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, sms);
   if (BN == 256)
@@ -840,12 +909,88 @@ void gemm_swiglu_bf16(int mode, const void* A, long long lda, const void* B, lon
   p.ldaux = ldaux;
   p.h = static_cast<const __nv_bfloat16*>(h);
   p.ldh = ldh;
+  p.rope_cs = nullptr;
+  p.rope_pos = nullptr;
+  p.rope_seq = 1;
+  p.rope_cols = 0;
+  p.rope_hd = 2;
+  p.rope_max = 0;
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, sms);
   if (BM == 256)
     dispatch_majors<256, 256>(0, mode == 1 ? 0 : b_mn, 0, ta, tb, p, grid, stream);
   else
     dispatch_majors<128, 256>(0, mode == 1 ? 0 : b_mn, 0, ta, tb, p, grid, stream);
+}
+
+
+// x [M, K] @ w [N, K]^T with RoPE applied in the epilogue to columns [0, rope_cols) (see GemmParams).
+void gemm_rope_bf16(const void* A, long long lda, const void* B, long long ldb, void* D, long long ldd, int M, int N,
+                    int K, const void* cs, const int* pos, int seq, int rope_cols, int head_dim, int max_pos,
+                    cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) throw std::runtime_error("astrai gemm_rope: empty problem");
+  if (head_dim % 32 || rope_cols % head_dim || rope_cols > N || seq <= 0)
+    throw std::runtime_error("gemm_rope: head_dim multiple of 32, whole heads, seq > 0");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int sms = num_sms(dev);
+  int BM = 128, BN = 256;
+  pick_tile(M, N, 1, sms, BM, BN);
+  CUtensorMap ta, tb;
+  {
+    uint64_t dims[3] = {(uint64_t)K, (uint64_t)M, 1};
+    uint64_t strides[2] = {(uint64_t)lda * 2, (uint64_t)M * lda * 2};
+    uint32_t box[3] = {64, 128u, 1};
+    make_tmap_bf16(&ta, A, 3, dims, strides, box, true);
+  }
+  {
+    uint64_t dims[3] = {(uint64_t)K, (uint64_t)N, 1};
+    uint64_t strides[2] = {(uint64_t)ldb * 2, (uint64_t)N * ldb * 2};
+    uint32_t box[3] = {64, (uint32_t)BN, 1};
+    make_tmap_bf16(&tb, B, 3, dims, strides, box, true);
+  }
+  GemmParams p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.batch = 1;
+  p.tiles_m = (M + BM - 1) / BM;
+  p.tiles_n = (N + BN - 1) / BN;
+  p.k_blocks = (K + 63) / 64;
+  p.D = D;
+  p.ldd = ldd;
+  p.strideD = 0;
+  p.C = nullptr;
+  p.ldc = 0;
+  p.strideC = 0;
+  p.alpha = 1.f;
+  p.beta = 0.f;
+  p.vec_ok = ((reinterpret_cast<uintptr_t>(D) % 16) == 0) && ((ldd * 2) % 16 == 0);
+  p.err = error_word(dev);
+  p.group_tile = nullptr;
+  p.k_start = nullptr;
+  p.k_count = nullptr;
+  p.prof = g_gemm_prof;
+  p.epi = 3;
+  p.F = 0;
+  p.aux = nullptr;
+  p.ldaux = 0;
+  p.h = nullptr;
+  p.ldh = 0;
+  p.rope_cs = static_cast<const float2*>(cs);
+  p.rope_pos = pos;
+  p.rope_seq = seq;
+  p.rope_cols = rope_cols;
+  p.rope_hd = head_dim;
+  p.rope_max = max_pos;
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int grid = std::min(tiles, sms);
+  if (BM == 256)
+    dispatch_majors<256, 256>(0, 0, 0, ta, tb, p, grid, stream);
+  else if (BN == 256)
+    dispatch_majors<128, 256>(0, 0, 0, ta, tb, p, grid, stream);
+  else
+    dispatch_majors<128, 128>(0, 0, 0, ta, tb, p, grid, stream);
 }
 
 }  // namespace astrai_host

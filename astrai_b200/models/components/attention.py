@@ -96,11 +96,18 @@ class GQA(nn.Module):
         if fused and ctx.cache is not None:  # inference: the cache view runs RoPE + KV write + attention
             fused = getattr(ctx.cache, "supports_qkv", False) and x.is_cuda and x.dtype == torch.bfloat16
         if fused:
-            qkv = self.qkv_proj(x).reshape(B * S, (Hq + 2 * Hkv) * D)
+            qkv = None
+            if ctx.cache is None:  # training: RoPE in the QKV projection epilogue
+                qkv = self.qkv_proj_rope(x, ctx)
+            rotated = qkv is not None
+            if qkv is None:
+                qkv = self.qkv_proj(x)
+            qkv = qkv.reshape(B * S, (Hq + 2 * Hkv) * D)
             if ctx.cache is not None:
                 o = ctx.cache.attend_qkv(self.layer_id, qkv, B, S, Hq, Hkv, ctx.table)
             else:
-                o = attention_qkv(qkv, B, S, Hq, Hkv, ctx.table, ctx.positions, ctx.causal, ctx.seg)
+                o = attention_qkv(qkv, B, S, Hq, Hkv, ctx.table, ctx.positions, ctx.causal, ctx.seg,
+                                  rotated=rotated)
             o = o.view(B, S, Hq * D)
         else:
             qkv = self.qkv_proj(x)
@@ -119,6 +126,17 @@ class GQA(nn.Module):
         if self.use_gated_attention:
             o = o * torch.sigmoid(self.gate(x))
         return self.o_proj(o, residual=residual)
+
+    def qkv_proj_rope(self, x: torch.Tensor, ctx) -> Optional[torch.Tensor]:
+        """q|k|v projection with RoPE already applied to q and k (GEMM epilogue), or None."""
+        mods = (self.q_proj, self.k_proj, self.v_proj)
+        if not all(type(m) is Linear and m.bias is None for m in mods) or self.head_dim != 128:
+            return None
+        from astrai_b200.ops.gemm import packed_linear_rope
+
+        pos = ctx.positions.reshape(-1).to(torch.int32).contiguous() if ctx.positions is not None else None
+        return packed_linear_rope(x, [m.weight for m in mods], ctx.table, pos, ctx.S,
+                                  (self.n_heads + self.n_kv_heads) * self.head_dim, self.head_dim)
 
     def qkv_proj(self, x: torch.Tensor) -> torch.Tensor:
         """q|k|v projections as one GEMM over the concatenated weight (plain

@@ -72,16 +72,21 @@ def _sdpa(q, k, v, causal, seg, scale=None):
 
 # ----------------------------------------------------------------------------- fused training path
 class _AttnQKVFn(torch.autograd.Function):
+    """``rotated``: q/k already carry RoPE (applied in the QKV projection epilogue), so neither the
+    forward rotation nor the backward inverse rotation happens here."""
+
     @staticmethod
-    def forward(ctx, qkv, table, positions, seg, B, S, Hq, Hkv, causal):
+    def forward(ctx, qkv, table, positions, seg, B, S, Hq, Hkv, causal, rotated=False):
         D = HEAD_DIM
         C = native()
-        rope_inplace(qkv, 0, Hq + Hkv, D, table, positions, S)  # q and k heads are adjacent
+        if not rotated:
+            rope_inplace(qkv, 0, Hq + Hkv, D, table, positions, S)  # q and k heads are adjacent
         o = torch.empty((B * S, Hq * D), device=qkv.device, dtype=torch.bfloat16)
         lse = torch.empty((B, Hq, S), device=qkv.device, dtype=torch.float32)
         C.flash_fwd(qkv, 0, qkv, Hq * D, qkv, (Hq + Hkv) * D, o, lse, B, S, S, Hq, Hkv, 1.0 / math.sqrt(D), causal, seg)
         ctx.save_for_backward(qkv, o, lse, table, positions, seg)
         ctx.dims = (B, S, Hq, Hkv, causal)
+        ctx.rotated = rotated
         return o
 
     @staticmethod
@@ -96,24 +101,26 @@ class _AttnQKVFn(torch.autograd.Function):
         delta = torch.empty(2 * B * Hq * ((S + 63) // 64 * 64), device=qkv.device, dtype=torch.float32)
         C.flash_bwd(qkv, 0, qkv, Hq * D, qkv, (Hq + Hkv) * D, o, do, lse, delta, dq_acc, dqkv, 0, dqkv, Hq * D,
                     dqkv, (Hq + Hkv) * D, B, S, S, Hq, Hkv, 1.0 / math.sqrt(D), causal, seg)
-        rope_inplace(dqkv, 0, Hq + Hkv, D, table, positions, S, inverse=True)
-        return dqkv, None, None, None, None, None, None, None, None
+        if not ctx.rotated:
+            rope_inplace(dqkv, 0, Hq + Hkv, D, table, positions, S, inverse=True)
+        return dqkv, None, None, None, None, None, None, None, None, None
 
 
 def attention_qkv(qkv: torch.Tensor, B: int, S: int, Hq: int, Hkv: int, table: torch.Tensor,
                   positions: Optional[torch.Tensor] = None, causal: bool = True,
-                  seg: Optional[torch.Tensor] = None) -> torch.Tensor:
+                  seg: Optional[torch.Tensor] = None, rotated: bool = False) -> torch.Tensor:
     """RoPE + attention on a fused QKV buffer ``[B*S, (Hq+2Hkv)*D]``.
 
     ``table`` is the fp32 (cos, sin) table ``[max_pos, D/2, 2]`` on the same
     device; ``positions`` int [B, S] (None -> 0..S-1 per sequence).
-    On CUDA the buffer is rotated in place.
+    On CUDA the buffer is rotated in place, unless ``rotated`` (RoPE already applied by the
+    projection epilogue, see :func:`astrai_b200.ops.gemm.packed_linear_rope`).
     """
     D = qkv.shape[-1] // (Hq + 2 * Hkv)
     if qkv.is_cuda and qkv.dtype == torch.bfloat16 and D == HEAD_DIM:
         pos = positions.reshape(-1).to(torch.int32).contiguous() if positions is not None else None
         sg = seg.to(torch.int32).contiguous() if seg is not None else None
-        return _AttnQKVFn.apply(qkv, table, pos, sg, B, S, Hq, Hkv, causal)
+        return _AttnQKVFn.apply(qkv, table, pos, sg, B, S, Hq, Hkv, causal, rotated)
     q, k, v = qkv.view(B, S, Hq + 2 * Hkv, D).split([Hq, Hkv, Hkv], dim=2)
     if positions is None:
         cs = table[:S].unsqueeze(0).expand(B, -1, -1, -1)

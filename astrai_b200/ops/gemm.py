@@ -273,6 +273,53 @@ def swiglu_mlp(x: torch.Tensor, up: torch.Tensor, gate: torch.Tensor, down: torc
     return _SwiGLUMLPFn.apply(x, w_ug.detach(), down.detach(), residual, 2, up, gate, down)
 
 
+class _PackedLinearRopeFn(torch.autograd.Function):
+    """``rope(x @ cat(params)^T)`` on the first ``rope_cols`` columns, the rotation applied in the GEMM
+    epilogue; backward rotates the incoming gradient back (in place) before the usual products."""
+
+    @staticmethod
+    def forward(ctx, x, w, table, positions, seq_len, rope_cols, head_dim, *params):
+        x2 = _as_rows(x)
+        out = torch.empty((x2.shape[0], w.shape[0]), device=x.device, dtype=torch.bfloat16)
+        native().gemm_rope(x2, w, out, table, positions, seq_len, rope_cols, head_dim)
+        ctx.save_for_backward(x2, w, table, positions)
+        ctx.params, ctx.x_shape, ctx.rope = params, x.shape, (seq_len, rope_cols, head_dim)
+        return out.view(*x.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        from astrai_b200.ops.rope import rope_inplace
+
+        x2, w, table, positions = ctx.saved_tensors
+        seq_len, rope_cols, head_dim = ctx.rope
+        # the gradient arriving here is the attention kernel's fresh dqkv buffer (the projection's
+        # only consumer), so it is rotated back in place
+        dy2 = _as_rows(dy)
+        rope_inplace(dy2, 0, rope_cols // head_dim, head_dim, table, positions, seq_len, inverse=True)
+        C = native()
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = torch.empty_like(x2)
+            C.gemm(dy2, w, dx, None, 0, 1, 1.0, 0.0, 0)
+            dx = dx.view(ctx.x_shape)
+        accumulate_weight_grad(dy2, x2, w, ctx.params)
+        return (dx, None, None, None, None, None, None) + (None,) * len(ctx.params)
+
+
+def packed_linear_rope(x: torch.Tensor, params, table: torch.Tensor, positions: Optional[torch.Tensor],
+                       seq_len: int, rope_cols: int, head_dim: int) -> Optional[torch.Tensor]:
+    """Packed projection with interleaved RoPE on its first ``rope_cols`` output columns (the q and k heads
+    of a fused QKV projection), or None when the kernel path does not apply."""
+    params = list(params)
+    if not (x.is_cuda and x.dtype == torch.bfloat16 and all(
+            p.is_cuda and p.dtype == torch.bfloat16 and type(p.data) is torch.Tensor for p in params)):
+        return None
+    if (x.shape[-1] * 2) % 16 or head_dim % 32 or rope_cols % head_dim or not torch.is_grad_enabled():
+        return None
+    w = pack_params(params) if len(params) > 1 else params[0]
+    return _PackedLinearRopeFn.apply(x, w.detach(), table, positions, seq_len, rope_cols, head_dim, *params)
+
+
 def packed_linear(x: torch.Tensor, params, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``x @ cat(params)^T (+ residual)`` for bias-free 2-D bf16 parameters.
 

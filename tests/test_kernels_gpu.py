@@ -340,3 +340,34 @@ def test_swiglu_mlp_fused_epilogues(M, d, F):
     assert rel_err(y, yf) < 1e-2
     for n, t in (("up", up), ("gate", gate), ("down", down)):
         assert rel_err(t.grad, ref[n]) < 2e-2, n
+
+
+@pytest.mark.parametrize("with_pos", [False, True])
+def test_qkv_projection_with_rope_epilogue(with_pos):
+    """RoPE applied in the QKV projection epilogue + attention on pre-rotated q/k equals the
+    unfused projection + in-place RoPE + attention, in value and in the input/weight gradients."""
+    from astrai_b200.ops.attention import attention_qkv
+    from astrai_b200.ops.gemm import packed_linear, packed_linear_rope
+    from astrai_b200.ops.rope import rope_table
+
+    torch.manual_seed(12)
+    B, S, Hq, Hkv, D, d = 2, 256, 4, 2, 128, 512
+    tab = rope_table(D, 1024, 1e6, device="cuda")
+    ws = [torch.nn.Parameter((torch.randn(h * D, d, device="cuda") * d ** -0.5).to(torch.bfloat16))
+          for h in (Hq, Hkv, Hkv)]
+    ws2 = [torch.nn.Parameter(w.detach().clone()) for w in ws]
+    x = torch.randn(B, S, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    x2 = x.detach().clone().requires_grad_()
+    pos = (torch.arange(S, device="cuda") + 100).repeat(B, 1) if with_pos else None
+    p32 = pos.reshape(-1).to(torch.int32).contiguous() if pos is not None else None
+    qkv = packed_linear_rope(x, ws, tab, p32, S, (Hq + Hkv) * D, D)
+    o = attention_qkv(qkv.reshape(B * S, -1), B, S, Hq, Hkv, tab, pos, True, None, rotated=True)
+    qkv2 = packed_linear(x2, ws2)
+    o2 = attention_qkv(qkv2.reshape(B * S, -1), B, S, Hq, Hkv, tab, pos, True, None)
+    g = torch.randn_like(o)
+    o.backward(g)
+    o2.backward(g)
+    assert rel_err(o, o2) < 1e-2
+    assert rel_err(x.grad, x2.grad) < 2e-2
+    for a, b in zip(ws, ws2):
+        assert rel_err(a.grad, b.grad) < 2e-2
