@@ -71,6 +71,11 @@ struct GemmParams {
 
 __device__ __forceinline__ float sigmoid_f(float g) { return 1.f / (1.f + __expf(-g)); }
 
+// accumulator columns one epilogue thread drains in the fused modes (BN / CSPLIT); the paired
+// SwiGLU forward reads them as half as many (u, g) pairs
+template <int BN, int CSPLIT>
+__host__ __device__ constexpr int p_epi_per() { return BN / CSPLIT; }
+
 // Operand batch coordinates and K range of one output tile.
 struct TileK {
   int bA, bB, kbase, kblk;
@@ -298,168 +303,164 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
       const OutT* crow = p.C ? reinterpret_cast<const OutT*>(p.C) + (long long)b * p.strideC + (long long)row * p.ldc
                              : nullptr;
       const uint32_t t_acc = tmem_base + ((uint32_t)(q * 32) << 16) + (acc * MH + half) * BN + cpart * BNP;
-      if (!OUT_F32 && p.epi == 1) {
-        constexpr int HALF = BN / 2, PER = HALF / Cfg::CSPLIT;  // (u, g) pairs per thread
-        const int j0 = nb * HALF + cpart * PER;
-        const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (acc * MH + half) * BN + cpart * PER;
-        __nv_bfloat16* hrow = reinterpret_cast<__nv_bfloat16*>(p.D) + (long long)row * p.ldd;
-        __nv_bfloat16* arow = p.aux + (long long)row * p.ldaux;
+      if (MH == 1 && !OUT_F32 && p.epi != 0) {
+        // Fused epilogues (BM = 128 tiles only: their accumulator is double-buffered, so this work
+        // overlaps the next tile's MMAs): chunks of the thread's accumulator row are drained into
+        // packed bf16 registers, TMEM is released after the last chunk's reads, and the chunk's
+        // outputs are computed and stored. Rounding to bf16 first matches what the separate
+        // SwiGLU / RoPE kernels would read.
+        constexpr int HALF = BN / 2;
+        constexpr int PER = p_epi_per<BN, Cfg::CSPLIT>();  // output columns per thread (epi 2, 3)
+        constexpr int PER1 = PER / 2;                      // (u, g) pairs per thread (epi 1)
+        constexpr int CH = 128;                             // columns per chunk
+        constexpr int CH1 = CH / 2;                        // pairs per chunk
+        const int pos = (p.epi == 3) ? (p.rope_pos ? p.rope_pos[min(row, p.M - 1)] : row % p.rope_seq) : 0;
+        const bool pos_ok = pos >= 0 && pos < p.rope_max;
+        if (p.epi == 3 && row_ok && !pos_ok && lane == 0) set_error(p.err, kErrBadArg);
+        const int n_chunks = (p.epi == 1 ? PER1 : PER) / (p.epi == 1 ? CH1 : CH);
 #pragma unroll 1
-        for (int c = 0; c < PER; c += 32) {
-          uint32_t ru[32], rg[32];
-          tmem_ld32(tb + c, ru);
-          tmem_ld32(tb + HALF + c, rg);
-          tmem_wait_ld();
-          if (c + 32 >= PER) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[acc]);
-          }
-          if (!row_ok) continue;
+        for (int ck = 0; ck < n_chunks; ++ck) {
+          // packed bf16 values; epi 1 keeps u in pa[0, CH1 / 2) and g in pa[CH1 / 2, CH1)
+          uint32_t pa[CH / 2];
+          uint32_t* pb = pa + CH1 / 2;
+          if (p.epi == 1) {
+            const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (acc * MH + half) * BN + cpart * PER1 + ck * CH1;
 #pragma unroll
-          for (int g8 = 0; g8 < 32; g8 += 8) {
-            const int j = j0 + c + g8;
-            if (j >= p.F) break;
-            uint32_t hu[4], hg[4], ha[4];
+            for (int part = 0; part < 2; ++part) {  // u columns, then g columns: one 32-column load live
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float u0 = __uint_as_float(ru[g8 + 2 * e]) * p.alpha, u1 = __uint_as_float(ru[g8 + 2 * e + 1]) * p.alpha;
-              const float v0 = __uint_as_float(rg[g8 + 2 * e]) * p.alpha, v1 = __uint_as_float(rg[g8 + 2 * e + 1]) * p.alpha;
-              hu[e] = pack_bf16(u0, u1);
-              hg[e] = pack_bf16(v0, v1);
-              // a from the bf16-rounded h, exactly what the separate SwiGLU kernel would compute
-              const float2 ub = unpack_bf16(hu[e]), gb = unpack_bf16(hg[e]);
-              ha[e] = pack_bf16(ub.x * gb.x * sigmoid_f(gb.x), ub.y * gb.y * sigmoid_f(gb.y));
-            }
-            if (j + 8 <= p.F && p.vec_ok) {
-              *reinterpret_cast<uint4*>(hrow + j) = make_uint4(hu[0], hu[1], hu[2], hu[3]);
-              *reinterpret_cast<uint4*>(hrow + p.F + j) = make_uint4(hg[0], hg[1], hg[2], hg[3]);
-              *reinterpret_cast<uint4*>(arow + j) = make_uint4(ha[0], ha[1], ha[2], ha[3]);
-            } else {
+              for (int c = 0; c < CH1; c += 32) {
+                uint32_t r[32];
+                tmem_ld32(tb + part * HALF + c, r);
+                tmem_wait_ld();
 #pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                if (j + e >= p.F) continue;
-                const int sh = (e & 1) * 16;
-                hrow[j + e] = __ushort_as_bfloat16((unsigned short)(hu[e >> 1] >> sh));
-                hrow[p.F + j + e] = __ushort_as_bfloat16((unsigned short)(hg[e >> 1] >> sh));
-                arow[j + e] = __ushort_as_bfloat16((unsigned short)(ha[e >> 1] >> sh));
+                for (int e = 0; e < 16; ++e)
+                  pa[part * (CH1 / 2) + c / 2 + e] =
+                      pack_bf16(__uint_as_float(r[2 * e]) * p.alpha, __uint_as_float(r[2 * e + 1]) * p.alpha);
               }
             }
-          }
-        }
-        if (++acc == NACC) {
-          acc = 0;
-          acc_phase ^= 1;
-        }
-        continue;
-      }
-      if (!OUT_F32 && p.epi == 3) {
-        int pos = p.rope_pos ? p.rope_pos[min(row, p.M - 1)] : row % p.rope_seq;
-        const bool pos_ok = pos >= 0 && pos < p.rope_max;
-        if (row_ok && !pos_ok && lane == 0) set_error(p.err, kErrBadArg);
-        __nv_bfloat16* dr = reinterpret_cast<__nv_bfloat16*>(p.D) + (long long)row * p.ldd;
-#pragma unroll 1
-        for (int c = 0; c < BNP; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(t_acc + c, r);
-          tmem_wait_ld();
-          if (c + 32 >= BNP) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[acc]);
-          }
-          if (!row_ok) continue;
-          const int j0 = n0 + c;
-          uint32_t o[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            float x0 = no_k ? 0.f : __uint_as_float(r[2 * e]) * p.alpha;
-            float x1 = no_k ? 0.f : __uint_as_float(r[2 * e + 1]) * p.alpha;
-            const int j = j0 + 2 * e;
-            if (pos_ok && j < p.rope_cols) {
-              const float2 cs = p.rope_cs[(long long)pos * (p.rope_hd / 2) + (j % p.rope_hd) / 2];
-              const float y0 = x0 * cs.x - x1 * cs.y, y1 = x0 * cs.y + x1 * cs.x;
-              x0 = y0;
-              x1 = y1;
-            }
-            o[e] = pack_bf16(x0, x1);
-          }
-          if (j0 + 32 <= p.N && p.vec_ok) {
-            uint4* dst = reinterpret_cast<uint4*>(dr + j0);
-#pragma unroll
-            for (int v4 = 0; v4 < 4; ++v4) dst[v4] = make_uint4(o[4 * v4], o[4 * v4 + 1], o[4 * v4 + 2], o[4 * v4 + 3]);
           } else {
 #pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (j0 + e < p.N) dr[j0 + e] = __ushort_as_bfloat16((unsigned short)(o[e >> 1] >> ((e & 1) * 16)));
+            for (int c = 0; c < CH; c += 32) {
+              uint32_t r[32];
+              tmem_ld32(t_acc + ck * CH + c, r);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 16; ++e)
+                pa[c / 2 + e] = no_k ? 0u : pack_bf16(__uint_as_float(r[2 * e]) * p.alpha,
+                                                      __uint_as_float(r[2 * e + 1]) * p.alpha);
+            }
           }
-        }
-        if (++acc == NACC) {
-          acc = 0;
-          acc_phase ^= 1;
-        }
-        continue;
-      }
-      if (!OUT_F32 && p.epi == 2) {
-        const __nv_bfloat16* hr = p.h + (long long)row * p.ldh;
-        __nv_bfloat16* dh = p.aux + (long long)row * p.ldaux;
-#pragma unroll 1
-        for (int c = 0; c < BNP; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(t_acc + c, r);
-          tmem_wait_ld();
-          if (c + 32 >= BNP) {
+          if (ck + 1 == n_chunks) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[acc]);
           }
           if (!row_ok) continue;
+          if (p.epi == 1) {
+            // h = (u, g) and a = silu(g) * u for output columns j0 .. j0 + CH1
+            const int j0 = nb * HALF + cpart * PER1 + ck * CH1;
+            __nv_bfloat16* hrow = reinterpret_cast<__nv_bfloat16*>(p.D) + (long long)row * p.ldd;
+            __nv_bfloat16* arow = p.aux + (long long)row * p.ldaux;
 #pragma unroll
-          for (int g8 = 0; g8 < 32; g8 += 8) {
-            const int j = n0 + c + g8;
-            if (j >= p.N) break;
-            float u[8], gt[8], da[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) da[e] = no_k ? 0.f : __uint_as_float(r[g8 + e]) * p.alpha;
-            if (j + 8 <= p.N && p.vec_ok) {
-              const uint4 uu = *reinterpret_cast<const uint4*>(hr + j);
-              const uint4 gg = *reinterpret_cast<const uint4*>(hr + p.F + j);
-              const uint32_t uw[4] = {uu.x, uu.y, uu.z, uu.w}, gw[4] = {gg.x, gg.y, gg.z, gg.w};
+            for (int g8 = 0; g8 < CH1; g8 += 8) {
+              const int j = j0 + g8;
+              uint32_t ha[4];
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                const float2 a2 = unpack_bf16(uw[e]), b2 = unpack_bf16(gw[e]);
-                u[2 * e] = a2.x;
-                u[2 * e + 1] = a2.y;
-                gt[2 * e] = b2.x;
-                gt[2 * e + 1] = b2.y;
+                const float2 ub = unpack_bf16(pa[g8 / 2 + e]), gb = unpack_bf16(pb[g8 / 2 + e]);
+                ha[e] = pack_bf16(ub.x * gb.x * sigmoid_f(gb.x), ub.y * gb.y * sigmoid_f(gb.y));
               }
-            } else {
+              if (j + 8 <= p.F && p.vec_ok) {
+                *reinterpret_cast<uint4*>(hrow + j) =
+                    make_uint4(pa[g8 / 2], pa[g8 / 2 + 1], pa[g8 / 2 + 2], pa[g8 / 2 + 3]);
+                *reinterpret_cast<uint4*>(hrow + p.F + j) =
+                    make_uint4(pb[g8 / 2], pb[g8 / 2 + 1], pb[g8 / 2 + 2], pb[g8 / 2 + 3]);
+                *reinterpret_cast<uint4*>(arow + j) = make_uint4(ha[0], ha[1], ha[2], ha[3]);
+              } else {
 #pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                u[e] = j + e < p.N ? __bfloat162float(hr[j + e]) : 0.f;
-                gt[e] = j + e < p.N ? __bfloat162float(hr[p.F + j + e]) : 0.f;
+                for (int e = 0; e < 8; ++e) {
+                  if (j + e >= p.F) continue;
+                  const int sh = (e & 1) * 16;
+                  hrow[j + e] = __ushort_as_bfloat16((unsigned short)(pa[g8 / 2 + e / 2] >> sh));
+                  hrow[p.F + j + e] = __ushort_as_bfloat16((unsigned short)(pb[g8 / 2 + e / 2] >> sh));
+                  arow[j + e] = __ushort_as_bfloat16((unsigned short)(ha[e >> 1] >> sh));
+                }
               }
             }
-            // da rounded to bf16 first, as the separate SwiGLU backward kernel reads it
-            uint32_t du[4], dg[4];
+          } else if (p.epi == 2) {
+            // dh = (da * silu(g), da * u * silu'(g)) with the saved h
+            const __nv_bfloat16* hr = p.h + (long long)row * p.ldh;
+            __nv_bfloat16* dh = p.aux + (long long)row * p.ldaux;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 d2 = unpack_bf16(pack_bf16(da[2 * e], da[2 * e + 1]));
-              const float s0 = sigmoid_f(gt[2 * e]), s1 = sigmoid_f(gt[2 * e + 1]);
-              du[e] = pack_bf16(d2.x * gt[2 * e] * s0, d2.y * gt[2 * e + 1] * s1);
-              dg[e] = pack_bf16(d2.x * u[2 * e] * s0 * (1.f + gt[2 * e] * (1.f - s0)),
-                                d2.y * u[2 * e + 1] * s1 * (1.f + gt[2 * e + 1] * (1.f - s1)));
+            for (int g8 = 0; g8 < CH; g8 += 8) {
+              const int j = n0 + ck * CH + g8;
+              if (j >= p.N) break;
+              float u[8], gt[8];
+              if (j + 8 <= p.N && p.vec_ok) {
+                const uint4 uu = *reinterpret_cast<const uint4*>(hr + j);
+                const uint4 gg = *reinterpret_cast<const uint4*>(hr + p.F + j);
+                const uint32_t uw[4] = {uu.x, uu.y, uu.z, uu.w}, gw[4] = {gg.x, gg.y, gg.z, gg.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 a2 = unpack_bf16(uw[e]), b2 = unpack_bf16(gw[e]);
+                  u[2 * e] = a2.x;
+                  u[2 * e + 1] = a2.y;
+                  gt[2 * e] = b2.x;
+                  gt[2 * e + 1] = b2.y;
+                }
+              } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  u[e] = j + e < p.N ? __bfloat162float(hr[j + e]) : 0.f;
+                  gt[e] = j + e < p.N ? __bfloat162float(hr[p.F + j + e]) : 0.f;
+                }
+              }
+              uint32_t du[4], dg[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 d2 = unpack_bf16(pa[g8 / 2 + e]);
+                const float s0 = sigmoid_f(gt[2 * e]), s1 = sigmoid_f(gt[2 * e + 1]);
+                du[e] = pack_bf16(d2.x * gt[2 * e] * s0, d2.y * gt[2 * e + 1] * s1);
+                dg[e] = pack_bf16(d2.x * u[2 * e] * s0 * (1.f + gt[2 * e] * (1.f - s0)),
+                                  d2.y * u[2 * e + 1] * s1 * (1.f + gt[2 * e + 1] * (1.f - s1)));
+              }
+              if (j + 8 <= p.N && p.vec_ok) {
+                *reinterpret_cast<uint4*>(dh + j) = make_uint4(du[0], du[1], du[2], du[3]);
+                *reinterpret_cast<uint4*>(dh + p.F + j) = make_uint4(dg[0], dg[1], dg[2], dg[3]);
+              } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  if (j + e >= p.N) continue;
+                  const int sh = (e & 1) * 16;
+                  dh[j + e] = __ushort_as_bfloat16((unsigned short)(du[e >> 1] >> sh));
+                  dh[p.F + j + e] = __ushort_as_bfloat16((unsigned short)(dg[e >> 1] >> sh));
+                }
+              }
             }
-            if (j + 8 <= p.N && p.vec_ok) {
-              *reinterpret_cast<uint4*>(dh + j) = make_uint4(du[0], du[1], du[2], du[3]);
-              *reinterpret_cast<uint4*>(dh + p.F + j) = make_uint4(dg[0], dg[1], dg[2], dg[3]);
-            } else {
+          } else {
+            // epi 3: RoPE on the bf16-rounded values (as the separate in-place kernel does)
+            __nv_bfloat16* dr = reinterpret_cast<__nv_bfloat16*>(p.D) + (long long)row * p.ldd;
+            const int jb = n0 + ck * CH;
 #pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                if (j + e >= p.N) continue;
-                const int sh = (e & 1) * 16;
-                dh[j + e] = __ushort_as_bfloat16((unsigned short)(du[e >> 1] >> sh));
-                dh[p.F + j + e] = __ushort_as_bfloat16((unsigned short)(dg[e >> 1] >> sh));
+            for (int e = 0; e < CH / 2; ++e) {
+              const int j = jb + 2 * e;
+              if (pos_ok && j < p.rope_cols) {
+                const float2 x = unpack_bf16(pa[e]);
+                const float2 cs = p.rope_cs[(long long)pos * (p.rope_hd / 2) + (j % p.rope_hd) / 2];
+                pa[e] = pack_bf16(x.x * cs.x - x.y * cs.y, x.x * cs.y + x.y * cs.x);
+              }
+            }
+#pragma unroll
+            for (int g8 = 0; g8 < CH; g8 += 8) {
+              const int j = jb + g8;
+              if (j + 8 <= p.N && p.vec_ok) {
+                *reinterpret_cast<uint4*>(dr + j) =
+                    make_uint4(pa[g8 / 2], pa[g8 / 2 + 1], pa[g8 / 2 + 2], pa[g8 / 2 + 3]);
+              } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                  if (j + e < p.N)
+                    dr[j + e] = __ushort_as_bfloat16((unsigned short)(pa[g8 / 2 + e / 2] >> ((e & 1) * 16)));
               }
             }
           }
@@ -857,11 +858,7 @@ void gemm_swiglu_bf16(int mode, const void* A, long long lda, const void* B, lon
   cudaGetDevice(&dev);
   const int sms = num_sms(dev);
   const int BN = 256;
-  int BM = 128, bn_unused = 256;
-  if (mode == 1)
-    BM = M > 128 ? 256 : 128;
-  else
-    pick_tile(M, F, 1, sms, BM, bn_unused);
+  const int BM = 128;  // the fused epilogues run on 128-row tiles (double-buffered accumulator)
   if (mode == 2 && F <= 128) throw std::runtime_error("gemm_swiglu mode 2: F > 128");
   CUtensorMap ta, tb;
   {
@@ -917,10 +914,7 @@ void gemm_swiglu_bf16(int mode, const void* A, long long lda, const void* B, lon
   p.rope_max = 0;
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, sms);
-  if (BM == 256)
-    dispatch_majors<256, 256>(0, mode == 1 ? 0 : b_mn, 0, ta, tb, p, grid, stream);
-  else
-    dispatch_majors<128, 256>(0, mode == 1 ? 0 : b_mn, 0, ta, tb, p, grid, stream);
+  dispatch_majors<128, 256>(0, mode == 1 ? 0 : b_mn, 0, ta, tb, p, grid, stream);
 }
 
 
@@ -934,8 +928,8 @@ void gemm_rope_bf16(const void* A, long long lda, const void* B, long long ldb, 
   int dev = 0;
   cudaGetDevice(&dev);
   const int sms = num_sms(dev);
-  int BM = 128, BN = 256;
-  pick_tile(M, N, 1, sms, BM, BN);
+  const int BM = 128;  // the fused epilogues run on 128-row tiles (double-buffered accumulator)
+  const int BN = N <= 128 ? 128 : 256;
   CUtensorMap ta, tb;
   {
     uint64_t dims[3] = {(uint64_t)K, (uint64_t)M, 1};
@@ -985,9 +979,7 @@ void gemm_rope_bf16(const void* A, long long lda, const void* B, long long ldb, 
   p.rope_max = max_pos;
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, sms);
-  if (BM == 256)
-    dispatch_majors<256, 256>(0, 0, 0, ta, tb, p, grid, stream);
-  else if (BN == 256)
+  if (BN == 256)
     dispatch_majors<128, 256>(0, 0, 0, ta, tb, p, grid, stream);
   else
     dispatch_majors<128, 128>(0, 0, 0, ta, tb, p, grid, stream);

@@ -111,9 +111,12 @@ def pack_params(params) -> torch.Tensor:
     if len(params) > 1 and _packed(params):
         return _packed_view(params)
     rows = sum(p.shape[0] for p in params)
-    buf = torch.empty((rows, base.shape[1]), device=base.device, dtype=base.dtype)
+    # parameters must stay normal tensors even when first packed under inference_mode (a rollout
+    # before any training step): a buffer made there could never be saved for backward
+    with torch.inference_mode(False):
+        buf = torch.empty((rows, base.shape[1]), device=base.device, dtype=base.dtype)
     r = 0
-    with torch.no_grad():
+    with torch.inference_mode(False), torch.no_grad():
         for p in params:
             n = p.shape[0]
             buf[r:r + n].copy_(p.data)

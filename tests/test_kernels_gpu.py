@@ -308,16 +308,16 @@ def test_skinny_gemm(M, N, K):
     assert rel_err(y, ref) < 1e-2
 
 
-@pytest.mark.parametrize("M,d,F", [(512, 256, 384), (300, 512, 1408), (2048, 2048, 5632)])
-def test_swiglu_mlp_fused_epilogues(M, d, F):
+@pytest.mark.parametrize("M,d,Fw", [(512, 256, 384), (300, 512, 1408), (2048, 2048, 5632)])
+def test_swiglu_mlp_fused_epilogues(M, d, Fw):
     """Fused SwiGLU MLP (paired up/gate tiles writing h and a; dh from the down data-gradient
     epilogue) against an fp32 reference, with weight gradients accumulated over two calls."""
     from astrai_b200.ops.gemm import swiglu_mlp
 
     torch.manual_seed(M)
-    up, gate = (torch.nn.Parameter((torch.randn(F, d, device="cuda") * d ** -0.5).to(torch.bfloat16))
+    up, gate = (torch.nn.Parameter((torch.randn(Fw, d, device="cuda") * d ** -0.5).to(torch.bfloat16))
                 for _ in range(2))
-    down = torch.nn.Parameter((torch.randn(d, F, device="cuda") * F ** -0.5).to(torch.bfloat16))
+    down = torch.nn.Parameter((torch.randn(d, Fw, device="cuda") * Fw ** -0.5).to(torch.bfloat16))
     xs = [torch.randn(M, d, device="cuda", dtype=torch.bfloat16, requires_grad=True) for _ in range(2)]
     res = torch.randn(M, d, device="cuda", dtype=torch.bfloat16)
     gs = [torch.randn(M, d, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
