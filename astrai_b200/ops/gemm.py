@@ -56,6 +56,12 @@ def _as_rows(t: torch.Tensor) -> torch.Tensor:
 
 SKINNY_MAX_ROWS = 16
 
+# SwiGLU / RoPE in GEMM epilogues (gemm_swiglu, gemm_rope): correct, but measured slower on B200 in
+# the 1.1B training step (the 4 epilogue warps of a 128-row tile become the bottleneck once they
+# carry the extra memory traffic, and the larger 256-row tiles cannot hold the registers), so the
+# separate full-GPU kernels are the default; set ASTRAI_FUSED_EPILOGUES=1 to use the fused ones.
+FUSED_EPILOGUES = __import__("os").environ.get("ASTRAI_FUSED_EPILOGUES", "0") == "1"
+
 
 def _skinny(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
     """Decode-shaped products (<= 16 rows, no autograd): the skinny kernel that
@@ -264,6 +270,8 @@ def swiglu_mlp(x: torch.Tensor, up: torch.Tensor, gate: torch.Tensor, down: torc
     """Fused SwiGLU MLP on the kernel path, or None when it does not apply (then compose
     :func:`packed_linear`, :func:`astrai_b200.ops.activation.swiglu` and :func:`linear`)."""
     params = (up, gate, down)
+    if not FUSED_EPILOGUES:
+        return None
     if not (x.is_cuda and x.dtype == torch.bfloat16 and all(
             p.is_cuda and p.dtype == torch.bfloat16 and type(p.data) is torch.Tensor for p in params)):
         return None
@@ -314,6 +322,8 @@ def packed_linear_rope(x: torch.Tensor, params, table: torch.Tensor, positions: 
     """Packed projection with interleaved RoPE on its first ``rope_cols`` output columns (the q and k heads
     of a fused QKV projection), or None when the kernel path does not apply."""
     params = list(params)
+    if not FUSED_EPILOGUES:
+        return None
     if not (x.is_cuda and x.dtype == torch.bfloat16 and all(
             p.is_cuda and p.dtype == torch.bfloat16 and type(p.data) is torch.Tensor for p in params)):
         return None

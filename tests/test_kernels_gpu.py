@@ -312,8 +312,10 @@ def test_skinny_gemm(M, N, K):
 def test_swiglu_mlp_fused_epilogues(M, d, Fw):
     """Fused SwiGLU MLP (paired up/gate tiles writing h and a; dh from the down data-gradient
     epilogue) against an fp32 reference, with weight gradients accumulated over two calls."""
+    import astrai_b200.ops.gemm as G
     from astrai_b200.ops.gemm import swiglu_mlp
 
+    G.FUSED_EPILOGUES = True  # the test exercises the fused kernels whatever the default
     torch.manual_seed(M)
     up, gate = (torch.nn.Parameter((torch.randn(Fw, d, device="cuda") * d ** -0.5).to(torch.bfloat16))
                 for _ in range(2))
@@ -346,10 +348,12 @@ def test_swiglu_mlp_fused_epilogues(M, d, Fw):
 def test_qkv_projection_with_rope_epilogue(with_pos):
     """RoPE applied in the QKV projection epilogue + attention on pre-rotated q/k equals the
     unfused projection + in-place RoPE + attention, in value and in the input/weight gradients."""
+    import astrai_b200.ops.gemm as G
     from astrai_b200.ops.attention import attention_qkv
     from astrai_b200.ops.gemm import packed_linear, packed_linear_rope
     from astrai_b200.ops.rope import rope_table
 
+    G.FUSED_EPILOGUES = True  # the test exercises the fused kernels whatever the default
     torch.manual_seed(12)
     B, S, Hq, Hkv, D, d = 2, 256, 4, 2, 128, 512
     tab = rope_table(D, 1024, 1e6, device="cuda")
