@@ -23,8 +23,8 @@
 // dw; order them on one stream or serialise them.
 //
 // Setup: the first call on each device looks up the array's device address
-// (cudaGetSymbolAddress) and sets the kernels' shared-memory attribute, with
-// that device current. Make that first call before any stream capture begins.
+// (cudaGetSymbolAddress) with that device current. Make that first call before
+// any stream capture begins.
 //
 // Arguments: bf16 row-major dy / x / dx with row strides in elements (16-byte
 // aligned rows), bf16 weight w [D], fp32 rstd [rows] from the forward pass;

@@ -21,6 +21,7 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
                long long strideD, int out_f32, long long ldc, long long strideC, float alpha, float beta,
                int force_bn, cudaStream_t stream);
 void gemm_profile_set(unsigned long long* counters);
+void gemm_plan(int M, int N, int K, int batch, int* out);
 void gemm_rope_bf16(const void* A, long long lda, const void* B, long long ldb, void* D, long long ldd, int M, int N,
                     int K, const void* cs, const int* pos, int seq, int rope_cols, int head_dim, int max_pos,
                     cudaStream_t stream);
@@ -216,7 +217,7 @@ void rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, c10::o
   check_rows(y, "y");
   const int D = (int)x.size(1);
   TORCH_CHECK(w.numel() == D && w.is_contiguous(), "w shape");
-  TORCH_CHECK(D % 8 == 0 && (D <= 256 ? D % 32 == 0 : true), "rmsnorm: unsupported width ", D);
+  TORCH_CHECK(D % 8 == 0 && D <= 8192 && (D <= 256 ? D % 32 == 0 : true), "rmsnorm: unsupported width ", D);
   float* r = nullptr;
   if (rstd.has_value() && rstd->defined()) {
     TORCH_CHECK(rstd->scalar_type() == at::kFloat && rstd->numel() == x.size(0), "rstd");
@@ -436,6 +437,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "bf16 tcgen05 GEMM", py::arg("a"), py::arg("b"), py::arg("d"), py::arg("c") = py::none(),
         py::arg("a_mn") = 0, py::arg("b_mn") = 0, py::arg("alpha") = 1.0, py::arg("beta") = 0.0,
         py::arg("force_bn") = 0);
+  m.def("gemm_plan", [](int64_t M, int64_t N, int64_t K, int64_t batch) {
+    int o[5] = {0, 0, 0, 0, 0};
+    astrai_host::gemm_plan((int)M, (int)N, (int)K, (int)batch, o);
+    return py::make_tuple(o[0], o[1], (bool)o[2], o[3], o[4]);
+  }, py::arg("M"), py::arg("N"), py::arg("K"), py::arg("batch") = 1);
   m.def("gemm_profile_set", [](const c10::optional<at::Tensor>& counters) {
     // int64 [4] CUDA tensor that later GEMM launches add their wait cycles to, or None (off)
     if (counters.has_value() && counters->defined()) {

@@ -20,6 +20,9 @@
 // (astrai/model/components/linear.py:23-24) and the ATen matmuls of
 // torch.optim.Muon used by scripts/tools/train.py:58-72.
 #include <algorithm>
+#include <cstdlib>
+#include <mutex>
+#include <vector>
 #include <stdexcept>
 
 #include "common.cuh"
@@ -67,7 +70,91 @@ struct GemmParams {
   const float2* rope_cs;
   const int* rope_pos;
   int rope_seq, rope_cols, rope_hd, rope_max;
+  // Stream-K (sk_units > 0; plain GEMMs only): tiles [0, dp_tiles) are computed whole (CTA c takes
+  // c, c + G, ...); the k-blocks of the remaining tiles (sk_units = their count x k_blocks) are
+  // split evenly over the G CTAs, CTA c taking units [c U / G, (c + 1) U / G). Each CTA walks its
+  // unit range from the end, so its first stream-K item is the only one that can lack the tile's
+  // last k-block. Such a part (non-owner) stores its fp32 partial into its own slot sk_ws[c] and
+  // raises sk_flags[c]; the tile's owner (the CTA holding its last k-block, always the highest of
+  // the tile's CTAs) processes that tile last, waits for the flags of the lower CTAs that hold the
+  // tile's other parts, adds their slots into its accumulator, runs the normal epilogue and clears
+  // the flags for the next launch. Every wait is on a part that a lower CTA computed first.
+  int dp_tiles;
+  long long sk_units;
+  float* sk_ws;
+  int* sk_flags;
 };
+
+// One unit of a CTA's work: tile `tile`, k-blocks [kb0, kb1).
+struct WorkItem {
+  int tile, kb0, kb1;
+  int sk;       // stream-K tile index (tile - dp_tiles), -1 for a whole tile
+  int ord;      // number of lower CTAs holding parts of the tile
+  bool owner;   // holds the tile's last k-block
+  bool partial; // the tile is split over several CTAs
+};
+
+struct WorkIter {
+  int t;
+  long long u, u_end;
+  __device__ __forceinline__ void init(const GemmParams& p) {
+    t = blockIdx.x;
+    if (p.sk_units > 0) {
+      u = (long long)blockIdx.x * p.sk_units / gridDim.x;
+      u_end = (long long)(blockIdx.x + 1) * p.sk_units / gridDim.x;
+    } else {
+      u = u_end = 0;
+    }
+  }
+  // CTA whose unit range contains unit v (every range is non-empty: sk_units >= gridDim.x)
+  __device__ __forceinline__ static int cta_of_unit(const GemmParams& p, long long v) {
+    return (int)(((v + 1) * gridDim.x - 1) / p.sk_units);
+  }
+  __device__ __forceinline__ bool next(const GemmParams& p, int num_tiles, int kblk_full, WorkItem& w) {
+    const int limit = p.sk_units > 0 ? p.dp_tiles : num_tiles;
+    if (t < limit) {
+      w = {t, 0, kblk_full, -1, 0, true, false};
+      t += gridDim.x;
+      return true;
+    }
+    if (u >= u_end) return false;
+    // the last tile of the remaining range [u, u_end)
+    const int KB = p.k_blocks;
+    const long long tr = (u_end - 1) / KB;
+    const long long tbeg = tr * KB;
+    const long long lo = u > tbeg ? u : tbeg;
+    w.tile = p.dp_tiles + (int)tr;
+    w.kb0 = (int)(lo - tbeg);
+    w.kb1 = (int)(u_end - tbeg);
+    w.sk = (int)tr;
+    w.ord = (int)blockIdx.x - cta_of_unit(p, tbeg);  // lower CTAs holding parts of this tile
+    w.owner = w.kb1 == KB;
+    w.partial = !(w.kb0 == 0 && w.kb1 == KB);
+    u_end = lo;
+    return true;
+  }
+};
+
+__device__ __forceinline__ int ld_acquire_gpu_s32(const int* f) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu_s32(int* f, int v) {
+  asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+// Bounded wait until *f == want (other CTAs of this launch, all resident, advance it).
+__device__ __forceinline__ bool wait_flag_eq(const int* f, int want, int* err) {
+  const uint64_t t0 = globaltimer();
+  while (ld_acquire_gpu_s32(f) != want) {
+    if (globaltimer() - t0 > ASTRAI_WAIT_NS) {
+      set_error(err, kErrWaitFull);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
 
 __device__ __forceinline__ float sigmoid_f(float g) { return 1.f / (1.f + __expf(-g)); }
 
@@ -182,12 +269,17 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      WorkIter wi;
+      wi.init(p);
+      WorkItem w;
+      while (ok && wi.next(p, num_tiles, p.k_blocks, w)) {
+        const int tile = w.tile;
         int b, mb, nb;
         tile_coords(tile, p.tiles_m, p.tiles_n, b, mb, nb);
         const int m0 = mb * BM, n0 = nb * BN;
         const TileK tk = tile_k(p, b, mb, BK);
-        for (int kb = 0; kb < tk.kblk; ++kb) {
+        const int kbeg = w.sk >= 0 ? w.kb0 : 0, kend = w.sk >= 0 ? w.kb1 : tk.kblk;
+        for (int kb = kbeg; kb < kend; ++kb) {
           const long long tw0 = p.prof ? clock64() : 0;
           const bool got = mbar_wait(&empty[stage], phase ^ 1, p.err, kErrWaitEmpty);
           if (p.prof) atomicAdd(p.prof + 0, (unsigned long long)(clock64() - tw0));
@@ -234,17 +326,22 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      WorkIter wi;
+      wi.init(p);
+      WorkItem w;
+      while (ok && wi.next(p, num_tiles, p.k_blocks, w)) {
+        const int tile = w.tile;
         int b, mb, nb;
         tile_coords(tile, p.tiles_m, p.tiles_n, b, mb, nb);
         const int kblk = tile_k(p, b, mb, BK).kblk;
+        const int kbeg = w.sk >= 0 ? w.kb0 : 0, kend = w.sk >= 0 ? w.kb1 : kblk;
         const long long ta0 = p.prof ? clock64() : 0;
         const bool got_acc = mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err, kErrWaitAccEmpty);
         if (p.prof) atomicAdd(p.prof + 2, (unsigned long long)(clock64() - ta0));
         if (!got_acc) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * MH * BN;
-        for (int kb = 0; kb < kblk; ++kb) {
+        for (int kb = kbeg; kb < kend; ++kb) {
           const long long tf0 = p.prof ? clock64() : 0;
           const bool got = mbar_wait(&full[stage], phase, p.err, kErrWaitFull);
           if (p.prof) atomicAdd(p.prof + 1, (unsigned long long)(clock64() - tf0));
@@ -262,7 +359,7 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
             for (int h = 0; h < MH; ++h) {
               const uint64_t ad = A_MN ? sdesc_sw128(a_base + h * 16384 + k * 2048, 8192, 1024)
                                        : sdesc_sw128(a_base + h * 16384 + k * 32, 16, 1024);
-              umma_bf16(d_tmem + h * BN, ad, bd, idesc, (kb | k) != 0);
+              umma_bf16(d_tmem + h * BN, ad, bd, idesc, (kb != kbeg) || k != 0);
             }
           }
           umma_commit(&empty[stage]);
@@ -286,7 +383,13 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
     constexpr int BNP = BN / Cfg::CSPLIT;       // columns drained by one thread
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    WorkIter wi;
+    wi.init(p);
+    WorkItem w;
+    constexpr int EPI_THREADS = Cfg::EPI_WARPS * 32;
+    const int et = threadIdx.x - 64;  // epilogue thread index
+    while (wi.next(p, num_tiles, p.k_blocks, w)) {
+      const int tile = w.tile;
       int b, mb, nb;
       tile_coords(tile, p.tiles_m, p.tiles_n, b, mb, nb);
       const long long te0 = (p.prof && lane == 0) ? clock64() : 0;
@@ -294,6 +397,79 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
       if (p.prof && lane == 0 && warp == 2) atomicAdd(p.prof + 3, (unsigned long long)(clock64() - te0));
       if (!got_full) break;
       tc_fence_after();
+      if (w.partial) {
+        // stream-K part: a non-owner parks its fp32 partial in its own slot; the owner adds the
+        // lower CTAs' slots into its accumulator, then the regular epilogue below reads the sum.
+        // Slot layout is thread-major (float4 v of epilogue thread et at [v][et]), so every warp
+        // access is 512 contiguous bytes; owner and non-owner threads drain the same TMEM cells.
+        const uint32_t t_part = tmem_base + ((uint32_t)(q * 32) << 16) + (acc * MH + half) * BN + cpart * BNP;
+        if (!w.owner) {
+          float4* slot = reinterpret_cast<float4*>(p.sk_ws + (long long)blockIdx.x * BM * BN) + et;
+#pragma unroll 1
+          for (int c = 0; c < BNP; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(t_part + c, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int v4 = 0; v4 < 8; ++v4)
+              slot[(c / 4 + v4) * EPI_THREADS] =
+                  make_float4(__uint_as_float(r[4 * v4]), __uint_as_float(r[4 * v4 + 1]),
+                              __uint_as_float(r[4 * v4 + 2]), __uint_as_float(r[4 * v4 + 3]));
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[acc]);
+          __threadfence();
+          named_bar_sync(1, EPI_THREADS);
+          if (et == 0) st_release_gpu_s32(p.sk_flags + blockIdx.x, 1);
+          if (++acc == NACC) {
+            acc = 0;
+            acc_phase ^= 1;
+          }
+          continue;
+        }
+        const int c_first = (int)blockIdx.x - w.ord;
+        if (et == 0)
+          for (int j = c_first; j < (int)blockIdx.x; ++j)
+            if (!wait_flag_eq(p.sk_flags + j, 1, p.err)) break;
+        named_bar_sync(1, EPI_THREADS);
+#pragma unroll 1
+        for (int c = 0; c < BNP; c += 32) {
+          float4 y[8];
+          {
+            const float4* src = reinterpret_cast<const float4*>(p.sk_ws + (long long)c_first * BM * BN) + et;
+#pragma unroll
+            for (int v4 = 0; v4 < 8; ++v4) y[v4] = __ldcg(src + (c / 4 + v4) * EPI_THREADS);
+          }
+#pragma unroll 1
+          for (int j = c_first + 1; j < (int)blockIdx.x; ++j) {
+            const float4* src = reinterpret_cast<const float4*>(p.sk_ws + (long long)j * BM * BN) + et;
+#pragma unroll
+            for (int v4 = 0; v4 < 8; ++v4) {
+              const float4 z = __ldcg(src + (c / 4 + v4) * EPI_THREADS);
+              y[v4].x += z.x;
+              y[v4].y += z.y;
+              y[v4].z += z.z;
+              y[v4].w += z.w;
+            }
+          }
+          uint32_t r[32];
+          tmem_ld32(t_part + c, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int v4 = 0; v4 < 8; ++v4) {
+            r[4 * v4] = __float_as_uint(__uint_as_float(r[4 * v4]) + y[v4].x);
+            r[4 * v4 + 1] = __float_as_uint(__uint_as_float(r[4 * v4 + 1]) + y[v4].y);
+            r[4 * v4 + 2] = __float_as_uint(__uint_as_float(r[4 * v4 + 2]) + y[v4].z);
+            r[4 * v4 + 3] = __float_as_uint(__uint_as_float(r[4 * v4 + 3]) + y[v4].w);
+          }
+          tmem_st32(t_part + c, r);
+        }
+        tmem_wait_st();
+        named_bar_sync(1, EPI_THREADS);  // every thread has read the slots
+        if (et == 0)
+          for (int j = c_first; j < (int)blockIdx.x; ++j) p.sk_flags[j] = 0;  // ready for the next launch
+      }
       const bool no_k = tile_k(p, b, mb, 64).kblk == 0;  // nothing accumulated: the product is 0
       const int row = mb * BM + half * 128 + q * 32 + lane;
       const int n0 = nb * BN + cpart * BNP;
@@ -648,10 +824,67 @@ static void dispatch_majors(int a_mn, int b_mn, int out_f32, const CUtensorMap& 
 #undef ASTRAI_GEMM_CASE
 }
 
+// Stream-K decision: whole waves of tiles plus the last partial wave split into k-block units over
+// all CTAs (see GemmParams). Used when every CTA gets at least 4 k-blocks of the split wave and the
+// time saved, (whole waves - fractional waves) x k-blocks per tile, is at least 16 k-blocks: on
+// B200 the fix-up (partial slots through L2, the owner's fold) costs about as much as 10 k-blocks,
+// so shapes with short K (2048 - 3072) and a nearly full last wave measured slower split.
+// ASTRAI_STREAMK=0 disables it.
+static bool streamk_on() {
+  static const bool on = [] {
+    const char* e = std::getenv("ASTRAI_STREAMK");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+static bool use_streamk(long long tiles, int kb, int sms) {
+  if (!streamk_on() || tiles <= 0 || sms <= 0) return false;
+  const long long rem = tiles % sms;
+  if (rem == 0 || rem * kb < 4LL * sms) return false;
+  const double dp = (double)(tiles / sms + 1), sk = (double)tiles / sms + 0.08;
+  return (dp - sk) * kb >= 16.0;
+}
+static double effective_waves(long long tiles, int kb, int sms) {
+  return use_streamk(tiles, kb, sms) ? (double)tiles / sms + 0.08 : (double)((tiles + sms - 1) / sms);
+}
+
+// Stream-K fix-up buffers, one set per (device, stream), made once outside graph capture:
+// fp32 [sms][256 x 256] partial-tile slots (one per CTA) and [sms] slot flags (zero between launches).
+struct SkBuf {
+  cudaStream_t s;
+  float* ws;
+  int* flags;
+};
+static std::mutex g_sk_mu;
+static std::vector<SkBuf> g_sk_bufs[64];
+static bool sk_buffers(int dev, cudaStream_t s, int sms, float** ws, int** flags) {
+  std::lock_guard<std::mutex> lock(g_sk_mu);
+  for (const SkBuf& b : g_sk_bufs[dev & 63]) {
+    if (b.s == s) {
+      *ws = b.ws;
+      *flags = b.flags;
+      return true;
+    }
+  }
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return false;
+  SkBuf b{s, nullptr, nullptr};
+  if (cudaMalloc(&b.ws, (size_t)sms * 256 * 256 * sizeof(float)) != cudaSuccess) return false;
+  if (cudaMalloc(&b.flags, (size_t)sms * sizeof(int)) != cudaSuccess) {
+    cudaFree(b.ws);
+    return false;
+  }
+  cudaMemsetAsync(b.flags, 0, (size_t)sms * sizeof(int), s);
+  g_sk_bufs[dev & 63].push_back(b);
+  *ws = b.ws;
+  *flags = b.flags;
+  return true;
+}
+
 // Pick the tile shape minimising (waves x per-tile cost); per-tile costs are
 // relative throughputs of the three variants (256x256 moves the fewest bytes
-// per FLOP, 128x128 the most).
-static void pick_tile(int M, int N, int batch, int sms, int& bm, int& bn) {
+// per FLOP, 128x128 the most). Waves are fractional where Stream-K applies.
+static void pick_tile(int M, int N, int batch, int sms, int& bm, int& bn, int kb = 0) {
   // Measured on B200 (relative per-tile throughput at large K): 256x256 1.0,
   // 128x256 0.93; 128x128 is slower on every training shape and only used
   // when N <= 128.
@@ -664,8 +897,8 @@ static void pick_tile(int M, int N, int batch, int sms, int& bm, int& bn) {
   for (const Opt& o : opts) {
     if (o.bm == 256 && M <= 128) continue;
     const long long tiles = (long long)((M + o.bm - 1) / o.bm) * ((N + o.bn - 1) / o.bn) * batch;
-    const long long waves = (tiles + sms - 1) / sms;
-    const double t = (double)waves * o.bm * o.bn / o.rel_speed;
+    const double waves = kb > 0 ? effective_waves(tiles, kb, sms) : (double)((tiles + sms - 1) / sms);
+    const double t = waves * o.bm * o.bn / o.rel_speed;
     if (t < best * 0.999) {
       best = t;
       bm = o.bm;
@@ -678,6 +911,22 @@ static void pick_tile(int M, int N, int batch, int sms, int& bm, int& bn) {
 // a_mn == 0: A stored [batch][M][lda] (K contiguous); a_mn == 1: [batch][K][lda] (M contiguous).
 // b_mn == 0: B stored [batch][N][ldb];                b_mn == 1: [batch][K][ldb].
 // force_bn: 0 = automatic; 128 / 256 = BM 128 with that BN; 512 = 256 x 256 tiles.
+// The plan gemm_bf16 would use for a plain GEMM on the current device: tile shape and whether the
+// last partial wave is split Stream-K style (out: bm, bn, streamk, tiles, sms).
+void gemm_plan(int M, int N, int K, int batch, int* out) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int sms = num_sms(dev);
+  int BM = 128, BN = 256;
+  pick_tile(M, N, batch, sms, BM, BN, (K + 63) / 64);
+  const long long tiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN) * batch;
+  out[0] = BM;
+  out[1] = BN;
+  out[2] = use_streamk(tiles, (K + 63) / 64, sms) ? 1 : 0;
+  out[3] = (int)tiles;
+  out[4] = sms;
+}
+
 void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int N, int K, int batch, int a_mn,
                long long lda, long long strideA, int b_mn, long long ldb, long long strideB, long long ldd,
                long long strideD, int out_f32, long long ldc, long long strideC, float alpha, float beta,
@@ -692,7 +941,7 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
   } else if (force_bn == 512) {
     BM = 256;
   } else {
-    pick_tile(M, N, batch, sms, BM, BN);
+    pick_tile(M, N, batch, sms, BM, BN, (K + 63) / 64);
   }
 
   CUtensorMap ta, tb;
@@ -752,8 +1001,17 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
   p.rope_cols = 0;
   p.rope_hd = 2;
   p.rope_max = 0;
+  p.dp_tiles = 0;
+  p.sk_units = 0;
+  p.sk_ws = nullptr;
+  p.sk_flags = nullptr;
   const int tiles = batch * p.tiles_m * p.tiles_n;
-  const int grid = std::min(tiles, sms);
+  int grid = std::min(tiles, sms);
+  if (use_streamk(tiles, p.k_blocks, sms) && sk_buffers(dev, stream, sms, &p.sk_ws, &p.sk_flags)) {
+    p.dp_tiles = tiles / sms * sms;
+    p.sk_units = (long long)(tiles - p.dp_tiles) * p.k_blocks;
+    grid = sms;
+  }
   if (BM == 256)
     dispatch_majors<256, 256>(a_mn, b_mn, out_f32, ta, tb, p, grid, stream);
   else if (BN == 256)
@@ -834,6 +1092,10 @@ void gemm_grouped_bf16(int mode, const void* A, const void* B, void* D, const vo
   p.rope_cols = 0;
   p.rope_hd = 2;
   p.rope_max = 0;
+  p.dp_tiles = 0;
+  p.sk_units = 0;
+  p.sk_ws = nullptr;
+  p.sk_flags = nullptr;
   const int tiles = p.batch * p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, sms);
   if (BN == 256)
@@ -912,6 +1174,10 @@ void gemm_swiglu_bf16(int mode, const void* A, long long lda, const void* B, lon
   p.rope_cols = 0;
   p.rope_hd = 2;
   p.rope_max = 0;
+  p.dp_tiles = 0;
+  p.sk_units = 0;
+  p.sk_ws = nullptr;
+  p.sk_flags = nullptr;
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, sms);
   dispatch_majors<128, 256>(0, mode == 1 ? 0 : b_mn, 0, ta, tb, p, grid, stream);
@@ -977,6 +1243,10 @@ void gemm_rope_bf16(const void* A, long long lda, const void* B, long long ldb, 
   p.rope_cols = rope_cols;
   p.rope_hd = head_dim;
   p.rope_max = max_pos;
+  p.dp_tiles = 0;
+  p.sk_units = 0;
+  p.sk_ws = nullptr;
+  p.sk_flags = nullptr;
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, sms);
   if (BN == 256)

@@ -2,60 +2,87 @@
 //
 //   y = x * rsqrt(mean(x^2) + eps) * w          (astrai/model/components/norm.py:14-15)
 //
-// One warp per row; each lane owns a fixed set of 16-byte column chunks, so
-// the weight-gradient partial sums of a block stay in registers. Rows are
-// processed in fp32. Backward writes dx and per-block fp32 partials of dw,
-// which a second kernel reduces (dw is a sum over all rows).
+// Block per row: the 256 threads of a block share one row, each owning V fixed groups of 8
+// columns (16-byte loads and stores), and a block walks a contiguous range of rows. The loads of
+// row i + 1 are issued before row i's block-wide reduction, so each thread keeps one row's worth
+// of DRAM reads in flight while it waits on the reduction barrier; with every block resident
+// (about 4 per SM) that is enough memory parallelism to approach copy bandwidth. Rows are
+// processed in fp32. Backward writes dx (plus the residual-branch gradient when given) and one
+// fp32 dw partial per block, which stays in registers over the block's rows; a second kernel sums
+// the partials (dw is a sum over all rows). Small D (<= 256, per-head norms) uses one warp per row.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace astrai {
 
-template <int CHUNKS>  // 16-byte chunks (8 bf16) per lane; D = CHUNKS * 256
-__global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
-                                                          const __nv_bfloat16* __restrict__ w,
-                                                          __nv_bfloat16* __restrict__ y, long long ldy,
-                                                          float* __restrict__ rstd_out, int rows, int D, float eps) {
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  const __nv_bfloat16* xr = x + (long long)row * ldx;
-  float v[CHUNKS][8];
-  float ss = 0.f;
+constexpr int kNormThreads = 256;
+constexpr int kNormBlocksTarget = 592;  // 4 resident 256-thread blocks on each of 148 SMs
+
+// Sum of v over the block (nw warps), through red[buf] (double-buffered by the caller so that one
+// barrier per row suffices: a buffer is rewritten only after the next row's barrier).
+__device__ __forceinline__ float block_sum(float v, float* red, int nw) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int k = 0; k < nw; ++k) t += red[k];
+  return t;
+}
+
+template <int V>  // 8-column groups per thread; D <= V * 8 * blockDim.x
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
+                                                                   const __nv_bfloat16* __restrict__ w,
+                                                                   __nv_bfloat16* __restrict__ y, long long ldy,
+                                                                   float* __restrict__ rstd_out, int rows, int D,
+                                                                   float eps, int rows_per_block) {
+  __shared__ float red[2][32];
+  const int T = blockDim.x, nw = T >> 5;
+  int col[V];
+  uint4 wp[V], cur[V];
 #pragma unroll
-  for (int c = 0; c < CHUNKS; ++c) {
-    const int col = (c * 32 + lane) * 8;
-    if (col < D) {
-      uint4 u = *reinterpret_cast<const uint4*>(xr + col);
-      uint32_t uu[4] = {u.x, u.y, u.z, u.w};
+  for (int v = 0; v < V; ++v) {
+    col[v] = (v * T + threadIdx.x) * 8;
+    wp[v] = col[v] < D ? *reinterpret_cast<const uint4*>(w + col[v]) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  const int r0 = blockIdx.x * rows_per_block, r1 = min(rows, r0 + rows_per_block);
+#pragma unroll
+  for (int v = 0; v < V; ++v)
+    cur[v] = (r0 < r1 && col[v] < D) ? *reinterpret_cast<const uint4*>(x + (long long)r0 * ldx + col[v])
+                                     : make_uint4(0u, 0u, 0u, 0u);
+  for (int row = r0; row < r1; ++row) {
+    uint4 nxt[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v)
+      nxt[v] = (row + 1 < r1 && col[v] < D) ? *reinterpret_cast<const uint4*>(x + (long long)(row + 1) * ldx + col[v])
+                                            : make_uint4(0u, 0u, 0u, 0u);
+    float ss = 0.f;
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const uint32_t u[4] = {cur[v].x, cur[v].y, cur[v].z, cur[v].w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        float2 f = unpack_bf16(uu[j]);
-        v[c][2 * j] = f.x;
-        v[c][2 * j + 1] = f.y;
+        const float2 f = unpack_bf16(u[j]);
         ss += f.x * f.x + f.y * f.y;
       }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[c][j] = 0.f;
     }
-  }
-  ss = warp_sum(ss);
-  const float r = rsqrtf(ss / (float)D + eps);
-  if (lane == 0 && rstd_out) rstd_out[row] = r;
-  __nv_bfloat16* yr = y + (long long)row * ldy;
+    ss = block_sum(ss, red[row & 1], nw);
+    const float r = rsqrtf(ss / (float)D + eps);
+    if (threadIdx.x == 0 && rstd_out) rstd_out[row] = r;
 #pragma unroll
-  for (int c = 0; c < CHUNKS; ++c) {
-    const int col = (c * 32 + lane) * 8;
-    if (col < D) {
-      uint4 wu = *reinterpret_cast<const uint4*>(w + col);
-      uint32_t ww[4] = {wu.x, wu.y, wu.z, wu.w};
-      uint32_t o[4];
+    for (int v = 0; v < V; ++v) {
+      if (col[v] < D) {
+        const uint32_t u[4] = {cur[v].x, cur[v].y, cur[v].z, cur[v].w};
+        const uint32_t ww[4] = {wp[v].x, wp[v].y, wp[v].z, wp[v].w};
+        uint32_t o[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float2 wf = unpack_bf16(ww[j]);
-        o[j] = pack_bf16(v[c][2 * j] * r * wf.x, v[c][2 * j + 1] * r * wf.y);
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = unpack_bf16(u[j]), wf = unpack_bf16(ww[j]);
+          o[j] = pack_bf16(f.x * r * wf.x, f.y * r * wf.y);
+        }
+        *reinterpret_cast<uint4*>(y + (long long)row * ldy + col[v]) = make_uint4(o[0], o[1], o[2], o[3]);
       }
-      *reinterpret_cast<uint4*>(yr + col) = make_uint4(o[0], o[1], o[2], o[3]);
+      cur[v] = nxt[v];
     }
   }
 }
@@ -88,111 +115,92 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_small_kernel(const __nv_bfloa
     if (j < per) yr[lane * per + j] = __float2bfloat16_rn(v[j] * r * __bfloat162float(w[lane * per + j]));
 }
 
-// dx = r*w*dy - x * r^3 * mean(dy*w*x);   dw_partial[block] = sum_rows dy*x*r
-template <int CHUNKS>
-__global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, long long lddy,
-                                                          const __nv_bfloat16* __restrict__ x, long long ldx,
-                                                          const __nv_bfloat16* __restrict__ w,
-                                                          const float* __restrict__ rstd,
-                                                          __nv_bfloat16* __restrict__ dx, long long lddx,
-                                                          const __nv_bfloat16* __restrict__ dres, long long ldres,
-                                                          float* __restrict__ dw_part, int rows, int D,
-                                                          int rows_per_block) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float wv[CHUNKS][8];
-  float acc[CHUNKS][8];
+// dx = r*w*dy - x * r^3 * mean(dy*w*x) (+ dres);   dw_partial[block] = sum over the block's rows of dy*x*r
+template <int V>
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, long long lddy,
+                                                                   const __nv_bfloat16* __restrict__ x, long long ldx,
+                                                                   const __nv_bfloat16* __restrict__ w,
+                                                                   const float* __restrict__ rstd,
+                                                                   __nv_bfloat16* __restrict__ dx, long long lddx,
+                                                                   const __nv_bfloat16* __restrict__ dres,
+                                                                   long long ldres, float* __restrict__ dw_part,
+                                                                   int rows, int D, int rows_per_block) {
+  __shared__ float red[2][32];
+  const int T = blockDim.x, nw = T >> 5;
+  int col[V];
+  uint4 wp[V], cx[V], cg[V], cr[V];
+  float acc[V][8];
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-  for (int c = 0; c < CHUNKS; ++c) {
-    const int col = (c * 32 + lane) * 8;
+  for (int v = 0; v < V; ++v) {
+    col[v] = (v * T + threadIdx.x) * 8;
+    wp[v] = col[v] < D ? *reinterpret_cast<const uint4*>(w + col[v]) : z;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[c][j] = 0.f;
-    if (col < D) {
-      uint4 wu = *reinterpret_cast<const uint4*>(w + col);
-      uint32_t ww[4] = {wu.x, wu.y, wu.z, wu.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float2 f = unpack_bf16(ww[j]);
-        wv[c][2 * j] = f.x;
-        wv[c][2 * j + 1] = f.y;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) wv[c][j] = 0.f;
-    }
+    for (int j = 0; j < 8; ++j) acc[v][j] = 0.f;
   }
-  const int r0 = blockIdx.x * rows_per_block;
-  const int r1 = min(rows, r0 + rows_per_block);
-  for (int row = r0 + warp; row < r1; row += 8) {
-    const float r = rstd[row];
-    float xv[CHUNKS][8], gv[CHUNKS][8];
+  const int r0 = blockIdx.x * rows_per_block, r1 = min(rows, r0 + rows_per_block);
+  float crs = r0 < r1 ? rstd[r0] : 0.f;
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const bool ok = r0 < r1 && col[v] < D;
+    cx[v] = ok ? *reinterpret_cast<const uint4*>(x + (long long)r0 * ldx + col[v]) : z;
+    cg[v] = ok ? *reinterpret_cast<const uint4*>(dy + (long long)r0 * lddy + col[v]) : z;
+    cr[v] = (ok && dres) ? *reinterpret_cast<const uint4*>(dres + (long long)r0 * ldres + col[v]) : z;
+  }
+  for (int row = r0; row < r1; ++row) {
+    // next row's loads first: they overlap this row's reduction
+    const bool more = row + 1 < r1;
+    const float nrs = more ? rstd[row + 1] : 0.f;
+    uint4 nx[V], ng[V], nr[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const bool ok = more && col[v] < D;
+      nx[v] = ok ? *reinterpret_cast<const uint4*>(x + (long long)(row + 1) * ldx + col[v]) : z;
+      ng[v] = ok ? *reinterpret_cast<const uint4*>(dy + (long long)(row + 1) * lddy + col[v]) : z;
+      nr[v] = (ok && dres) ? *reinterpret_cast<const uint4*>(dres + (long long)(row + 1) * ldres + col[v]) : z;
+    }
     float dot = 0.f;
 #pragma unroll
-    for (int c = 0; c < CHUNKS; ++c) {
-      const int col = (c * 32 + lane) * 8;
-      if (col < D) {
-        uint4 xu = *reinterpret_cast<const uint4*>(x + (long long)row * ldx + col);
-        uint4 gu = *reinterpret_cast<const uint4*>(dy + (long long)row * lddy + col);
-        uint32_t xx[4] = {xu.x, xu.y, xu.z, xu.w}, gg[4] = {gu.x, gu.y, gu.z, gu.w};
+    for (int v = 0; v < V; ++v) {
+      const uint32_t xx[4] = {cx[v].x, cx[v].y, cx[v].z, cx[v].w}, gg[4] = {cg[v].x, cg[v].y, cg[v].z, cg[v].w};
+      const uint32_t ww[4] = {wp[v].x, wp[v].y, wp[v].z, wp[v].w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float2 xf = unpack_bf16(xx[j]), gf = unpack_bf16(gg[j]);
-          xv[c][2 * j] = xf.x;
-          xv[c][2 * j + 1] = xf.y;
-          gv[c][2 * j] = gf.x;
-          gv[c][2 * j + 1] = gf.y;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) xv[c][j] = gv[c][j] = 0.f;
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        dot += gv[c][j] * wv[c][j] * xv[c][j];
-        acc[c][j] += gv[c][j] * xv[c][j] * r;
+      for (int j = 0; j < 4; ++j) {
+        const float2 xf = unpack_bf16(xx[j]), gf = unpack_bf16(gg[j]), wf = unpack_bf16(ww[j]);
+        dot += gf.x * wf.x * xf.x + gf.y * wf.y * xf.y;
       }
     }
-    dot = warp_sum(dot);
-    const float k = dot * r * r * r / (float)D;
+    dot = block_sum(dot, red[row & 1], nw);
+    const float r = crs, k = dot * r * r * r / (float)D;
 #pragma unroll
-    for (int c = 0; c < CHUNKS; ++c) {
-      const int col = (c * 32 + lane) * 8;
-      if (col < D) {
-        float add[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (dres) {  // gradient of the residual branch that also reads x
-          const uint4 ru = *reinterpret_cast<const uint4*>(dres + (long long)row * ldres + col);
-          const uint32_t rr[4] = {ru.x, ru.y, ru.z, ru.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 f = unpack_bf16(rr[j]);
-            add[2 * j] = f.x;
-            add[2 * j + 1] = f.y;
-          }
-        }
+    for (int v = 0; v < V; ++v) {
+      if (col[v] < D) {
+        const uint32_t xx[4] = {cx[v].x, cx[v].y, cx[v].z, cx[v].w}, gg[4] = {cg[v].x, cg[v].y, cg[v].z, cg[v].w};
+        const uint32_t rr[4] = {cr[v].x, cr[v].y, cr[v].z, cr[v].w}, ww[4] = {wp[v].x, wp[v].y, wp[v].z, wp[v].w};
         uint32_t o[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          o[j] = pack_bf16(r * wv[c][2 * j] * gv[c][2 * j] - xv[c][2 * j] * k + add[2 * j],
-                           r * wv[c][2 * j + 1] * gv[c][2 * j + 1] - xv[c][2 * j + 1] * k + add[2 * j + 1]);
-        *reinterpret_cast<uint4*>(dx + (long long)row * lddx + col) = make_uint4(o[0], o[1], o[2], o[3]);
+        for (int j = 0; j < 4; ++j) {
+          const float2 xf = unpack_bf16(xx[j]), gf = unpack_bf16(gg[j]), af = unpack_bf16(rr[j]),
+                       wf = unpack_bf16(ww[j]);
+          o[j] = pack_bf16(r * wf.x * gf.x - xf.x * k + af.x, r * wf.y * gf.y - xf.y * k + af.y);
+          acc[v][2 * j] += gf.x * xf.x * r;
+          acc[v][2 * j + 1] += gf.y * xf.y * r;
+        }
+        *reinterpret_cast<uint4*>(dx + (long long)row * lddx + col[v]) = make_uint4(o[0], o[1], o[2], o[3]);
       }
+      cx[v] = nx[v];
+      cg[v] = ng[v];
+      cr[v] = nr[v];
     }
+    crs = nrs;
   }
-  // reduce the 8 warps' partial dw through shared memory, one row per block
-  extern __shared__ float red[];  // [8][D]
 #pragma unroll
-  for (int c = 0; c < CHUNKS; ++c) {
-    const int col = (c * 32 + lane) * 8;
-    if (col < D) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) red[warp * D + col + j] = acc[c][j];
+  for (int v = 0; v < V; ++v) {
+    if (col[v] < D) {
+      float4* o = reinterpret_cast<float4*>(dw_part + (long long)blockIdx.x * D + col[v]);
+      o[0] = make_float4(acc[v][0], acc[v][1], acc[v][2], acc[v][3]);
+      o[1] = make_float4(acc[v][4], acc[v][5], acc[v][6], acc[v][7]);
     }
-  }
-  __syncthreads();
-  for (int col = threadIdx.x; col < D; col += blockDim.x) {
-    float s = 0.f;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) s += red[k * D + col];
-    dw_part[(long long)blockIdx.x * D + col] = s;
   }
 }
 
@@ -247,44 +255,99 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_small_kernel(const __nv_bfloa
   }
 }
 
-// dw[col] = sum_b part[b, col]
-__global__ void reduce_cols_kernel(const float* __restrict__ part, int nblocks, int D, __nv_bfloat16* __restrict__ out_bf16,
-                                   float* __restrict__ out_f32) {
-  const int col = blockIdx.x * blockDim.x + threadIdx.x;
-  if (col >= D) return;
-  float s = 0.f;
-  for (int b = 0; b < nblocks; ++b) s += part[(long long)b * D + col];
-  if (out_f32) out_f32[col] = s;
-  if (out_bf16) out_bf16[col] = __float2bfloat16_rn(s);
+// dw[col] = sum_b part[b, col]: 8 columns (one 32-byte sector per partial row) per block of 1024
+// threads, the partial rows split over 128 thread rows with 2 accumulators each, then a tree sum
+// through smem. D / 8 blocks spread the reads over the SMs.
+__global__ void __launch_bounds__(1024) reduce_cols_kernel(const float* __restrict__ part, int nblocks, int D,
+                                                           __nv_bfloat16* __restrict__ out_bf16,
+                                                           float* __restrict__ out_f32) {
+  __shared__ float s[128][9];
+  const int tx = threadIdx.x & 7, ty = threadIdx.x >> 3;
+  const int col = blockIdx.x * 8 + tx;
+  float a0 = 0.f, a1 = 0.f;
+  if (col < D) {
+    int b = ty;
+    for (; b + 128 < nblocks; b += 256) {
+      a0 += part[(long long)b * D + col];
+      a1 += part[(long long)(b + 128) * D + col];
+    }
+    if (b < nblocks) a0 += part[(long long)b * D + col];
+  }
+  s[ty][tx] = a0 + a1;
+  __syncthreads();
+#pragma unroll
+  for (int h = 64; h > 0; h >>= 1) {
+    if (ty < h) s[ty][tx] += s[ty + h][tx];
+    __syncthreads();
+  }
+  if (ty == 0 && col < D) {
+    const float t = s[0][tx];
+    if (out_f32) out_f32[col] = t;
+    if (out_bf16) out_bf16[col] = __float2bfloat16_rn(t);
+  }
 }
 
 }  // namespace astrai
 
 namespace astrai_host {
 
+// Rows per block for the block-per-row kernels: about kNormBlocksTarget blocks (at most `cap`),
+// each a contiguous range of rows.
+static int norm_rows_per_block(int rows, long long cap) {
+  long long nb = std::min<long long>(std::min<long long>(rows, astrai::kNormBlocksTarget), std::max(1LL, cap));
+  return (int)((rows + nb - 1) / nb);
+}
+static bool norm_small(int D) { return D <= 256 && D % 32 == 0; }
+constexpr int kSmallRowsPerBlock = 64;
+
 void rmsnorm_fwd(const void* x, long long ldx, const void* w, void* y, long long ldy, float* rstd, int rows, int D,
                  float eps, cudaStream_t s) {
   using namespace astrai;
-  const int grid = (rows + 7) / 8;
+  if (rows <= 0) return;
   auto X = static_cast<const __nv_bfloat16*>(x);
   auto W = static_cast<const __nv_bfloat16*>(w);
   auto Y = static_cast<__nv_bfloat16*>(y);
-  if (D <= 256 && D % 32 == 0) {
-    (astrai::note_launch(), rmsnorm_fwd_small_kernel<<<grid, 256, 0, s>>>(X, ldx, W, Y, ldy, rstd, rows, D, eps));
-  } else if (D <= 1024) {
-    (astrai::note_launch(), rmsnorm_fwd_kernel<4><<<grid, 256, 0, s>>>(X, ldx, W, Y, ldy, rstd, rows, D, eps));
-  } else if (D <= 2048) {
-    (astrai::note_launch(), rmsnorm_fwd_kernel<8><<<grid, 256, 0, s>>>(X, ldx, W, Y, ldy, rstd, rows, D, eps));
-  } else if (D <= 4096) {
-    (astrai::note_launch(), rmsnorm_fwd_kernel<16><<<grid, 256, 0, s>>>(X, ldx, W, Y, ldy, rstd, rows, D, eps));
-  } else {
-    (astrai::note_launch(), rmsnorm_fwd_kernel<32><<<grid, 256, 0, s>>>(X, ldx, W, Y, ldy, rstd, rows, D, eps));
+  if (norm_small(D)) {
+    (astrai::note_launch(), rmsnorm_fwd_small_kernel<<<(rows + 7) / 8, 256, 0, s>>>(X, ldx, W, Y, ldy, rstd, rows, D, eps));
+    return;
   }
+  const int rpb = norm_rows_per_block(rows, 1LL << 30);
+  const int nb = (rows + rpb - 1) / rpb;
+  const int T = std::min(kNormThreads, ((D / 8 + 31) / 32) * 32);
+  if (D <= 8 * kNormThreads)
+    (astrai::note_launch(), rmsnorm_fwd_kernel<1><<<nb, T, 0, s>>>(X, ldx, W, Y, ldy, rstd, rows, D, eps, rpb));
+  else if (D <= 16 * kNormThreads)
+    (astrai::note_launch(), rmsnorm_fwd_kernel<2><<<nb, kNormThreads, 0, s>>>(X, ldx, W, Y, ldy, rstd, rows, D, eps, rpb));
+  else
+    (astrai::note_launch(), rmsnorm_fwd_kernel<4><<<nb, kNormThreads, 0, s>>>(X, ldx, W, Y, ldy, rstd, rows, D, eps, rpb));
+}
+
+// Launch the backward kernels for nb blocks of rpb rows; dw partials go to scratch [nb][D].
+static void rmsnorm_bwd_launch(const void* dy, long long lddy, const void* x, long long ldx, const void* w,
+                               const float* rstd, void* dx, long long lddx, const void* dres, long long ldres,
+                               void* dw_bf16, float* dw_f32, float* scratch, int rows, int D, int nb, int rpb,
+                               cudaStream_t s) {
+  using namespace astrai;
+  auto DY = static_cast<const __nv_bfloat16*>(dy);
+  auto X = static_cast<const __nv_bfloat16*>(x);
+  auto W = static_cast<const __nv_bfloat16*>(w);
+  auto DX = static_cast<__nv_bfloat16*>(dx);
+  auto DR = static_cast<const __nv_bfloat16*>(dres);
+  if (norm_small(D)) {
+    (astrai::note_launch(), rmsnorm_bwd_small_kernel<<<nb, 256, 0, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, DR, ldres, scratch, rows, D, rpb));
+  } else {
+    const int T = std::min(kNormThreads, ((D / 8 + 31) / 32) * 32);
+    if (D <= 8 * kNormThreads)
+      (astrai::note_launch(), rmsnorm_bwd_kernel<1><<<nb, T, 0, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, DR, ldres, scratch, rows, D, rpb));
+    else
+      (astrai::note_launch(), rmsnorm_bwd_kernel<2><<<nb, kNormThreads, 0, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, DR, ldres, scratch, rows, D, rpb));
+  }
+  (astrai::note_launch(), reduce_cols_kernel<<<(D + 7) / 8, 1024, 0, s>>>(scratch, nb, D, static_cast<__nv_bfloat16*>(dw_bf16), dw_f32));
 }
 
 // Number of fp32 scratch elements rmsnorm_bwd needs for dw partials.
 long long rmsnorm_bwd_scratch(int rows, int D, int* nblocks_out) {
-  const int rpb = 64;
+  const int rpb = norm_small(D) ? kSmallRowsPerBlock : norm_rows_per_block(rows, 1LL << 30);
   const int nb = (rows + rpb - 1) / rpb;
   if (nblocks_out) *nblocks_out = nb;
   return (long long)nb * D;
@@ -293,35 +356,11 @@ long long rmsnorm_bwd_scratch(int rows, int D, int* nblocks_out) {
 void rmsnorm_bwd(const void* dy, long long lddy, const void* x, long long ldx, const void* w, const float* rstd,
                  void* dx, long long lddx, void* dw_bf16, float* dw_f32, float* scratch, int rows, int D,
                  cudaStream_t s, const void* dres, long long ldres) {
-  using namespace astrai;
+  if (rows <= 0) return;
   int nb = 0;
   rmsnorm_bwd_scratch(rows, D, &nb);
-  const int rpb = 64;
-  auto DY = static_cast<const __nv_bfloat16*>(dy);
-  auto X = static_cast<const __nv_bfloat16*>(x);
-  auto W = static_cast<const __nv_bfloat16*>(w);
-  auto DX = static_cast<__nv_bfloat16*>(dx);
-  auto DR = static_cast<const __nv_bfloat16*>(dres);
-  const size_t sm = (size_t)8 * D * sizeof(float);
-  static bool attr_done[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_done[dev & 63]) {
-    cudaFuncSetAttribute(rmsnorm_bwd_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 1024 * 4);
-    cudaFuncSetAttribute(rmsnorm_bwd_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 2048 * 4);
-    cudaFuncSetAttribute(rmsnorm_bwd_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 4096 * 4);
-    attr_done[dev & 63] = true;
-  }
-  if (D <= 256 && D % 32 == 0) {
-    (astrai::note_launch(), rmsnorm_bwd_small_kernel<<<nb, 256, 0, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, DR, ldres, scratch, rows, D, rpb));
-  } else if (D <= 1024) {
-    (astrai::note_launch(), rmsnorm_bwd_kernel<4><<<nb, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, DR, ldres, scratch, rows, D, rpb));
-  } else if (D <= 2048) {
-    (astrai::note_launch(), rmsnorm_bwd_kernel<8><<<nb, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, DR, ldres, scratch, rows, D, rpb));
-  } else {
-    (astrai::note_launch(), rmsnorm_bwd_kernel<16><<<nb, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, DR, ldres, scratch, rows, D, rpb));
-  }
-  (astrai::note_launch(), reduce_cols_kernel<<<(D + 255) / 256, 256, 0, s>>>(scratch, nb, D, static_cast<__nv_bfloat16*>(dw_bf16), dw_f32));
+  const int rpb = (rows + nb - 1) / nb;
+  rmsnorm_bwd_launch(dy, lddy, x, ldx, w, rstd, dx, lddx, dres, ldres, dw_bf16, dw_f32, scratch, rows, D, nb, rpb, s);
 }
 
 }  // namespace astrai_host
@@ -344,17 +383,10 @@ float* g_scratch_ptr[kMaxDevices] = {};
 cudaError_t g_setup_err[kMaxDevices] = {};
 std::once_flag g_setup_once[kMaxDevices];
 
-// Once per device, with that device current: the array's address and the
-// kernels' dynamic shared-memory limits. Allocates nothing.
+// Once per device, with that device current: the array's address. Allocates nothing.
 void static_scratch_setup(int dev) {
   float* p = nullptr;
-  cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_rmsnorm_bwd_scratch);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(astrai::rmsnorm_bwd_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 1024 * 4);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(astrai::rmsnorm_bwd_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 2048 * 4);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(astrai::rmsnorm_bwd_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 4096 * 4);
+  const cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_rmsnorm_bwd_scratch);
   g_setup_err[dev] = e;
   g_scratch_ptr[dev] = e == cudaSuccess ? p : nullptr;
 }
@@ -364,21 +396,25 @@ void static_scratch_setup(int dev) {
 extern "C" int astrai_rmsnorm_bwd_static_scratch(const void* dy, long long lddy, const void* x, long long ldx,
                                                  const void* w, const float* rstd, void* dx, long long lddx,
                                                  void* dw_bf16, float* dw_f32, int rows, int D, void* stream) {
-  using namespace astrai;
   if (rows <= 0 || D <= 0 || D % 8 != 0 || D > 4096) {
     std::fprintf(stderr, "astrai_rmsnorm_bwd_static_scratch: unsupported shape rows=%d D=%d "
                          "(need rows > 0, D a multiple of 8, D <= 4096)\n", rows, D);
     return -1;
   }
-  const int rpb = 64;
-  const long long nb = (static_cast<long long>(rows) + rpb - 1) / rpb;
-  const long long need = nb * D;
+  // Size rule (documented in astrai_c_api.h, independent of the launch's block count): the problem
+  // is accepted when ceil(rows / 64) * D floats fit the static array.
+  const long long need = (static_cast<long long>(rows) + 63) / 64 * D;
   if (need > ASTRAI_RMSNORM_BWD_SCRATCH_FLOATS) {
     std::fprintf(stderr, "astrai_rmsnorm_bwd_static_scratch: rows=%d D=%d needs %lld floats of scratch, "
                          "more than the %lld in the static array\n", rows, D, need,
                  static_cast<long long>(ASTRAI_RMSNORM_BWD_SCRATCH_FLOATS));
     return -1;
   }
+  // the launch itself uses at most ASTRAI_RMSNORM_BWD_SCRATCH_FLOATS / D blocks
+  const long long cap = ASTRAI_RMSNORM_BWD_SCRATCH_FLOATS / D;
+  const int rpb = astrai_host::norm_small(D) ? astrai_host::kSmallRowsPerBlock
+                                             : astrai_host::norm_rows_per_block(rows, cap);
+  const long long nb = (static_cast<long long>(rows) + rpb - 1) / rpb;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return static_cast<int>(e);
@@ -389,26 +425,8 @@ extern "C" int astrai_rmsnorm_bwd_static_scratch(const void* dy, long long lddy,
   }
   std::call_once(g_setup_once[dev], static_scratch_setup, dev);
   if (g_setup_err[dev] != cudaSuccess) return static_cast<int>(g_setup_err[dev]);
-  float* scratch = g_scratch_ptr[dev];
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  auto DY = static_cast<const __nv_bfloat16*>(dy);
-  auto X = static_cast<const __nv_bfloat16*>(x);
-  auto W = static_cast<const __nv_bfloat16*>(w);
-  auto DX = static_cast<__nv_bfloat16*>(dx);
-  const int blocks = static_cast<int>(nb);
-  const size_t sm = static_cast<size_t>(8) * D * sizeof(float);
-  if (D <= 256 && D % 32 == 0) {
-    (astrai::note_launch(), rmsnorm_bwd_small_kernel<<<blocks, 256, 0, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, nullptr, 0, scratch, rows, D, rpb));
-  } else if (D <= 1024) {
-    (astrai::note_launch(), rmsnorm_bwd_kernel<4><<<blocks, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, nullptr, 0, scratch, rows, D, rpb));
-  } else if (D <= 2048) {
-    (astrai::note_launch(), rmsnorm_bwd_kernel<8><<<blocks, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, nullptr, 0, scratch, rows, D, rpb));
-  } else {
-    (astrai::note_launch(), rmsnorm_bwd_kernel<16><<<blocks, 256, sm, s>>>(DY, lddy, X, ldx, W, rstd, DX, lddx, nullptr, 0, scratch, rows, D, rpb));
-  }
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return static_cast<int>(e);
-  (astrai::note_launch(), reduce_cols_kernel<<<(D + 255) / 256, 256, 0, s>>>(scratch, blocks, D, static_cast<__nv_bfloat16*>(dw_bf16),
-                                                     dw_f32));
+  astrai_host::rmsnorm_bwd_launch(dy, lddy, x, ldx, w, rstd, dx, lddx, nullptr, 0, dw_bf16, dw_f32,
+                                  g_scratch_ptr[dev], rows, D, static_cast<int>(nb), rpb,
+                                  static_cast<cudaStream_t>(stream));
   return static_cast<int>(cudaGetLastError());
 }

@@ -68,15 +68,17 @@ class _RMSNormForkFn(torch.autograd.Function):
         return dx.view(ctx.shape), dw, None
 
 
-def _fast(x: torch.Tensor, weight: torch.Tensor) -> bool:
+def _fast(x: torch.Tensor, weight: torch.Tensor, backward: bool = True) -> bool:
     D = x.shape[-1]
-    # the warp-per-row kernels hold a row in registers
+    # each thread of a row's block owns fixed 8-column groups: up to 2 per thread in the backward
+    # kernel (D <= 4096), 4 in the forward one (D <= 8192)
     return x.is_cuda and x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and D % 8 == 0 \
-        and (D > 256 or D % 32 == 0) and D <= 4096
+        and (D > 256 or D % 32 == 0) and D <= (4096 if backward else 8192)
 
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
-    if _fast(x, weight):
+    backward = torch.is_grad_enabled() and (x.requires_grad or weight.requires_grad)
+    if _fast(x, weight, backward):
         return _RMSNormFn.apply(x, weight, eps)
     return F.rms_norm(x, (x.shape[-1],), weight, eps)
 

@@ -116,12 +116,44 @@ def test_linear_autograd():
     assert rel_err(r.grad, rf.grad) < 1e-3
 
 
-@pytest.mark.parametrize("D", [128, 1024, 2048, 4096])
-def test_rmsnorm(D):
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 1)])
+@pytest.mark.parametrize("M,N,K", [(8192, 2048, 2048), (2048, 2048, 8192), (1000, 3000, 4000), (8192, 5632, 2048)])
+def test_gemm_streamk(a_mn, b_mn, M, N, K):
+    """Shapes whose last wave of tiles is split over all SMs by k-blocks (the plan says so), against
+    an fp32 matmul; run twice so the fix-up flags are shown to reset between launches."""
+    from astrai_b200.ops._ext import native
+    from astrai_b200.ops.gemm import gemm
+
+    bm, bn, streamk, tiles, sms = native().gemm_plan(M, N, K, 1)
+    if not streamk:
+        pytest.skip(f"plan for {M}x{N}x{K} has no stream-K part ({tiles} tiles of {bm}x{bn} on {sms} SMs)")
+    torch.manual_seed(1)
+    a = torch.randn((K, M) if a_mn else (M, K), device="cuda", dtype=torch.bfloat16)
+    b = torch.randn((K, N) if b_mn else (N, K), device="cuda", dtype=torch.bfloat16)
+    A = a.float().t() if a_mn else a.float()
+    B = b.float() if b_mn else b.float().t()
+    ref = A @ B
+    for _ in range(2):
+        d = gemm(a, b, a_mn=bool(a_mn), b_mn=bool(b_mn))
+        assert rel_err(d, ref) < 1e-2
+
+
+@pytest.mark.parametrize("rows,D", [(333, 128), (333, 1024), (333, 2048), (333, 4096), (5000, 2048), (4099, 1000),
+                                    (3001, 3072), (64, 8192)])
+def test_rmsnorm(rows, D):
+    """Few rows (one per block) and many (each block walks a range of rows with the next row's loads
+    in flight); widths that do not fill the 256 threads of a row."""
     from astrai_b200.ops.norm import rms_norm
 
+    if D > 4096:  # forward only: the backward kernel takes D <= 4096
+        x = torch.randn(rows, D, device="cuda", dtype=torch.bfloat16)
+        w = (1 + 0.1 * torch.randn(D, device="cuda")).to(torch.bfloat16)
+        with torch.no_grad():
+            y = rms_norm(x, w, 1e-5)
+        assert rel_err(y, F.rms_norm(x.float(), (D,), w.float(), 1e-5)) < 1e-2
+        return
     torch.manual_seed(4)
-    x = torch.randn(333, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    x = torch.randn(rows, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
     w = (1 + 0.1 * torch.randn(D, device="cuda")).to(torch.bfloat16).requires_grad_()
     y = rms_norm(x, w, 1e-5)
     g = torch.randn_like(y)
@@ -134,14 +166,14 @@ def test_rmsnorm(D):
     assert rel_err(w.grad, wf.grad) < 1e-2
 
 
-@pytest.mark.parametrize("D", [128, 2048])
-def test_rmsnorm_fork_adds_residual_gradient(D):
+@pytest.mark.parametrize("rows,D", [(257, 128), (257, 2048), (6000, 2048)])
+def test_rmsnorm_fork_adds_residual_gradient(rows, D):
     """(rms_norm(x), x) used by a norm branch and a residual branch: the kernel's dx equals the fp32
     sum of both branches' gradients."""
     from astrai_b200.ops.norm import rms_norm_fork
 
     torch.manual_seed(5)
-    x = torch.randn(257, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    x = torch.randn(rows, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
     w = (1 + 0.1 * torch.randn(D, device="cuda")).to(torch.bfloat16).requires_grad_()
     y, xr = rms_norm_fork(x, w, 1e-5)
     g1, g2 = torch.randn_like(y), torch.randn_like(y)
