@@ -4,8 +4,9 @@ Field names, defaults and the required-field validation follow the reference
 ``TrainConfig`` (astrai/config/train_config.py:17-181), because the CLI, the
 checkpoint ``meta.json`` (which embeds ``to_dict()``) and user scripts depend
 on them. Fields added here: ``comm_backend`` (``"nccl"`` or ``"fused"``: who
-moves gradients between GPUs), ``compile_graphs`` (capture the optimizer step
-in a CUDA graph) and ``profile_dir`` (torch.profiler trace output).
+moves gradients between GPUs), ``cuda_graph`` (replay each micro-step's forward
+and backward from a CUDA graph, for fixed-shape batches on the seq / sft
+strategies) and ``profile_dir`` (torch.profiler trace output).
 """
 
 from __future__ import annotations
@@ -66,6 +67,7 @@ class TrainConfig(BaseConfig):
     extra_kwargs: Dict[str, Any] = field(default_factory=dict)
     # additions
     comm_backend: str = "nccl"
+    cuda_graph: bool = False
     profile_dir: Optional[str] = None
 
     def __post_init__(self):

@@ -12,6 +12,7 @@
 
 namespace astrai_host {
 long long launch_count();
+void add_launches(long long n);
 void skinny_gemm(const void* X, long long ldx, const void* W, long long ldw, const void* residual, long long ldr,
                  void* Y, long long ldy, int M, int N, int K, int sms, cudaStream_t s);
 int num_sms(int device);
@@ -433,6 +434,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "astrai_b200 sm_100a kernels";
   m.def("launch_count", []() { return static_cast<int64_t>(astrai_host::launch_count()); },
         "kernel launches issued by this library so far (host counter)");
+  m.def("add_launches", [](int64_t n) { astrai_host::add_launches(n); },
+        "count kernels that ran from a CUDA-graph replay (captured launches x replays)");
   m.def("skinny_gemm", &skinny_gemm, py::arg("x"), py::arg("w"), py::arg("y"), py::arg("residual") = py::none());
   m.def("gemm", &gemm, "bf16 tcgen05 GEMM", py::arg("a"), py::arg("b"), py::arg("d"), py::arg("c") = py::none(),
         py::arg("a_mn") = 0, py::arg("b_mn") = 0, py::arg("alpha") = 1.0, py::arg("beta") = 0.0,

@@ -2,7 +2,7 @@
 //
 // Everything here is hand-written inline PTX for Blackwell (sm_100a):
 //   * mbarrier init / arrive / expect_tx / bounded parity wait
-//   * TMA tiled loads (cp.async.bulk.tensor, NO multicast anywhere)
+//   * TMA tiled loads (cp.async.bulk.tensor), each into the issuing CTA only
 //   * tcgen05: TMEM alloc/dealloc, UMMA issue (kind::f16), commit, tcgen05.ld
 //   * UMMA shared-memory / instruction descriptors
 //

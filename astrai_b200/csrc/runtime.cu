@@ -138,4 +138,6 @@ void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 namespace astrai_host {
 long long launch_count() { return astrai::g_launches.load(std::memory_order_relaxed); }
+// Launches that ran without passing a host launch site: CUDA-graph replays of captured kernels.
+void add_launches(long long n) { astrai::g_launches.fetch_add(n, std::memory_order_relaxed); }
 }  // namespace astrai_host

@@ -62,6 +62,8 @@ class MLP(nn.Module):
 
 @FFNFactory.register("moe")
 class DeepSeekMoE(nn.Module):
+    # routing reads per-expert token counts on the host: no CUDA-graph capture of the micro-step
+    cuda_graph_safe = False
     def __init__(self, dim: int, dim_ffn: int, n_routed_experts: int, n_shared_experts: int = 1,
                  n_activated_experts: int = 2, topk_method: str = "greedy", n_layers: int = 1,
                  moe_intermediate_size: Optional[int] = None, moe_aux_loss_coef: Optional[float] = None,

@@ -204,12 +204,14 @@ class ExecutorFactory(Registry[BaseExecutor]):
 
 @ExecutorFactory.register("none")
 class NoneExecutor(BaseExecutor):
-    pass
+    cuda_graph_safe = True  # nothing happens between backward and the optimizer step
 
 
 @ExecutorFactory.register("ddp")
 class DDPExecutor(BaseExecutor):
     """Replicated parameters, one gradient all-reduce (mean) per optimizer step."""
+
+    cuda_graph_safe = True  # the all-reduce runs after the last micro-step, outside any graph
 
     def __init__(self, grad_accum_steps: int = 1, comm_backend: str = "nccl", bucket_cap_mb: int = 256,
                  broadcast_params: bool = True, expert_parallel: bool = False, **_ignored):

@@ -92,6 +92,9 @@ class BaseStrategy(ABC):
     """Offline strategies consume dataset batches; with a RolloutRunner injected
     (``set_rollout_runner``) they produce their own batches from rollouts."""
 
+    # the loss of a fixed-shape batch is computed with device work only (see trainer/graph_step.py)
+    cuda_graph_safe = False
+
     def __init__(self, model, device, **kwargs):
         self.model = model
         self.device = device
@@ -137,6 +140,8 @@ class StrategyFactory(Registry["BaseStrategy"]):
 
 @StrategyFactory.register("seq")
 class SEQStrategy(BaseStrategy):
+    cuda_graph_safe = True
+
     def __init__(self, model, device, label_smoothing: float = 0.0, **kwargs):
         super().__init__(model, device, **kwargs)
         self.label_smoothing = label_smoothing
@@ -150,6 +155,8 @@ class SEQStrategy(BaseStrategy):
 
 @StrategyFactory.register("sft")
 class SFTStrategy(BaseStrategy):
+    cuda_graph_safe = True
+
     def __init__(self, model, device, label_smoothing: float = 0.0, **kwargs):
         super().__init__(model, device, **kwargs)
         self.label_smoothing = label_smoothing

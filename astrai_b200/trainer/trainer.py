@@ -16,9 +16,12 @@ from __future__ import annotations
 import logging
 from typing import List, Optional
 
+import torch
+
 from astrai_b200.config.train_config import TrainConfig
 from astrai_b200.parallel.setup import spawn_parallel_fn
 from astrai_b200.trainer.train_callback import CallbackFactory, TrainCallback, nvtx_range
+from astrai_b200.trainer.graph_step import GraphedMicroStep
 from astrai_b200.trainer.train_context import TrainContext, TrainContextBuilder
 
 logger = logging.getLogger(__name__)
@@ -60,10 +63,30 @@ class Trainer:
             if fn is not None:
                 fn(ctx)
 
+    def _graph_runner(self, ctx: TrainContext):
+        """The CUDA-graph micro-step when ``cuda_graph`` is set and this run can use it."""
+        c, ex, st = ctx.config, ctx.executor, ctx.strategy
+        if not getattr(c, "cuda_graph", False):
+            return None
+        why = None
+        if not getattr(st, "cuda_graph_safe", False) or getattr(st, "_rollout_runner", None) is not None:
+            why = f"strategy {type(st).__name__} is not graph-safe"
+        elif not getattr(ex, "cuda_graph_safe", False):
+            why = f"executor {type(ex).__name__} is not graph-safe"
+        elif torch.device(ctx.strategy.device).type != "cuda":
+            why = "not on a CUDA device"
+        if why is not None:
+            logger.warning("cuda_graph requested but %s: running eagerly", why)
+            return None
+        return GraphedMicroStep(st, ex.unwrap(ctx.model), torch.device(st.device), scale=1.0 / ex.grad_accum_steps,
+                                eager_calls=ex.grad_accum_steps)
+
     def _trainer_loop(self, param_path: Optional[str] = None, resume: bool = False) -> None:
         ctx = TrainContextBuilder(self.train_config).with_param_path(param_path, resume=resume).build()
         self.last_context = ctx
         ex = ctx.executor
+        graph = self._graph_runner(ctx)
+        ctx.kwargs["graph_step"] = graph
         per_micro = ctx.config.batch_per_device * ctx.world_size
         self._call("on_train_begin", ctx)
         try:
@@ -74,11 +97,17 @@ class Trainer:
                 for batch in ctx.dataloader:
                     with ex.accumulate(ctx.model):
                         self._call("on_batch_begin", ctx)
-                        with nvtx_range("forward"):
-                            loss = ctx.strategy(batch)
-                        ctx.loss = loss.detach()
-                        with nvtx_range("backward"):
-                            ex.backward(loss / ex.grad_accum_steps)
+                        if graph is not None:
+                            with nvtx_range("forward_backward"):
+                                ctx.loss = graph(batch)
+                            if ex.sync_gradients and ex.use_distributed:
+                                ex._reduce_gradients()
+                        else:
+                            with nvtx_range("forward"):
+                                loss = ctx.strategy(batch)
+                            ctx.loss = loss.detach()
+                            with nvtx_range("backward"):
+                                ex.backward(loss / ex.grad_accum_steps)
                         ctx.consumed_samples += per_micro
                         ctx.kwargs["tokens"] = ctx.kwargs.get("tokens", 0) + _batch_tokens(batch) * ctx.world_size
                         self._call("on_batch_end", ctx)
@@ -87,7 +116,8 @@ class Trainer:
                             with nvtx_range("optimizer"):
                                 ctx.optimizer.step()
                             ctx.strategy.on_optimizer_step()
-                            ctx.optimizer.zero_grad()
+                            # the graph accumulates into gradients that stay allocated
+                            ctx.optimizer.zero_grad(set_to_none=graph is None)
                             if ctx.scheduler:
                                 ctx.scheduler.step()
                 self._call("on_epoch_end", ctx)

@@ -52,7 +52,9 @@ REF_MOE_CFG = dict(CFG, num_hidden_layers=16, max_position_embeddings=4096, ffn_
                    n_shared_experts=2, n_activated_experts=6, intermediate_size=1408)
 MODEL = "dense"
 # owner-sharded Muon for N > 1 (each rank orthogonalises 1/N of the matrices, NVLink broadcast)
-SHARD_MUON = os.environ.get("ASTRAI_SHARD_MUON", "0") == "1"
+SHARD_MUON = os.environ.get("ASTRAI_SHARD_MUON", "1") == "1"
+# each micro-step's forward + backward replayed from a CUDA graph (dense model; MoE routing syncs)
+CUDA_GRAPH = os.environ.get("ASTRAI_CUDA_GRAPH", "1") == "1"
 
 
 def use_moe():
@@ -201,24 +203,40 @@ def run_ours(args, rank, world, local):
     n_batches = 4
     data = torch.randint(0, V, (n_batches, ACCUM, BATCH, SEQ + 1), device=dev)
 
+    def loss_fn(b):
+        seq = b["seq"]
+        out = model(seq[:, :-1])
+        loss = cross_entropy(out["logits"], seq[:, 1:])
+        if "aux_loss" in out:
+            loss = loss + out["aux_loss"]
+        return loss
+
+    graph = None
+    if CUDA_GRAPH and MODEL != "moe":
+        from astrai_b200.trainer.graph_step import GraphedMicroStep
+
+        graph = GraphedMicroStep(loss_fn, executor.unwrap(model), dev, scale=1.0 / ACCUM, eager_calls=ACCUM)
+
     def step(i):
         for mi in range(ACCUM):
             seq = data[i % n_batches, mi]
             with executor.micro_step(model, mi == ACCUM - 1):
-                out = model(seq[:, :-1])
-                loss = cross_entropy(out["logits"], seq[:, 1:])
-                if "aux_loss" in out:
-                    loss = loss + out["aux_loss"]
-                (loss / ACCUM).backward()
+                if graph is not None:
+                    loss = graph({"seq": seq})
+                else:
+                    loss = loss_fn({"seq": seq})
+                    (loss / ACCUM).backward()
         executor.finish_step(model)
         executor.clip_grad_norm(model, CLIP, as_tensor=True)
         opt.step()
-        opt.zero_grad(set_to_none=True)
+        opt.zero_grad(set_to_none=graph is None)
         return loss
 
     for i in range(args.warmup):
         step(i)
     assert native().read_error() == 0, "kernel bounded-wait error during warm-up"
+    if graph is not None and graph.disabled_reason is not None and rank == 0:
+        print(f"[bench] CUDA-graph micro-step off: {graph.disabled_reason}", file=sys.stderr)
     clocks = ClockSampler(rank == 0)
     barrier()
     clocks.start()
@@ -240,9 +258,13 @@ def run_ours(args, rank, world, local):
         "value": world * ACCUM * BATCH * SEQ / (ms / 1e3),
         "clocks": ck,
         "loss": loss_val,
-        "gpu_launches": n_launch,  # counted by the extension's launch counter on this rank
+        "gpu_launches": n_launch,  # counted by the extension's launch counter on this rank (graph replays included)
+        "cuda_graph": graph is not None and graph.disabled_reason is None and graph.replays > 0,
     }
     if not args.no_e2e:
+        graph = None  # the e2e run captures its own micro-step; free this one's memory pool first
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
         result["e2e"] = run_ours_e2e(args, rank, world, local, model, executor, opt)
     return result
 
@@ -307,6 +329,7 @@ def run_ours_e2e(args, rank, world, local, model, executor, opt):
         parallel_mode="ddp" if world > 1 else "none", device_type="cuda", pin_memory=True,
         executor_kwargs={"comm_backend": "fused"},
         extra_kwargs={"label_smoothing": 0.0}, metrics=["loss", "lr", "grad_norm"],
+        cuda_graph=CUDA_GRAPH and MODEL != "moe",
     )
     Trainer(tc, callbacks=[Timer()]).train()
     if "ms" not in timing:
@@ -772,7 +795,8 @@ def main():
                            "optimizer": "Muon(0.02, ns5)+AdamW(1e-4, wd0.1), clip 1.0"
                            + (", Muon owner-sharded over ranks"
                               if SHARD_MUON and world > 1 and args.impl == "astrai_b200" else ""),
-                           "l2": "no flush: per-step working set (2.4 GB weights + activations) >> 126 MB L2"},
+                           "l2": "no flush: per-step working set (2.4 GB weights + activations) >> 126 MB L2",
+                           "cuda_graph": bool(res.get("cuda_graph")) if args.impl == "astrai_b200" else False},
                 "clocks": res.get("clocks"),
                 "e2e": res.get("e2e"),
                 "gpu_launches": res.get("gpu_launches") if args.impl == "astrai_b200" else None,

@@ -251,3 +251,24 @@ def test_profiler_callback_writes_trace(tmp_path):
     cb.on_train_end(None)
     names = os.listdir(tmp_path)
     assert "kernels.txt" in names and any(n.startswith("trace_step") for n in names)
+
+
+def test_cuda_graph_flag_falls_back_to_eager_on_cpu(tmpdir_path):
+    """``cuda_graph=True`` off a CUDA device: the loop runs eagerly with the same results."""
+    from astrai_b200.trainer import Trainer
+    from astrai_b200.trainer.graph_step import GraphedMicroStep
+
+    runs = []
+    for flag in (False, True):
+        torch.manual_seed(11)  # model init
+        t = Trainer(make_cfg(RandSeq(8), os.path.join(tmpdir_path, str(flag)), cuda_graph=flag))
+        t.train()
+        runs.append(t.last_context)
+    assert runs[1].kwargs["graph_step"] is None
+    for pa, pb in zip(runs[0].model.parameters(), runs[1].model.parameters()):
+        assert torch.equal(pa, pb)
+    m = torch.nn.Linear(4, 4)
+    step = GraphedMicroStep(lambda b: m(b["x"]).sum(), m, torch.device("cpu"))
+    assert step.disabled_reason == "not a CUDA device"
+    step({"x": torch.ones(2, 4)})
+    assert m.weight.grad is not None and step.replays == 0
