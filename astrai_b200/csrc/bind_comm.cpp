@@ -80,7 +80,7 @@ void muon_apply_peers(const c10::optional<at::Tensor>& pptr, const c10::optional
   i64_check(peer_base, "peer_base");
   TORCH_CHECK(peer_base.numel() == world && rank >= 0 && rank < world, "peer_base / rank mismatch");
   TORCH_CHECK(done.is_cuda() && done.scalar_type() == at::kInt && done.numel() >= 1, "done must be CUDA int32");
-  TORCH_CHECK(flag_off % 4 == 0 && slot >= 0, "bad flag offset / slot");
+  TORCH_CHECK(flag_off % 4 == 0 && slot >= -1, "bad flag offset / slot (-1: raise no flag)");
   const void* xp = nullptr;
   const long long* pp = nullptr;
   const long long* po = nullptr;

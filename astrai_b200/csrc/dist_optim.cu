@@ -35,7 +35,7 @@ struct PeerApplyParams {
   float decay, adj_lr;
   int rank, world;
   long long flag_off;  // byte offset of the flag block [rows][world] (u32) in the symmetric buffer
-  int slot;            // flag row raised by this launch
+  int slot;            // flag row raised by this launch (< 0: none, a later launch of the group raises it)
   unsigned epoch;
   unsigned* done;      // local grid-completion counter, zero between launches
 };
@@ -110,7 +110,7 @@ __global__ void __launch_bounds__(PA_THREADS) muon_apply_peers_kernel(PeerApplyP
     const unsigned total = gridDim.x * gridDim.y * gridDim.z;
     if (atomicAdd(p.done, 1u) == total - 1) {
       __threadfence_system();
-      for (int q = 0; q < p.world; ++q) {
+      for (int q = 0; q < p.world && p.slot >= 0; ++q) {
         if (q == p.rank) continue;
         unsigned* f = reinterpret_cast<unsigned*>(p.peer_base[q] + p.flag_off) + p.slot * p.world + p.rank;
         st_release_sys_u32(f, p.epoch);

@@ -24,6 +24,8 @@ CPU parameters use the plain torch implementations (the CPU/gloo path).
 
 from __future__ import annotations
 
+import os
+
 import math
 from typing import Dict, Iterable, List, Optional, Tuple
 
@@ -337,9 +339,14 @@ class Muon(Optimizer):
             adj = _adjust_lr(lr, group["adjust_lr_fn"], shape)
             dev = ps[0].device
             if own:
-                w, out, tall = self._orthogonalize(("own", gi, shape), own, group)
-                C.muon_apply_peers(w["pptr"], w["poff"], a.buf.peer_base, out, len(own), R, Cc, tall,
-                                   1.0 - lr * group["weight_decay"], adj, r, W, a.flag_off, slot, self._epoch, a.done)
+                chunks = _ns_chunks(own)
+                for ci, chunk in enumerate(chunks):
+                    t, out, tall = self._orthogonalize(("own", gi, shape, ci), chunk, group)
+                    # only the group's last launch raises its flag on the peers (slot -1: no flag); the
+                    # earlier launches' stores precede it in stream order
+                    C.muon_apply_peers(t["pptr"], t["poff"], a.buf.peer_base, out, len(chunk), R, Cc, tall,
+                                       1.0 - lr * group["weight_decay"], adj, r, W, a.flag_off,
+                                       slot if ci == len(chunks) - 1 else -1, self._epoch, a.done)
             else:  # nothing owned in this group: only raise its flag on the peers
                 C.muon_apply_peers(None, None, a.buf.peer_base, None, 0, R, Cc, False, 1.0, 0.0, r, W, a.flag_off,
                                    slot, self._epoch, a.done)
@@ -356,45 +363,56 @@ class Muon(Optimizer):
         if self._reset_clip and self.use_clip_coef and dev is not None:
             clip_state(dev).coef.fill_(1.0)
 
-    def _orthogonalize(self, key, ps, group):
-        """Momentum + Frobenius normalisation + Newton-Schulz of the same-shape matrices ``ps``."""
-        C = native()
-        dev = ps[0].device
-        R, Cc = ps[0].shape
-        tall = R > Cc
-        m, n = (Cc, R) if tall else (R, Cc)
-        Bn = len(ps)
-        ident = tuple(p.data_ptr() for p in ps)
-        w = self._work.get(key)
-        if w is None or w["ident"] != ident:
-            w = {
-                "ident": ident,
+    def _scratch(self, shape, Bn, dev):
+        """Newton-Schulz scratch for ``Bn`` matrices of ``shape``, shared by every group and chunk of that
+        shape and size (momentum lives in the optimizer state; nothing here outlives one call)."""
+        key = ("scratch", shape, Bn)
+        s = self._work.get(key)
+        if s is None:
+            R, Cc = shape
+            m, n = (Cc, R) if R > Cc else (R, Cc)
+            s = {
                 "U": torch.empty(Bn, R, Cc, device=dev, dtype=torch.bfloat16),
                 "X": torch.empty(Bn, m, n, device=dev, dtype=torch.bfloat16),
                 "Y": torch.empty(Bn, m, n, device=dev, dtype=torch.bfloat16),
                 "A": torch.empty(Bn, m, m, device=dev, dtype=torch.bfloat16),
                 "Bm": torch.empty(Bn, m, m, device=dev, dtype=torch.bfloat16),
                 "sumsq": torch.zeros(Bn, device=dev, dtype=torch.float32),
-                "pptr": _i64([p.data_ptr() for p in ps], dev),
-                "bptr": _i64([self._buf(p).data_ptr() for p in ps], dev),
             }
+            self._work[key] = s
+        return s
+
+    def _orthogonalize(self, key, ps, group):
+        """Momentum + Frobenius normalisation + Newton-Schulz of the same-shape matrices ``ps`` (one
+        chunk, see ``_ns_chunks``); returns the chunk's pointer tables, the update and its layout."""
+        C = native()
+        dev = ps[0].device
+        R, Cc = ps[0].shape
+        tall = R > Cc
+        s = self._scratch((R, Cc), len(ps), dev)
+        ident = tuple(p.data_ptr() for p in ps)
+        t = self._work.get(key)
+        if t is None or t["ident"] != ident:
+            t = {"ident": ident, "pptr": _i64([p.data_ptr() for p in ps], dev),
+                 "bptr": _i64([self._buf(p).data_ptr() for p in ps], dev)}
             if self._arena is not None and all(self._arena.holds(p) for p in ps):
-                w["poff"] = _i64([self._arena.offset[id(p)] for p in ps], dev)
-            self._work[key] = w
+                t["poff"] = _i64([self._arena.offset[id(p)] for p in ps], dev)
+            self._work[key] = t
         gptr = _i64([p.grad.data_ptr() for p in ps], dev)
-        w["sumsq"].zero_()
+        s["sumsq"].zero_()
         coef = clip_state(dev).coef if self.use_clip_coef else None
-        C.muon_momentum(gptr, w["bptr"], True, w["U"], group["momentum"], group["nesterov"], coef, w["sumsq"])
-        C.muon_normalize(w["U"], w["X"], tall, w["sumsq"], group["eps"])
-        out = newton_schulz_batched(w["X"], group["ns_steps"], group["ns_coefficients"], (w["Y"], w["A"], w["Bm"]))
-        return w, out, tall
+        C.muon_momentum(gptr, t["bptr"], True, s["U"], group["momentum"], group["nesterov"], coef, s["sumsq"])
+        C.muon_normalize(s["U"], s["X"], tall, s["sumsq"], group["eps"])
+        out = newton_schulz_batched(s["X"], group["ns_steps"], group["ns_coefficients"], (s["Y"], s["A"], s["Bm"]))
+        return t, out, tall
 
     def _step_batched(self, gi, shape, ps, group):
-        w, out, tall = self._orthogonalize((gi, shape), ps, group)
         R, Cc = shape
         lr = float(group["lr"])
         adj = _adjust_lr(lr, group["adjust_lr_fn"], shape)
-        native().muon_apply(w["pptr"], False, out, R, Cc, tall, 1.0 - lr * group["weight_decay"], adj)
+        for ci, chunk in enumerate(_ns_chunks(ps)):
+            t, out, tall = self._orthogonalize((gi, shape, ci), chunk, group)
+            native().muon_apply(t["pptr"], False, out, R, Cc, tall, 1.0 - lr * group["weight_decay"], adj)
 
     def _step_reference(self, params, group):
         mu = group["momentum"]
@@ -409,6 +427,20 @@ class Muon(Optimizer):
             lr = float(group["lr"])
             p.mul_(1 - lr * group["weight_decay"])
             p.add_(upd.to(p.dtype), alpha=-_adjust_lr(lr, group["adjust_lr_fn"], p.shape))
+
+
+# bf16 bytes of the matrices one batched Newton-Schulz chain handles at a time: the scratch (update,
+# two iterates, two Gram matrices) is about 5x this, so a model with thousands of same-shape matrices
+# (MoE experts) keeps a bounded workspace instead of one sized for every matrix of the shape.
+_NS_CHUNK_BYTES = int(os.environ.get("ASTRAI_NS_CHUNK_BYTES", str(1 << 30)))
+
+
+def _ns_chunks(ps):
+    """``ps`` split into near-equal chunks of at most ``_NS_CHUNK_BYTES`` (at least one matrix each)."""
+    R, Cc = ps[0].shape
+    n = max(1, -(-len(ps) * R * Cc * 2 // max(1, _NS_CHUNK_BYTES)))
+    per = -(-len(ps) // n)
+    return [ps[i:i + per] for i in range(0, len(ps), per)]
 
 
 def is_muon_param(name: str, p: torch.Tensor) -> bool:

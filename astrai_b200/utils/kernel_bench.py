@@ -1,6 +1,6 @@
 """Device-timed micro-benchmarks of the framework's kernels.
 
-    python -m astrai_b200.utils.kernel_bench [gemm|attn|decode|sample|all]
+    python -m astrai_b200.utils.kernel_bench [gemm [case]|attn|norm|skinny|sample|all]
     torchrun --nproc-per-node N -m astrai_b200.utils.kernel_bench allreduce|ep
 
 Each case is timed with CUDA events on the launching stream after warm-up,
@@ -43,7 +43,8 @@ def time_fn(fn, warmup=5, iters=20):
     return s.elapsed_time(e) / iters
 
 
-def bench_gemm():
+def bench_gemm(only=None):
+    """The GEMMs of the 1.1B training step (``only``: one case by name, e.g. for a profiler capture)."""
     from astrai_b200.ops._ext import native
 
     hbm, tf, src = peaks()
@@ -61,6 +62,8 @@ def bench_gemm():
         ("square_8192", 8192, 8192, 8192, 0, 0),
     ]
     for name, M, N, K, amn, bmn in cases:
+        if only is not None and name != only:
+            continue
         a = torch.randn((K, M) if amn else (M, K), device="cuda", dtype=torch.bfloat16)
         b = torch.randn((K, N) if bmn else (N, K), device="cuda", dtype=torch.bfloat16)
         d = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
@@ -78,7 +81,9 @@ def bench_gemm():
         w = [int(v) for v in cnt.tolist()]
         sms = torch.cuda.get_device_properties(0).multi_processor_count
         cyc = ms * 1e-3 * 1.9e9  # cycles of one CTA at ~1.9 GHz
+        bm, bn, streamk, tiles, _ = C.gemm_plan(M, N, K, 1)
         print(json.dumps({"kernel": "gemm", "case": name, "M": M, "N": N, "K": K, "ms": round(ms, 4),
+                          "tile": f"{bm}x{bn}", "tiles": tiles, "streamk": streamk,
                           "tflops": round(fl / ms / 1e9, 1), "frac_of_peak": round(fl / ms / 1e9 / tf, 3),
                           "peak_src": src, "cublas_ms": round(ms_ref, 4),
                           "cublas_tflops": round(fl / ms_ref / 1e9, 1),
@@ -267,8 +272,34 @@ def bench_sample():
             print(json.dumps({"kernel": "sample", "rows": rows, "case": name, "us": round(ms * 1e3, 2)}))
 
 
+def bench_norm(rows: int = 8192, D: int = 2048):
+    """RMSNorm forward, backward and the fork backward (residual-branch gradient added) at the 1.1B
+    step's shape; bytes are the algorithmic reads + writes (bf16 rows, fp32 rstd)."""
+    from astrai_b200.ops._ext import native
+
+    hbm, _, src = peaks()
+    C = native()
+    x = torch.randn(rows, D, device="cuda", dtype=torch.bfloat16)
+    dy, dres = torch.randn_like(x), torch.randn_like(x)
+    w = (1 + 0.1 * torch.randn(D, device="cuda")).to(torch.bfloat16)
+    y, dx = torch.empty_like(x), torch.empty_like(x)
+    rstd = torch.empty(rows, device="cuda", dtype=torch.float32)
+    dw = torch.empty(D, device="cuda", dtype=torch.bfloat16)
+    scratch = torch.empty(C.rmsnorm_bwd_scratch(rows, D), device="cuda", dtype=torch.float32)
+    row = rows * D * 2
+    cases = [("rmsnorm_fwd", lambda: C.rmsnorm_fwd(x, w, y, rstd, 1e-5), 2 * row + rows * 4),
+             ("rmsnorm_bwd", lambda: C.rmsnorm_bwd(dy, x, w, rstd, dx, dw, scratch), 3 * row + rows * 4),
+             ("rmsnorm_bwd_fork", lambda: C.rmsnorm_bwd(dy, x, w, rstd, dx, dw, scratch, dres), 4 * row + rows * 4)]
+    for name, fn, nbytes in cases:
+        ms = time_fn(fn, warmup=5, iters=50)
+        gbs = nbytes / ms / 1e6
+        print(json.dumps({"kernel": name, "rows": rows, "D": D, "us": round(ms * 1e3, 2), "GB/s": round(gbs, 1),
+                          "frac_of_hbm": round(gbs / hbm, 3), "peak_src": src}))
+
+
 def main(argv=None):
-    which = (argv or sys.argv[1:] or ["all"])[0]
+    args = argv or sys.argv[1:] or ["all"]
+    which = args[0]
     torch.manual_seed(0)
     if which == "allreduce":
         bench_allreduce()
@@ -281,7 +312,9 @@ def main(argv=None):
     if which in ("sample", "all"):
         bench_sample()
     if which in ("gemm", "all"):
-        bench_gemm()
+        bench_gemm(args[1] if which == "gemm" and len(args) > 1 else None)
+    if which in ("norm", "all"):
+        bench_norm()
     if which in ("attn", "all"):
         try:
             from astrai_b200.ops.attention import bench_attention

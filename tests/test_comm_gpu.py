@@ -189,7 +189,12 @@ def test_fused_allreduce_bounded_wait_reports_missing_peer():
 
 
 @need2
-def test_sharded_muon_matches_replicated(tmp_path):
+@pytest.mark.parametrize("chunk_bytes", [None, "1"])
+def test_sharded_muon_matches_replicated(tmp_path, monkeypatch, chunk_bytes):
+    """chunk_bytes "1": one matrix per Newton-Schulz launch, so a shape group's flag is raised only
+    by its last launch (the ranks started here read the variable at import)."""
+    if chunk_bytes is not None:
+        monkeypatch.setenv("ASTRAI_NS_CHUNK_BYTES", chunk_bytes)
     _spawn(_sharded_muon_worker, 2, str(tmp_path / "owned.pt"))
     owned = torch.load(tmp_path / "owned.pt")["owned"]
     assert sum(owned) == 7 and all(n > 0 for n in owned)  # each matrix has exactly one owner

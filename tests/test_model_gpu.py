@@ -50,9 +50,14 @@ def test_lm_forward_backward_matches_cpu(tied):
         assert rel(p.grad, gc[n].grad) < 6e-2, n
 
 
-def test_fused_optimizers_match_torch():
+@pytest.mark.parametrize("chunk_bytes", [None, 1])
+def test_fused_optimizers_match_torch(chunk_bytes, monkeypatch):
+    """chunk_bytes=1: every batched Newton-Schulz chain holds one matrix (the chunked path)."""
+    import astrai_b200.optim.fused as fused
     from astrai_b200.optim import FusedAdamW, Muon, clip_grad_norm_, newton_schulz_reference
 
+    if chunk_bytes is not None:
+        monkeypatch.setattr(fused, "_NS_CHUNK_BYTES", chunk_bytes)
     torch.manual_seed(1)
     shapes = [(256, 512), (512, 256), (256, 512), (128, 128)]
     ps = [torch.randn(s, device="cuda").to(torch.bfloat16) for s in shapes]
