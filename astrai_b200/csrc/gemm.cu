@@ -825,11 +825,13 @@ static void dispatch_majors(int a_mn, int b_mn, int out_f32, const CUtensorMap& 
 }
 
 // Stream-K decision: whole waves of tiles plus the last partial wave split into k-block units over
-// all CTAs (see GemmParams). Used when every CTA gets at least 4 k-blocks of the split wave and the
-// time saved, (whole waves - fractional waves) x k-blocks per tile, is at least 16 k-blocks: on
-// B200 the fix-up (partial slots through L2, the owner's fold) costs about as much as 10 k-blocks,
-// so shapes with short K (2048 - 3072) and a nearly full last wave measured slower split.
-// ASTRAI_STREAMK=0 disables it.
+// all CTAs (see GemmParams). Measured on B200 over the 1.1B step's GEMMs, the split paid off on
+// every shape with long K (>= 128 k-blocks: weight gradients over 8192 tokens, K = 32000) and at
+// least half a wave of tiles (0.26 vs 0.33 ms for 11264x2048x8192, 0.69 vs 0.73 ms for
+// 8192x2048x32000), and lost 5 - 20 us on shorter K (2048 - 5632) and on grids of fewer than half
+// the SMs, where the unsplit tiles run faster per CTA for want of contention. So it is used only
+// there, and only when every CTA gets at least 4 k-blocks and the split saves at least 16 k-blocks
+// of time. ASTRAI_STREAMK=0 disables it.
 static bool streamk_on() {
   static const bool on = [] {
     const char* e = std::getenv("ASTRAI_STREAMK");
@@ -840,6 +842,7 @@ static bool streamk_on() {
 static bool use_streamk(long long tiles, int kb, int sms) {
   if (!streamk_on() || tiles <= 0 || sms <= 0) return false;
   const long long rem = tiles % sms;
+  if (kb < 128 || 2 * tiles < sms) return false;
   if (rem == 0 || rem * kb < 4LL * sms) return false;
   const double dp = (double)(tiles / sms + 1), sk = (double)tiles / sms + 0.08;
   return (dp - sk) * kb >= 16.0;

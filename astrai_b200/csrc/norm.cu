@@ -17,7 +17,8 @@
 namespace astrai {
 
 constexpr int kNormThreads = 256;
-constexpr int kNormBlocksTarget = 592;  // 4 resident 256-thread blocks on each of 148 SMs
+constexpr int kNormBlocksTarget = 592;     // forward: 4 resident 256-thread blocks on each of 148 SMs
+constexpr int kNormBwdBlocksTarget = 444;  // backward (<= 85 registers): 3 per SM, one wave
 
 // Sum of v over the block (nw warps), through red[buf] (double-buffered by the caller so that one
 // barrier per row suffices: a buffer is rewritten only after the next row's barrier).
@@ -116,8 +117,11 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_small_kernel(const __nv_bfloa
 }
 
 // dx = r*w*dy - x * r^3 * mean(dy*w*x) (+ dres);   dw_partial[block] = sum over the block's rows of dy*x*r
+// Issue-bound at this size once the loads overlap, so the inner loop is kept short: w is
+// converted to fp32 once per block, each row's x and dy once (g*w is reused by the dot product and
+// by dx), and dx / dw are single FMAs per element.
 template <int V>
-__global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, long long lddy,
+__global__ void __launch_bounds__(kNormThreads, V == 1 ? 3 : 2) rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, long long lddy,
                                                                    const __nv_bfloat16* __restrict__ x, long long ldx,
                                                                    const __nv_bfloat16* __restrict__ w,
                                                                    const float* __restrict__ rstd,
@@ -128,24 +132,35 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(const __nv_bf
   __shared__ float red[2][32];
   const int T = blockDim.x, nw = T >> 5;
   int col[V];
-  uint4 wp[V], cx[V], cg[V], cr[V];
-  float acc[V][8];
+  float wf[V][8], acc[V][8];
+  uint4 cx[V], cg[V], cr[V];
   const uint4 z = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
   for (int v = 0; v < V; ++v) {
     col[v] = (v * T + threadIdx.x) * 8;
-    wp[v] = col[v] < D ? *reinterpret_cast<const uint4*>(w + col[v]) : z;
+    const uint4 wu = col[v] < D ? *reinterpret_cast<const uint4*>(w + col[v]) : z;
+    const uint32_t ww[4] = {wu.x, wu.y, wu.z, wu.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16(ww[j]);
+      wf[v][2 * j] = f.x;
+      wf[v][2 * j + 1] = f.y;
+    }
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[v][j] = 0.f;
   }
   const int r0 = blockIdx.x * rows_per_block, r1 = min(rows, r0 + rows_per_block);
+  const __nv_bfloat16* xp = x + (long long)r0 * ldx;
+  const __nv_bfloat16* gp = dy + (long long)r0 * lddy;
+  const __nv_bfloat16* rp = dres ? dres + (long long)r0 * ldres : nullptr;
+  __nv_bfloat16* op = dx + (long long)r0 * lddx;
   float crs = r0 < r1 ? rstd[r0] : 0.f;
 #pragma unroll
   for (int v = 0; v < V; ++v) {
     const bool ok = r0 < r1 && col[v] < D;
-    cx[v] = ok ? *reinterpret_cast<const uint4*>(x + (long long)r0 * ldx + col[v]) : z;
-    cg[v] = ok ? *reinterpret_cast<const uint4*>(dy + (long long)r0 * lddy + col[v]) : z;
-    cr[v] = (ok && dres) ? *reinterpret_cast<const uint4*>(dres + (long long)r0 * ldres + col[v]) : z;
+    cx[v] = ok ? *reinterpret_cast<const uint4*>(xp + col[v]) : z;
+    cg[v] = ok ? *reinterpret_cast<const uint4*>(gp + col[v]) : z;
+    cr[v] = (ok && rp) ? *reinterpret_cast<const uint4*>(rp + col[v]) : z;
   }
   for (int row = r0; row < r1; ++row) {
     // next row's loads first: they overlap this row's reduction
@@ -155,44 +170,55 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(const __nv_bf
 #pragma unroll
     for (int v = 0; v < V; ++v) {
       const bool ok = more && col[v] < D;
-      nx[v] = ok ? *reinterpret_cast<const uint4*>(x + (long long)(row + 1) * ldx + col[v]) : z;
-      ng[v] = ok ? *reinterpret_cast<const uint4*>(dy + (long long)(row + 1) * lddy + col[v]) : z;
-      nr[v] = (ok && dres) ? *reinterpret_cast<const uint4*>(dres + (long long)(row + 1) * ldres + col[v]) : z;
+      nx[v] = ok ? *reinterpret_cast<const uint4*>(xp + ldx + col[v]) : z;
+      ng[v] = ok ? *reinterpret_cast<const uint4*>(gp + lddy + col[v]) : z;
+      nr[v] = (ok && rp) ? *reinterpret_cast<const uint4*>(rp + ldres + col[v]) : z;
     }
+    float xf[V][8], gw[V][8], gf[V][8];
     float dot = 0.f;
 #pragma unroll
     for (int v = 0; v < V; ++v) {
       const uint32_t xx[4] = {cx[v].x, cx[v].y, cx[v].z, cx[v].w}, gg[4] = {cg[v].x, cg[v].y, cg[v].z, cg[v].w};
-      const uint32_t ww[4] = {wp[v].x, wp[v].y, wp[v].z, wp[v].w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float2 xf = unpack_bf16(xx[j]), gf = unpack_bf16(gg[j]), wf = unpack_bf16(ww[j]);
-        dot += gf.x * wf.x * xf.x + gf.y * wf.y * xf.y;
+        const float2 a = unpack_bf16(xx[j]), b = unpack_bf16(gg[j]);
+        xf[v][2 * j] = a.x;
+        xf[v][2 * j + 1] = a.y;
+        gf[v][2 * j] = b.x;
+        gf[v][2 * j + 1] = b.y;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        gw[v][j] = gf[v][j] * wf[v][j];
+        dot = fmaf(gw[v][j], xf[v][j], dot);
       }
     }
     dot = block_sum(dot, red[row & 1], nw);
-    const float r = crs, k = dot * r * r * r / (float)D;
+    const float r = crs, nk = -dot * r * r * r / (float)D;
 #pragma unroll
     for (int v = 0; v < V; ++v) {
       if (col[v] < D) {
-        const uint32_t xx[4] = {cx[v].x, cx[v].y, cx[v].z, cx[v].w}, gg[4] = {cg[v].x, cg[v].y, cg[v].z, cg[v].w};
-        const uint32_t rr[4] = {cr[v].x, cr[v].y, cr[v].z, cr[v].w}, ww[4] = {wp[v].x, wp[v].y, wp[v].z, wp[v].w};
+        const uint32_t rr[4] = {cr[v].x, cr[v].y, cr[v].z, cr[v].w};
         uint32_t o[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float2 xf = unpack_bf16(xx[j]), gf = unpack_bf16(gg[j]), af = unpack_bf16(rr[j]),
-                       wf = unpack_bf16(ww[j]);
-          o[j] = pack_bf16(r * wf.x * gf.x - xf.x * k + af.x, r * wf.y * gf.y - xf.y * k + af.y);
-          acc[v][2 * j] += gf.x * xf.x * r;
-          acc[v][2 * j + 1] += gf.y * xf.y * r;
+          const float2 af = unpack_bf16(rr[j]);
+          o[j] = pack_bf16(fmaf(r, gw[v][2 * j], fmaf(xf[v][2 * j], nk, af.x)),
+                           fmaf(r, gw[v][2 * j + 1], fmaf(xf[v][2 * j + 1], nk, af.y)));
         }
-        *reinterpret_cast<uint4*>(dx + (long long)row * lddx + col[v]) = make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(op + col[v]) = make_uint4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[v][j] = fmaf(gf[v][j] * r, xf[v][j], acc[v][j]);
       }
       cx[v] = nx[v];
       cg[v] = ng[v];
       cr[v] = nr[v];
     }
     crs = nrs;
+    xp += ldx;
+    gp += lddy;
+    if (rp) rp += ldres;
+    op += lddx;
   }
 #pragma unroll
   for (int v = 0; v < V; ++v) {
@@ -291,10 +317,10 @@ __global__ void __launch_bounds__(1024) reduce_cols_kernel(const float* __restri
 
 namespace astrai_host {
 
-// Rows per block for the block-per-row kernels: about kNormBlocksTarget blocks (at most `cap`),
-// each a contiguous range of rows.
-static int norm_rows_per_block(int rows, long long cap) {
-  long long nb = std::min<long long>(std::min<long long>(rows, astrai::kNormBlocksTarget), std::max(1LL, cap));
+// Rows per block for the block-per-row kernels: about `target` blocks (at most `cap`), each a
+// contiguous range of rows.
+static int norm_rows_per_block(int rows, long long cap, int target = astrai::kNormBwdBlocksTarget) {
+  long long nb = std::min<long long>(std::min<long long>(rows, target), std::max(1LL, cap));
   return (int)((rows + nb - 1) / nb);
 }
 static bool norm_small(int D) { return D <= 256 && D % 32 == 0; }
@@ -311,7 +337,7 @@ void rmsnorm_fwd(const void* x, long long ldx, const void* w, void* y, long long
     (astrai::note_launch(), rmsnorm_fwd_small_kernel<<<(rows + 7) / 8, 256, 0, s>>>(X, ldx, W, Y, ldy, rstd, rows, D, eps));
     return;
   }
-  const int rpb = norm_rows_per_block(rows, 1LL << 30);
+  const int rpb = norm_rows_per_block(rows, 1LL << 30, kNormBlocksTarget);
   const int nb = (rows + rpb - 1) / rpb;
   const int T = std::min(kNormThreads, ((D / 8 + 31) / 32) * 32);
   if (D <= 8 * kNormThreads)

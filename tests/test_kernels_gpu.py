@@ -117,7 +117,7 @@ def test_linear_autograd():
 
 
 @pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 1)])
-@pytest.mark.parametrize("M,N,K", [(8192, 2048, 2048), (2048, 2048, 8192), (1000, 3000, 4000), (8192, 5632, 2048)])
+@pytest.mark.parametrize("M,N,K", [(3072, 2048, 8192), (2048, 5632, 8192), (3000, 2000, 8200)])
 def test_gemm_streamk(a_mn, b_mn, M, N, K):
     """Shapes whose last wave of tiles is split over all SMs by k-blocks (the plan says so), against
     an fp32 matmul; run twice so the fix-up flags are shown to reset between launches."""
