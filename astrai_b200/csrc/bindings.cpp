@@ -17,10 +17,17 @@ void skinny_gemm(const void* X, long long ldx, const void* W, long long ldw, con
                  void* Y, long long ldy, int M, int N, int K, int sms, cudaStream_t s);
 int num_sms(int device);
 int read_and_clear_error();
+struct GatherArgs {
+  int npeers;
+  long long peer_delta[7];
+  unsigned* flag;
+  unsigned* done;
+  unsigned epoch;
+};
 void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int N, int K, int batch, int a_mn,
                long long lda, long long strideA, int b_mn, long long ldb, long long strideB, long long ldd,
                long long strideD, int out_f32, long long ldc, long long strideC, float alpha, float beta,
-               int force_bn, cudaStream_t stream);
+               int force_bn, cudaStream_t stream, const GatherArgs* gather = nullptr);
 void gemm_profile_set(unsigned long long* counters);
 void gemm_plan(int M, int N, int K, int batch, int* out);
 void gemm_rope_bf16(const void* A, long long lda, const void* B, long long ldb, void* D, long long ldd, int M, int N,
@@ -207,6 +214,37 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& d, const c10::op
                          a.stride(ar), batched ? a.stride(0) : 0, (int)b_mn, b.stride(ar), batched ? b.stride(0) : 0,
                          d.stride(ar), batched ? d.stride(0) : 0, d.scalar_type() == at::kFloat ? 1 : 0, ldc, sc,
                          (float)alpha, (float)beta, (int)force_bn, stream());
+}
+
+// GEMM fused with an all-gather over NVLink peer memory: d is this rank's column block of the
+// gathered output inside a symmetric buffer; the epilogue also stores every output vector into each
+// peer's copy (d + peer_deltas[q] bytes) and the last CTA raises this rank's flag on every peer
+// (flag_addr + peer_deltas[q] <- epoch). The caller waits for the peers' flags.
+void gemm_gather(const at::Tensor& a, const at::Tensor& b, at::Tensor& d, const std::vector<int64_t>& peer_deltas,
+                 int64_t flag_addr, int64_t done_addr, int64_t epoch, int64_t a_mn, int64_t b_mn) {
+  check_bf16(a, "a");
+  check_bf16(b, "b");
+  check_bf16(d, "d");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && d.dim() == 2, "gemm_gather: 2-D operands");
+  TORCH_CHECK(peer_deltas.size() <= 7, "gemm_gather: at most 7 peers");
+  TORCH_CHECK(flag_addr % 4 == 0 && done_addr % 4 == 0 && flag_addr != 0 && done_addr != 0, "gemm_gather: flags");
+  const long long M = a_mn ? a.size(1) : a.size(0);
+  const long long K = a_mn ? a.size(0) : a.size(1);
+  const long long N = b_mn ? b.size(1) : b.size(0);
+  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K, "gemm_gather: K mismatch");
+  TORCH_CHECK(d.size(0) == M && d.size(1) == N && d.stride(1) == 1, "gemm_gather: output shape");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && (a.stride(0) * 2) % 16 == 0 && (b.stride(0) * 2) % 16 == 0,
+              "gemm_gather: operands need contiguous rows with 16-byte strides");
+  astrai_host::GatherArgs g{};
+  g.npeers = (int)peer_deltas.size();
+  for (size_t q = 0; q < peer_deltas.size(); ++q) g.peer_delta[q] = peer_deltas[q];
+  g.flag = reinterpret_cast<unsigned*>(flag_addr);
+  g.done = reinterpret_cast<unsigned*>(done_addr);
+  g.epoch = (unsigned)epoch;
+  c10::cuda::CUDAGuard guard(a.device());
+  astrai_host::gemm_bf16(a.data_ptr(), b.data_ptr(), d.data_ptr(), nullptr, (int)M, (int)N, (int)K, 1, (int)a_mn,
+                         a.stride(0), 0, (int)b_mn, b.stride(0), 0, d.stride(0), 0, 0, 0, 0, 1.f, 0.f, 0, stream(),
+                         &g);
 }
 
 // ----------------------------------------------------------------- RMSNorm
@@ -440,6 +478,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "bf16 tcgen05 GEMM", py::arg("a"), py::arg("b"), py::arg("d"), py::arg("c") = py::none(),
         py::arg("a_mn") = 0, py::arg("b_mn") = 0, py::arg("alpha") = 1.0, py::arg("beta") = 0.0,
         py::arg("force_bn") = 0);
+  m.def("gemm_gather", &gemm_gather, "bf16 GEMM whose epilogue also stores into every peer's copy (fused all-gather)",
+        py::arg("a"), py::arg("b"), py::arg("d"), py::arg("peer_deltas"), py::arg("flag_addr"), py::arg("done_addr"),
+        py::arg("epoch"), py::arg("a_mn") = 0, py::arg("b_mn") = 0);
   m.def("gemm_plan", [](int64_t M, int64_t N, int64_t K, int64_t batch) {
     int o[5] = {0, 0, 0, 0, 0};
     astrai_host::gemm_plan((int)M, (int)N, (int)K, (int)batch, o);

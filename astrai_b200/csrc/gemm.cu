@@ -29,6 +29,8 @@
 
 namespace astrai {
 
+constexpr int kMaxGatherPeers = 7;  // 8 ranks per node
+
 struct GemmParams {
   int M, N, K, batch;
   int tiles_m, tiles_n, k_blocks;
@@ -83,7 +85,46 @@ struct GemmParams {
   long long sk_units;
   float* sk_ws;
   int* sk_flags;
+  // Fused all-gather (npeers > 0; plain bf16 GEMMs without C): D is this rank's column block of a
+  // row-major output that every rank holds at the same offset of a symmetric buffer. Every vector
+  // the epilogue stores at D + o is also stored at D + o + peer_delta[q] bytes (rank q's copy, over
+  // NVLink) for q < npeers. When the grid's last tile is stored, the last CTA to finish raises
+  // this rank's flag on every peer (gather_flag + peer_delta[q] <- gather_epoch, release).
+  int npeers;
+  long long peer_delta[kMaxGatherPeers];
+  unsigned* gather_flag;
+  unsigned* gather_done;  // grid-completion counter, zero between launches
+  unsigned gather_epoch;
 };
+
+// Fused all-gather: after the epilogue warps stored tile (b, mb, nb) into the local D, copy it from
+// L2 to every peer's copy, one 16-byte vector per thread and consecutive threads along a row, so a
+// warp writes 512 contiguous bytes per instruction over NVLink (the row-per-thread layout of the
+// epilogue stores would send 16-byte fragments of 32 different rows).
+template <int BM, int BN>
+__device__ __forceinline__ void gather_copy_tile(const GemmParams& p, int b, int mb, int nb, int et, int nthreads) {
+  constexpr int VPR = BN / 8;  // 16-byte vectors per tile row
+  const __nv_bfloat16* D = reinterpret_cast<const __nv_bfloat16*>(p.D) + (long long)b * p.strideD;
+  for (int i = et; i < BM * VPR; i += nthreads) {
+    const int row = mb * BM + i / VPR, col = nb * BN + (i % VPR) * 8;
+    if (row >= p.M || col >= p.N) continue;
+    const __nv_bfloat16* src = D + (long long)row * p.ldd + col;
+    char* dst0 = reinterpret_cast<char*>(const_cast<__nv_bfloat16*>(src));
+    if (col + 8 <= p.N && p.vec_ok) {
+      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src));
+#pragma unroll
+      for (int q = 0; q < kMaxGatherPeers; ++q)
+        if (q < p.npeers) *reinterpret_cast<uint4*>(dst0 + p.peer_delta[q]) = v;
+    } else {
+      for (int e = 0; e < 8 && col + e < p.N; ++e) {
+        const __nv_bfloat16 v = src[e];
+#pragma unroll
+        for (int q = 0; q < kMaxGatherPeers; ++q)
+          if (q < p.npeers) *reinterpret_cast<__nv_bfloat16*>(dst0 + 2 * e + p.peer_delta[q]) = v;
+      }
+    }
+  }
+}
 
 // One unit of a CTA's work: tile `tile`, k-blocks [kb0, kb1).
 struct WorkItem {
@@ -686,6 +727,10 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
             }
           }
         }
+        if (p.npeers > 0) {
+          named_bar_sync(1, EPI_THREADS);  // the whole tile is in the local D
+          gather_copy_tile<BM, BN>(p, b, mb, nb, et, EPI_THREADS);
+        }
         if (++acc == NACC) {
           acc = 0;
           acc_phase ^= 1;
@@ -770,16 +815,32 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
           }
         }
       }
+      if (!OUT_F32 && p.npeers > 0) {
+        named_bar_sync(1, EPI_THREADS);  // the whole tile is in the local D
+        gather_copy_tile<BM, BN>(p, b, mb, nb, et, EPI_THREADS);
+      }
       if (++acc == NACC) {
         acc = 0;
         acc_phase ^= 1;
       }
     }
   }
+  if (p.npeers > 0) __threadfence_system();  // this thread's peer stores, before the grid count
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::TMEM_COLS < 32 ? 32 : Cfg::TMEM_COLS);
+  }
+  if (p.npeers > 0 && threadIdx.x == 0 && atomicAdd(p.gather_done, 1u) == gridDim.x - 1) {
+    // last CTA: every CTA's stores are fenced; tell every peer that this rank's block has landed
+    __threadfence_system();
+#pragma unroll
+    for (int q = 0; q < kMaxGatherPeers; ++q)
+      if (q < p.npeers) {
+        unsigned* f = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(p.gather_flag) + p.peer_delta[q]);
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(p.gather_epoch) : "memory");
+      }
+    *p.gather_done = 0u;
   }
 }
 
@@ -914,6 +975,15 @@ static void pick_tile(int M, int N, int batch, int sms, int& bm, int& bn, int kb
 // a_mn == 0: A stored [batch][M][lda] (K contiguous); a_mn == 1: [batch][K][lda] (M contiguous).
 // b_mn == 0: B stored [batch][N][ldb];                b_mn == 1: [batch][K][ldb].
 // force_bn: 0 = automatic; 128 / 256 = BM 128 with that BN; 512 = 256 x 256 tiles.
+// Fused all-gather arguments of gemm_bf16 (see GemmParams::npeers).
+struct GatherArgs {
+  int npeers;
+  long long peer_delta[astrai::kMaxGatherPeers];
+  unsigned* flag;
+  unsigned* done;
+  unsigned epoch;
+};
+
 // The plan gemm_bf16 would use for a plain GEMM on the current device: tile shape and whether the
 // last partial wave is split Stream-K style (out: bm, bn, streamk, tiles, sms).
 void gemm_plan(int M, int N, int K, int batch, int* out) {
@@ -933,7 +1003,7 @@ void gemm_plan(int M, int N, int K, int batch, int* out) {
 void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int N, int K, int batch, int a_mn,
                long long lda, long long strideA, int b_mn, long long ldb, long long strideB, long long ldd,
                long long strideD, int out_f32, long long ldc, long long strideC, float alpha, float beta,
-               int force_bn, cudaStream_t stream) {
+               int force_bn, cudaStream_t stream, const GatherArgs* gather) {
   if (M <= 0 || N <= 0 || K <= 0 || batch <= 0) throw std::runtime_error("astrai gemm: empty problem");
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1008,9 +1078,21 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
   p.sk_units = 0;
   p.sk_ws = nullptr;
   p.sk_flags = nullptr;
+  p.npeers = 0;
+  p.gather_flag = nullptr;
+  p.gather_done = nullptr;
+  p.gather_epoch = 0;
   const int tiles = batch * p.tiles_m * p.tiles_n;
   int grid = std::min(tiles, sms);
-  if (use_streamk(tiles, p.k_blocks, sms) && sk_buffers(dev, stream, sms, &p.sk_ws, &p.sk_flags)) {
+  if (gather != nullptr) {
+    if (C != nullptr || out_f32 || batch != 1 || gather->npeers < 0 || gather->npeers > astrai::kMaxGatherPeers)
+      throw std::runtime_error("astrai gemm: the fused all-gather takes a plain bf16 GEMM and at most 7 peers");
+    p.npeers = gather->npeers;
+    for (int q = 0; q < gather->npeers; ++q) p.peer_delta[q] = gather->peer_delta[q];
+    p.gather_flag = gather->flag;
+    p.gather_done = gather->done;
+    p.gather_epoch = gather->epoch;
+  } else if (use_streamk(tiles, p.k_blocks, sms) && sk_buffers(dev, stream, sms, &p.sk_ws, &p.sk_flags)) {
     p.dp_tiles = tiles / sms * sms;
     p.sk_units = (long long)(tiles - p.dp_tiles) * p.k_blocks;
     grid = sms;
@@ -1099,6 +1181,10 @@ void gemm_grouped_bf16(int mode, const void* A, const void* B, void* D, const vo
   p.sk_units = 0;
   p.sk_ws = nullptr;
   p.sk_flags = nullptr;
+  p.npeers = 0;
+  p.gather_flag = nullptr;
+  p.gather_done = nullptr;
+  p.gather_epoch = 0;
   const int tiles = p.batch * p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, sms);
   if (BN == 256)
@@ -1181,6 +1267,10 @@ void gemm_swiglu_bf16(int mode, const void* A, long long lda, const void* B, lon
   p.sk_units = 0;
   p.sk_ws = nullptr;
   p.sk_flags = nullptr;
+  p.npeers = 0;
+  p.gather_flag = nullptr;
+  p.gather_done = nullptr;
+  p.gather_epoch = 0;
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, sms);
   dispatch_majors<128, 256>(0, mode == 1 ? 0 : b_mn, 0, ta, tb, p, grid, stream);
@@ -1250,6 +1340,10 @@ void gemm_rope_bf16(const void* A, long long lda, const void* B, long long ldb, 
   p.sk_units = 0;
   p.sk_ws = nullptr;
   p.sk_flags = nullptr;
+  p.npeers = 0;
+  p.gather_flag = nullptr;
+  p.gather_done = nullptr;
+  p.gather_epoch = 0;
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, sms);
   if (BN == 256)

@@ -12,6 +12,11 @@ Differences: the local products run on the framework's GEMM (CUDA bf16) or
 correctly (the backward of the sum is the identity on every rank, the
 backward of the gather is the rank's slice of the output gradient); the
 reference calls ``dist.all_reduce`` / ``dist.all_gather`` outside autograd.
+
+``ColumnParallelLinear(..., fused=True)`` (CUDA, bf16, no bias, ranks on one NVLink
+domain) replaces "GEMM, then all-gather" by :class:`GatherGemm`: ONE GEMM kernel per rank
+whose epilogue stores every output tile into every rank's copy of the gathered output
+over NVLink peer memory, so the transfer overlaps the remaining tiles' math.
 """
 
 from __future__ import annotations
@@ -24,6 +29,7 @@ import torch.nn as nn
 from torch import Tensor
 
 from astrai_b200.ops.gemm import linear
+from astrai_b200.parallel.symm import SymmetricBuffer, _align
 
 
 class _AllReduceSum(torch.autograd.Function):
@@ -51,6 +57,99 @@ class _AllGatherLast(torch.autograd.Function):
     def backward(ctx, g):
         s = ctx.rank * ctx.width
         return g[..., s:s + ctx.width].contiguous(), None, None, None
+
+
+class GatherGemm:
+    """``y[M, world*n] = all_gather_columns(x[M, K] @ w[n, K]^T)`` as one fused kernel per rank.
+
+    The gathered output lives in a symmetric buffer (same offset on every rank, each rank's copy
+    mapped into every rank). Call ``e`` on every rank:
+
+    1. wait (bounded) until every peer has copied call ``e-1``'s result out of its buffer
+       (flag row 1), so no peer's stores of call ``e`` can overwrite data still being read;
+    2. ``gemm_gather``: the GEMM writes its column block into every rank's copy; its last CTA
+       raises this rank's flag in row 0 of every peer;
+    3. wait (bounded) for row 0 of every peer, copy the gathered result out, raise row 1.
+
+    Every rank must make the same calls with the same shapes (as with any collective).
+    """
+
+    def __init__(self, group=None, wait_s: float = 20.0):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.wait_s = wait_s
+        self.buf: SymmetricBuffer = None
+        self.cap = 0
+        self.epoch = 0
+
+    def _ensure(self, nbytes: int, dev: torch.device) -> None:
+        if self.buf is not None and self.cap >= nbytes:
+            return
+        if self.buf is not None:
+            torch.cuda.synchronize(dev)
+            dist.barrier(group=self.group)
+            self.buf.close()
+        self.flag_off = _align(nbytes)
+        self.done_off = self.flag_off + _align(4 * 2 * self.world)
+        self.buf = SymmetricBuffer(self.done_off + 256, self.group, dev)
+        self.buf.local_view(self.flag_off, self.done_off + 256 - self.flag_off).zero_()
+        self.deltas = [self.buf.ptrs[q] - self.buf.ptrs[self.rank] for q in range(self.world) if q != self.rank]
+        self.raise_done = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.cap, self.epoch = nbytes, 0
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=self.group)
+
+    def __call__(self, x: Tensor, w: Tensor) -> Tensor:
+        from astrai_b200.ops._ext import native
+
+        C = native()
+        M, n = x.shape[0], w.shape[0]
+        Nt = n * self.world
+        dev = x.device
+        self._ensure(M * Nt * 2, dev)
+        full = self.buf.local_view(0, M * Nt * 2).view(torch.bfloat16).view(M, Nt)
+        flags = self.buf.local_ptr + self.flag_off
+        if self.epoch > 0:
+            C.peer_flags_wait(flags + 4 * self.world, dev.index, self.rank, self.world, 1, self.epoch, self.wait_s)
+        self.epoch += 1
+        C.gemm_gather(x, w, full[:, self.rank * n:(self.rank + 1) * n], self.deltas, flags + 4 * self.rank,
+                      self.buf.local_ptr + self.done_off, self.epoch)
+        C.peer_flags_wait(flags, dev.index, self.rank, self.world, 1, self.epoch, self.wait_s)
+        y = full.clone()
+        # this rank is done reading call `epoch`: raise its flag in row 1 on every peer
+        C.muon_apply_peers(None, None, self.buf.peer_base, None, 0, 1, 1, False, 1.0, 0.0, self.rank, self.world,
+                           self.flag_off, 1, self.epoch, self.raise_done)
+        return y
+
+    def close(self) -> None:
+        if self.buf is not None:
+            self.buf.close()
+            self.buf = None
+
+
+class _GatherLinearFn(torch.autograd.Function):
+    """Forward through :class:`GatherGemm`; backward on this rank's column slice of the gradient."""
+
+    @staticmethod
+    def forward(ctx, x2, w, gg, rank):
+        ctx.save_for_backward(x2, w)
+        ctx.rank = rank
+        return gg(x2, w)
+
+    @staticmethod
+    def backward(ctx, g):
+        from astrai_b200.ops._ext import native
+
+        x2, w = ctx.saved_tensors
+        n = w.shape[0]
+        gl = g[:, ctx.rank * n:(ctx.rank + 1) * n].contiguous()
+        C = native()
+        dx = torch.empty_like(x2)
+        C.gemm(gl, w, dx, None, 0, 1)   # [M, n] @ [n, K]
+        dw = torch.empty_like(w)
+        C.gemm(gl, x2, dw, None, 1, 1)  # [M, n]^T @ [M, K]
+        return dx, dw, None, None
 
 
 class ParallelModel(nn.Module):
@@ -95,8 +194,10 @@ class RowParallelLinear(ParallelModel):
 
 class ColumnParallelLinear(ParallelModel):
     def __init__(self, process_group, in_features: int, out_features: int, bias: bool = True,
-                 gather_results: bool = True):
+                 gather_results: bool = True, fused: bool = False):
         super().__init__(process_group)
+        self.fused = fused
+        self._gg = None
         if out_features % self.world_size:
             raise ValueError(f"out_features must be divisible by world_size. Got {out_features} and {self.world_size}")
         self.in_features, self.out_features = in_features, out_features
@@ -106,7 +207,18 @@ class ColumnParallelLinear(ParallelModel):
         nn.init.normal_(self.weight, std=0.02)
         self.bias = nn.Parameter(torch.zeros(self.out_features_per_rank)) if bias else None
 
+    def _fused_ok(self, x: Tensor) -> bool:
+        return (self.fused and self.gather_results and self.world_size > 1 and self.bias is None and x.is_cuda
+                and x.dtype == torch.bfloat16 and self.weight.dtype == torch.bfloat16 and self.in_features % 8 == 0
+                and self.out_features_per_rank % 8 == 0)
+
     def forward(self, input: Tensor) -> Tensor:
+        if self._fused_ok(input):
+            if self._gg is None:
+                self._gg = GatherGemm(self.process_group)
+            x2 = input.reshape(-1, self.in_features).contiguous()
+            out = _GatherLinearFn.apply(x2, self.weight, self._gg, self.rank)
+            return out.view(*input.shape[:-1], self.out_features)
         out = _matmul(input, self.weight)
         if self.bias is not None:
             out = out + self.bias

@@ -1,7 +1,7 @@
 """Device-timed micro-benchmarks of the framework's kernels.
 
     python -m astrai_b200.utils.kernel_bench [gemm [case]|attn|norm|skinny|sample|all]
-    torchrun --nproc-per-node N -m astrai_b200.utils.kernel_bench allreduce|ep
+    torchrun --nproc-per-node N -m astrai_b200.utils.kernel_bench allreduce|ep|tpgather
 
 Each case is timed with CUDA events on the launching stream after warm-up,
 with a synchronize on both sides; inputs larger than L2 are used where the
@@ -90,6 +90,17 @@ def bench_gemm(only=None):
                           "wait_frac_per_cta": {k: round(v / sms / cyc, 3) for k, v in
                                                 zip(("producer_empty", "mma_full", "mma_acc_empty", "epi_acc_full"),
                                                     w)}}))
+
+
+def _dist_init():
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return dist.get_rank(), dist.get_world_size()
 
 
 def bench_allreduce():
@@ -235,6 +246,62 @@ def bench_ep(tokens: int = 8192, d: int = 2048, n_experts: int = 64, k: int = 6)
     dist.destroy_process_group()
 
 
+def bench_tpgather(M: int = 8192, K: int = 2048, N: int = 8192):
+    """Column-parallel linear over the ranks: y[M, N] = all-gather of x @ w_r^T ([M, N / world] per
+    rank). Fused: one GEMM whose epilogue stores into every rank's copy (GatherGemm, including its
+    flag waits and the copy out of the symmetric buffer). Baseline: the same GEMM, then NCCL
+    all_gather_into_tensor and the column interleave. Device time, max over ranks."""
+    import torch.distributed as dist
+
+    from astrai_b200.ops._ext import native
+    from astrai_b200.parallel.module import GatherGemm
+
+    rank, world = _dist_init()
+    C = native()
+    hbm, tf, src = peaks()
+    n = N // world
+    torch.manual_seed(rank)
+    x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(n, K, device="cuda") * 0.05).to(torch.bfloat16)
+    gg = GatherGemm()
+    loc = torch.empty(M, n, device="cuda", dtype=torch.bfloat16)
+    flat = torch.empty(world * M, n, device="cuda", dtype=torch.bfloat16)
+
+    def fused():
+        return gg(x, w)
+
+    def gemm_only():
+        C.gemm(x, w, loc, None, 0, 0)
+
+    def nccl():
+        C.gemm(x, w, loc, None, 0, 0)
+        dist.all_gather_into_tensor(flat, loc)
+        return flat.view(world, M, n).permute(1, 0, 2).reshape(M, N)
+
+    ref = nccl()
+    assert torch.equal(fused(), ref), "fused all-gather GEMM differs from GEMM + NCCL"
+    res = {}
+    for name, fn in (("fused_ms", fused), ("gemm_only_ms", gemm_only), ("gemm_nccl_ms", nccl)):
+        dist.barrier()
+        ms = time_fn(fn, warmup=5, iters=20)
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        res[name] = round(t.item(), 4)
+    torch.cuda.synchronize()
+    err = int(C.read_error())
+    gg.close()
+    dist.barrier()
+    if rank == 0:
+        fl = 2.0 * M * n * K
+        link = 770.0  # measured NVLink peer copy GB/s per direction
+        nv_ms = M * n * 2 * (world - 1) / (link * 1e6)
+        print(json.dumps({"kernel": "gemm_allgather", "world": world, "M": M, "K": K, "N": N, **res,
+                          "speedup_vs_nccl": round(res["gemm_nccl_ms"] / res["fused_ms"], 2),
+                          "roofline_ms": round(max(fl / (tf * 1e9), nv_ms), 4),
+                          "device_error_word": err}))
+    dist.destroy_process_group()
+
+
 def bench_skinny():
     """Decode GEMMs (M token rows x weight [N, K]): device time and weight-read bandwidth."""
     from astrai_b200.ops._ext import native
@@ -306,6 +373,9 @@ def main(argv=None):
         return
     if which == "ep":
         bench_ep()
+        return
+    if which == "tpgather":
+        bench_tpgather()
         return
     if which in ("skinny", "all"):
         bench_skinny()

@@ -158,12 +158,66 @@ def _sharded_muon_worker(rank, world, port, out_path):
         dist.destroy_process_group()
 
 
+def _gather_worker(rank, world, port):
+    """GEMM fused with the all-gather (epilogue stores into every rank's copy) against the local GEMM
+    plus an NCCL all-gather: four calls with new inputs (the buffer is reused, so the flag handshake
+    between calls is exercised), then the fused ColumnParallelLinear forward and backward."""
+    dist = _init(rank, world, port)
+    try:
+        from astrai_b200.ops._ext import native
+        from astrai_b200.parallel.module import ColumnParallelLinear, GatherGemm
+
+        native().read_error()
+        C = native()
+        M, K, n = 1000, 512, 264
+        gg = GatherGemm()
+        for it in range(4):
+            torch.manual_seed(100 * it + rank)
+            x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+            w = (torch.randn(n, K, device="cuda") * 0.05).to(torch.bfloat16)
+            y = gg(x, w)
+            loc = torch.empty(M, n, device="cuda", dtype=torch.bfloat16)
+            C.gemm(x, w, loc, None, 0, 0)
+            parts = [torch.empty_like(loc) for _ in range(world)]
+            dist.all_gather(parts, loc)
+            torch.testing.assert_close(y, torch.cat(parts, dim=1), atol=0, rtol=0)
+        torch.cuda.synchronize()
+        assert native().read_error() == 0
+        gg.close()
+        torch.manual_seed(7)
+        layers = [ColumnParallelLinear(None, 512, 1024, bias=False, fused=f).cuda().to(torch.bfloat16) for f in (1, 0)]
+        layers[1].weight.data.copy_(layers[0].weight.data)
+        torch.manual_seed(8 + rank)
+        x0 = torch.randn(4, 300, 512, device="cuda").to(torch.bfloat16)
+        g = torch.randn(4, 300, 1024, device="cuda").to(torch.bfloat16)
+        outs = []
+        for layer in layers:
+            x = x0.clone().requires_grad_()
+            y = layer(x)
+            y.backward(g)
+            outs.append((y, x.grad, layer.weight.grad))
+        assert layers[0]._gg is not None and layers[1]._gg is None
+        for a, b in zip(outs[0], outs[1]):
+            torch.testing.assert_close(a.float(), b.float(), atol=2e-2, rtol=2e-2)
+        torch.cuda.synchronize()
+        assert native().read_error() == 0
+        dist.barrier()
+        layers[0]._gg.close()
+    finally:
+        dist.destroy_process_group()
+
+
 def _spawn(fn, world, *args):
     import torch.multiprocessing as mp
 
     from astrai_b200.parallel import find_free_port
 
     mp.start_processes(fn, args=(world, find_free_port()) + args, nprocs=world, start_method="spawn", join=True)
+
+
+@need2
+def test_gemm_fused_allgather_matches_nccl():
+    _spawn(_gather_worker, min(NGPU, 4))
 
 
 @need2
