@@ -21,6 +21,10 @@ void muon_apply_peers(const long long* pptr, const long long* poff, const long l
                       long long flag_off, int slot, unsigned epoch, unsigned* done, cudaStream_t s);
 void peer_flags_wait(const unsigned* flags, int rank, int world, int rows, unsigned epoch, double wait_s,
                      cudaStream_t s);
+void row_reduce_bcast(const void* part, const void* recv, void* out, long long ld, int M, int N, int rank, int world,
+                      int rpo, const long long* rank_delta, unsigned* flag, unsigned epoch, unsigned* done,
+                      int sms, cudaStream_t s);
+int num_sms(int device);
 }  // namespace astrai_host
 
 namespace {
@@ -117,7 +121,26 @@ void peer_flags_wait(int64_t flags_addr, int64_t device, int64_t rank, int64_t w
 
 }  // namespace
 
+// Row-parallel all-reduce, second half: sum this rank's rows of the partial products (own partial
+// at part_addr, peers' in the receive slots at recv_addr) and store the result into every rank's
+// output (out_addr + rank_deltas[q]); the last CTA raises flag_addr on every peer.
+static void row_reduce_bcast(int64_t part_addr, int64_t recv_addr, int64_t out_addr, int64_t ld, int64_t M, int64_t N,
+                      int64_t rank, int64_t world, int64_t rpo, const std::vector<int64_t>& rank_deltas,
+                      int64_t flag_addr, int64_t epoch, int64_t done_addr, int64_t device) {
+  TORCH_CHECK((int64_t)rank_deltas.size() == world && world >= 1 && world <= 8, "row_reduce_bcast: one delta per rank");
+  TORCH_CHECK(part_addr % 16 == 0 && recv_addr % 16 == 0 && out_addr % 16 == 0 && N % 8 == 0 && ld % 8 == 0,
+              "row_reduce_bcast: 16-byte aligned rows");
+  std::vector<long long> d(rank_deltas.begin(), rank_deltas.end());
+  c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  astrai_host::row_reduce_bcast(reinterpret_cast<const void*>(part_addr), reinterpret_cast<const void*>(recv_addr),
+                                reinterpret_cast<void*>(out_addr), ld, (int)M, (int)N, (int)rank, (int)world, (int)rpo,
+                                d.data(), reinterpret_cast<unsigned*>(flag_addr), (unsigned)epoch,
+                                reinterpret_cast<unsigned*>(done_addr), astrai_host::num_sms((int)device),
+                                at::cuda::getCurrentCUDAStream().stream());
+}
+
 void register_comm(pybind11::module& m) {
+  m.def("row_reduce_bcast", &row_reduce_bcast);
   m.def("muon_apply_peers", &muon_apply_peers);
   m.def("peer_flags_wait", &peer_flags_wait);
   m.def("symm_alloc", &symm_alloc, "cudaMalloc + IPC handle -> (address, 64-byte handle)");

@@ -23,6 +23,9 @@ struct GatherArgs {
   unsigned* flag;
   unsigned* done;
   unsigned epoch;
+  int scatter_rpo, scatter_rank;
+  long long scatter_recv_off;
+  long long rank_delta[8];
 };
 void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int N, int K, int batch, int a_mn,
                long long lda, long long strideA, int b_mn, long long ldb, long long strideB, long long ldd,
@@ -221,7 +224,9 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& d, const c10::op
 // peer's copy (d + peer_deltas[q] bytes) and the last CTA raises this rank's flag on every peer
 // (flag_addr + peer_deltas[q] <- epoch). The caller waits for the peers' flags.
 void gemm_gather(const at::Tensor& a, const at::Tensor& b, at::Tensor& d, const std::vector<int64_t>& peer_deltas,
-                 int64_t flag_addr, int64_t done_addr, int64_t epoch, int64_t a_mn, int64_t b_mn) {
+                 int64_t flag_addr, int64_t done_addr, int64_t epoch, int64_t a_mn, int64_t b_mn,
+                 int64_t scatter_rpo, int64_t scatter_rank, int64_t scatter_recv_off,
+                 const std::vector<int64_t>& rank_deltas) {
   check_bf16(a, "a");
   check_bf16(b, "b");
   check_bf16(d, "d");
@@ -241,6 +246,15 @@ void gemm_gather(const at::Tensor& a, const at::Tensor& b, at::Tensor& d, const 
   g.flag = reinterpret_cast<unsigned*>(flag_addr);
   g.done = reinterpret_cast<unsigned*>(done_addr);
   g.epoch = (unsigned)epoch;
+  g.scatter_rpo = (int)scatter_rpo;
+  g.scatter_rank = (int)scatter_rank;
+  g.scatter_recv_off = scatter_recv_off;
+  if (scatter_rpo > 0) {
+    TORCH_CHECK(rank_deltas.size() == peer_deltas.size() + 1 && scatter_rank >= 0 &&
+                    scatter_rank < (int64_t)rank_deltas.size() && d.is_contiguous(),
+                "gemm_gather: reduce-scatter push needs one delta per rank and a contiguous partial");
+    for (size_t q = 0; q < rank_deltas.size(); ++q) g.rank_delta[q] = rank_deltas[q];
+  }
   c10::cuda::CUDAGuard guard(a.device());
   astrai_host::gemm_bf16(a.data_ptr(), b.data_ptr(), d.data_ptr(), nullptr, (int)M, (int)N, (int)K, 1, (int)a_mn,
                          a.stride(0), 0, (int)b_mn, b.stride(0), 0, d.stride(0), 0, 0, 0, 0, 1.f, 0.f, 0, stream(),
@@ -480,7 +494,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("force_bn") = 0);
   m.def("gemm_gather", &gemm_gather, "bf16 GEMM whose epilogue also stores into every peer's copy (fused all-gather)",
         py::arg("a"), py::arg("b"), py::arg("d"), py::arg("peer_deltas"), py::arg("flag_addr"), py::arg("done_addr"),
-        py::arg("epoch"), py::arg("a_mn") = 0, py::arg("b_mn") = 0);
+        py::arg("epoch"), py::arg("a_mn") = 0, py::arg("b_mn") = 0, py::arg("scatter_rpo") = 0,
+        py::arg("scatter_rank") = 0, py::arg("scatter_recv_off") = 0,
+        py::arg("rank_deltas") = std::vector<int64_t>{});
   m.def("gemm_plan", [](int64_t M, int64_t N, int64_t K, int64_t batch) {
     int o[5] = {0, 0, 0, 0, 0};
     astrai_host::gemm_plan((int)M, (int)N, (int)K, (int)batch, o);

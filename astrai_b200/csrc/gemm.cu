@@ -95,6 +95,14 @@ struct GemmParams {
   unsigned* gather_flag;
   unsigned* gather_done;  // grid-completion counter, zero between launches
   unsigned gather_epoch;
+  // Fused reduce-scatter push (scatter_rpo > 0, with npeers / peer_delta / gather_* set for the
+  // completion flag): D holds this rank's partial product; rows are owned in blocks of scatter_rpo
+  // (rank o owns [o rpo, (o + 1) rpo)). After a tile is stored, its rows owned by another rank o go
+  // into o's receive slot for this rank, D + scatter_recv_off + (rank rpo + row - o rpo) ldd (+ col)
+  // elements, at rank o's copy (rank_delta[o] bytes away).
+  int scatter_rpo, scatter_rank;
+  long long scatter_recv_off;  // bytes from D to the receive slots
+  long long rank_delta[kMaxGatherPeers + 1];
 };
 
 // Fused all-gather: after the epilogue warps stored tile (b, mb, nb) into the local D, copy it from
@@ -122,6 +130,32 @@ __device__ __forceinline__ void gather_copy_tile(const GemmParams& p, int b, int
         for (int q = 0; q < kMaxGatherPeers; ++q)
           if (q < p.npeers) *reinterpret_cast<__nv_bfloat16*>(dst0 + 2 * e + p.peer_delta[q]) = v;
       }
+    }
+  }
+}
+
+// Fused reduce-scatter push of tile (b, mb, nb): rows owned by other ranks go to their receive slots
+// (row-contiguous 16-byte stores, as in gather_copy_tile).
+template <int BM, int BN>
+__device__ __forceinline__ void scatter_copy_tile(const GemmParams& p, int mb, int nb, int et, int nthreads) {
+  constexpr int VPR = BN / 8;
+  const __nv_bfloat16* D = reinterpret_cast<const __nv_bfloat16*>(p.D);
+  for (int i = et; i < BM * VPR; i += nthreads) {
+    const int row = mb * BM + i / VPR, col = nb * BN + (i % VPR) * 8;
+    if (row >= p.M || col >= p.N) continue;
+    const int o = row / p.scatter_rpo;
+    if (o == p.scatter_rank) continue;
+    long long dl = 0;
+#pragma unroll
+    for (int q = 0; q <= kMaxGatherPeers; ++q)
+      if (q == o) dl = p.rank_delta[q];
+    const __nv_bfloat16* src = D + (long long)row * p.ldd + col;
+    char* dst = reinterpret_cast<char*>(const_cast<__nv_bfloat16*>(D)) + p.scatter_recv_off + dl +
+                ((long long)(p.scatter_rank * p.scatter_rpo + row - o * p.scatter_rpo) * p.ldd + col) * 2;
+    if (col + 8 <= p.N && p.vec_ok) {
+      *reinterpret_cast<uint4*>(dst) = __ldcg(reinterpret_cast<const uint4*>(src));
+    } else {
+      for (int e = 0; e < 8 && col + e < p.N; ++e) reinterpret_cast<__nv_bfloat16*>(dst)[e] = src[e];
     }
   }
 }
@@ -729,7 +763,10 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
         }
         if (p.npeers > 0) {
           named_bar_sync(1, EPI_THREADS);  // the whole tile is in the local D
-          gather_copy_tile<BM, BN>(p, b, mb, nb, et, EPI_THREADS);
+          if (p.scatter_rpo > 0)
+            scatter_copy_tile<BM, BN>(p, mb, nb, et, EPI_THREADS);
+          else
+            gather_copy_tile<BM, BN>(p, b, mb, nb, et, EPI_THREADS);
         }
         if (++acc == NACC) {
           acc = 0;
@@ -817,7 +854,10 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
       }
       if (!OUT_F32 && p.npeers > 0) {
         named_bar_sync(1, EPI_THREADS);  // the whole tile is in the local D
-        gather_copy_tile<BM, BN>(p, b, mb, nb, et, EPI_THREADS);
+        if (p.scatter_rpo > 0)
+          scatter_copy_tile<BM, BN>(p, mb, nb, et, EPI_THREADS);
+        else
+          gather_copy_tile<BM, BN>(p, b, mb, nb, et, EPI_THREADS);
       }
       if (++acc == NACC) {
         acc = 0;
@@ -982,6 +1022,9 @@ struct GatherArgs {
   unsigned* flag;
   unsigned* done;
   unsigned epoch;
+  int scatter_rpo, scatter_rank;  // > 0: reduce-scatter push instead of the all-gather copy
+  long long scatter_recv_off;
+  long long rank_delta[astrai::kMaxGatherPeers + 1];
 };
 
 // The plan gemm_bf16 would use for a plain GEMM on the current device: tile shape and whether the
@@ -1082,6 +1125,9 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
   p.gather_flag = nullptr;
   p.gather_done = nullptr;
   p.gather_epoch = 0;
+  p.scatter_rpo = 0;
+  p.scatter_rank = 0;
+  p.scatter_recv_off = 0;
   const int tiles = batch * p.tiles_m * p.tiles_n;
   int grid = std::min(tiles, sms);
   if (gather != nullptr) {
@@ -1092,6 +1138,10 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
     p.gather_flag = gather->flag;
     p.gather_done = gather->done;
     p.gather_epoch = gather->epoch;
+    p.scatter_rpo = gather->scatter_rpo;
+    p.scatter_rank = gather->scatter_rank;
+    p.scatter_recv_off = gather->scatter_recv_off;
+    for (int q = 0; q <= astrai::kMaxGatherPeers; ++q) p.rank_delta[q] = gather->rank_delta[q];
   } else if (use_streamk(tiles, p.k_blocks, sms) && sk_buffers(dev, stream, sms, &p.sk_ws, &p.sk_flags)) {
     p.dp_tiles = tiles / sms * sms;
     p.sk_units = (long long)(tiles - p.dp_tiles) * p.k_blocks;
@@ -1185,6 +1235,9 @@ void gemm_grouped_bf16(int mode, const void* A, const void* B, void* D, const vo
   p.gather_flag = nullptr;
   p.gather_done = nullptr;
   p.gather_epoch = 0;
+  p.scatter_rpo = 0;
+  p.scatter_rank = 0;
+  p.scatter_recv_off = 0;
   const int tiles = p.batch * p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, sms);
   if (BN == 256)
@@ -1271,6 +1324,9 @@ void gemm_swiglu_bf16(int mode, const void* A, long long lda, const void* B, lon
   p.gather_flag = nullptr;
   p.gather_done = nullptr;
   p.gather_epoch = 0;
+  p.scatter_rpo = 0;
+  p.scatter_rank = 0;
+  p.scatter_recv_off = 0;
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, sms);
   dispatch_majors<128, 256>(0, mode == 1 ? 0 : b_mn, 0, ta, tb, p, grid, stream);
@@ -1344,6 +1400,9 @@ void gemm_rope_bf16(const void* A, long long lda, const void* B, long long ldb, 
   p.gather_flag = nullptr;
   p.gather_done = nullptr;
   p.gather_epoch = 0;
+  p.scatter_rpo = 0;
+  p.scatter_rank = 0;
+  p.scatter_recv_off = 0;
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, sms);
   if (BN == 256)

@@ -17,6 +17,10 @@ reference calls ``dist.all_reduce`` / ``dist.all_gather`` outside autograd.
 domain) replaces "GEMM, then all-gather" by :class:`GatherGemm`: ONE GEMM kernel per rank
 whose epilogue stores every output tile into every rank's copy of the gathered output
 over NVLink peer memory, so the transfer overlaps the remaining tiles' math.
+``RowParallelLinear(..., fused=True)`` replaces "GEMM, then all-reduce" by
+:class:`ReduceGemm`: the GEMM's epilogue pushes the rows other ranks own into their receive
+slots as tiles finish (a reduce-scatter overlapped with the GEMM), then one kernel per rank
+sums its rows and writes them into every rank's output (the all-gather half).
 """
 
 from __future__ import annotations
@@ -128,6 +132,111 @@ class GatherGemm:
             self.buf = None
 
 
+class ReduceGemm:
+    """``y[M, N] = sum over ranks of x_r[M, K_r] @ w_r[N, K_r]^T`` (the row-parallel linear's
+    all-reduce), fused with the GEMM.
+
+    Rows are owned in blocks of ``rpo = ceil(M / world)``. Call ``e`` on every rank:
+
+    1. wait until every peer consumed call ``e-1`` (flag row 2): its receive slots and output
+       are free again;
+    2. the GEMM computes the partial product into ``part``; as each tile finishes, its rows owned
+       by other ranks are pushed into their receive slots over NVLink; the last CTA raises this
+       rank's flag in row 0 of every peer;
+    3. wait for row 0 of every peer (all partials of this rank's rows are here), then
+       ``row_reduce_bcast`` sums this rank's rows in fp32 and writes them into every rank's
+       output; its last CTA raises row 1 on every peer;
+    4. wait for row 1 of every peer, copy the output out, raise row 2.
+    """
+
+    def __init__(self, group=None, wait_s: float = 20.0):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.wait_s = wait_s
+        self.buf: SymmetricBuffer = None
+        self.key = None
+        self.epoch = 0
+
+    def _ensure(self, M: int, N: int, dev: torch.device) -> None:
+        if self.key == (M, N):
+            return
+        if self.buf is not None:
+            torch.cuda.synchronize(dev)
+            dist.barrier(group=self.group)
+            self.buf.close()
+        W = self.world
+        self.rpo = -(-M // W)
+        part = _align(M * N * 2)
+        recv = _align(W * self.rpo * N * 2)
+        out = _align(M * N * 2)
+        self.off_part, self.off_recv, self.off_out = 0, part, part + recv
+        self.off_flag = part + recv + out
+        self.off_done = self.off_flag + _align(4 * 3 * W)
+        self.buf = SymmetricBuffer(self.off_done + 256, self.group, dev)
+        self.buf.local_view(self.off_flag, self.off_done + 256 - self.off_flag).zero_()
+        self.rank_deltas = [self.buf.ptrs[q] - self.buf.ptrs[self.rank] for q in range(W)]
+        self.peer_deltas = [d for q, d in enumerate(self.rank_deltas) if q != self.rank]
+        self.raise_done = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.key, self.epoch = (M, N), 0
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=self.group)
+
+    def __call__(self, x: Tensor, w: Tensor) -> Tensor:
+        from astrai_b200.ops._ext import native
+
+        C = native()
+        M, N = x.shape[0], w.shape[0]
+        dev = x.device
+        self._ensure(M, N, dev)
+        W, r, base = self.world, self.rank, self.buf.local_ptr
+        part = self.buf.local_view(self.off_part, M * N * 2).view(torch.bfloat16).view(M, N)
+        out = self.buf.local_view(self.off_out, M * N * 2).view(torch.bfloat16).view(M, N)
+        flags = base + self.off_flag
+        if self.epoch > 0:
+            C.peer_flags_wait(flags + 8 * W, dev.index, r, W, 1, self.epoch, self.wait_s)
+        self.epoch += 1
+        C.gemm_gather(x, w, part, self.peer_deltas, flags + 4 * r, base + self.off_done, self.epoch,
+                      scatter_rpo=self.rpo, scatter_rank=r, scatter_recv_off=self.off_recv - self.off_part,
+                      rank_deltas=self.rank_deltas)
+        C.peer_flags_wait(flags, dev.index, r, W, 1, self.epoch, self.wait_s)
+        C.row_reduce_bcast(base + self.off_part, base + self.off_recv, base + self.off_out, N, M, N, r, W, self.rpo,
+                           self.rank_deltas, flags + 4 * W + 4 * r, self.epoch, base + self.off_done + 64, dev.index)
+        C.peer_flags_wait(flags + 4 * W, dev.index, r, W, 1, self.epoch, self.wait_s)
+        y = out.clone()
+        C.muon_apply_peers(None, None, self.buf.peer_base, None, 0, 1, 1, False, 1.0, 0.0, r, W, self.off_flag, 2,
+                           self.epoch, self.raise_done)
+        return y
+
+    def close(self) -> None:
+        if self.buf is not None:
+            self.buf.close()
+            self.buf = None
+            self.key = None
+
+
+class _ReduceLinearFn(torch.autograd.Function):
+    """Forward through :class:`ReduceGemm`; the backward of the sum is the identity on every rank."""
+
+    @staticmethod
+    def forward(ctx, x2, w, rg):
+        ctx.save_for_backward(x2, w)
+        return rg(x2, w)
+
+    @staticmethod
+    def backward(ctx, g):
+        from astrai_b200.ops._ext import native
+
+        x2, w = ctx.saved_tensors
+        g = g.contiguous()
+        C = native()
+        dx = torch.empty_like(x2)
+        C.gemm(g, w, dx, None, 0, 1)   # [M, N] @ [N, K_r]
+        dw = torch.empty_like(w)
+        C.gemm(g, x2, dw, None, 1, 1)  # [M, N]^T @ [M, K_r]
+        return dx, dw, None
+
+
 class _GatherLinearFn(torch.autograd.Function):
     """Forward through :class:`GatherGemm`; backward on this rank's column slice of the gradient."""
 
@@ -166,8 +275,10 @@ def _matmul(x: Tensor, w: Tensor) -> Tensor:
 
 class RowParallelLinear(ParallelModel):
     def __init__(self, process_group, in_features: int, out_features: int, bias: bool = True,
-                 reduce_results: bool = True):
+                 reduce_results: bool = True, fused: bool = False):
         super().__init__(process_group)
+        self.fused = fused
+        self._rg = None
         if in_features % self.world_size:
             raise ValueError(f"in_features must be divisible by world_size. Got {in_features} and {self.world_size}")
         self.in_features, self.out_features = in_features, out_features
@@ -177,8 +288,19 @@ class RowParallelLinear(ParallelModel):
         nn.init.normal_(self.weight, std=0.02)
         self.bias = nn.Parameter(torch.zeros(out_features)) if bias else None
 
+    def _fused_ok(self, x: Tensor) -> bool:
+        return (self.fused and self.reduce_results and self.world_size > 1 and x.is_cuda
+                and x.dtype == torch.bfloat16 and self.weight.dtype == torch.bfloat16
+                and self.in_features_per_rank % 8 == 0 and self.out_features % 8 == 0)
+
     def forward(self, input: Tensor) -> Tensor:
         """``input`` holds this rank's slice of the input features."""
+        if self._fused_ok(input):
+            if self._rg is None:
+                self._rg = ReduceGemm(self.process_group)
+            x2 = input.reshape(-1, self.in_features_per_rank).contiguous()
+            out = _ReduceLinearFn.apply(x2, self.weight, self._rg).view(*input.shape[:-1], self.out_features)
+            return out + self.bias if self.bias is not None else out
         out = _matmul(input, self.weight)
         if self.reduce_results and self.world_size > 1:
             out = _AllReduceSum.apply(out, self.process_group)

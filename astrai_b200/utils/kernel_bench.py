@@ -1,7 +1,7 @@
 """Device-timed micro-benchmarks of the framework's kernels.
 
     python -m astrai_b200.utils.kernel_bench [gemm [case]|attn|norm|skinny|sample|all]
-    torchrun --nproc-per-node N -m astrai_b200.utils.kernel_bench allreduce|ep|tpgather
+    torchrun --nproc-per-node N -m astrai_b200.utils.kernel_bench allreduce|ep|tpgather|tprow
 
 Each case is timed with CUDA events on the launching stream after warm-up,
 with a synchronize on both sides; inputs larger than L2 are used where the
@@ -302,6 +302,57 @@ def bench_tpgather(M: int = 8192, K: int = 2048, N: int = 8192):
     dist.destroy_process_group()
 
 
+def bench_tprow(M: int = 8192, K: int = 8192, N: int = 2048):
+    """Row-parallel linear: y[M, N] = sum over ranks of x_r[M, K / world] @ w_r^T. Fused: ReduceGemm
+    (GEMM pushing partial rows to their owners as tiles finish, owners sum and broadcast, flag waits,
+    copy out). Baseline: the same GEMM, then NCCL all_reduce. Device time, max over ranks."""
+    import torch.distributed as dist
+
+    from astrai_b200.ops._ext import native
+    from astrai_b200.parallel.module import ReduceGemm
+
+    rank, world = _dist_init()
+    C = native()
+    _, tf, _ = peaks()
+    k = K // world
+    torch.manual_seed(rank)
+    x = torch.randn(M, k, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(N, k, device="cuda") * 0.05).to(torch.bfloat16)
+    rg = ReduceGemm()
+    loc = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+
+    def gemm_only():
+        C.gemm(x, w, loc, None, 0, 0)
+
+    def nccl():
+        C.gemm(x, w, loc, None, 0, 0)
+        dist.all_reduce(loc)
+        return loc
+
+    y = rg(x, w)
+    ref = nccl().float()
+    err = ((y.float() - ref).norm() / ref.norm()).item()
+    res = {}
+    for name, fn in (("fused_ms", lambda: rg(x, w)), ("gemm_only_ms", gemm_only), ("gemm_nccl_ms", nccl)):
+        dist.barrier()
+        ms = time_fn(fn, warmup=5, iters=20)
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        res[name] = round(t.item(), 4)
+    torch.cuda.synchronize()
+    werr = int(C.read_error())
+    rg.close()
+    dist.barrier()
+    if rank == 0:
+        fl = 2.0 * M * N * k
+        nv_ms = 2 * M * N * 2 * (world - 1) / world / (770.0 * 1e6)
+        print(json.dumps({"kernel": "gemm_allreduce", "world": world, "M": M, "K": K, "N": N, **res,
+                          "speedup_vs_nccl": round(res["gemm_nccl_ms"] / res["fused_ms"], 2),
+                          "roofline_ms": round(max(fl / (tf * 1e9), nv_ms), 4), "rel_err_vs_nccl": round(err, 5),
+                          "device_error_word": werr}))
+    dist.destroy_process_group()
+
+
 def bench_skinny():
     """Decode GEMMs (M token rows x weight [N, K]): device time and weight-read bandwidth."""
     from astrai_b200.ops._ext import native
@@ -376,6 +427,9 @@ def main(argv=None):
         return
     if which == "tpgather":
         bench_tpgather()
+        return
+    if which == "tprow":
+        bench_tprow()
         return
     if which in ("skinny", "all"):
         bench_skinny()

@@ -207,12 +207,70 @@ def _gather_worker(rank, world, port):
         dist.destroy_process_group()
 
 
+def _reduce_worker(rank, world, port):
+    """GEMM fused with the all-reduce (partials pushed to the row owners as tiles finish, owners sum
+    and broadcast) against the local GEMM + an fp32 sum of every rank's bf16 partial; repeated calls
+    and a row count that does not divide evenly; then RowParallelLinear fused vs NCCL, fwd and bwd."""
+    dist = _init(rank, world, port)
+    try:
+        from astrai_b200.ops._ext import native
+        from astrai_b200.parallel.module import ReduceGemm, RowParallelLinear
+
+        native().read_error()
+        C = native()
+        rg = ReduceGemm()
+        for it, (M, K, N) in enumerate([(1000, 256, 520), (1000, 256, 520), (777, 128, 264), (777, 128, 264)]):
+            torch.manual_seed(100 * it + rank)
+            x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+            w = (torch.randn(N, K, device="cuda") * 0.05).to(torch.bfloat16)
+            y = rg(x, w)
+            loc = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+            C.gemm(x, w, loc, None, 0, 0)
+            parts = [torch.empty_like(loc) for _ in range(world)]
+            dist.all_gather(parts, loc)
+            ref = torch.stack([t.float() for t in parts]).sum(0)
+            torch.testing.assert_close(y.float(), ref, atol=1e-2, rtol=1e-2)
+            same = [torch.empty_like(y) for _ in range(world)]
+            dist.all_gather(same, y)
+            assert all(torch.equal(same[0], t) for t in same), "ranks disagree on the reduced output"
+        torch.cuda.synchronize()
+        assert native().read_error() == 0
+        rg.close()
+        torch.manual_seed(9)
+        layers = [RowParallelLinear(None, 1024, 512, bias=True, fused=f).cuda().to(torch.bfloat16) for f in (1, 0)]
+        layers[1].weight.data.copy_(layers[0].weight.data)
+        torch.manual_seed(10 + rank)
+        x0 = torch.randn(3, 200, 1024 // world, device="cuda").to(torch.bfloat16)
+        torch.manual_seed(11)
+        g = torch.randn(3, 200, 512, device="cuda").to(torch.bfloat16)
+        outs = []
+        for layer in layers:
+            x = x0.clone().requires_grad_()
+            y = layer(x)
+            y.backward(g)
+            outs.append((y, x.grad, layer.weight.grad))
+        assert layers[0]._rg is not None and layers[1]._rg is None
+        for a, b in zip(outs[0], outs[1]):
+            torch.testing.assert_close(a.float(), b.float(), atol=3e-2, rtol=2e-2)
+        torch.cuda.synchronize()
+        assert native().read_error() == 0
+        dist.barrier()
+        layers[0]._rg.close()
+    finally:
+        dist.destroy_process_group()
+
+
 def _spawn(fn, world, *args):
     import torch.multiprocessing as mp
 
     from astrai_b200.parallel import find_free_port
 
     mp.start_processes(fn, args=(world, find_free_port()) + args, nprocs=world, start_method="spawn", join=True)
+
+
+@need2
+def test_gemm_fused_allreduce_matches_sum():
+    _spawn(_reduce_worker, min(NGPU, 4))
 
 
 @need2
