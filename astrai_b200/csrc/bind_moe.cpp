@@ -18,6 +18,10 @@ void ep_dispatch(const astrai::EPArena& a, const void* x, long long ldx, const i
                  const int* base_row, int n_slots, int k, int e_local, int* slot_row, unsigned epoch, int ctas,
                  cudaStream_t s);
 void ep_wait(const astrai::EPArena& a, int phase, unsigned epoch, cudaStream_t s);
+void ep_dispatch_fp8(const astrai::EPArena& a, const void* x, long long ldx, const int* idx, const int* pos,
+                     const int* base_row, int n_slots, int k, int e_local, int* slot_row, unsigned epoch, int ctas,
+                     cudaStream_t s);
+void ep_dequant(const astrai::EPArena& a, long long rows, int ctas, cudaStream_t s);
 void ep_return(const astrai::EPArena& a, const void* rows, long long total_rows, const int* group_tile,
                const int* starts, const int* n_rows, int to_ret2, unsigned epoch, int ctas, cudaStream_t s);
 void ep_combine(const void* slots, const float* w, const void* add, void* out, int T, int k, int d, cudaStream_t s);
@@ -40,14 +44,15 @@ void chk(const at::Tensor& t, at::ScalarType st, const char* n) {
   TORCH_CHECK(t.is_cuda() && t.scalar_type() == st && t.is_contiguous(), n, ": wrong dtype / device / layout");
 }
 
-// Arena description passed from Python: peer_base int64 [W], offs [6] (flags, srcmap, xin, dyin, ret, ret2).
+// Arena description passed from Python: peer_base int64 [W], offs [8] (flags, srcmap, xin, dyin, ret, ret2,
+// xin8, xsc; the last two 0 without fp8 dispatch).
 astrai::EPArena arena_of(const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done,
                          int64_t rank, int64_t world, int64_t rows_cap, int64_t slots_cap, int64_t d, double wait_s) {
   chk(peer_base, at::kLong, "peer_base");
   chk(done, at::kInt, "done");
-  TORCH_CHECK(offs.size() == 6 && peer_base.numel() == world && d % 8 == 0, "bad arena description");
-  static thread_local long long o[6];
-  for (int i = 0; i < 6; ++i) o[i] = offs[i];
+  TORCH_CHECK(offs.size() == 8 && peer_base.numel() == world && d % 8 == 0, "bad arena description");
+  static thread_local long long o[8];
+  for (int i = 0; i < 8; ++i) o[i] = offs[i];
   return astrai_host::make_arena(reinterpret_cast<const long long*>(peer_base.data_ptr<int64_t>()),
                                  static_cast<int>(rank), static_cast<int>(world), o, rows_cap, slots_cap,
                                  static_cast<int>(d), reinterpret_cast<unsigned*>(done.data_ptr<int>()),
@@ -77,10 +82,10 @@ void moe_router(const at::Tensor& logits, int64_t k, at::Tensor& probs, at::Tens
 
 int ctas_for(const at::Tensor& t) { return astrai_host::num_sms(t.device().index()); }
 
-void ep_dispatch(const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done, int64_t rank,
-                 int64_t world, int64_t rows_cap, int64_t slots_cap, int64_t d, double wait_s, const at::Tensor& x,
-                 const at::Tensor& idx, const at::Tensor& pos, const at::Tensor& base_row, int64_t e_local,
-                 at::Tensor& slot_row, int64_t epoch) {
+void ep_dispatch_any(bool fp8, const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done,
+                     int64_t rank, int64_t world, int64_t rows_cap, int64_t slots_cap, int64_t d, double wait_s,
+                     const at::Tensor& x, const at::Tensor& idx, const at::Tensor& pos, const at::Tensor& base_row,
+                     int64_t e_local, at::Tensor& slot_row, int64_t epoch) {
   auto a = arena_of(peer_base, offs, done, rank, world, rows_cap, slots_cap, d, wait_s);
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1 && x.size(1) == d &&
                   (x.stride(0) * 2) % 16 == 0,
@@ -93,9 +98,34 @@ void ep_dispatch(const at::Tensor& peer_base, const std::vector<int64_t>& offs, 
   TORCH_CHECK(n_slots <= slots_cap && pos.numel() == n_slots && slot_row.numel() == n_slots, "slot counts");
   const int k = static_cast<int>(n_slots / x.size(0));
   const c10::cuda::CUDAGuard g(x.device());
-  astrai_host::ep_dispatch(a, x.data_ptr(), x.stride(0), idx.data_ptr<int>(), pos.data_ptr<int>(),
+  (fp8 ? astrai_host::ep_dispatch_fp8 : astrai_host::ep_dispatch)(a, x.data_ptr(), x.stride(0), idx.data_ptr<int>(), pos.data_ptr<int>(),
                            base_row.data_ptr<int>(), static_cast<int>(n_slots), k, static_cast<int>(e_local),
                            slot_row.data_ptr<int>(), static_cast<unsigned>(epoch), ctas_for(x), cur());
+}
+
+void ep_dispatch(const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done, int64_t rank,
+                 int64_t world, int64_t rows_cap, int64_t slots_cap, int64_t d, double wait_s, const at::Tensor& x,
+                 const at::Tensor& idx, const at::Tensor& pos, const at::Tensor& base_row, int64_t e_local,
+                 at::Tensor& slot_row, int64_t epoch) {
+  ep_dispatch_any(false, peer_base, offs, done, rank, world, rows_cap, slots_cap, d, wait_s, x, idx, pos, base_row,
+                  e_local, slot_row, epoch);
+}
+
+// Token rows as fp8 e4m3 with one fp32 scale per 128 columns (the arena's fp8 block).
+void ep_dispatch_fp8(const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done,
+                     int64_t rank, int64_t world, int64_t rows_cap, int64_t slots_cap, int64_t d, double wait_s,
+                     const at::Tensor& x, const at::Tensor& idx, const at::Tensor& pos, const at::Tensor& base_row,
+                     int64_t e_local, at::Tensor& slot_row, int64_t epoch) {
+  ep_dispatch_any(true, peer_base, offs, done, rank, world, rows_cap, slots_cap, d, wait_s, x, idx, pos, base_row,
+                  e_local, slot_row, epoch);
+}
+
+// bf16 expert-input rows [0, rows) of this rank's arena from its fp8 block.
+void ep_dequant(const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done, int64_t rank,
+                int64_t world, int64_t rows_cap, int64_t slots_cap, int64_t d, double wait_s, int64_t rows) {
+  auto a = arena_of(peer_base, offs, done, rank, world, rows_cap, slots_cap, d, wait_s);
+  const c10::cuda::CUDAGuard g(peer_base.device());
+  astrai_host::ep_dequant(a, rows, ctas_for(peer_base), cur());
 }
 
 void ep_wait(const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done, int64_t rank,
@@ -250,6 +280,8 @@ at::Tensor symm_view(int64_t ptr, int64_t nbytes, int64_t device) {
 void register_moe(pybind11::module& m) {
   m.def("moe_router", &moe_router);
   m.def("ep_dispatch", &ep_dispatch);
+  m.def("ep_dispatch_fp8", &ep_dispatch_fp8);
+  m.def("ep_dequant", &ep_dequant);
   m.def("ep_wait", &ep_wait);
   m.def("ep_return", &ep_return);
   m.def("ep_combine", &ep_combine, pybind11::arg("slots"), pybind11::arg("w"), pybind11::arg("add"),

@@ -13,6 +13,8 @@ struct EPArena {
   long long off_dyin;    // [rows_cap, d] expert output-gradient block
   long long off_ret;     // [slots_cap, d] returned expert outputs (forward)
   long long off_ret2;    // [slots_cap, d] returned input gradients (backward)
+  long long off_xin8;    // [rows_cap, d] fp8 e4m3 expert input (fp8 dispatch; 0 when unused)
+  long long off_xsc;     // [rows_cap, d / 128] fp32 block scales of off_xin8
   long long rows_cap, slots_cap;
   int d;
   unsigned* done;        // local grid-completion counter

@@ -29,6 +29,8 @@
 #include <stdexcept>
 #include <string>
 
+#include <cuda_fp8.h>
+
 #include "common.cuh"
 #include "ep_arena.h"
 
@@ -186,6 +188,101 @@ __global__ void __launch_bounds__(512) ep_dispatch_kernel(EPArena a, const __nv_
              lane);
   }
   grid_done_signal(a, 0, epoch);
+}
+
+// fp8 dispatch (opt-in; the reference only moves bf16): the token row is quantised to e4m3 with one
+// fp32 scale per 128 columns (scale = amax / 448, the largest finite e4m3) and stored into the
+// owner's fp8 block (d bytes) and scale block (d / 128 floats) instead of the bf16 block (2 d
+// bytes): half the NVLink bytes. The owner rebuilds the bf16 block with ep_dequant_kernel.
+// A warp covers 256 columns per step: 16 lanes x 8 columns form one 128-column scale block.
+__global__ void __launch_bounds__(512) ep_dispatch_fp8_kernel(EPArena a, const __nv_bfloat16* __restrict__ x,
+                                                              long long ldx, const int* __restrict__ idx,
+                                                              const int* __restrict__ pos,
+                                                              const int* __restrict__ base_row, int n_slots, int k,
+                                                              int e_local, int* __restrict__ slot_row,
+                                                              unsigned epoch) {
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  for (int s = gw; s < n_slots; s += nw) {
+    const int e = idx[s];
+    const int r = e / e_local;
+    const long long row = (long long)base_row[e] + pos[s];
+    if (r < 0 || r >= a.world || row < 0 || row >= a.rows_cap) {
+      if (lane == 0) set_error(a.err, kErrBadArg);
+      continue;
+    }
+    if (lane == 0) {
+      slot_row[s] = static_cast<int>(row);
+      reinterpret_cast<long long*>(arena(a, r, a.off_srcmap))[row] =
+          (static_cast<long long>(a.rank) << 32) | static_cast<unsigned>(s);
+    }
+    const __nv_bfloat16* src = x + (long long)(s / k) * ldx;
+    unsigned char* q8 = reinterpret_cast<unsigned char*>(arena(a, r, a.off_xin8)) + row * a.d;
+    float* sc = reinterpret_cast<float*>(arena(a, r, a.off_xsc)) + row * (a.d / 128);
+    for (int c0 = 0; c0 < a.d; c0 += 256) {
+      const int col = c0 + lane * 8;
+      float v[8];
+      float amax = 0.f;
+      if (col < a.d) {
+        const uint4 u = *reinterpret_cast<const uint4*>(src + col);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = unpack_bf16(w[j]);
+          v[2 * j] = f.x;
+          v[2 * j + 1] = f.y;
+          amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = 0.f;
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffff, amax, o));  // 16-lane block
+      const float scale = amax > 0.f ? amax / 448.f : 1.f;
+      const float inv = 1.f / scale;
+      if (col < a.d) {
+        uint32_t pk[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(v[4 * j] * inv, v[4 * j + 1] * inv),
+                                                                   __NV_SATFINITE, __NV_E4M3);
+          const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(
+              make_float2(v[4 * j + 2] * inv, v[4 * j + 3] * inv), __NV_SATFINITE, __NV_E4M3);
+          pk[j] = (uint32_t)lo | ((uint32_t)hi << 16);
+        }
+        *reinterpret_cast<uint2*>(q8 + col) = make_uint2(pk[0], pk[1]);
+        if ((lane & 15) == 0) sc[col / 128] = scale;
+      }
+    }
+  }
+  grid_done_signal(a, 0, epoch);
+}
+
+// bf16 expert-input rows [0, rows) <- fp8 rows x their 128-column scales (own arena).
+__global__ void __launch_bounds__(256) ep_dequant_kernel(EPArena a, long long rows) {
+  const int vpr = a.d / 8;
+  const long long n = rows * vpr;
+  const unsigned char* q8 = reinterpret_cast<const unsigned char*>(arena(a, a.rank, a.off_xin8));
+  const float* sc = reinterpret_cast<const float*>(arena(a, a.rank, a.off_xsc));
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(arena(a, a.rank, a.off_xin));
+  for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < n; v += (long long)gridDim.x * blockDim.x) {
+    const long long row = v / vpr;
+    const int col = (int)(v % vpr) * 8;
+    const uint2 u = *reinterpret_cast<const uint2*>(q8 + row * a.d + col);
+    const float s = sc[row * (a.d / 128) + col / 128];
+    const uint32_t w[2] = {u.x, u.y};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float2 lo = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[j] & 0xffffu), __NV_E4M3)));
+      const float2 hi = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[j] >> 16), __NV_E4M3)));
+      o[2 * j] = pack_bf16(lo.x * s, lo.y * s);
+      o[2 * j + 1] = pack_bf16(hi.x * s, hi.y * s);
+    }
+    *reinterpret_cast<uint4*>(out + row * a.d + col) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
 }
 
 // Bounded wait until flag [phase][q] >= epoch for every rank q.
@@ -348,6 +445,8 @@ EPArena make_arena(const long long* peer_base, int rank, int world, const long l
   a.off_dyin = offs[3];
   a.off_ret = offs[4];
   a.off_ret2 = offs[5];
+  a.off_xin8 = offs[6];
+  a.off_xsc = offs[7];
   a.rows_cap = rows_cap;
   a.slots_cap = slots_cap;
   a.d = d;
@@ -361,6 +460,22 @@ void ep_dispatch(const EPArena& a, const void* x, long long ldx, const int* idx,
                  int n_slots, int k, int e_local, int* slot_row, unsigned epoch, int ctas, cudaStream_t s) {
   (astrai::note_launch(), ep_dispatch_kernel<<<ctas, 512, 0, s>>>(a, static_cast<const __nv_bfloat16*>(x), ldx, idx, pos, base_row, n_slots, k,
                                           e_local, slot_row, epoch));
+}
+
+void ep_dispatch_fp8(const EPArena& a, const void* x, long long ldx, const int* idx, const int* pos,
+                     const int* base_row, int n_slots, int k, int e_local, int* slot_row, unsigned epoch, int ctas,
+                     cudaStream_t s) {
+  if (a.off_xin8 == 0 || a.off_xsc == 0 || a.d % 128 != 0)
+    throw std::runtime_error("ep_dispatch_fp8: the arena has no fp8 block, or d is not a multiple of 128");
+  (astrai::note_launch(), ep_dispatch_fp8_kernel<<<ctas, 512, 0, s>>>(a, static_cast<const __nv_bfloat16*>(x), ldx, idx,
+                                                                        pos, base_row, n_slots, k, e_local, slot_row,
+                                                                        epoch));
+}
+
+void ep_dequant(const EPArena& a, long long rows, int ctas, cudaStream_t s) {
+  if (rows <= 0) return;
+  if (a.off_xin8 == 0 || rows > a.rows_cap) throw std::runtime_error("ep_dequant: no fp8 block or too many rows");
+  (astrai::note_launch(), ep_dequant_kernel<<<ctas * 4, 256, 0, s>>>(a, rows));
 }
 
 void ep_wait(const EPArena& a, int phase, unsigned epoch, cudaStream_t s) {

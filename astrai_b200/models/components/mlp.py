@@ -24,6 +24,8 @@ stay ``routed_experts.{j}...`` (a sharded layer holds its own experts only).
 
 from __future__ import annotations
 
+import os
+
 from typing import Optional
 
 import torch
@@ -83,6 +85,9 @@ class DeepSeekMoE(nn.Module):
         self.shared_experts = nn.ModuleList([MLP(dim, ffn, down_std) for _ in range(self.n_shared_experts)])
         self.routed_experts = nn.ModuleDict({str(j): MLP(dim, ffn, down_std) for j in range(n_routed_experts)})
         self.capacity_factor = 2.0  # EP arena rows per expert, relative to the mean load
+        # expert-parallel dispatch payload as fp8 e4m3 with 1x128 block scales (opt-in, halves the
+        # dispatch bytes over NVLink; the reference moves no tokens between ranks at all)
+        self.fp8_dispatch = os.environ.get("ASTRAI_EP_FP8", "0") == "1"
         self._ep = None
         self._arena = None
         self._stack = None
@@ -140,7 +145,8 @@ class DeepSeekMoE(nn.Module):
         if self._arena is None or self._arena.slots_cap < T * k:
             if self._arena is not None:
                 self._arena.close()
-            self._arena = EPArena(ep, d, T, k, self.n_routed_experts, self.capacity_factor, xf.device)
+            self._arena = EPArena(ep, d, T, k, self.n_routed_experts, self.capacity_factor, xf.device,
+                                  fp8=self.fp8_dispatch)
         counts_all = ep.all_gather_counts(counts).cpu()
         layout = EPLayout(counts_all.numpy(), ep.rank, self.n_routed_experts // ep.world, xf.device)
         if layout.max_rows > self._arena.rows_cap:
@@ -148,7 +154,7 @@ class DeepSeekMoE(nn.Module):
             # (the previous use of this layer's arena finished with its backward)
             self._arena.close()
             self._arena = EPArena(ep, d, T, k, self.n_routed_experts, self.capacity_factor, xf.device,
-                                  min_rows=layout.max_rows * 5 // 4)
+                                  min_rows=layout.max_rows * 5 // 4, fp8=self.fp8_dispatch)
         self._arena.check(layout)
         self._stack = stack_expert_params(self.routed_experts.values())
         add = self._shared(xf)

@@ -114,8 +114,11 @@ class _ExpertsFn(torch.autograd.Function):
         dev = x.device
         slot_row = torch.empty(T * k, device=dev, dtype=torch.int32)
         ep = arena.next_epoch(PH_DISPATCH)
-        C.ep_dispatch(*arena.args(), x, idx.view(-1), pos, layout.base_row, El, slot_row, ep)
+        dispatch = C.ep_dispatch_fp8 if arena.fp8 else C.ep_dispatch
+        dispatch(*arena.args(), x, idx.view(-1), pos, layout.base_row, El, slot_row, ep)
         C.ep_wait(*arena.args(), PH_DISPATCH, ep)
+        if arena.fp8:
+            C.ep_dequant(*arena.args(), R)
         h = torch.empty((R, 2 * F), device=dev, dtype=torch.bfloat16)
         a = torch.empty((R, F), device=dev, dtype=torch.bfloat16)
         y = torch.empty((R, d), device=dev, dtype=torch.bfloat16)

@@ -101,7 +101,7 @@ class EPArena:
     """Symmetric buffer of one MoE layer (see module docstring)."""
 
     def __init__(self, ep: EPGroup, d: int, tokens: int, top_k: int, n_experts: int, capacity_factor: float = 2.0,
-                 device=None, wait_s: float = 20.0, min_rows: int = 0):
+                 device=None, wait_s: float = 20.0, min_rows: int = 0, fp8: bool = False):
         self.ep, self.d = ep, d
         self.e_local = n_experts // ep.world
         self.slots_cap = tokens * top_k
@@ -116,7 +116,14 @@ class EPArena:
         o_ret = o_dyin + _align(self.rows_cap * d * 2)
         o_ret2 = o_ret + _align(self.slots_cap * d * 2)
         total = o_ret2 + _align(self.slots_cap * d * 2)
-        self.offs = [o_flags, o_src, o_xin, o_dyin, o_ret, o_ret2]
+        # fp8 dispatch (opt-in): e4m3 rows and one fp32 scale per 128 columns, dequantised into xin
+        self.fp8 = bool(fp8) and d % 128 == 0
+        o_xin8 = o_xsc = 0
+        if self.fp8:
+            o_xin8 = total
+            o_xsc = o_xin8 + _align(self.rows_cap * d)
+            total = o_xsc + _align(self.rows_cap * (d // 128) * 4)
+        self.offs = [o_flags, o_src, o_xin, o_dyin, o_ret, o_ret2, o_xin8, o_xsc]
         self.buf = SymmetricBuffer(total, ep.group, device, local_only=ep.world == 1)
         self.device = self.buf.device
         self.done = torch.zeros(1, dtype=torch.int32, device=self.device)

@@ -179,6 +179,7 @@ def bench_ep(tokens: int = 8192, d: int = 2048, n_experts: int = 64, k: int = 6)
     w, _, idx, counts, pos = moe_route(logits, k)
     layout = EPLayout(ep.all_gather_counts(counts).cpu().numpy(), rank, n_experts // W, dev)
     arena = EPArena(ep, d, tokens, k, n_experts, 2.0, dev, min_rows=layout.max_rows)
+    arena8 = EPArena(ep, d, tokens, k, n_experts, 2.0, dev, min_rows=layout.max_rows, fp8=True)
     El, R = layout.e_local, layout.total
     slot_row = torch.empty(tokens * k, device=dev, dtype=torch.int32)
     y = torch.randn(max(R, 1), d, device=dev, generator=g).to(torch.bfloat16)
@@ -188,6 +189,12 @@ def bench_ep(tokens: int = 8192, d: int = 2048, n_experts: int = 64, k: int = 6)
         e = arena.next_epoch(PH_DISPATCH)
         C.ep_dispatch(*arena.args(), x, idx.view(-1), pos, layout.base_row, El, slot_row, e)
         C.ep_wait(*arena.args(), PH_DISPATCH, e)
+
+    def dispatch_fp8():  # e4m3 rows + 1x128 scales over NVLink, dequantised by the owner
+        e = arena8.next_epoch(PH_DISPATCH)
+        C.ep_dispatch_fp8(*arena8.args(), x, idx.view(-1), pos, layout.base_row, El, slot_row, e)
+        C.ep_wait(*arena8.args(), PH_DISPATCH, e)
+        C.ep_dequant(*arena8.args(), R)
 
     def combine():
         e = arena.next_epoch(PH_RETURN)
@@ -220,7 +227,7 @@ def bench_ep(tokens: int = 8192, d: int = 2048, n_experts: int = 64, k: int = 6)
         dist.all_reduce(v, op=dist.ReduceOp.MAX)
         return float(v) * 1e3  # us
 
-    res = {"dispatch_us": t_max(dispatch), "combine_us": t_max(combine),
+    res = {"dispatch_us": t_max(dispatch), "dispatch_fp8_us": t_max(dispatch_fp8), "combine_us": t_max(combine),
            "dispatch_combine_us": t_max(lambda: (dispatch(), combine())),
            "nccl_dispatch_us": t_max(nccl_dispatch), "nccl_combine_us": t_max(nccl_combine),
            "nccl_dispatch_combine_us": t_max(lambda: (nccl_dispatch(), nccl_combine()))}
@@ -232,6 +239,7 @@ def bench_ep(tokens: int = 8192, d: int = 2048, n_experts: int = 64, k: int = 6)
     dist.all_reduce(remote, op=dist.ReduceOp.MAX)
     nbytes = float(remote) * d * 2
     arena.close()
+    arena8.close()
     if rank == 0:
         link = 770.0  # GB/s per direction, measured peer copy on this pool
         floor_us = nbytes / (link * 1e3)

@@ -97,7 +97,9 @@ def test_fused_moe_model_matches_fp32_reference():
     assert not torch.equal(m.layers[1].mlp.routed_experts["3"].up.weight.grad, g0)
 
 
-def _ep_worker(rank, world, port):
+def _ep_worker(rank, world, port, fp8=False):
+    """fp8: token rows cross NVLink as e4m3 with 1x128 block scales, so the forward carries a
+    quantisation error of a few per cent (relative norm) against the bf16 replicated layer."""
     import torch.distributed as dist
 
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -115,6 +117,7 @@ def _ep_worker(rank, world, port):
         ep = DeepSeekMoE(256, 512, n_routed_experts=16, n_shared_experts=1, n_activated_experts=4,
                          moe_intermediate_size=256).cuda().to(torch.bfloat16)
         ep.load_state_dict(full.state_dict())
+        ep.fp8_dispatch = fp8
         ep.shard_experts()
         assert len(ep.routed_experts) == 16 // world
         for step in range(3):
@@ -122,11 +125,18 @@ def _ep_worker(rank, world, port):
             x = torch.randn(300, 256, device="cuda", generator=g).to(torch.bfloat16)
             x1, x2 = x.clone().requires_grad_(), x.clone().requires_grad_()
             y_full, y_ep = full(x1), ep(x2)
-            torch.testing.assert_close(y_ep.float(), y_full.float(), atol=2e-2, rtol=2e-2)
+            assert ep._arena.fp8 == fp8
+            if fp8:
+                assert ((y_ep.float() - y_full.float()).norm() / y_full.float().norm()).item() < 5e-2
+            else:
+                torch.testing.assert_close(y_ep.float(), y_full.float(), atol=2e-2, rtol=2e-2)
             gy = torch.randn(y_full.shape, device="cuda", generator=g).to(torch.bfloat16)
             y_full.backward(gy)
             y_ep.backward(gy)
-            torch.testing.assert_close(x2.grad.float(), x1.grad.float(), atol=2e-2, rtol=2e-2)
+            if fp8:
+                assert ((x2.grad.float() - x1.grad.float()).norm() / x1.grad.float().norm()).item() < 5e-2
+            else:
+                torch.testing.assert_close(x2.grad.float(), x1.grad.float(), atol=2e-2, rtol=2e-2)
         # expert weight grads: EP holds the sum over every rank's tokens (reduce every
         # expert in the same order on all ranks, then compare this rank's experts)
         for key in sorted(full.routed_experts, key=int):
@@ -135,7 +145,7 @@ def _ep_worker(rank, world, port):
                 dist.all_reduce(ref_g)
                 if key in ep.routed_experts:
                     got = getattr(ep.routed_experts[key], name).weight.grad.float()
-                    assert ((got - ref_g).norm() / ref_g.norm()).item() < 3e-2, (key, name)
+                    assert ((got - ref_g).norm() / ref_g.norm()).item() < (8e-2 if fp8 else 3e-2), (key, name)
         torch.cuda.synchronize()
         assert native().read_error() == 0
     finally:
@@ -143,13 +153,50 @@ def _ep_worker(rank, world, port):
 
 
 @pytest.mark.skipif(NGPU < 2, reason="needs 2 GPUs")
-def test_expert_parallel_matches_replicated():
+@pytest.mark.parametrize("fp8", [False, True])
+def test_expert_parallel_matches_replicated(fp8):
     import torch.multiprocessing as mp
 
     from astrai_b200.parallel import find_free_port
 
     world = 4 if NGPU >= 4 else 2
-    mp.start_processes(_ep_worker, args=(world, find_free_port()), nprocs=world, start_method="spawn", join=True)
+    mp.start_processes(_ep_worker, args=(world, find_free_port(), fp8), nprocs=world, start_method="spawn", join=True)
+
+
+def test_fp8_dispatch_roundtrip_single_rank():
+    """fp8 dispatch inside a one-rank EP group: every dispatched row equals the bf16 token row up to
+    e4m3 rounding (<= 2^-4 relative to its 128-column block's amax, plus bf16 rounding)."""
+    from astrai_b200.ops._ext import native
+    from astrai_b200.parallel.ep import EPArena, EPGroup, EPLayout
+
+    C = native()
+    C.read_error()
+    T, d, k, E = 200, 256, 2, 8
+    torch.manual_seed(0)
+    x = (torch.randn(T, d, device="cuda") * torch.logspace(-2, 2, d, device="cuda")).to(torch.bfloat16)
+    idx = torch.randint(0, E, (T, k), device="cuda", dtype=torch.int32)
+    counts = torch.bincount(idx.view(-1).long(), minlength=E)
+    pos = torch.empty(T * k, device="cuda", dtype=torch.int32)
+    seen = [0] * E
+    for s, e in enumerate(idx.view(-1).tolist()):
+        pos[s] = seen[e]
+        seen[e] += 1
+    ep = EPGroup.local()
+    layout = EPLayout(counts.view(1, -1).cpu().numpy(), 0, E, "cuda")
+    arena = EPArena(ep, d, T, k, E, 2.0, torch.device("cuda"), min_rows=layout.max_rows, fp8=True)
+    assert arena.fp8
+    slot_row = torch.empty(T * k, device="cuda", dtype=torch.int32)
+    e1 = arena.next_epoch(0)
+    C.ep_dispatch_fp8(*arena.args(), x, idx.view(-1), pos, layout.base_row, E, slot_row, e1)
+    C.ep_wait(*arena.args(), 0, e1)
+    C.ep_dequant(*arena.args(), layout.total)
+    torch.cuda.synchronize()
+    got = arena.block("xin", layout.total)[slot_row.long()].float()
+    ref = x.float().repeat_interleave(k, dim=0)
+    amax = ref.abs().view(T * k, d // 128, 128).amax(-1, keepdim=True).expand(-1, -1, 128).reshape(T * k, d)
+    assert ((got - ref).abs() <= amax * 2.0 ** -4 + ref.abs() * 2.0 ** -7 + 1e-6).all()
+    assert C.read_error() == 0
+    arena.close()
 
 
 @pytest.mark.parametrize("mode", [0, 1])
