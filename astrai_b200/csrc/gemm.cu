@@ -884,6 +884,322 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
   }
 }
 
+
+// ---------------------------------------------------------------------------------------------
+// CTA-pair GEMM (plain and batched modes): a cluster of two CTAs on two SMs computes one 256 x 256
+// output tile with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16 per instruction), issued by
+// one thread of the even CTA. Each CTA stages its own 128 rows of A and 128 of the tile's 256 B
+// rows (N), so the smem bytes per FLOP of each SM equal those of the single-CTA 256 x 256 tile,
+// but each CTA's accumulator (its 128 rows x 256 columns) takes only 256 TMEM columns: two fit,
+// and the epilogue of tile t overlaps the MMAs of tile t+1 (the single-CTA 256 x 256 tile fills
+// TMEM, so its MMAs stall while the epilogue drains). Each CTA's stage is 32 KB: a 6-deep ring.
+// A 256 x 128 variant (each CTA stages 64 B rows; 24 KB stages, 8 deep) halves the tile for
+// shapes whose 256 x 256 tiles leave much of the last wave of pairs idle.
+//
+//   warp 0     TMA producer (both CTAs): loads into its own smem, completion counted on the
+//              even CTA's `full` barrier (cta_group::2 form of the tiled load, no multicast)
+//   warp 1     TMEM allocation for the pair (both CTAs); MMA issuer (even CTA only): commits
+//              release the stage in both CTAs and publish an accumulator to both epilogues
+//              (tcgen05.commit ... multicast::cluster, mask 0b11)
+//   warps 2-9  epilogue: two warps per TMEM lane quadrant, BN / 2 columns each; they drain this
+//              CTA's accumulator and arrive on the even CTA's acc_empty barrier
+// All waits are time-bounded (common.cuh); both CTAs meet at a cluster barrier before the TMEM
+// is freed, so neither leaves while the other can still signal its barriers.
+template <int BN_>
+struct PairCfg {
+  static constexpr int BN = BN_;                 // output columns of a pair tile (256 or 128)
+  static constexpr int BK = 64;
+  static constexpr int A_BYTES = 128 * BK * 2;   // this CTA's 128 rows of A
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;  // this CTA's BN / 2 of the tile's B rows
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;  // 6 (BN 256) or 8 (BN 128)
+  static constexpr int EPI_WARPS = 8;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int TMEM_COLS = 2 * BN;       // two accumulators
+  static_assert(BN == 256 || BN == 128, "pair tiles are 256 x 256 or 256 x 128");
+};
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// shared::cluster address of the same smem offset in CTA `rank` of this cluster
+__device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// tiled 3-D load into this CTA's smem whose completion is counted on `bar_cluster`, a barrier of
+// either CTA of the pair
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* m, uint32_t bar_cluster, int c0,
+                                                 int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// arrive on `bar` (same smem offset) in both CTAs once this thread's MMAs are done
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+template <int BN, int A_MN, int B_MN, int OUT_F32>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+  using Cfg = PairCfg<BN>;
+  constexpr int BK = Cfg::BK, A_BYTES = Cfg::A_BYTES, B_BYTES = Cfg::B_BYTES, STAGE_BYTES = Cfg::STAGE_BYTES;
+  constexpr int STAGES = Cfg::STAGES, EPI_WARPS = Cfg::EPI_WARPS, TMEM_COLS = Cfg::TMEM_COLS;
+  constexpr int BNH = BN / 2;  // B rows per CTA; output columns per epilogue warp
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const uint32_t rank = cluster_ctarank();  // 0: MMA issuer of the pair
+  const int pair_id = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 2 * EPI_WARPS);
+    }
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before either signals the other's
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_tiles = p.batch * p.tiles_m * p.tiles_n;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- producer (both CTAs)
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair_id; ok && tile < num_tiles; tile += npairs) {
+        int b, mb, nb;
+        tile_coords(tile, p.tiles_m, p.tiles_n, b, mb, nb);
+        const int m0 = mb * 256 + (int)rank * 128, n0 = nb * BN + (int)rank * BNH;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_expect_tx(&full[stage], 2 * STAGE_BYTES);
+          const uint32_t bar = mapa_shared(&full[stage], 0);
+          uint8_t* a_dst = sA + stage * A_BYTES;
+          uint8_t* b_dst = sB + stage * B_BYTES;
+          const int k0 = kb * BK;
+          if (A_MN) {
+            tma_load_3d_pair(a_dst, &tmA, bar, m0, k0, b);
+            tma_load_3d_pair(a_dst + 8192, &tmA, bar, m0 + 64, k0, b);
+          } else {
+            tma_load_3d_pair(a_dst, &tmA, bar, k0, m0, b);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int c = 0; c < BNH / 64; ++c) tma_load_3d_pair(b_dst + c * 8192, &tmB, bar, n0 + c * 64, k0, b);
+          } else {
+            tma_load_3d_pair(b_dst, &tmB, bar, k0, n0, b);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---------------------------------------------------------- MMA issuer (even CTA)
+      constexpr uint32_t idesc = idesc_bf16(256, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = pair_id; ok && tile < num_tiles; tile += npairs) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err, kErrWaitAccEmpty)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? sdesc_sw128(a_base + k * 2048, 8192, 1024) : sdesc_sw128(a_base + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc_sw128(b_base + k * 2048, 8192, 1024) : sdesc_sw128(b_base + k * 32, 16, 1024);
+            umma_bf16_pair(d_tmem, ad, bd, idesc, (kb != 0) || k != 0);
+          }
+          umma_commit_pair(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&acc_full[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;              // TMEM lane quadrant this warp may access
+    const int cpart = (warp - 2) >> 2;   // column half: [cpart * BNH, (cpart + 1) * BNH)
+    const uint32_t empty_bar0 = mapa_shared(&acc_empty[0], 0);
+    const uint32_t empty_bar1 = mapa_shared(&acc_empty[1], 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    using OutT = typename std::conditional<OUT_F32, float, __nv_bfloat16>::type;
+    const bool use_c = p.C != nullptr && p.beta != 0.f;
+    for (int tile = pair_id; tile < num_tiles; tile += npairs) {
+      int b, mb, nb;
+      tile_coords(tile, p.tiles_m, p.tiles_n, b, mb, nb);
+      if (!mbar_wait(&acc_full[acc], acc_phase, p.err, kErrWaitAccFull)) break;
+      tc_fence_after();
+      const int row = mb * 256 + (int)rank * 128 + q * 32 + lane;
+      const int n0 = nb * BN + cpart * BNH;
+      const bool row_ok = row < p.M;
+      OutT* drow = reinterpret_cast<OutT*>(p.D) + (long long)b * p.strideD + (long long)row * p.ldd;
+      const OutT* crow =
+          use_c ? reinterpret_cast<const OutT*>(p.C) + (long long)b * p.strideC + (long long)row * p.ldc : nullptr;
+      const uint32_t t_acc = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + cpart * BNH;
+#pragma unroll 1
+      for (int c = 0; c < BNH; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(t_acc + c, r);
+        tmem_wait_ld();
+        if (c + 32 >= BNH) {
+          // last chunk read: hand the accumulator back before the global stores
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(acc ? empty_bar1 : empty_bar0);
+        }
+        const int col = n0 + c;
+        if (!row_ok || col >= p.N) continue;
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
+        if (col + 32 <= p.N && p.vec_ok) {
+          if (crow) {
+            if (OUT_F32) {
+              const float4* src = reinterpret_cast<const float4*>(crow + col);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float4 t = src[i];
+                v[4 * i] += p.beta * t.x;
+                v[4 * i + 1] += p.beta * t.y;
+                v[4 * i + 2] += p.beta * t.z;
+                v[4 * i + 3] += p.beta * t.w;
+              }
+            } else {
+              const uint4* src = reinterpret_cast<const uint4*>(crow + col);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const uint4 t = src[i];
+                const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const float2 f = unpack_bf16(w[j]);
+                  v[8 * i + 2 * j] += p.beta * f.x;
+                  v[8 * i + 2 * j + 1] += p.beta * f.y;
+                }
+              }
+            }
+          }
+          if (OUT_F32) {
+            float4* dst = reinterpret_cast<float4*>(drow + col);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          } else {
+            uint4* dst = reinterpret_cast<uint4*>(drow + col);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              dst[i] = make_uint4(pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
+                                  pack_bf16(v[8 * i + 4], v[8 * i + 5]), pack_bf16(v[8 * i + 6], v[8 * i + 7]));
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (col + i < p.N) {
+              float x = v[i];
+              if (crow) x += p.beta * to_f(crow[col + i]);
+              if (OUT_F32)
+                reinterpret_cast<float*>(drow)[col + i] = x;
+              else
+                reinterpret_cast<__nv_bfloat16*>(drow)[col + i] = __float2bfloat16_rn(x);
+            }
+          }
+        }
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the pair is done with each other's barriers and tensor memory
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
 }  // namespace astrai
 
 namespace astrai_host {
@@ -923,6 +1239,70 @@ static void dispatch_majors(int a_mn, int b_mn, int out_f32, const CUtensorMap& 
   ASTRAI_GEMM_CASE(1, 0, 1)
   ASTRAI_GEMM_CASE(1, 1, 1)
 #undef ASTRAI_GEMM_CASE
+}
+
+// CTA-pair kernel launch: persistent grid of as many clusters of two as can be resident at once
+// (queried once per device and instantiation), never more than one cluster per tile.
+template <int BN, int A_MN, int B_MN, int OUT_F32>
+static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int tiles,
+                             cudaStream_t stream) {
+  using pr = astrai::PairCfg<BN>;
+  auto kern = astrai::gemm_pair_kernel<BN, A_MN, B_MN, OUT_F32>;
+  static int max_clusters[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (max_clusters[dev & 63] == 0) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pr::SMEM);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(num_sms(dev) & ~1);
+    cfg.blockDim = dim3(pr::THREADS);
+    cfg.dynamicSmemBytes = pr::SMEM;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      (void)cudaGetLastError();
+      n = num_sms(dev) / 2;
+    }
+    max_clusters[dev & 63] = n;
+  }
+  const int pairs = std::min(tiles, max_clusters[dev & 63]);
+  (astrai::note_launch(), kern<<<2 * pairs, pr::THREADS, pr::SMEM, stream>>>(ta, tb, p));
+}
+
+template <int BN>
+static void dispatch_pair(int a_mn, int b_mn, int out_f32, const CUtensorMap& ta, const CUtensorMap& tb,
+                          const GemmParams& p, int tiles, cudaStream_t s) {
+#define ASTRAI_PAIR_CASE(AM, BMJ, OF) \
+  if (a_mn == AM && b_mn == BMJ && out_f32 == OF) return launch_gemm_pair<BN, AM, BMJ, OF>(ta, tb, p, tiles, s);
+  ASTRAI_PAIR_CASE(0, 0, 0)
+  ASTRAI_PAIR_CASE(0, 1, 0)
+  ASTRAI_PAIR_CASE(1, 0, 0)
+  ASTRAI_PAIR_CASE(1, 1, 0)
+  ASTRAI_PAIR_CASE(0, 0, 1)
+  ASTRAI_PAIR_CASE(0, 1, 1)
+  ASTRAI_PAIR_CASE(1, 0, 1)
+  ASTRAI_PAIR_CASE(1, 1, 1)
+#undef ASTRAI_PAIR_CASE
+}
+
+// CTA-pair policy: plain and batched GEMMs with M > 128 and N > 128 run on the pair kernel.
+// Measured on B200 over the 1.1B step's GEMMs (kernel_bench gemm, CUDA events), the pair kernel
+// was faster than the single-CTA kernel on every shape: 8192x3072x2048 1345 vs 1158 TFLOP/s,
+// 8192x32000x2048 1508 vs 1319, 8192x5632x2048 (MN-major B) 1135 vs 910, 2048x2048x8192 (both
+// MN-major; single-CTA 128x256) 1366 vs 1063, 11264x2048x8192 1449 vs 1430 (single-CTA with
+// Stream-K), 8192^3 equal. ASTRAI_GEMM_PAIR=0 keeps the single-CTA kernel.
+static bool pair_on() {
+  static const bool on = [] {
+    const char* e = std::getenv("ASTRAI_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 // Stream-K decision: whole waves of tiles plus the last partial wave split into k-block units over
@@ -1014,7 +1394,9 @@ static void pick_tile(int M, int N, int batch, int sms, int& bm, int& bn, int kb
 // Row strides (lda, ldb, ldd, ldc) and batch strides are in elements.
 // a_mn == 0: A stored [batch][M][lda] (K contiguous); a_mn == 1: [batch][K][lda] (M contiguous).
 // b_mn == 0: B stored [batch][N][ldb];                b_mn == 1: [batch][K][ldb].
-// force_bn: 0 = automatic; 128 / 256 = BM 128 with that BN; 512 = 256 x 256 tiles.
+// force_bn: 0 = automatic; 128 / 256 = BM 128 with that BN; 512 = 256 x 256 tiles; 1024 = 256 x 256
+// tiles on a CTA pair; 1025 = 256 x 128 tiles on a CTA pair; 2 = automatic among the single-CTA
+// shapes (with Stream-K where it applies).
 // Fused all-gather arguments of gemm_bf16 (see GemmParams::npeers).
 struct GatherArgs {
   int npeers;
@@ -1028,7 +1410,7 @@ struct GatherArgs {
 };
 
 // The plan gemm_bf16 would use for a plain GEMM on the current device: tile shape and whether the
-// last partial wave is split Stream-K style (out: bm, bn, streamk, tiles, sms).
+// last partial wave is split Stream-K style (out: bm, bn, streamk, tiles, sms, pair).
 void gemm_plan(int M, int N, int K, int batch, int* out) {
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1041,6 +1423,9 @@ void gemm_plan(int M, int N, int K, int batch, int* out) {
   out[2] = use_streamk(tiles, (K + 63) / 64, sms) ? 1 : 0;
   out[3] = (int)tiles;
   out[4] = sms;
+  // out[5]: the automatic choice runs this GEMM on 256 x 256 CTA-pair tiles instead (out[0..3]
+  // describe the single-CTA plan, which force_bn 2 selects)
+  out[5] = (M > 128 && N > 128 && pair_on()) ? 1 : 0;
 }
 
 void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int N, int K, int batch, int a_mn,
@@ -1054,10 +1439,17 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
   int BM = 128, BN = 256;
   if (force_bn == 128 || force_bn == 256) {
     BN = force_bn;
-  } else if (force_bn == 512) {
+  } else if (force_bn == 512 || force_bn == 1024) {
     BM = 256;
   } else {
     pick_tile(M, N, batch, sms, BM, BN, (K + 63) / 64);
+  }
+  // 256 x 256 tiles on a CTA pair (force_bn 1024, or the automatic pick under the pair policy)
+  const bool pair = gather == nullptr &&
+                    (force_bn == 1024 || force_bn == 1025 || (force_bn == 0 && M > 128 && N > 128 && pair_on()));
+  if (pair) {
+    BM = 256;
+    BN = force_bn == 1025 ? 128 : 256;
   }
 
   CUtensorMap ta, tb;
@@ -1076,7 +1468,7 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
     const uint64_t bstride = batch > 1 ? (uint64_t)strideB * 2 : (uint64_t)rows * ldb * 2;
     uint64_t dims[3] = {inner, rows, (uint64_t)batch};
     uint64_t strides[2] = {(uint64_t)ldb * 2, bstride ? bstride : 16};
-    uint32_t box[3] = {64, b_mn ? 64u : (uint32_t)BN, 1};
+    uint32_t box[3] = {64, b_mn ? 64u : (uint32_t)(pair ? BN / 2 : BN), 1};
     make_tmap_bf16(&tb, B, 3, dims, strides, box, true);
   }
   GemmParams p;
@@ -1129,6 +1521,8 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
   p.scatter_rank = 0;
   p.scatter_recv_off = 0;
   const int tiles = batch * p.tiles_m * p.tiles_n;
+  if (pair && BN == 128) return dispatch_pair<128>(a_mn, b_mn, out_f32, ta, tb, p, tiles, stream);
+  if (pair) return dispatch_pair<256>(a_mn, b_mn, out_f32, ta, tb, p, tiles, stream);
   int grid = std::min(tiles, sms);
   if (gather != nullptr) {
     if (C != nullptr || out_f32 || batch != 1 || gather->npeers < 0 || gather->npeers > astrai::kMaxGatherPeers)

@@ -40,7 +40,9 @@ class SymmetricBuffer:
         distributed = dist.is_available() and dist.is_initialized() and not local_only
         self.rank = dist.get_rank(group) if distributed else 0
         self.world = dist.get_world_size(group) if distributed else 1
-        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        device = torch.device(device) if device is not None else torch.device("cuda")
+        # an index-less "cuda" means the current device; keep the index explicit for the bindings
+        self.device = device if device.index is not None else torch.device("cuda", torch.cuda.current_device())
         self.nbytes = int(nbytes)
         with torch.cuda.device(self.device):
             self.local_ptr, handle = self.C.symm_alloc(self.nbytes)

@@ -42,7 +42,7 @@ def test_gemm_majors(a_mn, b_mn, M, N, K):
     assert rel_err(d, ref) < 1e-2
 
 
-@pytest.mark.parametrize("force_bn", [128, 256, 512])
+@pytest.mark.parametrize("force_bn", [128, 256, 512, 1024, 1025])
 def test_gemm_tiles_and_epilogue(force_bn):
     from astrai_b200.ops._ext import native
     from astrai_b200.ops.gemm import gemm_reference
@@ -61,7 +61,7 @@ def test_gemm_tiles_and_epilogue(force_bn):
     assert rel_err(d32, gemm_reference(a, b)) < 5e-3
 
 
-@pytest.mark.parametrize("force_bn", [0, 128, 256, 512])
+@pytest.mark.parametrize("force_bn", [0, 128, 256, 512, 1024, 1025])
 @pytest.mark.parametrize("out_f32,with_c", [(False, False), (False, True), (True, False)])
 def test_gemm_canary_padding_untouched(force_bn, out_f32, with_c):
     """Output written through a strided view of a larger canary-filled buffer: the kernel
@@ -83,6 +83,29 @@ def test_gemm_canary_padding_untouched(force_bn, out_f32, with_c):
     assert (big[M:] == canary).all() and (big[:, N:] == canary).all(), "write outside the output window"
     ref = gemm_reference(a, b, c=c.to(torch.bfloat16) if with_c else None, alpha=1.0, beta=1.0 if with_c else 0.0)
     assert rel_err(d, ref) < 1e-2
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("M,N,K,batch", [(256, 256, 64, 1), (384, 640, 200, 1), (1024, 768, 1024, 1),
+                                         (512, 384, 256, 3), (4096, 4352, 2048, 1)])
+@pytest.mark.parametrize("force_bn", [1024, 1025])
+def test_gemm_cta_pair(a_mn, b_mn, M, N, K, batch, force_bn):
+    """256 x 256 and 256 x 128 tiles on a CTA pair (tcgen05.mma.cta_group::2): every operand layout, ragged
+    tiles, batches, and more tiles than resident clusters (persistent walk over both
+    accumulator buffers)."""
+    from astrai_b200.ops._ext import native
+    from astrai_b200.ops.gemm import gemm_reference
+
+    torch.manual_seed(5)
+    a = torch.randn((batch, K, M) if a_mn else (batch, M, K), device="cuda", dtype=torch.bfloat16)
+    b = torch.randn((batch, K, N) if b_mn else (batch, N, K), device="cuda", dtype=torch.bfloat16)
+    d = torch.empty(batch, M, N, device="cuda", dtype=torch.bfloat16)
+    if batch == 1:
+        a, b, d = a[0], b[0], d[0]
+    native().gemm(a, b, d, None, a_mn, b_mn, 1.0, 0.0, force_bn)
+    ref = gemm_reference(a, b, a_mn=bool(a_mn), b_mn=bool(b_mn))
+    assert rel_err(d, ref) < 1e-2
+    assert native().read_error() == 0
 
 
 def test_gemm_batched():
@@ -119,12 +142,12 @@ def test_linear_autograd():
 @pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 1)])
 @pytest.mark.parametrize("M,N,K", [(3072, 2048, 8192), (2048, 5632, 8192), (3000, 2000, 8200)])
 def test_gemm_streamk(a_mn, b_mn, M, N, K):
-    """Shapes whose last wave of tiles is split over all SMs by k-blocks (the plan says so), against
-    an fp32 matmul; run twice so the fix-up flags are shown to reset between launches."""
+    """Shapes whose last wave of tiles is split over all SMs by k-blocks (the single-CTA plan says so,
+    force_bn 2), against an fp32 matmul; run twice so the fix-up flags are shown to reset between
+    launches."""
     from astrai_b200.ops._ext import native
-    from astrai_b200.ops.gemm import gemm
 
-    bm, bn, streamk, tiles, sms = native().gemm_plan(M, N, K, 1)
+    bm, bn, streamk, tiles, sms, _pair = native().gemm_plan(M, N, K, 1)
     if not streamk:
         pytest.skip(f"plan for {M}x{N}x{K} has no stream-K part ({tiles} tiles of {bm}x{bn} on {sms} SMs)")
     torch.manual_seed(1)
@@ -134,7 +157,8 @@ def test_gemm_streamk(a_mn, b_mn, M, N, K):
     B = b.float() if b_mn else b.float().t()
     ref = A @ B
     for _ in range(2):
-        d = gemm(a, b, a_mn=bool(a_mn), b_mn=bool(b_mn))
+        d = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        native().gemm(a, b, d, None, a_mn, b_mn, 1.0, 0.0, 2)
         assert rel_err(d, ref) < 1e-2
 
 
