@@ -893,8 +893,8 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
 // but each CTA's accumulator (its 128 rows x 256 columns) takes only 256 TMEM columns: two fit,
 // and the epilogue of tile t overlaps the MMAs of tile t+1 (the single-CTA 256 x 256 tile fills
 // TMEM, so its MMAs stall while the epilogue drains). Each CTA's stage is 32 KB: a 6-deep ring.
-// A 256 x 128 variant (each CTA stages 64 B rows; 24 KB stages, 8 deep) halves the tile for
-// shapes whose 256 x 256 tiles leave much of the last wave of pairs idle.
+// (A 256 x 128 pair tile moves 1.5x the operand bytes per FLOP and measured 0.5 - 0.75x the speed of
+// 256 x 256 on every training shape, so only 256 x 256 is instantiated.)
 //
 //   warp 0     TMA producer (both CTAs): loads into its own smem, completion counted on the
 //              even CTA's `full` barrier (cta_group::2 form of the tiled load, no multicast)
@@ -912,7 +912,7 @@ struct PairCfg {
   static constexpr int A_BYTES = 128 * BK * 2;   // this CTA's 128 rows of A
   static constexpr int B_BYTES = (BN / 2) * BK * 2;  // this CTA's BN / 2 of the tile's B rows
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;  // 6 (BN 256) or 8 (BN 128)
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;  // 6 for BN 256
   static constexpr int EPI_WARPS = 8;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
@@ -1395,8 +1395,7 @@ static void pick_tile(int M, int N, int batch, int sms, int& bm, int& bn, int kb
 // a_mn == 0: A stored [batch][M][lda] (K contiguous); a_mn == 1: [batch][K][lda] (M contiguous).
 // b_mn == 0: B stored [batch][N][ldb];                b_mn == 1: [batch][K][ldb].
 // force_bn: 0 = automatic; 128 / 256 = BM 128 with that BN; 512 = 256 x 256 tiles; 1024 = 256 x 256
-// tiles on a CTA pair; 1025 = 256 x 128 tiles on a CTA pair; 2 = automatic among the single-CTA
-// shapes (with Stream-K where it applies).
+// tiles on a CTA pair; 2 = automatic among the single-CTA shapes (with Stream-K where it applies).
 // Fused all-gather arguments of gemm_bf16 (see GemmParams::npeers).
 struct GatherArgs {
   int npeers;
@@ -1445,12 +1444,9 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
     pick_tile(M, N, batch, sms, BM, BN, (K + 63) / 64);
   }
   // 256 x 256 tiles on a CTA pair (force_bn 1024, or the automatic pick under the pair policy)
-  const bool pair = gather == nullptr &&
-                    (force_bn == 1024 || force_bn == 1025 || (force_bn == 0 && M > 128 && N > 128 && pair_on()));
-  if (pair) {
-    BM = 256;
-    BN = force_bn == 1025 ? 128 : 256;
-  }
+  const bool pair =
+      gather == nullptr && (force_bn == 1024 || (force_bn == 0 && M > 128 && N > 128 && pair_on()));
+  if (pair) BM = BN = 256;
 
   CUtensorMap ta, tb;
   {
@@ -1521,7 +1517,6 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
   p.scatter_rank = 0;
   p.scatter_recv_off = 0;
   const int tiles = batch * p.tiles_m * p.tiles_n;
-  if (pair && BN == 128) return dispatch_pair<128>(a_mn, b_mn, out_f32, ta, tb, p, tiles, stream);
   if (pair) return dispatch_pair<256>(a_mn, b_mn, out_f32, ta, tb, p, tiles, stream);
   int grid = std::min(tiles, sms);
   if (gather != nullptr) {

@@ -67,18 +67,17 @@ def bench_gemm(only=None):
         a = torch.randn((K, M) if amn else (M, K), device="cuda", dtype=torch.bfloat16)
         b = torch.randn((K, N) if bmn else (N, K), device="cuda", dtype=torch.bfloat16)
         d = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-        # force_bn 2: the single-CTA kernel (automatic tile shape, Stream-K where it applies)
-        ms = time_fn(lambda: C.gemm(a, b, d, None, amn, bmn, 1.0, 0.0, 2))
+        ms = time_fn(lambda: C.gemm(a, b, d, None, amn, bmn, 1.0, 0.0, 0))  # automatic plan
         A = a.t() if amn else a
         B = b if bmn else b.t()
         ms_ref = time_fn(lambda: torch.matmul(A, B))
-        # the same GEMM on 256 x 256 CTA-pair tiles (force_bn 1024), and its largest deviation
+        # the single-CTA kernel (force_bn 2: its automatic tile shape, Stream-K where it applies)
+        # and its largest deviation from the automatic plan's output
         d2 = torch.empty_like(d)
-        ms_pair = time_fn(lambda: C.gemm(a, b, d2, None, amn, bmn, 1.0, 0.0, 1024))
-        pair_dev = float((d2.float() - d.float()).abs().max() / d.float().abs().max().clamp_min(1e-30))
-        ms_pair128 = time_fn(lambda: C.gemm(a, b, d2, None, amn, bmn, 1.0, 0.0, 1025))
+        ms_1cta = time_fn(lambda: C.gemm(a, b, d2, None, amn, bmn, 1.0, 0.0, 2))
+        dev = float((d2.float() - d.float()).abs().max() / d.float().abs().max().clamp_min(1e-30))
         fl = 2.0 * M * N * K
-        # one extra launch with the wait-cycle counters on: where the pipeline stalls
+        # one extra launch of the single-CTA kernel with its wait-cycle counters on: where it stalls
         cnt = torch.zeros(4, device="cuda", dtype=torch.int64)
         C.gemm_profile_set(cnt)
         C.gemm(a, b, d, None, amn, bmn, 1.0, 0.0, 2)
@@ -86,17 +85,17 @@ def bench_gemm(only=None):
         C.gemm_profile_set(None)
         w = [int(v) for v in cnt.tolist()]
         sms = torch.cuda.get_device_properties(0).multi_processor_count
-        cyc = ms * 1e-3 * 1.9e9  # cycles of one CTA at ~1.9 GHz
+        cyc = ms_1cta * 1e-3 * 1.9e9  # cycles of one CTA at ~1.9 GHz
         bm, bn, streamk, tiles, _, pair = C.gemm_plan(M, N, K, 1)
         print(json.dumps({"kernel": "gemm", "case": name, "M": M, "N": N, "K": K, "ms": round(ms, 4),
-                          "tile": f"{bm}x{bn}", "tiles": tiles, "streamk": streamk, "auto_pair": pair,
+                          "pair": pair, "single_cta_tile": f"{bm}x{bn}", "single_cta_tiles": tiles,
+                          "single_cta_streamk": streamk,
                           "tflops": round(fl / ms / 1e9, 1), "frac_of_peak": round(fl / ms / 1e9 / tf, 3),
                           "peak_src": src, "cublas_ms": round(ms_ref, 4),
                           "cublas_tflops": round(fl / ms_ref / 1e9, 1),
-                          "pair_ms": round(ms_pair, 4), "pair_tflops": round(fl / ms_pair / 1e9, 1),
-                          "pair_rel_dev": round(pair_dev, 5), "pair128_ms": round(ms_pair128, 4),
-                          "pair128_tflops": round(fl / ms_pair128 / 1e9, 1),
-                          "wait_frac_per_cta": {k: round(v / sms / cyc, 3) for k, v in
+                          "single_cta_ms": round(ms_1cta, 4), "single_cta_tflops": round(fl / ms_1cta / 1e9, 1),
+                          "single_cta_rel_dev": round(dev, 5),
+                          "single_cta_wait_frac": {k: round(v / sms / cyc, 3) for k, v in
                                                 zip(("producer_empty", "mma_full", "mma_acc_empty", "epi_acc_full"),
                                                     w)}}))
 
