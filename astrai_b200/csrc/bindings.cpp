@@ -498,9 +498,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scatter_rank") = 0, py::arg("scatter_recv_off") = 0,
         py::arg("rank_deltas") = std::vector<int64_t>{});
   m.def("gemm_plan", [](int64_t M, int64_t N, int64_t K, int64_t batch) {
-    int o[6] = {0, 0, 0, 0, 0, 0};
+    int o[7] = {0, 0, 0, 0, 0, 0, 0};
     astrai_host::gemm_plan((int)M, (int)N, (int)K, (int)batch, o);
-    return py::make_tuple(o[0], o[1], (bool)o[2], o[3], o[4], (bool)o[5]);
+    return py::make_tuple(o[0], o[1], (bool)o[2], o[3], o[4], (bool)o[5], (bool)o[6]);
   }, py::arg("M"), py::arg("N"), py::arg("K"), py::arg("batch") = 1);
   m.def("gemm_profile_set", [](const c10::optional<at::Tensor>& counters) {
     // int64 [4] CUDA tensor that later GEMM launches add their wait cycles to, or None (off)

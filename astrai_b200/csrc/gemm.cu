@@ -169,27 +169,31 @@ struct WorkItem {
   bool partial; // the tile is split over several CTAs
 };
 
+// Work walk of one worker (a CTA, or a CTA pair in gemm_pair_kernel): `idx` of `cnt` workers.
 struct WorkIter {
-  int t;
+  int t, idx, cnt;
   long long u, u_end;
-  __device__ __forceinline__ void init(const GemmParams& p) {
-    t = blockIdx.x;
+  __device__ __forceinline__ void init(const GemmParams& p) { init(p, blockIdx.x, gridDim.x); }
+  __device__ __forceinline__ void init(const GemmParams& p, int worker, int workers) {
+    idx = worker;
+    cnt = workers;
+    t = worker;
     if (p.sk_units > 0) {
-      u = (long long)blockIdx.x * p.sk_units / gridDim.x;
-      u_end = (long long)(blockIdx.x + 1) * p.sk_units / gridDim.x;
+      u = (long long)worker * p.sk_units / workers;
+      u_end = (long long)(worker + 1) * p.sk_units / workers;
     } else {
       u = u_end = 0;
     }
   }
-  // CTA whose unit range contains unit v (every range is non-empty: sk_units >= gridDim.x)
-  __device__ __forceinline__ static int cta_of_unit(const GemmParams& p, long long v) {
-    return (int)(((v + 1) * gridDim.x - 1) / p.sk_units);
+  // worker whose unit range contains unit v (every range is non-empty: sk_units >= workers)
+  __device__ __forceinline__ int worker_of_unit(const GemmParams& p, long long v) const {
+    return (int)(((v + 1) * cnt - 1) / p.sk_units);
   }
   __device__ __forceinline__ bool next(const GemmParams& p, int num_tiles, int kblk_full, WorkItem& w) {
     const int limit = p.sk_units > 0 ? p.dp_tiles : num_tiles;
     if (t < limit) {
       w = {t, 0, kblk_full, -1, 0, true, false};
-      t += gridDim.x;
+      t += cnt;
       return true;
     }
     if (u >= u_end) return false;
@@ -202,7 +206,7 @@ struct WorkIter {
     w.kb0 = (int)(lo - tbeg);
     w.kb1 = (int)(u_end - tbeg);
     w.sk = (int)tr;
-    w.ord = (int)blockIdx.x - cta_of_unit(p, tbeg);  // lower CTAs holding parts of this tile
+    w.ord = idx - worker_of_unit(p, tbeg);  // lower workers holding parts of this tile
     w.owner = w.kb1 == KB;
     w.partial = !(w.kb0 == 0 && w.kb1 == KB);
     u_end = lo;
@@ -1019,11 +1023,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = pair_id; ok && tile < num_tiles; tile += npairs) {
+      WorkIter wi;
+      wi.init(p, pair_id, npairs);
+      WorkItem w;
+      while (ok && wi.next(p, num_tiles, p.k_blocks, w)) {
         int b, mb, nb;
-        tile_coords(tile, p.tiles_m, p.tiles_n, b, mb, nb);
+        tile_coords(w.tile, p.tiles_m, p.tiles_n, b, mb, nb);
         const int m0 = mb * 256 + (int)rank * 128, n0 = nb * BN + (int)rank * BNH;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kErrWaitEmpty)) {
             ok = false;
             break;
@@ -1061,11 +1068,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = pair_id; ok && tile < num_tiles; tile += npairs) {
+      WorkIter wi;
+      wi.init(p, pair_id, npairs);
+      WorkItem w;
+      while (ok && wi.next(p, num_tiles, p.k_blocks, w)) {
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err, kErrWaitAccEmpty)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.err, kErrWaitFull)) {
             ok = false;
             break;
@@ -1077,7 +1087,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t ad = A_MN ? sdesc_sw128(a_base + k * 2048, 8192, 1024) : sdesc_sw128(a_base + k * 32, 16, 1024);
             const uint64_t bd = B_MN ? sdesc_sw128(b_base + k * 2048, 8192, 1024) : sdesc_sw128(b_base + k * 32, 16, 1024);
-            umma_bf16_pair(d_tmem, ad, bd, idesc, (kb != 0) || k != 0);
+            umma_bf16_pair(d_tmem, ad, bd, idesc, (kb != w.kb0) || k != 0);
           }
           umma_commit_pair(&empty[stage]);
           if (++stage == STAGES) {
@@ -1103,11 +1113,87 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS
     uint32_t acc_phase = 0;
     using OutT = typename std::conditional<OUT_F32, float, __nv_bfloat16>::type;
     const bool use_c = p.C != nullptr && p.beta != 0.f;
-    for (int tile = pair_id; tile < num_tiles; tile += npairs) {
+    constexpr int EPI_THREADS = EPI_WARPS * 32;
+    const int et = threadIdx.x - 64;  // epilogue thread index
+    WorkIter wi;
+    wi.init(p, pair_id, npairs);
+    WorkItem w;
+    while (wi.next(p, num_tiles, p.k_blocks, w)) {
       int b, mb, nb;
-      tile_coords(tile, p.tiles_m, p.tiles_n, b, mb, nb);
+      tile_coords(w.tile, p.tiles_m, p.tiles_n, b, mb, nb);
       if (!mbar_wait(&acc_full[acc], acc_phase, p.err, kErrWaitAccFull)) break;
       tc_fence_after();
+      if (w.partial) {
+        // Stream-K part (see GemmParams): per CTA, as in the single-CTA kernel. A non-owner parks this
+        // CTA's 128 x BN fp32 partial in its own slot (thread-major float4s) and raises its flag; the
+        // owner waits for the same-rank CTAs of the lower pairs holding the tile's other parts and
+        // adds their slots into its accumulator before the regular epilogue below.
+        const uint32_t t_part = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + cpart * BNH;
+        if (!w.owner) {
+          float4* slot = reinterpret_cast<float4*>(p.sk_ws + (long long)blockIdx.x * 128 * BN) + et;
+#pragma unroll 1
+          for (int c = 0; c < BNH; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(t_part + c, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int v4 = 0; v4 < 8; ++v4)
+              slot[(c / 4 + v4) * EPI_THREADS] =
+                  make_float4(__uint_as_float(r[4 * v4]), __uint_as_float(r[4 * v4 + 1]),
+                              __uint_as_float(r[4 * v4 + 2]), __uint_as_float(r[4 * v4 + 3]));
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(acc ? empty_bar1 : empty_bar0);
+          __threadfence();
+          named_bar_sync(1, EPI_THREADS);
+          if (et == 0) st_release_gpu_s32(p.sk_flags + blockIdx.x, 1);
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1;
+          }
+          continue;
+        }
+        const int first = pair_id - w.ord;  // lowest pair holding a part of this tile
+        if (et == 0)
+          for (int j = first; j < pair_id; ++j)
+            if (!wait_flag_eq(p.sk_flags + 2 * j + (int)rank, 1, p.err)) break;
+        named_bar_sync(1, EPI_THREADS);
+#pragma unroll 1
+        for (int c = 0; c < BNH; c += 32) {
+          float4 y[8];
+#pragma unroll
+          for (int v4 = 0; v4 < 8; ++v4) y[v4] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+          for (int j = first; j < pair_id; ++j) {
+            const float4* src =
+                reinterpret_cast<const float4*>(p.sk_ws + (long long)(2 * j + (int)rank) * 128 * BN) + et;
+#pragma unroll
+            for (int v4 = 0; v4 < 8; ++v4) {
+              const float4 z = __ldcg(src + (c / 4 + v4) * EPI_THREADS);
+              y[v4].x += z.x;
+              y[v4].y += z.y;
+              y[v4].z += z.z;
+              y[v4].w += z.w;
+            }
+          }
+          uint32_t r[32];
+          tmem_ld32(t_part + c, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int v4 = 0; v4 < 8; ++v4) {
+            r[4 * v4] = __float_as_uint(__uint_as_float(r[4 * v4]) + y[v4].x);
+            r[4 * v4 + 1] = __float_as_uint(__uint_as_float(r[4 * v4 + 1]) + y[v4].y);
+            r[4 * v4 + 2] = __float_as_uint(__uint_as_float(r[4 * v4 + 2]) + y[v4].z);
+            r[4 * v4 + 3] = __float_as_uint(__uint_as_float(r[4 * v4 + 3]) + y[v4].w);
+          }
+          tmem_st32(t_part + c, r);
+        }
+        tmem_wait_st();
+        named_bar_sync(1, EPI_THREADS);  // every thread has read the slots
+        if (et == 0)
+          for (int j = first; j < pair_id; ++j) p.sk_flags[2 * j + (int)rank] = 0;  // ready for the next launch
+      }
       const int row = mb * 256 + (int)rank * 128 + q * 32 + lane;
       const int n0 = nb * BN + cpart * BNH;
       const bool row_ok = row < p.M;
@@ -1241,17 +1327,13 @@ static void dispatch_majors(int a_mn, int b_mn, int out_f32, const CUtensorMap& 
 #undef ASTRAI_GEMM_CASE
 }
 
-// CTA-pair kernel launch: persistent grid of as many clusters of two as can be resident at once
-// (queried once per device and instantiation), never more than one cluster per tile.
-template <int BN, int A_MN, int B_MN, int OUT_F32>
-static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int tiles,
-                             cudaStream_t stream) {
-  using pr = astrai::PairCfg<BN>;
-  auto kern = astrai::gemm_pair_kernel<BN, A_MN, B_MN, OUT_F32>;
+// Clusters of two that can be resident at once on this device (queried once per device; every
+// instantiation of the pair kernel has the same footprint: one CTA per SM by its shared memory).
+static int pair_clusters(int dev) {
   static int max_clusters[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
   if (max_clusters[dev & 63] == 0) {
+    using pr = astrai::PairCfg<256>;
+    auto kern = astrai::gemm_pair_kernel<256, 0, 0, 0>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pr::SMEM);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(num_sms(dev) & ~1);
@@ -1271,15 +1353,30 @@ static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const
     }
     max_clusters[dev & 63] = n;
   }
-  const int pairs = std::min(tiles, max_clusters[dev & 63]);
+  return max_clusters[dev & 63];
+}
+
+// CTA-pair kernel launch on `pairs` clusters of two (persistent; at most pair_clusters(dev)).
+template <int BN, int A_MN, int B_MN, int OUT_F32>
+static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int pairs,
+                             cudaStream_t stream) {
+  using pr = astrai::PairCfg<BN>;
+  auto kern = astrai::gemm_pair_kernel<BN, A_MN, B_MN, OUT_F32>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pr::SMEM);
+    attr_set[dev & 63] = true;
+  }
   (astrai::note_launch(), kern<<<2 * pairs, pr::THREADS, pr::SMEM, stream>>>(ta, tb, p));
 }
 
 template <int BN>
 static void dispatch_pair(int a_mn, int b_mn, int out_f32, const CUtensorMap& ta, const CUtensorMap& tb,
-                          const GemmParams& p, int tiles, cudaStream_t s) {
+                          const GemmParams& p, int pairs, cudaStream_t s) {
 #define ASTRAI_PAIR_CASE(AM, BMJ, OF) \
-  if (a_mn == AM && b_mn == BMJ && out_f32 == OF) return launch_gemm_pair<BN, AM, BMJ, OF>(ta, tb, p, tiles, s);
+  if (a_mn == AM && b_mn == BMJ && out_f32 == OF) return launch_gemm_pair<BN, AM, BMJ, OF>(ta, tb, p, pairs, s);
   ASTRAI_PAIR_CASE(0, 0, 0)
   ASTRAI_PAIR_CASE(0, 1, 0)
   ASTRAI_PAIR_CASE(1, 0, 0)
@@ -1327,6 +1424,26 @@ static bool use_streamk(long long tiles, int kb, int sms) {
   if (rem == 0 || rem * kb < 4LL * sms) return false;
   const double dp = (double)(tiles / sms + 1), sk = (double)tiles / sms + 0.08;
   return (dp - sk) * kb >= 16.0;
+}
+// Stream-K for the pair kernel over `pairs` workers: the last partial wave of 256 x 256 tiles can
+// be split when every pair gets at least 4 k-blocks of it and the split would save at least 8
+// k-blocks of time per pair. Measured on B200 it LOST on every step shape it applies to (8192 x
+// 3072 x 2048: 0.0847 vs 0.0768 ms unsplit; 8192 x 2048 x 2048: 0.0585 vs 0.0513; 11264 x 2048 x
+// 8192: 0.2848 vs 0.2663): the fix-up tail (partials out, flags, partials in, then the epilogue)
+// is exposed at the end of the launch. So it is opt-in (ASTRAI_PAIR_STREAMK=1, or force_bn 1026).
+static bool pair_streamk_on() {
+  static const bool on = [] {
+    const char* e = std::getenv("ASTRAI_PAIR_STREAMK");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+static bool use_streamk_pair(long long tiles, int kb, int pairs) {
+  if (tiles <= 0 || pairs <= 0) return false;
+  const long long rem = tiles % pairs;
+  if (rem == 0 || tiles < pairs || rem * kb < 4LL * pairs) return false;
+  const double whole = (double)(tiles / pairs + 1), split = (double)tiles / pairs + 0.05;
+  return (whole - split) * kb >= 8.0;
 }
 static double effective_waves(long long tiles, int kb, int sms) {
   return use_streamk(tiles, kb, sms) ? (double)tiles / sms + 0.08 : (double)((tiles + sms - 1) / sms);
@@ -1395,7 +1512,8 @@ static void pick_tile(int M, int N, int batch, int sms, int& bm, int& bn, int kb
 // a_mn == 0: A stored [batch][M][lda] (K contiguous); a_mn == 1: [batch][K][lda] (M contiguous).
 // b_mn == 0: B stored [batch][N][ldb];                b_mn == 1: [batch][K][ldb].
 // force_bn: 0 = automatic; 128 / 256 = BM 128 with that BN; 512 = 256 x 256 tiles; 1024 = 256 x 256
-// tiles on a CTA pair; 2 = automatic among the single-CTA shapes (with Stream-K where it applies).
+// tiles on a CTA pair; 1026 = the same with a Stream-K last wave where it applies;
+// 2 = automatic among the single-CTA shapes (with Stream-K where it applies).
 // Fused all-gather arguments of gemm_bf16 (see GemmParams::npeers).
 struct GatherArgs {
   int npeers;
@@ -1409,7 +1527,7 @@ struct GatherArgs {
 };
 
 // The plan gemm_bf16 would use for a plain GEMM on the current device: tile shape and whether the
-// last partial wave is split Stream-K style (out: bm, bn, streamk, tiles, sms, pair).
+// last partial wave is split Stream-K style (out: bm, bn, streamk, tiles, sms, pair, pair_streamk).
 void gemm_plan(int M, int N, int K, int batch, int* out) {
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1425,6 +1543,9 @@ void gemm_plan(int M, int N, int K, int batch, int* out) {
   // out[5]: the automatic choice runs this GEMM on 256 x 256 CTA-pair tiles instead (out[0..3]
   // describe the single-CTA plan, which force_bn 2 selects)
   out[5] = (M > 128 && N > 128 && pair_on()) ? 1 : 0;
+  // out[6]: the pair plan with Stream-K allowed (force_bn 1026) splits its last wave
+  const long long ptiles = (long long)((M + 255) / 256) * ((N + 255) / 256) * batch;
+  out[6] = use_streamk_pair(ptiles, (K + 63) / 64, pair_clusters(dev)) ? 1 : 0;
 }
 
 void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int N, int K, int batch, int a_mn,
@@ -1444,8 +1565,8 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
     pick_tile(M, N, batch, sms, BM, BN, (K + 63) / 64);
   }
   // 256 x 256 tiles on a CTA pair (force_bn 1024, or the automatic pick under the pair policy)
-  const bool pair =
-      gather == nullptr && (force_bn == 1024 || (force_bn == 0 && M > 128 && N > 128 && pair_on()));
+  const bool pair = gather == nullptr &&
+                    (force_bn == 1024 || force_bn == 1026 || (force_bn == 0 && M > 128 && N > 128 && pair_on()));
   if (pair) BM = BN = 256;
 
   CUtensorMap ta, tb;
@@ -1517,7 +1638,18 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
   p.scatter_rank = 0;
   p.scatter_recv_off = 0;
   const int tiles = batch * p.tiles_m * p.tiles_n;
-  if (pair) return dispatch_pair<256>(a_mn, b_mn, out_f32, ta, tb, p, tiles, stream);
+  if (pair) {
+    const int pmax = pair_clusters(dev);
+    int pairs = std::min(tiles, pmax);
+    const bool split = force_bn == 1026 || (force_bn != 1024 && pair_streamk_on() && streamk_on());
+    if (split && use_streamk_pair(tiles, p.k_blocks, pmax) &&
+        sk_buffers(dev, stream, sms, &p.sk_ws, &p.sk_flags)) {
+      p.dp_tiles = tiles / pmax * pmax;
+      p.sk_units = (long long)(tiles - p.dp_tiles) * p.k_blocks;
+      pairs = pmax;
+    }
+    return dispatch_pair<256>(a_mn, b_mn, out_f32, ta, tb, p, pairs, stream);
+  }
   int grid = std::min(tiles, sms);
   if (gather != nullptr) {
     if (C != nullptr || out_f32 || batch != 1 || gather->npeers < 0 || gather->npeers > astrai::kMaxGatherPeers)

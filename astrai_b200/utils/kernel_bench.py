@@ -86,9 +86,11 @@ def bench_gemm(only=None):
         w = [int(v) for v in cnt.tolist()]
         sms = torch.cuda.get_device_properties(0).multi_processor_count
         cyc = ms_1cta * 1e-3 * 1.9e9  # cycles of one CTA at ~1.9 GHz
-        bm, bn, streamk, tiles, _, pair = C.gemm_plan(M, N, K, 1)
+        bm, bn, streamk, tiles, _, pair, pair_sk = C.gemm_plan(M, N, K, 1)
+        ms_pair_sk = time_fn(lambda: C.gemm(a, b, d2, None, amn, bmn, 1.0, 0.0, 1026))  # pair + Stream-K
         print(json.dumps({"kernel": "gemm", "case": name, "M": M, "N": N, "K": K, "ms": round(ms, 4),
-                          "pair": pair, "single_cta_tile": f"{bm}x{bn}", "single_cta_tiles": tiles,
+                          "pair": pair, "pair_streamk_applies": pair_sk, "pair_streamk_ms": round(ms_pair_sk, 4),
+                          "single_cta_tile": f"{bm}x{bn}", "single_cta_tiles": tiles,
                           "single_cta_streamk": streamk,
                           "tflops": round(fl / ms / 1e9, 1), "frac_of_peak": round(fl / ms / 1e9 / tf, 3),
                           "peak_src": src, "cublas_ms": round(ms_ref, 4),

@@ -146,7 +146,7 @@ def test_gemm_streamk(a_mn, b_mn, M, N, K):
     launches."""
     from astrai_b200.ops._ext import native
 
-    bm, bn, streamk, tiles, sms, _pair = native().gemm_plan(M, N, K, 1)
+    bm, bn, streamk, tiles, sms, _pair, _pair_sk = native().gemm_plan(M, N, K, 1)
     if not streamk:
         pytest.skip(f"plan for {M}x{N}x{K} has no stream-K part ({tiles} tiles of {bm}x{bn} on {sms} SMs)")
     torch.manual_seed(1)
@@ -159,6 +159,33 @@ def test_gemm_streamk(a_mn, b_mn, M, N, K):
         d = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
         native().gemm(a, b, d, None, a_mn, b_mn, 1.0, 0.0, 2)
         assert rel_err(d, ref) < 1e-2
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 1)])
+@pytest.mark.parametrize("M,N,K", [(8192, 2048, 2048), (3072, 2048, 8192), (3000, 2000, 8200)])
+def test_gemm_cta_pair_streamk(a_mn, b_mn, M, N, K):
+    """Pair-tile plans whose last wave is split by k-blocks over all pairs (opt-in, force_bn 1026; the
+    plan says it applies), against an fp32 matmul and the unsplit pair kernel; twice, so the fix-up
+    flags reset between launches."""
+    from astrai_b200.ops._ext import native
+
+    *_, pair_sk = native().gemm_plan(M, N, K, 1)
+    if not pair_sk:
+        pytest.skip(f"pair plan for {M}x{N}x{K} has no stream-K part on this device")
+    torch.manual_seed(4)
+    a = torch.randn((K, M) if a_mn else (M, K), device="cuda", dtype=torch.bfloat16)
+    b = torch.randn((K, N) if b_mn else (N, K), device="cuda", dtype=torch.bfloat16)
+    A = a.float().t() if a_mn else a.float()
+    B = b.float() if b_mn else b.float().t()
+    ref = A @ B
+    whole = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    native().gemm(a, b, whole, None, a_mn, b_mn, 1.0, 0.0, 1024)
+    for _ in range(2):
+        d = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        native().gemm(a, b, d, None, a_mn, b_mn, 1.0, 0.0, 1026)
+        assert rel_err(d, ref) < 1e-2
+        assert rel_err(d, whole.float()) < 1e-2
+    assert native().read_error() == 0
 
 
 @pytest.mark.parametrize("rows,D", [(333, 128), (333, 1024), (333, 2048), (333, 4096), (5000, 2048), (4099, 1000),
