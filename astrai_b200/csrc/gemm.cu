@@ -1029,7 +1029,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS
       while (ok && wi.next(p, num_tiles, p.k_blocks, w)) {
         int b, mb, nb;
         tile_coords(w.tile, p.tiles_m, p.tiles_n, b, mb, nb);
-        const int m0 = mb * 256 + (int)rank * 128, n0 = nb * BN + (int)rank * BNH;
+        const int m0 = mb * 256 + (int)rank * 128;
+        // epi 1 (SwiGLU forward): the even CTA stages up rows, the odd one the gate rows of the same
+        // BNH output columns, so each accumulator holds u in columns [0, BNH) and g in [BNH, BN)
+        const int n0 = p.epi == 1 ? nb * BNH + (int)rank * p.F : nb * BN + (int)rank * BNH;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.err, kErrWaitEmpty)) {
             ok = false;
@@ -1200,6 +1203,62 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS
       OutT* drow = reinterpret_cast<OutT*>(p.D) + (long long)b * p.strideD + (long long)row * p.ldd;
       const OutT* crow =
           use_c ? reinterpret_cast<const OutT*>(p.C) + (long long)b * p.strideC + (long long)row * p.ldc : nullptr;
+      if (p.epi == 1) {
+        // SwiGLU forward: h = (u, g) and a = silu(g) * u for output columns j0 .. j0 + BNH / 2
+        constexpr int PER = BNH / 2;
+        const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+        uint32_t pu[PER / 2], pg[PER / 2];
+#pragma unroll
+        for (int c = 0; c < PER; c += 32) {
+          uint32_t ru[32], rg[32];
+          tmem_ld32(t_row + cpart * PER + c, ru);
+          tmem_ld32(t_row + BNH + cpart * PER + c, rg);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            pu[c / 2 + e] = pack_bf16(__uint_as_float(ru[2 * e]), __uint_as_float(ru[2 * e + 1]));
+            pg[c / 2 + e] = pack_bf16(__uint_as_float(rg[2 * e]), __uint_as_float(rg[2 * e + 1]));
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(acc ? empty_bar1 : empty_bar0);
+        if (row_ok) {
+          const int j0 = nb * BNH + cpart * PER;
+          __nv_bfloat16* hrow = reinterpret_cast<__nv_bfloat16*>(p.D) + (long long)row * p.ldd;
+          __nv_bfloat16* arow = p.aux + (long long)row * p.ldaux;
+#pragma unroll
+          for (int g8 = 0; g8 < PER; g8 += 8) {
+            const int j = j0 + g8;
+            uint32_t ha[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 ub = unpack_bf16(pu[g8 / 2 + e]), gb = unpack_bf16(pg[g8 / 2 + e]);
+              ha[e] = pack_bf16(ub.x * gb.x * sigmoid_f(gb.x), ub.y * gb.y * sigmoid_f(gb.y));
+            }
+            if (j + 8 <= p.F && p.vec_ok) {
+              *reinterpret_cast<uint4*>(hrow + j) = make_uint4(pu[g8 / 2], pu[g8 / 2 + 1], pu[g8 / 2 + 2], pu[g8 / 2 + 3]);
+              *reinterpret_cast<uint4*>(hrow + p.F + j) =
+                  make_uint4(pg[g8 / 2], pg[g8 / 2 + 1], pg[g8 / 2 + 2], pg[g8 / 2 + 3]);
+              *reinterpret_cast<uint4*>(arow + j) = make_uint4(ha[0], ha[1], ha[2], ha[3]);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                if (j + e >= p.F) continue;
+                const int sh = (e & 1) * 16;
+                hrow[j + e] = __ushort_as_bfloat16((unsigned short)(pu[g8 / 2 + e / 2] >> sh));
+                hrow[p.F + j + e] = __ushort_as_bfloat16((unsigned short)(pg[g8 / 2 + e / 2] >> sh));
+                arow[j + e] = __ushort_as_bfloat16((unsigned short)(ha[e >> 1] >> sh));
+              }
+            }
+          }
+        }
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+        continue;
+      }
       const uint32_t t_acc = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + cpart * BNH;
 #pragma unroll 1
       for (int c = 0; c < BNH; c += 32) {
@@ -1214,6 +1273,59 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS
         }
         const int col = n0 + c;
         if (!row_ok || col >= p.N) continue;
+        if (p.epi == 2) {
+          // SwiGLU backward: da (rounded to bf16, as stored by the unfused path) never leaves TMEM;
+          // dh = (da * silu(g), da * u * silu'(g)) with the saved h = (u, g)
+          const __nv_bfloat16* hr = p.h + (long long)row * p.ldh;
+          __nv_bfloat16* dh = p.aux + (long long)row * p.ldaux;
+#pragma unroll
+          for (int g8 = 0; g8 < 32; g8 += 8) {
+            const int j = col + g8;
+            if (j >= p.N) break;
+            float u[8], gt[8];
+            if (j + 8 <= p.N && p.vec_ok) {
+              const uint4 uu = *reinterpret_cast<const uint4*>(hr + j);
+              const uint4 gg = *reinterpret_cast<const uint4*>(hr + p.F + j);
+              const uint32_t uw[4] = {uu.x, uu.y, uu.z, uu.w}, gw[4] = {gg.x, gg.y, gg.z, gg.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 a2 = unpack_bf16(uw[e]), b2 = unpack_bf16(gw[e]);
+                u[2 * e] = a2.x;
+                u[2 * e + 1] = a2.y;
+                gt[2 * e] = b2.x;
+                gt[2 * e + 1] = b2.y;
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                u[e] = j + e < p.N ? __bfloat162float(hr[j + e]) : 0.f;
+                gt[e] = j + e < p.N ? __bfloat162float(hr[p.F + j + e]) : 0.f;
+              }
+            }
+            uint32_t du[4], dg[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 d2 = unpack_bf16(pack_bf16(__uint_as_float(r[g8 + 2 * e]), __uint_as_float(r[g8 + 2 * e + 1])));
+              const float s0 = sigmoid_f(gt[2 * e]), s1 = sigmoid_f(gt[2 * e + 1]);
+              du[e] = pack_bf16(d2.x * gt[2 * e] * s0, d2.y * gt[2 * e + 1] * s1);
+              dg[e] = pack_bf16(d2.x * u[2 * e] * s0 * (1.f + gt[2 * e] * (1.f - s0)),
+                                d2.y * u[2 * e + 1] * s1 * (1.f + gt[2 * e + 1] * (1.f - s1)));
+            }
+            if (j + 8 <= p.N && p.vec_ok) {
+              *reinterpret_cast<uint4*>(dh + j) = make_uint4(du[0], du[1], du[2], du[3]);
+              *reinterpret_cast<uint4*>(dh + p.F + j) = make_uint4(dg[0], dg[1], dg[2], dg[3]);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                if (j + e >= p.N) continue;
+                const int sh = (e & 1) * 16;
+                dh[j + e] = __ushort_as_bfloat16((unsigned short)(du[e >> 1] >> sh));
+                dh[p.F + j + e] = __ushort_as_bfloat16((unsigned short)(dg[e >> 1] >> sh));
+              }
+            }
+          }
+          continue;
+        }
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
@@ -1783,7 +1895,10 @@ void gemm_swiglu_bf16(int mode, const void* A, long long lda, const void* B, lon
   cudaGetDevice(&dev);
   const int sms = num_sms(dev);
   const int BN = 256;
-  const int BM = 128;  // the fused epilogues run on 128-row tiles (double-buffered accumulator)
+  // 256-row tiles on a CTA pair (double-buffered accumulators, see gemm_pair_kernel) where the pair
+  // policy applies, else 128-row single-CTA tiles (double-buffered accumulator)
+  const bool pair = M > 128 && pair_on();
+  const int BM = pair ? 256 : 128;
   if (mode == 2 && F <= 128) throw std::runtime_error("gemm_swiglu mode 2: F > 128");
   CUtensorMap ta, tb;
   {
@@ -1797,7 +1912,7 @@ void gemm_swiglu_bf16(int mode, const void* A, long long lda, const void* B, lon
     const uint64_t inner = mode == 1 ? (uint64_t)K : (b_mn ? (uint64_t)F : (uint64_t)K);
     uint64_t dims[3] = {inner, rows, 1};
     uint64_t strides[2] = {(uint64_t)ldb * 2, rows * ldb * 2};
-    const uint32_t box_rows = mode == 1 ? (uint32_t)(BN / 2) : (b_mn ? 64u : (uint32_t)BN);
+    const uint32_t box_rows = mode == 1 ? (uint32_t)(BN / 2) : (b_mn ? 64u : (uint32_t)(pair ? BN / 2 : BN));
     uint32_t box[3] = {64, box_rows, 1};
     make_tmap_bf16(&tb, B, 3, dims, strides, box, true);
   }
@@ -1849,6 +1964,8 @@ void gemm_swiglu_bf16(int mode, const void* A, long long lda, const void* B, lon
   p.scatter_rank = 0;
   p.scatter_recv_off = 0;
   const int tiles = p.tiles_m * p.tiles_n;
+  if (pair)
+    return dispatch_pair<256>(0, mode == 1 ? 0 : b_mn, 0, ta, tb, p, std::min(tiles, pair_clusters(dev)), stream);
   const int grid = std::min(tiles, sms);
   dispatch_majors<128, 256>(0, mode == 1 ? 0 : b_mn, 0, ta, tb, p, grid, stream);
 }

@@ -61,6 +61,11 @@ SKINNY_MAX_ROWS = 16
 # carry the extra memory traffic, and the larger 256-row tiles cannot hold the registers), so the
 # separate full-GPU kernels are the default; set ASTRAI_FUSED_EPILOGUES=1 to use the fused ones.
 FUSED_EPILOGUES = __import__("os").environ.get("ASTRAI_FUSED_EPILOGUES", "0") == "1"
+# The SwiGLU pair alone (ASTRAI_FUSED_SWIGLU=1): its GEMMs run on 256-row CTA-pair tiles, whose
+# accumulators are double-buffered like the 128-row tiles', so the epilogue work overlaps the MMAs.
+# Still measured slower in the 1.1B step on B200 (613 - 618 vs 586 - 590 ms per optimizer step, two
+# runs each on one box), so it stays opt-in.
+FUSED_SWIGLU = FUSED_EPILOGUES or __import__("os").environ.get("ASTRAI_FUSED_SWIGLU", "0") == "1"
 
 
 def _skinny(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
@@ -270,7 +275,7 @@ def swiglu_mlp(x: torch.Tensor, up: torch.Tensor, gate: torch.Tensor, down: torc
     """Fused SwiGLU MLP on the kernel path, or None when it does not apply (then compose
     :func:`packed_linear`, :func:`astrai_b200.ops.activation.swiglu` and :func:`linear`)."""
     params = (up, gate, down)
-    if not FUSED_EPILOGUES:
+    if not FUSED_SWIGLU:
         return None
     if not (x.is_cuda and x.dtype == torch.bfloat16 and all(
             p.is_cuda and p.dtype == torch.bfloat16 and type(p.data) is torch.Tensor for p in params)):

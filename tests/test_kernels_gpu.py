@@ -390,14 +390,15 @@ def test_skinny_gemm(M, N, K):
     assert rel_err(y, ref) < 1e-2
 
 
-@pytest.mark.parametrize("M,d,Fw", [(512, 256, 384), (300, 512, 1408), (2048, 2048, 5632)])
+@pytest.mark.parametrize("M,d,Fw", [(128, 256, 384), (512, 256, 384), (300, 512, 1408), (2048, 2048, 5632)])
 def test_swiglu_mlp_fused_epilogues(M, d, Fw):
     """Fused SwiGLU MLP (paired up/gate tiles writing h and a; dh from the down data-gradient
-    epilogue) against an fp32 reference, with weight gradients accumulated over two calls."""
+    epilogue) against an fp32 reference, with weight gradients accumulated over two calls. M > 128
+    runs the CTA-pair kernel's epilogues, M = 128 the single-CTA kernel's."""
     import astrai_b200.ops.gemm as G
     from astrai_b200.ops.gemm import swiglu_mlp
 
-    G.FUSED_EPILOGUES = True  # the test exercises the fused kernels whatever the default
+    G.FUSED_SWIGLU = True  # the test exercises the fused kernels whatever the default
     torch.manual_seed(M)
     up, gate = (torch.nn.Parameter((torch.randn(Fw, d, device="cuda") * d ** -0.5).to(torch.bfloat16))
                 for _ in range(2))
