@@ -23,8 +23,11 @@
 // dw; order them on one stream or serialise them.
 //
 // Setup: the first call on each device looks up the array's device address
-// (cudaGetSymbolAddress) with that device current. Make that first call before
-// any stream capture begins.
+// (cudaGetSymbolAddress) with that device current, and keeps it for the life
+// of the process (a failed lookup is not kept; the next call tries again).
+// Make that first call before any stream capture begins. A device reset
+// (cudaDeviceReset, or a reset of the primary context) after the first call is
+// not supported: the kept address would be stale.
 //
 // Arguments: bf16 row-major dy / x / dx with row strides in elements (16-byte
 // aligned rows), bf16 weight w [D], fp32 rstd [rows] from the forward pass;
@@ -32,8 +35,11 @@
 // stream is a cudaStream_t (NULL = legacy default stream). D must be a
 // multiple of 8 and at most 4096.
 //
-// Returns 0 on success, -1 for rejected sizes, otherwise the cudaError_t of
-// the failing setup call or launch.
+// Returns 0 on success, -1 for rejected sizes, otherwise a cudaError_t: of
+// the failing setup call, or the calling thread's pending runtime error after
+// the launches (cudaGetLastError). That pending error can also be one that an
+// earlier, unrelated runtime call of the same thread left behind; this call
+// reports and clears it. Check your own calls' errors before calling this.
 #ifndef ASTRAI_C_API_H_
 #define ASTRAI_C_API_H_
 

@@ -406,15 +406,21 @@ static __device__ __align__(256) float g_rmsnorm_bwd_scratch[ASTRAI_RMSNORM_BWD_
 
 constexpr int kMaxDevices = 64;
 float* g_scratch_ptr[kMaxDevices] = {};
-cudaError_t g_setup_err[kMaxDevices] = {};
-std::once_flag g_setup_once[kMaxDevices];
+std::mutex g_setup_mutex;
 
-// Once per device, with that device current: the array's address. Allocates nothing.
-void static_scratch_setup(int dev) {
-  float* p = nullptr;
-  const cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_rmsnorm_bwd_scratch);
-  g_setup_err[dev] = e;
-  g_scratch_ptr[dev] = e == cudaSuccess ? p : nullptr;
+// The array's device address on the current device `dev`. Looked up once per device with that device
+// current and kept for the life of the process; a failed lookup is not kept, so a later call retries.
+// Allocates nothing.
+cudaError_t static_scratch_address(int dev, float** out) {
+  std::lock_guard<std::mutex> lock(g_setup_mutex);
+  if (g_scratch_ptr[dev] == nullptr) {
+    float* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_rmsnorm_bwd_scratch);
+    if (e != cudaSuccess) return e;
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return cudaSuccess;
 }
 
 }  // namespace
@@ -449,10 +455,12 @@ extern "C" int astrai_rmsnorm_bwd_static_scratch(const void* dy, long long lddy,
                  kMaxDevices);
     return -1;
   }
-  std::call_once(g_setup_once[dev], static_scratch_setup, dev);
-  if (g_setup_err[dev] != cudaSuccess) return static_cast<int>(g_setup_err[dev]);
-  astrai_host::rmsnorm_bwd_launch(dy, lddy, x, ldx, w, rstd, dx, lddx, nullptr, 0, dw_bf16, dw_f32,
-                                  g_scratch_ptr[dev], rows, D, static_cast<int>(nb), rpb,
-                                  static_cast<cudaStream_t>(stream));
+  float* scratch = nullptr;
+  e = static_scratch_address(dev, &scratch);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  astrai_host::rmsnorm_bwd_launch(dy, lddy, x, ldx, w, rstd, dx, lddx, nullptr, 0, dw_bf16, dw_f32, scratch, rows,
+                                  D, static_cast<int>(nb), rpb, static_cast<cudaStream_t>(stream));
+  // the runtime's per-thread last error: this call's launches, or an error that earlier runtime calls
+  // of the calling thread left pending (reported and cleared here, as the header states)
   return static_cast<int>(cudaGetLastError());
 }

@@ -72,15 +72,47 @@ def test_static_scratch_matches_regular_entry_point_twice(rows, D):
         torch.testing.assert_close(dw, (gf * xf * r).sum(0), atol=5e-2, rtol=1e-3)
 
 
+def test_static_scratch_bf16_dw_on_the_legacy_default_stream():
+    """dw written as bf16 as well, launched on the legacy default stream (stream = NULL)."""
+    fn = _entry()
+    rows, D = 2048, 2048
+    for seed in (5, 6):
+        x, dy, w, rstd = _case(rows, D, seed)
+        dx = torch.empty_like(x)
+        dw32 = torch.empty(D, device="cuda", dtype=torch.float32)
+        dw16 = torch.empty(D, device="cuda", dtype=torch.bfloat16)
+        torch.cuda.synchronize()  # inputs were made on torch's current stream
+        rc = fn(dy.data_ptr(), D, x.data_ptr(), D, w.data_ptr(), rstd.data_ptr(), dx.data_ptr(), D,
+                dw16.data_ptr(), dw32.data_ptr(), rows, D, None)
+        assert rc == 0
+        torch.cuda.synchronize()
+        dx_ref, dw_ref = _regular(x, dy, w, rstd)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(dw32, dw_ref, atol=1e-3, rtol=1e-4)
+        torch.testing.assert_close(dw16, dw32.to(torch.bfloat16), atol=0, rtol=0)
+        torch.testing.assert_close(dx.float(), dx_ref.float(), atol=1e-2, rtol=1e-2)
+
+
+def _buffers(rows, D):
+    """Inputs and outputs sized for the claimed (rows, D): if the size rule ever let the call through,
+    the kernels would stay inside these buffers and only the assertion would fail."""
+    x = torch.zeros(rows, D, device="cuda", dtype=torch.bfloat16)
+    dy = torch.zeros_like(x)
+    dx = torch.empty_like(x)
+    w = torch.ones(D, device="cuda", dtype=torch.bfloat16)
+    rstd = torch.ones(rows, device="cuda", dtype=torch.float32)
+    dw = torch.empty(D, device="cuda", dtype=torch.float32)
+    return x, dy, dx, w, rstd, dw
+
+
 def test_static_scratch_rejects_oversized_problems():
     fn = _entry()
-    x, dy, w, rstd = _case(64, 2048, 0)
-    dx = torch.empty_like(x)
-    dw = torch.empty(2048, device="cuda", dtype=torch.float32)
     s = torch.cuda.current_stream().cuda_stream
-    too_many_rows = 64 * ((1 << 20) // 2048) + 1  # one block more than the array holds
-    assert fn(dy.data_ptr(), 2048, x.data_ptr(), 2048, w.data_ptr(), rstd.data_ptr(), dx.data_ptr(), 2048, None,
-              dw.data_ptr(), too_many_rows, 2048, s) == -1
-    assert fn(dy.data_ptr(), 2048, x.data_ptr(), 2048, w.data_ptr(), rstd.data_ptr(), dx.data_ptr(), 2048, None,
-              dw.data_ptr(), 64, 8192, s) == -1
+    too_many_rows = 64 * ((1 << 20) // 2048) + 1  # one 64-row block more than the array holds at D = 2048
+    for rows, D in ((too_many_rows, 2048), (64, 8192)):  # ~134 MB per bf16 tensor for the first case
+        x, dy, dx, w, rstd, dw = _buffers(rows, D)
+        rc = fn(dy.data_ptr(), D, x.data_ptr(), D, w.data_ptr(), rstd.data_ptr(), dx.data_ptr(), D, None,
+                dw.data_ptr(), rows, D, s)
+        assert rc == -1, (rows, D, rc)
+        del x, dy, dx, w, rstd, dw
     torch.cuda.synchronize()
