@@ -1,21 +1,26 @@
-"""Datasets per training type (parity: astrai/dataset/dataset.py:43-506).
+"""Training datasets: a :class:`Store` plus the key mapping of one training type.
 
-* ``seq``  - stream windows; ``input_ids`` and the +1-shifted ``target_ids``;
-* ``sft``  - as seq plus ``position_ids`` and the shifted ``loss_mask``;
-* ``dpo``  - one preference pair per record (``chosen``, ``rejected`` and
-  their masks); raw JSONL is tokenised lazily through the chat template;
-* ``grpo`` - one prompt with G responses, masks and rewards per record.
+Public names kept from the reference (astrai/dataset/dataset.py:43-506): ``BaseDataset``,
+``DatasetFactory`` (keys ``seq``, ``sft``, ``dpo``, ``grpo``), the four dataset classes,
+``dpo_tokenize``, ``dpo_processor``, ``dpo_collate_fn`` and ``grpo_collate_fn``.
 
-``DatasetFactory.load(train_type, load_path, window_size, stride, ...)``
-builds the store (format auto-detected) and the dataset; ``dpo_collate_fn``
-right-pads pairs, ``grpo_collate_fn`` left-pads prompts and right-pads
-responses.
+Each dataset class is declarative:
+
+* window datasets (``seq``, ``sft``) list ``fields``: output name, store key, target shift
+  (0 for inputs, 1 for next-token targets) and dtype. Sample ``i`` takes the store's window
+  ``[b, e)`` for shift 0 and ``[b + 1, e + 1)`` for shift 1;
+* record datasets (``dpo``, ``grpo``) list ``casts``: store key and dtype of one record's
+  tensors (lists of tensors for GRPO's nested keys).
+
+``DatasetFactory.load`` detects the storage format, picks the window (record types always
+read whole records), builds a lazy DPO processor for raw JSONL when a tokenizer is given,
+loads the store and wraps it.
 """
 
 from __future__ import annotations
 
 from functools import partial
-from typing import Callable, Dict, List, Optional
+from typing import Callable, Dict, List, Optional, Sequence, Tuple
 
 import torch
 from torch.utils.data import Dataset
@@ -23,104 +28,114 @@ from torch.utils.data import Dataset
 from astrai_b200.dataset.storage import Store, StoreFactory, detect_format
 from astrai_b200.factory import Registry
 
-
-def _to_messages(v) -> list:
-    if isinstance(v, str):
-        return [{"role": "user", "content": v}]
-    if isinstance(v, list):
-        return v
-    return [{"role": "user", "content": str(v)}]
+# ---------------------------------------------------------------------------------------- DPO records
 
 
-def _text(v) -> Optional[str]:
-    if v is None:
-        return None
-    if isinstance(v, str):
-        return v
-    if isinstance(v, list):
-        return "".join(m.get("content", "") for m in v if isinstance(m, dict))
+def _as_turns(prompt) -> List[dict]:
+    """A prompt given as a string (one user turn), a message list, or anything else (stringified)."""
+    if isinstance(prompt, list):
+        return prompt
+    return [{"role": "user", "content": prompt if isinstance(prompt, str) else str(prompt)}]
+
+
+def _response_text(resp) -> Optional[str]:
+    """A response given as a string or as a message list (contents joined)."""
+    if isinstance(resp, str):
+        return resp
+    if isinstance(resp, list):
+        return "".join(m.get("content", "") for m in resp if isinstance(m, dict))
     return None
 
 
 def dpo_tokenize(record: dict, tokenizer, max_len: int = 2048) -> Optional[dict]:
-    """Prompt rendered with the generation prompt, chosen / rejected appended as
-    one assistant turn; masks cover the response tokens only."""
+    """One preference record -> token ids and response masks, or None if a field is missing.
+
+    Accepted records: ``{"prompt" | "input": str or messages, "chosen": str or messages,
+    "rejected": ...}``. The prompt is rendered with the generation prompt; each response is
+    appended as one assistant turn. Masks are 1 on response tokens only; every list is cut
+    to ``max_len``."""
     prompt = record.get("prompt") or record.get("input")
-    ch, rj = _text(record.get("chosen")), _text(record.get("rejected"))
-    if prompt is None or ch is None or rj is None:
+    answers = [_response_text(record.get("chosen")), _response_text(record.get("rejected"))]
+    if prompt is None or None in answers:
         return None
-    pm = _to_messages(prompt)
-    p_ids = tokenizer.apply_chat_template(pm, tokenize=True, add_generation_prompt=True)
-    c_ids = tokenizer.apply_chat_template(pm + [{"role": "assistant", "content": ch}], tokenize=True,
-                                          add_generation_prompt=False)[:max_len]
-    r_ids = tokenizer.apply_chat_template(pm + [{"role": "assistant", "content": rj}], tokenize=True,
-                                          add_generation_prompt=False)[:max_len]
-    pl = min(len(p_ids), max_len)
-
-    def mask(ids):
-        return ([0] * pl + [1] * max(0, len(ids) - pl))[:max_len]
-
-    return {"chosen": c_ids, "rejected": r_ids, "chosen_mask": mask(c_ids), "rejected_mask": mask(r_ids)}
-
-
-def dpo_processor(record: dict, tokenizer, max_len: int = 2048) -> Dict[str, torch.Tensor]:
-    r = dpo_tokenize(record, tokenizer, max_len=max_len)
-    if r is None:
-        raise ValueError(f"Malformed DPO record: {list(record.keys())}")
-    return {"chosen": torch.tensor(r["chosen"], dtype=torch.int32),
-            "rejected": torch.tensor(r["rejected"], dtype=torch.int32),
-            "chosen_mask": torch.tensor(r["chosen_mask"], dtype=torch.bool),
-            "rejected_mask": torch.tensor(r["rejected_mask"], dtype=torch.bool)}
-
-
-def dpo_collate_fn(batch: List[Dict[str, torch.Tensor]]) -> Dict[str, torch.Tensor]:
-    B = len(batch)
-    S = max(max(b["chosen"].size(0), b["rejected"].size(0)) for b in batch)
-    out = {"chosen": torch.zeros(B, S, dtype=torch.long), "rejected": torch.zeros(B, S, dtype=torch.long),
-           "chosen_mask": torch.zeros(B, S, dtype=torch.bool), "rejected_mask": torch.zeros(B, S, dtype=torch.bool)}
-    for i, b in enumerate(batch):
-        for k in ("chosen", "rejected"):
-            n = b[k].size(0)
-            out[k][i, :n] = b[k]
-            out[k + "_mask"][i, :n] = b[k + "_mask"]
+    turns = _as_turns(prompt)
+    n_prompt = min(len(tokenizer.apply_chat_template(turns, tokenize=True, add_generation_prompt=True)), max_len)
+    out = {}
+    for name, text in zip(("chosen", "rejected"), answers):
+        ids = tokenizer.apply_chat_template(turns + [{"role": "assistant", "content": text}], tokenize=True,
+                                            add_generation_prompt=False)[:max_len]
+        out[name] = ids
+        out[name + "_mask"] = [int(i >= n_prompt) for i in range(len(ids))]
     return out
 
 
+def dpo_processor(record: dict, tokenizer, max_len: int = 2048) -> Dict[str, torch.Tensor]:
+    """:func:`dpo_tokenize` as tensors (ids int32, masks bool); raises on an unusable record."""
+    tok = dpo_tokenize(record, tokenizer, max_len=max_len)
+    if tok is None:
+        raise ValueError("DPO record needs 'prompt' (or 'input'), 'chosen' and 'rejected'; "
+                         f"this one has {sorted(record)}")
+    return {k: torch.tensor(v, dtype=torch.bool if k.endswith("_mask") else torch.int32) for k, v in tok.items()}
+
+
+# ---------------------------------------------------------------------------------------- collate
+
+
+def _pad_rows(rows: Sequence[torch.Tensor], width: int, dtype, left: bool = False) -> torch.Tensor:
+    out = torch.zeros(len(rows), width, dtype=dtype)
+    for i, r in enumerate(rows):
+        n = r.shape[0]
+        if n:
+            (out[i, width - n:] if left else out[i, :n]).copy_(r)
+    return out
+
+
+def dpo_collate_fn(batch: List[Dict[str, torch.Tensor]]) -> Dict[str, torch.Tensor]:
+    """Right-pad chosen / rejected ids and masks of a batch to one common length [B, S]."""
+    width = max(s[k].shape[0] for s in batch for k in ("chosen", "rejected"))
+    return {k: _pad_rows([s[k] for s in batch], width, torch.bool if k.endswith("_mask") else torch.long)
+            for k in ("chosen", "rejected", "chosen_mask", "rejected_mask")}
+
+
 def grpo_collate_fn(batch: List[Dict[str, torch.Tensor]]) -> Dict[str, torch.Tensor]:
-    B, G = len(batch), len(batch[0]["responses"])
-    P = max(b["prompts"].size(0) for b in batch)
-    R = max(r.size(0) for b in batch for r in b["responses"])
-    prompts = torch.zeros(B, P, dtype=torch.long)
-    pmask = torch.zeros(B, P, dtype=torch.bool)
-    resp = torch.zeros(B, G, R, dtype=torch.long)
-    masks = torch.zeros(B, G, R, dtype=torch.bool)
-    rewards = torch.zeros(B, G, dtype=torch.float32)
-    for i, b in enumerate(batch):
-        n = b["prompts"].size(0)
-        prompts[i, P - n:] = b["prompts"]
-        pmask[i, P - n:] = True
-        rewards[i, : b["rewards"].size(0)] = b["rewards"]
-        for g in range(min(G, len(b["responses"]))):
-            m = b["responses"][g].size(0)
-            resp[i, g, :m] = b["responses"][g]
-            if g < len(b["masks"]):
-                masks[i, g, :m] = b["masks"][g]
+    """Prompts left-padded to [B, P] (with ``prompt_mask``), the G responses per prompt and
+    their masks right-padded to [B, G, R], rewards [B, G] (missing entries stay 0)."""
+    G = len(batch[0]["responses"])
+    P = max(s["prompts"].shape[0] for s in batch)
+    R = max(r.shape[0] for s in batch for r in s["responses"])
+    prompts = _pad_rows([s["prompts"] for s in batch], P, torch.long, left=True)
+    pmask = _pad_rows([torch.ones(s["prompts"].shape[0], dtype=torch.bool) for s in batch], P, torch.bool,
+                      left=True)
+    resp = torch.zeros(len(batch), G, R, dtype=torch.long)
+    masks = torch.zeros(len(batch), G, R, dtype=torch.bool)
+    rewards = torch.zeros(len(batch), G)
+    for i, s in enumerate(batch):
+        resp[i, :len(s["responses"][:G])] = _pad_rows(s["responses"][:G], R, torch.long)
+        masks[i, :len(s["masks"][:G])] = _pad_rows(s["masks"][:G], R, torch.bool)
+        r = s["rewards"][:G]
+        rewards[i, :r.shape[0]] = r
     return {"prompts": prompts, "prompt_mask": pmask, "responses": resp, "masks": masks, "rewards": rewards}
 
 
-def validate_keys(store: Store, required: List[str]) -> None:
-    missing = [k for k in required if k not in set(store.keys)]
+# ---------------------------------------------------------------------------------------- datasets
+
+
+def validate_keys(store: Store, required: Sequence[str]) -> None:
+    have = set(store.keys)
+    missing = [k for k in required if k not in have]
     if missing:
-        raise KeyError(f"Store is missing required keys {missing}; available keys are {sorted(store.keys)}.")
+        raise KeyError(f"the store lacks {missing} (it has {sorted(have)})")
 
 
 class BaseDataset(Dataset):
+    """A store checked for the keys this dataset reads."""
+
     required_keys: List[str] = []
 
     def __init__(self, store: Store):
         super().__init__()
-        self.store = store
         validate_keys(store, self.required_keys)
+        self.store = store
 
     def __len__(self) -> int:
         return len(self.store)
@@ -133,84 +148,95 @@ class BaseDataset(Dataset):
     def token_count(self) -> int:
         return self.store.token_count
 
-    def __getitem__(self, index: int) -> Dict[str, torch.Tensor]:  # pragma: no cover - abstract
-        raise NotImplementedError
+    def __getitem__(self, index: int) -> Dict[str, torch.Tensor]:  # pragma: no cover - per dataset
+        raise NotImplementedError(f"{type(self).__name__} does not define samples")
+
+
+class _WindowDataset(BaseDataset):
+    #: (output name, store key, shift, dtype)
+    fields: Tuple[Tuple[str, str, int, torch.dtype], ...] = ()
+
+    def __init_subclass__(cls, **kw):
+        super().__init_subclass__(**kw)
+        cls.required_keys = sorted({key for _, key, _, _ in cls.fields})
+
+    def __getitem__(self, index: int) -> Dict[str, torch.Tensor]:
+        b, e = self.store.sample_window(index)
+        return {name: self.store.fetch(b + shift, e + shift, key).to(dtype) for name, key, shift, dtype in self.fields}
+
+
+class _RecordDataset(BaseDataset):
+    #: (store key, dtype); nested keys come back as lists of tensors
+    casts: Tuple[Tuple[str, torch.dtype], ...] = ()
+
+    def __init_subclass__(cls, **kw):
+        super().__init_subclass__(**kw)
+        cls.required_keys = [k for k, _ in cls.casts]
+
+    def __getitem__(self, index: int) -> Dict[str, torch.Tensor]:
+        rec = self.store.fetch_record(index, self.required_keys)
+        out = {}
+        for key, dtype in self.casts:
+            v = rec[key]
+            out[key] = [t.to(dtype) for t in v] if isinstance(v, list) else v.to(dtype)
+        return out
 
 
 class DatasetFactory(Registry["BaseDataset"]):
+    #: training types that read whole records, never windows
+    RECORD_TYPES = ("dpo", "grpo")
+
     @classmethod
     def load(cls, train_type: str, load_path: Optional[str] = None, window_size: int = 0, stride: Optional[int] = None,
              storage_type: Optional[str] = None, tokenizer_path: Optional[str] = None, max_len: int = 2048,
              store: Optional[Store] = None, **kwargs) -> BaseDataset:
-        if store is not None:
-            return cls.create(train_type, store=store)
-        if load_path is None:
-            raise ValueError("Either load_path or store must be provided")
-        storage_type = storage_type or detect_format(load_path)
-        stride = stride or window_size
-        processor = cls._maybe_build_processor(train_type, storage_type, tokenizer_path, max_len)
-        win = window_size if train_type in ("seq", "sft") else 0
-        st = StoreFactory.create(storage_type, window_size=win, stride=stride if stride else win)
-        if processor is not None:
-            st.load(load_path, processor=processor, **kwargs)
-        else:
-            kw = dict(kwargs)
-            if tokenizer_path and storage_type == "jsonl" and train_type in ("seq", "sft"):
+        """Dataset of ``train_type`` over ``store``, or over a store loaded from ``load_path``."""
+        if store is None:
+            if load_path is None:
+                raise ValueError("DatasetFactory.load needs a load_path to read, or a ready store=")
+            store = cls._open_store(train_type, load_path, window_size, stride, storage_type, tokenizer_path,
+                                    max_len, kwargs)
+        return cls.create(train_type, store=store)
+
+    @classmethod
+    def _open_store(cls, train_type, load_path, window_size, stride, storage_type, tokenizer_path, max_len,
+                    load_kw) -> Store:
+        fmt = storage_type or detect_format(load_path)
+        window = 0 if train_type in cls.RECORD_TYPES else window_size
+        st = StoreFactory.create(fmt, window_size=window, stride=(stride or window_size) if window else 0)
+        kw = dict(load_kw)
+        if fmt == "jsonl" and tokenizer_path:
+            if train_type == "dpo":
+                from astrai_b200.tokenize import AutoTokenizer
+
+                kw["processor"] = partial(dpo_processor, tokenizer=AutoTokenizer.from_pretrained(tokenizer_path),
+                                          max_len=max_len)
+            elif train_type in ("seq", "sft"):
                 kw.setdefault("tokenizer_path", tokenizer_path)
-            st.load(load_path, **kw)
-        return cls.create(train_type, store=st)
-
-    @staticmethod
-    def _maybe_build_processor(train_type, storage_type, tokenizer_path, max_len) -> Optional[Callable]:
-        if tokenizer_path is None or storage_type != "jsonl" or train_type != "dpo":
-            return None
-        from astrai_b200.tokenize import AutoTokenizer
-
-        return partial(dpo_processor, tokenizer=AutoTokenizer.from_pretrained(tokenizer_path), max_len=max_len)
+        st.load(load_path, **kw)
+        return st
 
 
 @DatasetFactory.register("seq")
-class SEQDataset(BaseDataset):
-    required_keys = ["sequence"]
-
-    def __getitem__(self, index: int):
-        b, e = self.store.sample_window(index)
-        return {"input_ids": self.store.fetch(b, e, "sequence").to(torch.long),
-                "target_ids": self.store.fetch(b + 1, e + 1, "sequence").to(torch.long)}
+class SEQDataset(_WindowDataset):
+    fields = (("input_ids", "sequence", 0, torch.long), ("target_ids", "sequence", 1, torch.long))
 
 
 @DatasetFactory.register("sft")
-class SFTDataset(BaseDataset):
-    required_keys = ["sequence", "loss_mask", "position_ids"]
-
-    def __getitem__(self, index: int):
-        b, e = self.store.sample_window(index)
-        return {"input_ids": self.store.fetch(b, e, "sequence").to(torch.long),
-                "target_ids": self.store.fetch(b + 1, e + 1, "sequence").to(torch.long),
-                "position_ids": self.store.fetch(b, e, "position_ids").to(torch.long),
-                "loss_mask": self.store.fetch(b + 1, e + 1, "loss_mask").to(torch.bool)}
+class SFTDataset(_WindowDataset):
+    fields = (("input_ids", "sequence", 0, torch.long), ("target_ids", "sequence", 1, torch.long),
+              ("position_ids", "position_ids", 0, torch.long), ("loss_mask", "loss_mask", 1, torch.bool))
 
 
 @DatasetFactory.register("dpo")
-class DPODataset(BaseDataset):
-    required_keys = ["chosen", "rejected", "chosen_mask", "rejected_mask"]
+class DPODataset(_RecordDataset):
+    casts = (("chosen", torch.long), ("rejected", torch.long), ("chosen_mask", torch.bool),
+             ("rejected_mask", torch.bool))
 
-    def make_processor(self, tokenizer, max_len: int):
+    def make_processor(self, tokenizer, max_len: int) -> Callable[[dict], Dict[str, torch.Tensor]]:
         return partial(dpo_processor, tokenizer=tokenizer, max_len=max_len)
-
-    def __getitem__(self, index: int):
-        r = self.store.fetch_record(index, self.required_keys)
-        return {"chosen": r["chosen"].to(torch.long), "rejected": r["rejected"].to(torch.long),
-                "chosen_mask": r["chosen_mask"].to(torch.bool), "rejected_mask": r["rejected_mask"].to(torch.bool)}
 
 
 @DatasetFactory.register("grpo")
-class GRPODataset(BaseDataset):
-    required_keys = ["prompts", "responses", "masks", "rewards"]
-
-    def __getitem__(self, index: int):
-        r = self.store.fetch_record(index, self.required_keys)
-        return {"prompts": r["prompts"].to(torch.long),
-                "responses": [x.to(torch.long) for x in r["responses"]],
-                "masks": [x.to(torch.bool) for x in r["masks"]],
-                "rewards": r["rewards"].to(torch.float32)}
+class GRPODataset(_RecordDataset):
+    casts = (("prompts", torch.long), ("responses", torch.long), ("masks", torch.bool), ("rewards", torch.float32))

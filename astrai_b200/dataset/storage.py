@@ -1,32 +1,36 @@
-"""Token stores (parity: astrai/dataset/storage.py:71-664).
+"""Token stores: where a dataset's tokens live and how sample indices map onto them.
 
-A store owns the tokens of a dataset and the sample-index arithmetic:
+Public names kept from the reference (astrai/dataset/storage.py:71-664): ``Store``,
+``StoreFactory`` (keys ``bin`` / ``h5`` / ``jsonl``), ``MmapStore``, ``H5Store``,
+``JsonlStore``, ``JsonlSource``, ``detect_format``, and the store methods the datasets call
+(``sample_window``, ``fetch``, ``fetch_record``, ``keys``, ``token_count``, ``num_records``,
+``num_samples``).
 
-* stream mode (``window_size > 0``): all shards form one token stream; the
-  number of samples is ``(total - 1 - w) // stride + 1`` and sample ``i``
-  covers ``[begin, begin + w)`` with ``begin = min(i * stride, total - 1 - w)``
-  (the +1 leaves room for the shifted next-token target). Slices spanning
-  shards are stitched by bisecting cumulative shard lengths - shards are
-  never concatenated in memory.
-* record mode: per-record tensors (H5 / JSONL segments, or ``bin`` shards
-  whose ``meta.json`` carries per-record offsets); ``len`` = record count.
+Design. A store is a dict of *columns*, one per key:
 
-Backends: ``bin`` (``np.memmap`` shards shared by all DataLoader workers
-through the page cache), ``h5`` (requires h5py), ``jsonl`` (eager
-tokenisation through a :class:`TokenizeTransform`, a ``dataset_config.json``
-next to the files, the built-in chat ``messages`` config, or lazy per-record
-tokenisation with ``processor=``). ``detect_format`` picks the backend from
-the files present.
+* :class:`_StreamColumn` - the key's shards viewed as one token stream. Shard ends are kept
+  as a prefix-sum array; a slice that spans shards is found with ``np.searchsorted`` and
+  stitched from views, so shards are never concatenated in memory (``bin`` shards stay
+  memory-mapped and shared by DataLoader workers through the page cache);
+* :class:`_RecordColumn` - per-record access, either one tensor per record or one flat tensor
+  cut at recorded offsets (``bin`` shards written with ``record_keys``);
+* :class:`_NestedColumn` - a list of tensor lists per record (GRPO responses).
+
+Stream mode (``window_size > 0``) is a contract shared with checkpoints (resuming at a sample
+index must see the same tokens): with ``T`` stream tokens, ``w`` the window and ``s`` the
+stride, there are ``(T - 1 - w) // s + 1`` samples, and sample ``i`` covers
+``[b, b + w)`` with ``b = min(i * s, T - 1 - w)``; the spare token is the last target.
+Record mode (``window_size == 0``): one sample per record.
 """
 
 from __future__ import annotations
 
-import bisect
 import json
 import logging
 from pathlib import Path
-from typing import Callable, Dict, List, Optional, Tuple, Union
+from typing import Callable, Dict, Iterable, List, Optional, Sequence, Tuple, Union
 
+import numpy as np
 import torch
 
 from astrai_b200.factory import Registry
@@ -34,169 +38,206 @@ from astrai_b200.serialization import load_bin, load_bin_offsets, load_h5
 
 logger = logging.getLogger(__name__)
 
+Keys = Union[str, Sequence[str]]
+
+_SUFFIX_FORMAT = {".h5": "h5", ".hdf5": "h5", ".jsonl": "jsonl"}
+
 
 def detect_format(load_path: str) -> str:
+    """``bin`` / ``h5`` / ``jsonl`` from a file's suffix or a directory's contents
+    (h5 files win over bin shards, which win over jsonl files)."""
     root = Path(load_path)
     if root.is_file():
-        suf = root.suffix.lower()
-        if suf in (".h5", ".hdf5"):
-            return "h5"
-        if suf == ".jsonl":
-            return "jsonl"
-        raise ValueError(f"Unsupported file format: {suf}")
-    if any(root.rglob("*.h5")) or any(root.rglob("*.hdf5")):
+        fmt = _SUFFIX_FORMAT.get(root.suffix.lower())
+        if fmt is None:
+            raise ValueError(f"cannot tell the storage format of {root.name}: expected .h5, .hdf5 or .jsonl")
+        return fmt
+    found = {p.suffix.lower() for p in root.rglob("*") if p.is_file()}
+    if ".h5" in found or ".hdf5" in found:
         return "h5"
-    if any(root.rglob("*.bin")) and any(root.rglob("meta.json")):
+    if ".bin" in found and any(root.rglob("meta.json")):
         return "bin"
-    if any(root.rglob("*.jsonl")):
+    if ".jsonl" in found:
         return "jsonl"
-    raise FileNotFoundError(f"No supported data files found at {load_path}")
+    raise FileNotFoundError(f"{load_path}: no .h5/.hdf5 files, no .bin shards with meta.json and no .jsonl files")
 
 
+# ---------------------------------------------------------------------------------------- columns
+class _StreamColumn:
+    """Shards of one key read as one stream of tokens."""
+
+    def __init__(self, shards: Sequence[torch.Tensor]):
+        self.shards = list(shards)
+        self.ends = np.cumsum([int(t.shape[0]) for t in self.shards], dtype=np.int64)
+
+    @property
+    def total(self) -> int:
+        return int(self.ends[-1]) if len(self.ends) else 0
+
+    def span(self, begin: int, end: int) -> torch.Tensor:
+        if end <= begin:
+            return self.shards[0][:0]
+        first = int(np.searchsorted(self.ends, begin, side="right"))
+        last = int(np.searchsorted(self.ends, end, side="left"))
+        pieces = []
+        for s in range(first, min(last, len(self.shards) - 1) + 1):
+            start = int(self.ends[s - 1]) if s else 0
+            pieces.append(self.shards[s][max(begin - start, 0):end - start])
+        return pieces[0] if len(pieces) == 1 else torch.cat(pieces)
+
+
+class _RecordColumn:
+    """Per-record tensors: a list of records, or one flat tensor cut at ``cuts`` (n + 1 offsets)."""
+
+    def __init__(self, records: Sequence[torch.Tensor], cuts: Optional[Sequence[int]] = None):
+        self.records = list(records)
+        self.cuts = None if cuts is None else np.asarray(cuts, dtype=np.int64)
+
+    def __len__(self) -> int:
+        return len(self.cuts) - 1 if self.cuts is not None else len(self.records)
+
+    def record(self, i: int) -> torch.Tensor:
+        if self.cuts is None:
+            return self.records[i]
+        return self.records[0][int(self.cuts[i]):int(self.cuts[i + 1])]
+
+
+class _NestedColumn(_RecordColumn):
+    """Records that are lists of tensors (e.g. GRPO responses / masks per prompt)."""
+
+
+# ---------------------------------------------------------------------------------------- store
 class Store:
-    """Common bookkeeping: segments per key, cumulative lengths, record offsets."""
+    """Columns of tokens plus the sample arithmetic of stream and record mode."""
 
+    #: True where each loaded segment is one record (h5 groups, jsonl lines); bin shards are
+    #: streams unless their meta.json carries record offsets
     segments_are_records = False
 
     def __init__(self, window_size: int = 0, stride: Optional[int] = None):
-        self._data: Dict[str, list] = {}
-        self._cum: Dict[str, List[int]] = {}
-        self._offsets: Dict[str, List[int]] = {}
-        self._length = 0
-        self._num_records = 0
-        self._window_size = int(window_size)
-        self._stride = int(stride) if stride else int(window_size)
+        self.window = max(int(window_size), 0)
+        self.step = int(stride) if stride else self.window
+        self.streams: Dict[str, _StreamColumn] = {}
+        self.records: Dict[str, _RecordColumn] = {}
+        self._order: List[str] = []
 
-    def load(self, path: str, **kwargs) -> None:  # pragma: no cover - abstract
-        raise NotImplementedError
+    def load(self, path: str, **kwargs) -> None:  # pragma: no cover - overridden by every backend
+        raise NotImplementedError(f"{type(self).__name__} does not implement load()")
 
-    # ------------------------------------------------------------------ properties
+    # ------------------------------------------------------------------ building
+    def _install(self, raw: Dict[str, list], cuts: Optional[Dict[str, Sequence[int]]] = None) -> None:
+        """Turn ``{key: [segments]}`` (and optional per-key record offsets) into columns."""
+        cuts = dict(cuts or {})
+        self.streams, self.records, self._order = {}, {}, list(raw)
+        for key, segs in raw.items():
+            if segs and isinstance(segs[0], list):
+                self.records[key] = _NestedColumn(segs)
+                continue
+            self.streams[key] = _StreamColumn(segs)
+            if key in cuts:
+                if len(segs) == 1 and len(cuts[key]) > 1:
+                    self.records[key] = _RecordColumn(segs, cuts[key])
+                else:
+                    logger.warning("record offsets of %r ignored: they need exactly one shard, found %d",
+                                   key, len(segs))
+            elif self.segments_are_records:
+                self.records[key] = _RecordColumn(segs)
+
+    # ------------------------------------------------------------------ sizes
     @property
     def keys(self) -> List[str]:
-        return list(self._data.keys())
+        return list(self._order)
 
     @property
     def window_size(self) -> int:
-        return self._window_size
+        return self.window
 
     @property
     def stride(self) -> int:
-        return self._stride
+        return self.step
 
     @property
     def token_count(self) -> int:
-        return self._length
+        """Tokens of the shortest stream key (0 when there is none)."""
+        return min((c.total for c in self.streams.values()), default=0)
 
     @property
     def num_records(self) -> int:
-        return self._num_records
+        return min((len(c) for c in self.records.values()), default=0)
+
+    @property
+    def stream_mode(self) -> bool:
+        return self.window > 0 and self.token_count > 0
 
     @property
     def num_samples(self) -> int:
-        if self._window_size > 0 and self._length > 0:
-            if self._length <= self._window_size:
-                return 0
-            return (self._length - 1 - self._window_size) // self._stride + 1
-        return self._num_records
+        if not self.stream_mode:
+            return self.num_records
+        spare = self.token_count - 1 - self.window
+        return spare // self.step + 1 if spare >= 0 else 0
 
     def __len__(self) -> int:
         return self.num_samples
 
+    # ------------------------------------------------------------------ samples
+    def sample_window(self, index: int) -> Tuple[int, int]:
+        """Token range ``[begin, end)`` of stream sample ``index`` (the contract formula)."""
+        if self.window <= 0:
+            raise RuntimeError(f"{type(self).__name__} was built with window_size=0 (record mode): no windows")
+        T, n = self.token_count, self.num_samples
+        if n == 0:
+            raise IndexError(f"{T} tokens cannot hold one window of {self.window} plus its target token")
+        if not 0 <= index < n:
+            raise IndexError(f"sample {index} requested from a store of {n} samples")
+        begin = min(index * self.step, T - 1 - self.window)
+        return begin, begin + self.window
+
     def __getitem__(self, index: int) -> Dict[str, torch.Tensor]:
         n = self.num_samples
-        if index < 0:
-            index += n
+        i = index + n if index < 0 else index
+        if not 0 <= i < n:
+            raise IndexError(f"sample {index} requested from a store of {n} samples")
+        if self.stream_mode:
+            begin, end = self.sample_window(i)
+            return self.fetch(begin, end, list(self.streams))
+        return self.fetch_record(i, self.keys)
+
+    def fetch(self, begin: int, end: int, keys: Keys):
+        """Stream tokens ``[begin, end)`` of one key (a tensor) or several (a dict)."""
+        if not self.streams:
+            raise RuntimeError(f"{type(self).__name__}: nothing loaded (call load() first)")
+        T = self.token_count
+        if not (0 <= begin < T and begin <= end <= T):
+            raise ValueError(f"token range [{begin}, {end}) is outside the stream of {T} tokens")
+        return self._pick(keys, lambda k: self._stream(k).span(begin, end))
+
+    def fetch_record(self, index: int, keys: Keys):
+        """Record ``index`` of one key (a tensor, or a list for nested keys) or several (a dict)."""
+        n = self.num_records
         if not 0 <= index < n:
-            raise IndexError(f"Store index out of range: {index}, num_samples={n}")
-        if self._window_size > 0 and self._length > 0:
-            b, e = self.sample_window(index)
-            return {k: self.fetch(b, e, k) for k in self._stream_keys()}
-        return self.fetch_record(index, list(self._data.keys()))
+            raise ValueError(f"record {index} requested from a store of {n} records")
+        return self._pick(keys, lambda k: self._record(k).record(index))
 
-    def sample_window(self, index: int) -> Tuple[int, int]:
-        if self._window_size <= 0:
-            raise RuntimeError("sample_window() requires window_size > 0 (stream mode)")
-        if self._length <= self._window_size:
-            raise IndexError(f"Data too short for window: token_count={self._length}, window_size={self._window_size}")
-        if not 0 <= index < self.num_samples:
-            raise IndexError(f"Sample index out of range: {index}, num_samples={self.num_samples}")
-        begin = min(index * self._stride, self._length - 1 - self._window_size)
-        return begin, min(begin + self._window_size, self._length - 1)
+    # ------------------------------------------------------------------ helpers
+    @staticmethod
+    def _pick(keys: Keys, get: Callable[[str], object]):
+        return get(keys) if isinstance(keys, str) else {k: get(k) for k in keys}
 
-    def _stream_keys(self) -> List[str]:
-        return [k for k, v in self._data.items() if not (v and isinstance(v[0], list))]
+    def _stream(self, key: str) -> _StreamColumn:
+        col = self.streams.get(key)
+        if col is None:
+            raise KeyError(f"{key!r} is not a stream key of this store (stream keys: {sorted(self.streams)})")
+        return col
 
-    # ------------------------------------------------------------------ normalisation
-    def _normalize(self, raw: Dict[str, list], offsets: Optional[Dict[str, List[int]]] = None) -> None:
-        lengths = []
-        for key, segs in raw.items():
-            self._data[key] = segs
-            if not segs:
-                self._cum[key] = []
-                lengths.append(0)
-                continue
-            if isinstance(segs[0], list):  # nested per-record groups (GRPO)
-                self._cum[key] = []
-                continue
-            cum, tot = [], 0
-            for t in segs:
-                tot += int(t.shape[0])
-                cum.append(tot)
-            self._cum[key] = cum
-            lengths.append(tot)
-        self._length = min(lengths) if lengths else 0
-        good: Dict[str, List[int]] = {}
-        for key, off in (offsets or {}).items():
-            segs = self._data.get(key, [])
-            if len(segs) == 1 and len(off) > 1:
-                good[key] = off
-            elif len(segs) > 1:
-                logger.warning("Key '%s' has %d segments with offsets; record mode disabled for it", key, len(segs))
-        self._offsets = good
-        if good:
-            self._num_records = min(len(v) - 1 for v in good.values())
-        elif self.segments_are_records:
-            counts = [len(v) for v in self._data.values() if not (v and isinstance(v[0], list))]
-            self._num_records = min(counts) if counts else 0
-        else:
-            self._num_records = 0
-
-    # ------------------------------------------------------------------ access
-    def fetch(self, begin: int, end: int, keys: Union[str, List[str]]):
-        if not self._data:
-            raise RuntimeError("Store not loaded")
-        if not (0 <= begin < self._length and 0 <= end <= self._length):
-            raise ValueError(f"Index out of bounds: begin={begin}, end={end}, length={self._length}")
-        if isinstance(keys, str):
-            return self._fetch_key(keys, begin, end)
-        return {k: self._fetch_key(k, begin, end) for k in keys}
-
-    def _fetch_key(self, key: str, begin: int, end: int) -> torch.Tensor:
-        segs, cum = self._data[key], self._cum[key]
-        first = bisect.bisect_right(cum, begin)
-        last = bisect.bisect_left(cum, end)
-        parts = []
-        for i in range(first, last + 1):
-            prev = cum[i - 1] if i > 0 else 0
-            parts.append(segs[i][max(begin - prev, 0):min(end - prev, segs[i].shape[0])])
-        return parts[0] if len(parts) == 1 else torch.cat(parts, 0)
-
-    def fetch_record(self, index: int, keys: Union[str, List[str]]):
-        if not 0 <= index < self._num_records:
-            raise ValueError(f"Record index out of bounds: {index}, num_records={self._num_records}")
-        if isinstance(keys, str):
-            return self._record_key(keys, index)
-        return {k: self._record_key(k, index) for k in keys}
-
-    def _record_key(self, key: str, index: int):
-        off = self._offsets.get(key)
-        if off:
-            end = off[index + 1] if index + 1 < len(off) else self._data[key][0].shape[0]
-            return self._data[key][0][off[index]:end]
-        return self._data[key][index]
+    def _record(self, key: str) -> _RecordColumn:
+        col = self.records.get(key)
+        if col is None:
+            raise KeyError(f"{key!r} has no per-record layout in this store (record keys: {sorted(self.records)})")
+        return col
 
 
-Streamable = Store  # access traits are folded into Store
+# the reference splits access into mixins; here both are part of Store
+Streamable = Store
 Recordable = Store
 
 
@@ -206,61 +247,66 @@ class StoreFactory(Registry["Store"]):
 
 @StoreFactory.register("h5")
 class H5Store(Store):
+    """``*.h5`` files (needs h5py): one group per key, one dataset per record."""
+
     segments_are_records = True
 
     def load(self, path: str, **kwargs) -> None:
-        self._normalize(load_h5(path))
+        self._install(load_h5(path))
 
 
 @StoreFactory.register("bin")
 class MmapStore(Store):
-    def __init__(self, window_size: int = 0, stride: Optional[int] = None):
-        super().__init__(window_size, stride)
-        self._mmap_refs: List[torch.Tensor] = []
+    """Directories of ``meta.json`` + ``<key>.bin`` shards, memory-mapped copy-on-write."""
 
     def load(self, path: str, **kwargs) -> None:
-        root = Path(path)
-        metas = sorted(root.rglob("meta.json")) if root.is_dir() else []
-        if not metas:
-            raise FileNotFoundError(f"No meta.json found under {path}")
+        shard_dirs = sorted({m.parent for m in Path(path).rglob("meta.json")}) if Path(path).is_dir() else []
+        if not shard_dirs:
+            raise FileNotFoundError(f"{path}: no shard directory with a meta.json below it")
         raw: Dict[str, List[torch.Tensor]] = {}
-        offs: Dict[str, List[int]] = {}
-        for m in metas:
-            for k, ts in load_bin(str(m.parent)).items():
-                raw.setdefault(k, []).extend(ts)
-            for k, o in load_bin_offsets(str(m.parent)).items():
-                offs.setdefault(k, []).extend(o)
-        self._normalize(raw, offsets=offs or None)
-        self._mmap_refs = [t for ts in self._data.values() for t in ts if isinstance(t, torch.Tensor)]
+        cuts: Dict[str, List[int]] = {}
+        for d in shard_dirs:
+            for key, tensors in load_bin(str(d)).items():
+                raw.setdefault(key, []).extend(tensors)
+            for key, offs in load_bin_offsets(str(d)).items():
+                cuts.setdefault(key, []).extend(offs)
+        self._install(raw, cuts)
 
 
 class JsonlSource:
-    """Reads a .jsonl file or every *.jsonl of a directory (bad lines skipped)."""
+    """The records of one ``.jsonl`` file, or of every ``*.jsonl`` in a directory (sorted by name),
+    read once and cached. Lines that are not valid JSON are skipped with a warning."""
 
     def __init__(self, path: str):
         self.path = Path(path)
-        self._records: Optional[List[dict]] = None
+        self._cache: Optional[List[dict]] = None
+
+    def files(self) -> List[Path]:
+        return [self.path] if self.path.is_file() else sorted(self.path.glob("*.jsonl"))
 
     def load(self) -> List[dict]:
-        if self._records is None:
-            files = [self.path] if self.path.is_file() else sorted(self.path.glob("*.jsonl"))
-            recs: List[dict] = []
-            for f in files:
-                with open(f, "r", encoding="utf-8") as fh:
-                    for line in fh:
-                        line = line.strip()
-                        if not line:
-                            continue
-                        try:
-                            recs.append(json.loads(line))
-                        except json.JSONDecodeError:
-                            logger.warning("Failed to parse JSON line in %s, skipping", f)
-            self._records = recs
-        return self._records
+        if self._cache is None:
+            self._cache = [rec for f in self.files() for rec in self._parse(f)]
+        return self._cache
+
+    @staticmethod
+    def _parse(file: Path) -> Iterable[dict]:
+        with open(file, encoding="utf-8") as fh:
+            for lineno, line in enumerate(fh, 1):
+                if not line.strip():
+                    continue
+                try:
+                    yield json.loads(line)
+                except json.JSONDecodeError as err:
+                    logger.warning("%s:%d skipped (%s)", file, lineno, err.msg)
 
 
 @StoreFactory.register("jsonl")
 class JsonlStore(Store):
+    """Raw JSONL records, tokenised either eagerly at load time (a transform built from
+    ``dataset_config.json`` next to the files, an explicit ``transform``, or the built-in chat
+    ``messages`` config with ``tokenizer_path``), or lazily per record (``processor``)."""
+
     CONFIG_NAME = "dataset_config.json"
     segments_are_records = True
     DEFAULT_MESSAGES_CONFIG = {
@@ -273,58 +319,60 @@ class JsonlStore(Store):
 
     def __init__(self, window_size: int = 0, stride: Optional[int] = None):
         super().__init__(window_size, stride)
-        self._source: Optional[JsonlSource] = None
-        self._processor: Optional[Callable[[dict], Dict[str, torch.Tensor]]] = None
-        self._keys_cache: Optional[List[str]] = None
+        self.source: Optional[JsonlSource] = None
+        self.processor: Optional[Callable[[dict], Dict[str, torch.Tensor]]] = None
+        self._lazy_keys: Optional[List[str]] = None
 
     def load(self, path: str, transform=None, processor=None, **kwargs) -> None:
-        self._source = JsonlSource(path)
-        records = self._source.load()
+        self.source = JsonlSource(path)
+        recs = self.source.load()
         if processor is not None:
-            self._processor = processor
-            self._num_records = len(records)
+            self.processor = processor
             return
-        if transform is None:
-            from astrai_b200.config.preprocess_config import PipelineConfig
-            from astrai_b200.preprocessing.pipeline import TokenizeTransform
+        self._install((transform or self._find_transform(path, kwargs.get("tokenizer_path"))).apply(recs))
 
-            root = Path(path)
-            cfg = root / self.CONFIG_NAME if root.is_dir() else None
-            if cfg is not None and cfg.exists():
-                transform = TokenizeTransform.from_config_file(str(cfg))
-            else:
-                tok = kwargs.get("tokenizer_path")
-                if not tok:
-                    raise FileNotFoundError(
-                        f"JSONL dataset config not found. Expected {self.CONFIG_NAME} alongside *.jsonl files, pass "
-                        "an explicit transform, processor= for lazy tokenisation, or tokenizer_path= for the "
-                        "built-in messages config.")
-                transform = TokenizeTransform(PipelineConfig.from_dict(self.DEFAULT_MESSAGES_CONFIG), tok)
-        self._normalize(transform.apply(records))
+    def _find_transform(self, path: str, tokenizer_path: Optional[str]):
+        from astrai_b200.config.preprocess_config import PipelineConfig
+        from astrai_b200.preprocessing.pipeline import TokenizeTransform
+
+        cfg = Path(path) / self.CONFIG_NAME
+        if Path(path).is_dir() and cfg.exists():
+            return TokenizeTransform.from_config_file(str(cfg))
+        if tokenizer_path:
+            return TokenizeTransform(PipelineConfig.from_dict(self.DEFAULT_MESSAGES_CONFIG), tokenizer_path)
+        raise FileNotFoundError(f"{path}: don't know how to tokenise these records. Put a {self.CONFIG_NAME} next "
+                                "to the .jsonl files, or pass transform=, processor= (lazy, per record) or "
+                                "tokenizer_path= (chat 'messages' records)")
+
+    # ------------------------------------------------------------------ lazy (processor) mode
+    @property
+    def lazy(self) -> bool:
+        return self.processor is not None
 
     @property
     def keys(self) -> List[str]:
-        if self._processor is not None:
-            if self._keys_cache is None and self._num_records > 0:
-                self._keys_cache = list(self._processor(self._source.load()[0]).keys())
-            return self._keys_cache or []
-        return list(self._data.keys())
+        if not self.lazy:
+            return super().keys
+        if self._lazy_keys is None:
+            recs = self.source.load()
+            self._lazy_keys = list(self.processor(recs[0])) if recs else []
+        return list(self._lazy_keys)
 
-    def fetch_record(self, index: int, keys):
-        if self._processor is not None:
-            if not 0 <= index < self._num_records:
-                raise ValueError(f"Record index out of bounds: {index}, num_records={self._num_records}")
-            data = self._processor(self._source.load()[index])
-            return data[keys] if isinstance(keys, str) else {k: data[k] for k in keys}
-        return super().fetch_record(index, keys)
+    @property
+    def num_records(self) -> int:
+        return len(self.source.load()) if self.lazy else super().num_records
 
-    def fetch(self, begin: int, end: int, keys):
-        if self._processor is not None:
-            raise RuntimeError("JsonlStore in lazy (processor) mode does not support stream fetch(); "
-                               "use fetch_record() instead.")
+    def fetch_record(self, index: int, keys: Keys):
+        if not self.lazy:
+            return super().fetch_record(index, keys)
+        n = self.num_records
+        if not 0 <= index < n:
+            raise ValueError(f"record {index} requested from a store of {n} records")
+        out = self.processor(self.source.load()[index])
+        return self._pick(keys, out.__getitem__)
+
+    def fetch(self, begin: int, end: int, keys: Keys):
+        if self.lazy:
+            raise RuntimeError("a JsonlStore loaded with processor= tokenises one record at a time and has no "
+                               "token stream; use fetch_record()")
         return super().fetch(begin, end, keys)
-
-    def __getitem__(self, index: int):
-        if self._processor is not None:
-            return self.fetch_record(index, self.keys)
-        return super().__getitem__(index)

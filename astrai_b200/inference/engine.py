@@ -1,19 +1,27 @@
-"""Inference engine facade.
+"""Inference engine: the user-facing generation API over the continuous-batching scheduler.
 
-Parity: astrai/inference/engine.py:16-348 (``GenerateResult``,
-``GenerationRequest`` with the same validation, ``InferenceEngine`` with
-``generate`` (str or list, streaming or not), ``generate_async``,
-``generate_with_request``, ``get_stats``, ``shutdown`` and context-manager
-use). ``page_size`` builds a :class:`PageCache` (prefix sharing) instead of
-the per-slot cache when ``n_pages`` is given.
+Public surface kept from the reference (astrai/inference/engine.py:17-348): ``GenerateResult``,
+``GenerationRequest``, and ``InferenceEngine`` with ``generate`` (one prompt or a list, streamed
+or blocking), ``generate_async``, ``generate_with_request``, ``get_stats``, ``shutdown`` and
+context-manager use.
+
+Design: every call submits its prompts as scheduler tasks whose stream callbacks push
+``(prompt index, piece)`` events into one FIFO owned by the call (:class:`GenerateResult`). The
+scheduler thread only enqueues; the caller's thread is the only consumer. Blocking and streaming
+generation are the same drain loop (:meth:`GenerateResult.events`); the blocking form just joins
+the pieces. The end of a prompt's stream is the ``STOP`` sentinel. Leaving a drain loop early
+(a consumer that stops iterating, a timeout) removes the call's tasks from the scheduler, so
+their KV pages come back. With ``n_pages`` set, the engine builds a :class:`PageCache` (prefix
+sharing across requests) instead of the per-slot contiguous cache.
 """
 
 from __future__ import annotations
 
 import asyncio
 import gc
-import threading
-from typing import Any, AsyncGenerator, Dict, Generator, List, Optional, Tuple, Union
+import queue
+import time
+from typing import Any, AsyncIterator, Dict, Iterator, List, Optional, Sequence, Tuple, Union
 
 import torch
 import torch.nn as nn
@@ -22,76 +30,106 @@ from astrai_b200.inference.core.cache import KVCache, PageCache
 from astrai_b200.inference.core.scheduler import InferenceScheduler, model_head_dim
 from astrai_b200.inference.core.task import STOP
 
+_POLL_S = 0.05  # how often a blocked consumer re-checks its deadline
+
 
 class GenerateResult:
-    """Thread-safe collector of streamed pieces for ``count`` prompts."""
+    """Event FIFO for one generation call over ``count`` prompts.
+
+    ``append(piece, idx)`` is the scheduler-side callback (thread-safe, never blocks).
+    ``events(timeout)`` yields ``(idx, piece)`` in arrival order until every prompt has
+    delivered ``STOP``; the pieces are also kept so ``get_results()`` returns the full texts.
+    """
 
     def __init__(self, count: int = 1):
-        self._cond = threading.Condition()
-        self._event = threading.Event()
-        self.tokens: List[Tuple[int, Any]] = []
-        self.results: List[str] = [""] * count
-        self._done = [False] * count
-        self._completed = 0
-        self._total = count
+        self._fifo: "queue.SimpleQueue[Tuple[int, Any]]" = queue.SimpleQueue()
+        self._pieces: List[List[str]] = [[] for _ in range(count)]
+        self._open = set(range(count))
 
-    def append(self, token, idx: int = 0) -> None:
-        with self._cond:
-            self.tokens.append((idx, token))
-            if token is STOP:
-                if not self._done[idx]:
-                    self._done[idx] = True
-                    self._completed += 1
-                    self._cond.notify_all()
-            else:
-                self.results[idx] += token
-            self._event.set()
+    # producer side (scheduler thread)
+    def append(self, token: Any, idx: int = 0) -> None:
+        self._fifo.put((idx, token))
 
-    def pop_all(self) -> List[Tuple[int, Any]]:
-        with self._cond:
-            out, self.tokens = self.tokens, []
-            if not out:
-                self._event.clear()
-            return out
+    # consumer side (the calling thread)
+    @property
+    def finished(self) -> bool:
+        return not self._open
 
-    def wait(self, timeout: Optional[float] = None) -> bool:
-        return self._event.wait(timeout=timeout)
-
-    def wait_completion(self, timeout: float = 300.0) -> None:
-        with self._cond:
-            if not self._cond.wait_for(lambda: self._completed >= self._total, timeout=timeout):
-                raise TimeoutError(f"Generation timeout after {timeout}s ({self._completed}/{self._total} completed)")
+    def events(self, timeout: Optional[float] = None) -> Iterator[Tuple[int, str]]:
+        """Drain the FIFO until every prompt is finished. ``timeout`` bounds the silence between
+        two events (None: wait for ever); on expiry a ``TimeoutError`` names the open prompts."""
+        last = time.monotonic()
+        while self._open:
+            try:
+                idx, piece = self._fifo.get(timeout=_POLL_S)
+            except queue.Empty:
+                if timeout is not None and time.monotonic() - last > timeout:
+                    raise TimeoutError(f"no output for {timeout:.0f} s; prompts still running: "
+                                       f"{sorted(self._open)} of {len(self._pieces)}") from None
+                continue
+            last = time.monotonic()
+            if piece is STOP:
+                self._open.discard(idx)
+                continue
+            self._pieces[idx].append(piece)
+            yield idx, piece
 
     def get_results(self) -> List[str]:
-        with self._cond:
-            return list(self.results)
+        return ["".join(p) for p in self._pieces]
+
+
+def _check_sampling(top_k, top_p, temperature, frequency_penalty, rep_window) -> None:
+    problems = []
+    if not isinstance(top_k, int) or isinstance(top_k, bool) or top_k < 0:
+        problems.append(f"top_k={top_k!r} (want an int >= 0; 0 disables the cut)")
+    if not isinstance(top_p, (int, float)) or not 0.0 <= top_p <= 1.0:
+        problems.append(f"top_p={top_p!r} (want a number in [0, 1])")
+    if not isinstance(temperature, (int, float)) or temperature < 0:
+        problems.append(f"temperature={temperature!r} (want a number >= 0; 0 is greedy)")
+    if not isinstance(frequency_penalty, (int, float)) or abs(frequency_penalty) > 2.0:
+        problems.append(f"frequency_penalty={frequency_penalty!r} (want a number in [-2, 2])")
+    if not isinstance(rep_window, int) or rep_window <= 0:
+        problems.append(f"rep_window={rep_window!r} (want an int > 0)")
+    if problems:
+        raise ValueError("invalid sampling parameters: " + "; ".join(problems))
 
 
 class GenerationRequest:
-    """Chat request with validated sampling parameters."""
+    """A chat-formatted request (``messages`` in the tokenizer's chat-template format) with its
+    sampling parameters, validated on construction (``ValueError`` lists every bad field)."""
 
     def __init__(self, messages: List[Dict[str, str]], top_k: int = 50, top_p: float = 1.0,
                  temperature: float = 1.0, max_tokens: Optional[int] = None, frequency_penalty: float = 0.0,
                  rep_window: int = 64, stream: bool = False):
-        if not (isinstance(top_k, int) and top_k >= 0):
-            raise ValueError("top_k must be a non-negative integer")
-        if not (0.0 <= top_p <= 1.0):
-            raise ValueError("top_p must be a float between 0.0 and 1.0")
-        if not (isinstance(temperature, (int, float)) and temperature >= 0):
-            raise ValueError("temperature must be a non-negative number")
-        if not (isinstance(frequency_penalty, (int, float)) and -2.0 <= frequency_penalty <= 2.0):
-            raise ValueError("frequency_penalty must be between -2.0 and 2.0")
-        if not (isinstance(rep_window, int) and rep_window > 0):
-            raise ValueError("rep_window must be a positive integer")
+        _check_sampling(top_k, top_p, temperature, frequency_penalty, rep_window)
         self.messages = messages
-        self.top_k, self.top_p, self.temperature = top_k, top_p, temperature
+        self.top_k = top_k
+        self.top_p = top_p
+        self.temperature = temperature
         self.max_tokens = max_tokens
-        self.frequency_penalty, self.rep_window = frequency_penalty, rep_window
+        self.frequency_penalty = frequency_penalty
+        self.rep_window = rep_window
         self.stream = stream
+
+    def sampling(self) -> Dict[str, Any]:
+        return {"max_tokens": self.max_tokens, "temperature": self.temperature, "top_p": self.top_p,
+                "top_k": self.top_k, "frequency_penalty": self.frequency_penalty, "rep_window": self.rep_window}
+
+
+def _text_only(events: Iterator[Tuple[int, str]]) -> Iterator[str]:
+    try:
+        for _, piece in events:
+            yield piece
+    finally:
+        events.close()  # release the tasks now, not when the garbage collector gets to it
 
 
 class InferenceEngine:
-    """Continuous-batching generation behind a simple API."""
+    """Generation front end. The scheduler thread starts with the engine and stops in
+    :meth:`shutdown` (or on leaving a ``with`` block)."""
+
+    #: seconds without any output after which a blocking call gives up
+    timeout_s: float = 300.0
 
     def __init__(self, model: nn.Module, tokenizer, max_batch_size: int = 1, max_seq_len: Optional[int] = None,
                  max_prompt_len: int = 2048, page_size: int = 128, cache: Optional[KVCache] = None,
@@ -99,113 +137,98 @@ class InferenceEngine:
         self.model = model
         self.tokenizer = tokenizer
         if cache is None and n_pages:
-            p = next(model.parameters())
-            cfg = model.config
-            cache = PageCache(cfg.num_hidden_layers, n_pages, page_size, cfg.num_key_value_heads,
-                              model_head_dim(model), p.device, p.dtype)
+            cache = self._paged_cache(model, n_pages, page_size)
         self.scheduler = InferenceScheduler(model, tokenizer, max_batch_size=max_batch_size, max_seq_len=max_seq_len,
                                             max_prompt_len=max_prompt_len, cache=cache,
                                             use_cuda_graph=use_cuda_graph, seed=seed)
         self.scheduler.start()
 
-    def __enter__(self):
+    @staticmethod
+    def _paged_cache(model: nn.Module, n_pages: int, page_size: int) -> PageCache:
+        ref = next(model.parameters())
+        c = model.config
+        return PageCache(c.num_hidden_layers, n_pages, page_size, c.num_key_value_heads, model_head_dim(model),
+                         ref.device, ref.dtype)
+
+    def __enter__(self) -> "InferenceEngine":
         return self
 
-    def __exit__(self, exc_type, exc, tb):
+    def __exit__(self, *exc) -> bool:
         self.shutdown()
         return False
+
+    # ------------------------------------------------------------------ submission
+    def _launch(self, prompts: Sequence[str], sampling: Dict[str, Any]) -> Tuple[GenerateResult, List[str]]:
+        res = GenerateResult(len(prompts))
+        tasks = [self.scheduler.add_task(text, stream_callback=lambda piece, i=i: res.append(piece, i), **sampling)
+                 for i, text in enumerate(prompts)]
+        return res, tasks
+
+    def _release(self, tasks: Sequence[str]) -> None:
+        for t in tasks:
+            self.scheduler.remove_task(t)
+
+    def _drain(self, prompts: Sequence[str], sampling: Dict[str, Any],
+               timeout: Optional[float]) -> Iterator[Tuple[int, str]]:
+        """(idx, piece) events of a fresh call; the tasks are released however the loop ends."""
+        res, tasks = self._launch(prompts, sampling)
+        try:
+            yield from res.events(timeout)
+        finally:
+            self._release(tasks)
 
     # ------------------------------------------------------------------ public API
     def generate(self, prompt: Union[str, List[str]], stream: bool = False, max_tokens: Optional[int] = None,
                  temperature: float = 1.0, top_p: float = 1.0, top_k: int = 50, frequency_penalty: float = 0.0,
-                 rep_window: int = 64) -> Union[Generator, str, List[str]]:
-        batch = isinstance(prompt, list)
-        prompts = prompt if batch else [prompt]
-        params = dict(max_tokens=max_tokens, temperature=temperature, top_p=top_p, top_k=top_k,
-                      frequency_penalty=frequency_penalty, rep_window=rep_window)
+                 rep_window: int = 64) -> Union[Iterator, str, List[str]]:
+        """Blocking: the generated text (a list of texts for a list of prompts). Streaming: an
+        iterator of text pieces (of ``(prompt index, piece)`` pairs for a list of prompts)."""
+        as_list = isinstance(prompt, list)
+        prompts = prompt if as_list else [prompt]
+        sampling = {"max_tokens": max_tokens, "temperature": temperature, "top_p": top_p, "top_k": top_k,
+                    "frequency_penalty": frequency_penalty, "rep_window": rep_window}
         if stream:
-            return self._generate_streaming(prompts, batch, **params)
-        return self._generate_blocking(prompts, batch, **params)
+            events = self._drain(prompts, sampling, None)
+            return events if as_list else _text_only(events)
+        texts: List[List[str]] = [[] for _ in prompts]
+        for i, piece in self._drain(prompts, sampling, self.timeout_s):
+            texts[i].append(piece)
+        out = ["".join(t) for t in texts]
+        return out if as_list else out[0]
 
     def generate_async(self, prompt: str, max_tokens: Optional[int] = None, temperature: float = 1.0,
                        top_p: float = 1.0, top_k: int = 50, frequency_penalty: float = 0.0,
-                       rep_window: int = 64) -> AsyncGenerator[str, None]:
-        gen = self._generate_streaming([prompt], False, max_tokens=max_tokens, temperature=temperature, top_p=top_p,
-                                       top_k=top_k, frequency_penalty=frequency_penalty, rep_window=rep_window)
+                       rep_window: int = 64) -> AsyncIterator[str]:
+        """Async iterator of text pieces for one prompt. The blocking queue reads run in the event
+        loop's default executor; closing the iterator early cancels the task."""
+        pieces = self.generate(prompt, stream=True, max_tokens=max_tokens, temperature=temperature, top_p=top_p,
+                               top_k=top_k, frequency_penalty=frequency_penalty, rep_window=rep_window)
+        end = object()
 
-        async def agen():
+        def pull():
+            return next(pieces, end)
+
+        async def stream():
             loop = asyncio.get_running_loop()
             try:
-                while True:
-                    piece = await loop.run_in_executor(None, self._next_token, gen)
-                    if piece is None:
-                        break
+                while (piece := await loop.run_in_executor(None, pull)) is not end:
                     yield piece
-            finally:  # closing early (stop sequence, client gone) cancels the task
-                gen.close()
+            finally:
+                pieces.close()
 
-        return agen()
-
-    @staticmethod
-    def _next_token(gen: Generator) -> Optional[str]:
-        try:
-            return next(gen)
-        except StopIteration:
-            return None
+        return stream()
 
     def generate_with_request(self, request: GenerationRequest):
-        prompt = self.tokenizer.apply_chat_template(request.messages, tokenize=False)
-        return self.generate(prompt, stream=request.stream, max_tokens=request.max_tokens,
-                             temperature=request.temperature, top_p=request.top_p, top_k=request.top_k,
-                             frequency_penalty=request.frequency_penalty, rep_window=request.rep_window)
+        """Render ``request.messages`` with the tokenizer's chat template, then :meth:`generate`."""
+        text = self.tokenizer.apply_chat_template(request.messages, tokenize=False)
+        return self.generate(text, stream=request.stream, **request.sampling())
 
     def get_stats(self) -> Dict[str, Any]:
         return self.scheduler.get_stats()
 
     def shutdown(self) -> None:
+        """Stop the scheduler thread and hand cached device memory back."""
         self.scheduler.stop()
+        gc.collect()
         if torch.cuda.is_available():
             torch.cuda.empty_cache()
-        gc.collect()
-
-    # ------------------------------------------------------------------ internals
-    def _submit(self, prompts: List[str], **params) -> Tuple[GenerateResult, List[str]]:
-        result = GenerateResult(len(prompts))
-        ids = []
-        for i, p in enumerate(prompts):
-            ids.append(self.scheduler.add_task(p, stream_callback=(lambda tok, i=i: result.append(tok, i)), **params))
-        return result, ids
-
-    def _generate_streaming(self, prompts: List[str], batch: bool, **params) -> Generator:
-        result, task_ids = self._submit(prompts, **params)
-        n = len(prompts)
-
-        def gen():
-            done = [False] * n
-            left = n
-            try:
-                while left:
-                    for idx, tok in result.pop_all():
-                        if tok is STOP:
-                            if not done[idx]:
-                                done[idx] = True
-                                left -= 1
-                        else:
-                            yield (idx, tok) if batch else tok
-                    if left:
-                        result.wait(timeout=0.05)
-            finally:
-                for tid in task_ids:
-                    self.scheduler.remove_task(tid)
-
-        return gen()
-
-    def _generate_blocking(self, prompts: List[str], batch: bool, **params) -> Union[str, List[str]]:
-        result, task_ids = self._submit(prompts, **params)
-        try:
-            result.wait_completion()
-        finally:
-            for tid in task_ids:
-                self.scheduler.remove_task(tid)
-        res = result.get_results()
-        return res if batch else res[0]
