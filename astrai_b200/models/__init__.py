@@ -1,4 +1,4 @@
-from astrai_b200.models.automodel import AutoModel, disable_random_init
+from astrai_b200.models.automodel import AutoModel
 from astrai_b200.models.components import (
     GQA, MLA, MLP, AttnFactory, DecoderBlock, DeepSeekMoE, Embedding, FFNFactory, Linear, LoRAConfig, LoRALinear,
     RMSNorm, RotaryEmbedding, inject_lora, load_lora, merge_lora, save_lora,
@@ -9,5 +9,5 @@ from astrai_b200.models.transformer import AutoRegressiveLM
 __all__ = [
     "AutoModel", "AutoRegressiveLM", "EmbeddingEncoder", "Linear", "RMSNorm", "MLP", "GQA", "MLA", "DeepSeekMoE",
     "DecoderBlock", "Embedding", "RotaryEmbedding", "AttnFactory", "FFNFactory", "LoRAConfig", "LoRALinear",
-    "inject_lora", "merge_lora", "save_lora", "load_lora", "disable_random_init",
+    "inject_lora", "merge_lora", "save_lora", "load_lora",
 ]

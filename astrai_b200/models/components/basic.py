@@ -111,6 +111,10 @@ class RotaryEmbedding(nn.Module):
             self.freqs_cis = rope_table(self.dim, self.max_len, self.base, device=self.freqs_cis.device)
         return self
 
+    def reset_buffers(self) -> None:
+        """Recompute the angle table in place (after ``to_empty`` left it uninitialised)."""
+        self.freqs_cis = rope_table(self.dim, self.max_len, self.base, device=self.freqs_cis.device)
+
     def table(self) -> torch.Tensor:
         return self.freqs_cis
 

@@ -1,78 +1,81 @@
-"""Embedding encoder (parity: astrai/model/encoder.py:16-97).
+"""Sentence-embedding encoder, model type ``embedding``.
 
-Same trunk as the LM without ``lm_head``; bidirectional attention (a 2-D
-key mask marks padding); pooling ``cls`` / ``last`` / ``mean`` (masked);
-optional L2 normalisation. Registered as model type ``embedding``.
+Behaviour kept from the reference (astrai/model/encoder.py:16-97), so encoder checkpoints load
+in both frameworks: the decoder trunk of the LM without ``lm_head`` (a saved ``lm_head.weight``
+is ignored on load), attention over the whole sequence with padding keys masked out, and one
+vector per sequence pooled as ``cls`` (first position), ``last`` (last valid position) or
+``mean`` (over valid positions; the default), optionally L2-normalised.
+
+Here the trunk is the LM's own (:func:`build_trunk` / :func:`run_trunk`), and padding is
+expressed as segment ids for the flash-attention kernel: valid tokens share segment 0 and every
+padding position gets a segment of its own, so no valid query attends to padding.
 """
 
 from __future__ import annotations
 
-from typing import Any, Mapping, Optional
+from typing import Any, Callable, Dict, Mapping, Optional
 
 import torch
-import torch.nn as nn
+import torch.nn.functional as F
 
 from astrai_b200.config.model_config import EncoderConfig
 from astrai_b200.models.automodel import AutoModel
 from astrai_b200.models.components.attention import AttnContext
-from astrai_b200.models.components.basic import Embedding, RMSNorm, RotaryEmbedding
-from astrai_b200.models.components.decoder_block import DecoderBlock
+from astrai_b200.models.transformer import build_trunk, run_trunk
+
+
+def _pool_cls(h: torch.Tensor, mask: Optional[torch.Tensor]) -> torch.Tensor:
+    return h[:, 0]
+
+
+def _pool_last(h: torch.Tensor, mask: Optional[torch.Tensor]) -> torch.Tensor:
+    if mask is None:
+        return h[:, -1]
+    last = mask.long().sum(1) - 1
+    return h[torch.arange(h.shape[0], device=h.device), last]
+
+
+def _pool_mean(h: torch.Tensor, mask: Optional[torch.Tensor]) -> torch.Tensor:
+    if mask is None:
+        return h.mean(1)
+    w = mask.to(h.dtype).unsqueeze(-1)
+    return (h * w).sum(1) / w.sum(1).clamp(min=1.0)
+
+
+POOLERS: Dict[str, Callable[[torch.Tensor, Optional[torch.Tensor]], torch.Tensor]] = {
+    "cls": _pool_cls, "last": _pool_last, "mean": _pool_mean,
+}
+
+
+def padding_segments(mask: torch.Tensor) -> torch.Tensor:
+    """[B, S] validity mask -> segment ids: 0 for valid tokens, -(position + 1) for padding."""
+    S = mask.shape[1]
+    own = -torch.arange(1, S + 1, device=mask.device, dtype=torch.int32)
+    return torch.where(mask.bool(), torch.zeros_like(own), own).expand_as(mask).contiguous()
 
 
 @AutoModel.register("embedding")
 class EmbeddingEncoder(AutoModel):
     def __init__(self, config: EncoderConfig):
         super().__init__(config)
-        self.rotary_embedding = RotaryEmbedding(config.hidden_size // config.num_attention_heads,
-                                                config.max_position_embeddings,
-                                                config.rope_theta if config.rope_theta is not None else 10000,
-                                                rope_scaling=config.rope_scaling)
-        self.embed_tokens = Embedding(config.vocab_size, config.hidden_size, neftune_alpha=config.neftune_alpha)
-        self.layers = nn.ModuleList([DecoderBlock(config, i) for i in range(config.num_hidden_layers)])
-        self.norm = RMSNorm(config.hidden_size, config.rms_norm_eps)
+        build_trunk(self, config)
         self.pooling_type = config.pooling_type or "mean"
+        if self.pooling_type not in POOLERS:
+            raise ValueError(f"pooling_type {self.pooling_type!r}: choose one of {sorted(POOLERS)}")
         self.normalize_embeddings = bool(config.normalize_embeddings)
-        self.apply(self._init_weights)
-
-    @staticmethod
-    def _init_weights(module):
-        if hasattr(module, "reset_parameters") and not isinstance(module, AutoModel):
-            module.reset_parameters()
+        for m in self.modules():
+            if m is not self and hasattr(m, "reset_parameters"):
+                m.reset_parameters()
 
     def load_state_dict(self, state_dict: Mapping[str, Any], strict: bool = True, assign: bool = False):
-        sd = dict(state_dict)
-        sd.pop("lm_head.weight", None)
-        return super().load_state_dict(sd, strict=strict, assign=assign)
+        return super().load_state_dict({k: v for k, v in state_dict.items() if k != "lm_head.weight"},
+                                       strict=strict, assign=assign)
 
     def forward(self, input_ids: torch.Tensor, input_mask: Optional[torch.Tensor] = None,
                 position_ids: Optional[torch.Tensor] = None) -> torch.Tensor:
         B, S = input_ids.shape
-        # bidirectional; padding keys get unique negative segment ids
-        seg = None
-        if input_mask is not None:
-            valid = input_mask.bool()
-            pad_id = -(torch.arange(S, device=input_ids.device, dtype=torch.int32) + 1).expand(B, S)
-            seg = torch.where(valid, torch.zeros_like(pad_id), pad_id)
+        seg = padding_segments(input_mask) if input_mask is not None else None
         ctx = AttnContext(B=B, S=S, table=self.rotary_embedding.table(), positions=position_ids, seg=seg,
                           causal=False)
-        x = self.embed_tokens(input_ids)
-        for layer in self.layers:
-            x = layer(x, ctx)
-        h = self.norm(x)
-        if self.pooling_type == "cls":
-            pooled = h[:, 0]
-        elif self.pooling_type == "last":
-            if input_mask is not None:
-                lengths = input_mask.long().sum(1) - 1
-                pooled = h[torch.arange(B, device=h.device), lengths]
-            else:
-                pooled = h[:, -1]
-        else:
-            if input_mask is not None:
-                m = input_mask.unsqueeze(-1).to(h.dtype)
-                pooled = (h * m).sum(1) / m.sum(1).clamp(min=1.0)
-            else:
-                pooled = h.mean(1)
-        if self.normalize_embeddings:
-            pooled = torch.nn.functional.normalize(pooled, p=2, dim=-1)
-        return pooled
+        pooled = POOLERS[self.pooling_type](run_trunk(self, input_ids, ctx), input_mask)
+        return F.normalize(pooled, p=2, dim=-1) if self.normalize_embeddings else pooled

@@ -42,16 +42,30 @@ def _rope_dim(config) -> int:
     return config.hidden_size // config.num_attention_heads
 
 
+def build_trunk(model: nn.Module, config) -> None:
+    """The decoder stack shared by the LM and the embedding encoder, under the attribute names that
+    are the checkpoint keys: ``rotary_embedding`` (angle table, base 10000 when the config has
+    none), ``embed_tokens``, ``layers`` and the final ``norm``."""
+    base = config.rope_theta if config.rope_theta is not None else 10000
+    model.rotary_embedding = RotaryEmbedding(_rope_dim(config), config.max_position_embeddings, base,
+                                             rope_scaling=config.rope_scaling)
+    model.embed_tokens = Embedding(config.vocab_size, config.hidden_size, neftune_alpha=config.neftune_alpha)
+    model.layers = nn.ModuleList([DecoderBlock(config, i) for i in range(config.num_hidden_layers)])
+    model.norm = RMSNorm(config.hidden_size, config.rms_norm_eps)
+
+
+def run_trunk(model: nn.Module, input_ids: torch.Tensor, ctx: AttnContext) -> torch.Tensor:
+    x = model.embed_tokens(input_ids)
+    for layer in model.layers:
+        x = layer(x, ctx)
+    return model.norm(x)
+
+
 @AutoModel.register("autoregressive_lm")
 class AutoRegressiveLM(AutoModel):
     def __init__(self, config: AutoRegressiveLMConfig):
         super().__init__(config)
-        self.rotary_embedding = RotaryEmbedding(_rope_dim(config), config.max_position_embeddings,
-                                                config.rope_theta if config.rope_theta is not None else 10000,
-                                                rope_scaling=config.rope_scaling)
-        self.embed_tokens = Embedding(config.vocab_size, config.hidden_size, neftune_alpha=config.neftune_alpha)
-        self.layers = nn.ModuleList([DecoderBlock(config, i) for i in range(config.num_hidden_layers)])
-        self.norm = RMSNorm(config.hidden_size, config.rms_norm_eps)
+        build_trunk(self, config)
         self.lm_head = Linear(config.hidden_size, config.vocab_size)
         if config.tie_word_embeddings is True:
             self.lm_head.weight = self.embed_tokens.weight
@@ -61,6 +75,9 @@ class AutoRegressiveLM(AutoModel):
     def _init_weights(module):
         if hasattr(module, "reset_parameters") and not isinstance(module, AutoModel):
             module.reset_parameters()
+
+    def tied_parameters(self):
+        return [("lm_head.weight", "embed_tokens.weight")] if self.config.tie_word_embeddings is True else []
 
     # ------------------------------------------------------------------ state dict (tied lm_head)
     def load_state_dict(self, state_dict: Mapping[str, Any], strict: bool = True, assign: bool = False):
@@ -87,10 +104,7 @@ class AutoRegressiveLM(AutoModel):
                            aux_losses=[] if self.training else None)
 
     def backbone(self, input_ids: torch.Tensor, ctx: AttnContext) -> torch.Tensor:
-        x = self.embed_tokens(input_ids)
-        for layer in self.layers:
-            x = layer(x, ctx)
-        return self.norm(x)
+        return run_trunk(self, input_ids, ctx)
 
     def forward(self, input_ids: torch.Tensor, input_mask: Optional[torch.Tensor] = None, paged_cache=None,
                 position_ids: Optional[torch.Tensor] = None, seg_ids: Optional[torch.Tensor] = None,
