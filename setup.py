@@ -29,7 +29,7 @@ NVCC_FLAGS = [
 
 # name, version and dependencies live in pyproject.toml
 setup(
-    packages=find_packages(include=["astrai_b200*"]),
+    packages=find_packages(include=["astrai_b200*", "astrai"]),
     ext_modules=[
         CUDAExtension(
             name="astrai_b200._C",
