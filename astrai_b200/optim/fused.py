@@ -33,6 +33,7 @@ import torch
 from torch.optim import Optimizer
 
 from astrai_b200.ops._ext import native
+from astrai_b200.utils.phase_timer import phase
 
 NS_COEFFS = (3.4445, -4.7750, 2.0315)
 CHUNK = 1 << 16
@@ -293,7 +294,8 @@ class Muon(Optimizer):
             for p in params:
                 by_shape.setdefault(tuple(p.shape), []).append(p)
             for shape, ps in by_shape.items():
-                self._step_batched(gi, shape, ps, group)
+                with phase("muon_newton_schulz"):
+                    self._step_batched(gi, shape, ps, group)
             if self._reset_clip and self.use_clip_coef:
                 clip_state(params[0].device).coef.fill_(1.0)
         return loss
@@ -341,12 +343,14 @@ class Muon(Optimizer):
             if own:
                 chunks = _ns_chunks(own)
                 for ci, chunk in enumerate(chunks):
-                    t, out, tall = self._orthogonalize(("own", gi, shape, ci), chunk, group)
+                    with phase("muon_newton_schulz"):
+                        t, out, tall = self._orthogonalize(("own", gi, shape, ci), chunk, group)
                     # only the group's last launch raises its flag on the peers (slot -1: no flag); the
                     # earlier launches' stores precede it in stream order
-                    C.muon_apply_peers(t["pptr"], t["poff"], a.buf.peer_base, out, len(chunk), R, Cc, tall,
-                                       1.0 - lr * group["weight_decay"], adj, r, W, a.flag_off,
-                                       slot if ci == len(chunks) - 1 else -1, self._epoch, a.done)
+                    with phase("muon_apply_peers"):
+                        C.muon_apply_peers(t["pptr"], t["poff"], a.buf.peer_base, out, len(chunk), R, Cc, tall,
+                                           1.0 - lr * group["weight_decay"], adj, r, W, a.flag_off,
+                                           slot if ci == len(chunks) - 1 else -1, self._epoch, a.done)
             else:  # nothing owned in this group: only raise its flag on the peers
                 C.muon_apply_peers(None, None, a.buf.peer_base, None, 0, R, Cc, False, 1.0, 0.0, r, W, a.flag_off,
                                    slot, self._epoch, a.done)
@@ -359,7 +363,8 @@ class Muon(Optimizer):
             for shape, ps in by_shape.items():
                 self._step_batched(gi, shape, ps, group)
         if groups:
-            C.peer_flags_wait(a.flags_addr, dev.index, r, W, len(groups), self._epoch, self.wait_s)
+            with phase("muon_flag_wait"):
+                C.peer_flags_wait(a.flags_addr, dev.index, r, W, len(groups), self._epoch, self.wait_s)
         if self._reset_clip and self.use_clip_coef and dev is not None:
             clip_state(dev).coef.fill_(1.0)
 
@@ -481,7 +486,8 @@ class MuonMix(Optimizer):
         if self.muon:
             self.muon.step()
         if self.adamw:
-            self.adamw.step()
+            with phase("adamw"):
+                self.adamw.step()
         if self._device is not None and self._device.type == "cuda":
             clip_state(self._device).coef.fill_(1.0)
 

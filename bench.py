@@ -32,7 +32,7 @@ import types
 from datetime import timedelta
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-BASELINE_VALUE = None  # the reference publishes no number
+BASELINE_VALUE = None  # the reference publishes no performance number
 
 CFG = dict(vocab_size=32000, hidden_size=2048, num_hidden_layers=24, rms_norm_eps=1e-5, intermediate_size=5632,
            tie_word_embeddings=False, max_position_embeddings=2048, rope_theta=1e6, num_attention_heads=16,
@@ -165,6 +165,33 @@ class ClockSampler:
         return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
+PHASE_STEPS = 2  # extra steps after the timed region, timed per phase
+
+
+def phase_breakdown(step, first, n):
+    """Device ms per step of each named phase (``utils.phase_timer``) over ``n`` extra steps that run
+    after the timed region (the headline number carries no phase events), max over ranks per phase."""
+    import torch
+
+    from astrai_b200.utils.phase_timer import PhaseTimer
+
+    timer = PhaseTimer().activate()
+    barrier()
+    try:
+        for i in range(n):
+            step(first + i)
+        per = timer.collect()
+    finally:
+        timer.deactivate()
+    names = sorted(per)
+    t = torch.tensor([per[k] / n for k in names], device="cuda", dtype=torch.float64)
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized():
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return {k: round(float(v), 2) for k, v in zip(names, t.tolist())}
+
+
 def visible_gpu_indices(world):
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     if vis:
@@ -186,6 +213,7 @@ def run_ours(args, rank, world, local):
     from astrai_b200.ops.loss import cross_entropy
     from astrai_b200.optim import MuonMix, clip_grad_norm_
     from astrai_b200.parallel.executor import ExecutorFactory
+    from astrai_b200.utils.phase_timer import phase
 
     torch.manual_seed(3407 + rank)
     dev = torch.device("cuda", local)
@@ -218,17 +246,21 @@ def run_ours(args, rank, world, local):
         graph = GraphedMicroStep(loss_fn, executor.unwrap(model), dev, scale=1.0 / ACCUM, eager_calls=ACCUM)
 
     def step(i):
-        for mi in range(ACCUM):
-            seq = data[i % n_batches, mi]
-            with executor.micro_step(model, mi == ACCUM - 1):
-                if graph is not None:
-                    loss = graph({"seq": seq})
-                else:
-                    loss = loss_fn({"seq": seq})
-                    (loss / ACCUM).backward()
-        executor.finish_step(model)
-        executor.clip_grad_norm(model, CLIP, as_tensor=True)
-        opt.step()
+        with phase("forward_backward"):
+            for mi in range(ACCUM):
+                seq = data[i % n_batches, mi]
+                with executor.micro_step(model, mi == ACCUM - 1):
+                    if graph is not None:
+                        loss = graph({"seq": seq})
+                    else:
+                        loss = loss_fn({"seq": seq})
+                        (loss / ACCUM).backward()
+        with phase("grad_allreduce"):
+            executor.finish_step(model)
+        with phase("clip"):
+            executor.clip_grad_norm(model, CLIP, as_tensor=True)
+        with phase("optimizer"):
+            opt.step()
         opt.zero_grad(set_to_none=graph is None)
         return loss
 
@@ -252,6 +284,7 @@ def run_ours(args, rank, world, local):
     ms = max_over_ranks(s.elapsed_time(e)) / args.steps
     loss_val = float(last.item())
     assert native().read_error() == 0, "kernel bounded-wait error in the timed region"
+    phases = phase_breakdown(step, args.warmup + args.steps, PHASE_STEPS)
     del data
     result = {
         "ms_per_step": ms,
@@ -260,6 +293,7 @@ def run_ours(args, rank, world, local):
         "loss": loss_val,
         "gpu_launches": n_launch,  # counted by the extension's launch counter on this rank (graph replays included)
         "cuda_graph": graph is not None and graph.disabled_reason is None and graph.replays > 0,
+        "phases_ms": phases,
     }
     if not args.no_e2e:
         graph = None  # the e2e run captures its own micro-step; free this one's memory pool first
@@ -803,6 +837,8 @@ def main():
                 "loss": res.get("loss"),
                 "wall_s": round(time.time() - t0, 1),
             }
+            if res.get("phases_ms"):
+                line["phases_ms"] = res["phases_ms"]
             if MODEL in ("dpo", "grpo"):
                 line["config"]["optimizer"] = "AdamW(5e-7), clip 1.0"
                 line["config"]["grad_accum"] = 1
