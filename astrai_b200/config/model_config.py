@@ -73,6 +73,8 @@ class AutoRegressiveLMConfig(BaseModelConfig):
 @ConfigFactory.register("embedding")
 @dataclass
 class EncoderConfig(BaseModelConfig):
+    # saved into config.json, so AutoModel.from_pretrained rebuilds an encoder, not an LM
+    model_type: Optional[str] = "embedding"
     vocab_size: Optional[int] = None
     hidden_size: Optional[int] = None
     num_hidden_layers: Optional[int] = None
