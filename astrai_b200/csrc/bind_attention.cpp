@@ -7,6 +7,9 @@ namespace astrai_host {
 void flash_fwd(const void* q, long long ldq, int q_col0, const void* k, long long ldk, int k_col0, const void* v,
                long long ldv, int v_col0, void* o, long long ldo, float* lse, int B, int Sq, int Sk, int Hq, int Hkv,
                float scale, int causal, const int* seg, cudaStream_t s);
+void flash_fwd_pair(const void* q, long long ldq, int q_col0, const void* k, long long ldk, int k_col0, const void* v,
+                    long long ldv, int v_col0, void* o, long long ldo, float* lse, int B, int Sq, int Sk, int Hq,
+                    int Hkv, int D, float scale, int causal, const int* seg, cudaStream_t s);
 void flash_bwd(const void* q, long long ldq, int q_col0, const void* k, long long ldk, int k_col0, const void* v,
                long long ldv, int v_col0, const void* o, long long ldo, const void* dO, long long ld_do, int do_col0,
                const float* lse, float* delta, float* dq_acc, void* dq, long long ld_dq, int dq_col0, void* dk,
@@ -49,6 +52,30 @@ void flash_fwd(const at::Tensor& q, int64_t q_col0, const at::Tensor& k, int64_t
                          at::cuda::getCurrentCUDAStream().stream());
 }
 
+// Two query tiles per CTA, P in tensor memory; head_dim 64 or 128.
+void flash_fwd2(const at::Tensor& q, int64_t q_col0, const at::Tensor& k, int64_t k_col0, const at::Tensor& v,
+                int64_t v_col0, at::Tensor& o, at::Tensor& lse, int64_t B, int64_t Sq, int64_t Sk, int64_t Hq,
+                int64_t Hkv, int64_t D, double scale, bool causal, const c10::optional<at::Tensor>& seg) {
+  check_buf(q, "q");
+  check_buf(k, "k");
+  check_buf(v, "v");
+  check_buf(o, "o");
+  TORCH_CHECK(D == 64 || D == 128, "flash_fwd2: head_dim must be 64 or 128");
+  TORCH_CHECK(Hq % Hkv == 0, "Hq must be a multiple of Hkv");
+  TORCH_CHECK(q.size(0) == B * Sq && k.size(0) == B * Sk && v.size(0) == B * Sk && o.size(0) == B * Sq, "rows");
+  TORCH_CHECK(q.size(1) >= q_col0 + Hq * D && k.size(1) >= k_col0 + Hkv * D && v.size(1) >= v_col0 + Hkv * D,
+              "q/k/v too narrow for the heads");
+  TORCH_CHECK(o.size(1) >= Hq * D, "o too narrow");
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.is_contiguous() && lse.numel() == B * Hq * Sq,
+              "lse must be fp32 [B, Hq, Sq]");
+  TORCH_CHECK(q_col0 % 8 == 0 && k_col0 % 8 == 0 && v_col0 % 8 == 0, "column offsets must be 16-byte aligned");
+  c10::cuda::CUDAGuard g(q.device());
+  astrai_host::flash_fwd_pair(q.data_ptr(), q.stride(0), (int)q_col0, k.data_ptr(), k.stride(0), (int)k_col0,
+                              v.data_ptr(), v.stride(0), (int)v_col0, o.data_ptr(), o.stride(0), lse.data_ptr<float>(),
+                              (int)B, (int)Sq, (int)Sk, (int)Hq, (int)Hkv, (int)D, (float)scale, causal ? 1 : 0,
+                              seg_ptr(seg, B, Sk), at::cuda::getCurrentCUDAStream().stream());
+}
+
 void flash_bwd(const at::Tensor& q, int64_t q_col0, const at::Tensor& k, int64_t k_col0, const at::Tensor& v,
                int64_t v_col0, const at::Tensor& o, const at::Tensor& dout, const at::Tensor& lse, at::Tensor& delta,
                at::Tensor& dq_acc, at::Tensor& dq, int64_t dq_col0, at::Tensor& dk, int64_t dk_col0, at::Tensor& dv,
@@ -81,5 +108,6 @@ void flash_bwd(const at::Tensor& q, int64_t q_col0, const at::Tensor& k, int64_t
 
 void register_attention(pybind11::module& m) {
   m.def("flash_fwd", &flash_fwd);
+  m.def("flash_fwd2", &flash_fwd2);
   m.def("flash_bwd", &flash_bwd);
 }

@@ -9,12 +9,12 @@
 namespace astrai_host {
 int num_sms(int device);
 void paged_kv_write(const void* k, const void* v, long long ld_src, const int* slot, int T, int Hkv, int page_size,
-                    int n_pages, void* kc, void* vc, cudaStream_t s);
+                    int n_pages, void* kc, void* vc, int D, cudaStream_t s);
 void paged_kv_gather(const void* kc, const void* vc, const int* table, int max_pages, const int* lens, int B, int S_out,
-                     int Hkv, int page_size, int n_pages, void* ko, void* vo, cudaStream_t s);
+                     int Hkv, int page_size, int n_pages, void* ko, void* vo, int D, cudaStream_t s);
 void paged_decode_launch(const void* q, long long ldq, const void* kc, const void* vc, const int* table, int max_pages,
                          int n_pages, const int* lens, int B, int Hq, int Hkv, int page_size, int splits, float scale_log2,
-                         float* part_acc, float* part_ml, void* out, long long ldo, cudaStream_t s);
+                         float* part_acc, float* part_ml, void* out, long long ldo, int D, cudaStream_t s);
 int decode_splits(int B, int Hkv, int max_len, int sms);
 void sample_tokens(const void* logits, int f32, long long ld, int rows, int V, const float* temperature,
                    const int* top_k, const float* top_p, const float* penalty, const long long* hist, int hist_len,
@@ -26,11 +26,12 @@ namespace {
 
 cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 
-void check_cache(const at::Tensor& c, const char* name) {
-  // [n_pages, Hkv, page_size, 128] bf16 contiguous
+// [n_pages, Hkv, page_size, D] bf16 contiguous, D = 64 or 128; returns D
+int check_cache(const at::Tensor& c, const char* name) {
   TORCH_CHECK(c.is_cuda() && c.scalar_type() == at::kBFloat16, name, " must be a CUDA bfloat16 tensor");
-  TORCH_CHECK(c.dim() == 4 && c.size(3) == 128 && c.is_contiguous(), name,
-              " must be contiguous [n_pages, n_kv_heads, page_size, 128]");
+  TORCH_CHECK(c.dim() == 4 && (c.size(3) == 128 || c.size(3) == 64) && c.is_contiguous(), name,
+              " must be contiguous [n_pages, n_kv_heads, page_size, head_dim] with head_dim 64 or 128");
+  return static_cast<int>(c.size(3));
 }
 
 void check_i32(const at::Tensor& t, const char* name) {
@@ -45,42 +46,42 @@ void check_rows16(const at::Tensor& t, const char* name) {
               " rows must be 16-byte aligned");
 }
 
-// k / v: [T, >= Hkv*128] row views (e.g. column slices of a fused qkv buffer)
+// k / v: [T, >= Hkv*D] row views (e.g. column slices of a fused qkv buffer)
 void paged_kv_write(const at::Tensor& k, const at::Tensor& v, const at::Tensor& slot, at::Tensor& kc, at::Tensor& vc) {
   check_rows16(k, "k");
   check_rows16(v, "v");
   TORCH_CHECK(k.stride(0) == v.stride(0), "k and v must share a row stride");
   check_i32(slot, "slot");
-  check_cache(kc, "k_cache");
-  check_cache(vc, "v_cache");
+  const int D = check_cache(kc, "k_cache");
+  TORCH_CHECK(check_cache(vc, "v_cache") == D && vc.sizes() == kc.sizes(), "k_cache / v_cache shapes differ");
   const int T = static_cast<int>(k.size(0));
   TORCH_CHECK(slot.numel() == T && v.size(0) == T, "slot / v row count mismatch");
   const int Hkv = static_cast<int>(kc.size(1));
-  TORCH_CHECK(k.size(1) >= Hkv * 128 && v.size(1) >= Hkv * 128, "k/v narrower than n_kv_heads * 128");
+  TORCH_CHECK(k.size(1) >= Hkv * D && v.size(1) >= Hkv * D, "k/v narrower than n_kv_heads * head_dim");
   if (T == 0) return;
   const c10::cuda::CUDAGuard g(k.device());
   astrai_host::paged_kv_write(k.data_ptr(), v.data_ptr(), k.stride(0), slot.data_ptr<int>(), T, Hkv,
                               static_cast<int>(kc.size(2)), static_cast<int>(kc.size(0)), kc.data_ptr(), vc.data_ptr(),
-                              cur_stream());
+                              D, cur_stream());
 }
 
-// -> (k, v) [B, S_out, Hkv, 128]; rows past lens[b] are zero
+// -> (k, v) [B, S_out, Hkv, D]; rows past lens[b] are zero
 std::vector<at::Tensor> paged_kv_gather(const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& table,
                                         const at::Tensor& lens, int64_t S_out) {
-  check_cache(kc, "k_cache");
-  check_cache(vc, "v_cache");
+  const int D = check_cache(kc, "k_cache");
+  TORCH_CHECK(check_cache(vc, "v_cache") == D && vc.sizes() == kc.sizes(), "k_cache / v_cache shapes differ");
   check_i32(table, "page_table");
   check_i32(lens, "lens");
   TORCH_CHECK(table.dim() == 2 && lens.numel() == table.size(0), "page_table [B, max_pages] / lens [B] mismatch");
   const int B = static_cast<int>(table.size(0));
   const int Hkv = static_cast<int>(kc.size(1));
-  auto ko = at::empty({B, S_out, Hkv, 128}, kc.options());
-  auto vo = at::empty({B, S_out, Hkv, 128}, kc.options());
+  auto ko = at::empty({B, S_out, Hkv, D}, kc.options());
+  auto vo = at::empty({B, S_out, Hkv, D}, kc.options());
   if (B == 0 || S_out == 0) return {ko, vo};
   const c10::cuda::CUDAGuard g(kc.device());
   astrai_host::paged_kv_gather(kc.data_ptr(), vc.data_ptr(), table.data_ptr<int>(), static_cast<int>(table.size(1)),
                                lens.data_ptr<int>(), B, static_cast<int>(S_out), Hkv, static_cast<int>(kc.size(2)),
-                               static_cast<int>(kc.size(0)), ko.data_ptr(), vo.data_ptr(), cur_stream());
+                               static_cast<int>(kc.size(0)), ko.data_ptr(), vo.data_ptr(), D, cur_stream());
   return {ko, vo};
 }
 
@@ -89,15 +90,15 @@ int64_t decode_splits(int64_t B, int64_t Hkv, int64_t max_len, int64_t device) {
                                     astrai_host::num_sms(static_cast<int>(device)));
 }
 
-// q: [B, >= Hq*128] rows; out: [B, Hq*128] rows; workspace fp32 with
-// >= B*Hq*splits*130 elements when splits > 1
+// q: [B, >= Hq*D] rows; out: [B, Hq*D] rows; workspace fp32 with
+// >= B*Hq*splits*(D + 2) elements when splits > 1
 void paged_decode(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& table,
                   const at::Tensor& lens, at::Tensor& out, int64_t Hq, double scale, int64_t splits,
                   const c10::optional<at::Tensor>& workspace) {
   check_rows16(q, "q");
   check_rows16(out, "out");
-  check_cache(kc, "k_cache");
-  check_cache(vc, "v_cache");
+  const int D = check_cache(kc, "k_cache");
+  TORCH_CHECK(check_cache(vc, "v_cache") == D && vc.sizes() == kc.sizes(), "k_cache / v_cache shapes differ");
   check_i32(table, "page_table");
   check_i32(lens, "lens");
   const int B = static_cast<int>(q.size(0));
@@ -106,7 +107,7 @@ void paged_decode(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& v
   const int G = static_cast<int>(Hq / Hkv);
   TORCH_CHECK(G == 1 || G == 2 || G == 4 || G == 8, "paged_decode: n_heads / n_kv_heads must be 1, 2, 4 or 8");
   TORCH_CHECK(table.dim() == 2 && table.size(0) == B && lens.numel() == B, "page_table / lens batch mismatch");
-  TORCH_CHECK(q.size(1) >= Hq * 128 && out.size(0) == B && out.size(1) >= Hq * 128, "q/out shape mismatch");
+  TORCH_CHECK(q.size(1) >= Hq * D && out.size(0) == B && out.size(1) >= Hq * D, "q/out shape mismatch");
   TORCH_CHECK(splits >= 1 && splits <= 64, "splits must be in [1, 64]");
   if (B == 0) return;
   float* part_acc = nullptr;
@@ -115,10 +116,10 @@ void paged_decode(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& v
     TORCH_CHECK(workspace.has_value(), "paged_decode: splits > 1 needs a workspace");
     const auto& w = *workspace;
     TORCH_CHECK(w.is_cuda() && w.scalar_type() == at::kFloat && w.is_contiguous(), "workspace must be fp32 CUDA");
-    const long long need = (long long)B * Hq * splits * 130;
+    const long long need = (long long)B * Hq * splits * (D + 2);
     TORCH_CHECK(w.numel() >= need, "workspace too small: need ", need, " fp32 elements");
     part_acc = w.data_ptr<float>();
-    part_ml = part_acc + (long long)B * Hq * splits * 128;
+    part_ml = part_acc + (long long)B * Hq * splits * D;
   }
   const c10::cuda::CUDAGuard g(q.device());
   astrai_host::paged_decode_launch(q.data_ptr(), q.stride(0), kc.data_ptr(), vc.data_ptr(), table.data_ptr<int>(),
@@ -126,7 +127,7 @@ void paged_decode(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& v
                                    B, static_cast<int>(Hq), Hkv,
                                    static_cast<int>(kc.size(2)), static_cast<int>(splits),
                                    static_cast<float>(scale * 1.4426950408889634), part_acc, part_ml, out.data_ptr(),
-                                   out.stride(0), cur_stream());
+                                   out.stride(0), D, cur_stream());
 }
 
 // logits [rows, V] (bf16 or fp32, unit inner stride); per-row parameters are

@@ -1,7 +1,7 @@
 // Inference kernels (sm_100a): paged KV-cache write / gather, paged split-KV
 // decode attention, split combine, and the fused token sampler.
 //
-// Paged KV layout (per layer):  cache[page][kv_head][slot][128]  (bf16)
+// Paged KV layout (per layer):  cache[page][kv_head][slot][D]  (bf16, D = 64 or 128)
 // so the keys of one head inside a page are contiguous and a decode warp
 // streams them with fully coalesced 256-byte rows.
 //
@@ -36,15 +36,15 @@ namespace cg = cooperative_groups;
 
 namespace astrai {
 
-constexpr int DEC_D = 128;
 constexpr int DEC_MAXG = 16;
 
 // ------------------------------------------------------------------ KV write / gather
 // src k/v: [T, Hkv, D] rows with row stride ld (elements); slot[t] = page * page_size + offset
 __global__ void paged_kv_write_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
                                       long long ld_src, const int* __restrict__ slot, int T, int Hkv, int page_size,
-                                      int n_pages, __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc) {
-  const int per = DEC_D / 8;  // 16-byte chunks per head row
+                                      int n_pages, __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc,
+                                      int D) {
+  const int per = D / 8;  // 16-byte chunks per head row
   const long long total = (long long)T * Hkv * per;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
     const int c = i % per;
@@ -54,8 +54,8 @@ __global__ void paged_kv_write_kernel(const __nv_bfloat16* __restrict__ k, const
     const int s = slot[t];
     if (s < 0 || s >= n_pages * page_size) continue;  // -1 = skip; never write outside the cache
     const int page = s / page_size, off = s % page_size;
-    const long long dst = (((long long)page * Hkv + h) * page_size + off) * DEC_D + c * 8;
-    const long long src = (long long)t * ld_src + h * DEC_D + c * 8;
+    const long long dst = (((long long)page * Hkv + h) * page_size + off) * D + c * 8;
+    const long long src = (long long)t * ld_src + h * D + c * 8;
     *reinterpret_cast<uint4*>(kc + dst) = *reinterpret_cast<const uint4*>(k + src);
     *reinterpret_cast<uint4*>(vc + dst) = *reinterpret_cast<const uint4*>(v + src);
   }
@@ -65,8 +65,8 @@ __global__ void paged_kv_write_kernel(const __nv_bfloat16* __restrict__ k, const
 __global__ void paged_kv_gather_kernel(const __nv_bfloat16* __restrict__ kc, const __nv_bfloat16* __restrict__ vc,
                                        const int* __restrict__ table, int max_pages, const int* __restrict__ lens,
                                        int B, int S_out, int Hkv, int page_size, int n_pages, __nv_bfloat16* __restrict__ ko,
-                                       __nv_bfloat16* __restrict__ vo) {
-  const int per = DEC_D / 8;
+                                       __nv_bfloat16* __restrict__ vo, int D) {
+  const int per = D / 8;
   const long long total = (long long)B * S_out * Hkv * per;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
     const int c = i % per;
@@ -79,12 +79,12 @@ __global__ void paged_kv_gather_kernel(const __nv_bfloat16* __restrict__ kc, con
     if (pos < lens[b] && pos / page_size < max_pages) {
       const int page = table[(long long)b * max_pages + pos / page_size];
       if (page >= 0 && page < n_pages) {
-        const long long src = (((long long)page * Hkv + h) * page_size + pos % page_size) * DEC_D + c * 8;
+        const long long src = (((long long)page * Hkv + h) * page_size + pos % page_size) * D + c * 8;
         kk = *reinterpret_cast<const uint4*>(kc + src);
         vv = *reinterpret_cast<const uint4*>(vc + src);
       }
     }
-    const long long dst = (((long long)b * S_out + pos) * Hkv + h) * DEC_D + c * 8;
+    const long long dst = (((long long)b * S_out + pos) * Hkv + h) * D + c * 8;
     *reinterpret_cast<uint4*>(ko + dst) = kk;
     *reinterpret_cast<uint4*>(vo + dst) = vv;
   }
@@ -114,8 +114,29 @@ __device__ __forceinline__ float ex2f_fast(float x) {
   return y;
 }
 
-template <int G>
+// head-dim elements of a K/V row held by one lane: D / 32 (4 for D = 128, 2 for D = 64), loaded as one
+// 8- or 4-byte vector
+template <int DPL>
+struct LaneVec;
+template <>
+struct LaneVec<4> {
+  static __device__ __forceinline__ void load(const __nv_bfloat16* p, float (&f)[4]) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const float2 a = unpack_bf16(u.x), b = unpack_bf16(u.y);
+    f[0] = a.x, f[1] = a.y, f[2] = b.x, f[3] = b.y;
+  }
+};
+template <>
+struct LaneVec<2> {
+  static __device__ __forceinline__ void load(const __nv_bfloat16* p, float (&f)[2]) {
+    const float2 a = unpack_bf16(*reinterpret_cast<const uint32_t*>(p));
+    f[0] = a.x, f[1] = a.y;
+  }
+};
+
+template <int G, int D>
 __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams p) {
+  constexpr int DPL = D / 32;
   const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int len = p.lens[b];
@@ -123,31 +144,28 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams p) {
   const int kps = ((len + p.splits - 1) / p.splits + 15) & ~15;
   const int k0 = split * kps;
   const int k1 = min(len, k0 + kps);
-  // q for the G heads of this group: lane owns dims [4*lane, 4*lane+4)
-  float q[G][4];
+  // q for the G heads of this group: lane owns dims [DPL*lane, DPL*lane + DPL)
+  float q[G][DPL];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    const __nv_bfloat16* qp = p.q + (long long)b * p.ldq + (hk * G + g) * DEC_D + lane * 4;
-    const uint2 u = *reinterpret_cast<const uint2*>(qp);
-    const float2 a = unpack_bf16(u.x), c = unpack_bf16(u.y);
-    q[g][0] = a.x * p.scale_log2;
-    q[g][1] = a.y * p.scale_log2;
-    q[g][2] = c.x * p.scale_log2;
-    q[g][3] = c.y * p.scale_log2;
+    LaneVec<DPL>::load(p.q + (long long)b * p.ldq + (hk * G + g) * D + lane * DPL, q[g]);
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) q[g][i] *= p.scale_log2;
   }
-  float m[G], l[G], acc[G][4];
+  float m[G], l[G], acc[G][DPL];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     m[g] = -INFINITY;
     l[g] = 0.f;
-    acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.f;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) acc[g][i] = 0.f;
   }
   const int* trow = p.table + (long long)b * p.max_pages;
   // each warp takes 4 consecutive keys per iteration: 8 independent 8-byte
   // loads per lane in flight before any math
   constexpr int KU = 4;
   for (int kb = k0 + warp * KU; kb < k1; kb += 4 * KU) {
-    uint2 ku[KU], vu[KU];
+    float kf[KU][DPL], vf[KU][DPL];
     bool ok[KU];
 #pragma unroll
     for (int u = 0; u < KU; ++u) {
@@ -156,20 +174,24 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams p) {
       const int page = (k < k1 && pidx < p.max_pages) ? trow[pidx] : -1;
       ok[u] = page >= 0 && page < p.n_pages;
       if (ok[u]) {
-        const long long row = (((long long)page * p.Hkv + hk) * p.page_size + k % p.page_size) * DEC_D + lane * 4;
-        ku[u] = *reinterpret_cast<const uint2*>(p.kc + row);
-        vu[u] = *reinterpret_cast<const uint2*>(p.vc + row);
+        const long long row = (((long long)page * p.Hkv + hk) * p.page_size + k % p.page_size) * D + lane * DPL;
+        LaneVec<DPL>::load(p.kc + row, kf[u]);
+        LaneVec<DPL>::load(p.vc + row, vf[u]);
       } else {
-        ku[u] = vu[u] = make_uint2(0, 0);
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) kf[u][i] = vf[u][i] = 0.f;
       }
     }
     float s[KU][G];
 #pragma unroll
     for (int u = 0; u < KU; ++u) {
-      const float2 k01 = unpack_bf16(ku[u].x), k23 = unpack_bf16(ku[u].y);
 #pragma unroll
-      for (int g = 0; g < G; ++g)
-        s[u][g] = q[g][0] * k01.x + q[g][1] * k01.y + q[g][2] * k23.x + q[g][3] * k23.y;
+      for (int g = 0; g < G; ++g) {
+        float d = 0.f;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) d = fmaf(q[g][i], kf[u][i], d);
+        s[u][g] = d;
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -189,23 +211,20 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams p) {
       m[g] = mx;
       l[g] *= corr;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) acc[g][i] *= corr;
+      for (int i = 0; i < DPL; ++i) acc[g][i] *= corr;
 #pragma unroll
       for (int u = 0; u < KU; ++u) {
         if (!ok[u]) continue;
         const float e = ex2f_fast(s[u][g] - mx);
-        const float2 v01 = unpack_bf16(vu[u].x), v23 = unpack_bf16(vu[u].y);
         l[g] += e;
-        acc[g][0] += e * v01.x;
-        acc[g][1] += e * v01.y;
-        acc[g][2] += e * v23.x;
-        acc[g][3] += e * v23.y;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) acc[g][i] = fmaf(e, vf[u][i], acc[g][i]);
       }
     }
   }
   // merge the 4 warps through shared memory
   __shared__ float sm_ml[4][G][2];
-  __shared__ float sm_acc[4][G][DEC_D];
+  __shared__ float sm_acc[4][G][D];
   if (lane == 0) {
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -216,10 +235,10 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams p) {
 #pragma unroll
   for (int g = 0; g < G; ++g)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) sm_acc[warp][g][lane * 4 + i] = acc[g][i];
+    for (int i = 0; i < DPL; ++i) sm_acc[warp][g][lane * DPL + i] = acc[g][i];
   __syncthreads();
-  for (int idx = threadIdx.x; idx < G * DEC_D; idx += 128) {
-    const int g = idx / DEC_D, d = idx % DEC_D;
+  for (int idx = threadIdx.x; idx < G * D; idx += 128) {
+    const int g = idx / D, d = idx % D;
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_ml[w][g][0]);
@@ -233,10 +252,10 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams p) {
       }
     }
     if (p.splits == 1) {
-      p.out[(long long)b * p.ldo + (hk * G + g) * DEC_D + d] = __float2bfloat16_rn(L > 0.f ? A / L : 0.f);
+      p.out[(long long)b * p.ldo + (hk * G + g) * D + d] = __float2bfloat16_rn(L > 0.f ? A / L : 0.f);
     } else {
       const long long base = (((long long)b * p.Hkv + hk) * p.splits + split) * G + g;
-      p.part_acc[base * DEC_D + d] = A;
+      p.part_acc[base * D + d] = A;
       if (d == 0) {
         p.part_ml[base * 2] = M;
         p.part_ml[base * 2 + 1] = L;
@@ -247,7 +266,8 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams p) {
 
 // merge split partials: one block per (b, q head), D threads
 __global__ void decode_combine_kernel(const float* __restrict__ part_acc, const float* __restrict__ part_ml, int B,
-                                      int Hq, int Hkv, int splits, __nv_bfloat16* __restrict__ out, long long ldo) {
+                                      int Hq, int Hkv, int splits, __nv_bfloat16* __restrict__ out, long long ldo,
+                                      int D) {
   const int bh = blockIdx.x;
   const int b = bh / Hq, h = bh % Hq;
   const int G = Hq / Hkv, hk = h / G, g = h % G;
@@ -261,10 +281,10 @@ __global__ void decode_combine_kernel(const float* __restrict__ part_acc, const 
       const long long base = (((long long)b * Hkv + hk) * splits + s) * G + g;
       const float c = ex2f_fast(part_ml[base * 2] - M);
       L += part_ml[base * 2 + 1] * c;
-      A += part_acc[base * DEC_D + d] * c;
+      A += part_acc[base * D + d] * c;
     }
   }
-  out[(long long)b * ldo + h * DEC_D + d] = __float2bfloat16_rn(L > 0.f ? A / L : 0.f);
+  out[(long long)b * ldo + h * D + d] = __float2bfloat16_rn(L > 0.f ? A / L : 0.f);
 }
 
 // ------------------------------------------------------------------ sampling
@@ -704,30 +724,41 @@ namespace astrai_host {
 using namespace astrai;
 
 void paged_kv_write(const void* k, const void* v, long long ld_src, const int* slot, int T, int Hkv, int page_size,
-                    int n_pages, void* kc, void* vc, cudaStream_t s) {
-  const long long work = (long long)T * Hkv * (DEC_D / 8);
+                    int n_pages, void* kc, void* vc, int D, cudaStream_t s) {
+  const long long work = (long long)T * Hkv * (D / 8);
   int blocks = (int)std::min<long long>((work + 255) / 256, 148 * 8);
   if (blocks < 1) blocks = 1;
   (astrai::note_launch(), paged_kv_write_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(k),
                                                static_cast<const __nv_bfloat16*>(v), ld_src, slot, T, Hkv, page_size, n_pages,
-                                               static_cast<__nv_bfloat16*>(kc), static_cast<__nv_bfloat16*>(vc)));
+                                               static_cast<__nv_bfloat16*>(kc), static_cast<__nv_bfloat16*>(vc), D));
 }
 
 void paged_kv_gather(const void* kc, const void* vc, const int* table, int max_pages, const int* lens, int B, int S_out,
-                     int Hkv, int page_size, int n_pages, void* ko, void* vo, cudaStream_t s) {
-  const long long work = (long long)B * S_out * Hkv * (DEC_D / 8);
+                     int Hkv, int page_size, int n_pages, void* ko, void* vo, int D, cudaStream_t s) {
+  const long long work = (long long)B * S_out * Hkv * (D / 8);
   int blocks = (int)std::min<long long>((work + 255) / 256, 148 * 16);
   if (blocks < 1) blocks = 1;
   (astrai::note_launch(), paged_kv_gather_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(kc),
                                                 static_cast<const __nv_bfloat16*>(vc), table, max_pages, lens, B, S_out,
                                                 Hkv, page_size, n_pages, static_cast<__nv_bfloat16*>(ko),
-                                                static_cast<__nv_bfloat16*>(vo)));
+                                                static_cast<__nv_bfloat16*>(vo), D));
 }
 
-// splits > 1 writes partials to part_acc [B*Hq*splits*128] / part_ml [B*Hq*splits*2]
+template <int D>
+static void decode_dispatch(const DecodeParams& p, dim3 grid, int G, cudaStream_t s) {
+  switch (G) {
+    case 1: (astrai::note_launch(), paged_decode_kernel<1, D><<<grid, 128, 0, s>>>(p)); break;
+    case 2: (astrai::note_launch(), paged_decode_kernel<2, D><<<grid, 128, 0, s>>>(p)); break;
+    case 4: (astrai::note_launch(), paged_decode_kernel<4, D><<<grid, 128, 0, s>>>(p)); break;
+    case 8: (astrai::note_launch(), paged_decode_kernel<8, D><<<grid, 128, 0, s>>>(p)); break;
+    default: throw std::runtime_error("paged_decode: n_heads / n_kv_heads must be 1, 2, 4 or 8");
+  }
+}
+
+// splits > 1 writes partials to part_acc [B*Hq*splits*D] / part_ml [B*Hq*splits*2]; D = 64 or 128
 void paged_decode_launch(const void* q, long long ldq, const void* kc, const void* vc, const int* table, int max_pages,
                          int n_pages, const int* lens, int B, int Hq, int Hkv, int page_size, int splits, float scale_log2,
-                         float* part_acc, float* part_ml, void* out, long long ldo, cudaStream_t s) {
+                         float* part_acc, float* part_ml, void* out, long long ldo, int D, cudaStream_t s) {
   DecodeParams p;
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.ldq = ldq;
@@ -748,15 +779,15 @@ void paged_decode_launch(const void* q, long long ldq, const void* kc, const voi
   p.out = static_cast<__nv_bfloat16*>(out);
   p.ldo = ldo;
   dim3 grid(splits, Hkv, B);
-  switch (Hq / Hkv) {
-    case 1: (astrai::note_launch(), paged_decode_kernel<1><<<grid, 128, 0, s>>>(p)); break;
-    case 2: (astrai::note_launch(), paged_decode_kernel<2><<<grid, 128, 0, s>>>(p)); break;
-    case 4: (astrai::note_launch(), paged_decode_kernel<4><<<grid, 128, 0, s>>>(p)); break;
-    case 8: (astrai::note_launch(), paged_decode_kernel<8><<<grid, 128, 0, s>>>(p)); break;
-    default: throw std::runtime_error("paged_decode: n_heads / n_kv_heads must be 1, 2, 4 or 8");
-  }
+  if (D == 128)
+    decode_dispatch<128>(p, grid, Hq / Hkv, s);
+  else if (D == 64)
+    decode_dispatch<64>(p, grid, Hq / Hkv, s);
+  else
+    throw std::runtime_error("paged_decode: head_dim must be 64 or 128");
   if (splits > 1)
-    (astrai::note_launch(), decode_combine_kernel<<<B * Hq, DEC_D, 0, s>>>(part_acc, part_ml, B, Hq, Hkv, splits, static_cast<__nv_bfloat16*>(out), ldo));
+    (astrai::note_launch(), decode_combine_kernel<<<B * Hq, D, 0, s>>>(part_acc, part_ml, B, Hq, Hkv, splits,
+                                                                      static_cast<__nv_bfloat16*>(out), ldo, D));
 }
 
 // Splits per (batch row, kv head): enough CTAs for two waves of the SMs,

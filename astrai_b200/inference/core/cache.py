@@ -39,6 +39,7 @@ from torch import Tensor
 
 _MASK64 = 0xFFFFFFFFFFFFFFFF
 HEAD_DIM = 128
+KERNEL_HEAD_DIMS = (64, 128)  # head sizes the cache kernels (write, gather, decode) support
 
 
 def _page_hash_step(prev: int, token_ids: Sequence[int], start: int, end: int) -> int:
@@ -255,7 +256,7 @@ class Storage:
 
     @property
     def native_ok(self) -> bool:
-        return self.k_cache.is_cuda and self.k_cache.dtype == torch.bfloat16 and self.head_dim == HEAD_DIM
+        return self.k_cache.is_cuda and self.k_cache.dtype == torch.bfloat16 and self.head_dim in KERNEL_HEAD_DIMS
 
     # --------------------------------------------------------------- slot-level primitives
     def write_slots(self, layer_id: int, slots: Tensor, k: Tensor, v: Tensor) -> None:
@@ -384,7 +385,7 @@ class PageCacheView(CacheView):
 
     @property
     def supports_qkv(self) -> bool:
-        """True when :meth:`attend_qkv` runs natively (CUDA bf16, head dim 128)."""
+        """True when :meth:`attend_qkv` runs natively (CUDA bf16, head dim 64 or 128)."""
         return self._storage.native_ok
 
     # ------------------------------------------------------------ geometry
@@ -432,12 +433,13 @@ class PageCacheView(CacheView):
         if self._splits is None:
             cap = self.table.shape[1] * st.page_size
             self._splits = int(C.decode_splits(self.B, st.n_kv_heads, cap, q_rows.device.index or 0))
-        if self._splits > 1 and (self._workspace is None or self._workspace.numel() < self.B * Hq * self._splits * 130):
-            self._workspace = torch.empty(self.B * Hq * self._splits * 130, device=q_rows.device,
-                                          dtype=torch.float32)
-        out = torch.empty((self.B, Hq * HEAD_DIM), device=q_rows.device, dtype=torch.bfloat16)
+        D = st.head_dim
+        need = self.B * Hq * self._splits * (D + 2)
+        if self._splits > 1 and (self._workspace is None or self._workspace.numel() < need):
+            self._workspace = torch.empty(need, device=q_rows.device, dtype=torch.float32)
+        out = torch.empty((self.B, Hq * D), device=q_rows.device, dtype=torch.bfloat16)
         C.paged_decode(q_rows, st.k_cache[layer_id], st.v_cache[layer_id], self.table, self.lens, out, Hq,
-                       1.0 / math.sqrt(HEAD_DIM), self._splits, self._workspace)
+                       1.0 / math.sqrt(D), self._splits, self._workspace)
         return out
 
     def attend(self, layer_id: int, q: Tensor, k: Tensor, v: Tensor) -> Tensor:
@@ -446,7 +448,7 @@ class PageCacheView(CacheView):
 
         B, S, Hq, D = q.shape
         self.write(layer_id, k, v)
-        native = self._storage.native_ok and D == HEAD_DIM and q.dtype == torch.bfloat16
+        native = self._storage.native_ok and D == self._storage.head_dim and q.dtype == torch.bfloat16
         if native and S == 1:
             o = self._decode_native(layer_id, q.reshape(B, Hq * D).contiguous(), Hq)
             return o.view(B, 1, Hq, D)
@@ -459,13 +461,12 @@ class PageCacheView(CacheView):
         return self._ragged(layer_id, q, B, S, Hq)  # rows of different lengths
 
     def attend_qkv(self, layer_id: int, qkv: Tensor, B: int, S: int, Hq: int, Hkv: int, table: Tensor) -> Tensor:
-        """Fused path on a ``[B*S, (Hq+2Hkv)*128]`` bf16 buffer: RoPE in place,
-        K/V written straight from the buffer, attention -> ``[B*S, Hq*128]``."""
-        from astrai_b200.ops._ext import native
+        """Fused path on a ``[B*S, (Hq+2Hkv)*D]`` bf16 buffer (D = 64 or 128): RoPE in place,
+        K/V written straight from the buffer, attention -> ``[B*S, Hq*D]``."""
+        from astrai_b200.ops.attention import flash_forward
         from astrai_b200.ops.rope import rope_inplace
 
-        D = HEAD_DIM
-        C = native()
+        D = self._storage.head_dim
         pos = self.positions(S)
         rope_inplace(qkv, 0, Hq + Hkv, D, table, pos, S)
         self._storage.write_slots(layer_id, self.slots(S), qkv[:, Hq * D:(Hq + Hkv) * D],
@@ -477,15 +478,15 @@ class PageCacheView(CacheView):
         scale = 1.0 / math.sqrt(D)
         start = self._start(S)
         if start == 0:
-            C.flash_fwd(qkv, 0, qkv, Hq * D, qkv, (Hq + Hkv) * D, o, lse, B, S, S, Hq, Hkv, scale, True, None)
+            flash_forward(qkv, 0, qkv, Hq * D, qkv, (Hq + Hkv) * D, o, lse, B, S, S, Hq, Hkv, D, scale, True, None)
             return o
         if start is None:  # rows of different lengths (RoPE already applied in place)
             q = qkv[:, : Hq * D].reshape(B, S, Hq, D)
             return self._ragged(layer_id, q, B, S, Hq).reshape(B * S, Hq * D)
         total = start + S
         kk, vv = self._storage.gather_rows(layer_id, self.table, self.lens, total)
-        C.flash_fwd(qkv, 0, kk.view(B * total, Hkv * D), 0, vv.view(B * total, Hkv * D), 0, o, lse, B, S, total, Hq,
-                    Hkv, scale, True, None)
+        flash_forward(qkv, 0, kk.view(B * total, Hkv * D), 0, vv.view(B * total, Hkv * D), 0, o, lse, B, S, total,
+                      Hq, Hkv, D, scale, True, None)
         return o
 
     def _ragged(self, layer_id: int, q: Tensor, B: int, S: int, Hq: int) -> Tensor:

@@ -15,8 +15,10 @@ sequence (queries are the last ``Sq`` positions), GQA head ``h`` reads K/V head
 key-padding masks (DPO/GRPO) are passed as int32 segment ids: query q sees key
 k only if ``seg[q] == seg[k]`` (padding keys get unique negative ids).
 
-The CUDA kernels are specialised for head_dim 128; CPU tensors and other head
-sizes use the PyTorch reference math below.
+On CUDA the forward runs ``flash_fwd_pair_kernel`` (two query tiles per CTA, P kept in tensor
+memory; head_dim 64 or 128); ``ASTRAI_FLASH_FWD_PAIR=0`` selects the one-tile kernel
+(head_dim 128 only). The backward kernel covers head_dim 128. CPU tensors and other head sizes
+use the PyTorch reference math below.
 """
 
 from __future__ import annotations
@@ -31,6 +33,18 @@ from astrai_b200.ops._ext import native
 from astrai_b200.ops.rope import apply_rope_reference, rope_inplace
 
 HEAD_DIM = 128
+FWD_HEAD_DIMS = (64, 128)
+PAIR_FWD = __import__("os").environ.get("ASTRAI_FLASH_FWD_PAIR", "1") != "0"
+
+
+def flash_forward(q, q_col0, k, k_col0, v, v_col0, o, lse, B, Sq, Sk, Hq, Hkv, D, scale, causal, seg):
+    """Forward kernel on row buffers (head ``h`` of q at columns ``q_col0 + h*D``, same for k/v)."""
+    C = native()
+    if PAIR_FWD:
+        C.flash_fwd2(q, q_col0, k, k_col0, v, v_col0, o, lse, B, Sq, Sk, Hq, Hkv, D, scale, causal, seg)
+    else:
+        assert D == HEAD_DIM, "the one-tile forward kernel supports head_dim 128 only"
+        C.flash_fwd(q, q_col0, k, k_col0, v, v_col0, o, lse, B, Sq, Sk, Hq, Hkv, scale, causal, seg)
 
 
 # ----------------------------------------------------------------------------- reference math
@@ -83,7 +97,8 @@ class _AttnQKVFn(torch.autograd.Function):
             rope_inplace(qkv, 0, Hq + Hkv, D, table, positions, S)  # q and k heads are adjacent
         o = torch.empty((B * S, Hq * D), device=qkv.device, dtype=torch.bfloat16)
         lse = torch.empty((B, Hq, S), device=qkv.device, dtype=torch.float32)
-        C.flash_fwd(qkv, 0, qkv, Hq * D, qkv, (Hq + Hkv) * D, o, lse, B, S, S, Hq, Hkv, 1.0 / math.sqrt(D), causal, seg)
+        flash_forward(qkv, 0, qkv, Hq * D, qkv, (Hq + Hkv) * D, o, lse, B, S, S, Hq, Hkv, D, 1.0 / math.sqrt(D),
+                      causal, seg)
         ctx.save_for_backward(qkv, o, lse, table, positions, seg)
         ctx.dims = (B, S, Hq, Hkv, causal)
         ctx.rotated = rotated
@@ -143,7 +158,7 @@ class _AttnFn(torch.autograd.Function):
         v2 = v.reshape(B * Sk, Hkv * D).contiguous()
         o = torch.empty((B * Sq, Hq * D), device=q.device, dtype=torch.bfloat16)
         lse = torch.empty((B, Hq, Sq), device=q.device, dtype=torch.float32)
-        C.flash_fwd(q2, 0, k2, 0, v2, 0, o, lse, B, Sq, Sk, Hq, Hkv, 1.0 / math.sqrt(D), causal, seg)
+        flash_forward(q2, 0, k2, 0, v2, 0, o, lse, B, Sq, Sk, Hq, Hkv, D, 1.0 / math.sqrt(D), causal, seg)
         ctx.save_for_backward(q2, k2, v2, o, lse, seg)
         ctx.dims = (B, Sq, Sk, Hq, Hkv, causal)
         return o.view(B, Sq, Hq, D)
@@ -166,13 +181,31 @@ class _AttnFn(torch.autograd.Function):
         return dq.view(B, Sq, Hq, D), dk, dv, None, None
 
 
+def _forward_only(q, k, v, seg, causal):
+    """Kernel forward without autograd state (inference, or head sizes the backward kernel lacks)."""
+    B, Sq, Hq, D = q.shape
+    Sk, Hkv = k.shape[1], k.shape[2]
+    q2 = q.reshape(B * Sq, Hq * D).contiguous()
+    k2 = k.reshape(B * Sk, Hkv * D).contiguous()
+    v2 = v.reshape(B * Sk, Hkv * D).contiguous()
+    o = torch.empty((B * Sq, Hq * D), device=q.device, dtype=torch.bfloat16)
+    lse = torch.empty((B, Hq, Sq), device=q.device, dtype=torch.float32)
+    flash_forward(q2, 0, k2, 0, v2, 0, o, lse, B, Sq, Sk, Hq, Hkv, D, 1.0 / math.sqrt(D), causal, seg)
+    return o.view(B, Sq, Hq, D)
+
+
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
               seg: Optional[torch.Tensor] = None) -> torch.Tensor:
     """q [B,Sq,Hq,D], k/v [B,Sk,Hkv,D] -> [B,Sq,Hq,D]."""
     D = q.shape[-1]
-    if q.is_cuda and q.dtype == torch.bfloat16 and D == HEAD_DIM and k.shape[-1] == D and v.shape[-1] == D:
+    kernel_ok = q.is_cuda and q.dtype == torch.bfloat16 and k.shape[-1] == D and v.shape[-1] == D
+    if kernel_ok and D == HEAD_DIM:
         sg = seg.to(torch.int32).contiguous() if seg is not None else None
         return _AttnFn.apply(q, k, v, sg, causal)
+    grad = torch.is_grad_enabled() and any(t.requires_grad for t in (q, k, v))
+    if kernel_ok and PAIR_FWD and D in FWD_HEAD_DIMS and not grad:
+        sg = seg.to(torch.int32).contiguous() if seg is not None else None
+        return _forward_only(q, k, v, sg, causal)
     return _sdpa(q, k, v, causal, seg)
 
 
@@ -190,7 +223,10 @@ def bench_attention(time_fn, peaks):
     o = torch.empty(B * S, Hq * D, device="cuda", dtype=torch.bfloat16)
     lse = torch.empty(B, Hq, S, device="cuda", dtype=torch.float32)
     scale = 1.0 / math.sqrt(D)
-    fwd = lambda: C.flash_fwd(qkv, 0, qkv, Hq * D, qkv, (Hq + Hkv) * D, o, lse, B, S, S, Hq, Hkv, scale, True, None)
+    fwd1 = lambda: C.flash_fwd(qkv, 0, qkv, Hq * D, qkv, (Hq + Hkv) * D, o, lse, B, S, S, Hq, Hkv, scale, True, None)
+    fwd = lambda: C.flash_fwd2(qkv, 0, qkv, Hq * D, qkv, (Hq + Hkv) * D, o, lse, B, S, S, Hq, Hkv, D, scale, True,
+                               None)
+    ms1 = time_fn(fwd1)
     ms = time_fn(fwd)
     flops = 4.0 * B * Hq * S * S * D / 2  # causal
     q = qkv[:, : Hq * D].view(B, S, Hq, D).transpose(1, 2)
@@ -198,7 +234,8 @@ def bench_attention(time_fn, peaks):
     vv = qkv[:, (Hq + Hkv) * D:].view(B, S, Hkv, D).transpose(1, 2)
     ref = lambda: F.scaled_dot_product_attention(q, kk, vv, is_causal=True, enable_gqa=True)
     ms_ref = time_fn(ref)
-    print(json.dumps({"kernel": "flash_fwd", "B": B, "S": S, "Hq": Hq, "Hkv": Hkv, "ms": round(ms, 4),
+    print(json.dumps({"kernel": "flash_fwd_pair", "B": B, "S": S, "Hq": Hq, "Hkv": Hkv, "ms": round(ms, 4),
+                      "one_tile_kernel_ms": round(ms1, 4),
                       "tflops": round(flops / ms / 1e9, 1), "frac_of_peak": round(flops / ms / 1e9 / tf, 3),
                       "peak_src": src, "sdpa_ms": round(ms_ref, 4), "sdpa_tflops": round(flops / ms_ref / 1e9, 1)}))
     do = torch.randn_like(o)

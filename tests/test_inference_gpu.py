@@ -25,17 +25,17 @@ def _clean_error_word():
     assert native().read_error() == 0
 
 
-def _rand_cache(n_pages, Hkv, page, seed=0):
+def _rand_cache(n_pages, Hkv, page, seed=0, D=128):
     g = torch.Generator(device="cuda").manual_seed(seed)
-    kc = torch.randn(n_pages, Hkv, page, 128, device="cuda", generator=g).to(torch.bfloat16)
-    vc = torch.randn(n_pages, Hkv, page, 128, device="cuda", generator=g).to(torch.bfloat16)
+    kc = torch.randn(n_pages, Hkv, page, D, device="cuda", generator=g).to(torch.bfloat16)
+    vc = torch.randn(n_pages, Hkv, page, D, device="cuda", generator=g).to(torch.bfloat16)
     return kc, vc
 
 
 def _gather_ref(kc, vc, table, lens, total):
     B = table.shape[0]
     page = kc.shape[2]
-    k = torch.zeros(B, total, kc.shape[1], 128, device="cuda", dtype=torch.float32)
+    k = torch.zeros(B, total, kc.shape[1], kc.shape[3], device="cuda", dtype=torch.float32)
     v = torch.zeros_like(k)
     for b in range(B):
         for p in range(int(lens[b])):
@@ -46,17 +46,18 @@ def _gather_ref(kc, vc, table, lens, total):
     return k, v
 
 
+@pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("page", [16, 128])
-def test_paged_write_and_gather(page):
+def test_paged_write_and_gather(page, D):
     from astrai_b200.ops._ext import native
 
     C = native()
     Hkv, n_pages = 2, 12
-    kc, vc = _rand_cache(n_pages, Hkv, page)
+    kc, vc = _rand_cache(n_pages, Hkv, page, D=D)
     T = 3 * page // 2
-    qkv = torch.randn(T, (4 + 2 * Hkv) * 128, device="cuda").to(torch.bfloat16)
-    k = qkv[:, 4 * 128:(4 + Hkv) * 128]
-    v = qkv[:, (4 + Hkv) * 128:]
+    qkv = torch.randn(T, (4 + 2 * Hkv) * D, device="cuda").to(torch.bfloat16)
+    k = qkv[:, 4 * D:(4 + Hkv) * D]
+    v = qkv[:, (4 + Hkv) * D:]
     pages = torch.tensor([7, 3], device="cuda")
     pos = torch.arange(T, device="cuda")
     slots = (pages[pos // page] * page + pos % page).to(torch.int32)
@@ -66,10 +67,10 @@ def test_paged_write_and_gather(page):
     torch.cuda.synchronize()
     for t in (0, 5, T - 1):
         pg, off = int(pages[t // page]), t % page
-        want_k = kc0[pg, :, off] if t == 5 else k[t].view(Hkv, 128)
+        want_k = kc0[pg, :, off] if t == 5 else k[t].view(Hkv, D)
         assert torch.equal(kc[pg, :, off], want_k)
         if t != 5:
-            assert torch.equal(vc[pg, :, off], v[t].view(Hkv, 128))
+            assert torch.equal(vc[pg, :, off], v[t].view(Hkv, D))
     table = torch.tensor([[7, 3, -1], [3, -1, -1]], device="cuda", dtype=torch.int32)
     lens = torch.tensor([T, page // 2], device="cuda", dtype=torch.int32)
     ko, vo = C.paged_kv_gather(kc, vc, table, lens, 2 * page)
@@ -77,10 +78,11 @@ def test_paged_write_and_gather(page):
     assert torch.equal(ko.float(), kr) and torch.equal(vo.float(), vr)
 
 
+@pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("G", [1, 2, 4, 8])
 @pytest.mark.parametrize("page,lens", [(16, [1, 17, 300, 64]), (128, [513, 128, 5, 1000])])
 @pytest.mark.parametrize("splits", [1, 7])
-def test_paged_decode_matches_reference(G, page, lens, splits):
+def test_paged_decode_matches_reference(G, page, lens, splits, D):
     from astrai_b200.ops._ext import native
 
     C = native()
@@ -89,25 +91,25 @@ def test_paged_decode_matches_reference(G, page, lens, splits):
     Hq = G * Hkv
     max_pages = max(-(-L // page) for L in lens)
     n_pages = B * max_pages + 3
-    kc, vc = _rand_cache(n_pages, Hkv, page, seed=G)
+    kc, vc = _rand_cache(n_pages, Hkv, page, seed=G, D=D)
     perm = torch.randperm(n_pages)[: B * max_pages].view(B, max_pages)
     table = perm.to(torch.int32).cuda()
     for b, L in enumerate(lens):
         table[b, -(-L // page):] = -1
     ln = torch.tensor(lens, dtype=torch.int32, device="cuda")
-    q = torch.randn(B, Hq * 128, device="cuda").to(torch.bfloat16)
-    out = torch.empty(B, Hq * 128, device="cuda", dtype=torch.bfloat16)
-    ws = torch.empty(B * Hq * splits * 130, device="cuda", dtype=torch.float32)
-    scale = 1 / math.sqrt(128)
+    q = torch.randn(B, Hq * D, device="cuda").to(torch.bfloat16)
+    out = torch.empty(B, Hq * D, device="cuda", dtype=torch.bfloat16)
+    ws = torch.empty(B * Hq * splits * (D + 2), device="cuda", dtype=torch.float32)
+    scale = 1 / math.sqrt(D)
     C.paged_decode(q, kc, vc, table, ln, out, Hq, scale, splits, ws)
     kr, vr = _gather_ref(kc, vc, table, ln, max(lens))
     for b, L in enumerate(lens):
-        qb = q[b].view(Hq, 128).float()
+        qb = q[b].view(Hq, D).float()
         kb = kr[b, :L].repeat_interleave(G, dim=1)  # [L, Hq, D]
         vb = vr[b, :L].repeat_interleave(G, dim=1)
         s = torch.einsum("hd,lhd->hl", qb, kb) * scale
         o = torch.einsum("hl,lhd->hd", torch.softmax(s, -1), vb)
-        torch.testing.assert_close(out[b].view(Hq, 128).float(), o, atol=2e-2, rtol=2e-2)
+        torch.testing.assert_close(out[b].view(Hq, D).float(), o, atol=2e-2, rtol=2e-2)
 
 
 def _logits(rows, V, seed=0, spread=3.0):
@@ -178,12 +180,12 @@ def test_sample_distribution_matches_softmax():
     torch.testing.assert_close(k3[:3] / rows, p3, atol=1e-2, rtol=0)
 
 
-def _gpu_model(seed=0, layers=2, vocab=2048, heads=2, kv=1):
+def _gpu_model(seed=0, layers=2, vocab=2048, heads=2, kv=1, head_dim=128):
     from astrai_b200.config import AutoRegressiveLMConfig
     from astrai_b200.models import AutoRegressiveLM
 
     torch.manual_seed(seed)
-    cfg = AutoRegressiveLMConfig(vocab_size=vocab, hidden_size=128 * heads, num_attention_heads=heads,
+    cfg = AutoRegressiveLMConfig(vocab_size=vocab, hidden_size=head_dim * heads, num_attention_heads=heads,
                                  num_key_value_heads=kv, intermediate_size=384, num_hidden_layers=layers,
                                  max_position_embeddings=512, rms_norm_eps=1e-5, rope_theta=10000.0)
     m = AutoRegressiveLM(cfg).cuda().to(torch.bfloat16).eval()
@@ -202,13 +204,16 @@ class _Tok:
         return [int(x) for x in s.split()]
 
 
+@pytest.mark.parametrize("head_dim", [64, 128])
 @pytest.mark.parametrize("graph", [False, True])
 @pytest.mark.parametrize("paged", [False, True])
-def test_generation_matches_full_forward(graph, paged):
+def test_generation_matches_full_forward(graph, paged, head_dim):
+    """Prefill (flash forward), decode (paged split-KV kernel) and the sampler against a full forward pass;
+    head_dim 64 is the reference's benchmark model's head size (d 1536 over 24 heads)."""
     from astrai_b200.inference.core import InferenceScheduler, PageCache
 
-    m = _gpu_model(heads=4, kv=2)
-    cache = PageCache(2, 64, 16, 2, 128, "cuda", torch.bfloat16) if paged else None
+    m = _gpu_model(heads=4, kv=2, head_dim=head_dim)
+    cache = PageCache(2, 64, 16, 2, head_dim, "cuda", torch.bfloat16) if paged else None
     sch = InferenceScheduler(m, _Tok(), max_batch_size=4, max_seq_len=256, cache=cache, use_cuda_graph=graph)
     g = torch.Generator().manual_seed(0)
     prompts = [torch.randint(2, 2048, (n,), generator=g).tolist() for n in (5, 37, 16, 100)]
@@ -219,8 +224,9 @@ def test_generation_matches_full_forward(graph, paged):
             seq = torch.tensor([p + toks], device="cuda")
             ref = torch.log_softmax(m(seq)["logits"][0].float(), -1)[len(p) - 1:len(p) - 1 + len(toks)]
             ref_tok = ref.gather(1, torch.tensor(toks, device="cuda")[:, None]).squeeze(1)
-            # each generated token is (within bf16 noise) the argmax of the full forward pass
-            assert (ref.max(-1).values - ref_tok).max() < 0.1
+            # each generated token is (within bf16 noise) the argmax of the full forward pass: logits of
+            # magnitude 16 - 40 are spaced 0.125 - 0.25 apart in bf16, so near-ties may flip by one step
+            assert (ref.max(-1).values - ref_tok).max() <= 0.26
             # logits are O(30) here: bf16 rounding alone moves a log-probability by ~0.1
             torch.testing.assert_close(torch.tensor(lps, device="cuda"), ref_tok, atol=0.25, rtol=0.05)
     if paged:  # a second run over the same prompts reuses full prompt pages
