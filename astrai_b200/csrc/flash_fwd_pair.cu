@@ -223,22 +223,33 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     if (lane == 0 && n_blocks > 0) {
       constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);  // S = Q K^T, both K-major
       constexpr uint32_t idO = idesc_bf16(128, D, 0, 1);    // O += P V, V MN-major
-      const uint32_t q_base = smem_u32(sQ);
+      // Descriptors are built once; a K step only advances the 14-bit start-address field (in 16-byte
+      // units, no carry: shared addresses stay below 2^18 bytes), so each MMA costs a few instructions.
+      // The issuing warp shares its SM sub-partition with two softmax warps, and a 128x128x16 MMA
+      // lasts only ~64 tensor-core cycles, so issue cost decides whether the tensor core waits.
+      uint64_t dq[2], dk[ST], dv[ST];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) dq[i] = sdesc_sw128(smem_u32(sQ + i * Cfg::TILE), 16, 1024);
+#pragma unroll
+      for (int st = 0; st < ST; ++st) {
+        dk[st] = sdesc_sw128(smem_u32(sK + st * Cfg::TILE), 16, 1024);
+        dv[st] = sdesc_sw128(smem_u32(sV + st * Cfg::TILE), Cfg::CHUNK, 1024);
+      }
       auto issue_s = [&](int i, int j) {
-        const uint32_t qb = q_base + i * Cfg::TILE, kb = smem_u32(sK + (j % ST) * Cfg::TILE);
+        const uint64_t a = dq[i], b = dk[j % ST];
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
-          const uint32_t o = (k >> 2) * Cfg::CHUNK + (k & 3) * 32;
-          umma_bf16(tmem + 128 * i, sdesc_sw128(qb + o, 16, 1024), sdesc_sw128(kb + o, 16, 1024), idS, k > 0);
+          const uint64_t o = (uint64_t)(((k >> 2) * Cfg::CHUNK + (k & 3) * 32) >> 4);
+          umma_bf16(tmem + 128 * i, a + o, b + o, idS, k > 0);
         }
         umma_commit(&s_full[i]);
       };
       auto issue_pv = [&](int i, int j) {
-        const uint32_t vb = smem_u32(sV + (j % ST) * Cfg::TILE);
+        const uint64_t b = dv[j % ST];
         const uint32_t tP = tmem + 128 * i + 64, tO = tmem + 256 + D * i;
 #pragma unroll
         for (int k = 0; k < 128 / 16; ++k)
-          umma_bf16_ts(tO, tP + k * 8, sdesc_sw128(vb + k * 2048, Cfg::CHUNK, 1024), idO, (j | k) != 0);
+          umma_bf16_ts(tO, tP + k * 8, b + (uint64_t)(k * (2048 >> 4)), idO, (j | k) != 0);
         umma_commit(&pv_done[i]);
       };
       bool ok = mbar_wait(q_full, 0, p.err, kErrWaitFull) && mbar_wait(&k_full[0], 0, p.err, kErrWaitFull);
