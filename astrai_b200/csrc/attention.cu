@@ -534,26 +534,43 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
       constexpr uint32_t idGR = idesc_bf16(128, 128, 0, 1);  // dV, dK    : P^T/dS^T K-major, dO/Q MN-major
       constexpr uint32_t idDQ = idesc_bf16(128, 64, 1, 1);   // dQ^T      : K^T MN-major, dS^T MN-major
       bool ok = mbar_wait(kv_full, 0, p.err, kErrWaitFull);
-      const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV);
+      // Descriptors are built once; a K step only advances the start-address field (16-byte units,
+      // no carry: shared addresses stay below 2^18 bytes). The 128x64x16 MMAs of this kernel last
+      // ~32 tensor-core cycles each and the issuing warp shares its SM sub-partition with a softmax
+      // and a dQ warp, so building two descriptors per MMA left the tensor core waiting on issue.
+      const uint64_t dK_k = sdesc_sw128(smem_u32(sK), 16, 1024);         // K as A, K-major
+      const uint64_t dV_k = sdesc_sw128(smem_u32(sV), 16, 1024);         // V as A, K-major
+      const uint64_t dK_mn = sdesc_sw128(smem_u32(sK), FA_TILE, 1024);   // K^T as A, MN-major
+      const uint64_t dP = sdesc_sw128(smem_u32(sP), 16, 1024);           // P^T as A
+      const uint64_t dS_k = sdesc_sw128(smem_u32(sdS), 16, 1024);        // dS^T as A
+      const uint64_t dS_mn = sdesc_sw128(smem_u32(sdS), 2 * FA_TILE, 1024);  // dS^T as B, MN-major
+      uint64_t dQ_k[FB_QD], dO_k[FB_QD], dQ_mn[FB_QD], dO_mn[FB_QD];
+#pragma unroll
+      for (int i = 0; i < FB_QD; ++i) {
+        const uint32_t qb = smem_u32(sQ + i * 2 * FB_QT), ob = smem_u32(sdO + i * 2 * FB_QT);
+        dQ_k[i] = sdesc_sw128(qb, 16, 1024);
+        dO_k[i] = sdesc_sw128(ob, 16, 1024);
+        dQ_mn[i] = sdesc_sw128(qb, FB_QT, 1024);
+        dO_mn[i] = sdesc_sw128(ob, FB_QT, 1024);
+      }
+      // slot-indexed descriptors by selects, so the arrays stay in registers
+      auto pick = [](const uint64_t (&a)[FB_QD], int i) { return i == 0 ? a[0] : (i == 1 ? a[1] : a[2]); };
+      static_assert(FB_QD == 3, "pick() covers three slots");
       auto issue_grads = [&](int it) -> bool {
         // dV += P^T dO ; dK += dS^T Q   (M = keys, N = d, K = 64 queries)
         const int slot = it & 1, qs = it % FB_QD;
-        const uint32_t q_base = smem_u32(sQ + qs * 2 * FB_QT), do_base = smem_u32(sdO + qs * 2 * FB_QT);
-        const uint32_t p_base = smem_u32(sP), ds_base = smem_u32(sdS);
+        const uint64_t bo = pick(dO_mn, qs), bq = pick(dQ_mn, qs);
 #pragma unroll
         for (int k = 0; k < FB_BM / 16; ++k) {
-          umma_bf16(tdV, sdesc_sw128(p_base + k * 32, 16, 1024), sdesc_sw128(do_base + k * 2048, FB_QT, 1024), idGR,
-                    (it | k) != 0);
-          umma_bf16(tdK, sdesc_sw128(ds_base + k * 32, 16, 1024), sdesc_sw128(q_base + k * 2048, FB_QT, 1024), idGR,
-                    (it | k) != 0);
+          umma_bf16(tdV, dP + (uint64_t)(k * 2), bo + (uint64_t)(k * 128), idGR, (it | k) != 0);
+          umma_bf16(tdK, dS_k + (uint64_t)(k * 2), bq + (uint64_t)(k * 128), idGR, (it | k) != 0);
         }
         umma_commit(&qd_empty[qs]);
         // dQ^T = K^T dS^T  (M = d, N = 64 queries, K = 128 keys) over this iteration's S^T,
         // which the softmax has read (ps_ready waited by the caller)
 #pragma unroll
         for (int k = 0; k < FA_BN / 16; ++k)
-          umma_bf16(tmem + slot * 128, sdesc_sw128(k_base + k * 2048, FA_TILE, 1024),
-                    sdesc_sw128(ds_base + k * 2048, 2 * FA_TILE, 1024), idDQ, k > 0);
+          umma_bf16(tmem + slot * 128, dK_mn + (uint64_t)(k * 128), dS_mn + (uint64_t)(k * 128), idDQ, k > 0);
         umma_commit(&dq_full[slot]);
         return true;
       };
@@ -564,15 +581,15 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
         if (ok && it >= 2) ok = mbar_wait(&dq_free[slot], ((it - 2) >> 1) & 1, p.err, kErrWaitAccEmpty);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t q_base = smem_u32(sQ + qs * 2 * FB_QT), do_base = smem_u32(sdO + qs * 2 * FB_QT);
+        const uint64_t bq = pick(dQ_k, qs), bo = pick(dO_k, qs);
         const uint32_t tS = tmem + slot * 128, tdP = tS + 64;
         // S^T = K Q^T ; dP^T = V dO^T   (M = 128 keys, N = 64 queries, K = d)
 #pragma unroll
         for (int k = 0; k < FA_D / 16; ++k) {
-          const uint32_t o = (k >> 2) * FA_TILE + (k & 3) * 32;
-          const uint32_t oq = (k >> 2) * FB_QT + (k & 3) * 32;
-          umma_bf16(tS, sdesc_sw128(k_base + o, 16, 1024), sdesc_sw128(q_base + oq, 16, 1024), idSP, k > 0);
-          umma_bf16(tdP, sdesc_sw128(v_base + o, 16, 1024), sdesc_sw128(do_base + oq, 16, 1024), idSP, k > 0);
+          const uint64_t o = (uint64_t)(((k >> 2) * FA_TILE + (k & 3) * 32) >> 4);
+          const uint64_t oq = (uint64_t)(((k >> 2) * FB_QT + (k & 3) * 32) >> 4);
+          umma_bf16(tS, dK_k + o, bq + oq, idSP, k > 0);
+          umma_bf16(tdP, dV_k + o, bo + oq, idSP, k > 0);
         }
         umma_commit(&sd_full[slot]);
         // gradients of it-1 once its softmax is done; they overlap the softmax of it

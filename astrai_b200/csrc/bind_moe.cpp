@@ -13,21 +13,22 @@ int num_sms(int device);
 void moe_router(const void* logits, int f32, long long ld, int T, int E, int k, float* probs, int* idx, float* w,
                 int* counts, int* pos, cudaStream_t s);
 astrai::EPArena make_arena(const long long* peer_base, int rank, int world, const long long* offs, long long rows_cap,
-                           long long slots_cap, int d, unsigned* done, int* err, unsigned long long wait_ns);
+                           long long slots_cap, int d, unsigned* done, unsigned* expect, int* err,
+                           unsigned long long wait_ns);
 void ep_dispatch(const astrai::EPArena& a, const void* x, long long ldx, const int* idx, const int* pos,
-                 const int* base_row, int n_slots, int k, int e_local, int* slot_row, unsigned epoch, int ctas,
-                 cudaStream_t s);
-void ep_wait(const astrai::EPArena& a, int phase, unsigned epoch, cudaStream_t s);
+                 const int* base_row, int n_slots, int k, int e_local, int* slot_row, int ctas, cudaStream_t s);
+void ep_wait(const astrai::EPArena& a, int phase, cudaStream_t s);
+void ep_layout(const astrai::EPArena& a, const int* counts, int E, int e_local, int* base_row, int* n_rows, int* starts,
+               int* k_count, int* group_tile, int max_tiles, int* total, cudaStream_t s);
 void ep_dispatch_fp8(const astrai::EPArena& a, const void* x, long long ldx, const int* idx, const int* pos,
-                     const int* base_row, int n_slots, int k, int e_local, int* slot_row, unsigned epoch, int ctas,
+                     const int* base_row, int n_slots, int k, int e_local, int* slot_row, int ctas,
                      cudaStream_t s);
 void ep_dequant(const astrai::EPArena& a, long long rows, int ctas, cudaStream_t s);
 void ep_return(const astrai::EPArena& a, const void* rows, long long total_rows, const int* group_tile,
-               const int* starts, const int* n_rows, int to_ret2, unsigned epoch, int ctas, cudaStream_t s);
+               const int* starts, const int* n_rows, int to_ret2, int ctas, cudaStream_t s);
 void ep_combine(const void* slots, const float* w, const void* add, void* out, int T, int k, int d, cudaStream_t s);
 void ep_combine_bwd(const astrai::EPArena& a, const void* dout, const void* slots, const float* w, const int* idx,
-                    const int* slot_row, int n_slots, int k, int e_local, float* dw, unsigned epoch, int ctas,
-                    cudaStream_t s);
+                    const int* slot_row, int n_slots, int k, int e_local, float* dw, int ctas, cudaStream_t s);
 void ep_zero_pad(const astrai::EPArena& a, int which_dyin, long long total_rows, const int* group_tile,
                  const int* starts, const int* n_rows, cudaStream_t s);
 void gemm_grouped_bf16(int mode, const void* A, const void* B, void* D, const void* C, int M, int N, int K,
@@ -44,18 +45,23 @@ void chk(const at::Tensor& t, at::ScalarType st, const char* n) {
   TORCH_CHECK(t.is_cuda() && t.scalar_type() == st && t.is_contiguous(), n, ": wrong dtype / device / layout");
 }
 
-// Arena description passed from Python: peer_base int64 [W], offs [8] (flags, srcmap, xin, dyin, ret, ret2,
-// xin8, xsc; the last two 0 without fp8 dispatch).
+// Arena description passed from Python: peer_base int64 [W], offs [9] (flags, srcmap, xin, dyin, ret, ret2,
+// xin8, xsc, counts; xin8 / xsc are 0 without fp8 dispatch), the local grid-completion counter and the
+// local per-phase round counters (int32 [5]).
 astrai::EPArena arena_of(const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done,
-                         int64_t rank, int64_t world, int64_t rows_cap, int64_t slots_cap, int64_t d, double wait_s) {
+                         const at::Tensor& expect, int64_t rank, int64_t world, int64_t rows_cap, int64_t slots_cap,
+                         int64_t d, double wait_s) {
   chk(peer_base, at::kLong, "peer_base");
   chk(done, at::kInt, "done");
-  TORCH_CHECK(offs.size() == 8 && peer_base.numel() == world && d % 8 == 0, "bad arena description");
-  static thread_local long long o[8];
-  for (int i = 0; i < 8; ++i) o[i] = offs[i];
+  chk(expect, at::kInt, "expect");
+  TORCH_CHECK(offs.size() == 9 && peer_base.numel() == world && d % 8 == 0 && expect.numel() == astrai::kEPPhases,
+              "bad arena description");
+  static thread_local long long o[9];
+  for (int i = 0; i < 9; ++i) o[i] = offs[i];
   return astrai_host::make_arena(reinterpret_cast<const long long*>(peer_base.data_ptr<int64_t>()),
                                  static_cast<int>(rank), static_cast<int>(world), o, rows_cap, slots_cap,
                                  static_cast<int>(d), reinterpret_cast<unsigned*>(done.data_ptr<int>()),
+                                 reinterpret_cast<unsigned*>(expect.data_ptr<int>()),
                                  astrai_host::error_word(peer_base.device().index()),
                                  static_cast<unsigned long long>(wait_s * 1e9));
 }
@@ -83,10 +89,10 @@ void moe_router(const at::Tensor& logits, int64_t k, at::Tensor& probs, at::Tens
 int ctas_for(const at::Tensor& t) { return astrai_host::num_sms(t.device().index()); }
 
 void ep_dispatch_any(bool fp8, const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done,
-                     int64_t rank, int64_t world, int64_t rows_cap, int64_t slots_cap, int64_t d, double wait_s,
+                     const at::Tensor& expect, int64_t rank, int64_t world, int64_t rows_cap, int64_t slots_cap, int64_t d, double wait_s,
                      const at::Tensor& x, const at::Tensor& idx, const at::Tensor& pos, const at::Tensor& base_row,
-                     int64_t e_local, at::Tensor& slot_row, int64_t epoch) {
-  auto a = arena_of(peer_base, offs, done, rank, world, rows_cap, slots_cap, d, wait_s);
+                     int64_t e_local, at::Tensor& slot_row) {
+  auto a = arena_of(peer_base, offs, done, expect, rank, world, rows_cap, slots_cap, d, wait_s);
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1 && x.size(1) == d &&
                   (x.stride(0) * 2) % 16 == 0,
               "x must be bf16 [T, d] rows");
@@ -100,47 +106,70 @@ void ep_dispatch_any(bool fp8, const at::Tensor& peer_base, const std::vector<in
   const c10::cuda::CUDAGuard g(x.device());
   (fp8 ? astrai_host::ep_dispatch_fp8 : astrai_host::ep_dispatch)(a, x.data_ptr(), x.stride(0), idx.data_ptr<int>(), pos.data_ptr<int>(),
                            base_row.data_ptr<int>(), static_cast<int>(n_slots), k, static_cast<int>(e_local),
-                           slot_row.data_ptr<int>(), static_cast<unsigned>(epoch), ctas_for(x), cur());
+                           slot_row.data_ptr<int>(), ctas_for(x), cur());
 }
 
-void ep_dispatch(const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done, int64_t rank,
+void ep_dispatch(const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done,
+                 const at::Tensor& expect, int64_t rank,
                  int64_t world, int64_t rows_cap, int64_t slots_cap, int64_t d, double wait_s, const at::Tensor& x,
                  const at::Tensor& idx, const at::Tensor& pos, const at::Tensor& base_row, int64_t e_local,
-                 at::Tensor& slot_row, int64_t epoch) {
-  ep_dispatch_any(false, peer_base, offs, done, rank, world, rows_cap, slots_cap, d, wait_s, x, idx, pos, base_row,
-                  e_local, slot_row, epoch);
+                 at::Tensor& slot_row) {
+  ep_dispatch_any(false, peer_base, offs, done, expect, rank, world, rows_cap, slots_cap, d, wait_s, x, idx, pos, base_row,
+                  e_local, slot_row);
 }
 
 // Token rows as fp8 e4m3 with one fp32 scale per 128 columns (the arena's fp8 block).
 void ep_dispatch_fp8(const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done,
-                     int64_t rank, int64_t world, int64_t rows_cap, int64_t slots_cap, int64_t d, double wait_s,
+                     const at::Tensor& expect, int64_t rank, int64_t world, int64_t rows_cap, int64_t slots_cap, int64_t d, double wait_s,
                      const at::Tensor& x, const at::Tensor& idx, const at::Tensor& pos, const at::Tensor& base_row,
-                     int64_t e_local, at::Tensor& slot_row, int64_t epoch) {
-  ep_dispatch_any(true, peer_base, offs, done, rank, world, rows_cap, slots_cap, d, wait_s, x, idx, pos, base_row,
-                  e_local, slot_row, epoch);
+                     int64_t e_local, at::Tensor& slot_row) {
+  ep_dispatch_any(true, peer_base, offs, done, expect, rank, world, rows_cap, slots_cap, d, wait_s, x, idx, pos, base_row,
+                  e_local, slot_row);
 }
 
 // bf16 expert-input rows [0, rows) of this rank's arena from its fp8 block.
-void ep_dequant(const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done, int64_t rank,
+void ep_dequant(const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done,
+                 const at::Tensor& expect, int64_t rank,
                 int64_t world, int64_t rows_cap, int64_t slots_cap, int64_t d, double wait_s, int64_t rows) {
-  auto a = arena_of(peer_base, offs, done, rank, world, rows_cap, slots_cap, d, wait_s);
+  auto a = arena_of(peer_base, offs, done, expect, rank, world, rows_cap, slots_cap, d, wait_s);
   const c10::cuda::CUDAGuard g(peer_base.device());
   astrai_host::ep_dequant(a, rows, ctas_for(peer_base), cur());
 }
 
-void ep_wait(const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done, int64_t rank,
-             int64_t world, int64_t rows_cap, int64_t slots_cap, int64_t d, double wait_s, int64_t phase,
-             int64_t epoch) {
-  auto a = arena_of(peer_base, offs, done, rank, world, rows_cap, slots_cap, d, wait_s);
+void ep_wait(const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done,
+                 const at::Tensor& expect, int64_t rank,
+             int64_t world, int64_t rows_cap, int64_t slots_cap, int64_t d, double wait_s, int64_t phase) {
+  auto a = arena_of(peer_base, offs, done, expect, rank, world, rows_cap, slots_cap, d, wait_s);
   const c10::cuda::CUDAGuard g(peer_base.device());
-  astrai_host::ep_wait(a, static_cast<int>(phase), static_cast<unsigned>(epoch), cur());
+  astrai_host::ep_wait(a, static_cast<int>(phase), cur());
 }
 
-void ep_return(const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done, int64_t rank,
+// Counts exchange + dispatch layout on the device; outputs int32: base_row [E], n_rows / starts / k_count
+// [e_local], group_tile [max_tiles], total [1].
+void ep_layout(const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done,
+               const at::Tensor& expect, int64_t rank, int64_t world, int64_t rows_cap, int64_t slots_cap, int64_t d,
+               double wait_s, const at::Tensor& counts, int64_t e_local, at::Tensor& base_row, at::Tensor& n_rows,
+               at::Tensor& starts, at::Tensor& k_count, at::Tensor& group_tile, at::Tensor& total) {
+  auto a = arena_of(peer_base, offs, done, expect, rank, world, rows_cap, slots_cap, d, wait_s);
+  for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&counts, &base_row, &n_rows, &starts, &k_count,
+                                                                      &group_tile, &total})
+    chk(*t, at::kInt, "ep_layout tables");
+  const int64_t E = counts.numel();
+  TORCH_CHECK(base_row.numel() == E && n_rows.numel() == e_local && starts.numel() == e_local &&
+                  k_count.numel() == e_local && total.numel() == 1 && group_tile.numel() * 128 <= rows_cap,
+              "ep_layout: table sizes");
+  const c10::cuda::CUDAGuard g(counts.device());
+  astrai_host::ep_layout(a, counts.data_ptr<int>(), static_cast<int>(E), static_cast<int>(e_local),
+                         base_row.data_ptr<int>(), n_rows.data_ptr<int>(), starts.data_ptr<int>(),
+                         k_count.data_ptr<int>(), group_tile.data_ptr<int>(), static_cast<int>(group_tile.numel()),
+                         total.data_ptr<int>(), cur());
+}
+
+void ep_return(const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done,
+                 const at::Tensor& expect, int64_t rank,
                int64_t world, int64_t rows_cap, int64_t slots_cap, int64_t d, double wait_s, const at::Tensor& rows,
-               const at::Tensor& group_tile, const at::Tensor& starts, const at::Tensor& n_rows, int64_t to_ret2,
-               int64_t epoch) {
-  auto a = arena_of(peer_base, offs, done, rank, world, rows_cap, slots_cap, d, wait_s);
+               const at::Tensor& group_tile, const at::Tensor& starts, const at::Tensor& n_rows, int64_t to_ret2) {
+  auto a = arena_of(peer_base, offs, done, expect, rank, world, rows_cap, slots_cap, d, wait_s);
   chk(rows, at::kBFloat16, "rows");
   chk(group_tile, at::kInt, "group_tile");
   chk(starts, at::kInt, "starts");
@@ -149,8 +178,7 @@ void ep_return(const at::Tensor& peer_base, const std::vector<int64_t>& offs, co
   TORCH_CHECK(total % 128 == 0 && group_tile.numel() == total / 128 && total <= rows_cap, "rows must be [M_total, d]");
   const c10::cuda::CUDAGuard g(rows.device());
   astrai_host::ep_return(a, rows.data_ptr(), total, group_tile.data_ptr<int>(), starts.data_ptr<int>(),
-                         n_rows.data_ptr<int>(), static_cast<int>(to_ret2), static_cast<unsigned>(epoch),
-                         ctas_for(rows), cur());
+                         n_rows.data_ptr<int>(), static_cast<int>(to_ret2), ctas_for(rows), cur());
 }
 
 void ep_combine(const at::Tensor& slots, const c10::optional<at::Tensor>& w, const c10::optional<at::Tensor>& add,
@@ -178,10 +206,10 @@ void ep_combine(const at::Tensor& slots, const c10::optional<at::Tensor>& w, con
 }
 
 void ep_combine_bwd(const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done,
-                    int64_t rank, int64_t world, int64_t rows_cap, int64_t slots_cap, int64_t d, double wait_s,
+                    const at::Tensor& expect, int64_t rank, int64_t world, int64_t rows_cap, int64_t slots_cap, int64_t d, double wait_s,
                     const at::Tensor& dout, const at::Tensor& slots, const at::Tensor& w, const at::Tensor& idx,
-                    const at::Tensor& slot_row, int64_t e_local, at::Tensor& dw, int64_t epoch) {
-  auto a = arena_of(peer_base, offs, done, rank, world, rows_cap, slots_cap, d, wait_s);
+                    const at::Tensor& slot_row, int64_t e_local, at::Tensor& dw) {
+  auto a = arena_of(peer_base, offs, done, expect, rank, world, rows_cap, slots_cap, d, wait_s);
   chk(dout, at::kBFloat16, "dout");
   chk(slots, at::kBFloat16, "slots");
   chk(w, at::kFloat, "w");
@@ -195,14 +223,15 @@ void ep_combine_bwd(const at::Tensor& peer_base, const std::vector<int64_t>& off
   const c10::cuda::CUDAGuard g(dout.device());
   astrai_host::ep_combine_bwd(a, dout.data_ptr(), slots.data_ptr(), w.data_ptr<float>(), idx.data_ptr<int>(),
                               slot_row.data_ptr<int>(), static_cast<int>(n_slots), k, static_cast<int>(e_local),
-                              dw.data_ptr<float>(), static_cast<unsigned>(epoch), ctas_for(dout), cur());
+                              dw.data_ptr<float>(), ctas_for(dout), cur());
 }
 
-void ep_zero_pad(const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done, int64_t rank,
+void ep_zero_pad(const at::Tensor& peer_base, const std::vector<int64_t>& offs, const at::Tensor& done,
+                 const at::Tensor& expect, int64_t rank,
                  int64_t world, int64_t rows_cap, int64_t slots_cap, int64_t d, double wait_s, int64_t which_dyin,
                  int64_t total_rows, const at::Tensor& group_tile, const at::Tensor& starts,
                  const at::Tensor& n_rows) {
-  auto a = arena_of(peer_base, offs, done, rank, world, rows_cap, slots_cap, d, wait_s);
+  auto a = arena_of(peer_base, offs, done, expect, rank, world, rows_cap, slots_cap, d, wait_s);
   chk(group_tile, at::kInt, "group_tile");
   chk(starts, at::kInt, "starts");
   chk(n_rows, at::kInt, "n_rows");
@@ -282,6 +311,7 @@ void register_moe(pybind11::module& m) {
   m.def("ep_dispatch", &ep_dispatch);
   m.def("ep_dispatch_fp8", &ep_dispatch_fp8);
   m.def("ep_dequant", &ep_dequant);
+  m.def("ep_layout", &ep_layout);
   m.def("ep_wait", &ep_wait);
   m.def("ep_return", &ep_return);
   m.def("ep_combine", &ep_combine, pybind11::arg("slots"), pybind11::arg("w"), pybind11::arg("add"),

@@ -47,9 +47,10 @@ void rmsnorm_bwd(const void* dy, long long lddy, const void* x, long long ldx, c
                  cudaStream_t s, const void* dres = nullptr, long long ldres = 0);
 void rope_apply(void* x, long long ld, int rows, int col0, int n_heads, int head_dim, const int* pos, int seq_len,
                 const void* cs, int inverse, int rot_dim, int rot_off, int max_pos, cudaStream_t s);
-void swiglu_fwd(const void* h, long long ldh, void* out, long long ldo, int rows, int F, cudaStream_t s);
-void swiglu_bwd(const void* dy, long long lddy, const void* h, long long ldh, void* dh, long long lddh, int rows, int F,
+void swiglu_fwd(const void* h, long long ldh, void* out, long long ldo, int rows, int F, const int* live_rows,
                 cudaStream_t s);
+void swiglu_bwd(const void* dy, long long lddy, const void* h, long long ldh, void* dh, long long lddh, int rows, int F,
+                const int* live_rows, cudaStream_t s);
 void embedding_fwd(const long long* ids, const void* w, void* out, int n_tok, int d, int vocab, cudaStream_t s);
 void embedding_bwd(const long long* ids, const void* g, float* gw, int n_tok, int d, int vocab, cudaStream_t s);
 void f32_to_bf16(const float* in, void* out, long long n, int accumulate, cudaStream_t s);
@@ -332,7 +333,14 @@ void rope_(at::Tensor& x, int64_t col0, int64_t n_heads, int64_t head_dim, const
                           stream());
 }
 
-void swiglu_fwd(const at::Tensor& h, at::Tensor& out) {
+const int* live_ptr(const c10::optional<at::Tensor>& live) {
+  if (!live.has_value()) return nullptr;
+  TORCH_CHECK(live->is_cuda() && live->scalar_type() == at::kInt && live->numel() == 1, "live_rows: CUDA int32 [1]");
+  return live->data_ptr<int>();
+}
+
+// live_rows (optional CUDA int32 [1]): only that many leading rows are processed
+void swiglu_fwd(const at::Tensor& h, at::Tensor& out, const c10::optional<at::Tensor>& live_rows) {
   check_bf16(h, "h");
   check_bf16(out, "out");
   check_rows(h, "h");
@@ -340,10 +348,12 @@ void swiglu_fwd(const at::Tensor& h, at::Tensor& out) {
   const int F = (int)out.size(1);
   TORCH_CHECK(h.size(1) == 2 * F && F % 8 == 0, "swiglu: h must be [rows, 2F] with F % 8 == 0");
   c10::cuda::CUDAGuard g(h.device());
-  astrai_host::swiglu_fwd(h.data_ptr(), h.stride(0), out.data_ptr(), out.stride(0), (int)h.size(0), F, stream());
+  astrai_host::swiglu_fwd(h.data_ptr(), h.stride(0), out.data_ptr(), out.stride(0), (int)h.size(0), F,
+                          live_ptr(live_rows), stream());
 }
 
-void swiglu_bwd(const at::Tensor& dy, const at::Tensor& h, at::Tensor& dh) {
+void swiglu_bwd(const at::Tensor& dy, const at::Tensor& h, at::Tensor& dh,
+                const c10::optional<at::Tensor>& live_rows) {
   check_bf16(dy, "dy");
   check_bf16(h, "h");
   check_bf16(dh, "dh");
@@ -353,7 +363,7 @@ void swiglu_bwd(const at::Tensor& dy, const at::Tensor& h, at::Tensor& dh) {
   const int F = (int)dy.size(1);
   c10::cuda::CUDAGuard g(h.device());
   astrai_host::swiglu_bwd(dy.data_ptr(), dy.stride(0), h.data_ptr(), h.stride(0), dh.data_ptr(), dh.stride(0),
-                          (int)h.size(0), F, stream());
+                          (int)h.size(0), F, live_ptr(live_rows), stream());
 }
 
 void embedding_fwd(const at::Tensor& ids, const at::Tensor& w, at::Tensor& out) {
@@ -522,8 +532,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_bwd", &rmsnorm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"), py::arg("dx"),
         py::arg("dw"), py::arg("scratch"), py::arg("dres") = py::none());
   m.def("rope_", &rope_);
-  m.def("swiglu_fwd", &swiglu_fwd);
-  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("swiglu_fwd", &swiglu_fwd, pybind11::arg("h"), pybind11::arg("out"), pybind11::arg("live_rows") = pybind11::none());
+  m.def("swiglu_bwd", &swiglu_bwd, pybind11::arg("dy"), pybind11::arg("h"), pybind11::arg("dh"),
+        pybind11::arg("live_rows") = pybind11::none());
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);
   m.def("f32_to_bf16", &f32_to_bf16);

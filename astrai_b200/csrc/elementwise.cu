@@ -50,10 +50,12 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ x, long long ld, int row
 __device__ __forceinline__ float silu_f(float g) { return g / (1.f + __expf(-g)); }
 
 // h: [rows, ldh] with up = h[:, 0:F], gate = h[:, F:2F];  out: [rows, ldo]
+// live_rows (optional device count): only the first *live_rows of the `rows` rows hold data (an expert
+// block sized for its capacity); the rest are left untouched.
 __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ h, long long ldh, __nv_bfloat16* __restrict__ out,
-                                  long long ldo, int rows, int F) {
+                                  long long ldo, int rows, int F, const int* __restrict__ live_rows) {
   const int per_row = F / 8;
-  const long long total = (long long)rows * per_row;
+  const long long total = (long long)(live_rows ? min(rows, max(0, *live_rows)) : rows) * per_row;
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
        idx += (long long)gridDim.x * blockDim.x) {
     const int row = idx / per_row;
@@ -73,9 +75,9 @@ __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ h, long long
 // dh[:, :F] = dy * silu(g);  dh[:, F:] = dy * up * silu'(g)
 __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dy, long long lddy,
                                   const __nv_bfloat16* __restrict__ h, long long ldh, __nv_bfloat16* __restrict__ dh,
-                                  long long lddh, int rows, int F) {
+                                  long long lddh, int rows, int F, const int* __restrict__ live_rows) {
   const int per_row = F / 8;
-  const long long total = (long long)rows * per_row;
+  const long long total = (long long)(live_rows ? min(rows, max(0, *live_rows)) : rows) * per_row;
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
        idx += (long long)gridDim.x * blockDim.x) {
     const int row = idx / per_row;
@@ -186,16 +188,18 @@ void rope_apply(void* x, long long ld, int rows, int col0, int n_heads, int head
                                             rot_off, max_pos, error_word(dev)));
 }
 
-void swiglu_fwd(const void* h, long long ldh, void* out, long long ldo, int rows, int F, cudaStream_t s) {
+void swiglu_fwd(const void* h, long long ldh, void* out, long long ldo, int rows, int F, const int* live_rows,
+                cudaStream_t s) {
   (astrai::note_launch(), swiglu_fwd_kernel<<<ew_grid((long long)rows * F / 8), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(h), ldh,
-                                                                      static_cast<__nv_bfloat16*>(out), ldo, rows, F));
+                                                                      static_cast<__nv_bfloat16*>(out), ldo, rows, F,
+                                                                      live_rows));
 }
 
 void swiglu_bwd(const void* dy, long long lddy, const void* h, long long ldh, void* dh, long long lddh, int rows, int F,
-                cudaStream_t s) {
+                const int* live_rows, cudaStream_t s) {
   (astrai::note_launch(), swiglu_bwd_kernel<<<ew_grid((long long)rows * F / 8), 256, 0, s>>>(
       static_cast<const __nv_bfloat16*>(dy), lddy, static_cast<const __nv_bfloat16*>(h), ldh,
-      static_cast<__nv_bfloat16*>(dh), lddh, rows, F));
+      static_cast<__nv_bfloat16*>(dh), lddh, rows, F, live_rows));
 }
 
 void embedding_fwd(const long long* ids, const void* w, void* out, int n_tok, int d, int vocab, cudaStream_t s) {

@@ -4,10 +4,15 @@
 
 namespace astrai {
 
+// Exchange phases; each has a row of arrival counters in every rank's flag block.
+enum EPPhase : int { kPhDispatch = 0, kPhReturn = 1, kPhScatterBwd = 2, kPhReturnBwd = 3, kPhCounts = 4 };
+constexpr int kEPPhases = 5;
+
 struct EPArena {
   const long long* peer_base;  // [W] arena bases (this process's mappings)
   int rank, world;
-  long long off_flags;   // [4][W] u32 epochs, one row per phase
+  long long off_flags;   // [kEPPhases][W] u32 arrival counters, one row per phase, one column per source rank
+  long long off_counts;  // [W][E] int32 routed-slot counts per expert, one row per source rank
   long long off_srcmap;  // [rows_cap] int64 (src_rank << 32 | slot)
   long long off_xin;     // [rows_cap, d] expert input block
   long long off_dyin;    // [rows_cap, d] expert output-gradient block
@@ -18,6 +23,7 @@ struct EPArena {
   long long rows_cap, slots_cap;
   int d;
   unsigned* done;        // local grid-completion counter
+  unsigned* expect;      // local [kEPPhases] rounds of each phase this rank has waited for
   int* err;
   unsigned long long wait_ns;
 };

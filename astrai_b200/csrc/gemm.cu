@@ -169,6 +169,10 @@ struct WorkItem {
   bool partial; // the tile is split over several CTAs
 };
 
+// Grouped-M tiles whose group is negative are unused (an expert block sized for its capacity, of which
+// only a device-side count of tiles is live): every role of the kernel skips them through WorkIter.
+__device__ __forceinline__ bool tile_skipped(const GemmParams& p, int tile);
+
 // Work walk of one worker (a CTA, or a CTA pair in gemm_pair_kernel): `idx` of `cnt` workers.
 struct WorkIter {
   int t, idx, cnt;
@@ -191,6 +195,8 @@ struct WorkIter {
   }
   __device__ __forceinline__ bool next(const GemmParams& p, int num_tiles, int kblk_full, WorkItem& w) {
     const int limit = p.sk_units > 0 ? p.dp_tiles : num_tiles;
+    if (p.group_tile)
+      while (t < limit && tile_skipped(p, t)) t += cnt;
     if (t < limit) {
       w = {t, 0, kblk_full, -1, 0, true, false};
       t += cnt;
@@ -301,6 +307,12 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
   const int r = t - group * span;
   mb = first + r % gsize;
   nb = r / gsize;
+}
+
+__device__ __forceinline__ bool tile_skipped(const GemmParams& p, int tile) {
+  int b, mb, nb;
+  tile_coords(tile, p.tiles_m, p.tiles_n, b, mb, nb);
+  return p.group_tile[mb] < 0;
 }
 
 template <int BM, int BN, int A_MN, int B_MN, int OUT_F32>

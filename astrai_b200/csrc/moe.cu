@@ -21,11 +21,16 @@
 //   combine_bwd dw[t, j] = <dout[t], slot[t, j]>, and w[t, j] * dout[t] ->
 //              the expert input-gradient block on the owning rank (P2P);
 //   zero_pad   clears the padding rows of an expert block.
+//   layout     counts exchange + the dispatch layout, computed on the device
+//              (no host round trip, so a MoE step can be captured in a CUDA graph).
 // A scatter kernel ends with a grid-completion count; the last CTA fences
-// system-wide and raises this rank's flag (an epoch) on every rank. The
-// consumer runs ep_wait (bounded by wait_ns; kErrWaitPeer on expiry) before
-// the kernels that read the block. Row indices are bounds-checked against the
-// arena capacity (kErrBadArg, row skipped) so a bad layout cannot fault.
+// system-wide and adds 1 to its column of the phase's arrival counters on every
+// rank. The consumer's ep_wait (bounded by wait_ns; kErrWaitPeer on expiry)
+// waits until every column reached the number of rounds this rank has consumed
+// plus one, a count kept in device memory; no host-side epoch is involved, so
+// replaying a captured graph continues the sequence. Row indices are
+// bounds-checked against the arena capacity (kErrBadArg, row skipped) so a bad
+// layout cannot fault.
 #include <stdexcept>
 #include <string>
 
@@ -140,21 +145,43 @@ __device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned* p) {
   return v;
 }
 
-// Last CTA to finish raises flag [phase][rank] = epoch on every rank (itself included).
-__device__ void grid_done_signal(const EPArena& a, int phase, unsigned epoch) {
+__device__ __forceinline__ void red_release_sys_add_u32(unsigned* p, unsigned v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// This rank's arrival at `phase` on every rank (itself included): counter [phase][rank] += 1.
+__device__ __forceinline__ void arrive_all(const EPArena& a, int phase) {
+  __threadfence_system();
+  for (int q = 0; q < a.world; ++q)
+    red_release_sys_add_u32(reinterpret_cast<unsigned*>(arena(a, q, a.off_flags)) + phase * a.world + a.rank, 1u);
+}
+
+// Last CTA to finish announces this rank's arrival at `phase`.
+__device__ void grid_done_signal(const EPArena& a, int phase) {
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence_system();
     const unsigned prev = atomicAdd(a.done, 1u);
     if (prev == gridDim.x - 1) {
-      __threadfence_system();
-      for (int q = 0; q < a.world; ++q) {
-        unsigned* f = reinterpret_cast<unsigned*>(arena(a, q, a.off_flags)) + phase * a.world + a.rank;
-        st_release_sys_u32(f, epoch);
-      }
+      arrive_all(a, phase);
       *a.done = 0u;
     }
   }
+}
+
+// Bounded wait of one thread until counter [phase][q] of this rank's block reaches `want`
+// (wrap-around safe); false after flagging kErrWaitPeer.
+__device__ bool wait_arrival(const EPArena& a, int phase, int q, unsigned want) {
+  const unsigned* f = reinterpret_cast<const unsigned*>(arena(a, a.rank, a.off_flags)) + phase * a.world + q;
+  const uint64_t t0 = globaltimer();
+  while (static_cast<int>(ld_acquire_sys_u32(f) - want) < 0) {
+    if (globaltimer() - t0 > a.wait_ns) {
+      set_error(a.err, kErrWaitPeer);
+      return false;
+    }
+    __nanosleep(128);
+  }
+  return true;
 }
 
 __device__ __forceinline__ void copy_row(char* dst, const char* src, int d, int lane) {
@@ -166,8 +193,7 @@ __device__ __forceinline__ void copy_row(char* dst, const char* src, int d, int 
 __global__ void __launch_bounds__(512) ep_dispatch_kernel(EPArena a, const __nv_bfloat16* __restrict__ x,
                                                           long long ldx, const int* __restrict__ idx,
                                                           const int* __restrict__ pos, const int* __restrict__ base_row,
-                                                          int n_slots, int k, int e_local, int* __restrict__ slot_row,
-                                                          unsigned epoch) {
+                                                          int n_slots, int k, int e_local, int* __restrict__ slot_row) {
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int nw = gridDim.x * (blockDim.x >> 5);
@@ -187,7 +213,7 @@ __global__ void __launch_bounds__(512) ep_dispatch_kernel(EPArena a, const __nv_
     copy_row(arena(a, r, a.off_xin) + row * a.d * 2, reinterpret_cast<const char*>(x + (long long)(s / k) * ldx), a.d,
              lane);
   }
-  grid_done_signal(a, 0, epoch);
+  grid_done_signal(a, kPhDispatch);
 }
 
 // fp8 dispatch (opt-in; the reference only moves bf16): the token row is quantised to e4m3 with one
@@ -199,8 +225,7 @@ __global__ void __launch_bounds__(512) ep_dispatch_fp8_kernel(EPArena a, const _
                                                               long long ldx, const int* __restrict__ idx,
                                                               const int* __restrict__ pos,
                                                               const int* __restrict__ base_row, int n_slots, int k,
-                                                              int e_local, int* __restrict__ slot_row,
-                                                              unsigned epoch) {
+                                                              int e_local, int* __restrict__ slot_row) {
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int nw = gridDim.x * (blockDim.x >> 5);
@@ -257,7 +282,7 @@ __global__ void __launch_bounds__(512) ep_dispatch_fp8_kernel(EPArena a, const _
       }
     }
   }
-  grid_done_signal(a, 0, epoch);
+  grid_done_signal(a, kPhDispatch);
 }
 
 // bf16 expert-input rows [0, rows) <- fp8 rows x their 128-column scales (own arena).
@@ -285,19 +310,15 @@ __global__ void __launch_bounds__(256) ep_dequant_kernel(EPArena a, long long ro
   }
 }
 
-// Bounded wait until flag [phase][q] >= epoch for every rank q.
-__global__ void ep_wait_kernel(EPArena a, int phase, unsigned epoch) {
+// Bounded wait for every rank's next arrival at `phase`; then this rank's round count advances.
+__global__ void ep_wait_kernel(EPArena a, int phase) {
+  __shared__ unsigned want;
+  if (threadIdx.x == 0) want = a.expect[phase] + 1u;
+  __syncthreads();
   const int q = threadIdx.x;
-  if (q >= a.world) return;
-  const unsigned* f = reinterpret_cast<const unsigned*>(arena(a, a.rank, a.off_flags)) + phase * a.world + q;
-  const uint64_t t0 = globaltimer();
-  while (ld_acquire_sys_u32(f) < epoch) {
-    if (globaltimer() - t0 > a.wait_ns) {
-      set_error(a.err, kErrWaitPeer);
-      return;
-    }
-    __nanosleep(128);
-  }
+  if (q < a.world) wait_arrival(a, phase, q, want);
+  __syncthreads();
+  if (threadIdx.x == 0) a.expect[phase] = want;
 }
 
 // Valid rows of the local expert blocks -> the slot block of their source rank.
@@ -306,14 +327,14 @@ __global__ void ep_wait_kernel(EPArena a, int phase, unsigned epoch) {
 __global__ void __launch_bounds__(512) ep_return_kernel(EPArena a, const __nv_bfloat16* __restrict__ rows,
                                                         long long total_rows, const int* __restrict__ group_tile,
                                                         const int* __restrict__ starts, const int* __restrict__ n_rows,
-                                                        long long ret_off, int phase, unsigned epoch) {
+                                                        long long ret_off, int phase) {
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int nw = gridDim.x * (blockDim.x >> 5);
   const long long* srcmap = reinterpret_cast<const long long*>(arena(a, a.rank, a.off_srcmap));
   for (long long row = gw; row < total_rows; row += nw) {
     const int el = group_tile[row >> 7];
-    if (row - starts[el] >= n_rows[el]) continue;
+    if (el < 0 || row - starts[el] >= n_rows[el]) continue;  // unused tile / padding row
     const long long key = srcmap[row];
     const int q = static_cast<int>(key >> 32);
     const long long s = static_cast<long long>(key & 0xFFFFFFFFll);
@@ -323,7 +344,7 @@ __global__ void __launch_bounds__(512) ep_return_kernel(EPArena a, const __nv_bf
     }
     copy_row(arena(a, q, ret_off) + s * a.d * 2, reinterpret_cast<const char*>(rows + row * a.d), a.d, lane);
   }
-  grid_done_signal(a, phase, epoch);
+  grid_done_signal(a, phase);
 }
 
 // out[t] = add[t] + sum_j w[t, j] * slots[t * k + j]   (w == nullptr: weights 1)
@@ -371,7 +392,7 @@ __global__ void __launch_bounds__(512) ep_combine_bwd_kernel(EPArena a, const __
                                                              const __nv_bfloat16* __restrict__ slots,
                                                              const float* __restrict__ w, const int* __restrict__ idx,
                                                              const int* __restrict__ slot_row, int n_slots, int k,
-                                                             int e_local, float* __restrict__ dw, unsigned epoch) {
+                                                             int e_local, float* __restrict__ dw) {
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int nw = gridDim.x * (blockDim.x >> 5);
@@ -401,7 +422,7 @@ __global__ void __launch_bounds__(512) ep_combine_bwd_kernel(EPArena a, const __
     dot = warp_sum(dot);
     if (lane == 0) dw[s] = dot;
   }
-  grid_done_signal(a, 2, epoch);
+  grid_done_signal(a, kPhScatterBwd);
 }
 
 // Zero the padding rows (row - starts[el] >= n_rows[el]) of a block at `off` (own arena).
@@ -413,7 +434,94 @@ __global__ void ep_zero_pad_kernel(EPArena a, long long off, long long total_row
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
     const long long row = i / nv;
     const int el = group_tile[row >> 7];
-    if (row - starts[el] >= n_rows[el]) base[i] = make_uint4(0, 0, 0, 0);
+    if (el >= 0 && row - starts[el] >= n_rows[el]) base[i] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+// Counts exchange and dispatch layout on the device (one CTA). Every rank publishes its routed-slot
+// counts per expert into every rank's counts block and announces it (phase kPhCounts); once all W
+// rows are in, thread 0 derives what the host used to compute after an all-gather:
+//   loads[e]  = sum over source ranks of counts[q][e]   (rows expert e receives)
+//   padded[e] = loads[e] rounded up to 128-row tiles; experts of rank r' back to back from row 0
+//   base_row[e] (this rank's first row in expert e's block on its owner) = start of e on the owner
+//               + rows that lower source ranks send to e
+// and for this rank's own experts the row count, start and padded size of each block, the block's
+// total rows, and group_tile[t] = the expert of 128-row tile t (-1 past the total: the grouped GEMMs
+// and the row kernels skip those tiles). If a rank would need more rows than the arena holds, the
+// kernel flags kErrBadArg and publishes an empty layout (base rows out of range: the dispatch skips
+// every row) instead of writing past the blocks.
+constexpr int kEPMaxExperts = 256;
+__global__ void __launch_bounds__(256) ep_layout_kernel(EPArena a, const int* __restrict__ counts, int E, int e_local,
+                                                       int* __restrict__ base_row, int* __restrict__ n_rows,
+                                                       int* __restrict__ starts, int* __restrict__ k_count,
+                                                       int* __restrict__ group_tile, int max_tiles,
+                                                       int* __restrict__ total_out) {
+  __shared__ int s_load[kEPMaxExperts], s_start[kEPMaxExperts], s_total;
+  __shared__ unsigned want;
+  const int W = a.world;
+  // 1. publish this rank's counts row on every rank, then announce it
+  for (int i = threadIdx.x; i < W * E; i += blockDim.x) {
+    const int q = i / E, e = i % E;
+    reinterpret_cast<int*>(arena(a, q, a.off_counts))[a.rank * E + e] = counts[e];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    arrive_all(a, kPhCounts);
+    want = a.expect[kPhCounts] + 1u;
+  }
+  __syncthreads();
+  // 2. wait for every rank's row (one thread per source rank)
+  if (threadIdx.x < W) wait_arrival(a, kPhCounts, threadIdx.x, want);
+  __syncthreads();
+  // 3. the layout (tiny: E <= 256 experts, W <= 32 ranks)
+  if (threadIdx.x == 0) {
+    a.expect[kPhCounts] = want;
+    const volatile int* c = reinterpret_cast<const volatile int*>(arena(a, a.rank, a.off_counts));
+    bool over = false;
+    int mine = 0;
+    for (int r = 0; r < W; ++r) {
+      int row = 0;
+      for (int el = 0; el < e_local; ++el) {
+        const int e = r * e_local + el;
+        int load = 0;
+        for (int q = 0; q < W; ++q) load += c[q * E + e];
+        s_load[e] = load;
+        s_start[e] = row;
+        row += (load + 127) / 128 * 128;
+      }
+      if (row > a.rows_cap) over = true;
+      if (r == a.rank) mine = row;
+    }
+    for (int e = 0; e < E; ++e) {
+      int before = 0;
+      for (int q = 0; q < a.rank; ++q) before += c[q * E + e];
+      base_row[e] = over ? 0x40000000 : s_start[e] + before;
+    }
+    if (over) {
+      set_error(a.err, kErrBadArg);
+      mine = 0;
+    }
+    s_total = mine;
+    *total_out = mine;
+  }
+  __syncthreads();
+  const int first = a.rank * e_local;
+  for (int el = threadIdx.x; el < e_local; el += blockDim.x) {
+    const int load = s_total ? s_load[first + el] : 0;
+    n_rows[el] = load;
+    starts[el] = s_total ? s_start[first + el] : 0;
+    k_count[el] = (load + 127) / 128 * 128;
+  }
+  for (int t = threadIdx.x; t < max_tiles; t += blockDim.x) {
+    int g = -1;
+    const int row = t * 128;
+    if (row < s_total) {
+      for (int el = 0; el < e_local; ++el) {
+        const int st = s_start[first + el], len = (s_load[first + el] + 127) / 128 * 128;
+        if (row >= st && row < st + len) g = el;
+      }
+    }
+    group_tile[t] = g;
   }
 }
 
@@ -434,7 +542,8 @@ void moe_router(const void* logits, int f32, long long ld, int T, int E, int k, 
 }
 
 EPArena make_arena(const long long* peer_base, int rank, int world, const long long* offs, long long rows_cap,
-                   long long slots_cap, int d, unsigned* done, int* err, unsigned long long wait_ns) {
+                   long long slots_cap, int d, unsigned* done, unsigned* expect, int* err,
+                   unsigned long long wait_ns) {
   EPArena a;
   a.peer_base = peer_base;
   a.rank = rank;
@@ -447,6 +556,8 @@ EPArena make_arena(const long long* peer_base, int rank, int world, const long l
   a.off_ret2 = offs[5];
   a.off_xin8 = offs[6];
   a.off_xsc = offs[7];
+  a.off_counts = offs[8];
+  a.expect = expect;
   a.rows_cap = rows_cap;
   a.slots_cap = slots_cap;
   a.d = d;
@@ -457,19 +568,18 @@ EPArena make_arena(const long long* peer_base, int rank, int world, const long l
 }
 
 void ep_dispatch(const EPArena& a, const void* x, long long ldx, const int* idx, const int* pos, const int* base_row,
-                 int n_slots, int k, int e_local, int* slot_row, unsigned epoch, int ctas, cudaStream_t s) {
+                 int n_slots, int k, int e_local, int* slot_row, int ctas, cudaStream_t s) {
   (astrai::note_launch(), ep_dispatch_kernel<<<ctas, 512, 0, s>>>(a, static_cast<const __nv_bfloat16*>(x), ldx, idx, pos, base_row, n_slots, k,
-                                          e_local, slot_row, epoch));
+                                          e_local, slot_row));
 }
 
 void ep_dispatch_fp8(const EPArena& a, const void* x, long long ldx, const int* idx, const int* pos,
-                     const int* base_row, int n_slots, int k, int e_local, int* slot_row, unsigned epoch, int ctas,
+                     const int* base_row, int n_slots, int k, int e_local, int* slot_row, int ctas,
                      cudaStream_t s) {
   if (a.off_xin8 == 0 || a.off_xsc == 0 || a.d % 128 != 0)
     throw std::runtime_error("ep_dispatch_fp8: the arena has no fp8 block, or d is not a multiple of 128");
   (astrai::note_launch(), ep_dispatch_fp8_kernel<<<ctas, 512, 0, s>>>(a, static_cast<const __nv_bfloat16*>(x), ldx, idx,
-                                                                        pos, base_row, n_slots, k, e_local, slot_row,
-                                                                        epoch));
+                                                                        pos, base_row, n_slots, k, e_local, slot_row));
 }
 
 void ep_dequant(const EPArena& a, long long rows, int ctas, cudaStream_t s) {
@@ -478,16 +588,25 @@ void ep_dequant(const EPArena& a, long long rows, int ctas, cudaStream_t s) {
   (astrai::note_launch(), ep_dequant_kernel<<<ctas * 4, 256, 0, s>>>(a, rows));
 }
 
-void ep_wait(const EPArena& a, int phase, unsigned epoch, cudaStream_t s) {
-  (astrai::note_launch(), ep_wait_kernel<<<1, 32, 0, s>>>(a, phase, epoch));
+void ep_wait(const EPArena& a, int phase, cudaStream_t s) {
+  if (a.world > 32) throw std::runtime_error("ep_wait: at most 32 ranks");
+  (astrai::note_launch(), ep_wait_kernel<<<1, 32, 0, s>>>(a, phase));
+}
+
+void ep_layout(const EPArena& a, const int* counts, int E, int e_local, int* base_row, int* n_rows, int* starts,
+               int* k_count, int* group_tile, int max_tiles, int* total, cudaStream_t s) {
+  if (E > kEPMaxExperts || E != e_local * a.world || a.world > 256)
+    throw std::runtime_error("ep_layout: need n_experts = e_local * world <= 256");
+  (astrai::note_launch(), ep_layout_kernel<<<1, 256, 0, s>>>(a, counts, E, e_local, base_row, n_rows, starts, k_count,
+                                                            group_tile, max_tiles, total));
 }
 
 void ep_return(const EPArena& a, const void* rows, long long total_rows, const int* group_tile, const int* starts,
-               const int* n_rows, int to_ret2, unsigned epoch, int ctas, cudaStream_t s) {
+               const int* n_rows, int to_ret2, int ctas, cudaStream_t s) {
   (astrai::note_launch(), ep_return_kernel<<<ctas, 512, 0, s>>>(a, static_cast<const __nv_bfloat16*>(rows), total_rows,
                                                                group_tile, starts, n_rows,
-                                                               to_ret2 ? a.off_ret2 : a.off_ret, to_ret2 ? 3 : 1,
-                                                               epoch));
+                                                               to_ret2 ? a.off_ret2 : a.off_ret,
+                                                               to_ret2 ? kPhReturnBwd : kPhReturn));
 }
 
 void ep_combine(const void* slots, const float* w, const void* add, void* out, int T, int k, int d, cudaStream_t s) {
@@ -498,11 +617,10 @@ void ep_combine(const void* slots, const float* w, const void* add, void* out, i
 }
 
 void ep_combine_bwd(const EPArena& a, const void* dout, const void* slots, const float* w, const int* idx,
-                    const int* slot_row, int n_slots, int k, int e_local, float* dw, unsigned epoch, int ctas,
-                    cudaStream_t s) {
+                    const int* slot_row, int n_slots, int k, int e_local, float* dw, int ctas, cudaStream_t s) {
   (astrai::note_launch(), ep_combine_bwd_kernel<<<ctas, 512, 0, s>>>(a, static_cast<const __nv_bfloat16*>(dout),
                                              static_cast<const __nv_bfloat16*>(slots), w, idx, slot_row, n_slots, k,
-                                             e_local, dw, epoch));
+                                             e_local, dw));
 }
 
 void ep_zero_pad(const EPArena& a, int which_dyin, long long total_rows, const int* group_tile, const int* starts,

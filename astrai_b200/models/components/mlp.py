@@ -64,8 +64,9 @@ class MLP(nn.Module):
 
 @FFNFactory.register("moe")
 class DeepSeekMoE(nn.Module):
-    # routing reads per-expert token counts on the host: no CUDA-graph capture of the micro-step
-    cuda_graph_safe = False
+    # the expert layout is built on the device (no host round trip): the micro-step can be captured in a
+    # CUDA graph once the arena exists (it is sized for the token count of the first call)
+    cuda_graph_safe = True
     def __init__(self, dim: int, dim_ffn: int, n_routed_experts: int, n_shared_experts: int = 1,
                  n_activated_experts: int = 2, topk_method: str = "greedy", n_layers: int = 1,
                  moe_intermediate_size: Optional[int] = None, moe_aux_loss_coef: Optional[float] = None,
@@ -84,7 +85,9 @@ class DeepSeekMoE(nn.Module):
         down_std = 0.02 / (2 * n_layers * moe_scale) ** 0.5
         self.shared_experts = nn.ModuleList([MLP(dim, ffn, down_std) for _ in range(self.n_shared_experts)])
         self.routed_experts = nn.ModuleDict({str(j): MLP(dim, ffn, down_std) for j in range(n_routed_experts)})
-        self.capacity_factor = 2.0  # EP arena rows per expert, relative to the mean load
+        # EP arena rows per rank relative to the mean expert load; a heavier load is reported on the device
+        # error word (kErrBadArg) and its rows dropped: raise it for strongly imbalanced routing
+        self.capacity_factor = float(os.environ.get("ASTRAI_MOE_CAPACITY", "2.0"))
         # expert-parallel dispatch payload as fp8 e4m3 with 1x128 block scales (opt-in, halves the
         # dispatch bytes over NVLink; the reference moves no tokens between ranks at all)
         self.fp8_dispatch = os.environ.get("ASTRAI_EP_FP8", "0") == "1"
@@ -147,15 +150,8 @@ class DeepSeekMoE(nn.Module):
                 self._arena.close()
             self._arena = EPArena(ep, d, T, k, self.n_routed_experts, self.capacity_factor, xf.device,
                                   fp8=self.fp8_dispatch)
-        counts_all = ep.all_gather_counts(counts).cpu()
-        layout = EPLayout(counts_all.numpy(), ep.rank, self.n_routed_experts // ep.world, xf.device)
-        if layout.max_rows > self._arena.rows_cap:
-            # unbounded capacity: every rank sees the same layout, so all grow their arena together
-            # (the previous use of this layer's arena finished with its backward)
-            self._arena.close()
-            self._arena = EPArena(ep, d, T, k, self.n_routed_experts, self.capacity_factor, xf.device,
-                                  min_rows=layout.max_rows * 5 // 4, fp8=self.fp8_dispatch)
-        self._arena.check(layout)
+        # counts exchange + layout on the device: nothing is read back, so the layer can be graphed
+        layout = self._arena.compute_layout(counts)
         self._stack = stack_expert_params(self.routed_experts.values())
         add = self._shared(xf)
         if residual is not None:

@@ -5,8 +5,8 @@ runs the router kernel (fp32 softmax, top-k, renormalisation, per-expert slot
 tickets); its backward is closed-form on the small [T, E] tensors.
 
 ``moe_experts(...)`` runs dispatch -> grouped expert GEMMs (up|gate, SwiGLU,
-down; each expert's rows padded to whole 128-row tiles, so work follows the
-actual expert loads) -> return -> weighted combine with an additive input
+down; each expert's rows padded to whole 128-row tiles, tiles past the live
+rows skipped, so work follows the actual expert loads) -> return -> weighted combine with an additive input
 (residual + shared experts) in the forward, and the mirror image in the
 backward: combine-backward (gate-weight gradients + scaled output gradients
 pushed to the expert ranks) -> grouped dgrad / per-expert-K wgrad GEMMs ->
@@ -104,32 +104,33 @@ def _stacked_grad(params: Sequence[torch.nn.Parameter], shape, compute) -> None:
 
 
 class _ExpertsFn(torch.autograd.Function):
+    """Routed experts over the arena's capacity-sized blocks (``R = arena.rows_cap`` rows); the live
+    rows, their experts and the tiles to skip come from the device-side layout, so no value is read
+    back to the host."""
+
     @staticmethod
     def forward(ctx, x, add, w, idx, pos, w_gu, w_dn, arena: EPArena, layout: EPLayout, n_ug: int, *params):
         C = native()
         T, d = x.shape
         k = idx.shape[1]
-        El, R = layout.e_local, layout.total
+        El, R = layout.e_local, layout.rows
         F = w_dn.shape[2]
         dev = x.device
         slot_row = torch.empty(T * k, device=dev, dtype=torch.int32)
-        ep = arena.next_epoch(PH_DISPATCH)
         dispatch = C.ep_dispatch_fp8 if arena.fp8 else C.ep_dispatch
-        dispatch(*arena.args(), x, idx.view(-1), pos, layout.base_row, El, slot_row, ep)
-        C.ep_wait(*arena.args(), PH_DISPATCH, ep)
+        dispatch(*arena.args(), x, idx.view(-1), pos, layout.base_row, El, slot_row)
+        C.ep_wait(*arena.args(), PH_DISPATCH)
         if arena.fp8:
             C.ep_dequant(*arena.args(), R)
         h = torch.empty((R, 2 * F), device=dev, dtype=torch.bfloat16)
         a = torch.empty((R, F), device=dev, dtype=torch.bfloat16)
         y = torch.empty((R, d), device=dev, dtype=torch.bfloat16)
-        if R:
-            xin = arena.block("xin", R)
-            C.gemm_grouped(0, xin, w_gu, h, group_tile=layout.group_tile)
-            C.swiglu_fwd(h, a)
-            C.gemm_grouped(0, a, w_dn, y, group_tile=layout.group_tile)
-        ep = arena.next_epoch(PH_RETURN)
-        C.ep_return(*arena.args(), y, layout.group_tile, layout.starts, layout.n_rows, 0, ep)
-        C.ep_wait(*arena.args(), PH_RETURN, ep)
+        xin = arena.block("xin", R)
+        C.gemm_grouped(0, xin, w_gu, h, group_tile=layout.group_tile)
+        C.swiglu_fwd(h, a, layout.total)
+        C.gemm_grouped(0, a, w_dn, y, group_tile=layout.group_tile)
+        C.ep_return(*arena.args(), y, layout.group_tile, layout.starts, layout.n_rows, 0)
+        C.ep_wait(*arena.args(), PH_RETURN)
         out = torch.empty((T, d), device=dev, dtype=torch.bfloat16)
         C.ep_combine(arena.block("ret", T * k), w, add, out, k)
         ctx.save_for_backward(w, idx, slot_row, w_gu, w_dn, h, a)
@@ -143,38 +144,32 @@ class _ExpertsFn(torch.autograd.Function):
         w, idx, slot_row, w_gu, w_dn, h, a = ctx.saved_tensors
         arena, layout = ctx.arena, ctx.layout
         T, d, k, F = ctx.dims
-        El, R = layout.e_local, layout.total
+        El, R = layout.e_local, layout.rows
         dev = dout.device
         dout = dout.contiguous()
         dw = torch.empty((T, k), device=dev, dtype=torch.float32)
-        if R:
-            C.ep_zero_pad(*arena.args(), 1, R, layout.group_tile, layout.starts, layout.n_rows)
-        ep = arena.next_epoch(PH_SCATTER_BWD)
-        C.ep_combine_bwd(*arena.args(), dout, arena.block("ret", T * k), w, idx.view(-1), slot_row, El, dw, ep)
-        C.ep_wait(*arena.args(), PH_SCATTER_BWD, ep)
+        C.ep_zero_pad(*arena.args(), 1, R, layout.group_tile, layout.starts, layout.n_rows)
+        C.ep_combine_bwd(*arena.args(), dout, arena.block("ret", T * k), w, idx.view(-1), slot_row, El, dw)
+        C.ep_wait(*arena.args(), PH_SCATTER_BWD)
         ug, dn = ctx.params[:ctx.n_ug], ctx.params[ctx.n_ug:]
+        dy = arena.block("dyin", R)
+        xin = arena.block("xin", R)
+        da = torch.empty((R, F), device=dev, dtype=torch.bfloat16)
+        C.gemm_grouped(0, dy, w_dn, da, group_tile=layout.group_tile, b_mn=1)
+        # weight gradients over each expert's padded row range (an expert with no rows: k_count 0
+        # writes beta * C, i.e. zeros on the first micro-batch and no change after)
+        if any(p.requires_grad for p in dn):
+            _stacked_grad(dn, (El, d, F), lambda out, beta: C.gemm_grouped(
+                1, dy, a, out, out if beta else None, k_start=layout.starts, k_count=layout.k_count, beta=beta))
+        dh = torch.empty((R, 2 * F), device=dev, dtype=torch.bfloat16)
+        C.swiglu_bwd(da, h, dh, layout.total)
+        if any(p.requires_grad for p in ug):
+            _stacked_grad(ug, (El, 2 * F, d), lambda out, beta: C.gemm_grouped(
+                1, dh, xin, out, out if beta else None, k_start=layout.starts, k_count=layout.k_count, beta=beta))
         dxin = torch.empty((R, d), device=dev, dtype=torch.bfloat16)
-        if R:
-            dy = arena.block("dyin", R)
-            xin = arena.block("xin", R)
-            da = torch.empty((R, F), device=dev, dtype=torch.bfloat16)
-            C.gemm_grouped(0, dy, w_dn, da, group_tile=layout.group_tile, b_mn=1)
-            if any(p.requires_grad for p in dn):
-                _stacked_grad(dn, (El, d, F), lambda out, beta: C.gemm_grouped(
-                    1, dy, a, out, out if beta else None, k_start=layout.starts, k_count=layout.k_count, beta=beta))
-            dh = torch.empty((R, 2 * F), device=dev, dtype=torch.bfloat16)
-            C.swiglu_bwd(da, h, dh)
-            if any(p.requires_grad for p in ug):
-                _stacked_grad(ug, (El, 2 * F, d), lambda out, beta: C.gemm_grouped(
-                    1, dh, xin, out, out if beta else None, k_start=layout.starts, k_count=layout.k_count, beta=beta))
-            C.gemm_grouped(0, dh, w_gu, dxin, group_tile=layout.group_tile, b_mn=1)
-        else:  # no rows routed to this rank's experts: their gradients get nothing from this step
-            for p in ctx.params:
-                if p.requires_grad and p.grad is None:
-                    p.grad = torch.zeros_like(p)
-        ep = arena.next_epoch(PH_RETURN_BWD)
-        C.ep_return(*arena.args(), dxin, layout.group_tile, layout.starts, layout.n_rows, 1, ep)
-        C.ep_wait(*arena.args(), PH_RETURN_BWD, ep)
+        C.gemm_grouped(0, dh, w_gu, dxin, group_tile=layout.group_tile, b_mn=1)
+        C.ep_return(*arena.args(), dxin, layout.group_tile, layout.starts, layout.n_rows, 1)
+        C.ep_wait(*arena.args(), PH_RETURN_BWD)
         dx = torch.empty((T, d), device=dev, dtype=torch.bfloat16)
         C.ep_combine(arena.block("ret2", T * k), None, None, dx, k)
         return (dx, dout, dw, None, None, None, None, None, None, None) + (None,) * len(ctx.params)

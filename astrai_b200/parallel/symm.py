@@ -32,7 +32,8 @@ def _align(x: int) -> int:
 class SymmetricBuffer:
     """``nbytes`` of device memory on every rank, each mapped into every rank."""
 
-    def __init__(self, nbytes: int, group=None, device: Optional[torch.device] = None, local_only: bool = False):
+    def __init__(self, nbytes: int, group=None, device: Optional[torch.device] = None, local_only: bool = False,
+                 zero: bool = False):
         from astrai_b200.ops._ext import native
 
         self.C = native()
@@ -46,6 +47,9 @@ class SymmetricBuffer:
         self.nbytes = int(nbytes)
         with torch.cuda.device(self.device):
             self.local_ptr, handle = self.C.symm_alloc(self.nbytes)
+            if zero:  # cleared before any peer can map (and write into) the buffer
+                self.C.symm_view(self.local_ptr, self.nbytes, self.device.index).zero_()
+                torch.cuda.synchronize(self.device)
             handles: List[bytes] = [handle]
             if self.world > 1:
                 handles = [b""] * self.world

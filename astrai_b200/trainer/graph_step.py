@@ -13,8 +13,9 @@ What the capture relies on (checked before every replay, re-captured if violated
 * every parameter gradient exists and stays at the same address: the optimizer's ``zero_grad``
   must zero in place (``set_to_none=False``), and the captured backward accumulates into the
   gradients as eager autograd does when they exist;
-* nothing in the forward or backward synchronises with the host (the dense and SFT paths do not;
-  MoE routing reads expert counts on the host, so MoE models run eagerly).
+* nothing in the forward or backward synchronises with the host (the dense, SFT and MoE paths do
+  not: the MoE expert layout is computed on the device and the rank exchanges wait on device
+  counters); a module whose ``cuda_graph_safe`` is False keeps the micro-step eager.
 
 The first ``eager_calls`` micro-steps run eagerly, so that everything built lazily on first use
 (optimizer state, gradient buckets, packed weights, GEMM fix-up buffers, RoPE tables) exists

@@ -174,7 +174,7 @@ def bench_ep(tokens: int = 8192, d: int = 2048, n_experts: int = 64, k: int = 6)
 
     from astrai_b200.ops._ext import native
     from astrai_b200.ops.moe import moe_route
-    from astrai_b200.parallel.ep import PH_DISPATCH, PH_RETURN, EPArena, EPGroup, EPLayout
+    from astrai_b200.parallel.ep import PH_DISPATCH, PH_RETURN, EPArena, EPGroup
 
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -187,29 +187,30 @@ def bench_ep(tokens: int = 8192, d: int = 2048, n_experts: int = 64, k: int = 6)
     x = torch.randn(tokens, d, device=dev, generator=g).to(torch.bfloat16)
     logits = torch.randn(tokens, n_experts, device=dev, generator=g).to(torch.bfloat16)
     w, _, idx, counts, pos = moe_route(logits, k)
-    layout = EPLayout(ep.all_gather_counts(counts).cpu().numpy(), rank, n_experts // W, dev)
-    arena = EPArena(ep, d, tokens, k, n_experts, 2.0, dev, min_rows=layout.max_rows)
-    arena8 = EPArena(ep, d, tokens, k, n_experts, 2.0, dev, min_rows=layout.max_rows, fp8=True)
-    El, R = layout.e_local, layout.total
+    arena = EPArena(ep, d, tokens, k, n_experts, 2.0, dev)
+    arena8 = EPArena(ep, d, tokens, k, n_experts, 2.0, dev, fp8=True)
+    layout = arena.compute_layout(counts)  # device-side counts exchange + layout
+    layout8 = arena8.compute_layout(counts)
+    El, R = layout.e_local, layout.rows
     slot_row = torch.empty(tokens * k, device=dev, dtype=torch.int32)
-    y = torch.randn(max(R, 1), d, device=dev, generator=g).to(torch.bfloat16)
+    y = torch.randn(R, d, device=dev, generator=g).to(torch.bfloat16)
     out = torch.empty(tokens, d, device=dev, dtype=torch.bfloat16)
 
     def dispatch():
-        e = arena.next_epoch(PH_DISPATCH)
-        C.ep_dispatch(*arena.args(), x, idx.view(-1), pos, layout.base_row, El, slot_row, e)
-        C.ep_wait(*arena.args(), PH_DISPATCH, e)
+        C.ep_dispatch(*arena.args(), x, idx.view(-1), pos, layout.base_row, El, slot_row)
+        C.ep_wait(*arena.args(), PH_DISPATCH)
 
     def dispatch_fp8():  # e4m3 rows + 1x128 scales over NVLink, dequantised by the owner
-        e = arena8.next_epoch(PH_DISPATCH)
-        C.ep_dispatch_fp8(*arena8.args(), x, idx.view(-1), pos, layout.base_row, El, slot_row, e)
-        C.ep_wait(*arena8.args(), PH_DISPATCH, e)
+        C.ep_dispatch_fp8(*arena8.args(), x, idx.view(-1), pos, layout8.base_row, El, slot_row)
+        C.ep_wait(*arena8.args(), PH_DISPATCH)
         C.ep_dequant(*arena8.args(), R)
 
+    def layout_only():
+        arena.compute_layout(counts)
+
     def combine():
-        e = arena.next_epoch(PH_RETURN)
-        C.ep_return(*arena.args(), y[:R], layout.group_tile, layout.starts, layout.n_rows, 0, e)
-        C.ep_wait(*arena.args(), PH_RETURN, e)
+        C.ep_return(*arena.args(), y, layout.group_tile, layout.starts, layout.n_rows, 0)
+        C.ep_wait(*arena.args(), PH_RETURN)
         C.ep_combine(arena.block("ret", tokens * k), w, None, out, k)
 
     # NCCL arm: rows ordered by destination rank (experts are contiguous per rank)
@@ -237,7 +238,8 @@ def bench_ep(tokens: int = 8192, d: int = 2048, n_experts: int = 64, k: int = 6)
         dist.all_reduce(v, op=dist.ReduceOp.MAX)
         return float(v) * 1e3  # us
 
-    res = {"dispatch_us": t_max(dispatch), "dispatch_fp8_us": t_max(dispatch_fp8), "combine_us": t_max(combine),
+    res = {"layout_us": t_max(layout_only), "dispatch_us": t_max(dispatch), "dispatch_fp8_us": t_max(dispatch_fp8),
+           "combine_us": t_max(combine),
            "dispatch_combine_us": t_max(lambda: (dispatch(), combine())),
            "nccl_dispatch_us": t_max(nccl_dispatch), "nccl_combine_us": t_max(nccl_combine),
            "nccl_dispatch_combine_us": t_max(lambda: (nccl_dispatch(), nccl_combine()))}

@@ -97,6 +97,53 @@ def test_fused_moe_model_matches_fp32_reference():
     assert not torch.equal(m.layers[1].mlp.routed_experts["3"].up.weight.grad, g0)
 
 
+def test_moe_micro_step_has_no_host_sync_and_replays_from_a_graph():
+    """The expert layout is computed on the device, so an MoE forward+backward reads nothing back
+    (sync debug mode raises on any synchronising call) and the micro-step replays from a CUDA graph
+    with the gradients an eager micro-step gives."""
+    from astrai_b200.models import AutoRegressiveLM
+    from astrai_b200.trainer.graph_step import GraphedMicroStep
+
+    torch.manual_seed(0)
+    m = AutoRegressiveLM(_moe_cfg()).cuda().to(torch.bfloat16)
+    x = torch.randint(0, 1024, (2, 128), device="cuda")
+
+    def loss_fn(b):
+        out = m(b["x"])
+        return out["logits"].float().logsumexp(-1).mean() + out["aux_loss"]
+
+    loss_fn({"x": x}).backward()  # first call sizes the arenas
+    torch.cuda.synchronize()
+    torch.cuda.set_sync_debug_mode("error")
+    try:
+        loss_fn({"x": x}).backward()
+    finally:
+        torch.cuda.set_sync_debug_mode(0)
+    torch.cuda.synchronize()
+
+    def grads():
+        return [p.grad.detach().float().clone() for p in m.parameters()]
+
+    def zero():
+        for p in m.parameters():
+            p.grad.zero_()
+
+    step = GraphedMicroStep(loss_fn, m, torch.device("cuda"), eager_calls=1)
+    zero()
+    l_eager = step({"x": x}).float().item()  # eager
+    g_eager = grads()
+    zero()
+    step({"x": x})  # capture (runs the micro-step once eagerly, then records it)
+    assert step.graph is not None, step.disabled_reason
+    zero()
+    l_graph = step({"x": x}).float().item()  # replay
+    assert step.replays == 1
+    assert abs(l_graph - l_eager) < 1e-3 * max(1.0, abs(l_eager))
+    for (n, _), a, b in zip(m.named_parameters(), g_eager, grads()):
+        rel = ((a - b).norm() / a.norm().clamp_min(1e-12)).item()
+        assert rel < 1e-2, (n, rel)
+
+
 def _ep_worker(rank, world, port, fp8=False):
     """fp8: token rows cross NVLink as e4m3 with 1x128 block scales, so the forward carries a
     quantisation error of a few per cent (relative norm) against the bf16 replicated layer."""
@@ -167,7 +214,7 @@ def test_fp8_dispatch_roundtrip_single_rank():
     """fp8 dispatch inside a one-rank EP group: every dispatched row equals the bf16 token row up to
     e4m3 rounding (<= 2^-4 relative to its 128-column block's amax, plus bf16 rounding)."""
     from astrai_b200.ops._ext import native
-    from astrai_b200.parallel.ep import EPArena, EPGroup, EPLayout
+    from astrai_b200.parallel.ep import PH_DISPATCH, EPArena, EPGroup
 
     C = native()
     C.read_error()
@@ -175,23 +222,21 @@ def test_fp8_dispatch_roundtrip_single_rank():
     torch.manual_seed(0)
     x = (torch.randn(T, d, device="cuda") * torch.logspace(-2, 2, d, device="cuda")).to(torch.bfloat16)
     idx = torch.randint(0, E, (T, k), device="cuda", dtype=torch.int32)
-    counts = torch.bincount(idx.view(-1).long(), minlength=E)
+    counts = torch.bincount(idx.view(-1).long(), minlength=E).to(torch.int32)
     pos = torch.empty(T * k, device="cuda", dtype=torch.int32)
     seen = [0] * E
     for s, e in enumerate(idx.view(-1).tolist()):
         pos[s] = seen[e]
         seen[e] += 1
-    ep = EPGroup.local()
-    layout = EPLayout(counts.view(1, -1).cpu().numpy(), 0, E, "cuda")
-    arena = EPArena(ep, d, T, k, E, 2.0, torch.device("cuda"), min_rows=layout.max_rows, fp8=True)
+    arena = EPArena(EPGroup.local(), d, T, k, E, 2.0, torch.device("cuda"), fp8=True)
     assert arena.fp8
+    layout = arena.compute_layout(counts)
     slot_row = torch.empty(T * k, device="cuda", dtype=torch.int32)
-    e1 = arena.next_epoch(0)
-    C.ep_dispatch_fp8(*arena.args(), x, idx.view(-1), pos, layout.base_row, E, slot_row, e1)
-    C.ep_wait(*arena.args(), 0, e1)
-    C.ep_dequant(*arena.args(), layout.total)
+    C.ep_dispatch_fp8(*arena.args(), x, idx.view(-1), pos, layout.base_row, E, slot_row)
+    C.ep_wait(*arena.args(), PH_DISPATCH)
+    C.ep_dequant(*arena.args(), layout.rows)
     torch.cuda.synchronize()
-    got = arena.block("xin", layout.total)[slot_row.long()].float()
+    got = arena.block("xin", layout.rows)[slot_row.long()].float()
     ref = x.float().repeat_interleave(k, dim=0)
     amax = ref.abs().view(T * k, d // 128, 128).amax(-1, keepdim=True).expand(-1, -1, 128).reshape(T * k, d)
     assert ((got - ref).abs() <= amax * 2.0 ** -4 + ref.abs() * 2.0 ** -7 + 1e-6).all()
@@ -213,12 +258,15 @@ def test_grouped_gemm_matches_per_group_matmuls(mode):
     st = torch.tensor(starts, dtype=torch.int32, device="cuda")
     kc = torch.tensor(pad, dtype=torch.int32, device="cuda")
     if mode == 0:
+        # capacity tail: tiles marked -1 are skipped and their output rows left as they were
+        skip = torch.cat([tiles, torch.full((3,), -1, dtype=torch.int32, device="cuda")])
         for b_mn in (0, 1):
             K, N = 256, 384
-            a = torch.randn(R, K, device="cuda").to(torch.bfloat16)
+            a = torch.randn(R + 384, K, device="cuda").to(torch.bfloat16)
             b = torch.randn((G, K, N) if b_mn else (G, N, K), device="cuda").to(torch.bfloat16)
-            d = torch.empty(R, N, device="cuda", dtype=torch.bfloat16)
-            C.gemm_grouped(0, a, b, d, group_tile=tiles, b_mn=b_mn)
+            d = torch.full((R + 384, N), 5.0, device="cuda", dtype=torch.bfloat16)
+            C.gemm_grouped(0, a, b, d, group_tile=skip, b_mn=b_mn)
+            assert (d[R:] == 5.0).all()
             for g in range(G):
                 if n[g] == 0:
                     continue
