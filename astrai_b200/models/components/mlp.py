@@ -108,6 +108,8 @@ class DeepSeekMoE(nn.Module):
         self.routed_experts = nn.ModuleDict({k: m for k, m in self.routed_experts.items() if k in keep})
         for p in self.routed_experts.parameters():
             p._ep_local = True  # gradients come from every rank's tokens: no data-parallel all-reduce
+        if self._arena is not None:  # sharded again (a second executor over the same model)
+            self._arena.close()
         self._ep, self._arena, self._stack = ep, None, None
 
     @property

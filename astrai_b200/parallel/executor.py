@@ -231,7 +231,8 @@ class DDPExecutor(BaseExecutor):
         if self.use_distributed and self.broadcast_params:
             with torch.no_grad():
                 for t in list(model.parameters()) + list(model.buffers()):
-                    dist.broadcast(t.data, src=0)
+                    if not getattr(t, "_ep_local", False):  # expert shards differ per rank by design
+                        dist.broadcast(t.data, src=0)
         if self.use_distributed and self.expert_parallel:
             for m in model.modules():
                 if hasattr(m, "shard_experts"):

@@ -240,7 +240,7 @@ def run_ours(args, rank, world, local):
         return loss
 
     graph = None
-    if CUDA_GRAPH and MODEL != "moe":
+    if CUDA_GRAPH:
         from astrai_b200.trainer.graph_step import GraphedMicroStep
 
         graph = GraphedMicroStep(loss_fn, executor.unwrap(model), dev, scale=1.0 / ACCUM, eager_calls=ACCUM)
@@ -361,9 +361,9 @@ def run_ours_e2e(args, rank, world, local, model, executor, opt):
         batch_per_device=BATCH, grad_accum_steps=ACCUM, max_grad_norm=CLIP, ckpt_dir=None, ckpt_interval=10 ** 9,
         log_dir=tempfile.mkdtemp(prefix="astrai_bench_logs_"), nprocs=world,
         parallel_mode="ddp" if world > 1 else "none", device_type="cuda", pin_memory=True,
-        executor_kwargs={"comm_backend": "fused"},
+        executor_kwargs={"comm_backend": "fused", "expert_parallel": MODEL == "moe"},
         extra_kwargs={"label_smoothing": 0.0}, metrics=["loss", "lr", "grad_norm"],
-        cuda_graph=CUDA_GRAPH and MODEL != "moe",
+        cuda_graph=CUDA_GRAPH,
     )
     Trainer(tc, callbacks=[Timer()]).train()
     if "ms" not in timing:
