@@ -25,6 +25,10 @@ void row_reduce_bcast(const void* part, const void* recv, void* out, long long l
                       int rpo, const long long* rank_delta, unsigned* flag, unsigned epoch, unsigned* done,
                       int sms, cudaStream_t s);
 int num_sms(int device);
+void fsdp_reduce(const long long* peer_grad, const long long* seg_off, const long long* seg_vec, int n_seg,
+                 long long total_vec, int rank, int world, float scale, float* sumsq, cudaStream_t s);
+void fsdp_raise(const long long* peer_base, long long flag_off, int row, int rank, int world, unsigned epoch,
+                cudaStream_t s);
 }  // namespace astrai_host
 
 namespace {
@@ -119,6 +123,45 @@ void peer_flags_wait(int64_t flags_addr, int64_t device, int64_t rank, int64_t w
                                at::cuda::getCurrentCUDAStream().stream());
 }
 
+// Owner-side gradient reduction of the fused FSDP: peer_grad int64 [world] pool bases, seg_off int64
+// [n] byte offsets of this rank's owned gradients, seg_vec int64 [n + 1] prefix sums of their 16-byte
+// vectors; sumsq fp32 [1] (accumulated).
+void fsdp_reduce(const at::Tensor& peer_grad, const at::Tensor& seg_off, const at::Tensor& seg_vec, int64_t total_vec,
+                 int64_t rank, int64_t world, double scale, at::Tensor& sumsq) {
+  for (const at::Tensor* t : {&peer_grad, &seg_off, &seg_vec})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kLong && t->is_contiguous(), "fsdp_reduce: int64 CUDA tables");
+  TORCH_CHECK(peer_grad.numel() == world && seg_vec.numel() == seg_off.numel() + 1, "fsdp_reduce: table sizes");
+  TORCH_CHECK(sumsq.is_cuda() && sumsq.scalar_type() == at::kFloat && sumsq.numel() == 1, "fsdp_reduce: sumsq");
+  const c10::cuda::CUDAGuard g(peer_grad.device());
+  astrai_host::fsdp_reduce(reinterpret_cast<const long long*>(peer_grad.data_ptr<int64_t>()),
+                           reinterpret_cast<const long long*>(seg_off.data_ptr<int64_t>()),
+                           reinterpret_cast<const long long*>(seg_vec.data_ptr<int64_t>()),
+                           static_cast<int>(seg_off.numel()), total_vec, static_cast<int>(rank),
+                           static_cast<int>(world), static_cast<float>(scale), sumsq.data_ptr<float>(),
+                           at::cuda::getCurrentCUDAStream().stream());
+}
+
+// One device-to-device copy on the current stream, by the copy engines (addresses may be peer mappings).
+void peer_copy(int64_t dst, int64_t src, int64_t nbytes) {
+  TORCH_CHECK(nbytes >= 0 && (nbytes == 0 || (dst != 0 && src != 0)), "peer_copy: bad arguments");
+  if (nbytes == 0) return;
+  const cudaError_t e = cudaMemcpyAsync(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src),
+                                        static_cast<size_t>(nbytes), cudaMemcpyDeviceToDevice,
+                                        at::cuda::getCurrentCUDAStream().stream());
+  TORCH_CHECK(e == cudaSuccess, "peer_copy: ", cudaGetErrorString(e));
+}
+
+void fsdp_raise(const at::Tensor& peer_base, int64_t flag_off, int64_t row, int64_t rank, int64_t world,
+                int64_t epoch) {
+  TORCH_CHECK(peer_base.is_cuda() && peer_base.scalar_type() == at::kLong && peer_base.numel() == world,
+              "fsdp_raise: peer_base int64 [world]");
+  TORCH_CHECK(flag_off % 4 == 0 && row >= 0 && rank >= 0 && rank < world, "fsdp_raise: bad arguments");
+  const c10::cuda::CUDAGuard g(peer_base.device());
+  astrai_host::fsdp_raise(reinterpret_cast<const long long*>(peer_base.data_ptr<int64_t>()), flag_off,
+                          static_cast<int>(row), static_cast<int>(rank), static_cast<int>(world),
+                          static_cast<unsigned>(epoch), at::cuda::getCurrentCUDAStream().stream());
+}
+
 }  // namespace
 
 // Row-parallel all-reduce, second half: sum this rank's rows of the partial products (own partial
@@ -143,6 +186,9 @@ void register_comm(pybind11::module& m) {
   m.def("row_reduce_bcast", &row_reduce_bcast);
   m.def("muon_apply_peers", &muon_apply_peers);
   m.def("peer_flags_wait", &peer_flags_wait);
+  m.def("fsdp_reduce", &fsdp_reduce);
+  m.def("fsdp_raise", &fsdp_raise);
+  m.def("peer_copy", &peer_copy);
   m.def("symm_alloc", &symm_alloc, "cudaMalloc + IPC handle -> (address, 64-byte handle)");
   m.def("symm_open", &symm_open, "map a peer's IPC handle -> address");
   m.def("symm_close", [](int64_t p) { astrai_host::symm_close(reinterpret_cast<void*>(p)); });

@@ -1,5 +1,6 @@
 // Python bindings of the inference kernels: paged KV write / gather, paged
 // split-KV decode attention and the fused sampler.
+#include <cstdlib>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -16,6 +17,13 @@ void paged_decode_launch(const void* q, long long ldq, const void* kc, const voi
                          int n_pages, const int* lens, int B, int Hq, int Hkv, int page_size, int splits, float scale_log2,
                          float* part_acc, float* part_ml, void* out, long long ldo, int D, cudaStream_t s);
 int decode_splits(int B, int Hkv, int max_len, int sms);
+bool paged_decode_tc_supported(int D, int G, int page_size);
+void decode_combine(const float* part_acc, const float* part_ml, int B, int Hq, int Hkv, int splits, void* out,
+                    long long ldo, int D, cudaStream_t s);
+void paged_decode_tc(const void* q, long long ldq, const void* kc, const void* vc, const int* table, int max_pages,
+                     int n_pages, const int* lens, int B, int Hq, int Hkv, int page_size, int splits,
+                     float scale_log2, float* part_acc, float* part_ml, void* out, long long ldo, int D,
+                     cudaStream_t s);
 void sample_tokens(const void* logits, int f32, long long ld, int rows, int V, const float* temperature,
                    const int* top_k, const float* top_p, const float* penalty, const long long* hist, int hist_len,
                    long long ld_hist, const unsigned long long* rng, long long* out_tok, float* out_lp,
@@ -25,6 +33,14 @@ void sample_tokens(const void* logits, int f32, long long ld, int rows, int V, c
 namespace {
 
 cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+// ASTRAI_DECODE_TC=0 keeps decode on the CUDA-core kernel (for comparisons)
+bool decode_tc_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("ASTRAI_DECODE_TC");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 
 // [n_pages, Hkv, page_size, D] bf16 contiguous, D = 64 or 128; returns D
 int check_cache(const at::Tensor& c, const char* name) {
@@ -105,7 +121,11 @@ void paged_decode(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& v
   const int Hkv = static_cast<int>(kc.size(1));
   TORCH_CHECK(Hq % Hkv == 0, "n_heads must be a multiple of n_kv_heads");
   const int G = static_cast<int>(Hq / Hkv);
-  TORCH_CHECK(G == 1 || G == 2 || G == 4 || G == 8, "paged_decode: n_heads / n_kv_heads must be 1, 2, 4 or 8");
+  const int page_size = static_cast<int>(kc.size(2));
+  const bool tc = decode_tc_enabled() && astrai_host::paged_decode_tc_supported(D, G, page_size);
+  TORCH_CHECK(tc || G == 1 || G == 2 || G == 4 || G == 8,
+              "paged_decode: n_heads / n_kv_heads must be 1, 2, 4 or 8 (or a power of two up to 16 with head_dim "
+              "64 / 128 and page_size a multiple or divisor of 128)");
   TORCH_CHECK(table.dim() == 2 && table.size(0) == B && lens.numel() == B, "page_table / lens batch mismatch");
   TORCH_CHECK(q.size(1) >= Hq * D && out.size(0) == B && out.size(1) >= Hq * D, "q/out shape mismatch");
   TORCH_CHECK(splits >= 1 && splits <= 64, "splits must be in [1, 64]");
@@ -122,6 +142,17 @@ void paged_decode(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& v
     part_ml = part_acc + (long long)B * Hq * splits * D;
   }
   const c10::cuda::CUDAGuard g(q.device());
+  if (tc) {
+    astrai_host::paged_decode_tc(q.data_ptr(), q.stride(0), kc.data_ptr(), vc.data_ptr(), table.data_ptr<int>(),
+                                 static_cast<int>(table.size(1)), static_cast<int>(kc.size(0)), lens.data_ptr<int>(), B,
+                                 static_cast<int>(Hq), Hkv, page_size, static_cast<int>(splits),
+                                 static_cast<float>(scale * 1.4426950408889634), part_acc, part_ml, out.data_ptr(),
+                                 out.stride(0), D, cur_stream());
+    if (splits > 1)
+      astrai_host::decode_combine(part_acc, part_ml, B, static_cast<int>(Hq), Hkv, static_cast<int>(splits),
+                                  out.data_ptr(), out.stride(0), D, cur_stream());
+    return;
+  }
   astrai_host::paged_decode_launch(q.data_ptr(), q.stride(0), kc.data_ptr(), vc.data_ptr(), table.data_ptr<int>(),
                                    static_cast<int>(table.size(1)), static_cast<int>(kc.size(0)), lens.data_ptr<int>(),
                                    B, static_cast<int>(Hq), Hkv,

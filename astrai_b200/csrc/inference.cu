@@ -790,13 +790,20 @@ void paged_decode_launch(const void* q, long long ldq, const void* kc, const voi
                                                                       static_cast<__nv_bfloat16*>(out), ldo, D));
 }
 
-// Splits per (batch row, kv head): enough CTAs for two waves of the SMs,
-// at most one split per 64 keys of capacity, at most 32.
+void decode_combine(const float* part_acc, const float* part_ml, int B, int Hq, int Hkv, int splits, void* out,
+                    long long ldo, int D, cudaStream_t s) {
+  (astrai::note_launch(), decode_combine_kernel<<<B * Hq, D, 0, s>>>(part_acc, part_ml, B, Hq, Hkv, splits,
+                                                                    static_cast<__nv_bfloat16*>(out), ldo, D));
+}
+
+// Splits per (batch row, kv head). The tensor-core kernel runs one persistent CTA per SM over
+// (row, kv head, split) items of 128-key tiles: about 8 items per SM keep the last round of items
+// short, and a split keeps at least 2 tiles (256 keys of capacity) so its pipeline fills; at most 32.
 int decode_splits(int B, int Hkv, int max_len, int sms) {
-  const int ctas = B * Hkv;
-  int splits = (2 * sms + ctas - 1) / ctas;
-  const int max_splits = std::max(1, (max_len + 63) / 64);
-  return std::max(1, std::min(splits, std::min(max_splits, 32)));
+  const int pairs = std::max(1, B * Hkv);
+  const int want = (8 * sms + pairs - 1) / pairs;
+  const int max_splits = std::max(1, (max_len + 255) / 256);
+  return std::max(1, std::min(want, std::min(max_splits, 32)));
 }
 
 void sample_tokens(const void* logits, int f32, long long ld, int rows, int V, const float* temperature,

@@ -456,7 +456,7 @@ __global__ void __launch_bounds__(256) ep_layout_kernel(EPArena a, const int* __
                                                        int* __restrict__ starts, int* __restrict__ k_count,
                                                        int* __restrict__ group_tile, int max_tiles,
                                                        int* __restrict__ total_out) {
-  __shared__ int s_load[kEPMaxExperts], s_start[kEPMaxExperts], s_total;
+  __shared__ int s_load[kEPMaxExperts], s_start[kEPMaxExperts], s_before[kEPMaxExperts], s_total, s_over;
   __shared__ unsigned want;
   const int W = a.world;
   // 1. publish this rank's counts row on every rank, then announce it
@@ -473,38 +473,46 @@ __global__ void __launch_bounds__(256) ep_layout_kernel(EPArena a, const int* __
   // 2. wait for every rank's row (one thread per source rank)
   if (threadIdx.x < W) wait_arrival(a, kPhCounts, threadIdx.x, want);
   __syncthreads();
-  // 3. the layout (tiny: E <= 256 experts, W <= 32 ranks)
+  // 3. the layout, one thread per expert: its load over all source ranks, the rows sent by lower ranks,
+  //    and its first row inside its owner's block (padded loads of the owner's earlier experts)
+  const volatile int* c = reinterpret_cast<const volatile int*>(arena(a, a.rank, a.off_counts));
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int load = 0, before = 0;
+    for (int q = 0; q < W; ++q) {
+      const int v = c[q * E + e];
+      load += v;
+      if (q < a.rank) before += v;
+    }
+    s_load[e] = load;
+    s_before[e] = before;
+  }
+  if (threadIdx.x == 0) a.expect[kPhCounts] = want;
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int row = 0;
+    for (int f = (e / e_local) * e_local; f < e; ++f) row += (s_load[f] + 127) / 128 * 128;
+    s_start[e] = row;
+  }
+  __syncthreads();
   if (threadIdx.x == 0) {
-    a.expect[kPhCounts] = want;
-    const volatile int* c = reinterpret_cast<const volatile int*>(arena(a, a.rank, a.off_counts));
     bool over = false;
     int mine = 0;
     for (int r = 0; r < W; ++r) {
-      int row = 0;
-      for (int el = 0; el < e_local; ++el) {
-        const int e = r * e_local + el;
-        int load = 0;
-        for (int q = 0; q < W; ++q) load += c[q * E + e];
-        s_load[e] = load;
-        s_start[e] = row;
-        row += (load + 127) / 128 * 128;
-      }
-      if (row > a.rows_cap) over = true;
-      if (r == a.rank) mine = row;
-    }
-    for (int e = 0; e < E; ++e) {
-      int before = 0;
-      for (int q = 0; q < a.rank; ++q) before += c[q * E + e];
-      base_row[e] = over ? 0x40000000 : s_start[e] + before;
+      const int last = (r + 1) * e_local - 1;
+      const int rows = s_start[last] + (s_load[last] + 127) / 128 * 128;
+      if (rows > a.rows_cap) over = true;
+      if (r == a.rank) mine = rows;
     }
     if (over) {
       set_error(a.err, kErrBadArg);
       mine = 0;
     }
+    s_over = over ? 1 : 0;
     s_total = mine;
     *total_out = mine;
   }
   __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) base_row[e] = s_over ? 0x40000000 : s_start[e] + s_before[e];
   const int first = a.rank * e_local;
   for (int el = threadIdx.x; el < e_local; el += blockDim.x) {
     const int load = s_total ? s_load[first + el] : 0;

@@ -138,6 +138,13 @@ class GQA(nn.Module):
         return packed_linear_rope(x, [m.weight for m in mods], ctx.table, pos, ctx.S,
                                   (self.n_heads + self.n_kv_heads) * self.head_dim, self.head_dim)
 
+    def packed_groups(self):
+        """q, k and v projection weights: packed into one buffer for one GEMM."""
+        mods = (self.q_proj, self.k_proj, self.v_proj)
+        if all(type(m) is Linear and m.bias is None for m in mods):
+            return [[m.weight for m in mods]]
+        return []
+
     def qkv_proj(self, x: torch.Tensor) -> torch.Tensor:
         """q|k|v projections as one GEMM over the concatenated weight (plain
         Linear layers), else per-module calls (LoRA-wrapped or biased)."""

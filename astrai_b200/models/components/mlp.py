@@ -49,6 +49,12 @@ class MLP(nn.Module):
         self.gate = Linear(dim, dim_ffn)
         self.down = Linear(dim_ffn, dim, init_std=down_init_std)
 
+    def packed_groups(self):
+        """Parameters the kernel path packs into one buffer (up then gate: one GEMM)."""
+        if type(self.up) is Linear and type(self.gate) is Linear and self.up.bias is None and self.gate.bias is None:
+            return [[self.up.weight, self.gate.weight]]
+        return []
+
     def forward(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None, ctx=None) -> torch.Tensor:
         plain = all(type(m) is Linear and m.bias is None for m in (self.up, self.gate, self.down))
         if plain:
@@ -116,9 +122,22 @@ class DeepSeekMoE(nn.Module):
     def expert_parallel(self) -> bool:
         return self._ep is not None and self._ep.world > 1
 
-    def _fused_ok(self, x: torch.Tensor) -> bool:
+    def packed_groups(self):
+        """The routed experts' stacked weights (all up / gate rows, all down rows) and the shared
+        experts' up / gate pairs."""
+        groups = [g for e in self.shared_experts for g in e.packed_groups()]
         experts = list(self.routed_experts.values())
-        return (x.is_cuda and x.dtype == torch.bfloat16 and self.dim % 8 == 0 and self.n_activated_experts <= 8
+        if experts and all(type(m.up) is Linear and type(m.gate) is Linear and type(m.down) is Linear
+                           for m in experts):
+            groups.append([w for m in experts for w in (m.up.weight, m.gate.weight)])
+            groups.append([m.down.weight for m in experts])
+        return groups
+
+    def _fused_ok(self, x: torch.Tensor) -> bool:
+        from astrai_b200.ops import gemm as _gemm
+
+        experts = list(self.routed_experts.values())
+        return (_gemm.PACKING and x.is_cuda and x.dtype == torch.bfloat16 and self.dim % 8 == 0 and self.n_activated_experts <= 8
                 and self.n_routed_experts <= 256 and all(type(m.up) is Linear and type(m.down) is Linear
                                                          and m.up.weight.dtype == torch.bfloat16 for m in experts))
 

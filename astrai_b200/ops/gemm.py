@@ -55,6 +55,15 @@ def _as_rows(t: torch.Tensor) -> torch.Tensor:
 
 
 SKINNY_MAX_ROWS = 16
+# False while torch ``fully_shard`` manages the parameters: its unsharded parameters live in buffers it
+# frees and refills, so they must not be re-pointed into packed buffers (packed projections then
+# concatenate their weights per call instead)
+PACKING = True
+
+
+def set_packing(enabled: bool) -> None:
+    global PACKING
+    PACKING = bool(enabled)
 
 # SwiGLU / RoPE in GEMM epilogues (gemm_swiglu, gemm_rope): correct, but measured slower on B200 in
 # the 1.1B training step (the 4 epilogue warps of a 128-row tile become the bottleneck once they
@@ -275,7 +284,7 @@ def swiglu_mlp(x: torch.Tensor, up: torch.Tensor, gate: torch.Tensor, down: torc
     """Fused SwiGLU MLP on the kernel path, or None when it does not apply (then compose
     :func:`packed_linear`, :func:`astrai_b200.ops.activation.swiglu` and :func:`linear`)."""
     params = (up, gate, down)
-    if not FUSED_SWIGLU:
+    if not FUSED_SWIGLU or not PACKING:
         return None
     if not (x.is_cuda and x.dtype == torch.bfloat16 and all(
             p.is_cuda and p.dtype == torch.bfloat16 and type(p.data) is torch.Tensor for p in params)):
@@ -327,7 +336,7 @@ def packed_linear_rope(x: torch.Tensor, params, table: torch.Tensor, positions: 
     """Packed projection with interleaved RoPE on its first ``rope_cols`` output columns (the q and k heads
     of a fused QKV projection), or None when the kernel path does not apply."""
     params = list(params)
-    if not FUSED_EPILOGUES:
+    if not FUSED_EPILOGUES or not PACKING:
         return None
     if not (x.is_cuda and x.dtype == torch.bfloat16 and all(
             p.is_cuda and p.dtype == torch.bfloat16 and type(p.data) is torch.Tensor for p in params)):
@@ -348,7 +357,7 @@ def packed_linear(x: torch.Tensor, params, residual: Optional[torch.Tensor] = No
     params = list(params)
     cuda_ok = x.is_cuda and x.dtype == torch.bfloat16 and all(
         p.is_cuda and p.dtype == torch.bfloat16 and type(p.data) is torch.Tensor for p in params)
-    if not cuda_ok or (x.shape[-1] * 2) % 16:
+    if not cuda_ok or (x.shape[-1] * 2) % 16 or (len(params) > 1 and not PACKING):
         w = params[0] if len(params) == 1 else torch.cat(list(params), 0)
         return linear(x, w, residual=residual)
     w = pack_params(params) if len(params) > 1 else params[0]

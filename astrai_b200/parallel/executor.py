@@ -53,13 +53,16 @@ class GradientState:
 
 
 class AccumOptimizer:
-    def __init__(self, optimizer, gradient_state: GradientState):
+    def __init__(self, optimizer, gradient_state: GradientState, on_step: Optional[Callable[[], None]] = None):
         self.optimizer = optimizer
         self.gradient_state = gradient_state
+        self.on_step = on_step  # the executor's work after an optimizer step (publishing sharded parameters)
 
     def step(self, closure=None):
         if self.gradient_state.sync_gradients:
             self.optimizer.step(closure) if closure is not None else self.optimizer.step()
+            if self.on_step is not None:
+                self.on_step()
 
     def zero_grad(self, set_to_none: bool = True):
         if self.gradient_state.sync_gradients:
@@ -112,7 +115,7 @@ class BaseExecutor:
             optimizer = optimizer_fn(self.unwrap(model))
             if scheduler_fn is not None:
                 scheduler = scheduler_fn(optimizer)
-            optimizer = AccumOptimizer(optimizer, self.gradient_state)
+            optimizer = AccumOptimizer(optimizer, self.gradient_state, self.after_optimizer_step)
             if scheduler is not None:
                 scheduler = AccumScheduler(scheduler, self.gradient_state)
         return model, optimizer, scheduler
@@ -153,6 +156,9 @@ class BaseExecutor:
     def finish_step(self, model: nn.Module) -> None:
         if self.use_distributed:
             self._reduce_gradients(model)
+
+    def after_optimizer_step(self) -> None:
+        """Called after every optimizer step (explicit loops call it themselves)."""
 
     def _reduce_gradients(self, model: Optional[nn.Module] = None) -> None:
         pass
@@ -265,19 +271,41 @@ class DDPExecutor(BaseExecutor):
 
 @ExecutorFactory.register("fsdp2")
 class FSDP2Executor(BaseExecutor):
-    """Per-block parameter sharding with torch fully_shard (reference-compatible mode)."""
+    """Sharded data parallelism.
+
+    ``comm_backend="nccl"`` (default): torch ``fully_shard`` on every child module, as the reference
+    does (astrai/parallel/executor.py:316-407). ``comm_backend="fused"`` (CUDA, bf16, world > 1):
+    whole-tensor owners over NVLink peer memory (:mod:`astrai_b200.parallel.fsdp`): gradients reduced
+    to their owner in one kernel per step, the optimizer state and update sharded, parameters copied
+    from their owners by the copy engines after each optimizer step."""
 
     def __init__(self, grad_accum_steps: int = 1, mesh=None, mp_policy=None, reshard_after_forward: bool = True,
-                 **_ignored):
+                 comm_backend: str = "nccl", wait_s: float = 60.0, **_ignored):
         super().__init__(grad_accum_steps)
         self._kw = {k: v for k, v in dict(mesh=mesh, mp_policy=mp_policy,
                                           reshard_after_forward=reshard_after_forward).items() if v is not None}
+        self.comm_backend = comm_backend
+        self.wait_s = wait_s
+        self._fused = None
+
+    @property
+    def cuda_graph_safe(self) -> bool:
+        # torch FSDP2 and the fused backend both issue collectives or copies inside the micro-step
+        return False
 
     def wrap(self, model: nn.Module) -> nn.Module:
         if not self.use_distributed:
             return model
+        if self.comm_backend == "fused":
+            from astrai_b200.parallel.fsdp import FusedFSDP
+
+            self._fused = FusedFSDP(model, wait_s=self.wait_s)
+            return model
         from torch.distributed.fsdp import fully_shard
 
+        from astrai_b200.ops.gemm import set_packing
+
+        set_packing(False)  # fully_shard owns the parameter storage from here on
         for child in model.children():
             if isinstance(child, nn.ModuleList):
                 for sub in child:
@@ -288,6 +316,9 @@ class FSDP2Executor(BaseExecutor):
 
     @contextmanager
     def _no_sync(self, model: nn.Module):
+        if self._fused is not None:  # gradients accumulate locally until the step's reduction anyway
+            yield
+            return
         from torch.distributed.fsdp import FSDPModule
 
         mods = [m for m in model.modules() if isinstance(m, FSDPModule)]
@@ -301,13 +332,31 @@ class FSDP2Executor(BaseExecutor):
 
     def backward(self, loss: torch.Tensor) -> None:
         loss.backward()
+        if self._fused is not None and self.sync_gradients:
+            self._fused.reduce()
 
     def finish_step(self, model: nn.Module) -> None:
-        pass
+        if self._fused is not None:
+            self._fused.reduce()
+
+    def after_optimizer_step(self) -> None:
+        if self._fused is not None:
+            self._fused.after_optimizer_step()
 
     def clip_grad_norm(self, model: nn.Module, max_norm: Optional[float], as_tensor: bool = False):
         if not self.use_distributed:
             return super().clip_grad_norm(model, max_norm, as_tensor)
+        if self._fused is not None and self._fused.last_sumsq is not None:
+            from astrai_b200.ops._ext import native
+            from astrai_b200.optim.fused import clip_state
+
+            sumsq = self._fused.last_sumsq
+            st = clip_state(sumsq.device)
+            native().clip_coef(sumsq, float(max_norm) if max_norm is not None else -1.0, st.coef, st.norm)
+            self._fused.last_sumsq = None
+            norm = st.norm[0]
+            self.last_grad_norm = norm
+            return norm if as_tensor else float(norm)
         norm = torch.nn.utils.clip_grad_norm_(model.parameters(), max_norm if max_norm is not None else float("inf"))
         self.last_grad_norm = norm
         return norm if as_tensor else float(norm)
@@ -315,6 +364,10 @@ class FSDP2Executor(BaseExecutor):
     def unwrap_model(self, model: nn.Module):
         if not self.use_distributed:
             return model.state_dict()
+        if self._fused is not None:
+            self._fused.wait_gathers()
+            sd = {k: v for k, v in model.state_dict().items()}
+            return sd if get_rank() == 0 else None
         from torch.distributed.tensor import DTensor
 
         sd = model.state_dict()

@@ -410,6 +410,53 @@ def bench_sample():
             print(json.dumps({"kernel": "sample", "rows": rows, "case": name, "us": round(ms * 1e3, 2)}))
 
 
+def time_flushed(fn, warmup=3, iters=20, flush_bytes=256 << 20):
+    """Per-call device time with L2 flushed before every call (a write of ``flush_bytes``, outside
+    the timed events): for kernels whose working set would otherwise sit in the 126 MB L2."""
+    buf = torch.empty(flush_bytes, dtype=torch.uint8, device="cuda")
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    total = 0.0
+    for _ in range(iters):
+        buf.fill_(1)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        e.synchronize()
+        total += s.elapsed_time(e)
+    return total / iters
+
+
+def bench_decode():
+    """Paged decode attention at the reference's own benchmark shapes
+    (csrc/tests/attn_paged_decode_test.cu:280-289: Hq 32, Hkv 4, D 128, page 128) plus batch 32 over
+    4096 keys; one query token per row, L2 flushed before every call. Bytes are the K and V rows read
+    once (2 x B x Hkv x kv_len x D x 2 bytes). ``ASTRAI_DECODE_TC=0`` times the CUDA-core kernel."""
+    from astrai_b200.ops._ext import native
+
+    hbm, _, src = peaks()
+    C = native()
+    D, Hq, Hkv, page = 128, 32, 4, 128
+    for B, L in ((1, 512), (1, 1024), (1, 2048), (1, 4096), (16, 2048), (32, 1024), (32, 4096)):
+        n_pages = B * (L // page)
+        kc = torch.randn(n_pages, Hkv, page, D, device="cuda").to(torch.bfloat16)
+        vc = torch.randn_like(kc)
+        table = torch.arange(n_pages, dtype=torch.int32, device="cuda").view(B, L // page)
+        lens = torch.full((B,), L, dtype=torch.int32, device="cuda")
+        q = torch.randn(B, Hq * D, device="cuda").to(torch.bfloat16)
+        out = torch.empty_like(q)
+        splits = int(C.decode_splits(B, Hkv, L, 0))
+        ws = torch.empty(B * Hq * splits * (D + 2), device="cuda", dtype=torch.float32)
+        ms = time_flushed(lambda: C.paged_decode(q, kc, vc, table, lens, out, Hq, D ** -0.5, splits, ws))
+        nbytes = 2 * B * Hkv * L * D * 2
+        print(json.dumps({"kernel": "paged_decode", "impl": "tc" if os.environ.get("ASTRAI_DECODE_TC", "1") != "0"
+                          else "cuda_core", "B": B, "Hq": Hq, "Hkv": Hkv, "kv_len": L, "D": D, "page": page,
+                          "splits": splits, "us": round(ms * 1e3, 2), "GBps": round(nbytes / ms / 1e6, 1),
+                          "frac_hbm": round(nbytes / ms / 1e6 / hbm, 3), "peak_src": src}))
+
+
 def bench_norm(rows: int = 8192, D: int = 2048):
     """RMSNorm forward, backward and the fork backward (residual-branch gradient added) at the 1.1B
     step's shape; bytes are the algorithmic reads + writes (bf16 rows, fp32 rstd)."""
@@ -455,6 +502,8 @@ def main(argv=None):
         bench_skinny()
     if which in ("sample", "all"):
         bench_sample()
+    if which in ("decode", "all"):
+        bench_decode()
     if which in ("gemm", "all"):
         bench_gemm(args[1] if which == "gemm" and len(args) > 1 else None)
     if which in ("norm", "all"):

@@ -446,6 +446,14 @@ def run_reference(args, rank, world, local):
 
     timing = {}
 
+    def ref_result():
+        ms = timing["ms"]
+        val = world * ACCUM * BATCH * SEQ / (ms / 1e3)
+        return {"ms_per_step": ms, "value": val, "clocks": timing.get("clocks"), "loss": timing.get("loss"),
+                "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": ACCUM * BATCH * SEQ * 8 * 2,
+                        "d2h_bytes_per_step": ACCUM * 4, "note": "the reference's Trainer is its only path"},
+                "gpu_launches": None}
+
     class Timer(TrainCallback):
         def __init__(self):
             self.n = 0
@@ -466,6 +474,8 @@ def run_reference(args, rank, world, local):
                 timing["clocks"] = self.clocks.stop(visible_gpu_indices(world))
                 timing["ms"] = max_over_ranks(self.ev["s"].elapsed_time(self.ev["e"])) / args.steps
                 timing["loss"] = ctx.loss
+                if world > 1:
+                    reference_exit_after_timing(ref_result(), args, rank, world)
             self.n += 1
 
     cfg = AutoRegressiveLMConfig(**(REF_MOE_CFG if MODEL == "moe" else CFG))
@@ -499,12 +509,7 @@ def run_reference(args, rank, world, local):
         shutil.rmtree(tmp, ignore_errors=True)
     if "ms" not in timing:
         return {"unavailable": "reference run ended before the timed steps completed"}
-    ms = timing["ms"]
-    val = world * ACCUM * BATCH * SEQ / (ms / 1e3)
-    return {"ms_per_step": ms, "value": val, "clocks": timing.get("clocks"), "loss": timing.get("loss"),
-            "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": ACCUM * BATCH * SEQ * 8 * 2,
-                    "d2h_bytes_per_step": ACCUM * 4, "note": "the reference's Trainer is its only path"},
-            "gpu_launches": None}
+    return ref_result()
 
 
 # ----------------------------------------------------------------------------- post-training configs
@@ -733,7 +738,14 @@ def _run_reference_dpo(args, rank, world, total_steps, Dataset, AutoRegressiveLM
                 barrier()
                 timing["clocks"] = self.clocks.stop(visible_gpu_indices(world))
                 timing["ms"] = max_over_ranks(self.ev["s"].elapsed_time(self.ev["e"])) / args.steps
+                if world > 1:
+                    reference_exit_after_timing(dpo_result(), args, rank, world)
             self.n += 1
+
+    def dpo_result():
+        ms = timing["ms"]
+        return {"ms_per_step": ms, "value": world * 2 * DPO_PAIRS * L / (ms / 1e3), "clocks": timing.get("clocks"),
+                "gpu_launches": None}
 
     cfg = AutoRegressiveLMConfig(**CFG)
     shm = "/dev/shm" if os.path.isdir("/dev/shm") else None
@@ -755,58 +767,31 @@ def _run_reference_dpo(args, rank, world, total_steps, Dataset, AutoRegressiveLM
         shutil.rmtree(tmp, ignore_errors=True)
     if "ms" not in timing:
         return {"unavailable": "reference DPO run ended before the timed steps completed"}
-    ms = timing["ms"]
-    return {"ms_per_step": ms, "value": world * 2 * DPO_PAIRS * L / (ms / 1e3), "clocks": timing.get("clocks"),
-            "gpu_launches": None}
+    return dpo_result()
 
 
 # ----------------------------------------------------------------------------- main
-def use_post_train(kind):
-    global MODEL_DESC, METRIC, MODEL, BATCH, SEQ, ACCUM
-    MODEL = kind
-    if kind == "dpo":
-        METRIC = "DPO train tokens/s (1B dense)"
-        BATCH, SEQ, ACCUM = 2 * DPO_PAIRS, DPO_PROMPT + DPO_RESP, 1
-        MODEL_DESC += f", DPO {DPO_PAIRS} pairs/GPU, prompt {DPO_PROMPT} + chosen/rejected {DPO_RESP}, beta 0.1"
-    else:
-        METRIC = "GRPO rollout decode tokens/s (1B dense)"
-        BATCH, SEQ, ACCUM = GRPO_PROMPTS_PER_GPU * GRPO_G, GRPO_PROMPT + GRPO_NEW, 1
-        MODEL_DESC += (f", GRPO {GRPO_PROMPTS_PER_GPU} prompts/GPU x G{GRPO_G}, prompt {GRPO_PROMPT}, "
-                       f"<= {GRPO_NEW} new tokens, T0.8 top_p0.95 top_k50, KL 0.04, clip 0.2")
+def reference_exit_after_timing(res, args, rank, world):
+    """At N > 1 the reference's stock FSDP2 path deadlocks when training ends: its end-of-training
+    checkpoint calls FSDP2Executor.unwrap_model, where ranks other than 0 return before the unshard
+    collective that rank 0 then waits in (astrai/parallel/executor.py:387-395, reached from
+    astrai/trainer/train_callback.py:174). The timed steps are complete at this point, so every rank
+    prints (rank 0) and leaves here, after a barrier, instead of entering that checkpoint."""
+    import torch.distributed as dist
+
+    res = dict(res)
+    res["note"] = ("reference FSDP2 deadlocks in its end-of-training checkpoint (unwrap_model unshards "
+                   "on rank 0 only): the harness exits after the timed steps")
+    emit_line(res, args, rank, world, getattr(args, "t0", time.time()))
+    torch.cuda.synchronize()
+    dist.barrier()
+    sys.stdout.flush()
+    sys.stderr.flush()
+    os._exit(0)
 
 
-def main():
-    args = parse()
-    if args.model == "moe":
-        use_moe()
-    elif args.model in ("dpo", "grpo"):
-        use_post_train(args.model)
-    if args.impl == "reference":
-        # the reference's own launcher initialises the process group (torchrun env)
-        import torch
-
-        rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
-        local = int(os.environ.get("LOCAL_RANK", "0"))
-        torch.cuda.set_device(local)
-    else:
-        rank, world, local = dist_setup()
-    if world != args.gpus and rank == 0:
-        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
-    t0 = time.time()
-    if args.impl == "reference":
-        if MODEL not in ("dense", "moe", "dpo"):
-            res = {"unavailable": f"reference arm for --model {MODEL} is not wired in this bench"}
-        else:
-            try:
-                res = run_reference(args, rank, world, local)
-            except Exception as exc:  # report the stock path's failure instead of a traceback
-                res = {"unavailable": f"reference run raised {type(exc).__name__}: {exc}"[:400]}
-    elif MODEL == "dpo":
-        res = run_ours_dpo(args, rank, world, local)
-    elif MODEL == "grpo":
-        res = run_ours_grpo(args, rank, world, local)
-    else:
-        res = run_ours(args, rank, world, local)
+def emit_line(res, args, rank, world, t0):
+    """Rank 0 prints the bench's one JSON line for ``res``."""
     if rank == 0:
         if "unavailable" in res:
             print(json.dumps({"impl": "reference", "unavailable": res["unavailable"]}), flush=True)
@@ -857,7 +842,59 @@ def main():
                     # the full-matrix one (2-rank check: max |difference| 2.5e-3 against an update of
                     # 7.6e-3); this is the reference's stock behaviour and is timed as such
                     line["config"]["note"] = "reference: torch Muon over FSDP2 DTensor parameters (stock path)"
+            if res.get("note"):
+                line["note"] = res["note"]
             print(json.dumps(line), flush=True)
+
+
+def use_post_train(kind):
+    global MODEL_DESC, METRIC, MODEL, BATCH, SEQ, ACCUM
+    MODEL = kind
+    if kind == "dpo":
+        METRIC = "DPO train tokens/s (1B dense)"
+        BATCH, SEQ, ACCUM = 2 * DPO_PAIRS, DPO_PROMPT + DPO_RESP, 1
+        MODEL_DESC += f", DPO {DPO_PAIRS} pairs/GPU, prompt {DPO_PROMPT} + chosen/rejected {DPO_RESP}, beta 0.1"
+    else:
+        METRIC = "GRPO rollout decode tokens/s (1B dense)"
+        BATCH, SEQ, ACCUM = GRPO_PROMPTS_PER_GPU * GRPO_G, GRPO_PROMPT + GRPO_NEW, 1
+        MODEL_DESC += (f", GRPO {GRPO_PROMPTS_PER_GPU} prompts/GPU x G{GRPO_G}, prompt {GRPO_PROMPT}, "
+                       f"<= {GRPO_NEW} new tokens, T0.8 top_p0.95 top_k50, KL 0.04, clip 0.2")
+
+
+def main():
+    args = parse()
+    if args.model == "moe":
+        use_moe()
+    elif args.model in ("dpo", "grpo"):
+        use_post_train(args.model)
+    if args.impl == "reference":
+        # the reference's own launcher initialises the process group (torchrun env)
+        import torch
+
+        rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+    else:
+        rank, world, local = dist_setup()
+    if world != args.gpus and rank == 0:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    t0 = time.time()
+    args.t0 = t0
+    if args.impl == "reference":
+        if MODEL not in ("dense", "moe", "dpo"):
+            res = {"unavailable": f"reference arm for --model {MODEL} is not wired in this bench"}
+        else:
+            try:
+                res = run_reference(args, rank, world, local)
+            except Exception as exc:  # report the stock path's failure instead of a traceback
+                res = {"unavailable": f"reference run raised {type(exc).__name__}: {exc}"[:400]}
+    elif MODEL == "dpo":
+        res = run_ours_dpo(args, rank, world, local)
+    elif MODEL == "grpo":
+        res = run_ours_grpo(args, rank, world, local)
+    else:
+        res = run_ours(args, rank, world, local)
+    emit_line(res, args, rank, world, t0)
     import torch.distributed as dist
 
     if dist.is_available() and dist.is_initialized():

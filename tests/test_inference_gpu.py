@@ -79,8 +79,9 @@ def test_paged_write_and_gather(page, D):
 
 
 @pytest.mark.parametrize("D", [64, 128])
-@pytest.mark.parametrize("G", [1, 2, 4, 8])
-@pytest.mark.parametrize("page,lens", [(16, [1, 17, 300, 64]), (128, [513, 128, 5, 1000])])
+@pytest.mark.parametrize("G", [1, 2, 4, 8, 16])
+@pytest.mark.parametrize("page,lens", [(16, [1, 17, 300, 64]), (64, [65, 700, 3, 128]),
+                                       (128, [513, 128, 5, 1000]), (256, [257, 1, 900, 256])])
 @pytest.mark.parametrize("splits", [1, 7])
 def test_paged_decode_matches_reference(G, page, lens, splits, D):
     from astrai_b200.ops._ext import native
@@ -283,3 +284,41 @@ def test_paged_decode_ignores_keys_beyond_the_table():
     C.paged_decode(q, kc, vc, table, torch.tensor([16, 16], dtype=torch.int32, device="cuda"), ref, 4,
                    1 / math.sqrt(128), 3, ws)
     torch.testing.assert_close(out.float(), ref.float(), atol=1e-2, rtol=1e-2)
+
+
+@pytest.mark.parametrize("page", [16, 128])
+def test_paged_decode_unwritten_slots_hold_nan(page):
+    """Cache slots past a row's length (and whole unused pages) may hold anything, NaN included:
+    the tensor-core kernel zeroes the V rows of those keys before the P V product, so NaN never
+    reaches the output."""
+    from astrai_b200.ops._ext import native
+
+    C = native()
+    torch.manual_seed(3)
+    Hkv, G, D, B = 2, 8, 128, 3
+    Hq = G * Hkv
+    lens = [100, 300, 129]
+    max_pages = max(-(-L // page) for L in lens)
+    n_pages = B * max_pages
+    kc, vc = _rand_cache(n_pages, Hkv, page, seed=9, D=D)
+    table = torch.arange(n_pages, dtype=torch.int32, device="cuda").view(B, max_pages)
+    kr, vr = _gather_ref(kc, vc, table, torch.tensor(lens, dtype=torch.int32, device="cuda"), max(lens))
+    for b, L in enumerate(lens):  # poison every slot past the row's length
+        for t in range(L, max_pages * page):
+            pg = int(table[b, t // page])
+            kc[pg, :, t % page] = float("nan")
+            vc[pg, :, t % page] = float("nan")
+    ln = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    q = torch.randn(B, Hq * D, device="cuda").to(torch.bfloat16)
+    scale = 1 / math.sqrt(D)
+    for splits in (1, 3):
+        out = torch.empty(B, Hq * D, device="cuda", dtype=torch.bfloat16)
+        ws = torch.empty(B * Hq * splits * (D + 2), device="cuda", dtype=torch.float32)
+        C.paged_decode(q, kc, vc, table, ln, out, Hq, scale, splits, ws)
+        assert torch.isfinite(out.float()).all()
+        for b, L in enumerate(lens):
+            qb = q[b].view(Hq, D).float()
+            kb = kr[b, :L].repeat_interleave(G, dim=1)
+            vb = vr[b, :L].repeat_interleave(G, dim=1)
+            o = torch.einsum("hl,lhd->hd", torch.softmax(torch.einsum("hd,lhd->hl", qb, kb) * scale, -1), vb)
+            torch.testing.assert_close(out[b].view(Hq, D).float(), o, atol=2e-2, rtol=2e-2)
