@@ -322,6 +322,119 @@ def bench_tpgather(M: int = 8192, K: int = 2048, N: int = 8192):
     dist.destroy_process_group()
 
 
+def bench_fsdp_gemm(M: int = 8192, K: int = 2048, N: int = 11264, layers: int = 8):
+    """Sharded weights feeding their GEMMs, layer after layer (the FSDP forward): y_l = x @ W_l^T with
+    W_l [N, K] (the 1.1B model's packed up|gate weight, 46 MB) held by its owner only.
+
+    Ours (the fused FSDP's path): W_l whole on rank l % world in a symmetric buffer; the copy engines
+    pull it over NVLink into one of two local staging buffers on a side stream while the GEMM of layer
+    l - 1 runs (no SM time for the transfer). NCCL (torch FSDP2's path): every rank holds 1/world of
+    each W_l; all_gather_into_tensor on a side stream, prefetched one layer ahead, then the GEMM.
+    Device time per layer, max over ranks; roofline = max(GEMM at the measured burst peak, bytes a
+    rank receives per layer over the measured 770 GB/s peer link)."""
+    import torch.distributed as dist
+
+    from astrai_b200.ops._ext import native
+    from astrai_b200.parallel.symm import SymmetricBuffer
+
+    rank, world = _dist_init()
+    C = native()
+    hbm, tf, src = peaks()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    torch.manual_seed(0)
+    x = torch.randn(M, K, device=dev).to(torch.bfloat16)
+    wbytes = N * K * 2
+    owned = [l for l in range(layers) if l % world == rank]
+    pool = SymmetricBuffer(max(1, len(owned)) * wbytes, None, dev, zero=True)
+    g = torch.Generator(device=dev).manual_seed(7)
+    full = [(torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16) for _ in range(layers)]
+    for j, l in enumerate(owned):
+        pool.local_view(j * wbytes, wbytes).view(torch.bfloat16).view(N, K).copy_(full[l])
+    src_ptr = [pool.ptrs[l % world] + (l // world) * wbytes for l in range(layers)]
+    stage = [torch.empty(N, K, device=dev, dtype=torch.bfloat16) for _ in range(2)]
+    shard = [f.view(-1).chunk(world)[rank].clone() for f in full]
+    gathered = [torch.empty(N * K, device=dev, dtype=torch.bfloat16) for _ in range(2)]
+    y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    side = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize()
+    dist.barrier()
+
+    def ours():
+        cur = torch.cuda.current_stream()
+        ready = [torch.cuda.Event() for _ in range(layers)]
+        used = [torch.cuda.Event() for _ in range(layers)]
+        for l in range(min(2, layers)):
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                C.peer_copy(stage[l % 2].data_ptr(), src_ptr[l], wbytes)
+                ready[l].record(side)
+        for l in range(layers):
+            cur.wait_event(ready[l])
+            C.gemm(x, stage[l % 2], y, None, 0, 0)
+            used[l].record(cur)
+            if l + 2 < layers:  # refill this buffer for layer l + 2 once the GEMM has read it
+                with torch.cuda.stream(side):
+                    side.wait_event(used[l])
+                    C.peer_copy(stage[l % 2].data_ptr(), src_ptr[l + 2], wbytes)
+                    ready[l + 2].record(side)
+
+    def nccl():
+        cur = torch.cuda.current_stream()
+        ready = [torch.cuda.Event() for _ in range(layers)]
+        used = [torch.cuda.Event() for _ in range(layers)]
+
+        def gather(l):
+            with torch.cuda.stream(side):
+                if l >= 2:
+                    side.wait_event(used[l - 2])
+                dist.all_gather_into_tensor(gathered[l % 2], shard[l])
+                ready[l].record(side)
+
+        side.wait_stream(cur)
+        gather(0)
+        if layers > 1:
+            gather(1)
+        for l in range(layers):
+            cur.wait_event(ready[l])
+            C.gemm(x, gathered[l % 2].view(N, K), y, None, 0, 0)
+            used[l].record(cur)
+            if l + 2 < layers:
+                gather(l + 2)
+
+    def gemm_only():
+        for l in range(layers):
+            C.gemm(x, full[l], y, None, 0, 0)
+
+    # correctness: the last layer's output of both paths equals the local GEMM
+    ref = torch.empty_like(y)
+    C.gemm(x, full[-1], ref, None, 0, 0)
+    for fn in (ours, nccl):
+        fn()
+        torch.cuda.synchronize()
+        assert torch.equal(y, ref), f"{fn.__name__}: output differs from the local GEMM"
+    res = {}
+    for name, fn in (("ours_ms", ours), ("nccl_ms", nccl), ("gemm_only_ms", gemm_only)):
+        dist.barrier()
+        ms = time_fn(fn, warmup=3, iters=10) / layers
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        res[name] = round(t.item(), 4)
+    torch.cuda.synchronize()
+    err = int(C.read_error())
+    dist.barrier()
+    pool.close()
+    if rank == 0:
+        fl = 2.0 * M * N * K
+        link = 770.0
+        nv_ms = wbytes * (world - 1) / world / (link * 1e6)
+        roof = max(fl / (tf * 1e9), nv_ms)
+        print(json.dumps({"kernel": "fsdp_gather_gemm", "world": world, "M": M, "K": K, "N": N, "layers": layers,
+                          **res, "speedup_vs_nccl": round(res["nccl_ms"] / res["ours_ms"], 3),
+                          "roofline_ms": round(roof, 4), "frac_of_roofline": round(roof / res["ours_ms"], 3),
+                          "peak_src": src, "device_error_word": err}))
+    dist.destroy_process_group()
+
+
 def bench_tprow(M: int = 8192, K: int = 8192, N: int = 2048):
     """Row-parallel linear: y[M, N] = sum over ranks of x_r[M, K / world] @ w_r^T. Fused: ReduceGemm
     (GEMM pushing partial rows to their owners as tiles finish, owners sum and broadcast, flag waits,
@@ -449,12 +562,46 @@ def bench_decode():
         out = torch.empty_like(q)
         splits = int(C.decode_splits(B, Hkv, L, 0))
         ws = torch.empty(B * Hq * splits * (D + 2), device="cuda", dtype=torch.float32)
-        ms = time_flushed(lambda: C.paged_decode(q, kc, vc, table, lens, out, Hq, D ** -0.5, splits, ws))
+        fn = lambda: C.paged_decode(q, kc, vc, table, lens, out, Hq, D ** -0.5, splits, ws)  # noqa: E731
+        ms = time_flushed(fn)
+        # back to back without a flush, as the reference's harness times (csrc/tests/test_utils.cuh:37-56)
+        warm = time_fn(fn, warmup=10, iters=100)
         nbytes = 2 * B * Hkv * L * D * 2
         print(json.dumps({"kernel": "paged_decode", "impl": "tc" if os.environ.get("ASTRAI_DECODE_TC", "1") != "0"
                           else "cuda_core", "B": B, "Hq": Hq, "Hkv": Hkv, "kv_len": L, "D": D, "page": page,
-                          "splits": splits, "us": round(ms * 1e3, 2), "GBps": round(nbytes / ms / 1e6, 1),
+                          "splits": splits, "us": round(ms * 1e3, 2), "us_warm": round(warm * 1e3, 2),
+                          "GBps": round(nbytes / ms / 1e6, 1),
                           "frac_hbm": round(nbytes / ms / 1e6 / hbm, 3), "peak_src": src}))
+
+
+def bench_prefill():
+    """Prefill attention forward at the reference's own benchmark shapes (csrc/tests/attn_prefill_test.cu
+    :12-20: Hq 32, Hkv 4, D 128, q = kv length, causal and not), timed back to back as that harness
+    does; SDPA on the same shapes beside it. FLOPs: 4 B Hq q kv D (half when causal)."""
+    import torch.nn.functional as F
+
+    from astrai_b200.ops.attention import flash_forward
+
+    _, tf, src = peaks()
+    Hq, Hkv, D = 32, 4, 128
+    for B, L, causal in ((1, 512, 0), (1, 1024, 0), (1, 2048, 0), (1, 2048, 1), (4, 2048, 1), (1, 4096, 1)):
+        q = torch.randn(B * L, Hq * D, device="cuda").to(torch.bfloat16)
+        kv = torch.randn(B * L, 2 * Hkv * D, device="cuda").to(torch.bfloat16)
+        o = torch.empty_like(q)
+        lse = torch.empty(B, Hq, L, device="cuda", dtype=torch.float32)
+        fn = lambda: flash_forward(q, 0, kv, 0, kv, Hkv * D, o, lse, B, L, L, Hq, Hkv, D, D ** -0.5,  # noqa: E731
+                                   bool(causal), None)
+        ms = time_fn(fn, warmup=10, iters=50)
+        qt = q.view(B, L, Hq, D).transpose(1, 2)
+        kt = kv[:, :Hkv * D].view(B, L, Hkv, D).transpose(1, 2)
+        vt = kv[:, Hkv * D:].view(B, L, Hkv, D).transpose(1, 2)
+        ms_ref = time_fn(lambda: F.scaled_dot_product_attention(qt, kt, vt, is_causal=bool(causal), enable_gqa=True),
+                         warmup=10, iters=50)
+        flops = 4.0 * B * Hq * L * L * D * (0.5 if causal else 1.0)
+        print(json.dumps({"kernel": "prefill_attention", "B": B, "Hq": Hq, "Hkv": Hkv, "q": L, "kv": L, "D": D,
+                          "causal": causal, "ms": round(ms, 4), "tflops": round(flops / ms / 1e9, 1),
+                          "frac_of_peak": round(flops / ms / 1e9 / tf, 3), "sdpa_ms": round(ms_ref, 4),
+                          "peak_src": src}))
 
 
 def bench_norm(rows: int = 8192, D: int = 2048):
@@ -498,12 +645,17 @@ def main(argv=None):
     if which == "tprow":
         bench_tprow()
         return
+    if which == "fsdp":
+        bench_fsdp_gemm()
+        return
     if which in ("skinny", "all"):
         bench_skinny()
     if which in ("sample", "all"):
         bench_sample()
     if which in ("decode", "all"):
         bench_decode()
+    if which in ("prefill", "all"):
+        bench_prefill()
     if which in ("gemm", "all"):
         bench_gemm(args[1] if which == "gemm" and len(args) > 1 else None)
     if which in ("norm", "all"):

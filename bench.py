@@ -777,13 +777,15 @@ def reference_exit_after_timing(res, args, rank, world):
     collective that rank 0 then waits in (astrai/parallel/executor.py:387-395, reached from
     astrai/trainer/train_callback.py:174). The timed steps are complete at this point, so every rank
     prints (rank 0) and leaves here, after a barrier, instead of entering that checkpoint."""
+    import torch
     import torch.distributed as dist
 
     res = dict(res)
     res["note"] = ("reference FSDP2 deadlocks in its end-of-training checkpoint (unwrap_model unshards "
                    "on rank 0 only): the harness exits after the timed steps")
     emit_line(res, args, rank, world, getattr(args, "t0", time.time()))
-    torch.cuda.synchronize()
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
     dist.barrier()
     sys.stdout.flush()
     sys.stderr.flush()
