@@ -511,8 +511,11 @@ def bench_skinny():
 
 
 def bench_sample():
-    """Fused sampler on [rows, 32000] logits: greedy, top-k, top-p, both."""
-    from astrai_b200.inference.sample import sample
+    """Fused sampler on [rows, 32000] logits: greedy, top-k, top-p, both. ``us``: the public
+    ``sample()`` per call (host argument handling included); ``kernel_us``: the kernel alone, as the
+    decode engine runs it (static argument tensors, 20 calls replayed from one CUDA graph).
+    ``ASTRAI_SAMPLE_CTA=0`` times the cluster kernel for every vocabulary."""
+    from astrai_b200.inference.sample import _as_row_tensor, _rng_for, fused_sample, sample
 
     for rows in (1, 4, 32):
         x = torch.randn(rows, 32000, device="cuda") * 3
@@ -520,7 +523,22 @@ def bench_sample():
                          ("topp0.95", dict(temperature=0.8, top_p=0.95)),
                          ("topk50_topp0.95", dict(temperature=0.8, top_k=50, top_p=0.95))):
             ms = time_fn(lambda: sample(x, **kw), warmup=5, iters=20)
-            print(json.dumps({"kernel": "sample", "rows": rows, "case": name, "us": round(ms * 1e3, 2)}))
+            args = [_as_row_tensor(kw.get("temperature", 1.0), rows, x.device, torch.float32),
+                    _as_row_tensor(kw.get("top_k", 0), rows, x.device, torch.int32),
+                    _as_row_tensor(kw.get("top_p", 1.0), rows, x.device, torch.float32),
+                    _as_row_tensor(0.0, rows, x.device, torch.float32)]
+            tok = torch.empty(rows, dtype=torch.int64, device="cuda")
+            lp = torch.empty(rows, dtype=torch.float32, device="cuda")
+            rng = _rng_for(x.device)
+            fused_sample(x, *args, None, rng, tok, lp)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(20):
+                    fused_sample(x, *args, None, rng, tok, lp)
+            kern = time_fn(g.replay, warmup=3, iters=10) / 20
+            print(json.dumps({"kernel": "sample", "rows": rows, "case": name, "us": round(ms * 1e3, 2),
+                              "kernel_us": round(kern * 1e3, 2)}))
 
 
 def time_flushed(fn, warmup=3, iters=20, flush_bytes=256 << 20):
@@ -566,10 +584,17 @@ def bench_decode():
         ms = time_flushed(fn)
         # back to back without a flush, as the reference's harness times (csrc/tests/test_utils.cuh:37-56)
         warm = time_fn(fn, warmup=10, iters=100)
+        # the same, 20 calls replayed from one CUDA graph: device time without the host binding's cost
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(20):
+                fn()
+        graph = time_fn(g.replay, warmup=3, iters=10) / 20
         nbytes = 2 * B * Hkv * L * D * 2
         print(json.dumps({"kernel": "paged_decode", "impl": "tc" if os.environ.get("ASTRAI_DECODE_TC", "1") != "0"
                           else "cuda_core", "B": B, "Hq": Hq, "Hkv": Hkv, "kv_len": L, "D": D, "page": page,
                           "splits": splits, "us": round(ms * 1e3, 2), "us_warm": round(warm * 1e3, 2),
+                          "us_graph": round(graph * 1e3, 2),
                           "GBps": round(nbytes / ms / 1e6, 1),
                           "frac_hbm": round(nbytes / ms / 1e6 / hbm, 3), "peak_src": src}))
 

@@ -783,6 +783,11 @@ def reference_exit_after_timing(res, args, rank, world):
     res = dict(res)
     res["note"] = ("reference FSDP2 deadlocks in its end-of-training checkpoint (unwrap_model unshards "
                    "on rank 0 only): the harness exits after the timed steps")
+    # the reference's progress bar leaves its line open on stderr: start the JSON on a fresh line
+    sys.stderr.write("\n")
+    sys.stderr.flush()
+    if rank == 0:
+        print(flush=True)
     emit_line(res, args, rank, world, getattr(args, "t0", time.time()))
     if torch.cuda.is_available():
         torch.cuda.synchronize()
