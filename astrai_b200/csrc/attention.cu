@@ -18,8 +18,8 @@
 //               smem tile for the PV MMA; final O / l and log-sum-exp.
 // Backward, one CTA per (128-key block, kv head, batch), looping over the
 // query heads of the group and the causal query blocks:
-//   S^T = K Q^T, dP^T = V dO^T (TMEM), P^T and dS^T (scaled) to smem,
-//   dV += P^T dO, dK += dS^T Q (TMEM accumulators for the whole CTA),
+//   S^T = K Q^T, dP^T = V dO^T (TMEM), P^T back to TMEM and dS^T (scaled) to smem,
+//   dV += P^T dO (P^T from TMEM), dK += dS^T Q (TMEM accumulators for the whole CTA),
 //   dQ_part = dS K -> fp32 atomics into a dQ accumulator.
 // All waits are time-bounded (common.cuh).
 #include <cfloat>
@@ -416,11 +416,14 @@ struct FlashBwdParams {
 // Query tile of the backward pass (keys per CTA stay 128).
 constexpr int FB_BM = 64;
 constexpr int FB_QT = 64 * 64 * 2;  // one 64-row x 64-col swizzled chunk (8 KB)
-// smem: K(2 chunks) V(2) | Q ring FB_QD x 2 chunks(8K) | dO ring FB_QD x 2 | P^T [128x64] | dS^T [128x64]
+// smem: K(2 chunks) V(2) | Q ring FB_QD x 2 chunks(8K) | dO ring FB_QD x 2 | dS^T [2 slots][128x64]
 // | lse / delta ring | dQ staging. The Q/dO ring is 3 deep so the loads of a query tile are issued one
 // tile earlier than a 2-deep ring allows (a slot frees only when the gradient MMAs of its tile finish,
-// which follow that tile's softmax); P^T / dS^T have one slot, which the softmax of tile t fills only
-// after the MMAs of tile t-1 read it (its own math overlaps those MMAs). Total: exactly 227 KB.
+// which follow that tile's softmax). P^T stays in TMEM (the dP^T columns of its buffer) as the A
+// operand of the dV MMA; dS^T, needed as an operand in shared memory by the dK and dQ MMAs, has two
+// slots, so the softmax of tile t only waits for the MMAs of tile t-2. The kernel is bound by shared-
+// memory bandwidth (the N = 64 MMAs read 6 KB of operands per 32 tensor cycles): keeping P^T out of
+// shared memory removes its 16 KB write and the dV MMA's 16 KB of A reads per tile. Total: 227 KB.
 constexpr int FB_QD = 3;
 constexpr int FB_DQ_BYTES = 64 * 128 * 4;  // fp32 dQ staging tile [64 q][128 d]
 constexpr int FA_BWD_SMEM =
@@ -438,9 +441,8 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
   uint8_t* sV = sK + 2 * FA_TILE;       // 2 chunks
   uint8_t* sQ = sV + 2 * FA_TILE;              // [FB_QD slots][2 chunks][64 q][64 d]
   uint8_t* sdO = sQ + FB_QD * 2 * FB_QT;       // same
-  uint8_t* sP = sdO + FB_QD * 2 * FB_QT;       // [128 keys][64 q]
-  uint8_t* sdS = sP + FA_TILE;                 // [128 keys][64 q]
-  float* sLse = reinterpret_cast<float*>(sdS + FA_TILE);  // [FB_QD][64] log2 units
+  uint8_t* sdS = sdO + FB_QD * 2 * FB_QT;      // [2 slots][128 keys][64 q] dS^T (P^T lives in TMEM)
+  float* sLse = reinterpret_cast<float*>(sdS + 2 * FA_TILE);  // [FB_QD][64] log2 units
   float* sDelta = sLse + FB_QD * 64;                       // [FB_QD][64]
   float* sdQ = sDelta + FB_QD * 64;                        // [64][128] fp32 staging
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sdQ) + FB_DQ_BYTES);
@@ -541,9 +543,12 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
       const uint64_t dK_k = sdesc_sw128(smem_u32(sK), 16, 1024);         // K as A, K-major
       const uint64_t dV_k = sdesc_sw128(smem_u32(sV), 16, 1024);         // V as A, K-major
       const uint64_t dK_mn = sdesc_sw128(smem_u32(sK), FA_TILE, 1024);   // K^T as A, MN-major
-      const uint64_t dP = sdesc_sw128(smem_u32(sP), 16, 1024);           // P^T as A
-      const uint64_t dS_k = sdesc_sw128(smem_u32(sdS), 16, 1024);        // dS^T as A
-      const uint64_t dS_mn = sdesc_sw128(smem_u32(sdS), 2 * FA_TILE, 1024);  // dS^T as B, MN-major
+      uint64_t dS_k[2], dS_mn[2];  // dS^T slot i as A (K-major) / as B (MN-major)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        dS_k[i] = sdesc_sw128(smem_u32(sdS + i * FA_TILE), 16, 1024);
+        dS_mn[i] = sdesc_sw128(smem_u32(sdS + i * FA_TILE), 2 * FA_TILE, 1024);
+      }
       uint64_t dQ_k[FB_QD], dO_k[FB_QD], dQ_mn[FB_QD], dO_mn[FB_QD];
 #pragma unroll
       for (int i = 0; i < FB_QD; ++i) {
@@ -560,17 +565,20 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
         // dV += P^T dO ; dK += dS^T Q   (M = keys, N = d, K = 64 queries)
         const int slot = it & 1, qs = it % FB_QD;
         const uint64_t bo = pick(dO_mn, qs), bq = pick(dQ_mn, qs);
+        // P^T of this iteration sits in TMEM (the dP^T columns of its buffer, bf16 pairs): the dV MMA
+        // takes it as the A operand, so only dO is read from shared memory
+        const uint32_t tP = tmem + slot * 128 + 64;
 #pragma unroll
         for (int k = 0; k < FB_BM / 16; ++k) {
-          umma_bf16(tdV, dP + (uint64_t)(k * 2), bo + (uint64_t)(k * 128), idGR, (it | k) != 0);
-          umma_bf16(tdK, dS_k + (uint64_t)(k * 2), bq + (uint64_t)(k * 128), idGR, (it | k) != 0);
+          umma_bf16_ts(tdV, tP + (uint32_t)(k * 8), bo + (uint64_t)(k * 128), idGR, (it | k) != 0);
+          umma_bf16(tdK, (slot ? dS_k[1] : dS_k[0]) + (uint64_t)(k * 2), bq + (uint64_t)(k * 128), idGR, (it | k) != 0);
         }
         umma_commit(&qd_empty[qs]);
         // dQ^T = K^T dS^T  (M = d, N = 64 queries, K = 128 keys) over this iteration's S^T,
         // which the softmax has read (ps_ready waited by the caller)
 #pragma unroll
         for (int k = 0; k < FA_BN / 16; ++k)
-          umma_bf16(tmem + slot * 128, dK_mn + (uint64_t)(k * 128), dS_mn + (uint64_t)(k * 128), idDQ, k > 0);
+          umma_bf16(tmem + slot * 128, dK_mn + (uint64_t)(k * 128), (slot ? dS_mn[1] : dS_mn[0]) + (uint64_t)(k * 128), idDQ, k > 0);
         umma_commit(&dq_full[slot]);
         return true;
       };
@@ -636,7 +644,7 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
         }
       }
       const uint32_t lse_a = smem_u32(sLse + qs * 64), dlt_a = smem_u32(sDelta + qs * 64);
-      const uint32_t pc = smem_u32(sP), dc = smem_u32(sdS);
+      const uint32_t dc = smem_u32(sdS + slot * FA_TILE);
       uint32_t sv[64], dpv[64];
       const uint32_t tS = tmem + slot * 128, tdP = tS + 64;
 #pragma unroll
@@ -671,20 +679,23 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
           dk[c][i] = pack_bf16(dsv[0], dsv[1]);
         }
       }
-      // the single P^T/dS^T slot was last read by the MMAs of it-1 (issued when its softmax
-      // arrived on ps_ready): wait only now, so this tile's math overlapped those MMAs
-      if (it >= 1 && !mbar_wait(&dq_full[(it - 1) & 1], ((it - 1) >> 1) & 1, p.err, kErrWaitAccFull)) {
+      // P^T into the dP^T columns of this buffer (already read into registers): bf16 pairs, the A operand
+      // of the dV MMA
+      tmem_st16(tdP + lane_off, pk[0]);
+      tmem_st16(tdP + 16 + lane_off, pk[1]);
+      // dS^T slot it & 1 was last read by the gradient MMAs of it-2: wait only now, so this tile's math
+      // overlapped them
+      if (it >= 2 && !mbar_wait(&dq_full[slot], ((it - 2) >> 1) & 1, p.err, kErrWaitAccFull)) {
         ok = false;
         break;
       }
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          st_shared_v4(swz(pc, r, c * 4 + g), pk[c][4 * g], pk[c][4 * g + 1], pk[c][4 * g + 2], pk[c][4 * g + 3]);
+        for (int g = 0; g < 4; ++g)
           st_shared_v4(swz(dc, r, c * 4 + g), dk[c][4 * g], dk[c][4 * g + 1], dk[c][4 * g + 2], dk[c][4 * g + 3]);
-        }
       }
+      tmem_wait_st();
       fence_async_smem();
       tc_fence_before();
       __syncwarp();

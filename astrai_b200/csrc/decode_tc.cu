@@ -40,6 +40,19 @@ constexpr int DT_N = 64;                // MMA N: query heads of one KV head, pa
 constexpr int DT_KCHUNK = 128 * 128;    // one [128 keys][64 d] bf16 chunk, 128B-swizzled (16 KB)
 constexpr int DT_QCHUNK = DT_N * 128;   // one [64 heads][64 d] chunk (8 KB)
 constexpr int DT_PSLOT = 128 * 128;     // P^T [128 keys][64 heads] (16 KB)
+// Ring depths: a K stage frees as soon as its S MMA is done, a V stage (with the P^T slot) only
+// after its P V MMA, so K runs ahead by a stage. Shared memory at D = 128: 3 x 32 KB K + 2 x 32 KB V
+// + 2 x 16 KB Q (double-buffered over items) + 2 x 16 KB P^T = 224 KB.
+template <int D>
+struct DtStages;
+template <>
+struct DtStages<128> {
+  static constexpr int K = 3, V = 2;
+};
+template <>
+struct DtStages<64> {
+  static constexpr int K = 4, V = 4;
+};
 
 __device__ __forceinline__ uint32_t swz128(uint32_t base, int r, int g) {
   return base + r * 128 + ((g ^ (r & 7)) << 4);
@@ -93,37 +106,46 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
   constexpr int GC = G < 8 ? 8 : G;                 // TMEM columns read per thread (x8 / x16 loads)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  // [stage 0: K | V][stage 1: K | V] | Q (2 chunks) | P^T (2 slots) | reductions | barriers
-  uint8_t* sKV = smem;
-  uint8_t* sQ = sKV + 4 * KV_BYTES;
-  uint8_t* sP = sQ + 2 * DT_QCHUNK;
+  constexpr int KST = DtStages<D>::K, VST = DtStages<D>::V;
+  // K ring | V ring | Q (2 item buffers x 2 chunks) | P^T (2 slots) | reductions | barriers. For D = 64
+  // the unused half of the V^T operand's M reads the 16 KB after a V stage (the next stage or Q).
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + KST * KV_BYTES;
+  uint8_t* sQ = sV + VST * KV_BYTES;
+  uint8_t* sP = sQ + 2 * 2 * DT_QCHUNK;
   float* sRed = reinterpret_cast<float*>(sP + 2 * DT_PSLOT);  // [2][4 warps][G] maxima, then [4][G] sums
   uint64_t* bars = reinterpret_cast<uint64_t*>(sRed + 2 * 4 * 16 + 4 * 16);
-  uint64_t* kfull = bars;        // [2] K tile landed
-  uint64_t* vfull = bars + 2;    // [2] V tile landed
-  uint64_t* kvfree = bars + 4;   // [2] PV of the stage done: K/V stage and P^T slot free, O^T updated
-  uint64_t* sfull = bars + 6;    // [2] S^T of the buffer in TMEM
-  uint64_t* sfree = bars + 8;    // [2] S^T read by the softmax (4 warps)
-  uint64_t* pfull = bars + 10;   // [2] P^T written (4 warps)
-  uint64_t* qfull = bars + 12;   // Q of the item staged (4 warps)
-  uint64_t* qfree = bars + 13;   // last S^T of the item issued and done
-  uint64_t* ofree = bars + 14;   // O^T of the item read out (4 warps)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  uint64_t* kfull = bars;           // [KST] K tile landed
+  uint64_t* kfree = kfull + KST;    // [KST] S MMA of the K tile done
+  uint64_t* vfull = kfree + KST;    // [VST] V tile landed
+  uint64_t* vfree = vfull + VST;    // [VST] P V of the tile done: V stage and P^T slot free, O^T updated
+  uint64_t* sfull = vfree + VST;    // [2] S^T of the buffer in TMEM
+  uint64_t* sfree = sfull + 2;      // [2] S^T read by the softmax (4 warps)
+  uint64_t* pfull = sfree + 2;      // [2] P^T written (4 warps)
+  uint64_t* qfull = pfull + 2;      // [2] Q of an item staged in buffer n & 1 (4 warps)
+  uint64_t* qfree = qfull + 2;      // [2] last S MMA of the item in buffer n & 1 done
+  uint64_t* ofree = qfree + 2;      // [2] O^T buffer n & 1 read out (4 warps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ofree + 2);
 
   const int warp = warp_id(), lane = lane_id();
   const int items = p.B * p.Hkv * p.splits;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < KST; ++i) {
       mbar_init(&kfull[i], 1);
+      mbar_init(&kfree[i], 1);
+    }
+    for (int i = 0; i < VST; ++i) {
       mbar_init(&vfull[i], 1);
-      mbar_init(&kvfree[i], 1);
+      mbar_init(&vfree[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&sfull[i], 1);
       mbar_init(&sfree[i], 4);
       mbar_init(&pfull[i], 4);
+      mbar_init(&qfull[i], 4);
+      mbar_init(&qfree[i], 1);
+      mbar_init(&ofree[i], 4);
     }
-    mbar_init(qfull, 4);
-    mbar_init(qfree, 1);
-    mbar_init(ofree, 4);
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, 256);
@@ -131,7 +153,8 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tO = tmem + 128;  // S^T buffers at tmem + 0 / + 64
+  // S^T buffers at tmem + 0 / + 64, O^T of item n at tmem + 128 + 64 (n & 1)
+  auto tO = [&](int n) { return tmem + 128u + 64u * (uint32_t)(n & 1); };
 
   // tile range of an item: tiles are the 128-key blocks of the row, split evenly
   auto item_range = [&](int item, int& b, int& hk, int& split, int& t0, int& t1, int& len) {
@@ -146,10 +169,15 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
   };
 
   if (warp == 0) {
-    // ---------------------------------------------------------- TMA producer
-    if (lane == 0) {
-      prefetch_tmap(&tmK);
-      prefetch_tmap(&tmV);
+    // ---------------------------------------------------------- TMA producers: lane 0 K, lane 1 V
+    if (lane < 2) {
+      const bool isk = lane == 0;
+      const CUtensorMap* map = isk ? &tmK : &tmV;
+      prefetch_tmap(map);
+      const int ST = isk ? KST : VST;
+      uint64_t* full = isk ? kfull : vfull;
+      uint64_t* freeb = isk ? kfree : vfree;
+      uint8_t* ring = isk ? sK : sV;
       const int nsub = 128 / p.box_rows;
       const uint32_t sub_bytes = (uint32_t)p.box_rows * 128u;
       long long g = 0;
@@ -159,8 +187,8 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
         item_range(item, b, hk, split, t0, t1, len);
         const int* trow = p.table + (long long)b * p.max_pages;
         for (int t = t0; t < t1; ++t, ++g) {
-          const int s = (int)(g & 1);
-          if (g >= 2 && !(ok = mbar_wait(&kvfree[s], (uint32_t)(((g - 2) >> 1) & 1), p.err, kErrWaitEmpty))) break;
+          const int s = (int)(g % ST);
+          if (g >= ST && !(ok = mbar_wait(&freeb[s], (uint32_t)(((g / ST) - 1) & 1), p.err, kErrWaitEmpty))) break;
           int rows[8];  // TMA row coordinate of each sub-block, -1 when skipped (nsub <= 8 needs box_rows >= 16)
           uint32_t bytes = 0;
           for (int i = 0; i < nsub; ++i) {
@@ -172,18 +200,12 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
                           : -1;
             if (rows[i] >= 0) bytes += sub_bytes * NCH;
           }
-          uint8_t* sK = sKV + s * 2 * KV_BYTES;
-          uint8_t* sV = sK + KV_BYTES;
-          mbar_expect_tx(&kfull[s], bytes);
+          uint8_t* dst = ring + s * KV_BYTES;
+          mbar_expect_tx(&full[s], bytes);
           for (int i = 0; i < nsub; ++i)
             if (rows[i] >= 0)
 #pragma unroll
-              for (int c = 0; c < NCH; ++c) tma_load_2d(sK + c * DT_KCHUNK + i * sub_bytes, &tmK, &kfull[s], c * 64, rows[i]);
-          mbar_expect_tx(&vfull[s], bytes);
-          for (int i = 0; i < nsub; ++i)
-            if (rows[i] >= 0)
-#pragma unroll
-              for (int c = 0; c < NCH; ++c) tma_load_2d(sV + c * DT_KCHUNK + i * sub_bytes, &tmV, &vfull[s], c * 64, rows[i]);
+              for (int c = 0; c < NCH; ++c) tma_load_2d(dst + c * DT_KCHUNK + i * sub_bytes, map, &full[s], c * 64, rows[i]);
         }
       }
     }
@@ -192,30 +214,22 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16(128, DT_N, 0, 0);  // S^T: K (K-major) x Q (K-major)
       constexpr uint32_t idO = idesc_bf16(128, DT_N, 1, 1);  // O^T: V^T (MN-major) x P^T (MN-major)
-      const uint64_t dQ = sdesc_sw128(smem_u32(sQ), 16, 1024);
-      uint64_t dK[2], dV[2], dP[2];
-#pragma unroll
-      for (int s = 0; s < 2; ++s) {
-        const uint32_t kb = smem_u32(sKV + s * 2 * KV_BYTES);
-        dK[s] = sdesc_sw128(kb, 16, 1024);
-        // V^T as A: M = head-dim rows in 64-row chunks DT_KCHUNK apart (for D = 64 the second half of M
-        // reads the next 16 KB of shared memory; those O^T rows are never read)
-        dV[s] = sdesc_sw128(kb + KV_BYTES, DT_KCHUNK, 1024);
-        dP[s] = sdesc_sw128(smem_u32(sP + s * DT_PSLOT), DT_PSLOT, 1024);
-      }
       long long g = 0;
       bool ok = true;
       int n_it = 0;
-      auto issue_pv = [&](long long gg, bool first) -> bool {
-        const int s = (int)(gg & 1);
-        const uint32_t ph = (uint32_t)((gg >> 1) & 1);
-        if (!mbar_wait(&pfull[s], ph, p.err, kErrWaitAccFull) || !mbar_wait(&vfull[s], ph, p.err, kErrWaitFull))
+      auto issue_pv = [&](long long gg, bool first, int n) -> bool {
+        const int vs = (int)(gg % VST), ps = (int)(gg & 1);
+        if (!mbar_wait(&pfull[ps], (uint32_t)((gg >> 1) & 1), p.err, kErrWaitAccFull) ||
+            !mbar_wait(&vfull[vs], (uint32_t)((gg / VST) & 1), p.err, kErrWaitFull))
           return false;
         tc_fence_after();
+        // V^T as A: M = head-dim rows in 64-row chunks DT_KCHUNK apart
+        const uint64_t dV = sdesc_sw128(smem_u32(sV + vs * KV_BYTES), DT_KCHUNK, 1024);
+        const uint64_t dP = sdesc_sw128(smem_u32(sP + ps * DT_PSLOT), DT_PSLOT, 1024);
 #pragma unroll
         for (int k = 0; k < 8; ++k)  // 16 keys per step: +2048 bytes in both MN-major operands
-          umma_bf16(tO, dV[s] + (uint64_t)(k * 128), dP[s] + (uint64_t)(k * 128), idO, !(first && k == 0));
-        umma_commit(&kvfree[s]);
+          umma_bf16(tO(n), dV + (uint64_t)(k * 128), dP + (uint64_t)(k * 128), idO, !(first && k == 0));
+        umma_commit(&vfree[vs]);
         return true;
       };
       // n_it counts the items with keys (the softmax warps stage Q / read O^T for those only)
@@ -223,26 +237,31 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
         int b, hk, split, t0, t1, len;
         item_range(item, b, hk, split, t0, t1, len);
         if (t1 <= t0) continue;
-        if (!(ok = mbar_wait(qfull, (uint32_t)(n_it & 1), p.err, kErrWaitFull))) break;
-        // the first PV of this item overwrites O^T: the previous item's epilogue must have read it
-        if (n_it > 0 && !(ok = mbar_wait(ofree, (uint32_t)((n_it - 1) & 1), p.err, kErrWaitAccEmpty))) break;
+        const int qb = n_it & 1;
+        if (!(ok = mbar_wait(&qfull[qb], (uint32_t)((n_it >> 1) & 1), p.err, kErrWaitFull))) break;
+        // the first P V of this item overwrites O^T buffer qb: the epilogue of item n_it - 2 must have read it
+        if (n_it >= 2 && !(ok = mbar_wait(&ofree[qb], (uint32_t)(((n_it - 2) >> 1) & 1), p.err, kErrWaitAccEmpty)))
+          break;
+        const uint64_t dQ = sdesc_sw128(smem_u32(sQ + qb * 2 * DT_QCHUNK), 16, 1024);
         for (int t = t0; t < t1 && ok; ++t, ++g) {
-          const int s = (int)(g & 1);
-          if (!(ok = mbar_wait(&kfull[s], (uint32_t)((g >> 1) & 1), p.err, kErrWaitFull))) break;
-          if (g >= 2 && !(ok = mbar_wait(&sfree[s], (uint32_t)(((g - 2) >> 1) & 1), p.err, kErrWaitAccEmpty))) break;
+          const int ks = (int)(g % KST), sb = (int)(g & 1);
+          if (!(ok = mbar_wait(&kfull[ks], (uint32_t)((g / KST) & 1), p.err, kErrWaitFull))) break;
+          if (g >= 2 && !(ok = mbar_wait(&sfree[sb], (uint32_t)(((g - 2) >> 1) & 1), p.err, kErrWaitAccEmpty))) break;
           tc_fence_after();
+          const uint64_t dK = sdesc_sw128(smem_u32(sK + ks * KV_BYTES), 16, 1024);
 #pragma unroll
           for (int k = 0; k < D / 16; ++k) {
             const uint64_t ok_ = (uint64_t)(((k >> 2) * DT_KCHUNK + (k & 3) * 32) >> 4);
             const uint64_t oq = (uint64_t)(((k >> 2) * DT_QCHUNK + (k & 3) * 32) >> 4);
-            umma_bf16(tmem + s * 64, dK[s] + ok_, dQ + oq, idS, k > 0);
+            umma_bf16(tmem + sb * 64, dK + ok_, dQ + oq, idS, k > 0);
           }
-          umma_commit(&sfull[s]);
-          if (t == t1 - 1) umma_commit(qfree);
-          // PV of the previous tile overlaps this tile's softmax
-          if (t > t0) ok = issue_pv(g - 1, t - 1 == t0);
+          umma_commit(&sfull[sb]);
+          umma_commit(&kfree[ks]);
+          if (t == t1 - 1) umma_commit(&qfree[qb]);
+          // P V of the previous tile overlaps this tile's softmax
+          if (t > t0) ok = issue_pv(g - 1, t - 1 == t0, n_it);
         }
-        if (ok) ok = issue_pv(g - 1, t1 - 1 == t0);
+        if (ok) ok = issue_pv(g - 1, t1 - 1 == t0, n_it);
         ++n_it;
       }
     }
@@ -273,19 +292,22 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
         }
         continue;  // the MMA warp skips this item too
       }
-      // stage Q: rows = the G heads, K-major 128B-swizzled chunks; the previous item's last S^T is done
-      if (n_it > 0 && !(ok = mbar_wait(qfree, (uint32_t)((n_it - 1) & 1), p.err, kErrWaitAccFull))) break;
+      // stage Q into buffer n & 1: rows = the G heads, K-major 128B-swizzled chunks; the last S MMA of
+      // item n - 2 (the buffer's previous user) is done
+      const int qb = n_it & 1;
+      if (n_it >= 2 && !(ok = mbar_wait(&qfree[qb], (uint32_t)(((n_it - 2) >> 1) & 1), p.err, kErrWaitAccFull))) break;
       {
         const __nv_bfloat16* qrow = p.q + (long long)b * p.ldq + (long long)hk * G * D;
+        uint8_t* qbuf = sQ + qb * 2 * DT_QCHUNK;
         for (int i = tid; i < G * (D / 8); i += 128) {
           const int h = i / (D / 8), gr = i % (D / 8);
           const uint4 v = *reinterpret_cast<const uint4*>(qrow + h * D + gr * 8);
-          sts128(swz128(smem_u32(sQ + (gr >> 3) * DT_QCHUNK), h, gr & 7), v.x, v.y, v.z, v.w);
+          sts128(swz128(smem_u32(qbuf + (gr >> 3) * DT_QCHUNK), h, gr & 7), v.x, v.y, v.z, v.w);
         }
       }
       fence_proxy_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(qfull);
+      if (lane == 0) mbar_arrive(&qfull[qb]);
       // validity of this thread's key per tile: inside the row and on a valid page
       const int* trow = p.table + (long long)b * p.max_pages;
       float m_run[G], l_t[G];
@@ -342,21 +364,23 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
           }
           if (t > t0) {
             // O^T holds the PV of tile t-1 once its commit arrived; rescale this thread's row in place
-            if (!(ok = mbar_wait(&kvfree[s ^ 1], (uint32_t)(((g - 1) >> 1) & 1), p.err, kErrWaitAccFull))) break;
+            if (!(ok = mbar_wait(&vfree[(int)((g - 1) % VST)], (uint32_t)(((g - 1) / VST) & 1), p.err,
+                                 kErrWaitAccFull)))
+              break;
             tc_fence_after();
             uint32_t o[GC];
             if constexpr (GC == 8) {
-              tmem_ld8(tO + lane_off, *reinterpret_cast<uint32_t(*)[8]>(o));
+              tmem_ld8(tO(n_it) + lane_off, *reinterpret_cast<uint32_t(*)[8]>(o));
             } else {
-              tmem_ld16(tO + lane_off, *reinterpret_cast<uint32_t(*)[16]>(o));
+              tmem_ld16(tO(n_it) + lane_off, *reinterpret_cast<uint32_t(*)[16]>(o));
             }
             tmem_wait_ld();
 #pragma unroll
             for (int h = 0; h < G; ++h) o[h] = __float_as_uint(__uint_as_float(o[h]) * alpha[h]);
             if constexpr (GC == 8) {
-              tmem_st8(tO + lane_off, *reinterpret_cast<uint32_t(*)[8]>(o));
+              tmem_st8(tO(n_it) + lane_off, *reinterpret_cast<uint32_t(*)[8]>(o));
             } else {
-              tmem_st16(tO + lane_off, *reinterpret_cast<uint32_t(*)[16]>(o));
+              tmem_st16(tO(n_it) + lane_off, *reinterpret_cast<uint32_t(*)[16]>(o));
             }
             tmem_wait_st();
           }
@@ -380,15 +404,18 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
         // a key outside the row (or on a skipped page) has p = 0, but its V row holds whatever the page
         // or an earlier tile left there, possibly NaN: zero it once the V tile has landed
         if (!valid) {
-          if (!(ok = mbar_wait(&vfull[s], ph, p.err, kErrWaitFull))) break;
-          const uint32_t vb = smem_u32(sKV + s * 2 * KV_BYTES + KV_BYTES);
+          const int vs = (int)(g % VST);
+          if (!(ok = mbar_wait(&vfull[vs], (uint32_t)((g / VST) & 1), p.err, kErrWaitFull))) break;
+          const uint32_t vb = smem_u32(sV + vs * KV_BYTES);
 #pragma unroll
           for (int c = 0; c < NCH; ++c)
 #pragma unroll
             for (int q = 0; q < 8; ++q) sts128(swz128(vb + c * DT_KCHUNK, r, q), 0u, 0u, 0u, 0u);
         }
         // the P^T slot was last read by the PV of tile g-2
-        if (g >= 2 && !(ok = mbar_wait(&kvfree[s], (uint32_t)(((g - 2) >> 1) & 1), p.err, kErrWaitAccFull))) break;
+        if (g >= 2 && !(ok = mbar_wait(&vfree[(int)((g - 2) % VST)], (uint32_t)(((g - 2) / VST) & 1), p.err,
+                                       kErrWaitAccFull)))
+          break;
         const uint32_t pb = smem_u32(sP + s * DT_PSLOT);
 #pragma unroll
         for (int q = 0; q < GC / 8; ++q) sts128(swz128(pb, r, q), pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
@@ -400,18 +427,18 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
       if (!ok) break;
       // epilogue: O^T row r (head-dim index), after the last PV of the item
       const long long gl = g - 1;
-      if (!(ok = mbar_wait(&kvfree[(int)(gl & 1)], (uint32_t)((gl >> 1) & 1), p.err, kErrWaitAccFull))) break;
+      if (!(ok = mbar_wait(&vfree[(int)(gl % VST)], (uint32_t)((gl / VST) & 1), p.err, kErrWaitAccFull))) break;
       tc_fence_after();
       uint32_t o[GC];
       if constexpr (GC == 8) {
-        tmem_ld8(tO + lane_off, *reinterpret_cast<uint32_t(*)[8]>(o));
+        tmem_ld8(tO(n_it) + lane_off, *reinterpret_cast<uint32_t(*)[8]>(o));
       } else {
-        tmem_ld16(tO + lane_off, *reinterpret_cast<uint32_t(*)[16]>(o));
+        tmem_ld16(tO(n_it) + lane_off, *reinterpret_cast<uint32_t(*)[16]>(o));
       }
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(ofree);
+      if (lane == 0) mbar_arrive(&ofree[qb]);
       float* sums = sRed + 2 * 4 * 16;
 #pragma unroll
       for (int h = 0; h < G; ++h) {
@@ -515,8 +542,9 @@ void paged_decode_tc(const void* q, long long ldq, const void* kc, const void* v
   const int dev_sms = num_sms(dev);
   const int items = B * Hkv * splits;
   const int grid = std::max(1, std::min(items, dev_sms));
-  const size_t smem = 1024 + 4 * (size_t)(D / 64) * DT_KCHUNK + 2 * DT_QCHUNK + 2 * DT_PSLOT +
-                      (2 * 4 * 16 + 4 * 16) * sizeof(float) + 16 * sizeof(uint64_t);
+  const int stages = D == 128 ? DtStages<128>::K + DtStages<128>::V : DtStages<64>::K + DtStages<64>::V;
+  const size_t smem = 1024 + (size_t)stages * (D / 64) * DT_KCHUNK + 2 * 2 * DT_QCHUNK + 2 * DT_PSLOT +
+                      (2 * 4 * 16 + 4 * 16) * sizeof(float) + 32 * sizeof(uint64_t);
 #define ASTRAI_DT_CASE(DD, GG) \
   if (D == DD && G == GG) return launch_dt<DD, GG>(tk, tv, p, grid, smem, s);
   ASTRAI_DT_CASE(128, 1) ASTRAI_DT_CASE(128, 2) ASTRAI_DT_CASE(128, 4) ASTRAI_DT_CASE(128, 8) ASTRAI_DT_CASE(128, 16)

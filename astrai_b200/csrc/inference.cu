@@ -25,6 +25,7 @@
 // (temperature 0) take the argmax of the raw logits. No host
 // synchronisation, no sort.
 #include <cfloat>
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -718,6 +719,321 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(
   }
 }
 
+// ------------------------------------------------------------------ sampling, one CTA per row
+// Vocabularies up to 32768: the row stays in registers of one 1024-thread CTA (32 values per
+// thread), so every row-wide step is a block reduction and no cluster barrier is needed. The top-k
+// and top-p thresholds come from a 4096-bin histogram of the order-preserving key (its top 12 bits:
+// sign, exponent and 3 mantissa bits) instead of a threshold search: one pass counts (top-k) or sums
+// the probability mass (top-p) per bin, a suffix scan over the bins finds the bin holding the
+// threshold, and only that bin's values are gathered and resolved exactly in shared memory (rank /
+// mass of strictly larger values). A bin holding more than SMC_CAND values (massive ties) falls
+// back to bisecting the key inside the bin. Same results as sample_kernel: keep key >= the k-th
+// largest key (ties kept), then keep a value iff the mass of strictly larger values <= top_p * Z,
+// then the frequency penalty, then an inverse-CDF draw in a fixed order.
+constexpr int SMC_THREADS = 1024;
+constexpr int SMC_PER = 32;
+constexpr int SMC_MAXV = SMC_THREADS * SMC_PER;  // 32768
+constexpr int SMC_BINS = 4096;
+constexpr int SMC_CAND = 2048;
+
+__device__ __forceinline__ float smc_block_max(float v, float* red) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = warp_max(red[lane]);
+    if (lane == 0) red[32] = v;
+  }
+  __syncthreads();
+  return red[32];
+}
+__device__ __forceinline__ float smc_block_min(float v, float* red) { return -smc_block_max(-v, red); }
+__device__ __forceinline__ float smc_block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = warp_sum(red[lane]);
+    if (lane == 0) red[32] = v;
+  }
+  __syncthreads();
+  return red[32];
+}
+// Exclusive prefix over threads (thread order) of v; also returns the block total.
+__device__ __forceinline__ float smc_block_exclusive(float v, float* red, float& total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  float incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  __syncthreads();
+  if (lane == 31) red[w] = incl;
+  __syncthreads();
+  if (w == 0) {
+    float t = red[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += y;
+    }
+    red[lane] = t;  // inclusive warp totals
+  }
+  __syncthreads();
+  total = red[31];
+  return incl - v + (w > 0 ? red[w - 1] : 0.f);
+}
+
+// Bin b* (scanning from the top) where the running total of `bins` first exceeds `target`
+// (strictly, or reaches it when `reach`); returns the total of the bins above b* in `above`. Four
+// bins per thread; -1 when the total never gets there.
+__device__ __forceinline__ int smc_find_bin(const float* bins, float target, bool reach, float* red, int* s_bin,
+                                           float* s_above, float& above) {
+  const int t = threadIdx.x;
+  float own = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) own += bins[4 * t + i];
+  // the total of bins above this thread's four = (block total) - (inclusive prefix up to this thread)
+  float total;
+  const float excl = smc_block_exclusive(own, red, total);
+  float cum = total - excl - own;
+  if (t == 0) *s_bin = -1;
+  __syncthreads();
+#pragma unroll
+  for (int i = 3; i >= 0; --i) {
+    const float h = bins[4 * t + i];
+    const bool hit = reach ? (cum < target && cum + h >= target) : (cum <= target && cum + h > target);
+    if (hit && h > 0.f) {
+      *s_bin = 4 * t + i;
+      *s_above = cum;
+    }
+    cum += h;
+  }
+  __syncthreads();
+  above = *s_above;
+  return *s_bin;
+}
+
+__global__ void __launch_bounds__(SMC_THREADS, 1) sample_cta_kernel(
+    const void* __restrict__ logits, int logits_f32, long long ld, int V, const float* __restrict__ temperature,
+    const int* __restrict__ top_k, const float* __restrict__ top_p, const float* __restrict__ penalty,
+    const long long* __restrict__ hist, int hist_len, long long ld_hist,
+    const unsigned long long* __restrict__ rng, long long* __restrict__ out_tok, float* __restrict__ out_lp) {
+  __shared__ float bins[SMC_BINS];
+  __shared__ float cand[SMC_CAND];
+  __shared__ float red[40];
+  __shared__ int s_cnt, s_bin;
+  __shared__ float s_above;
+  const int row = blockIdx.x, t = threadIdx.x;
+  float x[SMC_PER];
+  float raw_max = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < SMC_PER; ++j) {
+    const int i = t + j * SMC_THREADS;
+    float v = -INFINITY;
+    if (i < V) {
+      v = logits_f32 ? reinterpret_cast<const float*>(logits)[(long long)row * ld + i]
+                     : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(logits)[(long long)row * ld + i]);
+      if (v != v) v = -INFINITY;  // NaN never wins
+    }
+    x[j] = v;
+    raw_max = fmaxf(raw_max, v);
+  }
+  const float temp = temperature ? temperature[row] : 1.f;
+  const float gmax = smc_block_max(raw_max, red);
+  if (temp == 0.f) {
+    float sum = 0.f, best = 3.0e38f;
+#pragma unroll
+    for (int j = 0; j < SMC_PER; ++j) {
+      sum += (x[j] == -INFINITY) ? 0.f : __expf(x[j] - gmax);
+      if (x[j] == gmax) best = fminf(best, (float)(t + j * SMC_THREADS));
+    }
+    const float Z = smc_block_sum(sum, red);
+    const float bi = smc_block_min(best, red);
+    if (t == 0) {
+      out_tok[row] = bi > 1.0e38f ? 0 : (long long)bi;
+      if (out_lp) out_lp[row] = gmax == -INFINITY ? -INFINITY : -__logf(Z);
+    }
+    return;
+  }
+  const float inv_t = 1.f / fmaxf(temp, 1e-8f);
+#pragma unroll
+  for (int j = 0; j < SMC_PER; ++j) x[j] *= inv_t;
+  const float mx = gmax * inv_t;
+  // ---- top-k
+  const int k = top_k ? top_k[row] : 0;
+  uint32_t thr = 0;  // keep fkey >= thr
+  if (k > 0 && k < V) {
+    for (int b = t; b < SMC_BINS; b += SMC_THREADS) bins[b] = 0.f;
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < SMC_PER; ++j)
+      if (x[j] != -INFINITY) atomicAdd(&bins[fkey(x[j]) >> 20], 1.f);
+    __syncthreads();
+    float above;
+    const int bstar = smc_find_bin(bins, (float)k, true, red, &s_bin, &s_above, above);
+    if (bstar >= 0) {
+      const int need = k - (int)above;  // values of bin b* to keep (its `need` largest, ties kept)
+      const int nb = (int)bins[bstar];
+      if (nb <= SMC_CAND) {
+        if (t == 0) s_cnt = 0;
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < SMC_PER; ++j)
+          if (x[j] != -INFINITY && (int)(fkey(x[j]) >> 20) == bstar) cand[atomicAdd(&s_cnt, 1)] = x[j];
+        __syncthreads();
+        // the smallest value with fewer than `need` strictly larger values in the bin
+        float kth = INFINITY;
+        for (int i = t; i < nb; i += SMC_THREADS) {
+          const float c = cand[i];
+          int greater = 0;
+          for (int j = 0; j < nb; ++j) greater += cand[j] > c;
+          if (greater < need) kth = fminf(kth, c);
+        }
+        thr = fkey(smc_block_min(kth, red));
+      } else {
+        // massive ties: bisect the key inside the bin (count of keys >= mid must stay >= k)
+        uint32_t lo = (uint32_t)bstar << 20, hi = lo | 0xFFFFFu;
+        while (lo < hi) {
+          const uint32_t mid = lo + (hi - lo + 1) / 2;
+          float c = 0.f;
+#pragma unroll
+          for (int j = 0; j < SMC_PER; ++j) c += (x[j] != -INFINITY && fkey(x[j]) >= mid) ? 1.f : 0.f;
+          if (smc_block_sum(c, red) >= (float)k) lo = mid; else hi = mid - 1;
+        }
+        thr = lo;
+      }
+#pragma unroll
+      for (int j = 0; j < SMC_PER; ++j)
+        if (x[j] != -INFINITY && fkey(x[j]) < thr) x[j] = -INFINITY;
+    }
+  }
+  // ---- top-p: keep a value iff the mass of strictly larger values <= top_p * Z
+  const float pp = top_p ? top_p[row] : 1.f;
+  if (pp < 1.f) {
+    __syncthreads();
+    for (int b = t; b < SMC_BINS; b += SMC_THREADS) bins[b] = 0.f;
+    __syncthreads();
+    float zs = 0.f;
+#pragma unroll
+    for (int j = 0; j < SMC_PER; ++j) {
+      if (x[j] == -INFINITY) continue;
+      const float e = __expf(x[j] - mx);
+      zs += e;
+      atomicAdd(&bins[fkey(x[j]) >> 20], e);
+    }
+    const float Z = smc_block_sum(zs, red);
+    const float target = pp * Z;
+    float above;
+    const int bstar = smc_find_bin(bins, target, false, red, &s_bin, &s_above, above);
+    if (bstar >= 0) {
+      __syncthreads();
+      if (t == 0) s_cnt = 0;
+      __syncthreads();
+      // the values of bin b*: keep those whose strictly larger mass (bins above + larger in the bin) fits
+#pragma unroll
+      for (int j = 0; j < SMC_PER; ++j)
+        if (x[j] != -INFINITY && (int)(fkey(x[j]) >> 20) == bstar) {
+          const int slot = atomicAdd(&s_cnt, 1);
+          if (slot < SMC_CAND) cand[slot] = x[j];
+        }
+      __syncthreads();
+      const int nb = s_cnt;
+      float kept_min = INFINITY;
+      if (nb <= SMC_CAND) {
+        for (int i = t; i < nb; i += SMC_THREADS) {
+          const float c = cand[i];
+          float greater = above;
+          for (int j = 0; j < nb; ++j)
+            if (cand[j] > c) greater += __expf(cand[j] - mx);
+          if (greater <= target) kept_min = fminf(kept_min, c);
+        }
+        kept_min = smc_block_min(kept_min, red);
+      } else {
+        // bisect the key inside the bin: the smallest key whose strictly larger mass fits
+        uint32_t lo = (uint32_t)bstar << 20, hi = lo | 0xFFFFFu;
+        while (lo < hi) {
+          const uint32_t mid = lo + (hi - lo) / 2;
+          float m = 0.f;
+#pragma unroll
+          for (int j = 0; j < SMC_PER; ++j)
+            if (x[j] != -INFINITY && fkey(x[j]) > mid) m += __expf(x[j] - mx);
+          if (smc_block_sum(m, red) <= target) hi = mid; else lo = mid + 1;
+        }
+        kept_min = -INFINITY;
+        thr = lo;
+#pragma unroll
+        for (int j = 0; j < SMC_PER; ++j)
+          if (x[j] != -INFINITY && fkey(x[j]) < thr) x[j] = -INFINITY;
+      }
+      if (kept_min != -INFINITY) {
+        // no value of bin b* fits only when the bins above already hold the mass: keep from b* + 1 up
+        const uint32_t cut = kept_min == INFINITY ? ((uint32_t)(bstar + 1) << 20) : fkey(kept_min);
+#pragma unroll
+        for (int j = 0; j < SMC_PER; ++j)
+          if (x[j] != -INFINITY && fkey(x[j]) < cut) x[j] = -INFINITY;
+      }
+    }
+  }
+  // ---- frequency penalty: subtract penalty * count(token in the history window)
+  const float pen = penalty ? penalty[row] : 0.f;
+  if (pen != 0.f && hist) {
+    for (int h = 0; h < hist_len; ++h) {
+      const long long id = hist[(long long)row * ld_hist + h];
+      if (id < 0 || id >= V || (int)(id % SMC_THREADS) != t) continue;
+      const int jj = (int)(id / SMC_THREADS);
+#pragma unroll
+      for (int j = 0; j < SMC_PER; ++j)
+        if (j == jj && x[j] != -INFINITY) x[j] -= pen;
+    }
+  }
+  // ---- draw from softmax(x) by inverse CDF in (thread, slot) order
+  float m2 = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < SMC_PER; ++j) m2 = fmaxf(m2, x[j]);
+  m2 = smc_block_max(m2, red);
+  float tsum = 0.f;
+#pragma unroll
+  for (int j = 0; j < SMC_PER; ++j) tsum += (x[j] == -INFINITY) ? 0.f : __expf(x[j] - m2);
+  float Z;
+  const float before = smc_block_exclusive(tsum, red, Z);
+  const float last_owner = smc_block_max(tsum > 0.f ? (float)t : -1.f, red);
+  const float u = uniform_from(rng[0], rng[1], (unsigned long long)row) * Z;
+  const bool is_last = (float)t == last_owner;
+  if (tsum > 0.f && u >= before && (u < before + tsum || is_last)) {
+    float c = before;
+    int pick = -1, last_nz = -1;
+    float xv = -INFINITY, xlast = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < SMC_PER; ++j) {
+      const float e = (x[j] == -INFINITY) ? 0.f : __expf(x[j] - m2);
+      if (e > 0.f) {
+        last_nz = j;
+        xlast = x[j];
+      }
+      if (pick < 0 && e > 0.f && u < c + e) {
+        pick = j;
+        xv = x[j];
+      }
+      c += e;
+    }
+    if (pick < 0) {
+      pick = last_nz;
+      xv = xlast;
+    }
+    out_tok[row] = t + pick * SMC_THREADS;
+    if (out_lp) out_lp[row] = (xv - m2) - __logf(Z);
+  } else if (last_owner < 0.f && t == 0) {
+    out_tok[row] = 0;  // every logit was -inf / NaN
+    if (out_lp) out_lp[row] = -INFINITY;
+  }
+}
+
 }  // namespace astrai
 
 namespace astrai_host {
@@ -806,10 +1122,25 @@ int decode_splits(int B, int Hkv, int max_len, int sms) {
   return std::max(1, std::min(want, std::min(max_splits, 32)));
 }
 
+// ASTRAI_SAMPLE_CTA=0 keeps every vocabulary on the cluster kernel (for comparisons)
+static bool sample_cta_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("ASTRAI_SAMPLE_CTA");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 void sample_tokens(const void* logits, int f32, long long ld, int rows, int V, const float* temperature,
                    const int* top_k, const float* top_p, const float* penalty, const long long* hist, int hist_len,
                    long long ld_hist, const unsigned long long* rng, long long* out_tok, float* out_lp,
                    cudaStream_t s) {
+  if (V <= SMC_MAXV && sample_cta_enabled()) {
+    (astrai::note_launch(), sample_cta_kernel<<<rows, SMC_THREADS, 0, s>>>(logits, f32, ld, V, temperature, top_k, top_p,
+                                                                           penalty, hist, hist_len, ld_hist, rng,
+                                                                           out_tok, out_lp));
+    return;
+  }
   const int cs = (V + SMP_CHUNK - 1) / SMP_CHUNK;
   if (cs > SMP_MAX_CLUSTER) throw std::runtime_error("sample: vocabulary larger than 262144 is not supported");
   cudaLaunchConfig_t cfg = {};

@@ -151,7 +151,9 @@ class DeviceRNG:
     def __init__(self, device, seed: Optional[int] = None):
         if seed is None:
             seed = int(torch.randint(0, 2**62, (1,)).item())
-        self.state = torch.tensor([seed, 0], dtype=torch.int64, device=device)
+        # a normal tensor even when first made under inference_mode (a later advance outside it is legal)
+        with torch.inference_mode(False):
+            self.state = torch.tensor([seed, 0], dtype=torch.int64, device=device)
 
     def advance(self) -> None:
         self.state[1:].add_(1)

@@ -591,6 +591,13 @@ def bench_decode():
                 fn()
         graph = time_fn(g.replay, warmup=3, iters=10) / 20
         nbytes = 2 * B * Hkv * L * D * 2
+        if B == 32 and L == 4096:  # the split count against the default heuristic
+            sweep = {}
+            for sp in (1, 2, 3, 4, 6, 8, 16):
+                ws2 = torch.empty(B * Hq * sp * (D + 2), device="cuda", dtype=torch.float32)
+                sweep[sp] = round(time_flushed(lambda: C.paged_decode(q, kc, vc, table, lens, out, Hq, D ** -0.5, sp,
+                                                                      ws2)) * 1e3, 2)
+            print(json.dumps({"kernel": "paged_decode_split_sweep", "B": B, "kv_len": L, "us_by_splits": sweep}))
         print(json.dumps({"kernel": "paged_decode", "impl": "tc" if os.environ.get("ASTRAI_DECODE_TC", "1") != "0"
                           else "cuda_core", "B": B, "Hq": Hq, "Hkv": Hkv, "kv_len": L, "D": D, "page": page,
                           "splits": splits, "us": round(ms * 1e3, 2), "us_warm": round(warm * 1e3, 2),
