@@ -25,14 +25,26 @@ def tiny_cfg(**kw):
     return AutoRegressiveLMConfig(**base)
 
 
-@pytest.mark.parametrize("tied", [False, True])
-def test_lm_forward_backward_matches_cpu(tied):
+VARIANTS = {
+    "gqa": {},
+    "tied": dict(tie_word_embeddings=True),
+    # the attention options of the reference's model config, on the kernel path (head_dim 128)
+    "qk_norm_gated": dict(use_qk_norm=True, use_gated_attention=True),
+    "mla": dict(attn_type="mla", num_attention_heads=2, num_key_value_heads=2, kv_lora_rank=64,
+                qk_nope_head_dim=96, qk_rope_head_dim=32),
+    "mla_qk_norm_gated": dict(attn_type="mla", num_attention_heads=2, num_key_value_heads=1, kv_lora_rank=64,
+                              qk_nope_head_dim=96, qk_rope_head_dim=32, use_qk_norm=True, use_gated_attention=True),
+}
+
+
+@pytest.mark.parametrize("variant", sorted(VARIANTS))
+def test_lm_forward_backward_matches_cpu(variant):
     from astrai_b200.models import AutoRegressiveLM
     from astrai_b200.ops._ext import native
     from astrai_b200.ops.loss import cross_entropy
 
     torch.manual_seed(0)
-    cpu = AutoRegressiveLM(tiny_cfg(tie_word_embeddings=tied)).float()
+    cpu = AutoRegressiveLM(tiny_cfg(**VARIANTS[variant])).float()
     gpu = copy.deepcopy(cpu).cuda().to(torch.bfloat16)
     # compare against the bf16-rounded weights so only compute precision differs
     cpu.load_state_dict({k: v.to(torch.bfloat16).float() for k, v in cpu.state_dict().items()})
