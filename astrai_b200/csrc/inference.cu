@@ -915,7 +915,40 @@ __global__ void __launch_bounds__(SMC_THREADS, 1) sample_cta_kernel(
   }
   // ---- top-p: keep a value iff the mass of strictly larger values <= top_p * Z
   const float pp = top_p ? top_p[row] : 1.f;
-  if (pp < 1.f) {
+  bool topp_done = false;
+  if (pp < 1.f && thr != 0u) {
+    // after top-k only the k largest (plus ties) survive: decide on them in shared memory
+    __syncthreads();
+    if (t == 0) s_cnt = 0;
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < SMC_PER; ++j)
+      if (x[j] != -INFINITY) {
+        const int slot = atomicAdd(&s_cnt, 1);
+        if (slot < SMC_CAND) cand[slot] = x[j];
+      }
+    __syncthreads();
+    const int n = s_cnt;
+    if (n <= SMC_CAND) {
+      float e = 0.f;
+      for (int i = t; i < n; i += SMC_THREADS) e += __expf(cand[i] - mx);
+      const float target = pp * smc_block_sum(e, red);
+      float kept_min = INFINITY;
+      for (int i = t; i < n; i += SMC_THREADS) {
+        const float c = cand[i];
+        float greater = 0.f;
+        for (int j = 0; j < n; ++j)
+          if (cand[j] > c) greater += __expf(cand[j] - mx);
+        if (greater <= target) kept_min = fminf(kept_min, c);
+      }
+      kept_min = smc_block_min(kept_min, red);
+#pragma unroll
+      for (int j = 0; j < SMC_PER; ++j)
+        if (x[j] < kept_min) x[j] = -INFINITY;
+      topp_done = true;
+    }
+  }
+  if (pp < 1.f && !topp_done) {
     __syncthreads();
     for (int b = t; b < SMC_BINS; b += SMC_THREADS) bins[b] = 0.f;
     __syncthreads();
