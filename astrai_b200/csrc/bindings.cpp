@@ -30,7 +30,7 @@ struct GatherArgs {
 void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int N, int K, int batch, int a_mn,
                long long lda, long long strideA, int b_mn, long long ldb, long long strideB, long long ldd,
                long long strideD, int out_f32, long long ldc, long long strideC, float alpha, float beta,
-               int force_bn, cudaStream_t stream, const GatherArgs* gather = nullptr);
+               int force_bn, cudaStream_t stream, const GatherArgs* gather = nullptr, int sym = 0);
 void gemm_profile_set(unsigned long long* counters);
 void gemm_plan(int M, int N, int K, int batch, int* out);
 void gemm_rope_bf16(const void* A, long long lda, const void* B, long long ldb, void* D, long long ldd, int M, int N,
@@ -185,7 +185,7 @@ void gemm_rope(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const 
 //   a: [.., M, K] when a_mn == 0, [.., K, M] when a_mn == 1
 //   b: [.., N, K] when b_mn == 0, [.., K, N] when b_mn == 1
 void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& d, const c10::optional<at::Tensor>& c, int64_t a_mn,
-          int64_t b_mn, double alpha, double beta, int64_t force_bn) {
+          int64_t b_mn, double alpha, double beta, int64_t force_bn, bool sym) {
   check_bf16(a, "a");
   check_bf16(b, "b");
   check_cuda(d, "d");
@@ -217,7 +217,7 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& d, const c10::op
   astrai_host::gemm_bf16(a.data_ptr(), b.data_ptr(), d.data_ptr(), cptr, (int)M, (int)N, (int)K, batch, (int)a_mn,
                          a.stride(ar), batched ? a.stride(0) : 0, (int)b_mn, b.stride(ar), batched ? b.stride(0) : 0,
                          d.stride(ar), batched ? d.stride(0) : 0, d.scalar_type() == at::kFloat ? 1 : 0, ldc, sc,
-                         (float)alpha, (float)beta, (int)force_bn, stream());
+                         (float)alpha, (float)beta, (int)force_bn, stream(), nullptr, sym ? 1 : 0);
 }
 
 // GEMM fused with an all-gather over NVLink peer memory: d is this rank's column block of the
@@ -501,7 +501,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("skinny_gemm", &skinny_gemm, py::arg("x"), py::arg("w"), py::arg("y"), py::arg("residual") = py::none());
   m.def("gemm", &gemm, "bf16 tcgen05 GEMM", py::arg("a"), py::arg("b"), py::arg("d"), py::arg("c") = py::none(),
         py::arg("a_mn") = 0, py::arg("b_mn") = 0, py::arg("alpha") = 1.0, py::arg("beta") = 0.0,
-        py::arg("force_bn") = 0);
+        py::arg("force_bn") = 0, py::arg("sym") = false);
   m.def("gemm_gather", &gemm_gather, "bf16 GEMM whose epilogue also stores into every peer's copy (fused all-gather)",
         py::arg("a"), py::arg("b"), py::arg("d"), py::arg("peer_deltas"), py::arg("flag_addr"), py::arg("done_addr"),
         py::arg("epoch"), py::arg("a_mn") = 0, py::arg("b_mn") = 0, py::arg("scatter_rpo") = 0,

@@ -103,6 +103,10 @@ struct GemmParams {
   int scatter_rpo, scatter_rank;
   long long scatter_recv_off;  // bytes from D to the receive slots
   long long rank_delta[kMaxGatherPeers + 1];
+  // Symmetric output (sym != 0; M == N, D known to equal D^T, e.g. X X^T or A A with A symmetric):
+  // tiles lying entirely below the diagonal (every column < every row; tiles of sym_bm x sym_bn) are
+  // skipped, and sym_mirror_kernel copies the transpose of the upper triangle into them afterwards.
+  int sym, sym_bm, sym_bn;
 };
 
 // Fused all-gather: after the epilogue warps stored tile (b, mb, nb) into the local D, copy it from
@@ -195,7 +199,7 @@ struct WorkIter {
   }
   __device__ __forceinline__ bool next(const GemmParams& p, int num_tiles, int kblk_full, WorkItem& w) {
     const int limit = p.sk_units > 0 ? p.dp_tiles : num_tiles;
-    if (p.group_tile)
+    if (p.group_tile || p.sym)
       while (t < limit && tile_skipped(p, t)) t += cnt;
     if (t < limit) {
       w = {t, 0, kblk_full, -1, 0, true, false};
@@ -312,7 +316,30 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
 __device__ __forceinline__ bool tile_skipped(const GemmParams& p, int tile) {
   int b, mb, nb;
   tile_coords(tile, p.tiles_m, p.tiles_n, b, mb, nb);
+  if (p.sym) return (long long)(nb + 1) * p.sym_bn <= (long long)mb * p.sym_bm;
   return p.group_tile[mb] < 0;
+}
+
+// Lower triangle of a symmetric output from its upper triangle: one 32 x 32 block pair per CTA
+// (block (bi, bj), bi >= bj, is written from the transpose of block (bj, bi)).
+template <typename T>
+__global__ void sym_mirror_kernel(T* __restrict__ D, int M, long long ldd, long long strideD) {
+  __shared__ T tile[32][33];
+  const int bi = blockIdx.x, bj = blockIdx.y;
+  if (bj > bi) return;
+  T* d = D + (long long)blockIdx.z * strideD;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  // read block (bj, bi) (rows bj*32.., cols bi*32..): upper side
+  for (int r = ty; r < 32; r += blockDim.y) {
+    const int row = bj * 32 + r, col = bi * 32 + tx;
+    if (row < M && col < M) tile[r][tx] = d[(long long)row * ldd + col];
+  }
+  __syncthreads();
+  // write block (bi, bj) = transpose; on the diagonal only below it
+  for (int r = ty; r < 32; r += blockDim.y) {
+    const int row = bi * 32 + r, col = bj * 32 + tx;
+    if (row < M && col < M && row > col) d[(long long)row * ldd + col] = tile[tx][r];
+  }
 }
 
 template <int BM, int BN, int A_MN, int B_MN, int OUT_F32>
@@ -1672,11 +1699,22 @@ void gemm_plan(int M, int N, int K, int batch, int* out) {
   out[6] = use_streamk_pair(ptiles, (K + 63) / 64, pair_clusters(dev)) ? 1 : 0;
 }
 
+static void sym_mirror(void* D, int out_f32, int M, long long ldd, long long strideD, int batch, cudaStream_t s) {
+  const int nb = (M + 31) / 32;
+  const dim3 grid(nb, nb, batch), block(32, 8);
+  if (out_f32)
+    (astrai::note_launch(), astrai::sym_mirror_kernel<float><<<grid, block, 0, s>>>(static_cast<float*>(D), M, ldd, strideD));
+  else
+    (astrai::note_launch(), astrai::sym_mirror_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(static_cast<__nv_bfloat16*>(D), M,
+                                                                                    ldd, strideD));
+}
+
 void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int N, int K, int batch, int a_mn,
                long long lda, long long strideA, int b_mn, long long ldb, long long strideB, long long ldd,
                long long strideD, int out_f32, long long ldc, long long strideC, float alpha, float beta,
-               int force_bn, cudaStream_t stream, const GatherArgs* gather) {
+               int force_bn, cudaStream_t stream, const GatherArgs* gather, int sym) {
   if (M <= 0 || N <= 0 || K <= 0 || batch <= 0) throw std::runtime_error("astrai gemm: empty problem");
+  if (sym && (M != N || gather != nullptr)) throw std::runtime_error("astrai gemm: a symmetric output needs M == N");
   int dev = 0;
   cudaGetDevice(&dev);
   const int sms = num_sms(dev);
@@ -1761,18 +1799,28 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
   p.scatter_rpo = 0;
   p.scatter_rank = 0;
   p.scatter_recv_off = 0;
+  p.sym = 0;
+  p.sym_bm = 1;
+  p.sym_bn = 1;
   const int tiles = batch * p.tiles_m * p.tiles_n;
+  if (sym) {
+    p.sym = 1;
+    p.sym_bm = BM;
+    p.sym_bn = BN;
+  }
   if (pair) {
     const int pmax = pair_clusters(dev);
     int pairs = std::min(tiles, pmax);
-    const bool split = force_bn == 1026 || (force_bn != 1024 && pair_streamk_on() && streamk_on());
+    const bool split = !sym && (force_bn == 1026 || (force_bn != 1024 && pair_streamk_on() && streamk_on()));
     if (split && use_streamk_pair(tiles, p.k_blocks, pmax) &&
         sk_buffers(dev, stream, sms, &p.sk_ws, &p.sk_flags)) {
       p.dp_tiles = tiles / pmax * pmax;
       p.sk_units = (long long)(tiles - p.dp_tiles) * p.k_blocks;
       pairs = pmax;
     }
-    return dispatch_pair<256>(a_mn, b_mn, out_f32, ta, tb, p, pairs, stream);
+    dispatch_pair<256>(a_mn, b_mn, out_f32, ta, tb, p, pairs, stream);
+    if (sym) sym_mirror(D, out_f32, M, ldd, strideD, batch, stream);
+    return;
   }
   int grid = std::min(tiles, sms);
   if (gather != nullptr) {
@@ -1787,7 +1835,7 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
     p.scatter_rank = gather->scatter_rank;
     p.scatter_recv_off = gather->scatter_recv_off;
     for (int q = 0; q <= astrai::kMaxGatherPeers; ++q) p.rank_delta[q] = gather->rank_delta[q];
-  } else if (use_streamk(tiles, p.k_blocks, sms) && sk_buffers(dev, stream, sms, &p.sk_ws, &p.sk_flags)) {
+  } else if (!sym && use_streamk(tiles, p.k_blocks, sms) && sk_buffers(dev, stream, sms, &p.sk_ws, &p.sk_flags)) {
     p.dp_tiles = tiles / sms * sms;
     p.sk_units = (long long)(tiles - p.dp_tiles) * p.k_blocks;
     grid = sms;
@@ -1798,6 +1846,7 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
     dispatch_majors<128, 256>(a_mn, b_mn, out_f32, ta, tb, p, grid, stream);
   else
     dispatch_majors<128, 128>(a_mn, b_mn, out_f32, ta, tb, p, grid, stream);
+  if (sym) sym_mirror(D, out_f32, M, ldd, strideD, batch, stream);
 }
 
 
@@ -1883,6 +1932,9 @@ void gemm_grouped_bf16(int mode, const void* A, const void* B, void* D, const vo
   p.scatter_rpo = 0;
   p.scatter_rank = 0;
   p.scatter_recv_off = 0;
+  p.sym = 0;
+  p.sym_bm = 1;
+  p.sym_bn = 1;
   const int tiles = p.batch * p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, sms);
   if (BN == 256)
@@ -1975,6 +2027,9 @@ void gemm_swiglu_bf16(int mode, const void* A, long long lda, const void* B, lon
   p.scatter_rpo = 0;
   p.scatter_rank = 0;
   p.scatter_recv_off = 0;
+  p.sym = 0;
+  p.sym_bm = 1;
+  p.sym_bn = 1;
   const int tiles = p.tiles_m * p.tiles_n;
   if (pair)
     return dispatch_pair<256>(0, mode == 1 ? 0 : b_mn, 0, ta, tb, p, std::min(tiles, pair_clusters(dev)), stream);
@@ -2053,6 +2108,9 @@ void gemm_rope_bf16(const void* A, long long lda, const void* B, long long ldb, 
   p.scatter_rpo = 0;
   p.scatter_rank = 0;
   p.scatter_recv_off = 0;
+  p.sym = 0;
+  p.sym_bm = 1;
+  p.sym_bn = 1;
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, sms);
   if (BN == 256)

@@ -221,6 +221,11 @@ def newton_schulz_reference(g: torch.Tensor, steps: int = 5, eps: float = 1e-7, 
     return x.T if tall else x
 
 
+# X X^T and c A A + b A (A symmetric) are symmetric: compute their upper triangle only
+# (ASTRAI_NS_SYM=0 computes every tile)
+NS_SYM = os.environ.get("ASTRAI_NS_SYM", "1") == "1"
+
+
 def newton_schulz_batched(X: torch.Tensor, steps: int = 5, coeffs=NS_COEFFS, work=None) -> torch.Tensor:
     """In-GPU batched NS on X [B, m, n] (m <= n, already normalised). Returns the result buffer."""
     C = native()
@@ -232,9 +237,10 @@ def newton_schulz_batched(X: torch.Tensor, steps: int = 5, coeffs=NS_COEFFS, wor
     Y, A, Bm = work
     cur, nxt = X, Y
     for _ in range(steps):
-        C.gemm(cur, cur, A, None, 0, 0, 1.0, 0.0, 0)            # A = X X^T
-        C.gemm(A, A, Bm, A, 0, 0, c, b, 0)                      # Bm = c A A + b A
-        C.gemm(Bm, cur, nxt, cur, 0, 1, 1.0, a, 0)              # X' = Bm X + a X
+        # A and Bm are symmetric: only the tiles on or above the diagonal are computed, then mirrored
+        C.gemm(cur, cur, A, None, 0, 0, 1.0, 0.0, 0, NS_SYM)        # A = X X^T
+        C.gemm(A, A, Bm, A, 0, 0, c, b, 0, NS_SYM)                  # Bm = c A A + b A
+        C.gemm(Bm, cur, nxt, cur, 0, 1, 1.0, a, 0)                  # X' = Bm X + a X
         cur, nxt = nxt, cur
     return cur
 

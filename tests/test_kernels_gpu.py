@@ -107,6 +107,31 @@ def test_gemm_cta_pair(a_mn, b_mn, M, N, K, batch):
     assert native().read_error() == 0
 
 
+@pytest.mark.parametrize("force_bn", [0, 1024, 256])
+@pytest.mark.parametrize("m,n,batch", [(256, 512, 1), (300, 200, 2), (2048, 1536, 3)])
+def test_gemm_symmetric_output(force_bn, m, n, batch):
+    """sym=True (Newton-Schulz's X X^T and c A A + b A): tiles below the diagonal are skipped and the
+    lower triangle is the mirror of the upper one; the result equals the full product."""
+    from astrai_b200.ops._ext import native
+    from astrai_b200.ops.gemm import gemm_reference
+
+    C = native()
+    torch.manual_seed(m + n)
+    x = (torch.randn(batch, m, n, device="cuda") / n ** 0.5).to(torch.bfloat16)
+    a = torch.full((batch, m, m), float("nan"), device="cuda", dtype=torch.bfloat16)  # every entry written
+    C.gemm(x, x, a, None, 0, 0, 1.0, 0.0, force_bn, True)
+    ref = gemm_reference(x, x)
+    assert torch.isfinite(a.float()).all()
+    assert rel_err(a, ref) < 1e-2
+    assert torch.equal(a, a.transpose(1, 2))
+    bm = torch.full_like(a, float("nan"))
+    C.gemm(a, a, bm, a, 0, 0, -4.775, 2.0315, force_bn, True)
+    ref2 = gemm_reference(a, a, c=a, alpha=-4.775, beta=2.0315)
+    assert torch.isfinite(bm.float()).all()
+    assert rel_err(bm, ref2) < 1e-2
+    assert C.read_error() == 0
+
+
 def test_gemm_batched():
     from astrai_b200.ops.gemm import gemm, gemm_reference
 
