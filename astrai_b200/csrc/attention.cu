@@ -421,9 +421,9 @@ constexpr int FB_QT = 64 * 64 * 2;  // one 64-row x 64-col swizzled chunk (8 KB)
 // tile earlier than a 2-deep ring allows (a slot frees only when the gradient MMAs of its tile finish,
 // which follow that tile's softmax). P^T stays in TMEM (the dP^T columns of its buffer) as the A
 // operand of the dV MMA; dS^T, needed as an operand in shared memory by the dK and dQ MMAs, has two
-// slots, so the softmax of tile t only waits for the MMAs of tile t-2. The kernel is bound by shared-
-// memory bandwidth (the N = 64 MMAs read 6 KB of operands per 32 tensor cycles): keeping P^T out of
-// shared memory removes its 16 KB write and the dV MMA's 16 KB of A reads per tile. Total: 227 KB.
+// slots, so the softmax of tile t only waits for the MMAs of tile t-2 (keeping P^T out of shared
+// memory removes its 16 KB write and the dV MMA's 16 KB of A reads per tile; the 128 x 64 x 16 MMAs
+// are limited by their instruction rate, ~69 cycles each, more than by operand bandwidth). 227 KB.
 constexpr int FB_QD = 3;
 constexpr int FB_DQ_BYTES = 64 * 128 * 4;  // fp32 dQ staging tile [64 q][128 d]
 constexpr int FA_BWD_SMEM =
