@@ -636,6 +636,28 @@ def bench_prefill():
                           "peak_src": src}))
 
 
+def bench_ns():
+    """Muon's batched Newton-Schulz chain (5 steps) on the 1.1B model's matrix groups (24 of each),
+    with the symmetric products computed on their upper triangle only and in full."""
+    import astrai_b200.optim.fused as F
+
+    _, tf, src = peaks()
+    for m, n in ((2048, 11264), (2048, 5632), (2048, 3072), (2048, 2048)):
+        X = (torch.randn(24, m, n, device="cuda") / (m * n) ** 0.5).to(torch.bfloat16)
+        work = (torch.empty_like(X), torch.empty(24, m, m, device="cuda", dtype=torch.bfloat16),
+                torch.empty(24, m, m, device="cuda", dtype=torch.bfloat16))
+        res = {}
+        for sym in (True, False):
+            F.NS_SYM = sym
+            res["sym" if sym else "full"] = round(time_fn(lambda: F.newton_schulz_batched(X, 5, work=work),
+                                                          warmup=2, iters=5), 3)
+        F.NS_SYM = True
+        flops = 24 * 5 * (4.0 * m * m * n + 2.0 * m ** 3)
+        print(json.dumps({"kernel": "newton_schulz_batched", "batch": 24, "m": m, "n": n, "ms_sym": res["sym"],
+                          "ms_full": res["full"], "tflops_full": round(flops / res["full"] / 1e9, 1),
+                          "peak_src": src}))
+
+
 def bench_norm(rows: int = 8192, D: int = 2048):
     """RMSNorm forward, backward and the fork backward (residual-branch gradient added) at the 1.1B
     step's shape; bytes are the algorithmic reads + writes (bf16 rows, fp32 rstd)."""
@@ -688,6 +710,8 @@ def main(argv=None):
         bench_decode()
     if which in ("prefill", "all"):
         bench_prefill()
+    if which in ("ns", "all"):
+        bench_ns()
     if which in ("gemm", "all"):
         bench_gemm(args[1] if which == "gemm" and len(args) > 1 else None)
     if which in ("norm", "all"):
