@@ -638,7 +638,7 @@ def bench_prefill():
 
 def bench_ns():
     """Muon's batched Newton-Schulz chain (5 steps) on the 1.1B model's matrix groups (24 of each),
-    with the symmetric products computed on their upper triangle only and in full."""
+    with the symmetric-output rule on (``ms_sym``: X X^T on its upper triangle for n >= 4 m) and off."""
     import astrai_b200.optim.fused as F
 
     _, tf, src = peaks()
