@@ -155,7 +155,34 @@ __global__ void muon_momentum_kernel(const long long* __restrict__ gptr, const l
   __nv_bfloat16* u = U + (long long)b * numel;
   const float k = coef ? coef[0] : 1.f;
   float s = 0.f;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < numel; i += (long long)gridDim.x * blockDim.x) {
+  // 8 elements per thread per step with 16-byte accesses (parameters are contiguous matrices)
+  long long i0 = 0;
+  const bool vec = (numel % 8 == 0) &&
+                   ((reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(buf) | reinterpret_cast<uintptr_t>(u)) &
+                    15) == 0;
+  if (vec) {
+    const long long nv = numel / 8;
+    for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < nv; j += (long long)gridDim.x * blockDim.x) {
+      float gf[8], bf[8], uf[8];
+      load8(g + 8 * j, gf);
+      load8(buf + 8 * j, bf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float gi = gf[e] * k;
+        bf[e] = mu * bf[e] + (1.f - mu) * gi;
+        uf[e] = nesterov ? gi + mu * (bf[e] - gi) : bf[e];
+      }
+      store8(buf + 8 * j, bf);
+      store8(u + 8 * j, uf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float r = __bfloat162float(__float2bfloat16_rn(uf[e]));  // the norm of the stored bf16 values
+        s += r * r;
+      }
+    }
+    i0 = numel;
+  }
+  for (long long i = i0 + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < numel; i += (long long)gridDim.x * blockDim.x) {
     const float gi = __bfloat162float(g[i]) * k;
     const float bi = mu * to_f(buf[i]) + (1.f - mu) * gi;
     buf[i] = from_f<B>(bi);
@@ -230,6 +257,62 @@ __global__ void muon_apply_kernel(const long long* __restrict__ pptr, const __nv
   }
 }
 
+// Muon stage 3 with 16-byte accesses. Not transposed: 8 consecutive elements per thread. Transposed
+// (X[b] stored [C][R]): 64 x 64 tiles, read along R and written along C in 8-element vectors,
+// transposed through shared memory.
+template <typename P>
+__global__ void __launch_bounds__(256) muon_apply_vec_kernel(const long long* __restrict__ pptr,
+                                                             const __nv_bfloat16* __restrict__ X, int R, int C,
+                                                             int transpose, float decay, float adj_lr) {
+  const int b = blockIdx.z;
+  P* p = reinterpret_cast<P*>(pptr[b]);
+  const __nv_bfloat16* x = X + (long long)b * R * C;
+  const bool aligned = (reinterpret_cast<uintptr_t>(p) & 15) == 0;  // X is a fresh, aligned buffer
+  if (!transpose && !aligned) {
+    for (long long i = (long long)blockIdx.x * 256 + threadIdx.x; i < (long long)R * C; i += (long long)gridDim.x * 256)
+      p[i] = from_f<P>(to_f(p[i]) * decay - adj_lr * __bfloat162float(x[i]));
+    return;
+  }
+  if (!transpose) {
+    const long long nv = (long long)R * C / 8;
+    for (long long j = (long long)blockIdx.x * 256 + threadIdx.x; j < nv; j += (long long)gridDim.x * 256) {
+      float pf[8], xf[8];
+      load8(p + 8 * j, pf);
+      load8(x + 8 * j, xf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) pf[e] = pf[e] * decay - adj_lr * xf[e];
+      store8(p + 8 * j, pf);
+    }
+    return;
+  }
+  __shared__ float tile[64][65];  // [c][r]
+  const int c0 = blockIdx.x * 64, r0 = blockIdx.y * 64;
+  // 64 rows (c) x 8 vectors (r) of X
+  for (int v = threadIdx.x; v < 512; v += 256) {
+    const int ci = v >> 3, rv = (v & 7) * 8;
+    float f[8];
+    load8(x + (long long)(c0 + ci) * R + r0 + rv, f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) tile[ci][rv + e] = f[e];
+  }
+  __syncthreads();
+  // 64 rows (r) x 8 vectors (c) of p
+  for (int v = threadIdx.x; v < 512; v += 256) {
+    const int ri = v >> 3, cv = (v & 7) * 8;
+    P* dst = p + (long long)(r0 + ri) * C + c0 + cv;
+    if (!aligned) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) dst[e] = from_f<P>(to_f(dst[e]) * decay - adj_lr * tile[cv + e][ri]);
+      continue;
+    }
+    float pf[8];
+    load8(dst, pf);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) pf[e] = pf[e] * decay - adj_lr * tile[cv + e][ri];
+    store8(dst, pf);
+  }
+}
+
 }  // namespace astrai
 
 namespace astrai_host {
@@ -278,6 +361,20 @@ void muon_normalize(const void* U, void* X, int batch, int R, int C, int transpo
 
 void muon_apply(const long long* pptr, int fp32_params, const void* X, int batch, int R, int C, int transpose,
                 float decay, float adj_lr, cudaStream_t s) {
+  // the vector kernel needs whole 8-element vectors (rows of 64 x 64 tiles when transposed); the
+  // parameters' own alignment is checked by the caller's contiguous, 16-byte aligned storage
+  const bool vec = transpose ? (R % 64 == 0 && C % 64 == 0) : (((long long)R * C) % 8 == 0);
+  if (vec) {
+    const dim3 grid = transpose ? dim3(C / 64, R / 64, batch)
+                                : dim3((unsigned)std::min<long long>(((long long)R * C / 8 + 255) / 256, 1024), 1, batch);
+    if (fp32_params)
+      (astrai::note_launch(), muon_apply_vec_kernel<float><<<grid, 256, 0, s>>>(
+                                  pptr, static_cast<const __nv_bfloat16*>(X), R, C, transpose, decay, adj_lr));
+    else
+      (astrai::note_launch(), muon_apply_vec_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+                                  pptr, static_cast<const __nv_bfloat16*>(X), R, C, transpose, decay, adj_lr));
+    return;
+  }
   dim3 grid((C + 31) / 32, (R + 31) / 32, batch);
   if (fp32_params)
     (astrai::note_launch(), muon_apply_kernel<float><<<grid, dim3(32, 8), 0, s>>>(pptr, static_cast<const __nv_bfloat16*>(X), R, C, transpose,
