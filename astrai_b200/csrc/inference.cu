@@ -719,122 +719,241 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(
   }
 }
 
-// ------------------------------------------------------------------ sampling, one CTA per row
-// Vocabularies up to 32768: the row stays in registers of one 1024-thread CTA (32 values per
-// thread), so every row-wide step is a block reduction and no cluster barrier is needed. The top-k
-// and top-p thresholds come from a 4096-bin histogram of the order-preserving key (its top 12 bits:
-// sign, exponent and 3 mantissa bits) instead of a threshold search: one pass counts (top-k) or sums
-// the probability mass (top-p) per bin, a suffix scan over the bins finds the bin holding the
-// threshold, and only that bin's values are gathered and resolved exactly in shared memory (rank /
-// mass of strictly larger values). A bin holding more than SMC_CAND values (massive ties) falls
-// back to bisecting the key inside the bin. Same results as sample_kernel: keep key >= the k-th
-// largest key (ties kept), then keep a value iff the mass of strictly larger values <= top_p * Z,
-// then the frequency penalty, then an inverse-CDF draw in a fixed order.
-constexpr int SMC_THREADS = 1024;
-constexpr int SMC_PER = 32;
-constexpr int SMC_MAXV = SMC_THREADS * SMC_PER;  // 32768
-constexpr int SMC_BINS = 4096;
-constexpr int SMC_CAND = 2048;
+// ------------------------------------------------------------------ sampling, histogram thresholds
+// Vocabularies up to 32768: the row lives in the registers of the CS CTAs of a thread-block cluster
+// (32 values per thread): one 1024-thread CTA (CS = 1), or four 256-thread CTAs on four SMs (CS = 4,
+// for small batches: a quarter of the per-SM instructions, a cluster barrier per row-wide step). The
+// top-k and top-p thresholds come from a 4096-bin histogram of the order-preserving key (its top 12
+// bits: sign, exponent and 3 mantissa bits) instead of a threshold search: one pass counts (top-k)
+// or sums the probability mass (top-p) per bin, a suffix scan over the cluster's summed bins finds
+// the bin holding the threshold, and only that bin's values are gathered (from every CTA, through
+// distributed shared memory) and resolved exactly: rank, or mass of strictly larger values. A bin
+// of more than SMH_CAND values (massive ties) falls back to bisecting the key inside the bin. Same
+// results as sample_kernel: keep key >= the k-th largest key (ties kept), then keep a value iff the
+// mass of strictly larger values <= top_p * Z, then the frequency penalty, then an inverse-CDF draw
+// in a fixed order.
+constexpr int SMH_PER = 32;
+constexpr int SMH_MAXV = 32768;
+constexpr int SMH_BINS = 4096;
+constexpr int SMH_CAND = 2048;
 
-__device__ __forceinline__ float smc_block_max(float v, float* red) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  v = warp_max(v);
-  __syncthreads();
-  if (lane == 0) red[w] = v;
-  __syncthreads();
-  if (w == 0) {
-    v = warp_max(red[lane]);
-    if (lane == 0) red[32] = v;
+template <int THREADS, int CS>
+struct SmhRow {
+  static constexpr int NW = THREADS / 32;
+  float* red;   // [NW + 1] block scratch
+  float* xch;   // [2] this CTA's value exchanged with the cluster
+  int rank;
+
+  // row-wide max / sum of v (every thread of every CTA of the row gets it)
+  __device__ __forceinline__ float reduce(float v, bool is_max) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float y = __shfl_xor_sync(0xffffffffu, v, o);
+      v = is_max ? fmaxf(v, y) : v + y;
+    }
+    __syncthreads();
+    if (lane == 0) red[w] = v;
+    __syncthreads();
+    if (w == 0) {
+      float t = lane < NW ? red[lane] : (is_max ? -INFINITY : 0.f);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float y = __shfl_xor_sync(0xffffffffu, t, o);
+        t = is_max ? fmaxf(t, y) : t + y;
+      }
+      if (lane == 0) red[NW] = t;
+    }
+    __syncthreads();
+    float r = red[NW];
+    if constexpr (CS > 1) {
+      cg::cluster_group cl = cg::this_cluster();
+      if (threadIdx.x == 0) xch[0] = r;
+      cl.sync();
+      r = is_max ? -INFINITY : 0.f;
+#pragma unroll
+      for (int q = 0; q < CS; ++q) {
+        const float y = *cl.map_shared_rank(xch, q);
+        r = is_max ? fmaxf(r, y) : r + y;
+      }
+      cl.sync();
+    }
+    return r;
   }
-  __syncthreads();
-  return red[32];
-}
-__device__ __forceinline__ float smc_block_min(float v, float* red) { return -smc_block_max(-v, red); }
-__device__ __forceinline__ float smc_block_sum(float v, float* red) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  v = warp_sum(v);
-  __syncthreads();
-  if (lane == 0) red[w] = v;
-  __syncthreads();
-  if (w == 0) {
-    v = warp_sum(red[lane]);
-    if (lane == 0) red[32] = v;
+  __device__ __forceinline__ float max(float v) { return reduce(v, true); }
+  __device__ __forceinline__ float sum(float v) { return reduce(v, false); }
+  __device__ __forceinline__ float min(float v) { return -reduce(-v, true); }
+
+  // exclusive prefix of v over (CTA rank, thread) order; the row total in `total`
+  __device__ __forceinline__ float exclusive(float v, float& total) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    float incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    __syncthreads();
+    if (lane == 31) red[w] = incl;
+    __syncthreads();
+    if (w == 0) {
+      float t = lane < NW ? red[lane] : 0.f;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, t, o);
+        if (lane >= o) t += y;
+      }
+      if (lane < NW) red[lane] = t;  // inclusive warp totals
+    }
+    __syncthreads();
+    const float block_total = red[NW - 1];
+    float before = incl - v + (w > 0 ? red[w - 1] : 0.f);
+    total = block_total;
+    if constexpr (CS > 1) {
+      cg::cluster_group cl = cg::this_cluster();
+      if (threadIdx.x == 0) xch[1] = block_total;
+      cl.sync();
+      float lower = 0.f, all = 0.f;
+#pragma unroll
+      for (int q = 0; q < CS; ++q) {
+        const float y = *cl.map_shared_rank(xch + 1, q);
+        all += y;
+        if (q < rank) lower += y;
+      }
+      cl.sync();
+      before += lower;
+      total = all;
+    }
+    return before;
   }
-  __syncthreads();
-  return red[32];
-}
-// Exclusive prefix over threads (thread order) of v; also returns the block total.
-__device__ __forceinline__ float smc_block_exclusive(float v, float* red, float& total) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  float incl = v;
+};
+
+// Bin b* (scanning from the top) where the running total of the cluster's summed bins first exceeds
+// `target` (strictly), or reaches it when `reach`; the total of the bins above b* in `above`. -1 when
+// the total never gets there. Every CTA computes the same answer from the same sums.
+template <int THREADS, int CS>
+__device__ __forceinline__ int smh_find_bin(float* bins, float target, bool reach, SmhRow<THREADS, CS>& row,
+                                            int* s_bin, float* s_above, float& above) {
+  constexpr int BPT = SMH_BINS / THREADS;
+  const int t = threadIdx.x;
+  float h[BPT];
+  if constexpr (CS > 1) {
+    cg::cluster_group cl = cg::this_cluster();
+    cl.sync();  // every CTA's histogram is complete
+#pragma unroll
+    for (int i = 0; i < BPT; ++i) {
+      float acc = 0.f;
+#pragma unroll
+      for (int q = 0; q < CS; ++q) acc += *cl.map_shared_rank(bins + BPT * t + i, q);
+      h[i] = acc;
+    }
+    cl.sync();  // peers may reuse their bins from here on
+  } else {
+#pragma unroll
+    for (int i = 0; i < BPT; ++i) h[i] = bins[BPT * t + i];
+  }
+  float own = 0.f;
+#pragma unroll
+  for (int i = 0; i < BPT; ++i) own += h[i];
+  // bins above this thread's range: the total minus the inclusive prefix up to this thread (block order
+  // = bin order; the cluster part of the prefix is not wanted here: every CTA holds all bins)
+  const int lane = t & 31, w = t >> 5;
+  float incl = own;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const float y = __shfl_up_sync(0xffffffffu, incl, o);
     if (lane >= o) incl += y;
   }
   __syncthreads();
-  if (lane == 31) red[w] = incl;
+  if (lane == 31) row.red[w] = incl;
   __syncthreads();
   if (w == 0) {
-    float t = red[lane];
+    float v = lane < THREADS / 32 ? row.red[lane] : 0.f;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const float y = __shfl_up_sync(0xffffffffu, t, o);
-      if (lane >= o) t += y;
+      const float y = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += y;
     }
-    red[lane] = t;  // inclusive warp totals
+    if (lane < THREADS / 32) row.red[lane] = v;
   }
   __syncthreads();
-  total = red[31];
-  return incl - v + (w > 0 ? red[w - 1] : 0.f);
-}
-
-// Bin b* (scanning from the top) where the running total of `bins` first exceeds `target`
-// (strictly, or reaches it when `reach`); returns the total of the bins above b* in `above`. Four
-// bins per thread; -1 when the total never gets there.
-__device__ __forceinline__ int smc_find_bin(const float* bins, float target, bool reach, float* red, int* s_bin,
-                                           float* s_above, float& above) {
-  const int t = threadIdx.x;
-  float own = 0.f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) own += bins[4 * t + i];
-  // the total of bins above this thread's four = (block total) - (inclusive prefix up to this thread)
-  float total;
-  const float excl = smc_block_exclusive(own, red, total);
-  float cum = total - excl - own;
+  const float total = row.red[THREADS / 32 - 1];
+  const float prefix = incl + (w > 0 ? row.red[w - 1] : 0.f);
+  float cum = total - prefix;
   if (t == 0) *s_bin = -1;
   __syncthreads();
 #pragma unroll
-  for (int i = 3; i >= 0; --i) {
-    const float h = bins[4 * t + i];
-    const bool hit = reach ? (cum < target && cum + h >= target) : (cum <= target && cum + h > target);
-    if (hit && h > 0.f) {
-      *s_bin = 4 * t + i;
+  for (int i = BPT - 1; i >= 0; --i) {
+    const bool hit = reach ? (cum < target && cum + h[i] >= target) : (cum <= target && cum + h[i] > target);
+    if (hit && h[i] > 0.f) {
+      *s_bin = BPT * t + i;
       *s_above = cum;
     }
-    cum += h;
+    cum += h[i];
   }
   __syncthreads();
   above = *s_above;
   return *s_bin;
 }
 
-__global__ void __launch_bounds__(SMC_THREADS, 1) sample_cta_kernel(
+// Values of x in bin `bin` (bin < 0: every finite value) from every CTA of the row, into `all`
+// (same order on every CTA); returns their count, or a count > SMH_CAND when they do not fit.
+template <int THREADS, int CS>
+__device__ __forceinline__ int smh_gather(const float (&x)[SMH_PER], int bin, float* mine, float* all, int* s_cnt,
+                                          int* s_tot) {
+  __syncthreads();
+  if (threadIdx.x == 0) *s_cnt = 0;
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < SMH_PER; ++j)
+    if (x[j] != -INFINITY && (bin < 0 || (int)(fkey(x[j]) >> 20) == bin)) {
+      const int slot = atomicAdd(s_cnt, 1);
+      if (slot < SMH_CAND) mine[slot] = x[j];
+    }
+  if constexpr (CS == 1) {
+    __syncthreads();
+    const int n = *s_cnt;
+    for (int i = threadIdx.x; i < n && i < SMH_CAND; i += THREADS) all[i] = mine[i];
+    __syncthreads();
+    return n;
+  } else {
+    cg::cluster_group cl = cg::this_cluster();
+    cl.sync();
+    int n = 0;
+#pragma unroll
+    for (int q = 0; q < CS; ++q) {
+      const int nq = *cl.map_shared_rank(s_cnt, q);
+      const float* src = cl.map_shared_rank(mine, q);
+      for (int i = threadIdx.x; i < nq && n + i < SMH_CAND; i += THREADS) all[n + i] = src[i];
+      n += nq;
+    }
+    if (threadIdx.x == 0) *s_tot = n;
+    cl.sync();
+    return n;
+  }
+}
+
+template <int THREADS, int CS>
+__global__ void __launch_bounds__(THREADS, 1) sample_hist_kernel(
     const void* __restrict__ logits, int logits_f32, long long ld, int V, const float* __restrict__ temperature,
     const int* __restrict__ top_k, const float* __restrict__ top_p, const float* __restrict__ penalty,
     const long long* __restrict__ hist, int hist_len, long long ld_hist,
     const unsigned long long* __restrict__ rng, long long* __restrict__ out_tok, float* __restrict__ out_lp) {
-  __shared__ float bins[SMC_BINS];
-  __shared__ float cand[SMC_CAND];
-  __shared__ float red[40];
-  __shared__ int s_cnt, s_bin;
+  constexpr int CHUNK = THREADS * SMH_PER;
+  __shared__ float bins[SMH_BINS];
+  __shared__ float cand_mine[SMH_CAND], cand[SMH_CAND];
+  __shared__ float red[THREADS / 32 + 1], xch[2];
+  __shared__ int s_cnt, s_tot, s_bin;
   __shared__ float s_above;
-  const int row = blockIdx.x, t = threadIdx.x;
-  float x[SMC_PER];
+  const int rank = CS > 1 ? (int)cg::this_cluster().block_rank() : 0;
+  const int row = blockIdx.x / CS, t = threadIdx.x;
+  SmhRow<THREADS, CS> rw{red, xch, rank};
+  const int base = rank * CHUNK;
+  float x[SMH_PER];
   float raw_max = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < SMC_PER; ++j) {
-    const int i = t + j * SMC_THREADS;
+  for (int j = 0; j < SMH_PER; ++j) {
+    const int i = base + t + j * THREADS;
     float v = -INFINITY;
     if (i < V) {
       v = logits_f32 ? reinterpret_cast<const float*>(logits)[(long long)row * ld + i]
@@ -845,17 +964,17 @@ __global__ void __launch_bounds__(SMC_THREADS, 1) sample_cta_kernel(
     raw_max = fmaxf(raw_max, v);
   }
   const float temp = temperature ? temperature[row] : 1.f;
-  const float gmax = smc_block_max(raw_max, red);
+  const float gmax = rw.max(raw_max);
   if (temp == 0.f) {
     float sum = 0.f, best = 3.0e38f;
 #pragma unroll
-    for (int j = 0; j < SMC_PER; ++j) {
+    for (int j = 0; j < SMH_PER; ++j) {
       sum += (x[j] == -INFINITY) ? 0.f : __expf(x[j] - gmax);
-      if (x[j] == gmax) best = fminf(best, (float)(t + j * SMC_THREADS));
+      if (x[j] == gmax) best = fminf(best, (float)(base + t + j * THREADS));
     }
-    const float Z = smc_block_sum(sum, red);
-    const float bi = smc_block_min(best, red);
-    if (t == 0) {
+    const float Z = rw.sum(sum);
+    const float bi = rw.min(best);
+    if (t == 0 && rank == 0) {
       out_tok[row] = bi > 1.0e38f ? 0 : (long long)bi;
       if (out_lp) out_lp[row] = gmax == -INFINITY ? -INFINITY : -__logf(Z);
     }
@@ -863,39 +982,33 @@ __global__ void __launch_bounds__(SMC_THREADS, 1) sample_cta_kernel(
   }
   const float inv_t = 1.f / fmaxf(temp, 1e-8f);
 #pragma unroll
-  for (int j = 0; j < SMC_PER; ++j) x[j] *= inv_t;
+  for (int j = 0; j < SMH_PER; ++j) x[j] *= inv_t;
   const float mx = gmax * inv_t;
   // ---- top-k
   const int k = top_k ? top_k[row] : 0;
   uint32_t thr = 0;  // keep fkey >= thr
   if (k > 0 && k < V) {
-    for (int b = t; b < SMC_BINS; b += SMC_THREADS) bins[b] = 0.f;
+    for (int b = t; b < SMH_BINS; b += THREADS) bins[b] = 0.f;
     __syncthreads();
 #pragma unroll
-    for (int j = 0; j < SMC_PER; ++j)
+    for (int j = 0; j < SMH_PER; ++j)
       if (x[j] != -INFINITY) atomicAdd(&bins[fkey(x[j]) >> 20], 1.f);
     __syncthreads();
     float above;
-    const int bstar = smc_find_bin(bins, (float)k, true, red, &s_bin, &s_above, above);
+    const int bstar = smh_find_bin<THREADS, CS>(bins, (float)k, true, rw, &s_bin, &s_above, above);
     if (bstar >= 0) {
       const int need = k - (int)above;  // values of bin b* to keep (its `need` largest, ties kept)
-      const int nb = (int)bins[bstar];
-      if (nb <= SMC_CAND) {
-        if (t == 0) s_cnt = 0;
-        __syncthreads();
-#pragma unroll
-        for (int j = 0; j < SMC_PER; ++j)
-          if (x[j] != -INFINITY && (int)(fkey(x[j]) >> 20) == bstar) cand[atomicAdd(&s_cnt, 1)] = x[j];
-        __syncthreads();
+      const int nb = smh_gather<THREADS, CS>(x, bstar, cand_mine, cand, &s_cnt, &s_tot);
+      if (nb <= SMH_CAND) {
         // the smallest value with fewer than `need` strictly larger values in the bin
         float kth = INFINITY;
-        for (int i = t; i < nb; i += SMC_THREADS) {
+        for (int i = t; i < nb; i += THREADS) {
           const float c = cand[i];
           int greater = 0;
           for (int j = 0; j < nb; ++j) greater += cand[j] > c;
           if (greater < need) kth = fminf(kth, c);
         }
-        thr = fkey(smc_block_min(kth, red));
+        thr = fkey(rw.min(kth));
       } else {
         // massive ties: bisect the key inside the bin (count of keys >= mid must stay >= k)
         uint32_t lo = (uint32_t)bstar << 20, hi = lo | 0xFFFFFu;
@@ -903,13 +1016,13 @@ __global__ void __launch_bounds__(SMC_THREADS, 1) sample_cta_kernel(
           const uint32_t mid = lo + (hi - lo + 1) / 2;
           float c = 0.f;
 #pragma unroll
-          for (int j = 0; j < SMC_PER; ++j) c += (x[j] != -INFINITY && fkey(x[j]) >= mid) ? 1.f : 0.f;
-          if (smc_block_sum(c, red) >= (float)k) lo = mid; else hi = mid - 1;
+          for (int j = 0; j < SMH_PER; ++j) c += (x[j] != -INFINITY && fkey(x[j]) >= mid) ? 1.f : 0.f;
+          if (rw.sum(c) >= (float)k) lo = mid; else hi = mid - 1;
         }
         thr = lo;
       }
 #pragma unroll
-      for (int j = 0; j < SMC_PER; ++j)
+      for (int j = 0; j < SMH_PER; ++j)
         if (x[j] != -INFINITY && fkey(x[j]) < thr) x[j] = -INFINITY;
     }
   }
@@ -917,76 +1030,61 @@ __global__ void __launch_bounds__(SMC_THREADS, 1) sample_cta_kernel(
   const float pp = top_p ? top_p[row] : 1.f;
   bool topp_done = false;
   if (pp < 1.f && thr != 0u) {
-    // after top-k only the k largest (plus ties) survive: decide on them in shared memory
-    __syncthreads();
-    if (t == 0) s_cnt = 0;
-    __syncthreads();
-#pragma unroll
-    for (int j = 0; j < SMC_PER; ++j)
-      if (x[j] != -INFINITY) {
-        const int slot = atomicAdd(&s_cnt, 1);
-        if (slot < SMC_CAND) cand[slot] = x[j];
-      }
-    __syncthreads();
-    const int n = s_cnt;
-    if (n <= SMC_CAND) {
+    // after top-k only the k largest (plus ties) survive: decide on all of them at once
+    const int n = smh_gather<THREADS, CS>(x, -1, cand_mine, cand, &s_cnt, &s_tot);
+    if (n <= SMH_CAND) {
       float e = 0.f;
-      for (int i = t; i < n; i += SMC_THREADS) e += __expf(cand[i] - mx);
-      const float target = pp * smc_block_sum(e, red);
+      for (int i = t; i < n; i += THREADS) e += __expf(cand[i] - mx);
+      // every CTA holds all n survivors: a block sum is the row sum
+      const float target = pp * SmhRow<THREADS, 1>{red, xch, 0}.sum(e);
       float kept_min = INFINITY;
-      for (int i = t; i < n; i += SMC_THREADS) {
+      for (int i = t; i < n; i += THREADS) {
         const float c = cand[i];
         float greater = 0.f;
         for (int j = 0; j < n; ++j)
           if (cand[j] > c) greater += __expf(cand[j] - mx);
         if (greater <= target) kept_min = fminf(kept_min, c);
       }
-      kept_min = smc_block_min(kept_min, red);
+      kept_min = SmhRow<THREADS, 1>{red, xch, 0}.min(kept_min);
 #pragma unroll
-      for (int j = 0; j < SMC_PER; ++j)
+      for (int j = 0; j < SMH_PER; ++j)
         if (x[j] < kept_min) x[j] = -INFINITY;
       topp_done = true;
     }
   }
   if (pp < 1.f && !topp_done) {
     __syncthreads();
-    for (int b = t; b < SMC_BINS; b += SMC_THREADS) bins[b] = 0.f;
+    for (int b = t; b < SMH_BINS; b += THREADS) bins[b] = 0.f;
     __syncthreads();
     float zs = 0.f;
 #pragma unroll
-    for (int j = 0; j < SMC_PER; ++j) {
+    for (int j = 0; j < SMH_PER; ++j) {
       if (x[j] == -INFINITY) continue;
       const float e = __expf(x[j] - mx);
       zs += e;
       atomicAdd(&bins[fkey(x[j]) >> 20], e);
     }
-    const float Z = smc_block_sum(zs, red);
+    const float Z = rw.sum(zs);
     const float target = pp * Z;
     float above;
-    const int bstar = smc_find_bin(bins, target, false, red, &s_bin, &s_above, above);
+    const int bstar = smh_find_bin<THREADS, CS>(bins, target, false, rw, &s_bin, &s_above, above);
     if (bstar >= 0) {
-      __syncthreads();
-      if (t == 0) s_cnt = 0;
-      __syncthreads();
-      // the values of bin b*: keep those whose strictly larger mass (bins above + larger in the bin) fits
-#pragma unroll
-      for (int j = 0; j < SMC_PER; ++j)
-        if (x[j] != -INFINITY && (int)(fkey(x[j]) >> 20) == bstar) {
-          const int slot = atomicAdd(&s_cnt, 1);
-          if (slot < SMC_CAND) cand[slot] = x[j];
-        }
-      __syncthreads();
-      const int nb = s_cnt;
+      const int nb = smh_gather<THREADS, CS>(x, bstar, cand_mine, cand, &s_cnt, &s_tot);
       float kept_min = INFINITY;
-      if (nb <= SMC_CAND) {
-        for (int i = t; i < nb; i += SMC_THREADS) {
+      if (nb <= SMH_CAND) {
+        // keep a value of bin b* when the mass above the bin plus the larger values in it fits
+        for (int i = t; i < nb; i += THREADS) {
           const float c = cand[i];
           float greater = above;
           for (int j = 0; j < nb; ++j)
             if (cand[j] > c) greater += __expf(cand[j] - mx);
           if (greater <= target) kept_min = fminf(kept_min, c);
         }
-        kept_min = smc_block_min(kept_min, red);
+        kept_min = SmhRow<THREADS, 1>{red, xch, 0}.min(kept_min);
+        const uint32_t cut = kept_min == INFINITY ? ((uint32_t)(bstar + 1) << 20) : fkey(kept_min);
+#pragma unroll
+        for (int j = 0; j < SMH_PER; ++j)
+          if (x[j] != -INFINITY && fkey(x[j]) < cut) x[j] = -INFINITY;
       } else {
         // bisect the key inside the bin: the smallest key whose strictly larger mass fits
         uint32_t lo = (uint32_t)bstar << 20, hi = lo | 0xFFFFFu;
@@ -994,22 +1092,13 @@ __global__ void __launch_bounds__(SMC_THREADS, 1) sample_cta_kernel(
           const uint32_t mid = lo + (hi - lo) / 2;
           float m = 0.f;
 #pragma unroll
-          for (int j = 0; j < SMC_PER; ++j)
+          for (int j = 0; j < SMH_PER; ++j)
             if (x[j] != -INFINITY && fkey(x[j]) > mid) m += __expf(x[j] - mx);
-          if (smc_block_sum(m, red) <= target) hi = mid; else lo = mid + 1;
+          if (rw.sum(m) <= target) hi = mid; else lo = mid + 1;
         }
-        kept_min = -INFINITY;
-        thr = lo;
 #pragma unroll
-        for (int j = 0; j < SMC_PER; ++j)
-          if (x[j] != -INFINITY && fkey(x[j]) < thr) x[j] = -INFINITY;
-      }
-      if (kept_min != -INFINITY) {
-        // no value of bin b* fits only when the bins above already hold the mass: keep from b* + 1 up
-        const uint32_t cut = kept_min == INFINITY ? ((uint32_t)(bstar + 1) << 20) : fkey(kept_min);
-#pragma unroll
-        for (int j = 0; j < SMC_PER; ++j)
-          if (x[j] != -INFINITY && fkey(x[j]) < cut) x[j] = -INFINITY;
+        for (int j = 0; j < SMH_PER; ++j)
+          if (x[j] != -INFINITY && fkey(x[j]) < lo) x[j] = -INFINITY;
       }
     }
   }
@@ -1018,32 +1107,35 @@ __global__ void __launch_bounds__(SMC_THREADS, 1) sample_cta_kernel(
   if (pen != 0.f && hist) {
     for (int h = 0; h < hist_len; ++h) {
       const long long id = hist[(long long)row * ld_hist + h];
-      if (id < 0 || id >= V || (int)(id % SMC_THREADS) != t) continue;
-      const int jj = (int)(id / SMC_THREADS);
+      if (id < base || id >= base + CHUNK || id >= V) continue;
+      const int local = (int)(id - base);
+      if (local % THREADS != t) continue;
+      const int jj = local / THREADS;
 #pragma unroll
-      for (int j = 0; j < SMC_PER; ++j)
+      for (int j = 0; j < SMH_PER; ++j)
         if (j == jj && x[j] != -INFINITY) x[j] -= pen;
     }
   }
-  // ---- draw from softmax(x) by inverse CDF in (thread, slot) order
+  // ---- draw from softmax(x) by inverse CDF in (CTA, thread, slot) order
   float m2 = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < SMC_PER; ++j) m2 = fmaxf(m2, x[j]);
-  m2 = smc_block_max(m2, red);
+  for (int j = 0; j < SMH_PER; ++j) m2 = fmaxf(m2, x[j]);
+  m2 = rw.max(m2);
   float tsum = 0.f;
 #pragma unroll
-  for (int j = 0; j < SMC_PER; ++j) tsum += (x[j] == -INFINITY) ? 0.f : __expf(x[j] - m2);
+  for (int j = 0; j < SMH_PER; ++j) tsum += (x[j] == -INFINITY) ? 0.f : __expf(x[j] - m2);
   float Z;
-  const float before = smc_block_exclusive(tsum, red, Z);
-  const float last_owner = smc_block_max(tsum > 0.f ? (float)t : -1.f, red);
+  const float before = rw.exclusive(tsum, Z);
+  const int me = rank * THREADS + t;
+  const float last_owner = rw.max(tsum > 0.f ? (float)me : -1.f);
   const float u = uniform_from(rng[0], rng[1], (unsigned long long)row) * Z;
-  const bool is_last = (float)t == last_owner;
+  const bool is_last = (float)me == last_owner;
   if (tsum > 0.f && u >= before && (u < before + tsum || is_last)) {
     float c = before;
     int pick = -1, last_nz = -1;
     float xv = -INFINITY, xlast = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < SMC_PER; ++j) {
+    for (int j = 0; j < SMH_PER; ++j) {
       const float e = (x[j] == -INFINITY) ? 0.f : __expf(x[j] - m2);
       if (e > 0.f) {
         last_nz = j;
@@ -1059,9 +1151,9 @@ __global__ void __launch_bounds__(SMC_THREADS, 1) sample_cta_kernel(
       pick = last_nz;
       xv = xlast;
     }
-    out_tok[row] = t + pick * SMC_THREADS;
+    out_tok[row] = base + t + pick * THREADS;
     if (out_lp) out_lp[row] = (xv - m2) - __logf(Z);
-  } else if (last_owner < 0.f && t == 0) {
+  } else if (last_owner < 0.f && t == 0 && rank == 0) {
     out_tok[row] = 0;  // every logit was -inf / NaN
     if (out_lp) out_lp[row] = -INFINITY;
   }
@@ -1168,10 +1260,29 @@ void sample_tokens(const void* logits, int f32, long long ld, int rows, int V, c
                    const int* top_k, const float* top_p, const float* penalty, const long long* hist, int hist_len,
                    long long ld_hist, const unsigned long long* rng, long long* out_tok, float* out_lp,
                    cudaStream_t s) {
-  if (V <= SMC_MAXV && sample_cta_enabled()) {
-    (astrai::note_launch(), sample_cta_kernel<<<rows, SMC_THREADS, 0, s>>>(logits, f32, ld, V, temperature, top_k, top_p,
-                                                                           penalty, hist, hist_len, ld_hist, rng,
-                                                                           out_tok, out_lp));
+  if (V <= SMH_MAXV && sample_cta_enabled()) {
+    // a cluster of four 256-thread CTAs per row while the rows leave SMs idle, one 1024-thread CTA after
+    if ((long long)rows * 4 <= 2LL * 148) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(rows * 4);
+      cfg.blockDim = dim3(256);
+      cfg.stream = s;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 4;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      note_launch();
+      const cudaError_t e = cudaLaunchKernelEx(&cfg, sample_hist_kernel<256, 4>, logits, f32, ld, V, temperature, top_k,
+                                               top_p, penalty, hist, hist_len, ld_hist, rng, out_tok, out_lp);
+      if (e != cudaSuccess) throw std::runtime_error(std::string("sample: launch failed: ") + cudaGetErrorString(e));
+    } else {
+      (astrai::note_launch(), sample_hist_kernel<1024, 1><<<rows, 1024, 0, s>>>(logits, f32, ld, V, temperature, top_k,
+                                                                                top_p, penalty, hist, hist_len, ld_hist,
+                                                                                rng, out_tok, out_lp));
+    }
     return;
   }
   const int cs = (V + SMP_CHUNK - 1) / SMP_CHUNK;
