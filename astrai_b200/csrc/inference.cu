@@ -1238,11 +1238,12 @@ void decode_combine(const float* part_acc, const float* part_ml, int B, int Hq, 
 }
 
 // Splits per (batch row, kv head). The tensor-core kernel runs one persistent CTA per SM over
-// (row, kv head, split) items of 128-key tiles: about 8 items per SM keep the last round of items
-// short, and a split keeps at least 2 tiles (256 keys of capacity) so its pipeline fills; at most 32.
+// (row, kv head, split) items of 128-key tiles, and every item boundary drains its pipeline: split
+// only as far as needed to give each SM an item (B32 x 4096 keys, Hkv 4: 1 split 63 us, 2 74 us,
+// 10 80 us on B200), keeping at least 2 tiles (256 keys of capacity) per split; at most 32.
 int decode_splits(int B, int Hkv, int max_len, int sms) {
   const int pairs = std::max(1, B * Hkv);
-  const int want = (8 * sms + pairs - 1) / pairs;
+  const int want = std::max(1, sms / pairs);
   const int max_splits = std::max(1, (max_len + 255) / 256);
   return std::max(1, std::min(want, std::min(max_splits, 32)));
 }
