@@ -99,6 +99,9 @@ template <int D, int G>
 __global__ void __launch_bounds__(DT_THREADS, 1)
     paged_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                            DecodeTcParams p) {
+  // a kernel launched after this one with programmatic dependent launch may start now (it waits for
+  // this grid to finish before reading what it writes)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
   static_assert(G >= 1 && G <= 16 && (G & (G - 1)) == 0, "G in {1, 2, 4, 8, 16}");
   constexpr int NCH = D / 64;                       // 64-column chunks per row

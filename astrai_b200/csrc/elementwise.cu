@@ -18,6 +18,9 @@ namespace astrai {
 __global__ void rope_kernel(__nv_bfloat16* __restrict__ x, long long ld, int rows, int col0, int n_heads, int head_dim,
                             const int* __restrict__ pos, int seq_len, const float2* __restrict__ cs, float sign,
                             int rot_dim, int rot_off, int max_pos, int* err) {
+  // a kernel launched after this one with programmatic dependent launch may start now (it waits for
+  // this grid to finish before reading what it writes)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   // each thread handles 8 consecutive elements (4 pairs) of one head
   const int per_head = rot_dim / 8;
   const long long total = (long long)rows * n_heads * per_head;
@@ -54,6 +57,9 @@ __device__ __forceinline__ float silu_f(float g) { return g / (1.f + __expf(-g))
 // block sized for its capacity); the rest are left untouched.
 __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ h, long long ldh, __nv_bfloat16* __restrict__ out,
                                   long long ldo, int rows, int F, const int* __restrict__ live_rows) {
+  // a kernel launched after this one with programmatic dependent launch may start now (it waits for
+  // this grid to finish before reading what it writes)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int per_row = F / 8;
   const long long total = (long long)(live_rows ? min(rows, max(0, *live_rows)) : rows) * per_row;
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
@@ -102,6 +108,9 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dy, long lon
 // out[t, :] = w[ids[t], :]   (d multiple of 8)
 __global__ void embedding_fwd_kernel(const long long* __restrict__ ids, const __nv_bfloat16* __restrict__ w,
                                      __nv_bfloat16* __restrict__ out, int n_tok, int d, int vocab, int* err) {
+  // a kernel launched after this one with programmatic dependent launch may start now (it waits for
+  // this grid to finish before reading what it writes)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int per = d / 8;
   const long long total = (long long)n_tok * per;
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;

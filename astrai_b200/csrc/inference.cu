@@ -269,6 +269,9 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams p) {
 __global__ void decode_combine_kernel(const float* __restrict__ part_acc, const float* __restrict__ part_ml, int B,
                                       int Hq, int Hkv, int splits, __nv_bfloat16* __restrict__ out, long long ldo,
                                       int D) {
+  // a kernel launched after this one with programmatic dependent launch may start now (it waits for
+  // this grid to finish before reading what it writes)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int bh = blockIdx.x;
   const int b = bh / Hq, h = bh % Hq;
   const int G = Hq / Hkv, hk = h / G, g = h % G;

@@ -37,6 +37,9 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(const __nv_bf
                                                                    __nv_bfloat16* __restrict__ y, long long ldy,
                                                                    float* __restrict__ rstd_out, int rows, int D,
                                                                    float eps, int rows_per_block) {
+  // a kernel launched after this one with programmatic dependent launch may start now (it waits for
+  // this grid to finish before reading what it writes)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ float red[2][32];
   const int T = blockDim.x, nw = T >> 5;
   int col[V];

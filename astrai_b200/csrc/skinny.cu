@@ -12,6 +12,7 @@
 // atomics, no second kernel.
 #include <cooperative_groups.h>
 
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -46,6 +47,22 @@ __global__ void __launch_bounds__(SK_WARPS * 32) skinny_gemm_kernel(const __nv_b
   for (int m = 0; m < MT; ++m)
 #pragma unroll
     for (int c = 0; c < SK_COLS; ++c) s[m][c] = 0.f;
+  // Programmatic dependent launch: this grid may start while the kernel before it (which writes X
+  // or R) is still running. The weights do not depend on it, so their lines are prefetched into L2
+  // first; X and R are read only after griddepcontrol.wait (the previous grid complete and its
+  // memory visible). Nothing is written before the wait. The next kernel may launch as soon as every
+  // CTA of this one has started.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (live) {
+    const char* r0p = reinterpret_cast<const char*>(W + (long long)n0 * ldw + kb);
+    const char* r1p = reinterpret_cast<const char*>(W + (long long)(has1 ? n0 + 1 : n0) * ldw + kb);
+    const int lines = ((ke - kb) * 2 + 127) / 128;
+    for (int l = lane; l < lines; l += 32) {
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(r0p + l * 128));
+      if (has1) asm volatile("prefetch.global.L2 [%0];" ::"l"(r1p + l * 128));
+    }
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (live) {
     const __nv_bfloat16* w0 = W + (long long)n0 * ldw;
     const __nv_bfloat16* w1 = W + (long long)(has1 ? n0 + 1 : n0) * ldw;
@@ -122,6 +139,15 @@ __global__ void __launch_bounds__(SK_WARPS * 32) skinny_gemm_kernel(const __nv_b
 namespace astrai_host {
 using namespace astrai;
 
+// ASTRAI_SKINNY_PDL=0 launches the skinny GEMM only after the previous kernel ends
+static bool skinny_pdl() {
+  static const bool on = [] {
+    const char* e = std::getenv("ASTRAI_SKINNY_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 template <int MT>
 static void launch_skinny(dim3 grid, int ks, cudaStream_t s, const __nv_bfloat16* X, long long ldx,
                           const __nv_bfloat16* W, long long ldw, const __nv_bfloat16* R, long long ldr,
@@ -130,13 +156,16 @@ static void launch_skinny(dim3 grid, int ks, cudaStream_t s, const __nv_bfloat16
   cfg.gridDim = grid;
   cfg.blockDim = dim3(SK_WARPS * 32);
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = ks;
   attr[0].val.clusterDim.z = 1;
+  // may start before the previous kernel on the stream ends (the kernel waits before reading X)
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = skinny_pdl() ? 2 : 1;
   note_launch();
   const cudaError_t e = cudaLaunchKernelEx(&cfg, skinny_gemm_kernel<MT>, X, ldx, W, ldw, R, ldr, Y, ldy, M, N, K,
                                            kchunk);
