@@ -149,6 +149,37 @@ def test_sample_topk_topp_support_and_logprob(V):
     torch.testing.assert_close(lp, chosen, atol=2e-3, rtol=2e-3)
 
 
+@pytest.mark.parametrize("V", [1000, 32000])
+def test_sample_topp_only_support_and_logprob(V):
+    """Top-p over the whole vocabulary (no top-k): the mass histogram and the exact in-bin cut."""
+    from astrai_b200.inference.sample import SamplingPipeline, TemperatureStrategy, TopPStrategy, sample
+
+    rows = 64
+    x = _logits(rows, V, seed=4)
+    temp = torch.full((rows,), 0.9, device="cuda")
+    topp = torch.rand(rows, device="cuda") * 0.9 + 0.05
+    tok, lp = sample(x, temperature=temp, top_k=0, top_p=topp, return_logprobs=True)
+    ref = SamplingPipeline([TemperatureStrategy(temp), TopPStrategy(topp)]).apply(x.clone())
+    chosen = torch.log_softmax(ref, -1).gather(1, tok[:, None]).squeeze(1)
+    assert torch.isfinite(chosen).all(), "sampled a token outside the nucleus"
+    torch.testing.assert_close(lp, chosen, atol=2e-3, rtol=2e-3)
+
+
+@pytest.mark.parametrize("V", [4096, 32000])
+def test_sample_massive_ties_keep_every_tied_token(V):
+    """Every logit equal: one histogram bin holds the whole row, so the thresholds come from the
+    in-bin bisection; ties at the threshold are all kept, so every token stays possible."""
+    from astrai_b200.inference.sample import sample
+
+    rows = 256
+    x = torch.zeros(rows, V, device="cuda")
+    for kw in (dict(top_k=50), dict(top_p=0.5), dict(top_k=50, top_p=0.5)):
+        tok, lp = sample(x, temperature=1.0, return_logprobs=True, **kw)
+        assert ((tok >= 0) & (tok < V)).all()
+        torch.testing.assert_close(lp, torch.full_like(lp, -math.log(V)), atol=1e-3, rtol=1e-3)
+        assert tok.unique().numel() > rows // 2  # spread over the tied tokens, not stuck on a few
+
+
 def test_sample_frequency_penalty_logprob():
     from astrai_b200.inference.sample import FrequencyPenaltyStrategy, sample
 
