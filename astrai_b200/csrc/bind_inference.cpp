@@ -124,8 +124,8 @@ void paged_decode(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& v
   const int page_size = static_cast<int>(kc.size(2));
   const bool tc = decode_tc_enabled() && astrai_host::paged_decode_tc_supported(D, G, page_size);
   TORCH_CHECK(tc || G == 1 || G == 2 || G == 4 || G == 8,
-              "paged_decode: n_heads / n_kv_heads must be 1, 2, 4 or 8 (or a power of two up to 16 with head_dim "
-              "64 / 128 and page_size a multiple or divisor of 128)");
+              "paged_decode: n_heads / n_kv_heads must be 1 - 8, 12 or 16 with head_dim 64 / 128 and page_size a "
+              "multiple or divisor of 128 (otherwise 1, 2, 4 or 8)");
   TORCH_CHECK(table.dim() == 2 && table.size(0) == B && lens.numel() == B, "page_table / lens batch mismatch");
   TORCH_CHECK(q.size(1) >= Hq * D && out.size(0) == B && out.size(1) >= Hq * D, "q/out shape mismatch");
   TORCH_CHECK(splits >= 1 && splits <= 64, "splits must be in [1, 64]");

@@ -103,10 +103,10 @@ __global__ void __launch_bounds__(DT_THREADS, 1)
   // this grid to finish before reading what it writes)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
-  static_assert(G >= 1 && G <= 16 && (G & (G - 1)) == 0, "G in {1, 2, 4, 8, 16}");
+  static_assert(G >= 1 && G <= 16, "1 to 16 query heads per KV head");
   constexpr int NCH = D / 64;                       // 64-column chunks per row
   constexpr int KV_BYTES = NCH * DT_KCHUNK;         // one K (or V) tile
-  constexpr int GC = G < 8 ? 8 : G;                 // TMEM columns read per thread (x8 / x16 loads)
+  constexpr int GC = G <= 8 ? 8 : 16;               // TMEM columns read per thread (x8 / x16 loads)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int KST = DtStages<D>::K, VST = DtStages<D>::V;
@@ -499,11 +499,11 @@ static void launch_dt(const CUtensorMap& tk, const CUtensorMap& tv, const Decode
   (astrai::note_launch(), k<<<grid, DT_THREADS, smem, s>>>(tk, tv, p));
 }
 
-// True when the tensor-core kernel takes this shape: head_dim 64 / 128, 1 - 16 query heads per KV
-// head (a power of two), page_size a multiple of 128 or a divisor of 128 of at least 16.
+// True when the tensor-core kernel takes this shape: head_dim 64 / 128, 1 - 8, 12 or 16 query heads
+// per KV head, page_size a multiple of 128 or a divisor of 128 of at least 16.
 bool paged_decode_tc_supported(int D, int G, int page_size) {
   if (D != 64 && D != 128) return false;
-  if (G < 1 || G > 16 || (G & (G - 1)) != 0) return false;
+  if (!(G >= 1 && (G <= 8 || G == 12 || G == 16))) return false;
   return page_size % 128 == 0 || (page_size >= 16 && 128 % page_size == 0);
 }
 
@@ -550,8 +550,10 @@ void paged_decode_tc(const void* q, long long ldq, const void* kc, const void* v
                       (2 * 4 * 16 + 4 * 16) * sizeof(float) + 32 * sizeof(uint64_t);
 #define ASTRAI_DT_CASE(DD, GG) \
   if (D == DD && G == GG) return launch_dt<DD, GG>(tk, tv, p, grid, smem, s);
-  ASTRAI_DT_CASE(128, 1) ASTRAI_DT_CASE(128, 2) ASTRAI_DT_CASE(128, 4) ASTRAI_DT_CASE(128, 8) ASTRAI_DT_CASE(128, 16)
-  ASTRAI_DT_CASE(64, 1) ASTRAI_DT_CASE(64, 2) ASTRAI_DT_CASE(64, 4) ASTRAI_DT_CASE(64, 8) ASTRAI_DT_CASE(64, 16)
+  ASTRAI_DT_CASE(128, 1) ASTRAI_DT_CASE(128, 2) ASTRAI_DT_CASE(128, 3) ASTRAI_DT_CASE(128, 4) ASTRAI_DT_CASE(128, 5)
+  ASTRAI_DT_CASE(128, 6) ASTRAI_DT_CASE(128, 7) ASTRAI_DT_CASE(128, 8) ASTRAI_DT_CASE(128, 12) ASTRAI_DT_CASE(128, 16)
+  ASTRAI_DT_CASE(64, 1) ASTRAI_DT_CASE(64, 2) ASTRAI_DT_CASE(64, 3) ASTRAI_DT_CASE(64, 4) ASTRAI_DT_CASE(64, 5)
+  ASTRAI_DT_CASE(64, 6) ASTRAI_DT_CASE(64, 7) ASTRAI_DT_CASE(64, 8) ASTRAI_DT_CASE(64, 12) ASTRAI_DT_CASE(64, 16)
 #undef ASTRAI_DT_CASE
 }
 

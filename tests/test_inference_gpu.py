@@ -79,7 +79,7 @@ def test_paged_write_and_gather(page, D):
 
 
 @pytest.mark.parametrize("D", [64, 128])
-@pytest.mark.parametrize("G", [1, 2, 4, 8, 16])
+@pytest.mark.parametrize("G", [1, 2, 3, 4, 6, 8, 12, 16])
 @pytest.mark.parametrize("page,lens", [(16, [1, 17, 300, 64]), (64, [65, 700, 3, 128]),
                                        (128, [513, 128, 5, 1000]), (256, [257, 1, 900, 256])])
 @pytest.mark.parametrize("splits", [1, 7])
