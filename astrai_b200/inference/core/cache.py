@@ -594,9 +594,11 @@ class ContiguousCache(_TableCache):
     def __init__(self, n_layers: int, max_batch_size: int, max_seq_len: int, n_kv_heads: int, head_dim: int, device,
                  dtype: torch.dtype):
         self.max_seq_len = max_seq_len
-        self.page_size = max_seq_len
-        self._storage = Storage(n_layers, max_batch_size, max_seq_len, n_kv_heads, head_dim, device, dtype)
-        self._table = TaskTable(max_seq_len)
+        # a slot holds max_seq_len keys, rounded up to the 128-key tile of the tensor-core decode kernel
+        # (its TMA boxes never straddle two slots); the capacity checks still use max_seq_len
+        self.page_size = (max_seq_len + 127) // 128 * 128
+        self._storage = Storage(n_layers, max_batch_size, self.page_size, n_kv_heads, head_dim, device, dtype)
+        self._table = TaskTable(self.page_size)
         self._free_slots = list(range(max_batch_size))
         self._lock = threading.Lock()
 
