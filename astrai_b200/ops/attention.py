@@ -136,6 +136,19 @@ def attention_qkv(qkv: torch.Tensor, B: int, S: int, Hq: int, Hkv: int, table: t
         pos = positions.reshape(-1).to(torch.int32).contiguous() if positions is not None else None
         sg = seg.to(torch.int32).contiguous() if seg is not None else None
         return _AttnQKVFn.apply(qkv, table, pos, sg, B, S, Hq, Hkv, causal, rotated)
+    if (qkv.is_cuda and qkv.dtype == torch.bfloat16 and D in FWD_HEAD_DIMS and PAIR_FWD
+            and not (torch.is_grad_enabled() and qkv.requires_grad) and qkv.is_contiguous()):
+        # forward only (prefill, evaluation) at another head size: RoPE in place on the fresh projection
+        # output, then the forward kernel (the backward kernel covers head_dim 128 only)
+        pos = positions.reshape(-1).to(torch.int32).contiguous() if positions is not None else None
+        sg = seg.to(torch.int32).contiguous() if seg is not None else None
+        if not rotated:
+            rope_inplace(qkv, 0, Hq + Hkv, D, table, pos, S)
+        o = torch.empty((B * S, Hq * D), device=qkv.device, dtype=torch.bfloat16)
+        lse = torch.empty((B, Hq, S), device=qkv.device, dtype=torch.float32)
+        flash_forward(qkv, 0, qkv, Hq * D, qkv, (Hq + Hkv) * D, o, lse, B, S, S, Hq, Hkv, D, 1.0 / math.sqrt(D),
+                      causal, sg)
+        return o
     q, k, v = qkv.view(B, S, Hq + 2 * Hkv, D).split([Hq, Hkv, Hkv], dim=2)
     if positions is None:
         cs = table[:S].unsqueeze(0).expand(B, -1, -1, -1)

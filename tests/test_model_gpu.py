@@ -98,3 +98,24 @@ def test_fused_optimizers_match_torch(chunk_bytes, monkeypatch):
     torch.optim.AdamW([wt], lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1).step()
     assert rel(w.data, wt.data) < 1e-2
     assert abs(float(n) - float(torch.linalg.vector_norm(w.grad.float()))) < 1e-1 * float(n)
+
+
+@pytest.mark.parametrize("heads,kv", [(4, 2), (6, 1)])
+def test_forward_only_head_dim_64_matches_cpu(heads, kv):
+    """head_dim 64 without gradients (prefill, evaluation): RoPE in place and the forward kernel on the
+    fused QKV buffer, against the fp32 CPU oracle."""
+    from astrai_b200.models import AutoRegressiveLM
+    from astrai_b200.ops._ext import native
+
+    torch.manual_seed(1)
+    cpu = AutoRegressiveLM(tiny_cfg(hidden_size=64 * heads, num_attention_heads=heads, num_key_value_heads=kv,
+                                    intermediate_size=512)).float().eval()
+    cpu.load_state_dict({k: v.to(torch.bfloat16).float() for k, v in cpu.state_dict().items()})
+    gpu = copy.deepcopy(cpu).cuda().to(torch.bfloat16).eval()
+    ids = torch.randint(0, 512, (2, 300))
+    with torch.inference_mode():
+        lg = gpu(ids.cuda())["logits"]
+    torch.cuda.synchronize()
+    assert native().read_error() == 0
+    lc = cpu(ids)["logits"].detach()
+    assert rel(lg, lc) < 2e-2
