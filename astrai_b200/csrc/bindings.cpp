@@ -136,14 +136,16 @@ void gemm_swiglu(int64_t mode, const at::Tensor& a, const at::Tensor& w, const c
   const int M = (int)a.size(0), K = (int)a.size(1);
   c10::cuda::CUDAGuard g(a.device());
   if (mode == 1) {
-    TORCH_CHECK(h_out.has_value() && h_out->defined(), "gemm_swiglu mode 1 needs h_out");
-    check_bf16(*h_out, "h_out");
+    // h_out None: only a = silu(g) * u is stored (inference; the backward needs h)
+    const bool has_h = h_out.has_value() && h_out->defined();
+    if (has_h) check_bf16(*h_out, "h_out");
     const int F = (int)w.size(0) / 2;
-    TORCH_CHECK(w.size(0) == 2 * F && w.size(1) == K && h_out->size(0) == M && h_out->size(1) == 2 * F &&
-                    out.size(0) == M && out.size(1) == F && h_out->stride(1) == 1,
-                "gemm_swiglu mode 1: shapes x [M, K], w [2F, K], h [M, 2F], a [M, F]");
-    astrai_host::gemm_swiglu_bf16(1, a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), 0, h_out->data_ptr(),
-                                  h_out->stride(0), out.data_ptr(), out.stride(0), nullptr, 0, M, F, K, stream());
+    TORCH_CHECK(w.size(0) == 2 * F && w.size(1) == K && out.size(0) == M && out.size(1) == F &&
+                    (!has_h || (h_out->size(0) == M && h_out->size(1) == 2 * F && h_out->stride(1) == 1)),
+                "gemm_swiglu mode 1: shapes x [M, K], w [2F, K], h [M, 2F] (or None), a [M, F]");
+    astrai_host::gemm_swiglu_bf16(1, a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), 0,
+                                  has_h ? h_out->data_ptr() : nullptr, has_h ? h_out->stride(0) : 0, out.data_ptr(),
+                                  out.stride(0), nullptr, 0, M, F, K, stream());
   } else {
     TORCH_CHECK(mode == 2 && h_saved.has_value() && h_saved->defined(), "gemm_swiglu mode 2 needs h_saved");
     check_bf16(*h_saved, "h_saved");

@@ -164,6 +164,12 @@ __device__ __forceinline__ void scatter_copy_tile(const GemmParams& p, int mb, i
   }
 }
 
+// Programmatic dependent launch (the launch attribute set by the host launchers below): `trigger`
+// lets the next kernel on the stream be scheduled, `wait` blocks until the previous grid has
+// completed and its memory operations are visible. Both are no-ops in a launch without the attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // One unit of a CTA's work: tile `tile`, k-blocks [kb0, kb1).
 struct WorkItem {
   int tile, kb0, kb1;
@@ -359,6 +365,9 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
 
   const int warp = warp_id();
   const int lane = lane_id();
+  // programmatic dependent launch: the next kernel on the stream may be scheduled now (it waits for
+  // this grid before reading anything), and this one reads global memory only after the wait below
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -378,6 +387,7 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the previous grid has completed and its writes are visible
 
   const int num_tiles = p.batch * p.tiles_m * p.tiles_n;
 
@@ -653,6 +663,7 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
           if (p.epi == 1) {
             // h = (u, g) and a = silu(g) * u for output columns j0 .. j0 + CH1
             const int j0 = nb * HALF + cpart * PER1 + ck * CH1;
+            const bool store_h = p.D != nullptr;  // h = (u, g) is kept for the backward only
             __nv_bfloat16* hrow = reinterpret_cast<__nv_bfloat16*>(p.D) + (long long)row * p.ldd;
             __nv_bfloat16* arow = p.aux + (long long)row * p.ldaux;
 #pragma unroll
@@ -665,18 +676,22 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
                 ha[e] = pack_bf16(ub.x * gb.x * sigmoid_f(gb.x), ub.y * gb.y * sigmoid_f(gb.y));
               }
               if (j + 8 <= p.F && p.vec_ok) {
-                *reinterpret_cast<uint4*>(hrow + j) =
-                    make_uint4(pa[g8 / 2], pa[g8 / 2 + 1], pa[g8 / 2 + 2], pa[g8 / 2 + 3]);
-                *reinterpret_cast<uint4*>(hrow + p.F + j) =
-                    make_uint4(pb[g8 / 2], pb[g8 / 2 + 1], pb[g8 / 2 + 2], pb[g8 / 2 + 3]);
+                if (store_h) {
+                  *reinterpret_cast<uint4*>(hrow + j) =
+                      make_uint4(pa[g8 / 2], pa[g8 / 2 + 1], pa[g8 / 2 + 2], pa[g8 / 2 + 3]);
+                  *reinterpret_cast<uint4*>(hrow + p.F + j) =
+                      make_uint4(pb[g8 / 2], pb[g8 / 2 + 1], pb[g8 / 2 + 2], pb[g8 / 2 + 3]);
+                }
                 *reinterpret_cast<uint4*>(arow + j) = make_uint4(ha[0], ha[1], ha[2], ha[3]);
               } else {
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
                   if (j + e >= p.F) continue;
                   const int sh = (e & 1) * 16;
-                  hrow[j + e] = __ushort_as_bfloat16((unsigned short)(pa[g8 / 2 + e / 2] >> sh));
-                  hrow[p.F + j + e] = __ushort_as_bfloat16((unsigned short)(pb[g8 / 2 + e / 2] >> sh));
+                  if (store_h) {
+                    hrow[j + e] = __ushort_as_bfloat16((unsigned short)(pa[g8 / 2 + e / 2] >> sh));
+                    hrow[p.F + j + e] = __ushort_as_bfloat16((unsigned short)(pb[g8 / 2 + e / 2] >> sh));
+                  }
                   arow[j + e] = __ushort_as_bfloat16((unsigned short)(ha[e >> 1] >> sh));
                 }
               }
@@ -1029,6 +1044,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS
   const int lane = lane_id();
   const uint32_t rank = cluster_ctarank();  // 0: MMA issuer of the pair
   const int pair_id = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  pdl_trigger();  // as in gemm_kernel: global memory is read only after pdl_wait below
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -1054,6 +1070,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS
   cluster_sync_all();  // both CTAs' barriers exist before either signals the other's
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();
   const int num_tiles = p.batch * p.tiles_m * p.tiles_n;
 
   if (warp == 0) {
@@ -1264,6 +1281,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS
         if (lane == 0) mbar_arrive_cluster(acc ? empty_bar1 : empty_bar0);
         if (row_ok) {
           const int j0 = nb * BNH + cpart * PER;
+          const bool store_h = p.D != nullptr;  // h = (u, g) is kept for the backward only
           __nv_bfloat16* hrow = reinterpret_cast<__nv_bfloat16*>(p.D) + (long long)row * p.ldd;
           __nv_bfloat16* arow = p.aux + (long long)row * p.ldaux;
 #pragma unroll
@@ -1276,17 +1294,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS
               ha[e] = pack_bf16(ub.x * gb.x * sigmoid_f(gb.x), ub.y * gb.y * sigmoid_f(gb.y));
             }
             if (j + 8 <= p.F && p.vec_ok) {
-              *reinterpret_cast<uint4*>(hrow + j) = make_uint4(pu[g8 / 2], pu[g8 / 2 + 1], pu[g8 / 2 + 2], pu[g8 / 2 + 3]);
-              *reinterpret_cast<uint4*>(hrow + p.F + j) =
-                  make_uint4(pg[g8 / 2], pg[g8 / 2 + 1], pg[g8 / 2 + 2], pg[g8 / 2 + 3]);
+              if (store_h) {
+                *reinterpret_cast<uint4*>(hrow + j) =
+                    make_uint4(pu[g8 / 2], pu[g8 / 2 + 1], pu[g8 / 2 + 2], pu[g8 / 2 + 3]);
+                *reinterpret_cast<uint4*>(hrow + p.F + j) =
+                    make_uint4(pg[g8 / 2], pg[g8 / 2 + 1], pg[g8 / 2 + 2], pg[g8 / 2 + 3]);
+              }
               *reinterpret_cast<uint4*>(arow + j) = make_uint4(ha[0], ha[1], ha[2], ha[3]);
             } else {
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
                 if (j + e >= p.F) continue;
                 const int sh = (e & 1) * 16;
-                hrow[j + e] = __ushort_as_bfloat16((unsigned short)(pu[g8 / 2 + e / 2] >> sh));
-                hrow[p.F + j + e] = __ushort_as_bfloat16((unsigned short)(pg[g8 / 2 + e / 2] >> sh));
+                if (store_h) {
+                  hrow[j + e] = __ushort_as_bfloat16((unsigned short)(pu[g8 / 2 + e / 2] >> sh));
+                  hrow[p.F + j + e] = __ushort_as_bfloat16((unsigned short)(pg[g8 / 2 + e / 2] >> sh));
+                }
                 arow[j + e] = __ushort_as_bfloat16((unsigned short)(ha[e >> 1] >> sh));
               }
             }
@@ -1448,6 +1471,35 @@ using astrai::GemmParams;
 static unsigned long long* g_gemm_prof = nullptr;
 void gemm_profile_set(unsigned long long* counters) { g_gemm_prof = counters; }
 
+// Programmatic dependent launch of the GEMM kernels (they wait for the previous grid after their
+// prologue: barrier init, TMEM allocation, tensor-map prefetch). Not used for the fused all-gather /
+// reduce-scatter launches, whose peer traffic then starts strictly after the previous kernel.
+// ASTRAI_GEMM_PDL=0 turns it off.
+static bool gemm_pdl() {
+  static const bool on = [] {
+    const char* e = std::getenv("ASTRAI_GEMM_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+template <typename Kern>
+static void launch_gemm_ex(Kern kern, int grid, int threads, int smem, cudaStream_t stream, bool pdl,
+                           const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  astrai::note_launch();
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("astrai gemm: launch failed: ") + cudaGetErrorString(e));
+}
+
 template <int BM, int BN, int A_MN, int B_MN, int OUT_F32>
 static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
                         cudaStream_t stream) {
@@ -1459,7 +1511,8 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BM, BN>::SMEM);
     attr_set[dev & 63] = true;
   }
-  (astrai::note_launch(), kern<<<grid, GemmCfg<BM, BN>::THREADS, GemmCfg<BM, BN>::SMEM, stream>>>(ta, tb, p));
+  const bool pdl = gemm_pdl() && p.npeers == 0 && p.scatter_rpo == 0;
+  launch_gemm_ex(kern, grid, GemmCfg<BM, BN>::THREADS, GemmCfg<BM, BN>::SMEM, stream, pdl, ta, tb, p);
 }
 
 template <int BM, int BN>
@@ -1520,7 +1573,7 @@ static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pr::SMEM);
     attr_set[dev & 63] = true;
   }
-  (astrai::note_launch(), kern<<<2 * pairs, pr::THREADS, pr::SMEM, stream>>>(ta, tb, p));
+  launch_gemm_ex(kern, 2 * pairs, pr::THREADS, pr::SMEM, stream, gemm_pdl(), ta, tb, p);
 }
 
 template <int BN>
@@ -1595,6 +1648,13 @@ static bool use_streamk_pair(long long tiles, int kb, int pairs) {
   if (rem == 0 || tiles < pairs || rem * kb < 4LL * pairs) return false;
   const double whole = (double)(tiles / pairs + 1), split = (double)tiles / pairs + 0.05;
   return (whole - split) * kb >= 8.0;
+}
+// Small grids (fewer 256 x 256 tiles than pairs, e.g. a 2048-token prefill's 2048 x 1536 x 6912 down
+// projection: 48 tiles on 74 pairs): every k-block of every tile is split evenly over all pairs, so
+// each pair runs tiles * kb / pairs k-blocks instead of kb, when that saves at least 16 k-blocks.
+static bool use_streamk_pair_small(long long tiles, int kb, int pairs) {
+  if (tiles <= 0 || pairs <= 0 || tiles >= pairs || tiles * kb < 4LL * pairs) return false;
+  return kb - (double)tiles * kb / pairs >= 16.0;
 }
 static double effective_waves(long long tiles, int kb, int sms) {
   return use_streamk(tiles, kb, sms) ? (double)tiles / sms + 0.08 : (double)((tiles + sms - 1) / sms);
@@ -1727,8 +1787,8 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
     pick_tile(M, N, batch, sms, BM, BN, (K + 63) / 64);
   }
   // 256 x 256 tiles on a CTA pair (force_bn 1024, or the automatic pick under the pair policy)
-  const bool pair = gather == nullptr &&
-                    (force_bn == 1024 || force_bn == 1026 || (force_bn == 0 && M > 128 && N > 128 && pair_on()));
+  const bool pair = gather == nullptr && (force_bn == 1024 || force_bn == 1026 || force_bn == 1027 ||
+                                          (force_bn == 0 && M > 128 && N > 128 && pair_on()));
   if (pair) BM = BN = 256;
 
   CUtensorMap ta, tb;
@@ -1812,8 +1872,16 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
     const int pmax = pair_clusters(dev);
     int pairs = std::min(tiles, pmax);
     const bool split = !sym && (force_bn == 1026 || (force_bn != 1024 && pair_streamk_on() && streamk_on()));
-    if (split && use_streamk_pair(tiles, p.k_blocks, pmax) &&
-        sk_buffers(dev, stream, sms, &p.sk_ws, &p.sk_flags)) {
+    // force_bn 1027: every k-block split over all pairs whatever the shape (needs tiles * kb >= pairs)
+    const bool small = !sym && (force_bn == 1027 ? (long long)tiles * p.k_blocks >= pmax
+                                                 : (force_bn == 0 && streamk_on() &&
+                                                    use_streamk_pair_small(tiles, p.k_blocks, pmax)));
+    if (small && sk_buffers(dev, stream, sms, &p.sk_ws, &p.sk_flags)) {
+      p.dp_tiles = 0;
+      p.sk_units = (long long)tiles * p.k_blocks;
+      pairs = pmax;
+    } else if (split && use_streamk_pair(tiles, p.k_blocks, pmax) &&
+               sk_buffers(dev, stream, sms, &p.sk_ws, &p.sk_flags)) {
       p.dp_tiles = tiles / pmax * pmax;
       p.sk_units = (long long)(tiles - p.dp_tiles) * p.k_blocks;
       pairs = pmax;
@@ -1945,8 +2013,9 @@ void gemm_grouped_bf16(int mode, const void* A, const void* B, void* D, const vo
 
 
 // GEMMs with a fused SwiGLU epilogue (see GemmParams::epi). A is K-major [M, K] (lda).
-//  mode 1: B = packed [up; gate] weight [2F, K] K-major (ldb); writes h [M, 2F] (ldd) and
-//          a = silu(g) * u [M, F] (ldaux). Needs F % 128 == 0 (tiles pair 128 up and 128 gate rows).
+//  mode 1: B = packed [up; gate] weight [2F, K] K-major (ldb); writes h [M, 2F] (ldd; skipped when D
+//          is null) and a = silu(g) * u [M, F] (ldaux). Needs F % 128 == 0 (tiles pair 128 up and 128
+//          gate rows).
 //  mode 2: B = W_down stored [K][F] (b_mn 1) or [F][K] (b_mn 0); with the saved h [M, 2F] (ldh)
 //          writes dh [M, 2F] (ldaux); da = A @ B^T itself is never stored.
 void gemm_swiglu_bf16(int mode, const void* A, long long lda, const void* B, long long ldb, int b_mn, void* D,

@@ -75,6 +75,10 @@ FUSED_EPILOGUES = __import__("os").environ.get("ASTRAI_FUSED_EPILOGUES", "0") ==
 # Still measured slower in the 1.1B step on B200 (613 - 618 vs 586 - 590 ms per optimizer step, two
 # runs each on one box), so it stays opt-in.
 FUSED_SWIGLU = FUSED_EPILOGUES or __import__("os").environ.get("ASTRAI_FUSED_SWIGLU", "0") == "1"
+# Without autograd (prefill, rollouts, evaluation) the SwiGLU GEMM stores only a = silu(g) * u, not
+# h = (u, g): one GEMM replaces the packed up/gate GEMM, the h round trip and the SwiGLU kernel.
+# ASTRAI_INFER_SWIGLU=0 keeps the separate kernels there.
+INFER_SWIGLU = __import__("os").environ.get("ASTRAI_INFER_SWIGLU", "1") == "1"
 
 
 def _skinny(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
@@ -284,7 +288,8 @@ def swiglu_mlp(x: torch.Tensor, up: torch.Tensor, gate: torch.Tensor, down: torc
     """Fused SwiGLU MLP on the kernel path, or None when it does not apply (then compose
     :func:`packed_linear`, :func:`astrai_b200.ops.activation.swiglu` and :func:`linear`)."""
     params = (up, gate, down)
-    if not FUSED_SWIGLU or not PACKING:
+    no_grad = not torch.is_grad_enabled() or not (x.requires_grad or any(p.requires_grad for p in params))
+    if not PACKING or not (INFER_SWIGLU if no_grad else FUSED_SWIGLU):
         return None
     if not (x.is_cuda and x.dtype == torch.bfloat16 and all(
             p.is_cuda and p.dtype == torch.bfloat16 and type(p.data) is torch.Tensor for p in params)):
@@ -292,9 +297,18 @@ def swiglu_mlp(x: torch.Tensor, up: torch.Tensor, gate: torch.Tensor, down: torc
     F_, d = up.shape
     if F_ % 128 or (d * 2) % 16 or down.shape != (d, F_) or x.shape[-1] != d:
         return None
-    if not torch.is_grad_enabled() and x.reshape(-1, d).shape[0] <= SKINNY_MAX_ROWS:
+    if no_grad and x.reshape(-1, d).shape[0] <= SKINNY_MAX_ROWS:
         return None  # decode rows: the skinny kernels stream each weight once
     w_ug = pack_params([up, gate])
+    if no_grad:
+        C = native()
+        x2 = _as_rows(x)
+        a = torch.empty((x2.shape[0], F_), device=x.device, dtype=torch.bfloat16)
+        C.gemm_swiglu(1, x2, w_ug.detach(), None, a, None)
+        out = torch.empty((x2.shape[0], d), device=x.device, dtype=torch.bfloat16)
+        r2 = _as_rows(residual) if residual is not None else None
+        C.gemm(a, down.detach(), out, r2, 0, 0, 1.0, 1.0 if r2 is not None else 0.0, 0)
+        return out.view(*x.shape[:-1], d)
     return _SwiGLUMLPFn.apply(x, w_ug.detach(), down.detach(), residual, 2, up, gate, down)
 
 

@@ -1,6 +1,6 @@
 """Runs each hot kernel of the framework once on a case larger than L2, for profiler captures.
 
-``python -m astrai_b200.utils.kernel_cases [ce rope swiglu embedding router sample decode adamw muon ep]``
+``python -m astrai_b200.utils.kernel_cases [ce rope swiglu gemm_swiglu embedding router sample decode adamw muon ep]``
 (no argument: all of them). One launch per kernel (two for the forward/backward pairs), shapes of
 the 1.1B dense step (8192 tokens, d 2048, FFN 5632, vocab 32000), the MoE layer (64 experts top-6,
 one-rank expert-parallel group) and batch-32 decode over a 4096-token paged cache, so an ``ncu``
@@ -41,6 +41,16 @@ def run(which):
         a = swiglu(h)
         a.backward(torch.randn_like(a))
         del h, a
+    if want("gemm_swiglu"):
+        # the up/gate projection of a 2048-token prefill at d 1536, FFN 6912: the plain GEMM writing
+        # h = (u, g), then the SwiGLU-epilogue GEMM writing only a = silu(g) * u
+        x = torch.randn(2048, 1536, device=dev).to(torch.bfloat16)
+        w = (torch.randn(2 * 6912, 1536, device=dev) * 0.02).to(torch.bfloat16)
+        h = torch.empty(2048, 2 * 6912, device=dev, dtype=torch.bfloat16)
+        a = torch.empty(2048, 6912, device=dev, dtype=torch.bfloat16)
+        C.gemm(x, w, h, None, 0, 0, 1.0, 0.0, 0)
+        C.gemm_swiglu(1, x, w, None, a, None)
+        del x, w, h, a
     if want("embedding"):
         from astrai_b200.ops.embedding import embedding
         w = (torch.randn(32000, 2048, device=dev) * 0.02).to(torch.bfloat16).requires_grad_()

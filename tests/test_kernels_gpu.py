@@ -452,6 +452,55 @@ def test_swiglu_mlp_fused_epilogues(M, d, Fw):
         assert rel_err(t.grad, ref[n]) < 2e-2, n
 
 
+@pytest.mark.parametrize("M,d,Fw", [(128, 256, 384), (300, 512, 1408), (2048, 1536, 6912)])
+@pytest.mark.parametrize("with_res", [False, True])
+def test_swiglu_mlp_forward_only(M, d, Fw, with_res):
+    """Without autograd the SwiGLU GEMM stores only a = silu(g) * u (no h): the MLP under no_grad
+    against an fp32 reference. M > 128 runs the CTA-pair kernel, M = 128 the single-CTA kernel."""
+    import astrai_b200.ops.gemm as G
+    from astrai_b200.ops._ext import native
+    from astrai_b200.ops.gemm import swiglu_mlp
+
+    assert G.INFER_SWIGLU
+    torch.manual_seed(M + d)
+    up, gate = ((torch.randn(Fw, d, device="cuda") * d ** -0.5).to(torch.bfloat16) for _ in range(2))
+    down = (torch.randn(d, Fw, device="cuda") * Fw ** -0.5).to(torch.bfloat16)
+    x = torch.randn(M, d, device="cuda", dtype=torch.bfloat16)
+    res = torch.randn(M, d, device="cuda", dtype=torch.bfloat16) if with_res else None
+    with torch.no_grad():
+        y = swiglu_mlp(x, up, gate, down, res)
+    assert y is not None and y.shape == (M, d)
+    xf = x.float()
+    a = (xf @ up.float().T) * F.silu(xf @ gate.float().T)
+    yf = a.to(torch.bfloat16).float() @ down.float().T + (res.float() if with_res else 0.0)
+    assert rel_err(y, yf) < 1e-2
+    assert native().read_error() == 0
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 1)])
+@pytest.mark.parametrize("M,N,K,fb", [(2048, 1536, 6912, 0), (2048, 1536, 1536, 1027), (1000, 704, 3000, 1027)])
+def test_gemm_cta_pair_streamk_small_grid(a_mn, b_mn, M, N, K, fb):
+    """Fewer 256 x 256 tiles than CTA pairs: every k-block of every tile split evenly over all pairs
+    (automatic for 2048 x 1536 x 6912, forced with force_bn 1027 otherwise), against an fp32 matmul
+    and the unsplit pair kernel; twice, so the fix-up flags reset between launches."""
+    from astrai_b200.ops._ext import native
+
+    torch.manual_seed(5)
+    a = torch.randn((K, M) if a_mn else (M, K), device="cuda", dtype=torch.bfloat16)
+    b = torch.randn((K, N) if b_mn else (N, K), device="cuda", dtype=torch.bfloat16)
+    A = a.float().t() if a_mn else a.float()
+    B = b.float() if b_mn else b.float().t()
+    ref = A @ B
+    whole = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    native().gemm(a, b, whole, None, a_mn, b_mn, 1.0, 0.0, 1024)
+    for _ in range(2):
+        d = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        native().gemm(a, b, d, None, a_mn, b_mn, 1.0, 0.0, fb)
+        assert rel_err(d, ref) < 1e-2
+        assert rel_err(d, whole.float()) < 1e-2
+    assert native().read_error() == 0
+
+
 @pytest.mark.parametrize("with_pos", [False, True])
 def test_qkv_projection_with_rope_epilogue(with_pos):
     """RoPE applied in the QKV projection epilogue + attention on pre-rotated q/k equals the
