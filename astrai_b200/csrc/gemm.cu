@@ -105,7 +105,9 @@ struct GemmParams {
   long long rank_delta[kMaxGatherPeers + 1];
   // Symmetric output (sym != 0; M == N, D known to equal D^T, e.g. X X^T or A A with A symmetric):
   // tiles lying entirely below the diagonal (every column < every row; tiles of sym_bm x sym_bn) are
-  // skipped, and sym_mirror_kernel copies the transpose of the upper triangle into them afterwards.
+  // not computed, and sym_mirror_kernel copies the transpose of the upper triangle into them
+  // afterwards. sym 2 (square tiles): the tile index space holds only the upper tiles (gemm_tile);
+  // sym 1: the walk skips the lower ones.
   int sym, sym_bm, sym_bn;
 };
 
@@ -205,7 +207,7 @@ struct WorkIter {
   }
   __device__ __forceinline__ bool next(const GemmParams& p, int num_tiles, int kblk_full, WorkItem& w) {
     const int limit = p.sk_units > 0 ? p.dp_tiles : num_tiles;
-    if (p.group_tile || p.sym)
+    if (p.group_tile || p.sym == 1)
       while (t < limit && tile_skipped(p, t)) t += cnt;
     if (t < limit) {
       w = {t, 0, kblk_full, -1, 0, true, false};
@@ -319,6 +321,28 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
   nb = r / gsize;
 }
 
+// Symmetric output on square tiles (sym == 2): only the tiles on or above the diagonal exist in the
+// tile index space, column by column (column nb holds rows 0 .. nb), so every worker's share of the
+// walk is live work; 1-tile-wide columns keep each B tile hot in L2 across its column.
+__device__ __forceinline__ int sym_tiles(int T) { return T * (T + 1) / 2; }
+__device__ __forceinline__ void gemm_tile(const GemmParams& p, int tile, int& b, int& mb, int& nb) {
+  if (p.sym == 2) {
+    const int per = sym_tiles(p.tiles_m);
+    b = tile / per;
+    const int r = tile - b * per;
+    int c = (int)((sqrtf(8.f * (float)r + 1.f) - 1.f) * 0.5f);
+    while ((c + 1) * (c + 2) / 2 <= r) ++c;
+    while (c * (c + 1) / 2 > r) --c;
+    nb = c;
+    mb = r - c * (c + 1) / 2;
+    return;
+  }
+  tile_coords(tile, p.tiles_m, p.tiles_n, b, mb, nb);
+}
+__device__ __forceinline__ int gemm_num_tiles(const GemmParams& p) {
+  return p.batch * (p.sym == 2 ? sym_tiles(p.tiles_m) : p.tiles_m * p.tiles_n);
+}
+
 __device__ __forceinline__ bool tile_skipped(const GemmParams& p, int tile) {
   int b, mb, nb;
   tile_coords(tile, p.tiles_m, p.tiles_n, b, mb, nb);
@@ -345,6 +369,61 @@ __global__ void sym_mirror_kernel(T* __restrict__ D, int M, long long ldd, long 
   for (int r = ty; r < 32; r += blockDim.y) {
     const int row = bi * 32 + r, col = bj * 32 + tx;
     if (row < M && col < M && row > col) d[(long long)row * ldd + col] = tile[tx][r];
+  }
+}
+
+// bf16 version on 64 x 64 blocks, one CTA per block (bi, bj) with bi >= bj (blockIdx.x enumerates
+// them row by row; blockIdx.y is the batch): the source block (bj, bi) is read with 16-byte row loads
+// into shared memory (33-word row pitch: conflict-free stores) and written transposed with 16-byte
+// stores, eight threads per 128-byte output row, so a warp stores four whole rows. Diagonal blocks
+// and blocks cut by M take an element-wise path that writes only below the diagonal.
+__global__ void __launch_bounds__(256) sym_mirror64_kernel(__nv_bfloat16* __restrict__ D, int M, long long ldd,
+                                                          long long strideD) {
+  __shared__ uint32_t tile[64 * 33];
+  const int r = blockIdx.x;
+  int bi = (int)((sqrtf(8.f * (float)r + 1.f) - 1.f) * 0.5f);  // r = bi (bi + 1) / 2 + bj, 0 <= bj <= bi
+  while (bi * (bi + 1) / 2 > r) --bi;
+  while ((bi + 1) * (bi + 2) / 2 <= r) ++bi;
+  const int bj = r - bi * (bi + 1) / 2;
+  const int i0 = bi * 64, j0 = bj * 64;
+  __nv_bfloat16* d = D + (long long)blockIdx.y * strideD;
+  const int tid = threadIdx.x;
+  if (bi != bj && i0 + 64 <= M) {
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+      const int q = tid + 256 * it, rr = q >> 3, k = q & 7;
+      const uint4 v = *reinterpret_cast<const uint4*>(d + (long long)(j0 + rr) * ldd + i0 + 8 * k);
+      uint32_t* t = tile + rr * 33 + 4 * k;
+      t[0] = v.x;
+      t[1] = v.y;
+      t[2] = v.z;
+      t[3] = v.w;
+    }
+    __syncthreads();
+    const unsigned short* th = reinterpret_cast<const unsigned short*>(tile);
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+      const int q = tid + 256 * it, c = q >> 3, k = q & 7;
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t lo = th[(8 * k + 2 * e) * 66 + c], hi = th[(8 * k + 2 * e + 1) * 66 + c];
+        w[e] = lo | (hi << 16);
+      }
+      *reinterpret_cast<uint4*>(d + (long long)(i0 + c) * ldd + j0 + 8 * k) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    return;
+  }
+  __nv_bfloat16* th = reinterpret_cast<__nv_bfloat16*>(tile);
+  for (int idx = tid; idx < 64 * 64; idx += 256) {
+    const int rr = idx >> 6, cc = idx & 63;
+    if (j0 + rr < M && i0 + cc < M) th[rr * 66 + cc] = d[(long long)(j0 + rr) * ldd + i0 + cc];
+  }
+  __syncthreads();
+  for (int idx = tid; idx < 64 * 64; idx += 256) {
+    const int c = idx >> 6, rc = idx & 63;
+    const int row = i0 + c, col = j0 + rc;
+    if (row < M && col < M && row > col) d[(long long)row * ldd + col] = th[rc * 66 + c];
   }
 }
 
@@ -389,7 +468,7 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
   pdl_wait();  // the previous grid has completed and its writes are visible
 
-  const int num_tiles = p.batch * p.tiles_m * p.tiles_n;
+  const int num_tiles = gemm_num_tiles(p);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -403,7 +482,7 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
       while (ok && wi.next(p, num_tiles, p.k_blocks, w)) {
         const int tile = w.tile;
         int b, mb, nb;
-        tile_coords(tile, p.tiles_m, p.tiles_n, b, mb, nb);
+        gemm_tile(p, tile, b, mb, nb);
         const int m0 = mb * BM, n0 = nb * BN;
         const TileK tk = tile_k(p, b, mb, BK);
         const int kbeg = w.sk >= 0 ? w.kb0 : 0, kend = w.sk >= 0 ? w.kb1 : tk.kblk;
@@ -460,7 +539,7 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
       while (ok && wi.next(p, num_tiles, p.k_blocks, w)) {
         const int tile = w.tile;
         int b, mb, nb;
-        tile_coords(tile, p.tiles_m, p.tiles_n, b, mb, nb);
+        gemm_tile(p, tile, b, mb, nb);
         const int kblk = tile_k(p, b, mb, BK).kblk;
         const int kbeg = w.sk >= 0 ? w.kb0 : 0, kend = w.sk >= 0 ? w.kb1 : kblk;
         const long long ta0 = p.prof ? clock64() : 0;
@@ -519,7 +598,7 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
     while (wi.next(p, num_tiles, p.k_blocks, w)) {
       const int tile = w.tile;
       int b, mb, nb;
-      tile_coords(tile, p.tiles_m, p.tiles_n, b, mb, nb);
+      gemm_tile(p, tile, b, mb, nb);
       const long long te0 = (p.prof && lane == 0) ? clock64() : 0;
       const bool got_full = mbar_wait(&acc_full[acc], acc_phase, p.err, kErrWaitAccFull);
       if (p.prof && lane == 0 && warp == 2) atomicAdd(p.prof + 3, (unsigned long long)(clock64() - te0));
@@ -1071,7 +1150,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   pdl_wait();
-  const int num_tiles = p.batch * p.tiles_m * p.tiles_n;
+  const int num_tiles = gemm_num_tiles(p);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1084,7 +1163,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS
       WorkItem w;
       while (ok && wi.next(p, num_tiles, p.k_blocks, w)) {
         int b, mb, nb;
-        tile_coords(w.tile, p.tiles_m, p.tiles_n, b, mb, nb);
+        gemm_tile(p, w.tile, b, mb, nb);
         const int m0 = mb * 256 + (int)rank * 128;
         // epi 1 (SwiGLU forward): the even CTA stages up rows, the odd one the gate rows of the same
         // BNH output columns, so each accumulator holds u in columns [0, BNH) and g in [BNH, BN)
@@ -1179,7 +1258,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS
     WorkItem w;
     while (wi.next(p, num_tiles, p.k_blocks, w)) {
       int b, mb, nb;
-      tile_coords(w.tile, p.tiles_m, p.tiles_n, b, mb, nb);
+      gemm_tile(p, w.tile, b, mb, nb);
       if (!mbar_wait(&acc_full[acc], acc_phase, p.err, kErrWaitAccFull)) break;
       tc_fence_after();
       if (w.partial) {
@@ -1260,45 +1339,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS
       const OutT* crow =
           use_c ? reinterpret_cast<const OutT*>(p.C) + (long long)b * p.strideC + (long long)row * p.ldc : nullptr;
       if (p.epi == 1) {
-        // SwiGLU forward: h = (u, g) and a = silu(g) * u for output columns j0 .. j0 + BNH / 2
+        // SwiGLU forward: h = (u, g) and a = silu(g) * u for output columns j0 .. j0 + BNH / 2, 32
+        // columns at a time straight from TMEM (only one chunk's u and g live in registers; the
+        // accumulator is handed back after the last chunk's loads, as in the plain epilogue)
         constexpr int PER = BNH / 2;
         const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
-        uint32_t pu[PER / 2], pg[PER / 2];
-#pragma unroll
+        const int j0 = nb * BNH + cpart * PER;
+        const bool store_h = p.D != nullptr;  // h = (u, g) is kept for the backward only
+        __nv_bfloat16* hrow = reinterpret_cast<__nv_bfloat16*>(p.D) + (long long)row * p.ldd;
+        __nv_bfloat16* arow = p.aux + (long long)row * p.ldaux;
+#pragma unroll 1
         for (int c = 0; c < PER; c += 32) {
           uint32_t ru[32], rg[32];
           tmem_ld32(t_row + cpart * PER + c, ru);
           tmem_ld32(t_row + BNH + cpart * PER + c, rg);
           tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            pu[c / 2 + e] = pack_bf16(__uint_as_float(ru[2 * e]), __uint_as_float(ru[2 * e + 1]));
-            pg[c / 2 + e] = pack_bf16(__uint_as_float(rg[2 * e]), __uint_as_float(rg[2 * e + 1]));
+          if (c + 32 >= PER) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc ? empty_bar1 : empty_bar0);
           }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(acc ? empty_bar1 : empty_bar0);
-        if (row_ok) {
-          const int j0 = nb * BNH + cpart * PER;
-          const bool store_h = p.D != nullptr;  // h = (u, g) is kept for the backward only
-          __nv_bfloat16* hrow = reinterpret_cast<__nv_bfloat16*>(p.D) + (long long)row * p.ldd;
-          __nv_bfloat16* arow = p.aux + (long long)row * p.ldaux;
+          if (!row_ok) continue;
 #pragma unroll
-          for (int g8 = 0; g8 < PER; g8 += 8) {
-            const int j = j0 + g8;
-            uint32_t ha[4];
+          for (int g8 = 0; g8 < 32; g8 += 8) {
+            const int j = j0 + c + g8;
+            uint32_t pu[4], pg[4], ha[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const float2 ub = unpack_bf16(pu[g8 / 2 + e]), gb = unpack_bf16(pg[g8 / 2 + e]);
+              // rounded to bf16 first: the values the separate SwiGLU kernel would read from h
+              pu[e] = pack_bf16(__uint_as_float(ru[g8 + 2 * e]), __uint_as_float(ru[g8 + 2 * e + 1]));
+              pg[e] = pack_bf16(__uint_as_float(rg[g8 + 2 * e]), __uint_as_float(rg[g8 + 2 * e + 1]));
+              const float2 ub = unpack_bf16(pu[e]), gb = unpack_bf16(pg[e]);
               ha[e] = pack_bf16(ub.x * gb.x * sigmoid_f(gb.x), ub.y * gb.y * sigmoid_f(gb.y));
             }
             if (j + 8 <= p.F && p.vec_ok) {
               if (store_h) {
-                *reinterpret_cast<uint4*>(hrow + j) =
-                    make_uint4(pu[g8 / 2], pu[g8 / 2 + 1], pu[g8 / 2 + 2], pu[g8 / 2 + 3]);
-                *reinterpret_cast<uint4*>(hrow + p.F + j) =
-                    make_uint4(pg[g8 / 2], pg[g8 / 2 + 1], pg[g8 / 2 + 2], pg[g8 / 2 + 3]);
+                *reinterpret_cast<uint4*>(hrow + j) = make_uint4(pu[0], pu[1], pu[2], pu[3]);
+                *reinterpret_cast<uint4*>(hrow + p.F + j) = make_uint4(pg[0], pg[1], pg[2], pg[3]);
               }
               *reinterpret_cast<uint4*>(arow + j) = make_uint4(ha[0], ha[1], ha[2], ha[3]);
             } else {
@@ -1307,8 +1384,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS
                 if (j + e >= p.F) continue;
                 const int sh = (e & 1) * 16;
                 if (store_h) {
-                  hrow[j + e] = __ushort_as_bfloat16((unsigned short)(pu[g8 / 2 + e / 2] >> sh));
-                  hrow[p.F + j + e] = __ushort_as_bfloat16((unsigned short)(pg[g8 / 2 + e / 2] >> sh));
+                  hrow[j + e] = __ushort_as_bfloat16((unsigned short)(pu[e >> 1] >> sh));
+                  hrow[p.F + j + e] = __ushort_as_bfloat16((unsigned short)(pg[e >> 1] >> sh));
                 }
                 arow[j + e] = __ushort_as_bfloat16((unsigned short)(ha[e >> 1] >> sh));
               }
@@ -1760,13 +1837,18 @@ void gemm_plan(int M, int N, int K, int batch, int* out) {
 }
 
 static void sym_mirror(void* D, int out_f32, int M, long long ldd, long long strideD, int batch, cudaStream_t s) {
-  const int nb = (M + 31) / 32;
-  const dim3 grid(nb, nb, batch), block(32, 8);
-  if (out_f32)
+  if (out_f32) {
+    const int nb = (M + 31) / 32;
+    const dim3 grid(nb, nb, batch), block(32, 8);
     (astrai::note_launch(), astrai::sym_mirror_kernel<float><<<grid, block, 0, s>>>(static_cast<float*>(D), M, ldd, strideD));
-  else
-    (astrai::note_launch(), astrai::sym_mirror_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(static_cast<__nv_bfloat16*>(D), M,
-                                                                                    ldd, strideD));
+    return;
+  }
+  // 64 x 64 blocks on or below the diagonal; 16-byte vectors need 16-byte rows (the GEMM checks ldd)
+  const int t64 = (M + 63) / 64;
+  if ((ldd * 2) % 16 || (reinterpret_cast<uintptr_t>(D) % 16) || (batch > 1 && (strideD * 2) % 16) || batch > 65535)
+    throw std::runtime_error("astrai gemm: symmetric output needs 16-byte aligned rows and batch <= 65535");
+  const dim3 grid(t64 * (t64 + 1) / 2, batch);
+  (astrai::note_launch(), astrai::sym_mirror64_kernel<<<grid, 256, 0, s>>>(static_cast<__nv_bfloat16*>(D), M, ldd, strideD));
 }
 
 void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int N, int K, int batch, int a_mn,
@@ -1862,11 +1944,14 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
   p.sym = 0;
   p.sym_bm = 1;
   p.sym_bn = 1;
-  const int tiles = batch * p.tiles_m * p.tiles_n;
+  int tiles = batch * p.tiles_m * p.tiles_n;
   if (sym) {
-    p.sym = 1;
+    // square tiles: the tile walk enumerates the upper triangle only (gemm_tile); otherwise the
+    // walk skips the tiles below the diagonal
+    p.sym = BM == BN ? 2 : 1;
     p.sym_bm = BM;
     p.sym_bn = BN;
+    if (p.sym == 2) tiles = batch * (p.tiles_m * (p.tiles_m + 1) / 2);
   }
   if (pair) {
     const int pmax = pair_clusters(dev);

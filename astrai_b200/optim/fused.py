@@ -235,13 +235,12 @@ def newton_schulz_batched(X: torch.Tensor, steps: int = 5, coeffs=NS_COEFFS, wor
                 torch.empty(Bn, m, m, device=X.device, dtype=X.dtype))
     Y, A, Bm = work
     cur, nxt = X, Y
-    # A = X X^T is symmetric: for wide X (n >= 4 m, a long reduction per tile) only the tiles on or
-    # above the diagonal are computed, then mirrored. Measured on B200 (24 matrices, 5 steps): 2048 x
-    # 11264 17.0 vs 19.1 ms; for n <= 2.75 m the uneven tile walk cost more than the skipped tiles saved
-    sym = NS_SYM and n >= 4 * m
+    # A = X X^T and Bm = c A A + b A are symmetric: only the tiles on or above the diagonal are
+    # computed (the tile walk enumerates just those), then the lower triangle is mirrored in
+    sym = NS_SYM
     for _ in range(steps):
         C.gemm(cur, cur, A, None, 0, 0, 1.0, 0.0, 0, sym)           # A = X X^T
-        C.gemm(A, A, Bm, A, 0, 0, c, b, 0)                          # Bm = c A A + b A
+        C.gemm(A, A, Bm, A, 0, 0, c, b, 0, sym)                     # Bm = c A A + b A
         C.gemm(Bm, cur, nxt, cur, 0, 1, 1.0, a, 0)                  # X' = Bm X + a X
         cur, nxt = nxt, cur
     return cur

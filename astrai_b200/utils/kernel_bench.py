@@ -1,6 +1,6 @@
 """Device-timed micro-benchmarks of the framework's kernels.
 
-    python -m astrai_b200.utils.kernel_bench [gemm [case]|attn|norm|skinny|sample|all]
+    python -m astrai_b200.utils.kernel_bench [gemm [case]|gemm_shapes|swiglu_gemm|ns|attn|norm|skinny|sample|decode|prefill|all]
     torchrun --nproc-per-node N -m astrai_b200.utils.kernel_bench allreduce|ep|tpgather|tprow
 
 Each case is timed with CUDA events on the launching stream after warm-up,
@@ -638,7 +638,8 @@ def bench_prefill():
 
 def bench_ns():
     """Muon's batched Newton-Schulz chain (5 steps) on the 1.1B model's matrix groups (24 of each),
-    with the symmetric-output rule on (``ms_sym``: X X^T on its upper triangle for n >= 4 m) and off."""
+    with the symmetric-output GEMMs on (``ms_sym``: X X^T and c A A + b A computed on their upper
+    triangle, then mirrored) and off."""
     import astrai_b200.optim.fused as F
 
     _, tf, src = peaks()
@@ -656,6 +657,51 @@ def bench_ns():
         print(json.dumps({"kernel": "newton_schulz_batched", "batch": 24, "m": m, "n": n, "ms_sym": res["sym"],
                           "ms_full": res["full"], "tflops_full": round(flops / res["full"] / 1e9, 1),
                           "peak_src": src}))
+
+
+def bench_swiglu_gemm():
+    """The up/gate projection with its SwiGLU: the plain GEMM writing h = (u, g) and the separate
+    SwiGLU kernel, against the SwiGLU-epilogue GEMM writing h and a (training) or only a (no
+    autograd); at a 2048-token prefill of d 1536 / FFN 6912 and the 1.1B step's 8192 x 2048 / 5632.
+    Warm (back to back) and with L2 flushed before every call, us per call."""
+    from astrai_b200.ops._ext import native
+    from astrai_b200.ops.activation import swiglu
+
+    C = native()
+    for M, d, F in ((2048, 1536, 6912), (8192, 2048, 5632)):
+        x = torch.randn(M, d, device="cuda").to(torch.bfloat16)
+        w = (torch.randn(2 * F, d, device="cuda") * 0.02).to(torch.bfloat16)
+        h = torch.empty(M, 2 * F, device="cuda", dtype=torch.bfloat16)
+        a = torch.empty(M, F, device="cuda", dtype=torch.bfloat16)
+        fns = {"gemm": lambda: C.gemm(x, w, h, None, 0, 0, 1.0, 0.0, 0),
+               "swiglu_kernel": lambda: swiglu(h),
+               "fused_h_and_a": lambda: C.gemm_swiglu(1, x, w, h, a, None),
+               "fused_a_only": lambda: C.gemm_swiglu(1, x, w, None, a, None)}
+        res = {k: [round(time_fn(f, 5, 30) * 1e3, 1), round(time_flushed(f, 3, 20) * 1e3, 1)] for k, f in fns.items()}
+        print(json.dumps({"kernel": "gemm_swiglu", "M": M, "d": d, "F": F, "us_warm_flushed": res}))
+
+
+def bench_gemm_shapes():
+    """Tile plans on the GEMMs of a 2048-token prefill (d 1536, 24/4 heads of 64, FFN 6912, vocab
+    10000) and of the 1.1B step, L2 flushed before every call (us): automatic plan (0), CTA pairs
+    unsplit (1024), pairs with the last-wave split (1026), pairs with every k-block split (1027),
+    single CTA 128 x 256 (256), cuBLAS."""
+    from astrai_b200.ops._ext import native
+
+    C = native()
+    shapes = [(2048, 2048, 1536, "qkv"), (2048, 1536, 1536, "o"), (2048, 13824, 1536, "upgate"),
+              (2048, 1536, 6912, "down"), (2048, 10000, 1536, "lm_head"), (8192, 3072, 2048, "step_qkv"),
+              (8192, 2048, 2048, "step_o"), (8192, 11264, 2048, "step_upgate"), (8192, 2048, 5632, "step_down"),
+              (8192, 32000, 2048, "step_lm_head")]
+    for M, N, K, name in shapes:
+        a = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+        b = torch.randn(N, K, device="cuda").to(torch.bfloat16)
+        d = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        res = {}
+        for fb in (0, 1024, 1026, 1027, 256):
+            res[str(fb)] = round(time_flushed(lambda: C.gemm(a, b, d, None, 0, 0, 1.0, 0.0, fb), 3, 20) * 1e3, 1)
+        res["cublas"] = round(time_flushed(lambda: torch.matmul(a, b.t()), 3, 20) * 1e3, 1)
+        print(json.dumps({"kernel": "gemm", "case": name, "M": M, "N": N, "K": K, "us": res}))
 
 
 def bench_norm(rows: int = 8192, D: int = 2048):
@@ -712,6 +758,10 @@ def main(argv=None):
         bench_prefill()
     if which in ("ns", "all"):
         bench_ns()
+    if which in ("swiglu_gemm", "all"):
+        bench_swiglu_gemm()
+    if which in ("gemm_shapes", "all"):
+        bench_gemm_shapes()
     if which in ("gemm", "all"):
         bench_gemm(args[1] if which == "gemm" and len(args) > 1 else None)
     if which in ("norm", "all"):

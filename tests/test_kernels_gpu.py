@@ -107,11 +107,13 @@ def test_gemm_cta_pair(a_mn, b_mn, M, N, K, batch):
     assert native().read_error() == 0
 
 
-@pytest.mark.parametrize("force_bn", [0, 1024, 256])
-@pytest.mark.parametrize("m,n,batch", [(256, 512, 1), (304, 200, 2), (2048, 1536, 3)])
+@pytest.mark.parametrize("force_bn", [0, 1024, 512, 256])
+@pytest.mark.parametrize("m,n,batch", [(256, 512, 1), (304, 200, 2), (1296, 704, 2), (2048, 1536, 3)])
 def test_gemm_symmetric_output(force_bn, m, n, batch):
-    """sym=True (Newton-Schulz's X X^T and c A A + b A): tiles below the diagonal are skipped and the
-    lower triangle is the mirror of the upper one; the result equals the full product."""
+    """sym=True (Newton-Schulz's X X^T and c A A + b A): tiles below the diagonal are not computed
+    (square tiles: the walk enumerates the upper triangle, force_bn 0 / 1024 on CTA pairs, 512 on one
+    CTA; 128 x 256 tiles: the walk skips the lower ones) and the lower triangle is the mirror of the
+    upper one; the result equals the full product."""
     from astrai_b200.ops._ext import native
     from astrai_b200.ops.gemm import gemm_reference
 
