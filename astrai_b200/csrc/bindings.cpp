@@ -320,7 +320,9 @@ void rope_(at::Tensor& x, int64_t col0, int64_t n_heads, int64_t head_dim, const
            int64_t seq_len, const at::Tensor& cs, bool inverse, int64_t rot_dim, int64_t rot_off) {
   check_bf16(x, "x");
   check_rows(x, "x");
-  TORCH_CHECK(cs.scalar_type() == at::kFloat && cs.is_contiguous() && cs.is_cuda(), "cos/sin table");
+  TORCH_CHECK(cs.scalar_type() == at::kFloat && cs.is_contiguous() && cs.is_cuda() &&
+                  reinterpret_cast<uintptr_t>(cs.data_ptr()) % 16 == 0,
+              "cos/sin table: contiguous CUDA fp32, 16-byte aligned (the kernel reads it as float4)");
   TORCH_CHECK(rot_dim % 8 == 0 && (col0 + rot_off) % 8 == 0 && head_dim % 8 == 0, "rope: alignment");
   const int* p = nullptr;
   if (pos.has_value() && pos->defined()) {

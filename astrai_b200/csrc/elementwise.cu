@@ -8,6 +8,8 @@
 // of the fused QKV projection output (any row stride), so no copy of q or k
 // is ever made. Backward is the same kernel with the rotation negated.
 // SwiGLU parity: astrai/model/components/mlp.py:22-25 (up * silu(gate)).
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace astrai {
@@ -21,37 +23,60 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ x, long long ld, int row
   // a kernel launched after this one with programmatic dependent launch may start now (it waits for
   // this grid to finish before reading what it writes)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  // each thread handles 8 consecutive elements (4 pairs) of one head
-  const int per_head = rot_dim / 8;
-  const long long total = (long long)rows * n_heads * per_head;
-  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
-       idx += (long long)gridDim.x * blockDim.x) {
-    const int chunk = idx % per_head;
-    const long long t = idx / per_head;
-    const int h = t % n_heads;
-    const int row = t / n_heads;
-    const int p = pos ? pos[row] : row % seq_len;
-    if (p < 0 || p >= max_pos) {
-      set_error(err, kErrBadArg);
-      continue;
-    }
-    __nv_bfloat16* ptr = x + (long long)row * ld + col0 + h * head_dim + rot_off + chunk * 8;
-    uint4 u = *reinterpret_cast<uint4*>(ptr);
-    uint32_t w[4] = {u.x, u.y, u.z, u.w};
-    const float2* c = cs + (long long)p * (rot_dim / 2) + chunk * 4;
+  // Row-walking: block b takes rows b, b + gridDim.x, ... two at a time (both rows' loads issued
+  // before the math); thread k owns the 8-element chunks k, k + blockDim.x, ... of a row's
+  // n_heads * rot_dim / 8, whose head and offsets are computed once; a row's position is read once.
+  const int per_head = rot_dim / 8, nchunk = n_heads * per_head, T = blockDim.x;
+  for (int k = threadIdx.x; k < nchunk; k += T) {
+    const int h = k / per_head, chunk = k - h * per_head;
+    const int coff = col0 + h * head_dim + rot_off + chunk * 8;
+    for (int row = blockIdx.x; row < rows; row += 2 * gridDim.x) {
+      const int rr[2] = {row, row + (int)gridDim.x};
+      int p[2];
+      uint4 u[2];
+      float4 c[2][2];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float2 v = unpack_bf16(w[j]);
-      float2 r = c[j];
-      const float sn = sign * r.y;
-      w[j] = pack_bf16(v.x * r.x - v.y * sn, v.x * sn + v.y * r.x);
+      for (int q = 0; q < 2; ++q) {
+        p[q] = -1;
+        if (rr[q] >= rows) continue;
+        p[q] = pos ? pos[rr[q]] : rr[q] % seq_len;
+        if (p[q] < 0 || p[q] >= max_pos) {
+          set_error(err, kErrBadArg);
+          p[q] = -1;
+          continue;
+        }
+        u[q] = *reinterpret_cast<const uint4*>(x + (long long)rr[q] * ld + coff);
+        const float4* cp = reinterpret_cast<const float4*>(cs + (long long)p[q] * (rot_dim / 2) + chunk * 4);
+        c[q][0] = cp[0];
+        c[q][1] = cp[1];
+      }
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        if (p[q] < 0) continue;
+        uint32_t w[4] = {u[q].x, u[q].y, u[q].z, u[q].w};
+        const float2 r4[4] = {make_float2(c[q][0].x, c[q][0].y), make_float2(c[q][0].z, c[q][0].w),
+                              make_float2(c[q][1].x, c[q][1].y), make_float2(c[q][1].z, c[q][1].w)};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 v = unpack_bf16(w[j]);
+          const float sn = sign * r4[j].y;
+          w[j] = pack_bf16(v.x * r4[j].x - v.y * sn, v.x * sn + v.y * r4[j].x);
+        }
+        *reinterpret_cast<uint4*>(x + (long long)rr[q] * ld + coff) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
     }
-    *reinterpret_cast<uint4*>(ptr) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
-__device__ __forceinline__ float silu_f(float g) { return g / (1.f + __expf(-g)); }
+// silu / sigmoid with the fast division (__fdividef: at most 2 ulp from the quotient for
+// denominators below 2^126; above, i.e. g < -87, it returns 0, where the quotient is below 1e-37):
+// invisible after the bf16 rounding of every output, and a tenth of the IEEE division's instructions
+__device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.f + __expf(-g)); }
+__device__ __forceinline__ float sigm_f(float g) { return __fdividef(1.f, 1.f + __expf(-g)); }
 
+// Row-walking layout of the SwiGLU kernels: block b takes rows b, b + gridDim.x, ...; its threads
+// cover the row's F / 8 16-byte chunks, two per thread per pass (both loads issued before the math),
+// so no index division is needed and two chunks' loads are in flight per thread.
 // h: [rows, ldh] with up = h[:, 0:F], gate = h[:, F:2F];  out: [rows, ldo]
 // live_rows (optional device count): only the first *live_rows of the `rows` rows hold data (an expert
 // block sized for its capacity); the rest are left untouched.
@@ -60,21 +85,33 @@ __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ h, long long
   // a kernel launched after this one with programmatic dependent launch may start now (it waits for
   // this grid to finish before reading what it writes)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  const int per_row = F / 8;
-  const long long total = (long long)(live_rows ? min(rows, max(0, *live_rows)) : rows) * per_row;
-  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
-       idx += (long long)gridDim.x * blockDim.x) {
-    const int row = idx / per_row;
-    const int c = (idx % per_row) * 8;
-    const uint4 uu = *reinterpret_cast<const uint4*>(h + (long long)row * ldh + c);
-    const uint4 gg = *reinterpret_cast<const uint4*>(h + (long long)row * ldh + F + c);
-    uint32_t u[4] = {uu.x, uu.y, uu.z, uu.w}, g[4] = {gg.x, gg.y, gg.z, gg.w}, o[4];
+  const int per_row = F / 8, T = blockDim.x;
+  const int nrows = live_rows ? min(rows, max(0, *live_rows)) : rows;
+  for (int row = blockIdx.x; row < nrows; row += gridDim.x) {
+    const __nv_bfloat16* hr = h + (long long)row * ldh;
+    __nv_bfloat16* orow = out + (long long)row * ldo;
+    for (int c0 = threadIdx.x; c0 < per_row; c0 += 2 * T) {
+      uint4 uu[2], gg[2];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float2 a = unpack_bf16(u[j]), b = unpack_bf16(g[j]);
-      o[j] = pack_bf16(a.x * silu_f(b.x), a.y * silu_f(b.y));
+      for (int k = 0; k < 2; ++k) {
+        const int c = (c0 + k * T) * 8;
+        const bool ok = c0 + k * T < per_row;
+        uu[k] = ok ? *reinterpret_cast<const uint4*>(hr + c) : make_uint4(0u, 0u, 0u, 0u);
+        gg[k] = ok ? *reinterpret_cast<const uint4*>(hr + F + c) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        if (c0 + k * T >= per_row) break;
+        const uint32_t u[4] = {uu[k].x, uu[k].y, uu[k].z, uu[k].w}, g[4] = {gg[k].x, gg[k].y, gg[k].z, gg[k].w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 a = unpack_bf16(u[j]), b = unpack_bf16(g[j]);
+          o[j] = pack_bf16(a.x * silu_f(b.x), a.y * silu_f(b.y));
+        }
+        *reinterpret_cast<uint4*>(orow + (c0 + k * T) * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
     }
-    *reinterpret_cast<uint4*>(out + (long long)row * ldo + c) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -82,26 +119,41 @@ __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ h, long long
 __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dy, long long lddy,
                                   const __nv_bfloat16* __restrict__ h, long long ldh, __nv_bfloat16* __restrict__ dh,
                                   long long lddh, int rows, int F, const int* __restrict__ live_rows) {
-  const int per_row = F / 8;
-  const long long total = (long long)(live_rows ? min(rows, max(0, *live_rows)) : rows) * per_row;
-  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
-       idx += (long long)gridDim.x * blockDim.x) {
-    const int row = idx / per_row;
-    const int c = (idx % per_row) * 8;
-    const uint4 uu = *reinterpret_cast<const uint4*>(h + (long long)row * ldh + c);
-    const uint4 gg = *reinterpret_cast<const uint4*>(h + (long long)row * ldh + F + c);
-    const uint4 dd = *reinterpret_cast<const uint4*>(dy + (long long)row * lddy + c);
-    uint32_t u[4] = {uu.x, uu.y, uu.z, uu.w}, g[4] = {gg.x, gg.y, gg.z, gg.w}, d[4] = {dd.x, dd.y, dd.z, dd.w};
-    uint32_t du[4], dg[4];
+  const int per_row = F / 8, T = blockDim.x;
+  const int nrows = live_rows ? min(rows, max(0, *live_rows)) : rows;
+  for (int row = blockIdx.x; row < nrows; row += gridDim.x) {
+    const __nv_bfloat16* hr = h + (long long)row * ldh;
+    const __nv_bfloat16* dr = dy + (long long)row * lddy;
+    __nv_bfloat16* dhr = dh + (long long)row * lddh;
+    for (int c0 = threadIdx.x; c0 < per_row; c0 += 2 * T) {
+      uint4 uu[2], gg[2], dd[2];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float2 a = unpack_bf16(u[j]), b = unpack_bf16(g[j]), e = unpack_bf16(d[j]);
-      const float s0 = 1.f / (1.f + __expf(-b.x)), s1 = 1.f / (1.f + __expf(-b.y));
-      du[j] = pack_bf16(e.x * b.x * s0, e.y * b.y * s1);
-      dg[j] = pack_bf16(e.x * a.x * s0 * (1.f + b.x * (1.f - s0)), e.y * a.y * s1 * (1.f + b.y * (1.f - s1)));
+      for (int k = 0; k < 2; ++k) {
+        const int c = (c0 + k * T) * 8;
+        const bool ok = c0 + k * T < per_row;
+        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+        uu[k] = ok ? *reinterpret_cast<const uint4*>(hr + c) : z;
+        gg[k] = ok ? *reinterpret_cast<const uint4*>(hr + F + c) : z;
+        dd[k] = ok ? *reinterpret_cast<const uint4*>(dr + c) : z;
+      }
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        if (c0 + k * T >= per_row) break;
+        const uint32_t u[4] = {uu[k].x, uu[k].y, uu[k].z, uu[k].w}, g[4] = {gg[k].x, gg[k].y, gg[k].z, gg[k].w},
+                       d[4] = {dd[k].x, dd[k].y, dd[k].z, dd[k].w};
+        uint32_t du[4], dg[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 a = unpack_bf16(u[j]), b = unpack_bf16(g[j]), e = unpack_bf16(d[j]);
+          const float s0 = sigm_f(b.x), s1 = sigm_f(b.y);
+          du[j] = pack_bf16(e.x * b.x * s0, e.y * b.y * s1);
+          dg[j] = pack_bf16(e.x * a.x * s0 * (1.f + b.x * (1.f - s0)), e.y * a.y * s1 * (1.f + b.y * (1.f - s1)));
+        }
+        const int c = (c0 + k * T) * 8;
+        *reinterpret_cast<uint4*>(dhr + c) = make_uint4(du[0], du[1], du[2], du[3]);
+        *reinterpret_cast<uint4*>(dhr + F + c) = make_uint4(dg[0], dg[1], dg[2], dg[3]);
+      }
     }
-    *reinterpret_cast<uint4*>(dh + (long long)row * lddh + c) = make_uint4(du[0], du[1], du[2], du[3]);
-    *reinterpret_cast<uint4*>(dh + (long long)row * lddh + F + c) = make_uint4(dg[0], dg[1], dg[2], dg[3]);
   }
 }
 
@@ -189,24 +241,48 @@ static inline int ew_grid(long long work) {
 
 void rope_apply(void* x, long long ld, int rows, int col0, int n_heads, int head_dim, const int* pos, int seq_len,
                 const void* cs, int inverse, int rot_dim, int rot_off, int max_pos, cudaStream_t s) {
-  const long long work = (long long)rows * n_heads * (rot_dim / 8);
+  if (rows <= 0 || n_heads <= 0) return;
+  // threads = the row's 16-byte chunks (rounded to a warp, at most 1024); blocks walk rows in pairs
+  const int nchunk = n_heads * (rot_dim / 8);
+  const int T = std::min(1024, std::max(32, (nchunk + 31) / 32 * 32));
   int dev = 0;
   cudaGetDevice(&dev);
-  (astrai::note_launch(), rope_kernel<<<ew_grid(work), 256, 0, s>>>(static_cast<__nv_bfloat16*>(x), ld, rows, col0, n_heads, head_dim, pos,
+  const long long cap = (long long)num_sms(dev) * (2048 / T);
+  const int grid = (int)std::max(1LL, std::min<long long>((rows + 1) / 2, cap));
+  (astrai::note_launch(), rope_kernel<<<grid, T, 0, s>>>(static_cast<__nv_bfloat16*>(x), ld, rows, col0, n_heads, head_dim, pos,
                                             seq_len, static_cast<const float2*>(cs), inverse ? -1.f : 1.f, rot_dim,
                                             rot_off, max_pos, error_word(dev)));
 }
 
+// Row-walking launch of the SwiGLU kernels: threads = half the row's 16-byte chunks (rounded to a
+// warp, at most 1024), blocks = rows, capped at what fills every SM with 2048 threads.
+static inline void row_launch_dims(int rows, int F, int* grid, int* threads) {
+  const int chunks = std::max(1, F / 8);
+  int T = ((chunks + 1) / 2 + 31) / 32 * 32;
+  T = std::min(1024, std::max(32, T));
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const long long cap = (long long)num_sms(dev) * (2048 / T);
+  *threads = T;
+  *grid = (int)std::max(1LL, std::min<long long>(rows, cap));
+}
+
 void swiglu_fwd(const void* h, long long ldh, void* out, long long ldo, int rows, int F, const int* live_rows,
                 cudaStream_t s) {
-  (astrai::note_launch(), swiglu_fwd_kernel<<<ew_grid((long long)rows * F / 8), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(h), ldh,
-                                                                      static_cast<__nv_bfloat16*>(out), ldo, rows, F,
-                                                                      live_rows));
+  if (rows <= 0) return;
+  int grid = 1, T = 32;
+  row_launch_dims(rows, F, &grid, &T);
+  (astrai::note_launch(), swiglu_fwd_kernel<<<grid, T, 0, s>>>(static_cast<const __nv_bfloat16*>(h), ldh,
+                                                                static_cast<__nv_bfloat16*>(out), ldo, rows, F,
+                                                                live_rows));
 }
 
 void swiglu_bwd(const void* dy, long long lddy, const void* h, long long ldh, void* dh, long long lddh, int rows, int F,
                 const int* live_rows, cudaStream_t s) {
-  (astrai::note_launch(), swiglu_bwd_kernel<<<ew_grid((long long)rows * F / 8), 256, 0, s>>>(
+  if (rows <= 0) return;
+  int grid = 1, T = 32;
+  row_launch_dims(rows, F, &grid, &T);
+  (astrai::note_launch(), swiglu_bwd_kernel<<<grid, T, 0, s>>>(
       static_cast<const __nv_bfloat16*>(dy), lddy, static_cast<const __nv_bfloat16*>(h), ldh,
       static_cast<__nv_bfloat16*>(dh), lddh, rows, F, live_rows));
 }

@@ -253,7 +253,9 @@ __device__ __forceinline__ bool wait_flag_eq(const int* f, int want, int* err) {
   return true;
 }
 
-__device__ __forceinline__ float sigmoid_f(float g) { return 1.f / (1.f + __expf(-g)); }
+// fast division (__fdividef: at most 2 ulp off for denominators below 2^126, 0 above, i.e. for
+// g < -87 where the quotient is below 1e-37), as in the separate SwiGLU kernels
+__device__ __forceinline__ float sigmoid_f(float g) { return __fdividef(1.f, 1.f + __expf(-g)); }
 
 // accumulator columns one epilogue thread drains in the fused modes (BN / CSPLIT); the paired
 // SwiGLU forward reads them as half as many (u, g) pairs

@@ -38,9 +38,30 @@ __global__ void sumsq_kernel(const Chunk* __restrict__ chunks, const long long* 
   const Chunk c = chunks[blockIdx.x];
   const __nv_bfloat16* g = reinterpret_cast<const __nv_bfloat16*>(gptr[c.tensor]) + c.start;
   float s = 0.f;
-  for (int i = threadIdx.x; i < c.len; i += blockDim.x) {
-    const float v = __bfloat162float(g[i]);
-    s += v * v;
+  if ((reinterpret_cast<uintptr_t>(g) & 15) == 0) {
+    // 16-byte loads, two in flight per thread; the tail (len % 8) element-wise
+    const int nv = c.len / 8;
+    const uint4* gv = reinterpret_cast<const uint4*>(g);
+    for (int j = threadIdx.x; j < nv; j += 2 * blockDim.x) {
+      const uint4 a = gv[j];
+      const uint4 b = j + (int)blockDim.x < nv ? gv[j + blockDim.x] : make_uint4(0u, 0u, 0u, 0u);
+      const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float2 f = unpack_bf16(w[e]);
+        s = fmaf(f.x, f.x, s);
+        s = fmaf(f.y, f.y, s);
+      }
+    }
+    for (int i = nv * 8 + threadIdx.x; i < c.len; i += blockDim.x) {
+      const float v = __bfloat162float(g[i]);
+      s += v * v;
+    }
+  } else {
+    for (int i = threadIdx.x; i < c.len; i += blockDim.x) {
+      const float v = __bfloat162float(g[i]);
+      s += v * v;
+    }
   }
   s = block_sum(s);
   if (threadIdx.x == 0) atomicAdd(&acc[group ? group[c.tensor] : 0], s);
@@ -223,6 +244,47 @@ __global__ void muon_normalize_kernel(const __nv_bfloat16* __restrict__ U, __nv_
   }
 }
 
+// Vector form of muon_normalize_kernel (U and X are whole, 16-byte aligned work buffers): 8 elements
+// per 16-byte access; transposed, 64 x 64 tiles go through shared memory (R and C multiples of 64).
+__global__ void __launch_bounds__(256) muon_normalize_vec_kernel(const __nv_bfloat16* __restrict__ U,
+                                                                 __nv_bfloat16* __restrict__ X, int R, int C,
+                                                                 int transpose, const float* __restrict__ sumsq,
+                                                                 float eps) {
+  const int b = blockIdx.z;
+  const float scale = 1.f / fmaxf(sqrtf(sumsq[b]), eps);
+  const __nv_bfloat16* src = U + (long long)b * R * C;
+  __nv_bfloat16* dst = X + (long long)b * R * C;
+  if (!transpose) {
+    const long long nv = (long long)R * C / 8;
+    for (long long j = (long long)blockIdx.x * 256 + threadIdx.x; j < nv; j += (long long)gridDim.x * 256) {
+      float f[8];
+      load8(src + 8 * j, f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] *= scale;
+      store8(dst + 8 * j, f);
+    }
+    return;
+  }
+  __shared__ float tile[64][65];  // [r][c] of U
+  const int c0 = blockIdx.x * 64, r0 = blockIdx.y * 64;
+  for (int v = threadIdx.x; v < 512; v += 256) {
+    const int ri = v >> 3, cv = (v & 7) * 8;
+    float f[8];
+    load8(src + (long long)(r0 + ri) * C + c0 + cv, f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) tile[ri][cv + e] = f[e];
+  }
+  __syncthreads();
+  // X = U^T: 64 rows (c) x 8 vectors (r)
+  for (int v = threadIdx.x; v < 512; v += 256) {
+    const int ci = v >> 3, rv = (v & 7) * 8;
+    float f[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) f[e] = tile[rv + e][ci] * scale;
+    store8(dst + (long long)(c0 + ci) * R + r0 + rv, f);
+  }
+}
+
 // Muon stage 3: p[b] = p[b] * (1 - lr*wd) - adj_lr * (transpose ? X[b]^T : X[b])
 template <typename P>
 __global__ void muon_apply_kernel(const long long* __restrict__ pptr, const __nv_bfloat16* __restrict__ X, int R, int C,
@@ -354,6 +416,15 @@ void muon_momentum(const long long* gptr, const long long* bufptr, int buf_fp32,
 
 void muon_normalize(const void* U, void* X, int batch, int R, int C, int transpose, const float* sumsq, float eps,
                     cudaStream_t s) {
+  const bool al = (reinterpret_cast<uintptr_t>(U) % 16) == 0 && (reinterpret_cast<uintptr_t>(X) % 16) == 0;
+  if (al && (transpose ? (R % 64 == 0 && C % 64 == 0) : ((long long)R * C % 8 == 0))) {
+    const dim3 grid = transpose ? dim3(C / 64, R / 64, batch)
+                                : dim3((unsigned)std::min<long long>(((long long)R * C / 8 + 255) / 256, 1024), 1, batch);
+    (astrai::note_launch(), muon_normalize_vec_kernel<<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(U),
+                                                                          static_cast<__nv_bfloat16*>(X), R, C, transpose,
+                                                                          sumsq, eps));
+    return;
+  }
   dim3 grid((C + 31) / 32, (R + 31) / 32, batch);
   (astrai::note_launch(), muon_normalize_kernel<<<grid, dim3(32, 8), 0, s>>>(static_cast<const __nv_bfloat16*>(U),
                                                      static_cast<__nv_bfloat16*>(X), R, C, transpose, sumsq, eps));

@@ -1,6 +1,6 @@
 """Device-timed micro-benchmarks of the framework's kernels.
 
-    python -m astrai_b200.utils.kernel_bench [gemm [case]|gemm_shapes|swiglu_gemm|ns|attn|norm|skinny|sample|decode|prefill|all]
+    python -m astrai_b200.utils.kernel_bench [gemm [case]|gemm_shapes|swiglu_gemm|elementwise|ns|attn|norm|skinny|sample|decode|prefill|all]
     torchrun --nproc-per-node N -m astrai_b200.utils.kernel_bench allreduce|ep|tpgather|tprow
 
 Each case is timed with CUDA events on the launching stream after warm-up,
@@ -693,15 +693,46 @@ def bench_gemm_shapes():
               (2048, 1536, 6912, "down"), (2048, 10000, 1536, "lm_head"), (8192, 3072, 2048, "step_qkv"),
               (8192, 2048, 2048, "step_o"), (8192, 11264, 2048, "step_upgate"), (8192, 2048, 5632, "step_down"),
               (8192, 32000, 2048, "step_lm_head")]
-    for M, N, K, name in shapes:
-        a = torch.randn(M, K, device="cuda").to(torch.bfloat16)
-        b = torch.randn(N, K, device="cuda").to(torch.bfloat16)
+    # the step's weight gradients dW = dY^T X: both operands MN-major ([tokens][out], [tokens][in])
+    wgrad = [(3072, 2048, 8192, "wgrad_qkv"), (2048, 2048, 8192, "wgrad_o"), (11264, 2048, 8192, "wgrad_upgate"),
+             (2048, 5632, 8192, "wgrad_down")]
+    for M, N, K, name in shapes + wgrad:
+        mn = name.startswith("wgrad")
+        a = torch.randn((K, M) if mn else (M, K), device="cuda").to(torch.bfloat16)
+        b = torch.randn((K, N) if mn else (N, K), device="cuda").to(torch.bfloat16)
         d = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
         res = {}
         for fb in (0, 1024, 1026, 1027, 256):
-            res[str(fb)] = round(time_flushed(lambda: C.gemm(a, b, d, None, 0, 0, 1.0, 0.0, fb), 3, 20) * 1e3, 1)
-        res["cublas"] = round(time_flushed(lambda: torch.matmul(a, b.t()), 3, 20) * 1e3, 1)
+            res[str(fb)] = round(time_flushed(lambda: C.gemm(a, b, d, None, int(mn), int(mn), 1.0, 0.0, fb), 3, 20)
+                                 * 1e3, 1)
+        res["cublas"] = round(time_flushed(lambda: torch.matmul(a.t(), b) if mn else torch.matmul(a, b.t()), 3, 20)
+                              * 1e3, 1)
         print(json.dumps({"kernel": "gemm", "case": name, "M": M, "N": N, "K": K, "us": res}))
+
+
+def bench_elementwise():
+    """SwiGLU forward / backward and in-place RoPE at the 1.1B step's shapes (8192 rows; FFN 5632;
+    q and k heads 16 + 4 of 128 in the 3072-wide QKV output), L2 flushed before every call; bytes
+    are the algorithmic reads + writes."""
+    from astrai_b200.ops._ext import native
+    from astrai_b200.ops.rope import rope_inplace, rope_table
+
+    hbm, _, src = peaks()
+    C = native()
+    rows, Fw = 8192, 5632
+    h = torch.randn(rows, 2 * Fw, device="cuda").to(torch.bfloat16)
+    a = torch.empty(rows, Fw, device="cuda", dtype=torch.bfloat16)
+    da = torch.randn(rows, Fw, device="cuda").to(torch.bfloat16)
+    dh = torch.empty_like(h)
+    qkv = torch.randn(rows, 24 * 128, device="cuda").to(torch.bfloat16)
+    tab = rope_table(128, 2048, 1e6, device="cuda")
+    cases = [("swiglu_fwd", lambda: C.swiglu_fwd(h, a), rows * Fw * 2 * 3),
+             ("swiglu_bwd", lambda: C.swiglu_bwd(da, h, dh), rows * Fw * 2 * 5),
+             ("rope", lambda: rope_inplace(qkv, 0, 20, 128, tab, None, 2048), rows * 20 * 128 * 2 * 2)]
+    for name, fn, nbytes in cases:
+        us = time_flushed(fn, 3, 20) * 1e3
+        print(json.dumps({"kernel": name, "us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1),
+                          "frac_of_hbm": round(nbytes / us / 1e3 / hbm, 3), "peak_src": src}))
 
 
 def bench_norm(rows: int = 8192, D: int = 2048):
@@ -758,6 +789,8 @@ def main(argv=None):
         bench_prefill()
     if which in ("ns", "all"):
         bench_ns()
+    if which in ("elementwise", "all"):
+        bench_elementwise()
     if which in ("swiglu_gemm", "all"):
         bench_swiglu_gemm()
     if which in ("gemm_shapes", "all"):

@@ -1,6 +1,6 @@
 """Runs each hot kernel of the framework once on a case larger than L2, for profiler captures.
 
-``python -m astrai_b200.utils.kernel_cases [ce rope swiglu gemm_swiglu embedding router sample decode adamw muon ep]``
+``python -m astrai_b200.utils.kernel_cases [ce rope swiglu gemm_swiglu gemm_swiglu_train embedding router sample decode adamw muon ep]``
 (no argument: all of them). One launch per kernel (two for the forward/backward pairs), shapes of
 the 1.1B dense step (8192 tokens, d 2048, FFN 5632, vocab 32000), the MoE layer (64 experts top-6,
 one-rank expert-parallel group) and batch-32 decode over a 4096-token paged cache, so an ``ncu``
@@ -50,6 +50,16 @@ def run(which):
         a = torch.empty(2048, 6912, device=dev, dtype=torch.bfloat16)
         C.gemm(x, w, h, None, 0, 0, 1.0, 0.0, 0)
         C.gemm_swiglu(1, x, w, None, a, None)
+        del x, w, h, a
+    if want("gemm_swiglu_train"):
+        # the 1.1B step's up/gate projection (8192 tokens, d 2048, FFN 5632): the plain GEMM writing
+        # h, then the SwiGLU-epilogue GEMM writing h and a (what training would store)
+        x = torch.randn(8192, 2048, device=dev).to(torch.bfloat16)
+        w = (torch.randn(2 * 5632, 2048, device=dev) * 0.02).to(torch.bfloat16)
+        h = torch.empty(8192, 2 * 5632, device=dev, dtype=torch.bfloat16)
+        a = torch.empty(8192, 5632, device=dev, dtype=torch.bfloat16)
+        C.gemm(x, w, h, None, 0, 0, 1.0, 0.0, 0)
+        C.gemm_swiglu(1, x, w, h, a, None)
         del x, w, h, a
     if want("embedding"):
         from astrai_b200.ops.embedding import embedding

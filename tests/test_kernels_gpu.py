@@ -263,32 +263,61 @@ def test_rmsnorm_fork_adds_residual_gradient(rows, D):
     assert rel_err(w.grad, wf.grad) < 1e-2
 
 
-def test_rope_inplace_roundtrip():
+@pytest.mark.parametrize("B,S,H,Hkv,D", [(2, 64, 4, 2, 128), (1, 1, 3, 1, 128), (3, 37, 24, 4, 64), (4, 512, 16, 4, 128)])
+@pytest.mark.parametrize("with_pos", [False, True])
+def test_rope_inplace_roundtrip(B, S, H, Hkv, D, with_pos):
+    """Rows walked in pairs (odd row counts included), positions from row % seq_len or given per
+    row, against the fp32 reference; the v columns are untouched and the inverse restores q/k."""
     from astrai_b200.ops.rope import apply_rope_reference, rope_inplace, rope_table
 
-    torch.manual_seed(5)
-    B, S, H, Hkv, D = 2, 64, 4, 2, 128
+    torch.manual_seed(5 + B * S)
     qkv = torch.randn(B * S, (H + 2 * Hkv) * D, device="cuda", dtype=torch.bfloat16)
-    tab = rope_table(D, 256, 10000.0, device="cuda")
-    ref_q = apply_rope_reference(qkv[:, : H * D].view(B, S, H, D), tab[:S].unsqueeze(0).expand(B, -1, -1, -1))
+    tab = rope_table(D, 1024, 10000.0, device="cuda")
+    if with_pos:
+        posn = torch.randint(0, 1024, (B * S,), device="cuda", dtype=torch.int32)
+        cs = tab[posn.long()].view(B, S, D // 2, 2)
+    else:
+        posn = None
+        cs = tab[:S].unsqueeze(0).expand(B, -1, -1, -1)
+    ref_q = apply_rope_reference(qkv[:, : H * D].view(B, S, H, D), cs)
     buf = qkv.clone()
-    rope_inplace(buf, 0, H + Hkv, D, tab, None, S)
+    rope_inplace(buf, 0, H + Hkv, D, tab, posn, S)
     assert rel_err(buf[:, : H * D].view(B, S, H, D), ref_q) < 1e-2
     assert torch.equal(buf[:, (H + Hkv) * D :], qkv[:, (H + Hkv) * D :])
-    rope_inplace(buf, 0, H + Hkv, D, tab, None, S, inverse=True)
+    rope_inplace(buf, 0, H + Hkv, D, tab, posn, S, inverse=True)
     assert rel_err(buf, qkv) < 1e-2
 
 
-def test_swiglu():
+def test_rope_partial_rotation():
+    """rot_dim / rot_off (MLA's rotary slice): only columns [rot_off, rot_off + rot_dim) of each head
+    rotate, by a table of rot_dim / 2 angles."""
+    from astrai_b200.ops.rope import apply_rope_reference, rope_inplace, rope_table
+
+    torch.manual_seed(8)
+    rows, H, D, rd, off = 77, 5, 192, 64, 128
+    x = torch.randn(rows, H * D, device="cuda", dtype=torch.bfloat16)
+    tab = rope_table(rd, 128, 10000.0, device="cuda")
+    buf = x.clone()
+    rope_inplace(buf, 0, H, D, tab, None, rows, rot_dim=rd, rot_off=off)
+    xv = x.view(1, rows, H, D)
+    ref = apply_rope_reference(xv[..., off:off + rd], tab[:rows].unsqueeze(0))
+    bv = buf.view(1, rows, H, D)
+    assert rel_err(bv[..., off:off + rd], ref) < 1e-2
+    assert torch.equal(bv[..., :off], xv[..., :off])
+
+
+@pytest.mark.parametrize("rows,Fw", [(257, 688), (1, 8), (33, 1408), (4096, 5632)])
+def test_swiglu(rows, Fw):
+    """Row-walking SwiGLU forward/backward (two 16-byte chunks per thread per pass) against fp32."""
     from astrai_b200.ops.activation import swiglu
 
     torch.manual_seed(6)
-    h = torch.randn(257, 2 * 688, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    h = torch.randn(rows, 2 * Fw, device="cuda", dtype=torch.bfloat16, requires_grad=True)
     y = swiglu(h)
     g = torch.randn_like(y)
     y.backward(g)
     hf = h.detach().float().requires_grad_()
-    yf = hf[:, :688] * F.silu(hf[:, 688:])
+    yf = hf[:, :Fw] * F.silu(hf[:, Fw:])
     yf.backward(g.float())
     assert rel_err(y, yf) < 1e-2
     assert rel_err(h.grad, hf.grad) < 1e-2

@@ -71,7 +71,8 @@ def test_fused_optimizers_match_torch(chunk_bytes, monkeypatch):
     if chunk_bytes is not None:
         monkeypatch.setattr(fused, "_NS_CHUNK_BYTES", chunk_bytes)
     torch.manual_seed(1)
-    shapes = [(256, 512), (512, 256), (256, 512), (128, 128)]
+    # vector normalize / apply paths (multiples of 64, 8-element rows) and the element-wise ones
+    shapes = [(256, 512), (512, 256), (256, 512), (128, 128), (96, 200), (200, 96)]
     ps = [torch.randn(s, device="cuda").to(torch.bfloat16) for s in shapes]
     ref = [p.clone() for p in ps]
     grads = [torch.randn_like(p) for p in ps]
@@ -88,8 +89,8 @@ def test_fused_optimizers_match_torch(chunk_bytes, monkeypatch):
         exp = p0.float() * (1 - 0.02 * 0.1) - adj * upd
         assert rel(p.data, exp) < 2e-2
     # AdamW + on-device clip coefficient
-    w = torch.nn.Parameter(torch.randn(1000, device="cuda").to(torch.bfloat16))
-    w.grad = (torch.randn(1000, device="cuda") * 10).to(torch.bfloat16)
+    w = torch.nn.Parameter(torch.randn(1003, device="cuda").to(torch.bfloat16))  # 16-byte loads + a 3-element tail
+    w.grad = (torch.randn(1003, device="cuda") * 10).to(torch.bfloat16)
     wt = torch.nn.Parameter(w.detach().float().clone())
     wt.grad = w.grad.float().clone()
     n = clip_grad_norm_([w], 1.0)
