@@ -1728,12 +1728,26 @@ static bool use_streamk_pair(long long tiles, int kb, int pairs) {
   const double whole = (double)(tiles / pairs + 1), split = (double)tiles / pairs + 0.05;
   return (whole - split) * kb >= 8.0;
 }
-// Small grids (fewer 256 x 256 tiles than pairs, e.g. a 2048-token prefill's 2048 x 1536 x 6912 down
-// projection: 48 tiles on 74 pairs): every k-block of every tile is split evenly over all pairs, so
-// each pair runs tiles * kb / pairs k-blocks instead of kb, when that saves at least 16 k-blocks.
-static bool use_streamk_pair_small(long long tiles, int kb, int pairs) {
-  if (tiles <= 0 || pairs <= 0 || tiles >= pairs || tiles * kb < 4LL * pairs) return false;
-  return kb - (double)tiles * kb / pairs >= 16.0;
+// Automatic k-block split of the pair kernel (0 none, 1 the last partial wave, 2 every k-block of
+// every tile over all pairs). Measured on B200 (L2 flushed, `kernel_bench gemm_shapes`), the fix-up
+// (partials out, flags, partials in) costs 10 - 20 us, so a split pays only where it saves many
+// k-blocks per pair:
+//   3072 x 2048 x 8192 weight gradient (96 tiles, 1.3 waves, 128 k-blocks): 151.6 us unsplit, 119.9
+//     last wave, 111.6 every k-block;  2048 x 5632 x 8192 (176 tiles, last wave 38 % full): 149.6,
+//     137.0, 146.9;  11264 x 2048 x 8192 (last wave 76 % full): 236.9, 234.6, 277.0;
+//   2048 x 1536 x 6912 (48 tiles < 74 pairs, 108 k-blocks): 49.1 unsplit, 48.1 every k-block;
+//     2048 x 2048 x 8192 (64 tiles): 81.3 unsplit, 85.1 every k-block;
+//   short K (32 k-blocks: 8192 x 3072 x 2048, 8192 x 2048 x 2048, lm_head) lost 10 - 15 % split.
+// So: at least 64 k-blocks; fewer tiles than pairs: every k-block if that saves >= 32 k-blocks per
+// pair; otherwise the last wave must save >= 64 k-blocks per pair, split over every k-block when the
+// grid is under two waves, else the last wave only.
+static int pair_split_mode(long long tiles, int kb, int pairs) {
+  if (tiles <= 0 || pairs <= 0 || kb < 64 || tiles * kb < 4LL * pairs) return 0;
+  if (tiles < pairs) return kb - (double)tiles * kb / pairs >= 32.0 ? 2 : 0;
+  const long long rem = tiles % pairs;
+  if (rem == 0) return 0;
+  if (kb * (1.0 - (double)rem / pairs) < 64.0) return 0;
+  return tiles < 2LL * pairs ? 2 : 1;
 }
 static double effective_waves(long long tiles, int kb, int sms) {
   return use_streamk(tiles, kb, sms) ? (double)tiles / sms + 0.08 : (double)((tiles + sms - 1) / sms);
@@ -1958,12 +1972,14 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
   if (pair) {
     const int pmax = pair_clusters(dev);
     int pairs = std::min(tiles, pmax);
-    const bool split = !sym && (force_bn == 1026 || (force_bn != 1024 && pair_streamk_on() && streamk_on()));
-    // force_bn 1027: every k-block split over all pairs whatever the shape (needs tiles * kb >= pairs)
-    const bool small = !sym && (force_bn == 1027 ? (long long)tiles * p.k_blocks >= pmax
-                                                 : (force_bn == 0 && streamk_on() &&
-                                                    use_streamk_pair_small(tiles, p.k_blocks, pmax)));
-    if (small && sk_buffers(dev, stream, sms, &p.sk_ws, &p.sk_flags)) {
+    // force_bn 1026: the last wave split wherever use_streamk_pair allows it (also ASTRAI_PAIR_STREAMK=1);
+    // force_bn 1027: every k-block split over all pairs whatever the shape (needs tiles * kb >= pairs);
+    // force_bn 0: pair_split_mode
+    const int automatic = (force_bn == 0 && streamk_on()) ? pair_split_mode(tiles, p.k_blocks, pmax) : 0;
+    const bool split = !sym && (force_bn == 1026 || automatic == 1 ||
+                                (force_bn != 1024 && force_bn != 1027 && pair_streamk_on() && streamk_on()));
+    const bool all_units = !sym && (force_bn == 1027 ? (long long)tiles * p.k_blocks >= pmax : automatic == 2);
+    if (all_units && sk_buffers(dev, stream, sms, &p.sk_ws, &p.sk_flags)) {
       p.dp_tiles = 0;
       p.sk_units = (long long)tiles * p.k_blocks;
       pairs = pmax;

@@ -696,16 +696,17 @@ def bench_gemm_shapes():
     # the step's weight gradients dW = dY^T X: both operands MN-major ([tokens][out], [tokens][in])
     wgrad = [(3072, 2048, 8192, "wgrad_qkv"), (2048, 2048, 8192, "wgrad_o"), (11264, 2048, 8192, "wgrad_upgate"),
              (2048, 5632, 8192, "wgrad_down")]
-    for M, N, K, name in shapes + wgrad:
-        mn = name.startswith("wgrad")
-        a = torch.randn((K, M) if mn else (M, K), device="cuda").to(torch.bfloat16)
-        b = torch.randn((K, N) if mn else (N, K), device="cuda").to(torch.bfloat16)
+    # data gradients dX = dY W: B = W stored [out][in] = [K][N], MN-major
+    dgrad = [(8192, 2048, 11264, "dgrad_upgate"), (8192, 2048, 32000, "dgrad_lm_head"), (8192, 5632, 2048, "dgrad_down")]
+    for M, N, K, name in shapes + wgrad + dgrad:
+        amn, bmn = int(name.startswith("wgrad")), int(name.startswith(("wgrad", "dgrad")))
+        a = torch.randn((K, M) if amn else (M, K), device="cuda").to(torch.bfloat16)
+        b = torch.randn((K, N) if bmn else (N, K), device="cuda").to(torch.bfloat16)
         d = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
         res = {}
         for fb in (0, 1024, 1026, 1027, 256):
-            res[str(fb)] = round(time_flushed(lambda: C.gemm(a, b, d, None, int(mn), int(mn), 1.0, 0.0, fb), 3, 20)
-                                 * 1e3, 1)
-        res["cublas"] = round(time_flushed(lambda: torch.matmul(a.t(), b) if mn else torch.matmul(a, b.t()), 3, 20)
+            res[str(fb)] = round(time_flushed(lambda: C.gemm(a, b, d, None, amn, bmn, 1.0, 0.0, fb), 3, 20) * 1e3, 1)
+        res["cublas"] = round(time_flushed(lambda: torch.matmul(a.t() if amn else a, b if bmn else b.t()), 3, 20)
                               * 1e3, 1)
         print(json.dumps({"kernel": "gemm", "case": name, "M": M, "N": N, "K": K, "us": res}))
 

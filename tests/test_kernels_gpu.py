@@ -509,11 +509,13 @@ def test_swiglu_mlp_forward_only(M, d, Fw, with_res):
 
 
 @pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 1)])
-@pytest.mark.parametrize("M,N,K,fb", [(2048, 1536, 6912, 0), (2048, 1536, 1536, 1027), (1000, 704, 3000, 1027)])
-def test_gemm_cta_pair_streamk_small_grid(a_mn, b_mn, M, N, K, fb):
-    """Fewer 256 x 256 tiles than CTA pairs: every k-block of every tile split evenly over all pairs
-    (automatic for 2048 x 1536 x 6912, forced with force_bn 1027 otherwise), against an fp32 matmul
-    and the unsplit pair kernel; twice, so the fix-up flags reset between launches."""
+@pytest.mark.parametrize("M,N,K,fb", [(2048, 1536, 6912, 0), (3072, 2048, 8192, 0), (2048, 5632, 8192, 0),
+                                      (2048, 1536, 1536, 1027), (1000, 704, 3000, 1027)])
+def test_gemm_cta_pair_kblock_split(a_mn, b_mn, M, N, K, fb):
+    """k-block splits of the pair kernel: automatic (force_bn 0) on 2048 x 1536 x 6912 (fewer tiles
+    than pairs: every k-block), 3072 x 2048 x 8192 (under two waves: every k-block) and 2048 x 5632 x
+    8192 (the last wave), forced over every k-block (force_bn 1027) elsewhere; against an fp32 matmul
+    and the unsplit pair kernel, twice, so the fix-up flags reset between launches."""
     from astrai_b200.ops._ext import native
 
     torch.manual_seed(5)
