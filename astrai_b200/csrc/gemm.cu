@@ -1337,6 +1337,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS
       const int row = mb * 256 + (int)rank * 128 + q * 32 + lane;
       const int n0 = nb * BN + cpart * BNH;
       const bool row_ok = row < p.M;
+      // epi 3 (RoPE in the QKV projection): this row's position, read once per tile
+      int rope_p = 0;
+      bool rope_ok = false;
+      if (p.epi == 3) {
+        rope_p = p.rope_pos ? p.rope_pos[min(row, p.M - 1)] : row % p.rope_seq;
+        rope_ok = rope_p >= 0 && rope_p < p.rope_max;
+        if (row_ok && !rope_ok) set_error(p.err, kErrBadArg);
+      }
       OutT* drow = reinterpret_cast<OutT*>(p.D) + (long long)b * p.strideD + (long long)row * p.ldd;
       const OutT* crow =
           use_c ? reinterpret_cast<const OutT*>(p.C) + (long long)b * p.strideC + (long long)row * p.ldc : nullptr;
@@ -1470,6 +1478,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
+        if (p.epi == 3 && rope_ok && col < p.rope_cols) {
+          // RoPE of interleaved pairs on the bf16-rounded values (what the separate in-place kernel
+          // reads); the 32 columns lie in one head (head_dim and rope_cols are multiples of 32), so
+          // their 16 (cos, sin) pairs are contiguous in the table: eight 16-byte loads
+          const float4* tcs = reinterpret_cast<const float4*>(p.rope_cs + (long long)rope_p * (p.rope_hd / 2) +
+                                                              (col % p.rope_hd) / 2);
+#pragma unroll
+          for (int q4 = 0; q4 < 8; ++q4) {
+            const float4 c2 = tcs[q4];
+            const float x0 = __bfloat162float(__float2bfloat16_rn(v[4 * q4])),
+                        y0 = __bfloat162float(__float2bfloat16_rn(v[4 * q4 + 1])),
+                        x1 = __bfloat162float(__float2bfloat16_rn(v[4 * q4 + 2])),
+                        y1 = __bfloat162float(__float2bfloat16_rn(v[4 * q4 + 3]));
+            v[4 * q4] = x0 * c2.x - y0 * c2.y;
+            v[4 * q4 + 1] = x0 * c2.y + y0 * c2.x;
+            v[4 * q4 + 2] = x1 * c2.z - y1 * c2.w;
+            v[4 * q4 + 3] = x1 * c2.w + y1 * c2.z;
+          }
+        }
         if (col + 32 <= p.N && p.vec_ok) {
           if (crow) {
             if (OUT_F32) {
@@ -2220,8 +2247,12 @@ void gemm_rope_bf16(const void* A, long long lda, const void* B, long long ldb, 
   int dev = 0;
   cudaGetDevice(&dev);
   const int sms = num_sms(dev);
-  const int BM = 128;  // the fused epilogues run on 128-row tiles (double-buffered accumulator)
+  // 256 x 256 tiles on a CTA pair where the pair policy applies (as in gemm_bf16), else 128-row
+  // single-CTA tiles; both double-buffer the accumulator, so the rotation overlaps the next MMAs
+  const bool pair = M > 128 && N > 128 && pair_on();
+  const int BM = pair ? 256 : 128;
   const int BN = N <= 128 ? 128 : 256;
+  if (reinterpret_cast<uintptr_t>(cs) % 16) throw std::runtime_error("gemm_rope: cos/sin table must be 16-byte aligned");
   CUtensorMap ta, tb;
   {
     uint64_t dims[3] = {(uint64_t)K, (uint64_t)M, 1};
@@ -2232,7 +2263,7 @@ void gemm_rope_bf16(const void* A, long long lda, const void* B, long long ldb, 
   {
     uint64_t dims[3] = {(uint64_t)K, (uint64_t)N, 1};
     uint64_t strides[2] = {(uint64_t)ldb * 2, (uint64_t)N * ldb * 2};
-    uint32_t box[3] = {64, (uint32_t)BN, 1};
+    uint32_t box[3] = {64, (uint32_t)(pair ? BN / 2 : BN), 1};
     make_tmap_bf16(&tb, B, 3, dims, strides, box, true);
   }
   GemmParams p;
@@ -2284,6 +2315,7 @@ void gemm_rope_bf16(const void* A, long long lda, const void* B, long long ldb, 
   p.sym_bm = 1;
   p.sym_bn = 1;
   const int tiles = p.tiles_m * p.tiles_n;
+  if (pair) return dispatch_pair<256>(0, 0, 0, ta, tb, p, std::min(tiles, pair_clusters(dev)), stream);
   const int grid = std::min(tiles, sms);
   if (BN == 256)
     dispatch_majors<128, 256>(0, 0, 0, ta, tb, p, grid, stream);

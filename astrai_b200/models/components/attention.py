@@ -130,7 +130,7 @@ class GQA(nn.Module):
     def qkv_proj_rope(self, x: torch.Tensor, ctx) -> Optional[torch.Tensor]:
         """q|k|v projection with RoPE already applied to q and k (GEMM epilogue), or None."""
         mods = (self.q_proj, self.k_proj, self.v_proj)
-        if not all(type(m) is Linear and m.bias is None for m in mods) or self.head_dim != 128:
+        if not all(type(m) is Linear and m.bias is None for m in mods) or self.head_dim % 32:
             return None
         from astrai_b200.ops.gemm import packed_linear_rope
 

@@ -150,12 +150,13 @@ def attention_qkv(qkv: torch.Tensor, B: int, S: int, Hq: int, Hkv: int, table: t
                       causal, sg)
         return o
     q, k, v = qkv.view(B, S, Hq + 2 * Hkv, D).split([Hq, Hkv, Hkv], dim=2)
-    if positions is None:
-        cs = table[:S].unsqueeze(0).expand(B, -1, -1, -1)
-    else:
-        cs = table[positions]
-    q = apply_rope_reference(q, cs)
-    k = apply_rope_reference(k, cs)
+    if not rotated:
+        if positions is None:
+            cs = table[:S].unsqueeze(0).expand(B, -1, -1, -1)
+        else:
+            cs = table[positions]
+        q = apply_rope_reference(q, cs)
+        k = apply_rope_reference(k, cs)
     return _sdpa(q, k, v, causal, seg).reshape(B * S, Hq * D)
 
 

@@ -535,17 +535,20 @@ def test_gemm_cta_pair_kblock_split(a_mn, b_mn, M, N, K, fb):
 
 
 @pytest.mark.parametrize("with_pos", [False, True])
-def test_qkv_projection_with_rope_epilogue(with_pos):
-    """RoPE applied in the QKV projection epilogue + attention on pre-rotated q/k equals the
-    unfused projection + in-place RoPE + attention, in value and in the input/weight gradients."""
+@pytest.mark.parametrize("B,S,D", [(2, 256, 128), (2, 300, 64)])
+def test_qkv_projection_with_rope_epilogue(with_pos, B, S, D, monkeypatch):
+    """RoPE applied in the QKV projection epilogue (CTA-pair tiles; 600 rows leave a partial tile) +
+    attention on pre-rotated q/k equals the unfused projection + in-place RoPE + attention, in value
+    and in the input/weight gradients; without autograd the rotated projection equals the in-place
+    kernel's rotation of the plain one."""
     import astrai_b200.ops.gemm as G
     from astrai_b200.ops.attention import attention_qkv
     from astrai_b200.ops.gemm import packed_linear, packed_linear_rope
-    from astrai_b200.ops.rope import rope_table
+    from astrai_b200.ops.rope import rope_inplace, rope_table
 
-    G.FUSED_EPILOGUES = True  # the test exercises the fused kernels whatever the default
+    monkeypatch.setattr(G, "FUSED_ROPE", True)  # the test exercises the fused kernel whatever the default
     torch.manual_seed(12)
-    B, S, Hq, Hkv, D, d = 2, 256, 4, 2, 128, 512
+    Hq, Hkv, d = 4, 2, 512
     tab = rope_table(D, 1024, 1e6, device="cuda")
     ws = [torch.nn.Parameter((torch.randn(h * D, d, device="cuda") * d ** -0.5).to(torch.bfloat16))
           for h in (Hq, Hkv, Hkv)]
@@ -555,6 +558,7 @@ def test_qkv_projection_with_rope_epilogue(with_pos):
     pos = (torch.arange(S, device="cuda") + 100).repeat(B, 1) if with_pos else None
     p32 = pos.reshape(-1).to(torch.int32).contiguous() if pos is not None else None
     qkv = packed_linear_rope(x, ws, tab, p32, S, (Hq + Hkv) * D, D)
+    assert qkv is not None
     o = attention_qkv(qkv.reshape(B * S, -1), B, S, Hq, Hkv, tab, pos, True, None, rotated=True)
     qkv2 = packed_linear(x2, ws2)
     o2 = attention_qkv(qkv2.reshape(B * S, -1), B, S, Hq, Hkv, tab, pos, True, None)
@@ -565,3 +569,9 @@ def test_qkv_projection_with_rope_epilogue(with_pos):
     assert rel_err(x.grad, x2.grad) < 2e-2
     for a, b in zip(ws, ws2):
         assert rel_err(a.grad, b.grad) < 2e-2
+    with torch.no_grad():
+        r = packed_linear_rope(x.detach(), ws, tab, p32, S, (Hq + Hkv) * D, D)
+        ref = packed_linear(x.detach(), ws).reshape(B * S, -1).clone()
+        rope_inplace(ref, 0, Hq + Hkv, D, tab, p32, S)
+    assert r is not None
+    assert rel_err(r.reshape(B * S, -1), ref) < 1e-2
