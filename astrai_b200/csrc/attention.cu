@@ -402,7 +402,7 @@ struct FlashBwdParams {
   const float* lse2;   // [B, Hq, Sq_pad] LSE in log2 units (+inf past Sq)
   const float* delta;  // [B, Hq, Sq_pad] rowsum(dO * O) (0 past Sq)
   int Sq_pad;          // Sq rounded up to the 64-query tile
-  float* dq_acc;       // [B*Sq, Hq*128] fp32, zero-initialised
+  float* dq_acc;       // [B*Sq, Hq*128] fp32, zeroed by flash_bwd_pre_kernel
   __nv_bfloat16* dk;   // [B*Sk, ldk_out]  head hk at column dk_col0 + hk*128
   __nv_bfloat16* dv;
   long long ld_dkv;
@@ -794,52 +794,80 @@ __global__ void __launch_bounds__(FB_THREADS, 1)
 __global__ void flash_bwd_pre_kernel(const __nv_bfloat16* __restrict__ dO, long long ld_do, int do_col0,
                                      const __nv_bfloat16* __restrict__ O, long long ldo,
                                      const float* __restrict__ lse, float* __restrict__ lse2,
-                                     float* __restrict__ delta, int B, int S, int S_pad, int H) {
+                                     float* __restrict__ delta, int B, int S, int S_pad, int H,
+                                     float* __restrict__ dq_acc, int dq_width) {
+  // One warp per (batch, query row padded to 64-query tiles): delta = rowsum(dO * O) per head and
+  // lse2 = lse * log2(e) (padding rows get 0 and +inf), and the row's fp32 dQ accumulator is zeroed
+  // (the main kernel reduce-adds into it). The loads of four heads (two per half-warp) are issued
+  // before their reductions.
   const long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (w >= (long long)B * S_pad) return;
   const int b = (int)(w / S_pad), si = (int)(w % S_pad);
   const int half = lane >> 4, sub = lane & 15;
-  for (int h0 = 0; h0 < H; h0 += 2) {
-    const int h = h0 + half;
-    float sum = 0.f;
-    if (si < S && h < H) {
-      const long long row = (long long)b * S + si;
-      const uint4 ua = *reinterpret_cast<const uint4*>(dO + row * ld_do + do_col0 + h * FA_D + sub * 8);
-      const uint4 uo = *reinterpret_cast<const uint4*>(O + row * ldo + h * FA_D + sub * 8);
-      const uint32_t a4[4] = {ua.x, ua.y, ua.z, ua.w}, o4[4] = {uo.x, uo.y, uo.z, uo.w};
+  if (si < S && dq_acc != nullptr) {
+    float4* z = reinterpret_cast<float4*>(dq_acc + ((long long)b * S + si) * dq_width);
+    for (int c = lane; c < dq_width / 4; c += 32) z[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const long long row = (long long)b * S + si;
+  for (int h0 = 0; h0 < H; h0 += 4) {
+    uint4 ua[2], uo[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int h = h0 + 2 * k + half;
+      if (si < S && h < H) {
+        ua[k] = *reinterpret_cast<const uint4*>(dO + row * ld_do + do_col0 + h * FA_D + sub * 8);
+        uo[k] = *reinterpret_cast<const uint4*>(O + row * ldo + h * FA_D + sub * 8);
+      } else {
+        ua[k] = uo[k] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int h = h0 + 2 * k + half;
+      const uint32_t a4[4] = {ua[k].x, ua[k].y, ua[k].z, ua[k].w}, o4[4] = {uo[k].x, uo[k].y, uo[k].z, uo[k].w};
+      float sum = 0.f;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 a = unpack_bf16(a4[j]), o = unpack_bf16(o4[j]);
         sum = fmaf(a.x, o.x, fmaf(a.y, o.y, sum));
       }
-    }
 #pragma unroll
-    for (int off = 8; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffff, sum, off);
-    if (sub == 0 && h < H) {
-      const long long out = ((long long)b * H + h) * S_pad + si;
-      if (si >= S) {
-        delta[out] = 0.f;
-        lse2[out] = INFINITY;
-      } else {
-        delta[out] = sum;
-        const float ls = lse[((long long)b * H + h) * S + si];
-        lse2[out] = (ls == -INFINITY) ? INFINITY : ls * 1.4426950408889634f;
+      for (int off = 8; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffff, sum, off);
+      if (sub == 0 && h < H) {
+        const long long out = ((long long)b * H + h) * S_pad + si;
+        if (si >= S) {
+          delta[out] = 0.f;
+          lse2[out] = INFINITY;
+        } else {
+          delta[out] = sum;
+          const float ls = lse[((long long)b * H + h) * S + si];
+          lse2[out] = (ls == -INFINITY) ? INFINITY : ls * 1.4426950408889634f;
+        }
       }
     }
   }
 }
 
-// dq_out[row, col0 + c] = bf16(dq_acc[row, c])
+// dq_out[row, col0 + c] = bf16(dq_acc[row, c]): blocks walk rows, each thread converts two float4s
+// of a row per pass (both loads issued first), no index division
 __global__ void flash_dq_convert_kernel(const float* __restrict__ acc, int width, long long rows,
                                         __nv_bfloat16* __restrict__ out, long long ld_out, int col0) {
-  const long long n = rows * (width / 4);
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const long long row = i / (width / 4);
-    const int c = (i % (width / 4)) * 4;
-    const float4 v = *reinterpret_cast<const float4*>(acc + row * width + c);
-    uint2 o = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
-    *reinterpret_cast<uint2*>(out + row * ld_out + col0 + c) = o;
+  const int nv = width / 4, T = blockDim.x;
+  for (long long row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float4* src = reinterpret_cast<const float4*>(acc + row * width);
+    __nv_bfloat16* dst = out + row * ld_out + col0;
+    for (int c0 = threadIdx.x; c0 < nv; c0 += 2 * T) {
+      float4 v[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) v[k] = c0 + k * T < nv ? src[c0 + k * T] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int c = c0 + k * T;
+        if (c < nv)
+          *reinterpret_cast<uint2*>(dst + 4 * c) = make_uint2(pack_bf16(v[k].x, v[k].y), pack_bf16(v[k].z, v[k].w));
+      }
+    }
   }
 }
 
@@ -907,7 +935,7 @@ void flash_bwd(const void* q, long long ldq, int q_col0, const void* k, long lon
     const int blocks = (int)((warps * 32 + 255) / 256);
     (astrai::note_launch(), flash_bwd_pre_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(dO), ld_do, do_col0,
                                                 static_cast<const __nv_bfloat16*>(o), ldo, lse, lse2, delta, B, Sq,
-                                                Sq_pad, Hq));
+                                                Sq_pad, Hq, dq_acc, Hq * FA_D));
   }
   // 2) main kernel
   CUtensorMap tq, tk, tv, tdo;
@@ -959,8 +987,7 @@ void flash_bwd(const void* q, long long ldq, int q_col0, const void* k, long lon
   {
     const long long rows = (long long)B * Sq;
     const int width = Hq * FA_D;
-    long long n = rows * (width / 4);
-    int blocks = (int)std::min<long long>((n + 255) / 256, 148 * 32);
+    const int blocks = (int)std::max(1LL, std::min<long long>(rows, (long long)num_sms(dev) * 8));
     (astrai::note_launch(), flash_dq_convert_kernel<<<blocks, 256, 0, s>>>(dq_acc, width, rows, static_cast<__nv_bfloat16*>(dq), ld_dq,
                                                    dq_col0));
   }

@@ -112,7 +112,7 @@ class _AttnQKVFn(torch.autograd.Function):
         C = native()
         do = do.contiguous()
         dqkv = torch.empty_like(qkv)
-        dq_acc = torch.zeros((B * S, Hq * D), device=qkv.device, dtype=torch.float32)
+        dq_acc = torch.empty((B * S, Hq * D), device=qkv.device, dtype=torch.float32)  # zeroed by the kernel
         delta = torch.empty(2 * B * Hq * ((S + 63) // 64 * 64), device=qkv.device, dtype=torch.float32)
         C.flash_bwd(qkv, 0, qkv, Hq * D, qkv, (Hq + Hkv) * D, o, do, lse, delta, dq_acc, dqkv, 0, dqkv, Hq * D,
                     dqkv, (Hq + Hkv) * D, B, S, S, Hq, Hkv, 1.0 / math.sqrt(D), causal, seg)
@@ -186,7 +186,7 @@ class _AttnFn(torch.autograd.Function):
         do2 = do.reshape(B * Sq, Hq * D).contiguous()
         dq = torch.empty_like(q2)
         dkv = torch.empty((B * Sk, 2 * Hkv * D), device=q2.device, dtype=torch.bfloat16)
-        dq_acc = torch.zeros((B * Sq, Hq * D), device=q2.device, dtype=torch.float32)
+        dq_acc = torch.empty((B * Sq, Hq * D), device=q2.device, dtype=torch.float32)  # zeroed by the kernel
         delta = torch.empty(2 * B * Hq * ((Sq + 63) // 64 * 64), device=q2.device, dtype=torch.float32)
         C.flash_bwd(q2, 0, k2, 0, v2, 0, o, do2, lse, delta, dq_acc, dq, 0, dkv, 0, dkv, Hkv * D, B, Sq, Sk, Hq, Hkv,
                     1.0 / math.sqrt(D), causal, seg)
@@ -254,11 +254,10 @@ def bench_attention(time_fn, peaks):
                       "peak_src": src, "sdpa_ms": round(ms_ref, 4), "sdpa_tflops": round(flops / ms_ref / 1e9, 1)}))
     do = torch.randn_like(o)
     dqkv = torch.empty_like(qkv)
-    dq_acc = torch.zeros(B * S, Hq * D, device="cuda", dtype=torch.float32)
+    dq_acc = torch.empty(B * S, Hq * D, device="cuda", dtype=torch.float32)
     delta = torch.empty(2 * B * Hq * S, device="cuda", dtype=torch.float32)
 
     def bwd():
-        dq_acc.zero_()
         C.flash_bwd(qkv, 0, qkv, Hq * D, qkv, (Hq + Hkv) * D, o, do, lse, delta, dq_acc, dqkv, 0, dqkv, Hq * D, dqkv,
                     (Hq + Hkv) * D, B, S, S, Hq, Hkv, scale, True, None)
 

@@ -81,8 +81,9 @@ FUSED_SWIGLU = FUSED_EPILOGUES or __import__("os").environ.get("ASTRAI_FUSED_SWI
 INFER_SWIGLU = __import__("os").environ.get("ASTRAI_INFER_SWIGLU", "1") == "1"
 # RoPE in the QKV projection's epilogue (the CTA-pair tiles rotate q and k before the store; the
 # attention kernel then skips its own rotation, and the backward rotates the gradient back in place).
-# Measured on B200: the reference benchmark's prefill forward 4.56 -> 4.21 ms, the 1.1B step's
-# forward+backward 512 -> 505 ms. ASTRAI_FUSED_ROPE=0 keeps the separate in-place kernel.
+# Measured on B200: the reference benchmark's prefill forward 4.56 -> 4.21 ms; the 1.1B step is
+# unchanged within run-to-run noise (547.3 vs 549.7 ms on one box). ASTRAI_FUSED_ROPE=0 keeps the
+# separate in-place kernel.
 FUSED_ROPE = FUSED_EPILOGUES or __import__("os").environ.get("ASTRAI_FUSED_ROPE", "1") == "1"
 
 
