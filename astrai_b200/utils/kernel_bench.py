@@ -59,6 +59,7 @@ def bench_gemm(only=None):
         ("down_dgrad", 8192, 5632, 2048, 0, 1),
         ("upgate_wgrad", 11264, 2048, 8192, 1, 1),
         ("o_wgrad", 2048, 2048, 8192, 1, 1),
+        ("qkv_wgrad", 3072, 2048, 8192, 1, 1),
         ("square_8192", 8192, 8192, 8192, 0, 0),
     ]
     for name, M, N, K, amn, bmn in cases:
