@@ -1033,7 +1033,9 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
 // and the epilogue of tile t overlaps the MMAs of tile t+1 (the single-CTA 256 x 256 tile fills
 // TMEM, so its MMAs stall while the epilogue drains). Each CTA's stage is 32 KB: a 6-deep ring.
 // (A 256 x 128 pair tile moves 1.5x the operand bytes per FLOP and measured 0.5 - 0.75x the speed of
-// 256 x 256 on every training shape, so only 256 x 256 is instantiated.)
+// 256 x 256 on every training shape, so it is not instantiated. 256 x 192 tiles, 1.17x the bytes
+// per FLOP, are instantiated for a K-major B and picked by pair_tile_n where their waves finish
+// sooner: wave quantisation of 256-wide tiles costs more on those shapes.)
 //
 //   warp 0     TMA producer (both CTAs): loads into its own smem, completion counted on the
 //              even CTA's `full` barrier (cta_group::2 form of the tiled load, no multicast)
@@ -1046,7 +1048,7 @@ __global__ void __launch_bounds__(GemmCfg<BM, BN>::THREADS, 1)
 // is freed, so neither leaves while the other can still signal its barriers.
 template <int BN_>
 struct PairCfg {
-  static constexpr int BN = BN_;                 // output columns of a pair tile (256 or 128)
+  static constexpr int BN = BN_;                 // output columns of a pair tile (256, 192 or 128)
   static constexpr int BK = 64;
   static constexpr int A_BYTES = 128 * BK * 2;   // this CTA's 128 rows of A
   static constexpr int B_BYTES = (BN / 2) * BK * 2;  // this CTA's BN / 2 of the tile's B rows
@@ -1056,7 +1058,11 @@ struct PairCfg {
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
   static constexpr int TMEM_COLS = 2 * BN;       // two accumulators
-  static_assert(BN == 256 || BN == 128, "pair tiles are 256 x 256 or 256 x 128");
+  // tcgen05.alloc takes a power of two of at least 32 columns
+  static constexpr int TMEM_ALLOC = TMEM_COLS <= 32 ? 32 : TMEM_COLS <= 64 ? 64 : TMEM_COLS <= 128 ? 128
+                                    : TMEM_COLS <= 256 ? 256 : 512;
+  static_assert(BN == 256 || BN == 192 || BN == 128, "pair tiles are 256 x 256, 256 x 192 or 256 x 128");
+  static_assert(TMEM_COLS <= 512, "accumulators exceed tensor memory");
 };
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -1109,7 +1115,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
   using Cfg = PairCfg<BN>;
   constexpr int BK = Cfg::BK, A_BYTES = Cfg::A_BYTES, B_BYTES = Cfg::B_BYTES, STAGE_BYTES = Cfg::STAGE_BYTES;
-  constexpr int STAGES = Cfg::STAGES, EPI_WARPS = Cfg::EPI_WARPS, TMEM_COLS = Cfg::TMEM_COLS;
+  constexpr int STAGES = Cfg::STAGES, EPI_WARPS = Cfg::EPI_WARPS, TMEM_ALLOC = Cfg::TMEM_ALLOC;
+  // 256 x 192 tiles: K-major B only (an MN-major B stage is loaded in whole 64-column boxes)
+  static_assert(BN != 192 || !B_MN, "256 x 192 pair tiles take a K-major B");
   constexpr int BNH = BN / 2;  // B rows per CTA; output columns per epilogue warp
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1142,7 +1150,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(TMEM_COLS)
+                 "r"(TMEM_ALLOC)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
@@ -1561,7 +1569,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN>::THREADS
   cluster_sync_all();  // the pair is done with each other's barriers and tensor memory
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_ALLOC)
                  : "memory");
   }
 }
@@ -1696,6 +1704,30 @@ static void dispatch_pair(int a_mn, int b_mn, int out_f32, const CUtensorMap& ta
   ASTRAI_PAIR_CASE(1, 0, 1)
   ASTRAI_PAIR_CASE(1, 1, 1)
 #undef ASTRAI_PAIR_CASE
+}
+
+// 256 x 192 pair tiles (K-major B only): A K- or MN-major, bf16 or fp32 output.
+static void dispatch_pair192(int a_mn, int out_f32, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
+                             int pairs, cudaStream_t s) {
+  if (a_mn == 0 && out_f32 == 0) return launch_gemm_pair<192, 0, 0, 0>(ta, tb, p, pairs, s);
+  if (a_mn == 1 && out_f32 == 0) return launch_gemm_pair<192, 1, 0, 0>(ta, tb, p, pairs, s);
+  if (a_mn == 0 && out_f32 == 1) return launch_gemm_pair<192, 0, 0, 1>(ta, tb, p, pairs, s);
+  return launch_gemm_pair<192, 1, 0, 1>(ta, tb, p, pairs, s);
+}
+
+// Pair tile width for a GEMM with a K-major B: 192 where its waves of 256 x 192 tiles finish sooner
+// than the waves of 256 x 256 tiles by at least 3 %, else 256. A 192-wide wave does 0.75 of the
+// work but measured 0.88 of the time at 32 k-blocks (8192 x 3072 x 2048: 7 waves 80.7 us against 6
+// waves 77.8 us) and 0.76 at 88 (8192 x 2048 x 5632: 154.1 against 161.4 us; L2 flushed), so the
+// wave cost is 0.88 below 64 k-blocks and 0.76 from there. One-wave grids (a 2048-token prefill's
+// 2048 x 1536 projections) always take the smaller tile: 21.0 / 45.2 against 22.7 / 49.2 us.
+static int pair_tile_n(int M, int N, int K, int batch, int pairs) {
+  if (N <= 192 || pairs <= 0) return 256;
+  const long long tm = (long long)((M + 255) / 256) * batch;
+  const long long t256 = tm * ((N + 255) / 256), t192 = tm * ((N + 191) / 192);
+  const double w192 = (K + 63) / 64 >= 64 ? 0.76 : 0.88;
+  const double c256 = (double)((t256 + pairs - 1) / pairs), c192 = w192 * (double)((t192 + pairs - 1) / pairs);
+  return c192 < 0.97 * c256 ? 192 : 256;
 }
 
 // CTA-pair policy: plain and batched GEMMs with M > 128 and N > 128 run on the pair kernel.
@@ -1911,10 +1943,16 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
   } else {
     pick_tile(M, N, batch, sms, BM, BN, (K + 63) / 64);
   }
-  // 256 x 256 tiles on a CTA pair (force_bn 1024, or the automatic pick under the pair policy)
-  const bool pair = gather == nullptr && (force_bn == 1024 || force_bn == 1026 || force_bn == 1027 ||
-                                          (force_bn == 0 && M > 128 && N > 128 && pair_on()));
-  if (pair) BM = BN = 256;
+  // 256 x 256 tiles on a CTA pair (force_bn 1024, or the automatic pick under the pair policy);
+  // 256 x 192 for a K-major B where pair_tile_n picks it (force_bn 192 forces it)
+  const bool pair = gather == nullptr && (force_bn == 192 || force_bn == 1024 || force_bn == 1026 ||
+                                          force_bn == 1027 || (force_bn == 0 && M > 128 && N > 128 && pair_on()));
+  if (pair) {
+    if (force_bn == 192 && (b_mn || sym)) throw std::runtime_error("astrai gemm: 256 x 192 tiles take a K-major B");
+    BM = 256;
+    BN = force_bn == 192 ? 192
+                         : (force_bn == 0 && !b_mn && !sym ? pair_tile_n(M, N, K, batch, pair_clusters(dev)) : 256);
+  }
 
   CUtensorMap ta, tb;
   {
@@ -2002,10 +2040,12 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
     // force_bn 1026: the last wave split wherever use_streamk_pair allows it (also ASTRAI_PAIR_STREAMK=1);
     // force_bn 1027: every k-block split over all pairs whatever the shape (needs tiles * kb >= pairs);
     // force_bn 0: pair_split_mode
-    const int automatic = (force_bn == 0 && streamk_on()) ? pair_split_mode(tiles, p.k_blocks, pmax) : 0;
-    const bool split = !sym && (force_bn == 1026 || automatic == 1 ||
-                                (force_bn != 1024 && force_bn != 1027 && pair_streamk_on() && streamk_on()));
-    const bool all_units = !sym && (force_bn == 1027 ? (long long)tiles * p.k_blocks >= pmax : automatic == 2);
+    const int automatic = (force_bn == 0 && BN == 256 && streamk_on()) ? pair_split_mode(tiles, p.k_blocks, pmax) : 0;
+    const bool split = !sym && BN == 256 && (force_bn == 1026 || automatic == 1 ||
+                                             (force_bn != 1024 && force_bn != 1027 && pair_streamk_on() &&
+                                              streamk_on()));
+    const bool all_units = !sym && BN == 256 &&
+                           (force_bn == 1027 ? (long long)tiles * p.k_blocks >= pmax : automatic == 2);
     if (all_units && sk_buffers(dev, stream, sms, &p.sk_ws, &p.sk_flags)) {
       p.dp_tiles = 0;
       p.sk_units = (long long)tiles * p.k_blocks;
@@ -2016,7 +2056,10 @@ void gemm_bf16(const void* A, const void* B, void* D, const void* C, int M, int 
       p.sk_units = (long long)(tiles - p.dp_tiles) * p.k_blocks;
       pairs = pmax;
     }
-    dispatch_pair<256>(a_mn, b_mn, out_f32, ta, tb, p, pairs, stream);
+    if (BN == 192)
+      dispatch_pair192(a_mn, out_f32, ta, tb, p, pairs, stream);
+    else
+      dispatch_pair<256>(a_mn, b_mn, out_f32, ta, tb, p, pairs, stream);
     if (sym) sym_mirror(D, out_f32, M, ldd, strideD, batch, stream);
     return;
   }
@@ -2251,7 +2294,7 @@ void gemm_rope_bf16(const void* A, long long lda, const void* B, long long ldb, 
   // single-CTA tiles; both double-buffer the accumulator, so the rotation overlaps the next MMAs
   const bool pair = M > 128 && N > 128 && pair_on();
   const int BM = pair ? 256 : 128;
-  const int BN = N <= 128 ? 128 : 256;
+  const int BN = pair ? pair_tile_n(M, N, K, 1, pair_clusters(dev)) : (N <= 128 ? 128 : 256);
   if (reinterpret_cast<uintptr_t>(cs) % 16) throw std::runtime_error("gemm_rope: cos/sin table must be 16-byte aligned");
   CUtensorMap ta, tb;
   {
@@ -2315,6 +2358,7 @@ void gemm_rope_bf16(const void* A, long long lda, const void* B, long long ldb, 
   p.sym_bm = 1;
   p.sym_bn = 1;
   const int tiles = p.tiles_m * p.tiles_n;
+  if (pair && BN == 192) return dispatch_pair192(0, 0, ta, tb, p, std::min(tiles, pair_clusters(dev)), stream);
   if (pair) return dispatch_pair<256>(0, 0, 0, ta, tb, p, std::min(tiles, pair_clusters(dev)), stream);
   const int grid = std::min(tiles, sms);
   if (BN == 256)

@@ -686,7 +686,7 @@ def bench_gemm_shapes():
     """Tile plans on the GEMMs of a 2048-token prefill (d 1536, 24/4 heads of 64, FFN 6912, vocab
     10000) and of the 1.1B step, L2 flushed before every call (us): automatic plan (0), CTA pairs
     unsplit (1024), pairs with the last-wave split (1026), pairs with every k-block split (1027),
-    single CTA 128 x 256 (256), cuBLAS."""
+    single CTA 128 x 256 (256), 256 x 192 pair tiles (192, K-major B only), cuBLAS."""
     from astrai_b200.ops._ext import native
 
     C = native()
@@ -705,7 +705,7 @@ def bench_gemm_shapes():
         b = torch.randn((K, N) if bmn else (N, K), device="cuda").to(torch.bfloat16)
         d = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
         res = {}
-        for fb in (0, 1024, 1026, 1027, 256):
+        for fb in (0, 1024, 1026, 1027, 256) + (() if bmn else (192,)):
             res[str(fb)] = round(time_flushed(lambda: C.gemm(a, b, d, None, amn, bmn, 1.0, 0.0, fb), 3, 20) * 1e3, 1)
         res["cublas"] = round(time_flushed(lambda: torch.matmul(a.t() if amn else a, b if bmn else b.t()), 3, 20)
                               * 1e3, 1)

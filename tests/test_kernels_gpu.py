@@ -508,6 +508,29 @@ def test_swiglu_mlp_forward_only(M, d, Fw, with_res):
     assert native().read_error() == 0
 
 
+@pytest.mark.parametrize("a_mn", [0, 1])
+@pytest.mark.parametrize("out_f32,with_c", [(False, False), (False, True), (True, False)])
+@pytest.mark.parametrize("M,N,K,fb", [(8192, 2048, 5632, 0), (2048, 1536, 1536, 0), (1000, 704, 3000, 192),
+                                      (520, 200, 512, 192)])
+def test_gemm_cta_pair_256x192(a_mn, out_f32, with_c, M, N, K, fb):
+    """256 x 192 CTA-pair tiles (K-major B): picked automatically where their waves finish sooner
+    (8192 x 2048 x 5632, 2048 x 1536 x 1536) and forced with force_bn 192 (ragged M, N, a partial
+    last column tile), against an fp32 matmul (plus beta C)."""
+    from astrai_b200.ops._ext import native
+
+    torch.manual_seed(M + N)
+    a = torch.randn((K, M) if a_mn else (M, K), device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+    dt = torch.float32 if out_f32 else torch.bfloat16
+    c = torch.randn(M, N, device="cuda", dtype=dt) if with_c else None
+    A = a.float().t() if a_mn else a.float()
+    ref = A @ b.float().t() * 0.5 + (2.0 * c.float() if with_c else 0.0)
+    d = torch.full((M, N), float("nan"), device="cuda", dtype=dt)
+    native().gemm(a, b, d, c, a_mn, 0, 0.5, 2.0 if with_c else 0.0, fb)
+    assert torch.isfinite(d.float()).all()
+    assert rel_err(d, ref) < 1e-2
+
+
 @pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 1)])
 @pytest.mark.parametrize("M,N,K,fb", [(2048, 1536, 6912, 0), (3072, 2048, 8192, 0), (2048, 5632, 8192, 0),
                                       (2048, 1536, 1536, 1027), (1000, 704, 3000, 1027)])
