@@ -819,8 +819,8 @@ def emit_line(res, args, rank, world, t0):
                 "vs_baseline": None if BASELINE_VALUE is None else res["value"] / BASELINE_VALUE,
                 "dtype": "bf16",
                 "data": "synthetic uniform token ids, random-init weights",
-                "config": {"model": MODEL_DESC if args.impl == "astrai_b200" or MODEL == "dense"
-                           else MODEL_DESC + " [reference: all 16 layers MoE, no aux loss]",
+                "config": {"model": MODEL_DESC + " [reference: all 16 layers MoE, no aux loss]"
+                           if args.impl == "reference" and MODEL == "moe" else MODEL_DESC,
                            "global_batch": BATCH * ACCUM * world, "seq_len": SEQ, "parallelism": par,
                            "micro_batch": BATCH, "grad_accum": ACCUM,
                            "optimizer": "Muon(0.02, ns5)+AdamW(1e-4, wd0.1), clip 1.0"
