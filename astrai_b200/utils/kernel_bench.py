@@ -1,6 +1,6 @@
 """Device-timed micro-benchmarks of the framework's kernels.
 
-    python -m astrai_b200.utils.kernel_bench [gemm [case]|gemm_shapes|swiglu_gemm|elementwise|ns|attn|norm|skinny|sample|decode|prefill|all]
+    python -m astrai_b200.utils.kernel_bench [gemm [case]|gemm_shapes|swiglu_gemm|rope_gemm|elementwise|ns|attn|norm|skinny|sample|decode|prefill|all]
     torchrun --nproc-per-node N -m astrai_b200.utils.kernel_bench allreduce|ep|tpgather|tprow
 
 Each case is timed with CUDA events on the launching stream after warm-up,
@@ -682,6 +682,31 @@ def bench_swiglu_gemm():
         print(json.dumps({"kernel": "gemm_swiglu", "M": M, "d": d, "F": F, "us_warm_flushed": res}))
 
 
+def bench_rope_gemm():
+    """The QKV projection with RoPE: the plain GEMM followed by the in-place RoPE kernel, against the
+    GEMM with RoPE on its q and k columns in the epilogue; at the 1.1B step's shape (8192 x 2048 ->
+    3072, 20 rotated heads of 128) and a 2048-token prefill of the reference benchmark's model
+    (2048 x 1536 -> 2048, 28 rotated heads of 64). Warm and L2 flushed, us per call."""
+    from astrai_b200.ops._ext import native
+    from astrai_b200.ops.rope import rope_inplace, rope_table
+
+    C = native()
+    for M, d, N, hd, heads, seq in ((8192, 2048, 3072, 128, 20, 2048), (2048, 1536, 2048, 64, 28, 512)):
+        x = torch.randn(M, d, device="cuda").to(torch.bfloat16)
+        w = (torch.randn(N, d, device="cuda") * 0.02).to(torch.bfloat16)
+        y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        tab = rope_table(hd, 4096, 1e6, device="cuda")
+
+        def separate():
+            C.gemm(x, w, y, None, 0, 0, 1.0, 0.0, 0)
+            rope_inplace(y, 0, heads, hd, tab, None, seq)
+
+        fns = {"gemm_then_rope": separate,
+               "gemm_rope_epilogue": lambda: C.gemm_rope(x, w, y, tab, None, seq, heads * hd, hd)}
+        res = {k: [round(time_fn(f, 5, 30) * 1e3, 1), round(time_flushed(f, 3, 20) * 1e3, 1)] for k, f in fns.items()}
+        print(json.dumps({"kernel": "gemm_rope", "M": M, "K": d, "N": N, "head_dim": hd, "us_warm_flushed": res}))
+
+
 def bench_gemm_shapes():
     """Tile plans on the GEMMs of a 2048-token prefill (d 1536, 24/4 heads of 64, FFN 6912, vocab
     10000) and of the 1.1B step, L2 flushed before every call (us): automatic plan (0), CTA pairs
@@ -795,6 +820,8 @@ def main(argv=None):
         bench_elementwise()
     if which in ("swiglu_gemm", "all"):
         bench_swiglu_gemm()
+    if which in ("rope_gemm", "all"):
+        bench_rope_gemm()
     if which in ("gemm_shapes", "all"):
         bench_gemm_shapes()
     if which in ("gemm", "all"):

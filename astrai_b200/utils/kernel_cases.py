@@ -1,6 +1,6 @@
 """Runs each hot kernel of the framework once on a case larger than L2, for profiler captures.
 
-``python -m astrai_b200.utils.kernel_cases [ce rope swiglu gemm_swiglu gemm_swiglu_train embedding router sample decode adamw muon ep]``
+``python -m astrai_b200.utils.kernel_cases [ce rope swiglu gemm_swiglu gemm_swiglu_train gemm_rope embedding router sample decode adamw muon ep]``
 (no argument: all of them). One launch per kernel (two for the forward/backward pairs), shapes of
 the 1.1B dense step (8192 tokens, d 2048, FFN 5632, vocab 32000), the MoE layer (64 experts top-6,
 one-rank expert-parallel group) and batch-32 decode over a 4096-token paged cache, so an ``ncu``
@@ -61,6 +61,17 @@ def run(which):
         C.gemm(x, w, h, None, 0, 0, 1.0, 0.0, 0)
         C.gemm_swiglu(1, x, w, h, a, None)
         del x, w, h, a
+    if want("gemm_rope"):
+        # the 1.1B step's QKV projection (8192 tokens, d 2048 -> 16 + 4 + 4 heads of 128): the plain
+        # GEMM, then the GEMM with RoPE on the q and k columns in its epilogue
+        from astrai_b200.ops.rope import rope_table
+        x = torch.randn(8192, 2048, device=dev).to(torch.bfloat16)
+        w = (torch.randn(3072, 2048, device=dev) * 0.02).to(torch.bfloat16)
+        y = torch.empty(8192, 3072, device=dev, dtype=torch.bfloat16)
+        tab = rope_table(128, 2048, 1e6, device=dev)
+        C.gemm(x, w, y, None, 0, 0, 1.0, 0.0, 0)
+        C.gemm_rope(x, w, y, tab, None, 2048, 20 * 128, 128)
+        del x, w, y
     if want("embedding"):
         from astrai_b200.ops.embedding import embedding
         w = (torch.randn(32000, 2048, device=dev) * 0.02).to(torch.bfloat16).requires_grad_()
